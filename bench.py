@@ -1,0 +1,404 @@
+#!/usr/bin/env python
+"""MARS B200 benchmark: fused score x decay x importance -> top-K scan.
+
+Workload (the metric of BASELINE.json: queries/s + p99 at N=1M, D=768, K=10,
+HBM GB/s vs peak):
+  * corpus N = 1,000,000 rows x D = 768 fp32, i.i.d. Gaussian rows divided by
+    (||v|| + 1e-8), timestamps U[0, 600] s, importance U[0, 1], 4 modalities;
+    seeded synthetic data (no dataset is involved);
+  * every query is one fused scan (dot x exp(-lambda * age) x importance) over
+    all N rows with top-K = 10, lambda = 0.01; a step is 16 such queries;
+  * N GPUs: the corpus is row-sharded (strong scaling: total N fixed); each
+    GPU scans its shard, the per-query local top-K lists are all-gathered over
+    NCCL and merged on every GPU.
+
+`value` is queries/s with queries and corpus resident in HBM, timed with CUDA
+events on the scan stream (max over ranks).  `e2e` goes through the C ABI with
+host buffers: queries copied host->device and results device->host inside the
+timed region.  `--impl reference` times the CPU implementation of the same
+path (the oracle port) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "cuda-multimodal-memory_b200"), os.path.join(ROOT, "oracle")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import numpy as np
+
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["mars", "reference"], default="mars")
+    ap.add_argument("--n", type=int, default=1_000_000)
+    ap.add_argument("--dim", type=int, default=768)
+    ap.add_argument("--k", type=int, default=10)
+    ap.add_argument("--queries-per-step", type=int, default=16)
+    ap.add_argument("--lam", type=float, default=0.01)
+    ap.add_argument("--ts-max", type=float, default=600.0)
+    ap.add_argument("--seed", type=int, default=42)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=10.0)
+    return ap.parse_args()
+
+
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def metric_name(a):
+    return (f"queries/s (fused score*decay*importance top-K scan, N={a.n}, D={a.dim}, "
+            f"K={a.k})")
+
+
+def config_dict(a, world):
+    return {
+        "workload": f"fused_scan_topk N={a.n} D={a.dim} K={a.k}: one scan of all rows per query, "
+                    f"{a.queries_per_step} queries per step",
+        "n_rows": a.n, "dim": a.dim, "top_k": a.k, "queries_per_step": a.queries_per_step,
+        "lambda": a.lam, "importance": True, "shards": world,
+        "parallelism": f"row-shard x{world}" + (" + NCCL all-gather + merge" if world > 1 else ""),
+        "l2": "inputs larger than L2: each query streams "
+              f"{a.n // world * (a.dim * 4 + 8) / 1e9:.3f} GB per GPU (L2 126 MB)",
+    }
+
+
+def measured_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            j = json.load(f)
+        return float(j["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def committed_traffic():
+    """dram bytes per scan launch from the committed ncu summary (or None)."""
+    p = os.path.join(ROOT, "profiles", "scan_topk_traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)
+    except Exception:
+        return None
+
+
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], None, set()
+        names = ["active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown",
+                 "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names[1:], parts[5:9]):
+                if v.lower() in ("active", "0x1", "1", "yes"):
+                    reasons.add(nm)
+        if not sm:
+            return None
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+def run_reference(a):
+    """CPU implementation of the same path (oracle port), rank 0 only."""
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    import oracle as O
+    from mars_b200 import datagen
+    E, mod, ts, imp = datagen.gaussian_rows(0, a.n, a.dim, seed=a.seed, ts_max=a.ts_max)
+    c = O.Corpus(E=E, ts=ts, mod=mod, imp=imp)
+    Q = datagen.queries(64, a.dim, seed=a.seed + 1)
+    threads = os.cpu_count() or 1
+    for w in range(a.warmup):
+        O.scan_topk_fast(c, Q[w % 64], a.ts_max, a.lam, a.k, use_importance=True, n_threads=threads)
+    t0 = time.perf_counter()
+    for s in range(a.steps):
+        O.scan_topk_fast(c, Q[s % 64], a.ts_max, a.lam, a.k, use_importance=True, n_threads=threads)
+    dt = time.perf_counter() - t0
+    v = a.steps / dt
+    line = {
+        "impl": "reference", "metric": metric_name(a), "value": v, "unit": "queries/s",
+        "n_gpus": world, "steps": a.steps, "warmup": a.warmup, "ms_per_step": dt / a.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded Gaussian corpus)", "config": config_dict(a, 1),
+        "cpu_baseline": {"value": v, "unit": "queries/s", "cores": threads, "kind": "port",
+                         "sample": f"each step = 1 query scanned over all {a.n} rows "
+                                   f"(oracle/mars_oracle.c orc_scan_topk_fast, {threads} threads)"},
+        "e2e": {"value": v, "unit": "queries/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+def cpu_baseline(a, E, mod, ts, imp, Qh):
+    import oracle as O
+    c = O.Corpus(E=E, ts=ts, mod=mod, imp=imp)
+    threads = os.cpu_count() or 1
+    t0 = time.perf_counter()
+    O.scan_topk_fast(c, Qh[0], a.ts_max, a.lam, a.k, use_importance=True, n_threads=threads)
+    t1 = time.perf_counter() - t0
+    n = int(max(2, min(32, math.ceil(a.cpu_budget_s / max(t1, 1e-3)))))
+    t0 = time.perf_counter()
+    for i in range(n):
+        O.scan_topk_fast(c, Qh[i % Qh.shape[0]], a.ts_max, a.lam, a.k, use_importance=True,
+                         n_threads=threads)
+    dt = time.perf_counter() - t0
+    return {"value": n / dt, "unit": "queries/s", "cores": threads, "kind": "port",
+            "sample": f"{n} queries, each scanning all {a.n} rows (same corpus, same K/lambda), "
+                      f"oracle/mars_oracle.c orc_scan_topk_fast with {threads} OpenMP threads"}
+
+
+def run_mars(a):
+    import torch
+    import mars_b200 as mb
+    from mars_b200 import datagen
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist_mod
+        from datetime import timedelta
+        dist = dist_mod
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    lo, hi = a.n * rank // world, a.n * (rank + 1) // world
+    n_local = hi - lo
+    E, mod, ts, imp = datagen.gaussian_rows(lo, hi, a.dim, seed=a.seed, ts_max=a.ts_max)
+    Qh = datagen.queries(64, a.dim, seed=a.seed + 1)
+    store = mb.Store(n_local, a.dim, device=local)
+    store.upload(E, mod, ts, imp)
+    ctx = mb.QueryContext(n_local, a.dim, max_k=a.k, device=local)
+    stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
+    torch.cuda.set_stream(stream)
+    K, Q = a.k, a.queries_per_step
+    Qd = torch.from_numpy(Qh).cuda()
+    ids = torch.empty((Q, K), dtype=torch.int32, device="cuda")
+    vals = torch.empty((Q, K), dtype=torch.float32, device="cuda")
+    if world > 1:
+        gids = torch.empty((world, Q, K), dtype=torch.int32, device="cuda")
+        gvals = torch.empty((world, Q, K), dtype=torch.float32, device="cuda")
+        mids = torch.empty((Q, K), dtype=torch.int32, device="cuda")
+        mvals = torch.empty((Q, K), dtype=torch.float32, device="cuda")
+    n_ev = (a.steps + a.warmup) * Q
+    ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
+    st_a = [torch.cuda.Event(enable_timing=True) for _ in range(a.steps + a.warmup)]
+    st_b = [torch.cuda.Event(enable_timing=True) for _ in range(a.steps + a.warmup)]
+
+    def step(i, timed_events=True):
+        if timed_events:
+            st_a[i].record(stream)
+        for j in range(Q):
+            qi = (i * Q + j) % Qd.shape[0]
+            if timed_events:
+                ev_a[i * Q + j].record(stream)
+            ctx.scan_topk(store, Qd[qi], a.ts_max, a.lam, K, ids[j], vals[j],
+                          use_importance=True, row_offset=lo, stream=ctx.stream)
+            if timed_events:
+                ev_b[i * Q + j].record(stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gids, ids)
+            dist.all_gather_into_tensor(gvals, vals)
+            ctx.topk_merge_batch(gids, gvals, world, K, Q, mids, mvals, stream=ctx.stream)
+        if timed_events:
+            st_b[i].record(stream)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    for w in range(a.warmup):
+        step(a.steps + w)
+    barrier()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    barrier()
+    t_start.record(stream)
+    for s in range(a.steps):
+        step(s)
+    t_end.record(stream)
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    elapsed_ms = t_start.elapsed_time(t_end)
+    scan_ms = [ev_a[i].elapsed_time(ev_b[i]) for i in range(a.steps * Q)]
+    step_ms = [st_a[i].elapsed_time(st_b[i]) for i in range(a.steps)]
+    if world > 1:
+        t = torch.tensor([elapsed_ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(t.item())
+
+    # correctness spot check of the last step against a local recompute (rank 0)
+    ok = True
+    if world > 1:
+        torch.cuda.synchronize()
+
+    # ---- end to end through the C ABI with host buffers ---------------------
+    e2e = None
+    pitch = (a.dim + 3) // 4 * 4
+    if world == 1:
+        cfg = mb.RetrievalConfig(top_k=K, bfs_max_hops=0, time_decay_lambda=a.lam,
+                                 use_importance=True)
+        for i in range(3):
+            ctx.query(store, Qh[i], a.ts_max, cfg)
+        lat = []
+        t0 = time.perf_counter()
+        for s in range(a.steps):
+            for j in range(Q):
+                c0 = time.perf_counter()
+                ctx.query(store, Qh[(s * Q + j) % 64], a.ts_max, cfg)
+                lat.append(time.perf_counter() - c0)
+        dt = time.perf_counter() - t0
+        e2e = {"value": a.steps * Q / dt, "unit": "queries/s",
+               "h2d_bytes_per_step": Q * (64 + pitch * 4), "d2h_bytes_per_step": Q * (K * 16 + 8),
+               "p50_us": float(np.percentile(lat, 50) * 1e6),
+               "p99_us": float(np.percentile(lat, 99) * 1e6),
+               "path": "mars_query (C ABI): pinned H2D of query + descriptor, scan, "
+                       "select, D2H of K results, one CUDA graph per call"}
+    else:
+        Qpin = torch.from_numpy(Qh).pin_memory()
+        qbuf = torch.empty((Q, a.dim), dtype=torch.float32, device="cuda")
+        out_ids = torch.empty((Q, K), dtype=torch.int32).pin_memory()
+        out_vals = torch.empty((Q, K), dtype=torch.float32).pin_memory()
+        barrier()
+        t0 = time.perf_counter()
+        for s in range(a.steps):
+            base = (s * Q) % (64 - Q + 1)
+            qbuf.copy_(Qpin[base:base + Q], non_blocking=True)
+            for j in range(Q):
+                ctx.scan_topk(store, qbuf[j], a.ts_max, a.lam, K, ids[j], vals[j],
+                              use_importance=True, row_offset=lo, stream=ctx.stream)
+            dist.all_gather_into_tensor(gids, ids)
+            dist.all_gather_into_tensor(gvals, vals)
+            ctx.topk_merge_batch(gids, gvals, world, K, Q, mids, mvals, stream=ctx.stream)
+            out_ids.copy_(mids, non_blocking=True)
+            out_vals.copy_(mvals, non_blocking=True)
+            stream.synchronize()
+        dt = time.perf_counter() - t0
+        t = torch.tensor([dt], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dt = float(t.item())
+        e2e = {"value": a.steps * Q / dt, "unit": "queries/s",
+               "h2d_bytes_per_step": Q * a.dim * 4, "d2h_bytes_per_step": Q * K * 8,
+               "path": "pinned H2D of queries, mars_scan_topk per shard, NCCL all-gather, "
+                       "mars_topk_merge_batch, D2H of merged top-K"}
+
+    if rank == 0:
+        peak, peak_kind = measured_peak()
+        bytes_per_launch = n_local * (a.dim * 4 + 4 + 4)
+        mean_scan_ms = statistics.mean(scan_ms)
+        achieved = bytes_per_launch / (mean_scan_ms * 1e-3) / 1e9
+        tr = committed_traffic()
+        traffic = None
+        if tr and tr.get("n_rows") and tr.get("dram_bytes"):
+            traffic = tr["dram_bytes"] * n_local / tr["n_rows"]
+        qps = a.steps * Q / (elapsed_ms * 1e-3)
+        line = {
+            "metric": metric_name(a), "value": qps, "unit": "queries/s", "n_gpus": world,
+            "steps": a.steps, "warmup": a.warmup, "ms_per_step": elapsed_ms / a.steps,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded Gaussian corpus and queries)",
+            "config": config_dict(a, world),
+            "latency_us": {
+                "scan_kernel_p50": float(np.percentile(scan_ms, 50) * 1e3),
+                "scan_kernel_p99": float(np.percentile(scan_ms, 99) * 1e3),
+                "step_p50": float(np.percentile(step_ms, 50) * 1e3),
+                "step_p99": float(np.percentile(step_ms, 99) * 1e3)},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "peak_kind": peak_kind,
+                         "traffic": traffic,
+                         "kernel": "scan_topk_kernel",
+                         "algorithmic_bytes_per_launch": bytes_per_launch},
+            "e2e": e2e,
+            "gpu_launches": a.steps * (Q + (1 if world > 1 else 0)),
+            "clocks": clocks,
+        }
+        if world == 1 and not a.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(a, E, mod, ts, imp, Qh)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    del ok
+
+
+def main():
+    a = parse_args()
+    if a.impl == "reference":
+        run_reference(a)
+    else:
+        run_mars(a)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,128 @@
+// mars_internal.h -- host-side objects behind the C ABI handles.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+#include <vector>
+
+#include "mars_b200.h"
+
+// ---- error plumbing ------------------------------------------------------
+namespace mars {
+
+void set_error(const std::string& msg);
+int fail(int status, const std::string& msg);
+int cuda_fail(cudaError_t e, const char* what, const char* file, int line);
+
+}  // namespace mars
+
+#define MARS_CUDA_TRY(call)                                                  \
+    do {                                                                     \
+        cudaError_t mars_e__ = (call);                                       \
+        if (mars_e__ != cudaSuccess)                                         \
+            return mars::cuda_fail(mars_e__, #call, __FILE__, __LINE__);     \
+    } while (0)
+
+#define MARS_TRY(call)                                                       \
+    do {                                                                     \
+        int mars_s__ = (call);                                               \
+        if (mars_s__ != MARS_OK) return mars_s__;                            \
+    } while (0)
+
+// Scoped device selection: restores the caller's current device.
+struct MarsDeviceGuard {
+    int prev = -1;
+    bool ok = true;
+    explicit MarsDeviceGuard(int dev) {
+        if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+        if (prev != dev) ok = cudaSetDevice(dev) == cudaSuccess;
+    }
+    ~MarsDeviceGuard() {
+        int cur = -1;
+        if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+    }
+};
+
+// ---- store (DeviceMemoryGraph) -------------------------------------------
+struct mars_store {
+    int32_t device = 0;
+    int32_t capacity = 0;
+    int32_t dim = 0;
+    int32_t pitch = 0;          // floats per row (dim rounded up to 4)
+    int32_t n = 0;              // host mirror of *d_n
+    int32_t edge_slack = 0;
+    bool owns = true;           // false: wraps memory owned by a caller
+
+    float* d_E = nullptr;       // capacity x pitch
+    float* d_ts = nullptr;
+    float* d_imp = nullptr;
+    int32_t* d_mod = nullptr;
+    int32_t* d_n = nullptr;     // device N
+
+    // CSR over nodes [0, csr_n)
+    int32_t csr_n = 0;
+    int32_t num_edges = 0;
+    int32_t csr_edge_cap = 0;
+    int32_t* d_row_offsets = nullptr;
+    int32_t* d_col_indices = nullptr;
+
+    // append-only neighbour slack: node u's extras at d_extra[u*slack ...]
+    int32_t* d_extra = nullptr;
+    int32_t* d_extra_cnt = nullptr;
+    std::vector<int32_t> h_extra_cnt;
+
+    cudaStream_t stream = nullptr;
+    cudaEvent_t written = nullptr;  // last write to the store
+
+    // raw view of a caller-owned DeviceMemoryGraph (compat layer)
+    void* compat_key = nullptr;
+};
+
+// ---- query context (QueryContext) ----------------------------------------
+
+struct mars_query_ctx {
+    int32_t device = 0;
+    int32_t max_nodes = 0;
+    int32_t dim = 0;
+    int32_t pitch = 0;
+    int32_t max_k = 0;
+    int32_t num_sms = 0;
+    int32_t scan_blocks = 0;
+    int32_t bfs_blocks = 0;
+
+    cudaStream_t stream = nullptr;
+    cudaEvent_t ev[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
+
+    // per-query descriptor: host pinned staging + device copy
+    void* h_desc = nullptr;
+    void* d_desc = nullptr;
+    size_t desc_bytes = 0;
+
+    // scan scratch
+    float* d_part_val = nullptr;    // scan_blocks * kMaxTopK
+    int32_t* d_part_idx = nullptr;
+    unsigned int* d_ticket = nullptr;   // [4] tickets for scan / bfs / finalize / merge
+
+    // BFS scratch
+    unsigned long long* d_stamp = nullptr;  // max_nodes
+    uint32_t epoch = 0;
+    int32_t* d_vis_ids = nullptr;           // max_nodes
+    float* d_vis_score = nullptr;           // max_nodes
+    int32_t* d_lvl = nullptr;               // [16] level offsets + [16] tail
+    float* d_seed_val = nullptr;            // kMaxTopK
+    int32_t* d_seed_idx = nullptr;
+    int32_t* d_seed_cnt = nullptr;
+
+    // results
+    mars_query_result* d_results = nullptr;   // max_k
+    int32_t* d_result_cnt = nullptr;
+    mars_query_result* h_results = nullptr;    // pinned
+    int32_t* h_result_cnt = nullptr;           // pinned [2]: count, visited
+
+    // graph replay of the whole query (H2D desc -> kernels -> D2H)
+    bool use_graph = true;
+    cudaGraphExec_t graph = nullptr;
+    uint64_t graph_key = 0;
+};

@@ -1,0 +1,386 @@
+// mars_store.cu -- the device store (DeviceMemoryGraph) and streaming insert.
+//
+// Layout in HBM (one allocation per array, capacity rows, 256-byte aligned):
+//   E        capacity x pitch fp32, pitch = D rounded up to 4 (16-byte rows),
+//            pad columns zero;
+//   ts, imp  capacity fp32 (imp initialised to 1), mod capacity int32;
+//   d_n      the current row count, read by every kernel so that appends need
+//            no relaunch or graph re-capture;
+//   CSR      row_offsets / col_indices over the rows present at upload;
+//   slack    capacity x edge_slack int32 append-only neighbour lists + counts.
+//
+// Reference: upload_to_device / free_device (src/memory_cuda.cu:593-627) and
+// engine_server's add_node + ensure_device (src/engine_server.cu:154-213),
+// which grows host vectors and re-uploads the whole corpus on the next query.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "mars_b200.h"
+#include "mars_internal.h"
+
+namespace mars {
+
+static thread_local std::string g_last_error = "no error";
+
+void set_error(const std::string& msg) { g_last_error = msg; }
+
+int fail(int status, const std::string& msg) {
+    g_last_error = msg;
+    return status;
+}
+
+int cuda_fail(cudaError_t e, const char* what, const char* file, int line) {
+    char buf[512];
+    std::snprintf(buf, sizeof(buf), "CUDA error %s (%s) in %s at %s:%d", cudaGetErrorName(e),
+                  cudaGetErrorString(e), what, file, line);
+    g_last_error = buf;
+    return e == cudaErrorMemoryAllocation ? MARS_ERR_OOM : MARS_ERR_CUDA;
+}
+
+// ---------------------------------------------------------------------------
+// Normalisation of appended rows, bit-identical to the reference's host rule
+// (src/engine_server.cu:165-171): norm = sqrtf(sequential fp32 sum of x*x)
+// + 1e-8f, then x / norm.  One thread forms the sequential sum of its row
+// (the order is what makes it bit-exact); the warp then divides the row.
+__global__ void normalize_rows_kernel(float* __restrict__ E, int64_t pitch, int32_t first,
+                                      int32_t count, int32_t dim) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= count) return;
+    float* row = E + (int64_t)(first + warp) * pitch;
+    float norm = 0.0f;
+    if (lane == 0) {
+        for (int32_t d = 0; d < dim; ++d) norm = __fadd_rn(norm, __fmul_rn(row[d], row[d]));
+        norm = __fadd_rn(__fsqrt_rn(norm), 1e-8f);
+    }
+    norm = __shfl_sync(0xffffffffu, norm, 0);
+    for (int32_t d = lane; d < dim; d += 32) row[d] = __fdiv_rn(row[d], norm);
+}
+
+__global__ void fill_f32_kernel(float* p, int64_t n, float v) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i < n) p[i] = v;
+}
+
+__global__ void scatter_edges_kernel(int32_t* __restrict__ extra, int32_t* __restrict__ cnt,
+                                     const int32_t* __restrict__ slot_pos,
+                                     const int32_t* __restrict__ dst,
+                                     const int32_t* __restrict__ src,
+                                     const int32_t* __restrict__ new_cnt, int32_t n) {
+    const int32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n) return;
+    extra[slot_pos[i]] = dst[i];
+    // every edge of a node writes the same final count; the value is the
+    // node's count after this whole batch
+    cnt[src[i]] = new_cnt[i];
+}
+
+}  // namespace mars
+
+using namespace mars;
+
+static int alloc_store(mars_store* s) {
+    const size_t rows = (size_t)s->capacity;
+    MARS_CUDA_TRY(cudaMalloc(&s->d_E, rows * (size_t)s->pitch * sizeof(float)));
+    MARS_CUDA_TRY(cudaMemsetAsync(s->d_E, 0, rows * (size_t)s->pitch * sizeof(float), s->stream));
+    MARS_CUDA_TRY(cudaMalloc(&s->d_ts, rows * sizeof(float)));
+    MARS_CUDA_TRY(cudaMemsetAsync(s->d_ts, 0, rows * sizeof(float), s->stream));
+    MARS_CUDA_TRY(cudaMalloc(&s->d_imp, rows * sizeof(float)));
+    if (rows > 0) {
+        fill_f32_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s->stream>>>(s->d_imp, (int64_t)rows, 1.0f);
+        MARS_CUDA_TRY(cudaGetLastError());
+    }
+    MARS_CUDA_TRY(cudaMalloc(&s->d_mod, rows * sizeof(int32_t)));
+    MARS_CUDA_TRY(cudaMemsetAsync(s->d_mod, 0, rows * sizeof(int32_t), s->stream));
+    MARS_CUDA_TRY(cudaMalloc(&s->d_n, sizeof(int32_t)));
+    MARS_CUDA_TRY(cudaMemsetAsync(s->d_n, 0, sizeof(int32_t), s->stream));
+    if (s->edge_slack > 0) {
+        MARS_CUDA_TRY(cudaMalloc(&s->d_extra, rows * (size_t)s->edge_slack * sizeof(int32_t)));
+        MARS_CUDA_TRY(cudaMalloc(&s->d_extra_cnt, rows * sizeof(int32_t)));
+        MARS_CUDA_TRY(cudaMemsetAsync(s->d_extra_cnt, 0, rows * sizeof(int32_t), s->stream));
+        s->h_extra_cnt.assign(rows, 0);
+    }
+    MARS_CUDA_TRY(cudaEventRecord(s->written, s->stream));
+    return MARS_OK;
+}
+
+static void release_store(mars_store* s) {
+    if (s->owns) {
+        cudaFree(s->d_E);
+        cudaFree(s->d_ts);
+        cudaFree(s->d_imp);
+        cudaFree(s->d_mod);
+        cudaFree(s->d_row_offsets);
+        cudaFree(s->d_col_indices);
+    }
+    cudaFree(s->d_n);
+    cudaFree(s->d_extra);
+    cudaFree(s->d_extra_cnt);
+    if (s->written) cudaEventDestroy(s->written);
+    if (s->stream) cudaStreamDestroy(s->stream);
+}
+
+extern "C" {
+
+const char* mars_last_error(void) { return g_last_error.c_str(); }
+
+const char* mars_status_string(int status) {
+    switch (status) {
+    case MARS_OK: return "ok";
+    case MARS_ERR_INVALID: return "invalid argument";
+    case MARS_ERR_CUDA: return "CUDA error";
+    case MARS_ERR_OOM: return "out of memory";
+    case MARS_ERR_CAPACITY: return "capacity exceeded";
+    case MARS_ERR_UNSUPPORTED: return "unsupported";
+    case MARS_ERR_TIMEOUT: return "device wait timed out";
+    case MARS_ERR_NO_DEVICE: return "no sm_100 device";
+    case MARS_ERR_DEVICE: return "device-side check failed";
+    default: return "unknown status";
+    }
+}
+
+int mars_abi_version(void) { return MARS_B200_ABI_VERSION; }
+
+int mars_store_create(int32_t device, int32_t capacity, int32_t dim, int32_t edge_slack,
+                      mars_store** out) {
+    if (out == nullptr) return fail(MARS_ERR_INVALID, "mars_store_create: out is NULL");
+    *out = nullptr;
+    if (capacity < 0 || dim <= 0 || dim > 1024 || edge_slack < 0)
+        return fail(MARS_ERR_INVALID, "mars_store_create: need capacity >= 0, 0 < dim <= 1024, edge_slack >= 0");
+    int ndev = 0;
+    if (cudaGetDeviceCount(&ndev) != cudaSuccess || device < 0 || device >= ndev)
+        return fail(MARS_ERR_NO_DEVICE, "mars_store_create: no such CUDA device");
+    MarsDeviceGuard g(device);
+    if (!g.ok) return fail(MARS_ERR_CUDA, "mars_store_create: cudaSetDevice failed");
+    mars_store* s = new mars_store();
+    s->device = device;
+    s->capacity = capacity;
+    s->dim = dim;
+    s->pitch = (dim + 3) & ~3;
+    s->edge_slack = edge_slack;
+    int st = MARS_OK;
+    if (cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&s->written, cudaEventDisableTiming) != cudaSuccess) {
+        st = fail(MARS_ERR_CUDA, "mars_store_create: stream/event creation failed");
+    } else {
+        st = alloc_store(s);
+    }
+    if (st == MARS_OK) st = (cudaStreamSynchronize(s->stream) == cudaSuccess)
+                                ? MARS_OK : fail(MARS_ERR_CUDA, "mars_store_create: initialisation failed");
+    if (st != MARS_OK) {
+        release_store(s);
+        delete s;
+        return st;
+    }
+    *out = s;
+    return MARS_OK;
+}
+
+int mars_store_upload(mars_store* s, int32_t n, const float* embeddings, const int32_t* modalities,
+                      const float* timestamps, const float* importance, const int32_t* row_offsets,
+                      const int32_t* col_indices, int32_t num_edges) {
+    if (s == nullptr) return fail(MARS_ERR_INVALID, "mars_store_upload: store is NULL");
+    if (n < 0 || n > s->capacity)
+        return fail(MARS_ERR_CAPACITY, "mars_store_upload: n exceeds the store capacity");
+    if (n > 0 && (embeddings == nullptr || modalities == nullptr || timestamps == nullptr))
+        return fail(MARS_ERR_INVALID, "mars_store_upload: embeddings, modalities and timestamps are required");
+    if (row_offsets != nullptr && (num_edges < 0 || (num_edges > 0 && col_indices == nullptr)))
+        return fail(MARS_ERR_INVALID, "mars_store_upload: bad CSR arguments");
+    if (!s->owns) return fail(MARS_ERR_INVALID, "mars_store_upload: store wraps caller memory");
+    MarsDeviceGuard g(s->device);
+    cudaStream_t st = s->stream;
+    const size_t D = (size_t)s->dim, P = (size_t)s->pitch;
+    if (n > 0) {
+        MARS_CUDA_TRY(cudaMemcpy2DAsync(s->d_E, P * sizeof(float), embeddings, D * sizeof(float),
+                                        D * sizeof(float), (size_t)n, cudaMemcpyDefault, st));
+        MARS_CUDA_TRY(cudaMemcpyAsync(s->d_mod, modalities, (size_t)n * 4, cudaMemcpyDefault, st));
+        MARS_CUDA_TRY(cudaMemcpyAsync(s->d_ts, timestamps, (size_t)n * 4, cudaMemcpyDefault, st));
+        if (importance != nullptr) {
+            MARS_CUDA_TRY(cudaMemcpyAsync(s->d_imp, importance, (size_t)n * 4, cudaMemcpyDefault, st));
+        } else {
+            fill_f32_kernel<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(s->d_imp, n, 1.0f);
+            MARS_CUDA_TRY(cudaGetLastError());
+        }
+    }
+    // graph
+    if (row_offsets != nullptr) {
+        if (s->d_row_offsets == nullptr || s->csr_n < n) {
+            cudaFree(s->d_row_offsets);
+            s->d_row_offsets = nullptr;
+            MARS_CUDA_TRY(cudaMalloc(&s->d_row_offsets, ((size_t)n + 1) * sizeof(int32_t)));
+        }
+        if (s->d_col_indices == nullptr || s->csr_edge_cap < num_edges) {
+            cudaFree(s->d_col_indices);
+            s->d_col_indices = nullptr;
+            MARS_CUDA_TRY(cudaMalloc(&s->d_col_indices, (size_t)std::max(num_edges, 1) * sizeof(int32_t)));
+            s->csr_edge_cap = std::max(num_edges, 1);
+        }
+        MARS_CUDA_TRY(cudaMemcpyAsync(s->d_row_offsets, row_offsets, ((size_t)n + 1) * 4, cudaMemcpyDefault, st));
+        if (num_edges > 0)
+            MARS_CUDA_TRY(cudaMemcpyAsync(s->d_col_indices, col_indices, (size_t)num_edges * 4, cudaMemcpyDefault, st));
+        s->csr_n = n;
+        s->num_edges = num_edges;
+    } else {
+        s->csr_n = 0;
+        s->num_edges = 0;
+    }
+    if (s->edge_slack > 0) {
+        MARS_CUDA_TRY(cudaMemsetAsync(s->d_extra_cnt, 0, (size_t)s->capacity * 4, st));
+        std::fill(s->h_extra_cnt.begin(), s->h_extra_cnt.end(), 0);
+    }
+    MARS_CUDA_TRY(cudaMemcpyAsync(s->d_n, &n, sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    MARS_CUDA_TRY(cudaStreamSynchronize(st));   // n lives on this stack frame
+    s->n = n;
+    MARS_CUDA_TRY(cudaEventRecord(s->written, st));
+    return MARS_OK;
+}
+
+int mars_store_append(mars_store* s, int32_t n, const float* embeddings, const int32_t* modalities,
+                      const float* timestamps, const float* importance, int32_t normalize,
+                      int32_t* first_id) {
+    if (s == nullptr) return fail(MARS_ERR_INVALID, "mars_store_append: store is NULL");
+    if (n < 0) return fail(MARS_ERR_INVALID, "mars_store_append: n < 0");
+    if (n > 0 && (embeddings == nullptr || modalities == nullptr || timestamps == nullptr))
+        return fail(MARS_ERR_INVALID, "mars_store_append: embeddings, modalities and timestamps are required");
+    if (!s->owns) return fail(MARS_ERR_INVALID, "mars_store_append: store wraps caller memory");
+    if ((int64_t)s->n + n > s->capacity)
+        return fail(MARS_ERR_CAPACITY, "mars_store_append: store is full (capacity " +
+                                           std::to_string(s->capacity) + ")");
+    if (first_id) *first_id = s->n;
+    if (n == 0) return MARS_OK;
+    MarsDeviceGuard g(s->device);
+    cudaStream_t st = s->stream;
+    const size_t D = (size_t)s->dim, P = (size_t)s->pitch;
+    const int32_t first = s->n;
+    MARS_CUDA_TRY(cudaMemcpy2DAsync(s->d_E + (size_t)first * P, P * sizeof(float), embeddings,
+                                    D * sizeof(float), D * sizeof(float), (size_t)n,
+                                    cudaMemcpyDefault, st));
+    if (normalize) {
+        const int threads = 256;
+        const int blocks = (int)(((int64_t)n * 32 + threads - 1) / threads);
+        normalize_rows_kernel<<<blocks, threads, 0, st>>>(s->d_E, (int64_t)P, first, n, s->dim);
+        MARS_CUDA_TRY(cudaGetLastError());
+    }
+    MARS_CUDA_TRY(cudaMemcpyAsync(s->d_mod + first, modalities, (size_t)n * 4, cudaMemcpyDefault, st));
+    MARS_CUDA_TRY(cudaMemcpyAsync(s->d_ts + first, timestamps, (size_t)n * 4, cudaMemcpyDefault, st));
+    if (importance != nullptr)
+        MARS_CUDA_TRY(cudaMemcpyAsync(s->d_imp + first, importance, (size_t)n * 4, cudaMemcpyDefault, st));
+    // publish the new count after the rows (same stream)
+    const int32_t new_n = first + n;
+    MARS_CUDA_TRY(cudaMemcpyAsync(s->d_n, &new_n, sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    MARS_CUDA_TRY(cudaStreamSynchronize(st));   // new_n and caller buffers live on the host
+    s->n = new_n;
+    MARS_CUDA_TRY(cudaEventRecord(s->written, st));
+    return MARS_OK;
+}
+
+int mars_store_append_edges(mars_store* s, int32_t n, const int32_t* src, const int32_t* dst) {
+    if (s == nullptr) return fail(MARS_ERR_INVALID, "mars_store_append_edges: store is NULL");
+    if (n < 0 || (n > 0 && (src == nullptr || dst == nullptr)))
+        return fail(MARS_ERR_INVALID, "mars_store_append_edges: bad arguments");
+    if (n == 0) return MARS_OK;
+    if (s->edge_slack <= 0)
+        return fail(MARS_ERR_CAPACITY, "mars_store_append_edges: store was created with edge_slack 0");
+    // plan on the host (deterministic slot order = call order), then scatter
+    std::vector<int32_t> slot(n), fin(n), cnt_after;
+    std::vector<int32_t> local = s->h_extra_cnt;
+    for (int32_t i = 0; i < n; ++i) {
+        const int32_t u = src[i], v = dst[i];
+        if (u < 0 || u >= s->n || v < 0 || v >= s->n)
+            return fail(MARS_ERR_INVALID, "mars_store_append_edges: endpoint out of range");
+        if (local[u] >= s->edge_slack)
+            return fail(MARS_ERR_CAPACITY, "mars_store_append_edges: node " + std::to_string(u) +
+                                               " has no free neighbour slot");
+        slot[i] = u * s->edge_slack + local[u];
+        local[u] += 1;
+    }
+    for (int32_t i = 0; i < n; ++i) fin[i] = local[src[i]];
+    MarsDeviceGuard g(s->device);
+    cudaStream_t st = s->stream;
+    int32_t* d_tmp = nullptr;
+    MARS_CUDA_TRY(cudaMallocAsync(&d_tmp, (size_t)n * 4 * 4, st));
+    int rc = MARS_OK;
+    do {
+        if (cudaMemcpyAsync(d_tmp, slot.data(), (size_t)n * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(d_tmp + n, dst, (size_t)n * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(d_tmp + 2 * (size_t)n, src, (size_t)n * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+            cudaMemcpyAsync(d_tmp + 3 * (size_t)n, fin.data(), (size_t)n * 4, cudaMemcpyHostToDevice, st) != cudaSuccess) {
+            rc = fail(MARS_ERR_CUDA, "mars_store_append_edges: copy failed");
+            break;
+        }
+        scatter_edges_kernel<<<(n + 255) / 256, 256, 0, st>>>(s->d_extra, s->d_extra_cnt, d_tmp, d_tmp + n,
+                                                               d_tmp + 2 * (size_t)n, d_tmp + 3 * (size_t)n, n);
+        if (cudaGetLastError() != cudaSuccess) { rc = fail(MARS_ERR_CUDA, "mars_store_append_edges: launch failed"); break; }
+    } while (0);
+    cudaFreeAsync(d_tmp, st);
+    MARS_CUDA_TRY(cudaStreamSynchronize(st));
+    if (rc != MARS_OK) return rc;
+    s->h_extra_cnt.swap(local);
+    MARS_CUDA_TRY(cudaEventRecord(s->written, st));
+    return MARS_OK;
+}
+
+int mars_store_set_importance(mars_store* s, int32_t first, int32_t n, const float* importance) {
+    if (s == nullptr || importance == nullptr || first < 0 || n < 0 || (int64_t)first + n > s->capacity)
+        return fail(MARS_ERR_INVALID, "mars_store_set_importance: bad arguments");
+    if (n == 0) return MARS_OK;
+    MarsDeviceGuard g(s->device);
+    MARS_CUDA_TRY(cudaMemcpyAsync(s->d_imp + first, importance, (size_t)n * 4, cudaMemcpyDefault, s->stream));
+    MARS_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    MARS_CUDA_TRY(cudaEventRecord(s->written, s->stream));
+    return MARS_OK;
+}
+
+int mars_store_info_get(const mars_store* s, mars_store_info* out) {
+    if (s == nullptr || out == nullptr) return fail(MARS_ERR_INVALID, "mars_store_info_get: NULL argument");
+    out->device = s->device;
+    out->num_nodes = s->n;
+    out->capacity = s->capacity;
+    out->embedding_dim = s->dim;
+    out->row_pitch = s->pitch;
+    out->num_edges = s->num_edges;
+    out->csr_nodes = s->csr_n;
+    out->edge_slack = s->edge_slack;
+    out->d_embeddings = s->d_E;
+    out->d_modalities = s->d_mod;
+    out->d_timestamps = s->d_ts;
+    out->d_importance = s->d_imp;
+    out->d_row_offsets = s->d_row_offsets;
+    out->d_col_indices = s->d_col_indices;
+    out->d_num_nodes = s->d_n;
+    return MARS_OK;
+}
+
+int mars_store_read(const mars_store* s, int32_t first, int32_t n, float* embeddings,
+                    int32_t* modalities, float* timestamps, float* importance) {
+    if (s == nullptr || first < 0 || n < 0 || (int64_t)first + n > s->n)
+        return fail(MARS_ERR_INVALID, "mars_store_read: rows out of range");
+    if (n == 0) return MARS_OK;
+    MarsDeviceGuard g(s->device);
+    cudaStream_t st = s->stream;
+    const size_t D = (size_t)s->dim, P = (size_t)s->pitch;
+    if (embeddings)
+        MARS_CUDA_TRY(cudaMemcpy2DAsync(embeddings, D * 4, s->d_E + (size_t)first * P, P * 4, D * 4,
+                                        (size_t)n, cudaMemcpyDefault, st));
+    if (modalities) MARS_CUDA_TRY(cudaMemcpyAsync(modalities, s->d_mod + first, (size_t)n * 4, cudaMemcpyDefault, st));
+    if (timestamps) MARS_CUDA_TRY(cudaMemcpyAsync(timestamps, s->d_ts + first, (size_t)n * 4, cudaMemcpyDefault, st));
+    if (importance) MARS_CUDA_TRY(cudaMemcpyAsync(importance, s->d_imp + first, (size_t)n * 4, cudaMemcpyDefault, st));
+    MARS_CUDA_TRY(cudaStreamSynchronize(st));
+    return MARS_OK;
+}
+
+int mars_store_destroy(mars_store* s) {
+    if (s == nullptr) return MARS_OK;
+    MarsDeviceGuard g(s->device);
+    if (s->stream) cudaStreamSynchronize(s->stream);
+    release_store(s);
+    delete s;
+    return MARS_OK;
+}
+
+}  // extern "C"

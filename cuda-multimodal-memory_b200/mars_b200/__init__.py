@@ -1,0 +1,316 @@
+"""Python binding of the MARS B200 C ABI (include/mars_b200.h).
+
+A thin ctypes layer for tests, benchmarks and Python callers.  All compute
+runs in lib/libmars_b200.so; importing this module fails loudly when that
+library has not been built, and there is no CPU fallback.
+
+Device buffers may be passed as torch tensors (their data_ptr is used) or as
+raw integer addresses.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+
+import numpy as np
+
+_PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(_PKG, "lib", "libmars_b200.so")
+
+MARS_OK = 0
+MARS_ERR_INVALID = 1
+MARS_ERR_CUDA = 2
+MARS_ERR_OOM = 3
+MARS_ERR_CAPACITY = 4
+MARS_ERR_UNSUPPORTED = 5
+MARS_ERR_TIMEOUT = 6
+MARS_ERR_NO_DEVICE = 7
+MARS_ERR_DEVICE = 8
+MAX_TOP_K = 128
+MAX_BFS_HOPS = 14
+
+RESULT_DTYPE = np.dtype([("node_id", "<i4"), ("score", "<f4"), ("modality", "<i4"),
+                         ("hops", "<i4")])
+
+
+class MarsError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"[{status}] {msg}")
+        self.status = status
+
+
+class RetrievalConfig(C.Structure):
+    """mars_retrieval_config (RetrievalConfig, include/memory_cuda.cuh:92-99)."""
+    _fields_ = [("top_k", C.c_int32), ("bfs_max_hops", C.c_int32),
+                ("time_decay_lambda", C.c_float), ("bfs_score_decay", C.c_float),
+                ("modality_filter", C.c_int32), ("use_importance", C.c_int32)]
+
+    def __init__(self, top_k=10, bfs_max_hops=2, time_decay_lambda=1e-8, bfs_score_decay=0.5,
+                 modality_filter=-1, use_importance=False):
+        super().__init__(top_k, bfs_max_hops, time_decay_lambda, bfs_score_decay,
+                         modality_filter, int(use_importance))
+
+
+class RetrievalStats(C.Structure):
+    _fields_ = [("gpu_ms_similarity", C.c_float), ("gpu_ms_topk", C.c_float),
+                ("gpu_ms_bfs", C.c_float), ("gpu_ms_rerank", C.c_float),
+                ("gpu_ms_total", C.c_float), ("nodes_scanned", C.c_int32),
+                ("bfs_waves", C.c_int32), ("nodes_visited", C.c_int32)]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
+class StoreInfo(C.Structure):
+    _fields_ = [("device", C.c_int32), ("num_nodes", C.c_int32), ("capacity", C.c_int32),
+                ("embedding_dim", C.c_int32), ("row_pitch", C.c_int32), ("num_edges", C.c_int32),
+                ("csr_nodes", C.c_int32), ("edge_slack", C.c_int32),
+                ("d_embeddings", C.c_void_p), ("d_modalities", C.c_void_p),
+                ("d_timestamps", C.c_void_p), ("d_importance", C.c_void_p),
+                ("d_row_offsets", C.c_void_p), ("d_col_indices", C.c_void_p),
+                ("d_num_nodes", C.c_void_p)]
+
+
+_VP = C.c_void_p
+_I32 = C.c_int32
+_F32 = C.c_float
+
+# name -> argtypes (all return int status unless listed in _RESTYPE)
+_SIGS = {
+    "mars_store_create": [_I32, _I32, _I32, _I32, C.POINTER(_VP)],
+    "mars_store_upload": [_VP, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _I32],
+    "mars_store_append": [_VP, _I32, _VP, _VP, _VP, _VP, _I32, C.POINTER(_I32)],
+    "mars_store_append_edges": [_VP, _I32, _VP, _VP],
+    "mars_store_set_importance": [_VP, _I32, _I32, _VP],
+    "mars_store_info_get": [_VP, C.POINTER(StoreInfo)],
+    "mars_store_read": [_VP, _I32, _I32, _VP, _VP, _VP, _VP],
+    "mars_store_destroy": [_VP],
+    "mars_query_ctx_create": [_I32, _I32, _I32, _I32, C.POINTER(_VP)],
+    "mars_query_ctx_destroy": [_VP],
+    "mars_query_ctx_use_graph": [_VP, _I32],
+    "mars_query": [_VP, _VP, _VP, _F32, C.POINTER(RetrievalConfig), _VP, C.POINTER(_I32),
+                   C.POINTER(RetrievalStats)],
+    "mars_query_device": [_VP, _VP, _VP, _F32, C.POINTER(RetrievalConfig), _VP, _VP, _VP],
+    "mars_query_once": [_VP, _VP, _F32, C.POINTER(RetrievalConfig), _VP, C.POINTER(_I32),
+                        C.POINTER(RetrievalStats)],
+    "mars_scan_topk": [_VP, _VP, _VP, _F32, _F32, _I32, _I32, _I32, _I32, _VP, _VP, _VP, _VP],
+    "mars_topk_merge": [_VP, _VP, _VP, _I32, _I32, _VP, _VP, _VP, _VP],
+    "mars_topk_merge_batch": [_VP, _VP, _VP, _I32, _I32, _I32, _VP, _VP, _VP, _VP],
+    "mars_debug_fused_scores": [_VP, _VP, _VP, _F32, _F32, _I32, _I32, _VP, _VP],
+}
+_RESTYPE = {"mars_last_error": C.c_char_p, "mars_status_string": C.c_char_p,
+            "mars_abi_version": C.c_int, "mars_query_ctx_stream": C.c_void_p}
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    """Load lib/libmars_b200.so (raises if it is missing: no fallback)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise ImportError(f"MARS B200 library not built: {LIB_PATH} "
+                              "(run `make -C cuda-multimodal-memory_b200`)")
+        L = C.CDLL(LIB_PATH)
+        for name, args in _SIGS.items():
+            f = getattr(L, name)
+            f.argtypes = args
+            f.restype = C.c_int
+        for name, rt in _RESTYPE.items():
+            getattr(L, name).restype = rt
+        L.mars_status_string.argtypes = [C.c_int]
+        L.mars_query_ctx_stream.argtypes = [_VP]
+        _lib = L
+    return _lib
+
+
+def exported_symbols():
+    return sorted(list(_SIGS) + list(_RESTYPE))
+
+
+def _check(status: int):
+    if status != MARS_OK:
+        raise MarsError(status, lib().mars_last_error().decode())
+
+
+def _ptr(x):
+    """Device/host address of a torch tensor, numpy array, int or None."""
+    if x is None:
+        return None
+    if isinstance(x, int):
+        return x
+    if isinstance(x, np.ndarray):
+        return x.ctypes.data
+    if hasattr(x, "data_ptr"):
+        return x.data_ptr()
+    raise TypeError(f"cannot take the address of {type(x)}")
+
+
+def _host(a, dtype):
+    return None if a is None else np.ascontiguousarray(a, dtype=dtype)
+
+
+class Store:
+    """Device store (DeviceMemoryGraph) with in-place streaming append."""
+
+    def __init__(self, capacity: int, dim: int, device: int = 0, edge_slack: int = 0):
+        h = C.c_void_p()
+        _check(lib().mars_store_create(device, capacity, dim, edge_slack, C.byref(h)))
+        self.handle = h
+        self.device = device
+        self.dim = dim
+        self._keep = []
+
+    def upload(self, E, modalities, timestamps, importance=None, row_offsets=None,
+               col_indices=None):
+        """E etc. may be numpy arrays (host) or torch tensors (host or device)."""
+        keep = []
+
+        def prep(a, dt):
+            if a is None:
+                return None
+            if isinstance(a, np.ndarray) or not hasattr(a, "data_ptr"):
+                a = _host(a, dt)
+            keep.append(a)
+            return _ptr(a)
+        n = int(E.shape[0])
+        ne = 0 if col_indices is None else int(col_indices.shape[0])
+        _check(lib().mars_store_upload(self.handle, n, prep(E, np.float32),
+                                       prep(modalities, np.int32), prep(timestamps, np.float32),
+                                       prep(importance, np.float32),
+                                       prep(row_offsets, np.int32), prep(col_indices, np.int32),
+                                       ne))
+
+    def append(self, E, modalities, timestamps, importance=None, normalize=True) -> int:
+        E = _host(E, np.float32) if not hasattr(E, "data_ptr") else E
+        mod = _host(modalities, np.int32) if not hasattr(modalities, "data_ptr") else modalities
+        ts = _host(timestamps, np.float32) if not hasattr(timestamps, "data_ptr") else timestamps
+        imp = importance
+        if imp is not None and not hasattr(imp, "data_ptr"):
+            imp = _host(imp, np.float32)
+        first = C.c_int32()
+        _check(lib().mars_store_append(self.handle, int(E.shape[0]), _ptr(E), _ptr(mod), _ptr(ts),
+                                       _ptr(imp), int(normalize), C.byref(first)))
+        return first.value
+
+    def append_edges(self, src, dst):
+        src = _host(src, np.int32)
+        dst = _host(dst, np.int32)
+        _check(lib().mars_store_append_edges(self.handle, src.shape[0], _ptr(src), _ptr(dst)))
+
+    def set_importance(self, first, importance):
+        imp = importance if hasattr(importance, "data_ptr") else _host(importance, np.float32)
+        _check(lib().mars_store_set_importance(self.handle, first, int(imp.shape[0]), _ptr(imp)))
+
+    def read(self, first=0, n=None):
+        """Rows [first, first+n) back on the host: (E, modalities, ts, importance)."""
+        if n is None:
+            n = self.num_nodes - first
+        E = np.empty((n, self.dim), np.float32)
+        mod = np.empty(n, np.int32)
+        ts = np.empty(n, np.float32)
+        imp = np.empty(n, np.float32)
+        _check(lib().mars_store_read(self.handle, first, n, _ptr(E), _ptr(mod), _ptr(ts), _ptr(imp)))
+        return E, mod, ts, imp
+
+    def info(self) -> StoreInfo:
+        i = StoreInfo()
+        _check(lib().mars_store_info_get(self.handle, C.byref(i)))
+        return i
+
+    @property
+    def num_nodes(self) -> int:
+        return self.info().num_nodes
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().mars_store_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class QueryContext:
+    """Query scratch (QueryContext) bound to a device."""
+
+    def __init__(self, max_nodes: int, dim: int, max_k: int = 64, device: int = 0,
+                 use_graph: bool = True):
+        h = C.c_void_p()
+        _check(lib().mars_query_ctx_create(device, max_nodes, dim, max_k, C.byref(h)))
+        self.handle = h
+        self.device = device
+        self.dim = dim
+        if not use_graph:
+            _check(lib().mars_query_ctx_use_graph(self.handle, 0))
+
+    @property
+    def stream(self) -> int:
+        return lib().mars_query_ctx_stream(self.handle)
+
+    def query(self, store: Store, q, t_q: float, cfg: RetrievalConfig | None = None,
+              with_stats: bool = False):
+        """query_memory_fast: host (numpy) or device (torch) query -> numpy results."""
+        cfg = cfg or RetrievalConfig()
+        qa = q if hasattr(q, "data_ptr") else _host(q, np.float32)
+        out = np.zeros(max(cfg.top_k, 1), dtype=RESULT_DTYPE)
+        n = C.c_int32()
+        st = RetrievalStats()
+        _check(lib().mars_query(store.handle, self.handle, _ptr(qa), float(t_q), C.byref(cfg),
+                                out.ctypes.data, C.byref(n),
+                                C.byref(st) if with_stats else None))
+        res = out[:n.value]
+        return (res, st.as_dict()) if with_stats else res
+
+    def query_device(self, store: Store, d_query, t_q, cfg, d_out, d_count, stream=None):
+        _check(lib().mars_query_device(store.handle, self.handle, _ptr(d_query), float(t_q),
+                                       C.byref(cfg), _ptr(d_out), _ptr(d_count), stream))
+
+    def scan_topk(self, store: Store, d_query, t_q, lam, K, d_ids, d_vals, d_count=None,
+                  modality_filter=-1, use_importance=False, row_offset=0, stream=None):
+        _check(lib().mars_scan_topk(store.handle, self.handle, _ptr(d_query), float(t_q),
+                                    float(lam), modality_filter, int(use_importance), K,
+                                    row_offset, _ptr(d_ids), _ptr(d_vals), _ptr(d_count), stream))
+
+    def topk_merge(self, d_ids_in, d_vals_in, n_lists, K, d_ids_out, d_vals_out, d_count=None,
+                   stream=None):
+        _check(lib().mars_topk_merge(self.handle, _ptr(d_ids_in), _ptr(d_vals_in), n_lists, K,
+                                     _ptr(d_ids_out), _ptr(d_vals_out), _ptr(d_count), stream))
+
+    def topk_merge_batch(self, d_ids_in, d_vals_in, n_lists, K, Q, d_ids_out, d_vals_out,
+                         d_counts=None, stream=None):
+        _check(lib().mars_topk_merge_batch(self.handle, _ptr(d_ids_in), _ptr(d_vals_in), n_lists,
+                                           K, Q, _ptr(d_ids_out), _ptr(d_vals_out),
+                                           _ptr(d_counts), stream))
+
+    def debug_fused_scores(self, store: Store, d_query, t_q, lam, d_out, modality_filter=-1,
+                           use_importance=False, stream=None):
+        _check(lib().mars_debug_fused_scores(store.handle, self.handle, _ptr(d_query), float(t_q),
+                                             float(lam), modality_filter, int(use_importance),
+                                             _ptr(d_out), stream))
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().mars_query_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def query_once(store: Store, q, t_q, cfg: RetrievalConfig | None = None):
+    """query_memory (no persistent context)."""
+    cfg = cfg or RetrievalConfig()
+    qa = _host(q, np.float32)
+    out = np.zeros(max(cfg.top_k, 1), dtype=RESULT_DTYPE)
+    n = C.c_int32()
+    _check(lib().mars_query_once(store.handle, _ptr(qa), float(t_q), C.byref(cfg),
+                                 out.ctypes.data, C.byref(n), None))
+    return out[:n.value]

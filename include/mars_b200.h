@@ -1,0 +1,245 @@
+/*
+ * mars_b200.h -- C ABI of the B200-native MARS retrieval path.
+ *
+ * This is the drop-in boundary.  Every entry point takes plain pointers and
+ * sizes, returns an int status (MARS_OK or MARS_ERR_*), never exits the
+ * process, and never falls back to CPU code.  Each declaration names the
+ * reference interface it replaces (paths relative to the root of
+ * antonellof/cuda-multimodal-memory).  The reference's C++ API
+ * (memory_cuda.cuh, cmng.cuh) is provided on top of this ABI by the same
+ * library, so reference callers relink unchanged.
+ *
+ * Pointer arguments documented as "host or device" may point to pageable or
+ * pinned host memory or to device memory of the store's GPU (the library
+ * copies with cudaMemcpyDefault).  Streams are passed as void* (a
+ * cudaStream_t); NULL means the object's own stream.
+ *
+ * Threading: like the reference's QueryContext (include/memory_cuda.cuh:122),
+ * a context or store must not be used by two host threads at once.
+ */
+#ifndef MARS_B200_H
+#define MARS_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define MARS_B200_ABI_VERSION 1
+#define MARS_MAX_TOP_K 128      /* reference: MAX_TOP_K = 64 (src/memory_cuda.cu:38) */
+#define MARS_MAX_BFS_HOPS 14
+
+/* ---- status ------------------------------------------------------------ */
+enum {
+    MARS_OK              = 0,
+    MARS_ERR_INVALID     = 1,   /* bad argument                              */
+    MARS_ERR_CUDA        = 2,   /* CUDA runtime error                        */
+    MARS_ERR_OOM         = 3,   /* device or pinned allocation failed        */
+    MARS_ERR_CAPACITY    = 4,   /* store / context / edge slack exhausted    */
+    MARS_ERR_UNSUPPORTED = 5,   /* shape or option not supported             */
+    MARS_ERR_TIMEOUT     = 6,   /* a bounded device-side wait gave up        */
+    MARS_ERR_NO_DEVICE   = 7,   /* no usable sm_100 device                   */
+    MARS_ERR_DEVICE      = 8    /* a device-side check set the error flag    */
+};
+
+/* Message of the last failure on the calling thread (never NULL). */
+const char* mars_last_error(void);
+const char* mars_status_string(int status);
+int         mars_abi_version(void);
+
+/* ---- value types (binary layout of the reference structs) ------------- */
+
+/* QueryResult, include/memory_cuda.cuh:85-90 */
+typedef struct mars_query_result {
+    int32_t node_id;
+    float   score;
+    int32_t modality;
+    int32_t hops_from_seed;
+} mars_query_result;
+
+/* RetrievalConfig, include/memory_cuda.cuh:92-99 (bool use_importance is
+ * widened to int32 for a stable C layout). */
+typedef struct mars_retrieval_config {
+    int32_t top_k;
+    int32_t bfs_max_hops;
+    float   time_decay_lambda;
+    float   bfs_score_decay;
+    int32_t modality_filter;
+    int32_t use_importance;
+} mars_retrieval_config;
+
+/* RetrievalStats, include/memory_cuda.cuh:101-109, plus the device counts
+ * of this implementation. */
+typedef struct mars_retrieval_stats {
+    float   gpu_ms_similarity;   /* fused scan + top-K                      */
+    float   gpu_ms_topk;         /* 0: top-K is fused into the scan          */
+    float   gpu_ms_bfs;          /* BFS hops + final selection               */
+    float   gpu_ms_rerank;       /* 0: decay is fused into the scan          */
+    float   gpu_ms_total;
+    int32_t nodes_scanned;
+    int32_t bfs_waves;
+    int32_t nodes_visited;       /* seeds + BFS-discovered nodes             */
+} mars_retrieval_stats;
+
+/* ---- device store: DeviceMemoryGraph (include/memory_cuda.cuh:60-75) --- */
+typedef struct mars_store mars_store;
+
+typedef struct mars_store_info {
+    int32_t  device;
+    int32_t  num_nodes;        /* current N                                   */
+    int32_t  capacity;         /* rows allocated                              */
+    int32_t  embedding_dim;    /* D                                           */
+    int32_t  row_pitch;        /* floats between rows (D rounded up to 4)      */
+    int32_t  num_edges;        /* CSR edges                                   */
+    int32_t  csr_nodes;        /* nodes covered by the CSR                    */
+    int32_t  edge_slack;       /* append-only neighbour slots per node        */
+    float*   d_embeddings;     /* capacity x row_pitch, zero padded           */
+    int32_t* d_modalities;
+    float*   d_timestamps;
+    float*   d_importance;     /* initialised to 1                            */
+    int32_t* d_row_offsets;    /* csr_nodes + 1 (NULL without a graph)        */
+    int32_t* d_col_indices;
+    int32_t* d_num_nodes;      /* device copy of N read by every kernel       */
+} mars_store_info;
+
+/* Allocate an empty store with room for `capacity` rows of dimension `dim`
+ * on `device`, and `edge_slack` append-only neighbour slots per node.
+ * Replaces the allocation half of upload_to_device
+ * (include/memory_cuda.cuh:77, src/memory_cuda.cu:593-616). */
+int mars_store_create(int32_t device, int32_t capacity, int32_t dim,
+                      int32_t edge_slack, mars_store** out);
+
+/* Replace the contents with n rows (host or device pointers) and an
+ * optional CSR graph over them (row_offsets may be NULL).  importance may be
+ * NULL (all 1).  Embeddings are taken as given, like upload_to_device.
+ * Replaces the copy half of upload_to_device (src/memory_cuda.cu:599-615). */
+int mars_store_upload(mars_store* s, int32_t n, const float* embeddings,
+                      const int32_t* modalities, const float* timestamps,
+                      const float* importance, const int32_t* row_offsets,
+                      const int32_t* col_indices, int32_t num_edges);
+
+/* Streaming insert: append n rows in place (no rebuild, no re-upload).
+ * With normalize != 0 each row is divided by (sqrt(sum x^2) + 1e-8), summed
+ * sequentially in fp32 exactly as engine_server's add_node
+ * (src/engine_server.cu:154-176); the reference instead grows host vectors
+ * and re-uploads the whole corpus (src/engine_server.cu:188-213).
+ * first_id (may be NULL) receives the id of the first appended row. */
+int mars_store_append(mars_store* s, int32_t n, const float* embeddings,
+                      const int32_t* modalities, const float* timestamps,
+                      const float* importance, int32_t normalize,
+                      int32_t* first_id);
+
+/* Append n directed edges src[i] -> dst[i] (host arrays) to the per-node
+ * slack lists; MARS_ERR_CAPACITY if a node's slack is full (nothing is
+ * written then).  Replaces the periodic NSN rebuild of
+ * src/engine_server.cu:193-200 for incremental bridges. */
+int mars_store_append_edges(mars_store* s, int32_t n, const int32_t* src,
+                            const int32_t* dst);
+
+/* Overwrite importance weights of rows [first, first+n) (host or device). */
+int mars_store_set_importance(mars_store* s, int32_t first, int32_t n,
+                              const float* importance);
+
+int mars_store_info_get(const mars_store* s, mars_store_info* out);
+
+/* Copy rows [first, first+n) back to host arrays (any may be NULL): the
+ * embeddings as stored (n x dim), modalities, timestamps, importance. */
+int mars_store_read(const mars_store* s, int32_t first, int32_t n,
+                    float* embeddings, int32_t* modalities, float* timestamps,
+                    float* importance);
+
+/* free_device (include/memory_cuda.cuh:78).  NULL is accepted. */
+int mars_store_destroy(mars_store* s);
+
+/* ---- query context: QueryContext (include/memory_cuda.cuh:122-181) ---- */
+typedef struct mars_query_ctx mars_query_ctx;
+
+/* create_query_context (include/memory_cuda.cuh:183-184,
+ * src/memory_cuda.cu:789-854): scratch for stores of up to max_nodes rows,
+ * top-K up to max_k (<= MARS_MAX_TOP_K). */
+int mars_query_ctx_create(int32_t device, int32_t max_nodes, int32_t dim,
+                          int32_t max_k, mars_query_ctx** out);
+
+/* destroy_query_context (include/memory_cuda.cuh:185).  NULL is accepted. */
+int mars_query_ctx_destroy(mars_query_ctx* ctx);
+
+/* query_memory_fast (include/memory_cuda.cuh:188-194,
+ * src/memory_cuda.cu:1069-1158): fused score x decay [x importance] ->
+ * top-K seeds -> BFS over the store's graph -> best top_k visited nodes by
+ * (score desc, id asc).  query: host or device, D floats.  out: host array
+ * of cfg->top_k entries; *n_out receives the count.  stats may be NULL.
+ * Blocks until the results are on the host (like the reference). */
+int mars_query(const mars_store* s, mars_query_ctx* ctx, const float* query,
+               float query_timestamp, const mars_retrieval_config* cfg,
+               mars_query_result* out, int32_t* n_out,
+               mars_retrieval_stats* stats);
+
+/* Same pipeline, device in / device out, asynchronous on `stream` (NULL:
+ * the context's stream).  d_query: D floats on the device; d_out: top_k
+ * results; d_count: one int32.  Capturable in a CUDA graph once the first
+ * call with the same (store, top_k class, hops) has been made. */
+int mars_query_device(const mars_store* s, mars_query_ctx* ctx,
+                      const float* d_query, float query_timestamp,
+                      const mars_retrieval_config* cfg,
+                      mars_query_result* d_out, int32_t* d_count,
+                      void* stream);
+
+/* query_memory (include/memory_cuda.cuh:113-118): as mars_query with a
+ * temporary context. */
+int mars_query_once(const mars_store* s, const float* query,
+                    float query_timestamp, const mars_retrieval_config* cfg,
+                    mars_query_result* out, int32_t* n_out,
+                    mars_retrieval_stats* stats);
+
+/* Fused scan only (no BFS), device in / device out: top-K of
+ * dot(E_i, q) * __expf(-lambda * max(0, t_q - ts_i)) [* imp_i] over rows
+ * passing the modality filter, ranked (score desc, id asc), rows from
+ * `row_offset` on reported as row_offset + i.  d_ids / d_vals: K entries,
+ * unused tail = (-1, -inf); d_count: number found.  This is stages 1-3 of
+ * src/memory_cuda.cu:936-1021 (cublasSgemv -> temporal_rerank_kernel ->
+ * CUB radix sort) in one kernel. */
+int mars_scan_topk(const mars_store* s, mars_query_ctx* ctx,
+                   const float* d_query, float query_timestamp, float lambda,
+                   int32_t modality_filter, int32_t use_importance, int32_t K,
+                   int32_t row_offset, int32_t* d_ids, float* d_vals,
+                   int32_t* d_count, void* stream);
+
+/* Merge `n_lists` ranked lists of K (id, score) pairs that sit back to back
+ * in device memory (e.g. the gather buffer of an all-gather of per-shard
+ * mars_scan_topk results) into one ranked list of K.  Ties by id. */
+int mars_topk_merge(mars_query_ctx* ctx, const int32_t* d_ids_in,
+                    const float* d_vals_in, int32_t n_lists, int32_t K,
+                    int32_t* d_ids_out, float* d_vals_out, int32_t* d_count,
+                    void* stream);
+
+/* Batched form for Q queries: list l of query q starts at (l*Q + q)*K (the
+ * rank-major layout of an all-gather of per-rank [Q][K] buffers); outputs
+ * are [Q][K] and d_counts[Q] (may be NULL). */
+int mars_topk_merge_batch(mars_query_ctx* ctx, const int32_t* d_ids_in,
+                          const float* d_vals_in, int32_t n_lists, int32_t K,
+                          int32_t Q, int32_t* d_ids_out, float* d_vals_out,
+                          int32_t* d_counts, void* stream);
+
+/* Diagnostic: the fused score of every row (same arithmetic as the scan),
+ * d_out: N floats, -FLT_MAX for rows rejected by the filter. */
+int mars_debug_fused_scores(const mars_store* s, mars_query_ctx* ctx,
+                            const float* d_query, float query_timestamp,
+                            float lambda, int32_t modality_filter,
+                            int32_t use_importance, float* d_out,
+                            void* stream);
+
+/* Replay the host-facing mars_query as one CUDA graph (default on; the
+ * reference's QueryContext::use_cuda_graph, include/memory_cuda.cuh:163).
+ * Calls that request stats always run the kernels directly so the stage
+ * timings are real. */
+int mars_query_ctx_use_graph(mars_query_ctx* ctx, int32_t enable);
+
+/* The context's CUDA stream (cudaStream_t as void*). */
+void* mars_query_ctx_stream(mars_query_ctx* ctx);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MARS_B200_H */
