@@ -427,6 +427,33 @@ int mars_topk_merge_batch(mars_query_ctx* c, const int32_t* d_ids_in, const floa
     return MARS_OK;
 }
 
+int mars_novelty(const mars_store* s, mars_query_ctx* c, const float* d_query, float* d_max,
+                 void* stream) {
+    MARS_TRY(check_store_ctx(s, c, "mars_novelty"));
+    if (d_query == nullptr || d_max == nullptr) return fail(MARS_ERR_INVALID, "mars_novelty: NULL argument");
+    if ((reinterpret_cast<uintptr_t>(d_query) & 15u) != 0 || (s->dim & 3) != 0)
+        return fail(MARS_ERR_INVALID, "mars_novelty: aligned query and dim % 4 == 0 required");
+    MarsDeviceGuard g(c->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    MARS_CUDA_TRY(cudaStreamWaitEvent(st, s->written, 0));
+    ScanArgs sa{};
+    sa.s = make_view(s);
+    sa.d.t_q = 0.0f;
+    sa.d.lambda = 0.0f;     // weight exactly 1: the score is the dot product
+    sa.d.filter = -1;
+    sa.d.use_imp = 0;
+    sa.d.K = 1;
+    sa.q = reinterpret_cast<const float4*>(d_query);
+    sa.part_val = c->d_part_val;
+    sa.part_idx = c->d_part_idx;
+    sa.ticket = c->d_ticket + 5;
+    sa.out_val = d_max;
+    sa.out_idx = c->d_seed_idx;
+    sa.out_cnt = c->d_seed_cnt;
+    MARS_CUDA_TRY(launch_scan_topk(sa, 1, c->scan_blocks, st));
+    return MARS_OK;
+}
+
 int mars_debug_fused_scores(const mars_store* s, mars_query_ctx* c, const float* d_query, float t_q,
                             float lambda, int32_t modality_filter, int32_t use_importance, float* d_out,
                             void* stream) {

@@ -80,6 +80,30 @@ __global__ void scatter_edges_kernel(int32_t* __restrict__ extra, int32_t* __res
     cnt[src[i]] = new_cnt[i];
 }
 
+__global__ void importance_decay_kernel(float* __restrict__ imp, const int32_t* __restrict__ d_n,
+                                        float retain) {
+    const int32_t n = *d_n;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        imp[i] *= retain;
+}
+
+__global__ void importance_boost_kernel(float* __restrict__ imp, const int32_t* __restrict__ d_n,
+                                        const int32_t* __restrict__ ids, int32_t count, float boost,
+                                        float max_imp) {
+    const int32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= count) return;
+    const int32_t u = ids[i];
+    if (u < 0 || u >= *d_n) return;
+    unsigned int* p = reinterpret_cast<unsigned int*>(imp + u);
+    unsigned int old = *p, assumed;
+    do {
+        assumed = old;
+        const float nv = fminf(__uint_as_float(assumed) + boost, max_imp);
+        old = atomicCAS(p, assumed, __float_as_uint(nv));
+    } while (old != assumed);
+}
+
 }  // namespace mars
 
 using namespace mars;
@@ -333,6 +357,39 @@ int mars_store_set_importance(mars_store* s, int32_t first, int32_t n, const flo
     MARS_CUDA_TRY(cudaMemcpyAsync(s->d_imp + first, importance, (size_t)n * 4, cudaMemcpyDefault, s->stream));
     MARS_CUDA_TRY(cudaStreamSynchronize(s->stream));
     MARS_CUDA_TRY(cudaEventRecord(s->written, s->stream));
+    return MARS_OK;
+}
+
+int mars_importance_fill(mars_store* s, float value) {
+    if (s == nullptr) return fail(MARS_ERR_INVALID, "mars_importance_fill: store is NULL");
+    if (s->capacity == 0) return MARS_OK;
+    MarsDeviceGuard g(s->device);
+    fill_f32_kernel<<<(unsigned)((s->capacity + 255) / 256), 256, 0, s->stream>>>(s->d_imp, s->capacity, value);
+    MARS_CUDA_TRY(cudaGetLastError());
+    MARS_CUDA_TRY(cudaStreamSynchronize(s->stream));
+    MARS_CUDA_TRY(cudaEventRecord(s->written, s->stream));
+    return MARS_OK;
+}
+
+int mars_importance_update(mars_store* s, const int32_t* d_ids, int32_t n, float boost,
+                           float decay_rate, float max_importance, void* stream) {
+    if (s == nullptr || n < 0 || (n > 0 && d_ids == nullptr))
+        return fail(MARS_ERR_INVALID, "mars_importance_update: bad arguments");
+    MarsDeviceGuard g(s->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : s->stream;
+    MARS_CUDA_TRY(cudaStreamWaitEvent(st, s->written, 0));
+    const float retain = 1.0f - decay_rate;
+    if (s->capacity > 0) {
+        int blocks = std::min((s->n + 255) / 256 + 1, 4096);
+        importance_decay_kernel<<<blocks, 256, 0, st>>>(s->d_imp, s->d_n, retain);
+        MARS_CUDA_TRY(cudaGetLastError());
+    }
+    if (n > 0) {
+        importance_boost_kernel<<<(n + 255) / 256, 256, 0, st>>>(s->d_imp, s->d_n, d_ids, n, boost,
+                                                                 max_importance);
+        MARS_CUDA_TRY(cudaGetLastError());
+    }
+    MARS_CUDA_TRY(cudaEventRecord(s->written, st));
     return MARS_OK;
 }
 

@@ -84,6 +84,9 @@ _SIGS = {
     "mars_store_append_edges": [_VP, _I32, _VP, _VP],
     "mars_store_set_importance": [_VP, _I32, _I32, _VP],
     "mars_store_info_get": [_VP, C.POINTER(StoreInfo)],
+    "mars_importance_fill": [_VP, _F32],
+    "mars_importance_update": [_VP, _VP, _I32, _F32, _F32, _F32, _VP],
+    "mars_novelty": [_VP, _VP, _VP, _VP, _VP],
     "mars_store_read": [_VP, _I32, _I32, _VP, _VP, _VP, _VP],
     "mars_store_destroy": [_VP],
     "mars_query_ctx_create": [_I32, _I32, _I32, _I32, C.POINTER(_VP)],
@@ -214,6 +217,14 @@ class Store:
         _check(lib().mars_store_read(self.handle, first, n, _ptr(E), _ptr(mod), _ptr(ts), _ptr(imp)))
         return E, mod, ts, imp
 
+    def importance_fill(self, value=1.0):
+        _check(lib().mars_importance_fill(self.handle, float(value)))
+
+    def importance_update(self, d_ids, n, boost=0.1, decay_rate=0.001, max_importance=5.0,
+                          stream=None):
+        _check(lib().mars_importance_update(self.handle, _ptr(d_ids), n, boost, decay_rate,
+                                            max_importance, stream))
+
     def info(self) -> StoreInfo:
         i = StoreInfo()
         _check(lib().mars_store_info_get(self.handle, C.byref(i)))
@@ -286,6 +297,9 @@ class QueryContext:
         _check(lib().mars_topk_merge_batch(self.handle, _ptr(d_ids_in), _ptr(d_vals_in), n_lists,
                                            K, Q, _ptr(d_ids_out), _ptr(d_vals_out),
                                            _ptr(d_counts), stream))
+
+    def novelty(self, store: Store, d_query, d_max, stream=None):
+        _check(lib().mars_novelty(store.handle, self.handle, _ptr(d_query), _ptr(d_max), stream))
 
     def debug_fused_scores(self, store: Store, d_query, t_q, lam, d_out, modality_filter=-1,
                            use_importance=False, stream=None):

@@ -142,6 +142,20 @@ int mars_store_append_edges(mars_store* s, int32_t n, const int32_t* src,
 int mars_store_set_importance(mars_store* s, int32_t first, int32_t n,
                               const float* importance);
 
+/* init_importance (include/memory_cuda.cuh:203-205,
+ * src/memory_cuda.cu:1165-1176): importance of every row = value. */
+int mars_importance_fill(mars_store* s, float value);
+
+/* update_importance (include/memory_cuda.cuh:207-215,
+ * src/memory_cuda.cu:1179-1224): importance *= (1 - decay_rate) for all rows,
+ * then importance[id] = min(importance[id] + boost, max_importance) for each
+ * of the n device ids (ids < 0 or >= N are skipped).  A repeated id is
+ * boosted once per occurrence (atomic update; the reference's plain
+ * read-modify-write may lose repeats).  Asynchronous on `stream`. */
+int mars_importance_update(mars_store* s, const int32_t* d_ids, int32_t n,
+                           float boost, float decay_rate, float max_importance,
+                           void* stream);
+
 int mars_store_info_get(const mars_store* s, mars_store_info* out);
 
 /* Copy rows [first, first+n) back to host arrays (any may be NULL): the
@@ -221,6 +235,13 @@ int mars_topk_merge_batch(mars_query_ctx* ctx, const int32_t* d_ids_in,
                           const float* d_vals_in, int32_t n_lists, int32_t K,
                           int32_t Q, int32_t* d_ids_out, float* d_vals_out,
                           int32_t* d_counts, void* stream);
+
+/* compute_novelty (include/memory_cuda.cuh:217-222,
+ * src/memory_cuda.cu:1232-1290): the largest dot(E_i, q) over all rows,
+ * written to *d_max (device float) -- the fused scan with K = 1, no decay,
+ * no filter; no N-sized buffer and no host round trip. */
+int mars_novelty(const mars_store* s, mars_query_ctx* ctx, const float* d_query,
+                 float* d_max, void* stream);
 
 /* Diagnostic: the fused score of every row (same arithmetic as the scan),
  * d_out: N floats, -FLT_MAX for rows rejected by the filter. */
