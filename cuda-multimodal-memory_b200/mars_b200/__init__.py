@@ -101,6 +101,8 @@ _SIGS = {
     "mars_topk_merge": [_VP, _VP, _VP, _I32, _I32, _VP, _VP, _VP, _VP],
     "mars_topk_merge_batch": [_VP, _VP, _VP, _I32, _I32, _I32, _VP, _VP, _VP, _VP],
     "mars_debug_fused_scores": [_VP, _VP, _VP, _F32, _F32, _I32, _I32, _VP, _VP],
+    "mars_scan_topk_noalloc": [_VP, _I32, _VP, _VP, _VP, _I32, _I32, _VP, _F32, _F32, _I32, _I32,
+                               _I32, _I32, _VP, _VP, _VP, _VP],
 }
 _RESTYPE = {"mars_last_error": C.c_char_p, "mars_status_string": C.c_char_p,
             "mars_abi_version": C.c_int, "mars_query_ctx_stream": C.c_void_p}
@@ -317,6 +319,18 @@ class QueryContext:
             self.close()
         except Exception:
             pass
+
+
+def scan_topk_noalloc(d_embeddings, row_pitch, d_timestamps, d_importance, d_modalities, n, dim,
+                      d_query, t_q, lam, K, d_ids, d_vals, d_count=None, modality_filter=-1,
+                      use_importance=False, row_offset=0, stream=None):
+    """mars_scan_topk_noalloc: the fused scan over caller-owned device arrays
+    for callers that may not allocate GPU memory (no store, no context)."""
+    _check(lib().mars_scan_topk_noalloc(_ptr(d_embeddings), row_pitch, _ptr(d_timestamps),
+                                        _ptr(d_importance), _ptr(d_modalities), n, dim,
+                                        _ptr(d_query), float(t_q), float(lam), modality_filter,
+                                        int(use_importance), K, row_offset, _ptr(d_ids),
+                                        _ptr(d_vals), _ptr(d_count), stream))
 
 
 def query_once(store: Store, q, t_q, cfg: RetrievalConfig | None = None):

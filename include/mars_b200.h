@@ -243,6 +243,31 @@ int mars_topk_merge_batch(mars_query_ctx* ctx, const int32_t* d_ids_in,
 int mars_novelty(const mars_store* s, mars_query_ctx* ctx, const float* d_query,
                  float* d_max, void* stream);
 
+/* Fused scan top-K that allocates nothing.  No counterpart in the reference:
+ * it exists for callers that may not call cudaMalloc -- processes that
+ * reserve all GPU memory up front (for example a real-time loop whose memory
+ * budget is fixed before its deadline-bound phase) or hosts that forbid a
+ * library from growing their footprint.  The caller passes its own device
+ * arrays (embeddings with a row pitch in floats, timestamps, optional
+ * importance and modalities, the query; all 16-byte aligned rows) and the
+ * outputs (d_ids / d_vals: K entries, d_count may be NULL); results equal
+ * mars_scan_topk's.  Working memory is a library-owned device array of
+ * MARS_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
+ * exit; K above MARS_NOALLOC_MAX_K is rejected with MARS_ERR_CAPACITY.  The
+ * first call on a device looks the array up (cudaGetSymbolAddress): make it
+ * before any stream capture.  All calls share the array, so calls that
+ * overlap on the GPU race; serialise them.  Works on the current device. */
+#define MARS_NOALLOC_MAX_K 128
+#define MARS_NOALLOC_SCRATCH_BYTES 524548
+int mars_scan_topk_noalloc(const float* d_embeddings, int32_t row_pitch,
+                           const float* d_timestamps, const float* d_importance,
+                           const int32_t* d_modalities, int32_t n, int32_t dim,
+                           const float* d_query, float query_timestamp,
+                           float lambda, int32_t modality_filter,
+                           int32_t use_importance, int32_t K,
+                           int32_t row_offset, int32_t* d_ids, float* d_vals,
+                           int32_t* d_count, void* stream);
+
 /* Diagnostic: the fused score of every row (same arithmetic as the scan),
  * d_out: N floats, -FLT_MAX for rows rejected by the filter. */
 int mars_debug_fused_scores(const mars_store* s, mars_query_ctx* ctx,
