@@ -55,6 +55,10 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=42)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
+    ap.add_argument("--workload", choices=["scan", "c0", "c1"], default="scan",
+                    help="scan: the headline (default); c0: single-query latency at N=2400 "
+                         "with BFS depth 1; c1: streaming loop (append 10 rows + query per frame)")
+    ap.add_argument("--frames", type=int, default=10000)
     return ap.parse_args()
 
 
@@ -392,9 +396,111 @@ def run_mars(a):
     del ok
 
 
+# ---------------------------------------------------------------------------
+def _pct(xs, p):
+    return float(np.percentile(np.asarray(xs), p))
+
+
+def run_latency(a):
+    """c0 / c1: single-query latency through the public API (host query in,
+    host results out), one GPU.  c0: N = 2,400, lambda = 0.5, K = 10, BFS
+    depth 1 over 4 random cross-modal bridges per node.  c1: start with
+    N = 10,000 (same generator); every 1 ms frame appends 10 rows stamped with
+    the frame time (normalised on the device) and 2 bridge edges per new row,
+    then queries with lambda = 1.0, K = 10, depth 1; latency and freshness
+    (share of the top-K stamped within the last 100 ms) over all frames."""
+    import torch
+    import mars_b200 as mb
+    import oracle as O
+    from mars_b200 import datagen
+
+    D, K = a.dim, 10
+    if a.workload == "c0":
+        N0, lam, frames, per = 2400, 0.5, a.frames, 0
+    else:
+        N0, lam, frames, per = 10000, 1.0, a.frames, 10
+    E, mod, ts, imp = datagen.gaussian_corpus(N0, D, seed=a.seed, n_mod=4, ts_max=10.0)
+    ro, ci = datagen.random_bridges(mod, 4, seed=7)
+    cap = N0 + frames * per
+    rng = np.random.default_rng(a.seed + 3)
+    Q = datagen.queries(256, D, seed=0x5EED0000)
+    cfg_kw = dict(top_k=K, bfs_max_hops=1, time_decay_lambda=lam, bfs_score_decay=0.5)
+
+    if a.impl == "reference":
+        oc = O.Corpus(E=E, ts=ts, mod=mod, row_offsets=ro, col_indices=ci)
+        lat = []
+        for f in range(min(frames, 200)):
+            t0 = time.perf_counter()
+            O.query(oc, Q[f % 256], 10.0, top_k=K, bfs_max_hops=1, lam=lam, bfs_score_decay=0.5,
+                    dot_order=O.DOT_FAST)
+            lat.append(time.perf_counter() - t0)
+        v = len(lat) / sum(lat)
+        print(json.dumps({"impl": "reference", "workload": a.workload, "metric": "queries/s",
+                          "value": v, "unit": "queries/s", "p50_us": _pct(lat, 50) * 1e6,
+                          "p99_us": _pct(lat, 99) * 1e6,
+                          "cpu_baseline": {"value": v, "unit": "queries/s", "cores": 1,
+                                           "kind": "port", "sample": f"{len(lat)} queries, "
+                                           "oracle orc_query single thread (corpus fixed)"}}))
+        return
+
+    slack = 64 if per else 0
+    store = mb.Store(cap, D, edge_slack=slack)
+    slack_used = np.zeros(cap, np.int32)
+    store.upload(E, mod, ts, None, ro, ci)
+    ctx = mb.QueryContext(cap, D, max_k=K)
+    cfg = mb.RetrievalConfig(**cfg_kw)
+    for i in range(20):
+        ctx.query(store, Q[i], 10.0, cfg)
+    torch.cuda.synchronize()
+    q_lat, a_lat, fresh = [], [], []
+    ts_host = np.zeros(cap, np.float32)
+    ts_host[:N0] = ts
+    t_base = 10.0
+    t_all0 = time.perf_counter()
+    for f in range(frames):
+        t_now = t_base + f * 1e-3
+        if per:
+            raw = rng.standard_normal((per, D)).astype(np.float32)
+            m = rng.integers(0, 4, per).astype(np.int32)
+            t0 = time.perf_counter()
+            first = store.append(raw, m, np.full(per, t_now, np.float32), normalize=True)
+            ts_host[first:first + per] = np.float32(t_now)
+            # one bridge per new row to a random older row that still has a
+            # free neighbour slot (both directions)
+            src = np.arange(first, first + per, dtype=np.int32)
+            dst = rng.integers(0, first, per).astype(np.int32)
+            for i in range(per):
+                while slack_used[dst[i]] >= slack:
+                    dst[i] = rng.integers(0, first)
+                slack_used[dst[i]] += 1
+                slack_used[src[i]] += 1
+            store.append_edges(np.concatenate([src, dst]), np.concatenate([dst, src]))
+            a_lat.append(time.perf_counter() - t0)
+        t0 = time.perf_counter()
+        res = ctx.query(store, Q[f % 256], t_now, cfg)
+        q_lat.append(time.perf_counter() - t0)
+        if per:
+            fresh.append(float(np.mean(ts_host[res["node_id"]] >= np.float32(t_now - 0.1)))
+                         if len(res) else 0.0)
+    total = time.perf_counter() - t_all0
+    line = {"workload": a.workload, "metric": "single-query latency (mars_query, host in/out)",
+            "n_start": N0, "n_end": N0 + frames * per, "frames": frames, "dim": D, "top_k": K,
+            "lambda": lam, "bfs_max_hops": 1,
+            "query_p50_us": _pct(q_lat, 50) * 1e6, "query_p99_us": _pct(q_lat, 99) * 1e6,
+            "query_max_us": float(np.max(q_lat) * 1e6),
+            "queries_per_s": frames / sum(q_lat)}
+    if per:
+        line.update({"append_p50_us": _pct(a_lat, 50) * 1e6, "append_p99_us": _pct(a_lat, 99) * 1e6,
+                     "freshness_mean": float(np.mean(fresh)),
+                     "frames_per_s_incl_append": frames / total})
+    print(json.dumps(line), flush=True)
+
+
 def main():
     a = parse_args()
-    if a.impl == "reference":
+    if a.workload in ("c0", "c1"):
+        run_latency(a)
+    elif a.impl == "reference":
         run_reference(a)
     else:
         run_mars(a)

@@ -115,10 +115,14 @@ __global__ void __launch_bounds__(kBfsThreads) bfs_hop_kernel(const BfsArgs a, i
 
 // Finalize the scores of level `last` and select the top-K of all visited
 // nodes by (score desc, id asc).
+constexpr int kFinStage = 4096;
+
 template <int KPL>
 __global__ void __launch_bounds__(kBfsThreads) bfs_finalize_kernel(const BfsArgs a, int last) {
     __shared__ float   s_val[kBfsWarps][kMaxTopK];
     __shared__ int32_t s_idx[kBfsWarps][kMaxTopK];
+    __shared__ float   s_stage_v[kFinStage];
+    __shared__ int32_t s_stage_i[kFinStage];
     const MarsQueryDesc& d = a.d;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gw = blockIdx.x * kBfsWarps + warp;
@@ -138,13 +142,25 @@ __global__ void __launch_bounds__(kBfsThreads) bfs_finalize_kernel(const BfsArgs
     WarpTopK<KPL> top;
     top.init(K);
     // rank every visited node by (score desc, node id asc); a node's level
-    // is recovered from its stamp when the result is written.
-    for (int32_t base = warp * 32; base < total; base += kBfsWarps * 32) {
-        const int32_t j = base + lane;
-        float s = -INFINITY;
-        int32_t id = INT32_MAX;
-        if (j < total) { s = __ldcg(a.vis_score + j); id = __ldcg(a.vis_ids + j); }
-        top.offer_lanes(s, id, j < total, lane);
+    // is recovered from its stamp when the result is written.  The visited
+    // list is staged in shared memory batch by batch so that every thread's
+    // loads are in flight together.
+    for (int32_t b0 = 0; b0 < total; b0 += kFinStage) {
+        const int ne = min(kFinStage, total - b0);
+#pragma unroll 4
+        for (int j = threadIdx.x; j < ne; j += kBfsThreads) {
+            s_stage_v[j] = __ldcg(a.vis_score + b0 + j);
+            s_stage_i[j] = __ldcg(a.vis_ids + b0 + j);
+        }
+        __syncthreads();
+        for (int base = warp * 32; base < ne; base += kBfsWarps * 32) {
+            const int j = base + lane;
+            float s = -INFINITY;
+            int32_t id = INT32_MAX;
+            if (j < ne) { s = s_stage_v[j]; id = s_stage_i[j]; }
+            top.offer_lanes(s, id, j < ne, lane);
+        }
+        __syncthreads();
     }
     top.store(s_val[warp], s_idx[warp], lane);
     __syncthreads();

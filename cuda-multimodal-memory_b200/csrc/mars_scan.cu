@@ -23,10 +23,14 @@
 
 namespace mars {
 
+constexpr int kStageEntries = 3072;   // 24 KB of staged (score, id) pairs
+
 template <int KPL, int CPL, bool ALL>
 __global__ void __launch_bounds__(kScanThreads, 2) scan_topk_kernel(const ScanArgs a) {
     __shared__ float   s_val[kScanWarps][kMaxTopK];
     __shared__ int32_t s_idx[kScanWarps][kMaxTopK];
+    __shared__ float   s_stage_v[kStageEntries];
+    __shared__ int32_t s_stage_i[kStageEntries];
     __shared__ bool    s_last;
 
     const int lane = threadIdx.x & 31;
@@ -140,23 +144,27 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_topk_kernel(const ScanAr
     if (!s_last) return;
 
     // ---- last CTA: merge every CTA's list ----------------------------------
+    // Stage the lists in shared memory with all threads' loads in flight at
+    // once (one memory round trip per batch instead of one per list), then
+    // let each warp merge a subset of the staged lists.
     __threadfence();
     top.init(K);
-    for (int b = warp; b < (int)gridDim.x; b += kScanWarps) {
-        const float* pv = a.part_val + (int64_t)b * K;
-        const int32_t* pi = a.part_idx + (int64_t)b * K;
-        // bypass L1: the lists were written by other SMs
-        for (int base = 0; base < K; base += 32) {
-            const int j = base + lane;
-            float s = -INFINITY;
-            int32_t id = INT32_MAX;
-            if (j < K) { s = __ldcg(pv + j); id = __ldcg(pi + j); }
-            const unsigned m = __ballot_sync(MARS_FULL_MASK, j < K && top.admits(s, id));
-            if (m == 0) break;
-            top.offer_lanes(s, id, j < K, lane);
+    const int lists_per_batch = kStageEntries / K;
+    for (int b0 = 0; b0 < (int)gridDim.x; b0 += lists_per_batch) {
+        const int nl = min(lists_per_batch, (int)gridDim.x - b0);
+        const int ne = nl * K;
+        const float* pv = a.part_val + (int64_t)b0 * K;
+        const int32_t* pi = a.part_idx + (int64_t)b0 * K;
+#pragma unroll 4
+        for (int j = threadIdx.x; j < ne; j += kScanThreads) {
+            s_stage_v[j] = __ldcg(pv + j);   // written by other SMs: bypass L1
+            s_stage_i[j] = __ldcg(pi + j);
         }
+        __syncthreads();
+        for (int l = warp; l < nl; l += kScanWarps)
+            top.offer_sorted(s_stage_v + l * K, s_stage_i + l * K, K, lane);
+        __syncthreads();
     }
-    __syncthreads();
     top.store(s_val[warp], s_idx[warp], lane);
     __syncthreads();
     if (warp != 0) return;

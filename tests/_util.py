@@ -66,3 +66,35 @@ def assert_topk_matches_scores(ids, vals, all_scores, eligible=None, rtol=RTOL, 
     assert np.all(np.diff(vals) <= 0), f"{what}: not descending {vals}"
     assert np.all(close(vals, s[ids], rtol, atol)), f"{what}: returned scores disagree"
     assert_ranked_equivalent(ids, vals, ref_ids, ref_vals, rtol=rtol, atol=atol, what=what)
+
+
+def assert_bfs_set_valued(oracle_mod, corpus, q, t_q, lam, K, hops, decay, ref_ids, ref_scores,
+                          ref_hops, ours_scores=None, use_importance=False, rtol=RTOL, atol=ATOL,
+                          what=""):
+    """Check a reference BFS answer whose parent choice is racy (first claimer
+    wins, src/memory_cuda.cu:505-512): every returned node must be visited at
+    the same hop as in the canonical BFS, and its score must equal
+    fmaxf(parent * decay, own * 0.8) for SOME parent one level closer.  The
+    canonical (best-parent) answer dominates: its k-th score is >= the
+    reference's."""
+    O = oracle_mod
+    final = O.fused_scores(corpus, q, t_q, lam, use_importance=use_importance)
+    ids, vals = O.topk(final, corpus.mod, -1, K)
+    visited = O.bfs(corpus, ids, vals, final, hops, decay)
+    vmap = {int(v["node_id"]): v for v in visited}
+    ro, ci = corpus.row_offsets, corpus.col_indices
+    for nid, s, h in zip(np.asarray(ref_ids).tolist(), np.asarray(ref_scores).tolist(),
+                         np.asarray(ref_hops).tolist()):
+        assert nid in vmap, f"{what}: reference returned an unvisited node {nid}"
+        assert int(vmap[nid]["hops"]) == h, f"{what}: node {nid} hop differs"
+        if h == 0:
+            assert close(s, vmap[nid]["score"], rtol, atol), f"{what}: seed {nid} score"
+            continue
+        nbrs = ci[ro[nid]:ro[nid + 1]]
+        possible = [max(np.float32(vmap[int(p)]["score"]) * np.float32(decay),
+                        np.float32(final[nid]) * np.float32(0.8))
+                    for p in nbrs if int(p) in vmap and int(vmap[int(p)]["hops"]) == h - 1]
+        assert any(close(s, p, rtol, atol) for p in possible), \
+            f"{what}: node {nid} score {s} not reachable from any parent {possible}"
+    if ours_scores is not None and len(ours_scores) and len(ref_scores):
+        assert float(ours_scores[-1]) >= float(ref_scores[-1]) - atol - rtol * abs(ref_scores[-1])

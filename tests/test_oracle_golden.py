@@ -105,3 +105,14 @@ def test_l2_normalize_matches_engine_server_rule():
         norm = np.float32(norm + np.float32(x * x))
     norm = np.float32(np.sqrt(norm)) + np.float32(1e-8)
     assert np.array_equal(got, (v / norm).astype(np.float32))
+
+
+def test_reference_host_tests_pass():
+    """The reference's own host tests (tests/test_memory_graph.cpp) on its
+    corpus / NSN generator, built from its sources into oracle/_ref."""
+    import subprocess
+    exe = os.path.join(os.path.dirname(HERE), "oracle", "_ref", "ref_host_tests")
+    if not os.path.exists(exe):
+        pytest.skip("oracle/_ref not built")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0 and "0 failed" in r.stdout, r.stdout[-1000:]
