@@ -1,0 +1,644 @@
+// mars_batch.cu -- batched fused scan on the tensor cores (tcgen05 + TMEM).
+//
+// B queries x N rows: scores = Q * E^T (a dense contraction, 2*B*N*D flops)
+// followed by decay x importance and a per-query top-K.  The reference has no
+// batched path; its single-query pipeline (src/memory_cuda.cu:924-1067) run B
+// times reads E B times.  Here E streams through the tensor cores once per
+// 128 queries:
+//
+//  1. prep:      per-row weight w = __expf(-lambda*age) [x importance] (NaN for
+//                rows the modality filter rejects), per-query error margin.
+//  2. sample:    the GEMM over a strided sample of row tiles; each (query, tile)
+//                keeps its 16 best lower bounds.
+//  3. threshold: per query the j-th best sampled lower bound, theta.  j is
+//                chosen so that theta lies, with overwhelming probability,
+//                below the query's true K-th best score.
+//  4. candidates: the GEMM over all rows; a row becomes a candidate of a query
+//                when its upper bound reaches theta.
+//  5. rescore:   exact fp32 score of every candidate with the canonical dot
+//                (the same arithmetic as the single-query scan) and the top-K.
+//                If at least K candidates score >= theta exactly, no row
+//                outside the candidate set can beat the K-th result (its exact
+//                score is at most its upper bound, which was below theta), so
+//                the answer is exact; otherwise the query is flagged and the
+//                host re-runs it with the exact single-query scan.
+//
+// GEMM: kind::tf32 (fp32 operands read by TMA straight from the store, 128-byte
+// swizzled K-major tiles), M = 128 queries x N = 256 rows per tile, K steps of
+// 32, 4-stage TMA ring, accumulators double-buffered in TMEM (2 x 256 columns).
+// Warp roles: warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2-5
+// epilogue (one query row per thread, tcgen05.ld 32x32b).
+//
+// Error bound of the approximate score: operands keep 10 mantissa bits, so
+// |A - dot| <= (2^-9 + 2^-20) |q||e| + accumulation (<= D 2^-23 |q||e|); the
+// margin used is 2.6e-3 |q| max|e|, covering D <= 4096.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "mars_b200.h"
+#include "mars_common.cuh"
+#include "mars_internal.h"
+#include "mars_kernels.cuh"
+#include "mars_sm100.cuh"
+
+namespace mars {
+namespace batch {
+
+constexpr int kBM = 128;              // queries per tile (UMMA M)
+constexpr int kBN = 256;              // rows per tile (UMMA N)
+constexpr int kBK = 32;               // fp32 per 128-byte swizzle row
+constexpr int kStages = 4;
+constexpr int kStageA = kBM * kBK * 4;    // 16 KB
+constexpr int kStageB = kBN * kBK * 4;    // 32 KB
+constexpr int kStageBytes = kStageA + kStageB;
+constexpr int kThreads = 192;
+constexpr int kTmemCols = 512;
+constexpr int kJ = 16;                // sampled lower bounds kept per (query, tile)
+constexpr float kMarginRel = 2.6e-3f;
+
+enum Mode { kSample = 0, kCandidates = 1 };
+
+struct GemmArgs {
+    int32_t B, n, nkb;               // queries, rows, K blocks
+    int32_t qtiles, rtiles;          // tiles along queries / rows
+    int32_t n_tiles;                 // total tiles of this launch
+    const int32_t* sample_rt;        // sample mode: row tile of sample tile i
+    const float* wts;                // n row weights (NaN = rejected)
+    const float* theta;              // B thresholds (candidate mode)
+    const float* margin;             // B margins
+    float* sample_buf;               // [n_tiles][B][kJ]
+    int32_t* cand;                   // [B][cap]
+    int32_t* cand_cnt;               // [B]
+    int32_t cap;
+    int* err;
+};
+
+__device__ __forceinline__ void tile_coords(const GemmArgs& a, int t, int mode, int& qt, int& row0) {
+    if (mode == kSample) {
+        qt = t % a.qtiles;
+        row0 = a.sample_rt[t / a.qtiles] * kBN;
+    } else {
+        qt = t % a.qtiles;          // query tiles innermost: CTAs running side by
+        row0 = (t / a.qtiles) * kBN;  // side share the row tile through L2
+    }
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_e,
+            const GemmArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+    uint64_t* empty = full + kStages;
+    uint64_t* tfull = empty + kStages;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) { sm100::mbar_init(full + s, 1); sm100::mbar_init(empty + s, 1); }
+        for (int b = 0; b < 2; ++b) { sm100::mbar_init(tfull + b, 1); sm100::mbar_init(tempty + b, 128); }
+        sm100::fence_mbar_init();
+        sm100::prefetch_tmap(&tmap_q);
+        sm100::prefetch_tmap(&tmap_e);
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc(tmem_slot, kTmemCols);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_phase[kStages];
+            bool issued[kStages];
+            for (int s = 0; s < kStages; ++s) { issued[s] = false; issued_phase[s] = 0; }
+            bool ok = true;
+            for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
+                int qt, row0;
+                tile_coords(a, t, MODE, qt, row0);
+                for (int kb = 0; kb < a.nkb; ++kb) {
+                    if (!sm100::mbar_wait(empty + stage, phase ^ 1u, a.err, 1)) { ok = false; break; }
+                    uint8_t* sa = smem + stage * kStageBytes;
+                    sm100::mbar_arrive_expect_tx(full + stage, kStageBytes);
+                    sm100::tma_load_2d(sa, &tmap_q, full + stage, kb * kBK, qt * kBM);
+                    sm100::tma_load_2d(sa + kStageA, &tmap_e, full + stage, kb * kBK, row0);
+                    issued[stage] = true;
+                    issued_phase[stage] = phase;
+                    if (++stage == kStages) { stage = 0; phase ^= 1u; }
+                }
+            }
+            // every copy this thread started has landed before the CTA may exit
+            for (int s = 0; s < kStages; ++s)
+                if (issued[s]) sm100::mbar_wait(full + s, issued_phase[s], a.err, 2);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t idesc = sm100::idesc_tf32(kBM, kBN);
+            int stage = 0;
+            uint32_t phase = 0;
+            int buf = 0;
+            uint32_t bphase = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
+                if (!sm100::mbar_wait(tempty + buf, bphase ^ 1u, a.err, 3)) break;
+                sm100::tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(buf * kBN);
+                for (int kb = 0; kb < a.nkb; ++kb) {
+                    if (!sm100::mbar_wait(full + stage, phase, a.err, 4)) { ok = false; break; }
+                    sm100::tc_fence_after();
+                    const uint32_t sa = sm100::smem_u32(smem + stage * kStageBytes);
+                    const uint64_t da = sm100::smem_desc_sw128(sa);
+                    const uint64_t db = sm100::smem_desc_sw128(sa + kStageA);
+#pragma unroll
+                    for (int k = 0; k < kBK / 8; ++k)   // 8 tf32 (32 bytes) per MMA
+                        sm100::mma_tf32(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
+                                        (kb > 0 || k > 0) ? 1u : 0u);
+                    sm100::mma_commit(empty + stage);   // stage reusable when these MMAs finish
+                    if (++stage == kStages) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                sm100::mma_commit(tfull + buf);         // accumulator ready
+                if (++buf == 2) { buf = 0; bphase ^= 1u; }
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5) ----------------
+        const int sub = warp & 3;                   // TMEM lane quarter of this warp
+        const int row_in_tile = sub * 32 + lane;    // query row of this thread
+        int buf = 0;
+        uint32_t bphase = 0;
+        for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
+            int qt, row0;
+            tile_coords(a, t, MODE, qt, row0);
+            const int q = qt * kBM + row_in_tile;
+            const bool qv = q < a.B;
+            const float th = (MODE == kCandidates && qv) ? __ldg(a.theta + q) : 0.f;
+            const float mg = qv ? __ldg(a.margin + q) : 0.f;
+            if (!sm100::mbar_wait(tfull + buf, bphase, a.err, 5)) break;
+            sm100::tc_fence_after();
+            float best[kJ];
+#pragma unroll
+            for (int j = 0; j < kJ; ++j) best[j] = -INFINITY;
+            for (int c = 0; c < kBN / 32; ++c) {
+                uint32_t r[32];
+                sm100::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(sub * 32) << 16) +
+                                              (uint32_t)(buf * kBN + c * 32), r);
+                sm100::tmem_ld_wait();
+                if (!qv) continue;
+                const int rbase = row0 + c * 32;
+#pragma unroll
+                for (int j4 = 0; j4 < 8; ++j4) {
+                    float4 w4 = make_float4(NAN, NAN, NAN, NAN);
+                    if (rbase + 4 * j4 + 3 < a.n) {
+                        w4 = __ldg(reinterpret_cast<const float4*>(a.wts + rbase) + j4);
+                    } else {
+                        float* wp = &w4.x;
+#pragma unroll
+                        for (int u = 0; u < 4; ++u)
+                            if (rbase + 4 * j4 + u < a.n) wp[u] = __ldg(a.wts + rbase + 4 * j4 + u);
+                    }
+                    const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int j = 4 * j4 + u;
+                        const float w = wv[u];
+                        const float f = __uint_as_float(r[j]) * w;
+                        const float slack = mg * fabsf(w);
+                        if (MODE == kCandidates) {
+                            if (f + slack >= th) {      // NaN weights never pass
+                                const int pos = atomicAdd(a.cand_cnt + q, 1);
+                                if (pos < a.cap) a.cand[(int64_t)q * a.cap + pos] = rbase + j;
+                            }
+                        } else {
+                            float lo = f - slack;
+                            if (lo > best[kJ - 1]) {    // NaN never passes
+#pragma unroll
+                                for (int s = 0; s < kJ; ++s) {
+                                    if (lo > best[s]) { const float tmp = best[s]; best[s] = lo; lo = tmp; }
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+            sm100::tc_fence_before();
+            sm100::mbar_arrive(tempty + buf);
+            if (MODE == kSample && qv) {
+                float* dst = a.sample_buf + ((int64_t)(t / a.qtiles) * a.B + q) * kJ;
+#pragma unroll
+                for (int j = 0; j < kJ; ++j) dst[j] = best[j];
+            }
+            if (++buf == 2) { buf = 0; bphase ^= 1u; }
+        }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        sm100::tc_fence_after();
+        sm100::tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Row weights and per-query margins.
+__global__ void prep_rows_kernel(const float* __restrict__ ts, const float* __restrict__ imp,
+                                 const int32_t* __restrict__ mod, int32_t n, float t_q, float lambda,
+                                 int32_t filter, int32_t use_imp, float* __restrict__ wts) {
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        float w;
+        if (filter >= 0 && mod[i] != filter) {
+            w = NAN;
+        } else {
+            w = __expf(-lambda * fmaxf(0.0f, t_q - ts[i]));
+            if (use_imp) w = w * imp[i];
+        }
+        wts[i] = w;
+    }
+}
+
+__global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch, int32_t B, int32_t nc,
+                                    float max_row_norm, float* __restrict__ margin,
+                                    int32_t* __restrict__ cand_cnt) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= B) return;
+    const float4* q = reinterpret_cast<const float4*>(Q + (int64_t)warp * qpitch);
+    float s = 0.f;
+    for (int c = lane; c < nc; c += 32) {
+        const float4 v = q[c];
+        s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
+    s = warp_butterfly_sum(s);
+    if (lane == 0) {
+        // 1.0001: covers the fp32 rounding of this norm itself
+        margin[warp] = kMarginRel * sqrtf(s) * 1.0001f * max_row_norm;
+        cand_cnt[warp] = 0;
+    }
+}
+
+// theta[q] = the j-th best sampled lower bound of query q.
+__global__ void threshold_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tiles,
+                                 int32_t B, int32_t j, float* __restrict__ theta) {
+    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+    if (warp >= B) return;
+    WarpTopK<1> top;
+    top.init(j);
+    const int total = n_sample_tiles * kJ;
+    for (int base = 0; base < total; base += 32) {
+        const int i = base + lane;
+        float v = -INFINITY;
+        if (i < total) v = sample_buf[((int64_t)(i / kJ) * B + warp) * kJ + (i % kJ)];
+        top.offer_lanes(v, i, i < total && v > -INFINITY, lane);
+    }
+    if (lane == 0) theta[warp] = top.thr_v;   // -inf when fewer than j values exist
+}
+
+// Exact rescoring of candidates: one block per query.
+template <int KPL>
+__global__ void __launch_bounds__(256)
+rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t B, float t_q,
+               float lambda, int32_t filter, int32_t use_imp, int32_t K, int32_t row_offset,
+               const float* __restrict__ theta, const int32_t* __restrict__ cand,
+               const int32_t* __restrict__ cand_cnt, int32_t cap, int32_t* __restrict__ out_ids,
+               float* __restrict__ out_vals, int32_t* __restrict__ out_cnt,
+               int32_t* __restrict__ fallback) {
+    __shared__ float   s_val[8][kMaxTopK];
+    __shared__ int32_t s_idx[8][kMaxTopK];
+    __shared__ int     s_ge;
+    const int qi = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    if (threadIdx.x == 0) s_ge = 0;
+    __syncthreads();
+    const float4* q4 = reinterpret_cast<const float4*>(Q + (int64_t)qi * qpitch);
+    const int ncand = cand_cnt[qi];
+    const bool overflow = ncand > cap;
+    const int nc_ = min(ncand, cap);
+    const float th = theta[qi];
+    const bool use_w = use_imp != 0 && s.imp != nullptr;
+    WarpTopK<KPL> top;
+    top.init(K);
+    int ge = 0;
+    for (int i = warp; i < nc_; i += 8) {
+        const int32_t r = cand[(int64_t)qi * cap + i];
+        if (filter >= 0 && __ldg(s.mod + r) != filter) continue;
+        const float4* row = reinterpret_cast<const float4*>(s.E) + (int64_t)r * s.pitch4;
+        const float dot = warp_dot_canonical(row, q4, s.nc, lane);
+        float f = fused_weight_apply(dot, __ldg(s.ts + r), t_q, lambda);
+        if (use_w) f = f * __ldg(s.imp + r);
+        ge += (f >= th) ? 1 : 0;
+        top.push(f, r + row_offset, lane);
+    }
+    if (lane == 0) atomicAdd(&s_ge, ge);
+    top.store(s_val[warp], s_idx[warp], lane);
+    __syncthreads();
+    if (warp != 0) return;
+    for (int w = 1; w < 8; ++w) top.offer_sorted(s_val[w], s_idx[w], K, lane);
+    int cnt = 0;
+#pragma unroll
+    for (int sl = 0; sl < KPL; ++sl) {
+        const int p = sl * 32 + lane;
+        const bool valid = p < K && top.i[sl] != INT32_MAX;
+        cnt += __popc(__ballot_sync(0xffffffffu, valid));
+        if (p < K) {
+            out_vals[(int64_t)qi * K + p] = valid ? top.v[sl] : -INFINITY;
+            out_ids[(int64_t)qi * K + p] = valid ? top.i[sl] : -1;
+        }
+    }
+    if (lane == 0) {
+        if (out_cnt) out_cnt[qi] = cnt;
+        fallback[qi] = (overflow || s_ge < K) ? 1 : 0;
+    }
+}
+
+}  // namespace batch
+}  // namespace mars
+
+using namespace mars;
+using namespace mars::batch;
+
+// ---------------------------------------------------------------------------
+// Host side
+struct mars_batch_ctx {
+    int32_t device = 0;
+    int32_t max_batch = 0;
+    int32_t dim = 0;
+    int32_t max_k = 0;
+    int32_t max_nodes = 0;
+    int32_t cap = 0;
+    int32_t num_sms = 0;
+    cudaStream_t stream = nullptr;
+    float* d_wts = nullptr;          // max_nodes
+    float* d_margin = nullptr;       // max_batch
+    float* d_theta = nullptr;
+    int32_t* d_cand = nullptr;       // max_batch * cap
+    int32_t* d_cand_cnt = nullptr;
+    int32_t* d_fallback = nullptr;
+    float* d_sample = nullptr;       // sample_tiles_cap * max_batch * kJ
+    int32_t* d_sample_rt = nullptr;
+    int32_t sample_tiles_cap = 0;
+    int* d_err = nullptr;
+    int32_t* h_fallback = nullptr;   // pinned
+    int32_t* h_cand_cnt = nullptr;   // pinned
+    int* h_err = nullptr;
+    mars_query_ctx* scan_ctx = nullptr;   // exact single-query scans for fallbacks
+    mars_batch_stats last{};
+};
+
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2D fp32 tensor [rows][cols] with a row stride of `pitch` floats; box
+// (32 cols x box_rows), 128-byte swizzle, out-of-range elements read as 0.
+int make_map(CUtensorMap* m, const float* base, int64_t rows, int64_t cols, int64_t pitch, int box_rows) {
+    auto enc = get_encode();
+    if (enc == nullptr) return fail(MARS_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t gstride[1] = {(cuuint64_t)(pitch * 4)};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    cuuint32_t estride[2] = {1, 1};
+    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), gdim, gstride, box,
+                     estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MARS_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return MARS_OK;
+}
+
+constexpr size_t kGemmSmem = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+
+}  // namespace
+
+extern "C" {
+
+int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_t max_batch, int32_t max_k,
+                          mars_batch_ctx** out) {
+    if (out == nullptr) return fail(MARS_ERR_INVALID, "mars_batch_ctx_create: out is NULL");
+    *out = nullptr;
+    if (max_nodes <= 0 || dim <= 0 || dim > 1024 || max_batch <= 0 || max_k <= 0 || max_k > MARS_MAX_TOP_K)
+        return fail(MARS_ERR_INVALID, "mars_batch_ctx_create: bad sizes");
+    MarsDeviceGuard g(device);
+    if (!g.ok) return fail(MARS_ERR_NO_DEVICE, "mars_batch_ctx_create: cudaSetDevice failed");
+    cudaDeviceProp prop;
+    MARS_CUDA_TRY(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10) return fail(MARS_ERR_NO_DEVICE, "mars_batch_ctx_create: needs sm_100a");
+    auto* c = new mars_batch_ctx();
+    c->device = device;
+    c->max_batch = max_batch;
+    c->dim = dim;
+    c->max_k = max_k;
+    c->max_nodes = max_nodes;
+    c->cap = 16384;
+    c->num_sms = prop.multiProcessorCount;
+    c->sample_tiles_cap = (max_nodes + kBN - 1) / kBN;
+    int rc = MARS_OK;
+    auto T = [&](cudaError_t e, const char* w) { if (rc == MARS_OK && e != cudaSuccess) rc = cuda_fail(e, w, __FILE__, __LINE__); };
+    T(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
+    T(cudaMalloc(&c->d_wts, (size_t)max_nodes * 4 + 16), "weights");
+    T(cudaMalloc(&c->d_margin, (size_t)max_batch * 4), "margins");
+    T(cudaMalloc(&c->d_theta, (size_t)max_batch * 4), "thresholds");
+    T(cudaMalloc(&c->d_cand, (size_t)max_batch * c->cap * 4), "candidates");
+    T(cudaMalloc(&c->d_cand_cnt, (size_t)max_batch * 4), "candidate counts");
+    T(cudaMalloc(&c->d_fallback, (size_t)max_batch * 4), "fallback flags");
+    T(cudaMalloc(&c->d_err, sizeof(int)), "error word");
+    T(cudaMallocHost(&c->h_fallback, (size_t)max_batch * 4), "pinned flags");
+    T(cudaMallocHost(&c->h_cand_cnt, (size_t)max_batch * 4), "pinned counts");
+    T(cudaMallocHost(&c->h_err, sizeof(int)), "pinned error");
+    if (rc == MARS_OK) T(cudaMemset(c->d_err, 0, sizeof(int)), "memset");
+    if (rc == MARS_OK) {
+        static bool attr_done[64] = {};
+        if (device < 64 && !attr_done[device]) {
+            T(cudaFuncSetAttribute(gemm_kernel<kSample>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem), "smem attr");
+            T(cudaFuncSetAttribute(gemm_kernel<kCandidates>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem), "smem attr");
+            attr_done[device] = rc == MARS_OK;
+        }
+    }
+    if (rc == MARS_OK) rc = mars_query_ctx_create(device, max_nodes, dim, max_k, &c->scan_ctx);
+    if (rc != MARS_OK) { mars_batch_ctx_destroy(c); return rc; }
+    *out = c;
+    return MARS_OK;
+}
+
+int mars_batch_ctx_destroy(mars_batch_ctx* c) {
+    if (c == nullptr) return MARS_OK;
+    MarsDeviceGuard g(c->device);
+    if (c->stream) cudaStreamSynchronize(c->stream);
+    cudaFree(c->d_wts); cudaFree(c->d_margin); cudaFree(c->d_theta); cudaFree(c->d_cand);
+    cudaFree(c->d_cand_cnt); cudaFree(c->d_fallback); cudaFree(c->d_sample); cudaFree(c->d_sample_rt);
+    cudaFree(c->d_err);
+    cudaFreeHost(c->h_fallback); cudaFreeHost(c->h_cand_cnt); cudaFreeHost(c->h_err);
+    mars_query_ctx_destroy(c->scan_ctx);
+    if (c->stream) cudaStreamDestroy(c->stream);
+    delete c;
+    return MARS_OK;
+}
+
+int mars_batch_last_stats(const mars_batch_ctx* c, mars_batch_stats* out) {
+    if (c == nullptr || out == nullptr) return fail(MARS_ERR_INVALID, "mars_batch_last_stats: NULL argument");
+    *out = c->last;
+    return MARS_OK;
+}
+
+int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
+                          int32_t B, float t_q, float lambda, int32_t modality_filter, int32_t use_importance,
+                          int32_t K, int32_t row_offset, int32_t* d_ids, float* d_vals, int32_t* d_counts,
+                          void* stream) {
+    if (s == nullptr || c == nullptr || d_queries == nullptr || d_ids == nullptr || d_vals == nullptr)
+        return fail(MARS_ERR_INVALID, "mars_query_batch_topk: NULL argument");
+    if (s->device != c->device || s->dim != c->dim)
+        return fail(MARS_ERR_INVALID, "mars_query_batch_topk: store and context do not match");
+    if (B < 0 || B > c->max_batch || K <= 0 || K > c->max_k)
+        return fail(MARS_ERR_INVALID, "mars_query_batch_topk: B or K out of range");
+    if (query_pitch < s->pitch || (query_pitch & 3) != 0 || (reinterpret_cast<uintptr_t>(d_queries) & 15u) != 0)
+        return fail(MARS_ERR_INVALID, "mars_query_batch_topk: queries must be 16-byte aligned rows with pitch >= the store's");
+    if (s->n > c->max_nodes)
+        return fail(MARS_ERR_CAPACITY, "mars_query_batch_topk: store larger than the context");
+    c->last = mars_batch_stats{};
+    if (B == 0) return MARS_OK;
+    MarsDeviceGuard g(c->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    MARS_CUDA_TRY(cudaStreamWaitEvent(st, s->written, 0));
+    const int32_t n = s->n;
+    const int32_t rtiles = (n + kBN - 1) / kBN;
+    const int32_t qtiles = (B + kBM - 1) / kBM;
+    const int32_t nkb = (s->pitch + kBK - 1) / kBK;
+
+    // sample size: about mu = 2 expected true top-K members in the sample
+    int32_t n_sample = (int32_t)std::ceil(2.0 * (double)n / ((double)K * kBN));
+    n_sample = std::max(1, std::min(n_sample, rtiles));
+    const double mu = (double)K * std::min<int64_t>((int64_t)n_sample * kBN, n) / std::max(n, 1);
+    const int32_t j = (int32_t)std::ceil(mu + 5.0 * std::sqrt(mu) + 3.0);
+    const bool use_gemm = n >= 4 * kBN && K >= 3 && n_sample < rtiles && j <= kJ;
+    if (!use_gemm) {
+        // small corpora: exact single-query scans, one per query
+        for (int32_t b = 0; b < B; ++b)
+            MARS_TRY(mars_scan_topk(s, c->scan_ctx, d_queries + (int64_t)b * query_pitch, t_q, lambda,
+                                    modality_filter, use_importance, K, row_offset, d_ids + (int64_t)b * K,
+                                    d_vals + (int64_t)b * K, d_counts ? d_counts + b : nullptr, st));
+        c->last.fallbacks = B;
+        c->last.path = 0;
+        return MARS_OK;
+    }
+
+    if (c->d_sample == nullptr) {
+        MARS_CUDA_TRY(cudaMalloc(&c->d_sample, (size_t)c->sample_tiles_cap * c->max_batch * kJ * 4));
+        MARS_CUDA_TRY(cudaMalloc(&c->d_sample_rt, (size_t)c->sample_tiles_cap * 4));
+    }
+    // strided sample of row tiles
+    std::vector<int32_t> srt(n_sample);
+    for (int32_t i = 0; i < n_sample; ++i) srt[i] = (int32_t)(((int64_t)i * rtiles) / n_sample);
+    MARS_CUDA_TRY(cudaMemcpyAsync(c->d_sample_rt, srt.data(), (size_t)n_sample * 4, cudaMemcpyHostToDevice, st));
+
+    CUtensorMap mq, me;
+    MARS_TRY(make_map(&mq, d_queries, B, s->pitch, query_pitch, kBM));
+    MARS_TRY(make_map(&me, s->d_E, n, s->pitch, s->pitch, kBN));
+
+    const int wblocks = std::min((n + 255) / 256, c->num_sms * 8);
+    prep_rows_kernel<<<wblocks, 256, 0, st>>>(s->d_ts, s->d_imp, s->d_mod, n, t_q, lambda, modality_filter,
+                                              use_importance, c->d_wts);
+    MARS_CUDA_TRY(cudaGetLastError());
+    prep_queries_kernel<<<(B * 32 + 255) / 256, 256, 0, st>>>(d_queries, query_pitch, B, (s->dim + 3) / 4,
+                                                              s->max_row_norm, c->d_margin, c->d_cand_cnt);
+    MARS_CUDA_TRY(cudaGetLastError());
+    MARS_CUDA_TRY(cudaMemsetAsync(c->d_err, 0, sizeof(int), st));
+
+    GemmArgs ga{};
+    ga.B = B;
+    ga.n = n;
+    ga.nkb = nkb;
+    ga.qtiles = qtiles;
+    ga.rtiles = rtiles;
+    ga.sample_rt = c->d_sample_rt;
+    ga.wts = c->d_wts;
+    ga.theta = c->d_theta;
+    ga.margin = c->d_margin;
+    ga.sample_buf = c->d_sample;
+    ga.cand = c->d_cand;
+    ga.cand_cnt = c->d_cand_cnt;
+    ga.cap = c->cap;
+    ga.err = c->d_err;
+
+    // 2. sample
+    ga.n_tiles = n_sample * qtiles;
+    gemm_kernel<kSample><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
+    MARS_CUDA_TRY(cudaGetLastError());
+    // 3. thresholds
+    threshold_kernel<<<(B * 32 + 255) / 256, 256, 0, st>>>(c->d_sample, n_sample, B, j, c->d_theta);
+    MARS_CUDA_TRY(cudaGetLastError());
+    // 4. candidates
+    ga.n_tiles = rtiles * qtiles;
+    gemm_kernel<kCandidates><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
+    MARS_CUDA_TRY(cudaGetLastError());
+    // 5. rescore
+    StoreView v{};
+    v.E = s->d_E; v.ts = s->d_ts; v.imp = s->d_imp; v.mod = s->d_mod; v.d_n = s->d_n;
+    v.pitch4 = s->pitch / 4; v.nc = (s->dim + 3) / 4;
+    if (K <= 32)
+        rescore_kernel<1><<<B, 256, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, modality_filter, use_importance, K,
+                                            row_offset, c->d_theta, c->d_cand, c->d_cand_cnt, c->cap, d_ids, d_vals,
+                                            d_counts, c->d_fallback);
+    else if (K <= 64)
+        rescore_kernel<2><<<B, 256, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, modality_filter, use_importance, K,
+                                            row_offset, c->d_theta, c->d_cand, c->d_cand_cnt, c->cap, d_ids, d_vals,
+                                            d_counts, c->d_fallback);
+    else
+        rescore_kernel<4><<<B, 256, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, modality_filter, use_importance, K,
+                                            row_offset, c->d_theta, c->d_cand, c->d_cand_cnt, c->cap, d_ids, d_vals,
+                                            d_counts, c->d_fallback);
+    MARS_CUDA_TRY(cudaGetLastError());
+    MARS_CUDA_TRY(cudaMemcpyAsync(c->h_fallback, c->d_fallback, (size_t)B * 4, cudaMemcpyDeviceToHost, st));
+    MARS_CUDA_TRY(cudaMemcpyAsync(c->h_cand_cnt, c->d_cand_cnt, (size_t)B * 4, cudaMemcpyDeviceToHost, st));
+    MARS_CUDA_TRY(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    MARS_CUDA_TRY(cudaStreamSynchronize(st));
+    if (*c->h_err != 0)
+        return fail(MARS_ERR_TIMEOUT, "mars_query_batch_topk: a tensor-core pipeline wait gave up (code " +
+                                          std::to_string(*c->h_err) + ")");
+    int64_t total = 0;
+    int32_t fb = 0, maxc = 0;
+    for (int32_t b = 0; b < B; ++b) {
+        total += c->h_cand_cnt[b];
+        maxc = std::max(maxc, c->h_cand_cnt[b]);
+        if (c->h_fallback[b]) {
+            ++fb;
+            MARS_TRY(mars_scan_topk(s, c->scan_ctx, d_queries + (int64_t)b * query_pitch, t_q, lambda,
+                                    modality_filter, use_importance, K, row_offset, d_ids + (int64_t)b * K,
+                                    d_vals + (int64_t)b * K, d_counts ? d_counts + b : nullptr, st));
+        }
+    }
+    c->last.path = 1;
+    c->last.fallbacks = fb;
+    c->last.candidates = total;
+    c->last.max_candidates = maxc;
+    c->last.sample_tiles = n_sample;
+    c->last.sample_rank = j;
+    return MARS_OK;
+}
+
+}  // extern "C"

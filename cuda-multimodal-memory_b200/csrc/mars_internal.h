@@ -76,6 +76,10 @@ struct mars_store {
     cudaStream_t stream = nullptr;
     cudaEvent_t written = nullptr;  // last write to the store
 
+    // largest row norm (bounds the error of the tensor-core short list)
+    float max_row_norm = 0.0f;
+    unsigned int* d_norm_bits = nullptr;
+
     // raw view of a caller-owned DeviceMemoryGraph (compat layer)
     void* compat_key = nullptr;
 };

@@ -62,6 +62,20 @@ __global__ void normalize_rows_kernel(float* __restrict__ E, int64_t pitch, int3
     for (int32_t d = lane; d < dim; d += 32) row[d] = __fdiv_rn(row[d], norm);
 }
 
+// Largest L2 norm of rows [first, first + count): one warp per row, the
+// maximum kept as the bit pattern of a non-negative float (order-preserving).
+__global__ void row_norm_max_kernel(const float* __restrict__ E, int64_t pitch, int32_t first,
+                                    int32_t count, int32_t dim, unsigned int* __restrict__ out_bits) {
+    const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (warp >= count) return;
+    const float* row = E + (first + warp) * pitch;
+    float s = 0.f;
+    for (int32_t d = lane; d < dim; d += 32) s = fmaf(row[d], row[d], s);
+    for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane == 0) atomicMax(out_bits, __float_as_uint(sqrtf(s) * 1.0001f));
+}
+
 __global__ void fill_f32_kernel(float* p, int64_t n, float v) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) p[i] = v;
@@ -123,6 +137,8 @@ static int alloc_store(mars_store* s) {
     MARS_CUDA_TRY(cudaMemsetAsync(s->d_mod, 0, rows * sizeof(int32_t), s->stream));
     MARS_CUDA_TRY(cudaMalloc(&s->d_n, sizeof(int32_t)));
     MARS_CUDA_TRY(cudaMemsetAsync(s->d_n, 0, sizeof(int32_t), s->stream));
+    MARS_CUDA_TRY(cudaMalloc(&s->d_norm_bits, sizeof(unsigned int)));
+    MARS_CUDA_TRY(cudaMemsetAsync(s->d_norm_bits, 0, sizeof(unsigned int), s->stream));
     if (s->edge_slack > 0) {
         MARS_CUDA_TRY(cudaMalloc(&s->d_extra, rows * (size_t)s->edge_slack * sizeof(int32_t)));
         MARS_CUDA_TRY(cudaMalloc(&s->d_extra_cnt, rows * sizeof(int32_t)));
@@ -143,6 +159,7 @@ static void release_store(mars_store* s) {
         cudaFree(s->d_col_indices);
     }
     cudaFree(s->d_n);
+    cudaFree(s->d_norm_bits);
     cudaFree(s->d_extra);
     cudaFree(s->d_extra_cnt);
     if (s->written) cudaEventDestroy(s->written);
@@ -258,7 +275,16 @@ int mars_store_upload(mars_store* s, int32_t n, const float* embeddings, const i
         std::fill(s->h_extra_cnt.begin(), s->h_extra_cnt.end(), 0);
     }
     MARS_CUDA_TRY(cudaMemcpyAsync(s->d_n, &n, sizeof(int32_t), cudaMemcpyHostToDevice, st));
+    MARS_CUDA_TRY(cudaMemsetAsync(s->d_norm_bits, 0, sizeof(unsigned int), st));
+    unsigned int norm_bits = 0;
+    if (n > 0) {
+        row_norm_max_kernel<<<(unsigned)(((int64_t)n * 32 + 255) / 256), 256, 0, st>>>(
+            s->d_E, (int64_t)P, 0, n, s->dim, s->d_norm_bits);
+        MARS_CUDA_TRY(cudaGetLastError());
+        MARS_CUDA_TRY(cudaMemcpyAsync(&norm_bits, s->d_norm_bits, 4, cudaMemcpyDeviceToHost, st));
+    }
     MARS_CUDA_TRY(cudaStreamSynchronize(st));   // n lives on this stack frame
+    std::memcpy(&s->max_row_norm, &norm_bits, 4);
     s->n = n;
     MARS_CUDA_TRY(cudaEventRecord(s->written, st));
     return MARS_OK;
@@ -294,10 +320,16 @@ int mars_store_append(mars_store* s, int32_t n, const float* embeddings, const i
     MARS_CUDA_TRY(cudaMemcpyAsync(s->d_ts + first, timestamps, (size_t)n * 4, cudaMemcpyDefault, st));
     if (importance != nullptr)
         MARS_CUDA_TRY(cudaMemcpyAsync(s->d_imp + first, importance, (size_t)n * 4, cudaMemcpyDefault, st));
+    row_norm_max_kernel<<<(unsigned)(((int64_t)n * 32 + 255) / 256), 256, 0, st>>>(
+        s->d_E, (int64_t)P, first, n, s->dim, s->d_norm_bits);
+    MARS_CUDA_TRY(cudaGetLastError());
+    unsigned int norm_bits = 0;
+    MARS_CUDA_TRY(cudaMemcpyAsync(&norm_bits, s->d_norm_bits, 4, cudaMemcpyDeviceToHost, st));
     // publish the new count after the rows (same stream)
     const int32_t new_n = first + n;
     MARS_CUDA_TRY(cudaMemcpyAsync(s->d_n, &new_n, sizeof(int32_t), cudaMemcpyHostToDevice, st));
     MARS_CUDA_TRY(cudaStreamSynchronize(st));   // new_n and caller buffers live on the host
+    std::memcpy(&s->max_row_norm, &norm_bits, 4);
     s->n = new_n;
     MARS_CUDA_TRY(cudaEventRecord(s->written, st));
     return MARS_OK;

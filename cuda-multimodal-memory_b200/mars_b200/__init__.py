@@ -72,6 +72,15 @@ class StoreInfo(C.Structure):
                 ("d_num_nodes", C.c_void_p)]
 
 
+class BatchStats(C.Structure):
+    _fields_ = [("path", C.c_int32), ("fallbacks", C.c_int32), ("candidates", C.c_int64),
+                ("max_candidates", C.c_int32), ("sample_tiles", C.c_int32),
+                ("sample_rank", C.c_int32)]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
 _VP = C.c_void_p
 _I32 = C.c_int32
 _F32 = C.c_float
@@ -101,6 +110,11 @@ _SIGS = {
     "mars_topk_merge": [_VP, _VP, _VP, _I32, _I32, _VP, _VP, _VP, _VP],
     "mars_topk_merge_batch": [_VP, _VP, _VP, _I32, _I32, _I32, _VP, _VP, _VP, _VP],
     "mars_debug_fused_scores": [_VP, _VP, _VP, _F32, _F32, _I32, _I32, _VP, _VP],
+    "mars_batch_ctx_create": [_I32, _I32, _I32, _I32, _I32, C.POINTER(_VP)],
+    "mars_batch_ctx_destroy": [_VP],
+    "mars_query_batch_topk": [_VP, _VP, _VP, _I32, _I32, _F32, _F32, _I32, _I32, _I32, _I32, _VP,
+                              _VP, _VP, _VP],
+    "mars_batch_last_stats": [_VP, C.POINTER(BatchStats)],
     "mars_scan_topk_noalloc": [_VP, _I32, _VP, _VP, _VP, _I32, _I32, _VP, _F32, _F32, _I32, _I32,
                                _I32, _I32, _VP, _VP, _VP, _VP],
 }
@@ -312,6 +326,40 @@ class QueryContext:
     def close(self):
         if getattr(self, "handle", None):
             lib().mars_query_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class BatchContext:
+    """Scratch for batched top-K on the tensor cores (mars_query_batch_topk)."""
+
+    def __init__(self, max_nodes: int, dim: int, max_batch: int, max_k: int = 128, device: int = 0):
+        h = C.c_void_p()
+        _check(lib().mars_batch_ctx_create(device, max_nodes, dim, max_batch, max_k, C.byref(h)))
+        self.handle = h
+
+    def query_batch_topk(self, store: Store, d_queries, B, t_q, lam, K, d_ids, d_vals, d_counts=None,
+                         modality_filter=-1, use_importance=False, row_offset=0, query_pitch=None,
+                         stream=None):
+        pitch = query_pitch if query_pitch is not None else (store.dim + 3) // 4 * 4
+        _check(lib().mars_query_batch_topk(store.handle, self.handle, _ptr(d_queries), pitch, B,
+                                           float(t_q), float(lam), modality_filter,
+                                           int(use_importance), K, row_offset, _ptr(d_ids),
+                                           _ptr(d_vals), _ptr(d_counts), stream))
+
+    def last_stats(self):
+        st = BatchStats()
+        _check(lib().mars_batch_last_stats(self.handle, C.byref(st)))
+        return st.as_dict()
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().mars_batch_ctx_destroy(self.handle)
             self.handle = None
 
     def __del__(self):

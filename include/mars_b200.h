@@ -243,6 +243,44 @@ int mars_topk_merge_batch(mars_query_ctx* ctx, const int32_t* d_ids_in,
 int mars_novelty(const mars_store* s, mars_query_ctx* ctx, const float* d_query,
                  float* d_max, void* stream);
 
+/* ---- batched queries on the tensor cores --------------------------------
+ * No reference counterpart: the reference answers one query per call
+ * (query_memory_fast, include/memory_cuda.cuh:188); a batch of B queries there
+ * costs B full passes over the embeddings.  Here the scores of 128 queries x
+ * 256 rows are formed per tcgen05 tile (TF32 inputs, fp32 accumulation), rows
+ * that can still reach a query's top-K are short-listed with a proven error
+ * margin, and the short list is rescored in exact fp32 with the arithmetic of
+ * mars_scan_topk -- so each query's result equals mars_scan_topk's for it.
+ * Queries whose short list cannot be proven complete are recomputed with
+ * mars_scan_topk (counted in mars_batch_stats.fallbacks). */
+typedef struct mars_batch_ctx mars_batch_ctx;
+
+typedef struct mars_batch_stats {
+    int32_t path;            /* 1: tensor-core path, 0: per-query scans (small N) */
+    int32_t fallbacks;       /* queries recomputed exactly                         */
+    int64_t candidates;      /* short-listed (query, row) pairs                    */
+    int32_t max_candidates;  /* largest short list of one query                    */
+    int32_t sample_tiles;    /* 256-row tiles in the threshold sample              */
+    int32_t sample_rank;     /* rank of the sampled bound used as threshold        */
+} mars_batch_stats;
+
+int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim,
+                          int32_t max_batch, int32_t max_k, mars_batch_ctx** out);
+int mars_batch_ctx_destroy(mars_batch_ctx* ctx);
+
+/* d_queries: B rows of query_pitch floats (16-byte aligned; values past dim
+ * must be zero).  One query time t_q for the whole batch.  Outputs d_ids /
+ * d_vals: [B][K] (ids offset by row_offset), d_counts: [B] (may be NULL).
+ * Synchronises with the host once per call (to run fallbacks). */
+int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx,
+                          const float* d_queries, int32_t query_pitch, int32_t B,
+                          float query_timestamp, float lambda,
+                          int32_t modality_filter, int32_t use_importance,
+                          int32_t K, int32_t row_offset, int32_t* d_ids,
+                          float* d_vals, int32_t* d_counts, void* stream);
+
+int mars_batch_last_stats(const mars_batch_ctx* ctx, mars_batch_stats* out);
+
 /* Fused scan top-K that allocates nothing.  No counterpart in the reference:
  * it exists for callers that may not call cudaMalloc -- processes that
  * reserve all GPU memory up front (for example a real-time loop whose memory
