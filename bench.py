@@ -55,7 +55,8 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=42)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
-    ap.add_argument("--workload", choices=["scan", "c0", "c1"], default="scan",
+    ap.add_argument("--batch", type=int, default=1024)
+    ap.add_argument("--workload", choices=["scan", "c0", "c1", "c2"], default="scan",
                     help="scan: the headline (default); c0: single-query latency at N=2400 "
                          "with BFS depth 1; c1: streaming loop (append 10 rows + query per frame)")
     ap.add_argument("--frames", type=int, default=10000)
@@ -496,9 +497,106 @@ def run_latency(a):
     print(json.dumps(line), flush=True)
 
 
+def run_batch(a):
+    """c2: batched queries on the tensor cores.  N = 1M rows (row-sharded over
+    the ranks), B = 1024 queries per step, K = 100, lambda = 0.01, t_q = 600,
+    importance on.  A step is one mars_query_batch_topk per rank (+ NCCL
+    all-gather of the [B][K] lists and mars_topk_merge_batch when sharded)."""
+    import torch
+    import mars_b200 as mb
+    from mars_b200 import datagen
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist_mod
+        from datetime import timedelta
+        dist = dist_mod
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
+                                device_id=torch.device("cuda", local))
+    K, B, D = (a.k if a.k != 10 else 100), a.batch, a.dim
+    lo, hi = a.n * rank // world, a.n * (rank + 1) // world
+    E, mod, ts, imp = datagen.gaussian_rows(lo, hi, D, seed=a.seed, ts_max=a.ts_max)
+    store = mb.Store(hi - lo, D, device=local)
+    store.upload(E, mod, ts, imp)
+    del E
+    bc = mb.BatchContext(hi - lo, D, max_batch=B, max_k=K, device=local)
+    ctx = mb.QueryContext(hi - lo, D, max_k=K, device=local)
+    Qh = datagen.queries(B, D, seed=a.seed + 1)
+    Qd = torch.from_numpy(Qh).cuda()
+    ids = torch.empty((B, K), dtype=torch.int32, device="cuda")
+    vals = torch.empty((B, K), dtype=torch.float32, device="cuda")
+    if world > 1:
+        gids = torch.empty((world, B, K), dtype=torch.int32, device="cuda")
+        gvals = torch.empty((world, B, K), dtype=torch.float32, device="cuda")
+        mids = torch.empty((B, K), dtype=torch.int32, device="cuda")
+        mvals = torch.empty((B, K), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
+    torch.cuda.set_stream(stream)
+
+    def step():
+        bc.query_batch_topk(store, Qd, B, a.ts_max, a.lam, K, ids, vals, use_importance=True,
+                            row_offset=lo, stream=ctx.stream)
+        if world > 1:
+            dist.all_gather_into_tensor(gids, ids)
+            dist.all_gather_into_tensor(gvals, vals)
+            ctx.topk_merge_batch(gids, gvals, world, K, B, mids, mvals, stream=ctx.stream)
+
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(a.steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    stats = bc.last_stats()
+    if rank == 0:
+        peaks = {}
+        try:
+            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        except Exception:
+            pass
+        flops = 2.0 * B * a.n * D
+        per_batch_s = ms * 1e-3 / a.steps
+        achieved = flops / per_batch_s / 1e12 / world
+        bf16 = float(peaks.get("bf16_tflops", 1590.0))
+        line = {"workload": "c2", "metric": f"queries/s (batched top-K, N={a.n}, D={D}, B={B}, K={K})",
+                "value": B * a.steps / (ms * 1e-3), "unit": "queries/s", "n_gpus": world,
+                "steps": a.steps, "ms_per_step": ms / a.steps, "scaling": "strong",
+                "roofline": {"bound": "tensor", "achieved": achieved, "unit": "TFLOP/s per GPU",
+                             "peak_bf16_measured": bf16, "frac_of_bf16": achieved / bf16,
+                             "tf32_nominal": bf16 / 2,
+                             "frac_of_tf32_nominal": achieved / (bf16 / 2),
+                             "flops_per_batch": flops},
+                "batch_stats_rank0": stats, "clocks": clocks}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     a = parse_args()
-    if a.workload in ("c0", "c1"):
+    if a.workload == "c2":
+        run_batch(a)
+    elif a.workload in ("c0", "c1"):
         run_latency(a)
     elif a.impl == "reference":
         run_reference(a)

@@ -15,13 +15,13 @@
 //                below the query's true K-th best score.
 //  4. candidates: the GEMM over all rows; a row becomes a candidate of a query
 //                when its upper bound reaches theta.
-//  5. rescore:   exact fp32 score of every candidate with the canonical dot
-//                (the same arithmetic as the single-query scan) and the top-K.
-//                If at least K candidates score >= theta exactly, no row
-//                outside the candidate set can beat the K-th result (its exact
-//                score is at most its upper bound, which was below theta), so
-//                the answer is exact; otherwise the query is flagged and the
-//                host re-runs it with the exact single-query scan.
+//  5. rescore:   completeness check from the candidates' bounds (K of them
+//                with lower bound >= theta prove that no row outside the list
+//                can place), pruning by the K-th best lower bound, then the
+//                exact fp32 score of the survivors with the canonical dot (the
+//                same arithmetic as the single-query scan) and the top-K.
+//                Queries that fail the check are re-run by the host with the
+//                exact single-query scan.
 //
 // GEMM: kind::tf32 (fp32 operands read by TMA straight from the store, 128-byte
 // swizzled K-major tiles), M = 128 queries x N = 256 rows per tile, K steps of
@@ -75,7 +75,8 @@ struct GemmArgs {
     const float* theta;              // B thresholds (candidate mode)
     const float* margin;             // B margins
     float* sample_buf;               // [n_tiles][B][kJ]
-    int32_t* cand;                   // [B][cap]
+    int32_t* cand;                   // [B][cap] row ids
+    float* cand_f;                   // [B][cap] approximate fused scores
     int32_t* cand_cnt;               // [B]
     int32_t cap;
     int* err;
@@ -224,7 +225,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                         if (MODE == kCandidates) {
                             if (f + slack >= th) {      // NaN weights never pass
                                 const int pos = atomicAdd(a.cand_cnt + q, 1);
-                                if (pos < a.cap) a.cand[(int64_t)q * a.cap + pos] = rbase + j;
+                                if (pos < a.cap) {
+                                    a.cand[(int64_t)q * a.cap + pos] = rbase + j;
+                                    a.cand_f[(int64_t)q * a.cap + pos] = f;
+                                }
                             }
                         } else {
                             float lo = f - slack;
@@ -311,59 +315,145 @@ __global__ void threshold_kernel(const float* __restrict__ sample_buf, int32_t n
 }
 
 // Exact rescoring of candidates: one block per query.
-template <int KPL>
-__global__ void __launch_bounds__(256)
-rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t B, float t_q,
-               float lambda, int32_t filter, int32_t use_imp, int32_t K, int32_t row_offset,
-               const float* __restrict__ theta, const int32_t* __restrict__ cand,
-               const int32_t* __restrict__ cand_cnt, int32_t cap, int32_t* __restrict__ out_ids,
-               float* __restrict__ out_vals, int32_t* __restrict__ out_cnt,
-               int32_t* __restrict__ fallback) {
-    __shared__ float   s_val[8][kMaxTopK];
-    __shared__ int32_t s_idx[8][kMaxTopK];
-    __shared__ int     s_ge;
-    const int qi = blockIdx.x;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    if (threadIdx.x == 0) s_ge = 0;
-    __syncthreads();
-    const float4* q4 = reinterpret_cast<const float4*>(Q + (int64_t)qi * qpitch);
-    const int ncand = cand_cnt[qi];
-    const bool overflow = ncand > cap;
-    const int nc_ = min(ncand, cap);
-    const float th = theta[qi];
-    const bool use_w = use_imp != 0 && s.imp != nullptr;
-    WarpTopK<KPL> top;
-    top.init(K);
-    int ge = 0;
-    for (int i = warp; i < nc_; i += 8) {
-        const int32_t r = cand[(int64_t)qi * cap + i];
-        if (filter >= 0 && __ldg(s.mod + r) != filter) continue;
-        const float4* row = reinterpret_cast<const float4*>(s.E) + (int64_t)r * s.pitch4;
-        const float dot = warp_dot_canonical(row, q4, s.nc, lane);
-        float f = fused_weight_apply(dot, __ldg(s.ts + r), t_q, lambda);
-        if (use_w) f = f * __ldg(s.imp + r);
-        ge += (f >= th) ? 1 : 0;
-        top.push(f, r + row_offset, lane);
-    }
-    if (lane == 0) atomicAdd(&s_ge, ge);
-    top.store(s_val[warp], s_idx[warp], lane);
-    __syncthreads();
-    if (warp != 0) return;
-    for (int w = 1; w < 8; ++w) top.offer_sorted(s_val[w], s_idx[w], K, lane);
-    int cnt = 0;
-#pragma unroll
-    for (int sl = 0; sl < KPL; ++sl) {
-        const int p = sl * 32 + lane;
-        const bool valid = p < K && top.i[sl] != INT32_MAX;
-        cnt += __popc(__ballot_sync(0xffffffffu, valid));
-        if (p < K) {
-            out_vals[(int64_t)qi * K + p] = valid ? top.v[sl] : -INFINITY;
-            out_ids[(int64_t)qi * K + p] = valid ? top.i[sl] : -1;
+//
+// Every candidate c carries its approximate score f_c; with the row weight w_c
+// and the query margin m its exact score lies in [lo_c, hi_c] =
+// [f_c - m|w_c|, f_c + m|w_c|].
+//  * Completeness: if at least K candidates have lo_c >= theta, K rows score
+//    >= theta exactly, so every row of the true top-K scores >= theta and --
+//    its upper bound being at least its exact score -- was short-listed.
+//    Otherwise (or on overflow) the query is flagged for the exact scan.
+//  * Pruning: with theta2 the K-th largest lo_c, a candidate with
+//    hi_c < theta2 cannot enter the top-K, so only candidates with
+//    hi_c >= theta2 are rescored exactly (typically K plus a few).
+// Both selections are block-wide bitonic sorts in shared memory ranked by
+// (score desc, id asc).
+constexpr int kSortCap = 4096;
+constexpr int kRescoreThreads = 256;
+
+__device__ __forceinline__ void block_bitonic_desc(float* key, int32_t* id, int n) {
+    for (int k = 2; k <= n; k <<= 1) {
+        for (int j = k >> 1; j > 0; j >>= 1) {
+            for (int i = threadIdx.x; i < n; i += kRescoreThreads) {
+                const int p = i ^ j;
+                if (p > i) {
+                    const float a = key[i], b = key[p];
+                    const int32_t ia = id[i], ib = id[p];
+                    const bool a_first = better(a, ia, b, ib);
+                    const bool desc = (i & k) == 0;
+                    if (desc != a_first) {
+                        key[i] = b; key[p] = a;
+                        id[i] = ib; id[p] = ia;
+                    }
+                }
+            }
+            __syncthreads();
         }
     }
-    if (lane == 0) {
-        if (out_cnt) out_cnt[qi] = cnt;
-        fallback[qi] = (overflow || s_ge < K) ? 1 : 0;
+}
+
+__device__ __forceinline__ int pow2_at_least(int n) {
+    int p = 32;
+    while (p < n) p <<= 1;
+    return p;
+}
+
+__global__ void __launch_bounds__(kRescoreThreads)
+rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t B, float t_q,
+               float lambda, int32_t use_imp, int32_t K, int32_t row_offset,
+               const float* __restrict__ theta, const float* __restrict__ margin,
+               const float* __restrict__ wts, const int32_t* __restrict__ cand,
+               const float* __restrict__ cand_f, const int32_t* __restrict__ cand_cnt, int32_t cap,
+               int32_t* __restrict__ out_ids, float* __restrict__ out_vals,
+               int32_t* __restrict__ out_cnt, int32_t* __restrict__ fallback,
+               int32_t* __restrict__ rescored) {
+    __shared__ float   s_key[kSortCap];
+    __shared__ int32_t s_id[kSortCap];
+    __shared__ int     s_ge, s_n2;
+    const int qi = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int kWarps = kRescoreThreads / 32;
+    const int ncand = cand_cnt[qi];
+    const int nc_ = min(ncand, cap);
+    if (threadIdx.x == 0) { s_ge = 0; s_n2 = 0; }
+    __syncthreads();
+    if (ncand > kSortCap || nc_ < K) {
+        // too many candidates to sort here, or too few to be complete
+        if (threadIdx.x == 0) { fallback[qi] = 1; rescored[qi] = 0; if (out_cnt) out_cnt[qi] = 0; }
+        return;
+    }
+    const float th = theta[qi];
+    const float m = margin[qi];
+    const int32_t* ci = cand + (int64_t)qi * cap;
+    const float* cf = cand_f + (int64_t)qi * cap;
+
+    // ---- pass 1: lower bounds, completeness, K-th largest lower bound -------
+    const int n1 = pow2_at_least(nc_);
+    int ge = 0;
+    for (int i = threadIdx.x; i < n1; i += kRescoreThreads) {
+        float lo = -INFINITY;
+        int32_t id = INT32_MAX;
+        if (i < nc_) {
+            lo = cf[i] - m * fabsf(__ldg(wts + ci[i]));
+            id = i;
+            ge += (lo >= th) ? 1 : 0;
+        }
+        s_key[i] = lo;
+        s_id[i] = id;
+    }
+    ge = warp_reduce_sum_int(ge);
+    if (lane == 0) atomicAdd(&s_ge, ge);
+    __syncthreads();
+    if (s_ge < K) {
+        if (threadIdx.x == 0) { fallback[qi] = 1; rescored[qi] = 0; if (out_cnt) out_cnt[qi] = 0; }
+        return;
+    }
+    block_bitonic_desc(s_key, s_id, n1);
+    const float th2 = s_key[K - 1];
+    __syncthreads();
+
+    // ---- pass 2: exact scores of the candidates that can still place -------
+    const float4* q4 = reinterpret_cast<const float4*>(Q + (int64_t)qi * qpitch);
+    const bool use_w = use_imp != 0 && s.imp != nullptr;
+    for (int base = warp * 32; base < nc_; base += kWarps * 32) {
+        const int i = base + lane;
+        bool keep = false;
+        int32_t r = 0;
+        if (i < nc_) {
+            r = ci[i];
+            keep = cf[i] + m * fabsf(__ldg(wts + r)) >= th2;
+        }
+        unsigned mk = __ballot_sync(0xffffffffu, keep);
+        while (mk) {
+            const int src = __ffs(mk) - 1;
+            mk &= mk - 1;
+            const int32_t rr = __shfl_sync(0xffffffffu, r, src);
+            const float4* row = reinterpret_cast<const float4*>(s.E) + (int64_t)rr * s.pitch4;
+            const float dot = warp_dot_canonical(row, q4, s.nc, lane);
+            float f = fused_weight_apply(dot, __ldg(s.ts + rr), t_q, lambda);
+            if (use_w) f = f * __ldg(s.imp + rr);
+            if (lane == 0) {
+                const int pos = atomicAdd(&s_n2, 1);
+                s_key[pos] = f;
+                s_id[pos] = rr + row_offset;
+            }
+        }
+    }
+    __syncthreads();
+    const int n2 = s_n2;
+    const int p2 = pow2_at_least(n2);
+    for (int i = n2 + threadIdx.x; i < p2; i += kRescoreThreads) { s_key[i] = -INFINITY; s_id[i] = INT32_MAX; }
+    __syncthreads();
+    block_bitonic_desc(s_key, s_id, p2);
+    for (int p = threadIdx.x; p < K; p += kRescoreThreads) {
+        const bool valid = p < n2;
+        out_vals[(int64_t)qi * K + p] = valid ? s_key[p] : -INFINITY;
+        out_ids[(int64_t)qi * K + p] = valid ? s_id[p] : -1;
+    }
+    if (threadIdx.x == 0) {
+        if (out_cnt) out_cnt[qi] = min(n2, K);
+        fallback[qi] = 0;
+        rescored[qi] = n2;
     }
 }
 
@@ -388,6 +478,9 @@ struct mars_batch_ctx {
     float* d_margin = nullptr;       // max_batch
     float* d_theta = nullptr;
     int32_t* d_cand = nullptr;       // max_batch * cap
+    float* d_cand_f = nullptr;       // max_batch * cap
+    int32_t* d_rescored = nullptr;   // max_batch
+    int32_t* h_rescored = nullptr;   // pinned
     int32_t* d_cand_cnt = nullptr;
     int32_t* d_fallback = nullptr;
     float* d_sample = nullptr;       // sample_tiles_cap * max_batch * kJ
@@ -465,6 +558,9 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     T(cudaMalloc(&c->d_margin, (size_t)max_batch * 4), "margins");
     T(cudaMalloc(&c->d_theta, (size_t)max_batch * 4), "thresholds");
     T(cudaMalloc(&c->d_cand, (size_t)max_batch * c->cap * 4), "candidates");
+    T(cudaMalloc(&c->d_cand_f, (size_t)max_batch * c->cap * 4), "candidate scores");
+    T(cudaMalloc(&c->d_rescored, (size_t)max_batch * 4), "rescore counts");
+    T(cudaMallocHost(&c->h_rescored, (size_t)max_batch * 4), "pinned rescore counts");
     T(cudaMalloc(&c->d_cand_cnt, (size_t)max_batch * 4), "candidate counts");
     T(cudaMalloc(&c->d_fallback, (size_t)max_batch * 4), "fallback flags");
     T(cudaMalloc(&c->d_err, sizeof(int)), "error word");
@@ -491,6 +587,7 @@ int mars_batch_ctx_destroy(mars_batch_ctx* c) {
     MarsDeviceGuard g(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     cudaFree(c->d_wts); cudaFree(c->d_margin); cudaFree(c->d_theta); cudaFree(c->d_cand);
+    cudaFree(c->d_cand_f); cudaFree(c->d_rescored); cudaFreeHost(c->h_rescored);
     cudaFree(c->d_cand_cnt); cudaFree(c->d_fallback); cudaFree(c->d_sample); cudaFree(c->d_sample_rt);
     cudaFree(c->d_err);
     cudaFreeHost(c->h_fallback); cudaFreeHost(c->h_cand_cnt); cudaFreeHost(c->h_err);
@@ -581,6 +678,7 @@ int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d
     ga.margin = c->d_margin;
     ga.sample_buf = c->d_sample;
     ga.cand = c->d_cand;
+    ga.cand_f = c->d_cand_f;
     ga.cand_cnt = c->d_cand_cnt;
     ga.cap = c->cap;
     ga.err = c->d_err;
@@ -600,30 +698,25 @@ int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d
     StoreView v{};
     v.E = s->d_E; v.ts = s->d_ts; v.imp = s->d_imp; v.mod = s->d_mod; v.d_n = s->d_n;
     v.pitch4 = s->pitch / 4; v.nc = (s->dim + 3) / 4;
-    if (K <= 32)
-        rescore_kernel<1><<<B, 256, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, modality_filter, use_importance, K,
-                                            row_offset, c->d_theta, c->d_cand, c->d_cand_cnt, c->cap, d_ids, d_vals,
-                                            d_counts, c->d_fallback);
-    else if (K <= 64)
-        rescore_kernel<2><<<B, 256, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, modality_filter, use_importance, K,
-                                            row_offset, c->d_theta, c->d_cand, c->d_cand_cnt, c->cap, d_ids, d_vals,
-                                            d_counts, c->d_fallback);
-    else
-        rescore_kernel<4><<<B, 256, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, modality_filter, use_importance, K,
-                                            row_offset, c->d_theta, c->d_cand, c->d_cand_cnt, c->cap, d_ids, d_vals,
-                                            d_counts, c->d_fallback);
+    MARS_CUDA_TRY(cudaMemsetAsync(c->d_rescored, 0, (size_t)B * 4, st));
+    rescore_kernel<<<B, kRescoreThreads, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, use_importance, K,
+                                                  row_offset, c->d_theta, c->d_margin, c->d_wts, c->d_cand,
+                                                  c->d_cand_f, c->d_cand_cnt, c->cap, d_ids, d_vals, d_counts,
+                                                  c->d_fallback, c->d_rescored);
     MARS_CUDA_TRY(cudaGetLastError());
     MARS_CUDA_TRY(cudaMemcpyAsync(c->h_fallback, c->d_fallback, (size_t)B * 4, cudaMemcpyDeviceToHost, st));
     MARS_CUDA_TRY(cudaMemcpyAsync(c->h_cand_cnt, c->d_cand_cnt, (size_t)B * 4, cudaMemcpyDeviceToHost, st));
     MARS_CUDA_TRY(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    MARS_CUDA_TRY(cudaMemcpyAsync(c->h_rescored, c->d_rescored, (size_t)B * 4, cudaMemcpyDeviceToHost, st));
     MARS_CUDA_TRY(cudaStreamSynchronize(st));
     if (*c->h_err != 0)
         return fail(MARS_ERR_TIMEOUT, "mars_query_batch_topk: a tensor-core pipeline wait gave up (code " +
                                           std::to_string(*c->h_err) + ")");
-    int64_t total = 0;
+    int64_t total = 0, rescored = 0;
     int32_t fb = 0, maxc = 0;
     for (int32_t b = 0; b < B; ++b) {
         total += c->h_cand_cnt[b];
+        rescored += c->h_rescored[b];
         maxc = std::max(maxc, c->h_cand_cnt[b]);
         if (c->h_fallback[b]) {
             ++fb;
@@ -638,6 +731,7 @@ int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d
     c->last.max_candidates = maxc;
     c->last.sample_tiles = n_sample;
     c->last.sample_rank = j;
+    c->last.rescored = rescored;
     return MARS_OK;
 }
 

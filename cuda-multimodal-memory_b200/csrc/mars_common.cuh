@@ -56,6 +56,12 @@ __device__ __forceinline__ float warp_dot_canonical(const float4* __restrict__ r
     return warp_butterfly_sum(acc);
 }
 
+__device__ __forceinline__ int warp_reduce_sum_int(int v) {
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) v += __shfl_xor_sync(MARS_FULL_MASK, v, off);
+    return v;
+}
+
 // The one definition of the temporal decay (src/memory_cuda.cu:292-310:
 // final = sim * __expf(-lambda * max(0, t_q - ts))), shared by the scan and
 // the BFS kernels so a node's score is bit-identical whichever computes it.
