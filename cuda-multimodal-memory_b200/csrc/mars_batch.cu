@@ -79,6 +79,7 @@ struct GemmArgs {
     float* cand_f;                   // [B][cap] approximate fused scores
     int32_t* cand_cnt;               // [B]
     int32_t cap;
+    int32_t self_base;               // query b leaves out row self_base + b (-1: none)
     int* err;
 };
 
@@ -190,6 +191,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
             tile_coords(a, t, MODE, qt, row0);
             const int q = qt * kBM + row_in_tile;
             const bool qv = q < a.B;
+            const int32_t self_row = a.self_base >= 0 ? a.self_base + q : -1;
             const float th = (MODE == kCandidates && qv) ? __ldg(a.theta + q) : 0.f;
             const float mg = qv ? __ldg(a.margin + q) : 0.f;
             if (!sm100::mbar_wait(tfull + buf, bphase, a.err, 5)) break;
@@ -219,7 +221,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
                         const int j = 4 * j4 + u;
-                        const float w = wv[u];
+                        const float w = (rbase + j == self_row) ? NAN : wv[u];
                         const float f = __uint_as_float(r[j]) * w;
                         const float slack = mg * fabsf(w);
                         if (MODE == kCandidates) {
@@ -550,7 +552,7 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     c->max_nodes = max_nodes;
     c->cap = 16384;
     c->num_sms = prop.multiProcessorCount;
-    c->sample_tiles_cap = (max_nodes + kBN - 1) / kBN;
+    c->sample_tiles_cap = 0;
     int rc = MARS_OK;
     auto T = [&](cudaError_t e, const char* w) { if (rc == MARS_OK && e != cudaSuccess) rc = cuda_fail(e, w, __FILE__, __LINE__); };
     T(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
@@ -607,6 +609,16 @@ int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d
                           int32_t B, float t_q, float lambda, int32_t modality_filter, int32_t use_importance,
                           int32_t K, int32_t row_offset, int32_t* d_ids, float* d_vals, int32_t* d_counts,
                           void* stream) {
+    return mars::batch_topk(s, c, d_queries, query_pitch, B, t_q, lambda, modality_filter, use_importance, K,
+                            row_offset, -1, d_ids, d_vals, d_counts, stream);
+}
+
+}  // extern "C"
+
+int mars::batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
+                     int32_t B, float t_q, float lambda, int32_t modality_filter, int32_t use_importance,
+                     int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
+                     int32_t* d_counts, void* stream) {
     if (s == nullptr || c == nullptr || d_queries == nullptr || d_ids == nullptr || d_vals == nullptr)
         return fail(MARS_ERR_INVALID, "mars_query_batch_topk: NULL argument");
     if (s->device != c->device || s->dim != c->dim)
@@ -636,15 +648,23 @@ int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d
     if (!use_gemm) {
         // small corpora: exact single-query scans, one per query
         for (int32_t b = 0; b < B; ++b)
-            MARS_TRY(mars_scan_topk(s, c->scan_ctx, d_queries + (int64_t)b * query_pitch, t_q, lambda,
-                                    modality_filter, use_importance, K, row_offset, d_ids + (int64_t)b * K,
-                                    d_vals + (int64_t)b * K, d_counts ? d_counts + b : nullptr, st));
+            MARS_TRY(mars::scan_topk_excluding(s, c->scan_ctx, d_queries + (int64_t)b * query_pitch, t_q,
+                                               lambda, modality_filter, use_importance, K, row_offset,
+                                               self_base >= 0 ? self_base + b : -1, d_ids + (int64_t)b * K,
+                                               d_vals + (int64_t)b * K, d_counts ? d_counts + b : nullptr, st));
         c->last.fallbacks = B;
         c->last.path = 0;
         return MARS_OK;
     }
 
-    if (c->d_sample == nullptr) {
+    if (c->d_sample == nullptr || n_sample > c->sample_tiles_cap) {
+        // sized for this call's sample (about 2N / (256 K) row tiles)
+        MARS_CUDA_TRY(cudaStreamSynchronize(st));
+        cudaFree(c->d_sample);
+        cudaFree(c->d_sample_rt);
+        c->d_sample = nullptr;
+        c->d_sample_rt = nullptr;
+        c->sample_tiles_cap = std::max(n_sample, 16);
         MARS_CUDA_TRY(cudaMalloc(&c->d_sample, (size_t)c->sample_tiles_cap * c->max_batch * kJ * 4));
         MARS_CUDA_TRY(cudaMalloc(&c->d_sample_rt, (size_t)c->sample_tiles_cap * 4));
     }
@@ -681,6 +701,7 @@ int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d
     ga.cand_f = c->d_cand_f;
     ga.cand_cnt = c->d_cand_cnt;
     ga.cap = c->cap;
+    ga.self_base = self_base;
     ga.err = c->d_err;
 
     // 2. sample
@@ -720,9 +741,10 @@ int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d
         maxc = std::max(maxc, c->h_cand_cnt[b]);
         if (c->h_fallback[b]) {
             ++fb;
-            MARS_TRY(mars_scan_topk(s, c->scan_ctx, d_queries + (int64_t)b * query_pitch, t_q, lambda,
-                                    modality_filter, use_importance, K, row_offset, d_ids + (int64_t)b * K,
-                                    d_vals + (int64_t)b * K, d_counts ? d_counts + b : nullptr, st));
+            MARS_TRY(mars::scan_topk_excluding(s, c->scan_ctx, d_queries + (int64_t)b * query_pitch, t_q,
+                                               lambda, modality_filter, use_importance, K, row_offset,
+                                               self_base >= 0 ? self_base + b : -1, d_ids + (int64_t)b * K,
+                                               d_vals + (int64_t)b * K, d_counts ? d_counts + b : nullptr, st));
         }
     }
     c->last.path = 1;
@@ -735,4 +757,4 @@ int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d
     return MARS_OK;
 }
 
-}  // extern "C"
+

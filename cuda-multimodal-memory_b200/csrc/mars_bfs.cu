@@ -115,7 +115,7 @@ __global__ void __launch_bounds__(kBfsThreads) bfs_hop_kernel(const BfsArgs a, i
 
 // Finalize the scores of level `last` and select the top-K of all visited
 // nodes by (score desc, id asc).
-constexpr int kFinStage = 4096;
+constexpr int kFinStage = 3072;
 
 template <int KPL>
 __global__ void __launch_bounds__(kBfsThreads) bfs_finalize_kernel(const BfsArgs a, int last) {
@@ -204,8 +204,10 @@ cudaError_t launch_bfs_finalize(const BfsArgs& a, int last_level, int k_max, int
         bfs_finalize_kernel<1><<<grid, kBfsThreads, 0, st>>>(a, last_level);
     else if (k_max <= 64)
         bfs_finalize_kernel<2><<<grid, kBfsThreads, 0, st>>>(a, last_level);
-    else
+    else if (k_max <= 128)
         bfs_finalize_kernel<4><<<grid, kBfsThreads, 0, st>>>(a, last_level);
+    else
+        bfs_finalize_kernel<8><<<grid, kBfsThreads, 0, st>>>(a, last_level);
     return cudaGetLastError();
 }
 

@@ -1,0 +1,462 @@
+// mars_cmng.cu -- CMNG: kNN-graph build (G1/G2) and greedy beam search (C1).
+//
+// Build (build_cmng, src/cmng_build.cu:135-255).  The reference forms every
+// 4096 x 4096 tile of E*E^T with cuBLAS SGEMM and merges it into per-row
+// sorted lists of k_init = 2*degree candidates with 256 threads doing
+// unsynchronised read-modify-write on the same list (:28-71), then picks
+// neighbours and cross-modal bridges with one thread per row (:75-132).
+// Here the exact k_init nearest rows of every row come from the tensor-core
+// batched top-K (mars_batch.cu) with the row itself left out -- candidates
+// short-listed on TF32 tiles with a proven margin and rescored with the exact
+// canonical dot, so the lists equal an exact fp32 kNN ranked (dot desc, id
+// asc) -- and the selection runs one warp per row.
+//
+// Search (cmng_search, src/cmng_search.cu:110-308): one block of 256 threads
+// per query, any number of queries per launch.  The reference's semantics are
+// kept step by step, with its serial thread-0 phases replaced by parallel
+// equivalents:
+//  * seeds: warp w scores node (bits(q0) ^ bits(q1)) + 7919*w mod N;
+//  * the initial exchange sort over the valid seeds (thread 0, <= 8 entries);
+//  * iteration t expands the node at beam position t (the reference marks
+//    positions, not nodes, as expanded: position t is the first unmarked one
+//    while it holds a node, and the search ends when it does not);
+//  * unvisited neighbours are scored with the reference's warp dot order
+//    (lane-strided fma, shfl_down tree), so beams agree bit for bit;
+//  * the reference inserts candidates one by one (reject if not better than
+//    the worst, bubble up past strictly smaller scores); that equals keeping
+//    the beam-width best of (beam + candidates) under (score desc, beam entries
+//    before candidates, candidates in neighbour order), computed here as a
+//    parallel rank merge;
+//  * decay of the final beam, then the reference's selection sort (first
+//    position wins among equal scores) as block argmax passes.
+// The visited set is an exact open-addressing table in shared memory (the
+// reference's 32-probe table can give up near overflow), and an id repeated
+// inside one neighbour list is scored once, at its first slot (the reference's
+// warps race on it).
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cfloat>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "mars_b200.h"
+#include "mars_common.cuh"
+#include "mars_internal.h"
+#include "mars_kernels.cuh"
+
+namespace mars {
+namespace cmng {
+
+constexpr int kThreads = 256;
+constexpr int kWarps = kThreads / 32;
+constexpr int kMaxBeam = 256;      // reference MAX_BEAM (src/cmng_search.cu:25)
+constexpr int kMaxDegree = 128;    // reference MAX_DEGREE (src/cmng_search.cu:26)
+
+// ---------------------------------------------------------------------------
+// Neighbour selection with cross-modal bridges (src/cmng_build.cu:75-132).
+__global__ void select_kernel(const int32_t* __restrict__ knn, const int32_t* __restrict__ knn_cnt,
+                              int32_t k_init, const int32_t* __restrict__ mod, int32_t N, int32_t degree,
+                              int32_t degree_cross, int32_t num_modalities, int32_t* __restrict__ out) {
+    const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (row >= N) return;
+    const int32_t* kr = knn + row * k_init;
+    const int32_t cnt = min(knn_cnt[row], k_init);
+    int32_t* o = out + row * degree;
+    const int32_t intra = degree - degree_cross;
+    for (int j = lane; j < intra; j += 32) o[j] = j < cnt ? kr[j] : -1;
+    const int32_t my_mod = mod[row];
+    int32_t b = intra;
+    for (int32_t m = 0; m < num_modalities && b < degree; ++m) {
+        if (m == my_mod) continue;
+        int32_t found = -1;
+        for (int base = 0; base < cnt; base += 32) {
+            const int i = base + lane;
+            const bool hit = i < cnt && __ldg(mod + kr[i]) == m;
+            const unsigned bal = __ballot_sync(0xffffffffu, hit);
+            if (bal) { found = kr[base + __ffs(bal) - 1]; break; }
+        }
+        if (lane == 0) o[b] = found;
+        ++b;
+    }
+    for (int j = b + lane; j < degree; j += 32) o[j] = -1;
+}
+
+// ---------------------------------------------------------------------------
+// The reference's warp dot product (src/cmng_search.cu:59-70): lane-strided
+// fused multiply-add, then a shfl_down tree; lane 0's value is the result.
+__device__ __forceinline__ float warp_dot_ref(const float* __restrict__ a, const float* __restrict__ b,
+                                              int D, int lane) {
+    float s = 0.0f;
+    for (int d = lane; d < D; d += 32) s = __fmaf_rn(__ldg(a + d), b[d], s);
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, off));
+    return __shfl_sync(0xffffffffu, s, 0);
+}
+
+struct SearchArgs {
+    const int32_t* nbrs;      // N x degree
+    const float* E;           // N x pitch
+    const float* ts;
+    const int32_t* mod;
+    int64_t pitch;
+    int32_t N, D, degree;
+    const float* Q;           // nq x qpitch
+    int64_t qpitch;
+    int32_t nq;
+    float t_q, lambda;
+    int32_t K, beam, max_iter, num_parents;
+    int32_t hash_size;        // power of two
+    int32_t* out_ids;         // nq x K
+    float* out_scores;
+    int32_t* out_mods;
+    int32_t* out_cnt;         // nq
+    int32_t* stat_iters;      // nq (may be null)
+    int32_t* stat_scored;     // nq (may be null)
+};
+
+__device__ __forceinline__ uint32_t hash32(int32_t v) {
+    uint32_t x = (uint32_t)v;
+    x ^= x >> 16; x *= 0x7feb352dU; x ^= x >> 15; x *= 0x846ca68bU; x ^= x >> 16;
+    return x;
+}
+
+// Exact set: returns true when `v` was newly inserted.
+__device__ __forceinline__ bool set_insert(int32_t* table, uint32_t mask, int32_t v) {
+    uint32_t s = hash32(v) & mask;
+    for (uint32_t probe = 0; probe <= mask; ++probe) {
+        const int32_t old = atomicCAS(table + s, -1, v);
+        if (old == -1) return true;
+        if (old == v) return false;
+        s = (s + 1) & mask;
+    }
+    return false;   // unreachable: the table is sized to at most half full
+}
+
+__device__ __forceinline__ bool set_contains(const int32_t* table, uint32_t mask, int32_t v) {
+    uint32_t s = hash32(v) & mask;
+    for (uint32_t probe = 0; probe <= mask; ++probe) {
+        const int32_t cur = table[s];
+        if (cur == v) return true;
+        if (cur == -1) return false;
+        s = (s + 1) & mask;
+    }
+    return false;
+}
+
+__global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
+    extern __shared__ __align__(16) uint8_t smem[];
+    float* s_q = reinterpret_cast<float*>(smem);                        // D (padded to 4)
+    float* s_bs = s_q + ((a.D + 3) & ~3);                               // beam scores
+    int32_t* s_bi = reinterpret_cast<int32_t*>(s_bs + kMaxBeam);       // beam ids
+    float* s_nbs = reinterpret_cast<float*>(s_bi + kMaxBeam);          // merged beam scores
+    int32_t* s_nbi = reinterpret_cast<int32_t*>(s_nbs + kMaxBeam);     // merged beam ids
+    int32_t* s_nb = s_nbi + kMaxBeam;                                   // neighbour ids
+    float* s_dist = reinterpret_cast<float*>(s_nb + kMaxDegree);       // neighbour scores
+    int32_t* s_hash = reinterpret_cast<int32_t*>(s_dist + kMaxDegree);
+    __shared__ int s_scored;
+    __shared__ float s_red_v[kWarps];
+    __shared__ int s_red_i[kWarps];
+
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int bw = a.beam;
+    const uint32_t mask = (uint32_t)a.hash_size - 1u;
+
+    for (int qi = blockIdx.x; qi < a.nq; qi += gridDim.x) {
+        const float* q = a.Q + (int64_t)qi * a.qpitch;
+        for (int d = tid; d < a.D; d += kThreads) s_q[d] = q[d];
+        for (int i = tid; i < a.hash_size; i += kThreads) s_hash[i] = -1;
+        for (int i = tid; i < bw; i += kThreads) { s_bs[i] = -FLT_MAX; s_bi[i] = -1; }
+        if (tid == 0) s_scored = 0;
+        __syncthreads();
+
+        // ---- seeds (src/cmng_search.cu:158-180) ----
+        const int num_seeds = min(8 * a.num_parents, bw);
+        if (warp < num_seeds && warp < 8) {
+            const uint32_t h = __float_as_uint(s_q[0]) ^ __float_as_uint(s_q[1]);
+            const int32_t seed = (int32_t)((h + (uint32_t)warp * 7919u) % (uint32_t)a.N);
+            const float sim = warp_dot_ref(a.E + (int64_t)seed * a.pitch, s_q, a.D, lane);
+            if (lane == 0) {
+                s_bs[warp] = sim;
+                s_bi[warp] = seed;
+                if (set_insert(s_hash, mask, seed)) atomicAdd(&s_scored, 1);
+            }
+        }
+        __syncthreads();
+        // exchange sort of the seeded positions (src/cmng_search.cu:184-193)
+        if (tid == 0) {
+            const int ns = min(min(num_seeds, 8), bw);
+            for (int i = 0; i < ns - 1; ++i)
+                for (int j = i + 1; j < ns; ++j)
+                    if (s_bs[j] > s_bs[i]) {
+                        const float t = s_bs[i]; s_bs[i] = s_bs[j]; s_bs[j] = t;
+                        const int32_t u = s_bi[i]; s_bi[i] = s_bi[j]; s_bi[j] = u;
+                    }
+        }
+        __syncthreads();
+
+        // ---- main loop (src/cmng_search.cu:196-272) ----
+        int iters = 0;
+        for (int it = 0; it < a.max_iter; ++it) {
+            if (it >= bw) break;
+            const int32_t parent = s_bi[it];
+            if (parent < 0) break;
+            ++iters;
+            const int32_t* nb = a.nbrs + (int64_t)parent * a.degree;
+            // candidate slots: valid id, not visited, first occurrence in the list
+            for (int j = tid; j < a.degree; j += kThreads) s_nb[j] = __ldg(nb + j);
+            __syncthreads();
+            for (int j = tid; j < a.degree; j += kThreads) {
+                const int32_t v = s_nb[j];
+                bool ok = v >= 0 && v < a.N && !set_contains(s_hash, mask, v);
+                for (int k = 0; ok && k < j; ++k) ok = s_nb[k] != v;
+                s_dist[j] = ok ? 0.0f : -FLT_MAX;
+            }
+            __syncthreads();
+            for (int j = warp; j < a.degree; j += kWarps) {
+                if (s_dist[j] == -FLT_MAX) continue;                    // warp-uniform
+                const int32_t v = s_nb[j];
+                const float sim = warp_dot_ref(a.E + (int64_t)v * a.pitch, s_q, a.D, lane);
+                if (lane == 0) s_dist[j] = sim;
+            }
+            __syncthreads();
+            for (int j = tid; j < a.degree; j += kThreads)
+                if (s_dist[j] > -FLT_MAX * 0.5f) { set_insert(s_hash, mask, s_nb[j]); atomicAdd(&s_scored, 1); }
+            // rank merge: beam entries keep their order and precede equal candidates
+            for (int o = tid; o < bw; o += kThreads) {
+                const float so = s_bs[o];
+                int pos = o;
+                for (int j = 0; j < a.degree; ++j) pos += (s_dist[j] > -FLT_MAX * 0.5f && s_dist[j] > so) ? 1 : 0;
+                if (pos < bw) { s_nbs[pos] = so; s_nbi[pos] = s_bi[o]; }
+            }
+            for (int j = tid; j < a.degree; j += kThreads) {
+                const float d = s_dist[j];
+                if (!(d > -FLT_MAX * 0.5f)) continue;
+                int pos = 0;
+                for (int k = 0; k < a.degree; ++k) {
+                    const float dk = s_dist[k];
+                    pos += (dk > -FLT_MAX * 0.5f && (dk > d || (dk == d && k < j))) ? 1 : 0;
+                }
+                for (int o = 0; o < bw; ++o) pos += (s_bs[o] >= d) ? 1 : 0;
+                if (pos < bw) { s_nbs[pos] = d; s_nbi[pos] = s_nb[j]; }
+            }
+            __syncthreads();
+            for (int o = tid; o < bw; o += kThreads) { s_bs[o] = s_nbs[o]; s_bi[o] = s_nbi[o]; }
+            __syncthreads();
+        }
+
+        // ---- decay (src/cmng_search.cu:275-280) ----
+        for (int o = tid; o < bw; o += kThreads) {
+            const int32_t id = s_bi[o];
+            if (id >= 0) {
+                const float age = fmaxf(0.0f, a.t_q - __ldg(a.ts + id));
+                s_bs[o] *= __expf(-a.lambda * age);
+            }
+        }
+        __syncthreads();
+        // ---- selection of the first K (src/cmng_search.cu:283-295) ----
+        const int kk = min(a.K, bw);
+        for (int i = 0; i < kk - 1; ++i) {
+            float bv = -INFINITY;
+            int bi = INT32_MAX;
+            for (int o = i + tid; o < bw; o += kThreads) {
+                const float v = s_bs[o];
+                if (v > bv || (v == bv && o < bi)) { bv = v; bi = o; }
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+                const float ov = __shfl_down_sync(0xffffffffu, bv, off);
+                const int oi = __shfl_down_sync(0xffffffffu, bi, off);
+                if (ov > bv || (ov == bv && oi < bi)) { bv = ov; bi = oi; }
+            }
+            if (lane == 0) { s_red_v[warp] = bv; s_red_i[warp] = bi; }
+            __syncthreads();
+            if (tid == 0) {
+                float v = s_red_v[0];
+                int best = s_red_i[0];
+                for (int w = 1; w < kWarps; ++w)
+                    if (s_red_v[w] > v || (s_red_v[w] == v && s_red_i[w] < best)) { v = s_red_v[w]; best = s_red_i[w]; }
+                // (max score, lowest position) = the reference's strict '>' scan
+                if (best != i && best != INT32_MAX) {
+                    const float t = s_bs[i]; s_bs[i] = s_bs[best]; s_bs[best] = t;
+                    const int32_t u = s_bi[i]; s_bi[i] = s_bi[best]; s_bi[best] = u;
+                }
+            }
+            __syncthreads();
+        }
+        if (tid == 0) {
+            int cnt = 0;
+            for (int i = 0; i < kk; ++i) {
+                if (s_bi[i] < 0) break;
+                a.out_ids[(int64_t)qi * a.K + i] = s_bi[i];
+                a.out_scores[(int64_t)qi * a.K + i] = s_bs[i];
+                if (a.out_mods) a.out_mods[(int64_t)qi * a.K + i] = __ldg(a.mod + s_bi[i]);
+                ++cnt;
+            }
+            for (int i = cnt; i < a.K; ++i) {
+                a.out_ids[(int64_t)qi * a.K + i] = -1;
+                a.out_scores[(int64_t)qi * a.K + i] = -INFINITY;
+                if (a.out_mods) a.out_mods[(int64_t)qi * a.K + i] = -1;
+            }
+            a.out_cnt[qi] = cnt;
+            if (a.stat_iters) a.stat_iters[qi] = iters;
+            if (a.stat_scored) a.stat_scored[qi] = s_scored;
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace cmng
+}  // namespace mars
+
+// ===========================================================================
+// Host side
+using namespace mars;
+using namespace mars::cmng;
+
+namespace {
+
+int hash_size_for(int32_t max_iter, int32_t degree) {
+    int64_t need = 2 * (8 + (int64_t)max_iter * degree);
+    int64_t h = 256;
+    while (h < need) h <<= 1;
+    return (int)h;
+}
+
+size_t search_smem(int32_t D, int hash_size) {
+    return (size_t)((D + 3) & ~3) * 4 + 4 * kMaxBeam * 4 + 2 * kMaxDegree * 4 + (size_t)hash_size * 4;
+}
+
+}  // namespace
+
+extern "C" {
+
+int mars_cmng_build(const mars_store* s, int32_t degree, int32_t degree_cross, int32_t num_modalities,
+                    int32_t* d_neighbors, float* build_ms) {
+    if (s == nullptr || d_neighbors == nullptr) return fail(MARS_ERR_INVALID, "mars_cmng_build: NULL argument");
+    if (degree <= 0 || degree > kMaxDegree || degree_cross < 0 || degree_cross > degree || num_modalities < 0)
+        return fail(MARS_ERR_INVALID, "mars_cmng_build: need 0 < degree <= 128, 0 <= degree_cross <= degree");
+    const int32_t N = s->n;
+    if (N < 2) return fail(MARS_ERR_INVALID, "mars_cmng_build: need at least 2 rows");
+    const int32_t k_init = std::min(2 * degree, std::min(N - 1, (int32_t)MARS_MAX_TOP_K));
+    MarsDeviceGuard g(s->device);
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    MARS_CUDA_TRY(cudaEventCreate(&e0));
+    MARS_CUDA_TRY(cudaEventCreate(&e1));
+    const int32_t chunk = std::min(N, 4096);
+    mars_batch_ctx* bc = nullptr;
+    int rc = mars_batch_ctx_create(s->device, N, s->dim, chunk, k_init, &bc);
+    int32_t* d_knn = nullptr;
+    int32_t* d_cnt = nullptr;
+    float* d_vals = nullptr;
+    cudaStream_t st = s->stream;
+    if (rc == MARS_OK && (cudaMalloc(&d_knn, (size_t)N * k_init * 4) != cudaSuccess ||
+                          cudaMalloc(&d_vals, (size_t)N * k_init * 4) != cudaSuccess ||
+                          cudaMalloc(&d_cnt, (size_t)N * 4) != cudaSuccess))
+        rc = fail(MARS_ERR_OOM, "mars_cmng_build: kNN buffers");
+    if (rc == MARS_OK) cudaEventRecord(e0, st);
+    for (int32_t c0 = 0; rc == MARS_OK && c0 < N; c0 += chunk) {
+        const int32_t b = std::min(chunk, N - c0);
+        // rows as queries; plain dot products (lambda = 0: weight exactly 1)
+        rc = mars::batch_topk(s, bc, s->d_E + (size_t)c0 * s->pitch, s->pitch, b, 0.0f, 0.0f, -1, 0, k_init, 0,
+                              c0, d_knn + (size_t)c0 * k_init, d_vals + (size_t)c0 * k_init, d_cnt + c0, st);
+    }
+    if (rc == MARS_OK) {
+        select_kernel<<<(unsigned)(((int64_t)N * 32 + 255) / 256), 256, 0, st>>>(
+            d_knn, d_cnt, k_init, s->d_mod, N, degree, degree_cross, num_modalities, d_neighbors);
+        if (cudaGetLastError() != cudaSuccess) rc = fail(MARS_ERR_CUDA, "mars_cmng_build: select launch");
+    }
+    if (rc == MARS_OK) {
+        cudaEventRecord(e1, st);
+        if (cudaStreamSynchronize(st) != cudaSuccess) rc = fail(MARS_ERR_CUDA, "mars_cmng_build: sync");
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, e0, e1);
+        if (build_ms) *build_ms = ms;
+    }
+    cudaFree(d_knn);
+    cudaFree(d_vals);
+    cudaFree(d_cnt);
+    mars_batch_ctx_destroy(bc);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    return rc;
+}
+
+int mars_cmng_knn(const mars_store* s, int32_t k, int32_t* d_ids, float* d_vals, int32_t* d_counts) {
+    if (s == nullptr || d_ids == nullptr || d_vals == nullptr) return fail(MARS_ERR_INVALID, "mars_cmng_knn: NULL argument");
+    const int32_t N = s->n;
+    if (k <= 0 || k > MARS_MAX_TOP_K || k > N - 1) return fail(MARS_ERR_INVALID, "mars_cmng_knn: k out of range");
+    MarsDeviceGuard g(s->device);
+    const int32_t chunk = std::min(N, 4096);
+    mars_batch_ctx* bc = nullptr;
+    MARS_TRY(mars_batch_ctx_create(s->device, N, s->dim, chunk, k, &bc));
+    int rc = MARS_OK;
+    for (int32_t c0 = 0; rc == MARS_OK && c0 < N; c0 += chunk) {
+        const int32_t b = std::min(chunk, N - c0);
+        rc = mars::batch_topk(s, bc, s->d_E + (size_t)c0 * s->pitch, s->pitch, b, 0.0f, 0.0f, -1, 0, k, 0, c0,
+                              d_ids + (size_t)c0 * k, d_vals + (size_t)c0 * k, d_counts ? d_counts + c0 : nullptr,
+                              s->stream);
+    }
+    if (rc == MARS_OK && cudaStreamSynchronize(s->stream) != cudaSuccess) rc = fail(MARS_ERR_CUDA, "mars_cmng_knn: sync");
+    mars_batch_ctx_destroy(bc);
+    return rc;
+}
+
+int mars_cmng_search_batch(const mars_store* s, const int32_t* d_neighbors, int32_t degree,
+                           const float* d_queries, int32_t query_pitch, int32_t nq, float t_q,
+                           const mars_cmng_config* cfg, int32_t* d_ids, float* d_scores, int32_t* d_mods,
+                           int32_t* d_counts, int32_t* d_iters, int32_t* d_scored, void* stream) {
+    if (s == nullptr || d_neighbors == nullptr || d_queries == nullptr || cfg == nullptr || d_ids == nullptr ||
+        d_scores == nullptr || d_counts == nullptr)
+        return fail(MARS_ERR_INVALID, "mars_cmng_search_batch: NULL argument");
+    if (degree <= 0 || degree > kMaxDegree) return fail(MARS_ERR_INVALID, "mars_cmng_search_batch: degree must be in [1, 128]");
+    if (cfg->K <= 0 || cfg->max_iterations < 0 || cfg->num_parents < 0 || cfg->beam_width <= 0)
+        return fail(MARS_ERR_INVALID, "mars_cmng_search_batch: bad configuration");
+    if (query_pitch < s->dim || s->n <= 0 || s->dim < 2)
+        return fail(MARS_ERR_INVALID, "mars_cmng_search_batch: query pitch, empty store or dim < 2");
+    if (nq == 0) return MARS_OK;
+    const int hs = hash_size_for(cfg->max_iterations, degree);
+    if (hs > 32768) return fail(MARS_ERR_UNSUPPORTED, "mars_cmng_search_batch: max_iterations x degree too large");
+    MarsDeviceGuard g(s->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : s->stream;
+    MARS_CUDA_TRY(cudaStreamWaitEvent(st, s->written, 0));
+    SearchArgs a{};
+    a.nbrs = d_neighbors;
+    a.E = s->d_E;
+    a.ts = s->d_ts;
+    a.mod = s->d_mod;
+    a.pitch = s->pitch;
+    a.N = s->n;
+    a.D = s->dim;
+    a.degree = degree;
+    a.Q = d_queries;
+    a.qpitch = query_pitch;
+    a.nq = nq;
+    a.t_q = t_q;
+    a.lambda = cfg->time_decay_lambda;
+    a.K = cfg->K;
+    a.beam = std::min(cfg->beam_width, (int32_t)kMaxBeam);   // src/cmng_search.cu:356
+    a.max_iter = cfg->max_iterations;
+    a.num_parents = cfg->num_parents;
+    a.hash_size = hs;
+    a.out_ids = d_ids;
+    a.out_scores = d_scores;
+    a.out_mods = d_mods;
+    a.out_cnt = d_counts;
+    a.stat_iters = d_iters;
+    a.stat_scored = d_scored;
+    const size_t smem = search_smem(s->dim, hs);
+    if (smem > 48 * 1024)
+        MARS_CUDA_TRY(cudaFuncSetAttribute(search_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int nb = 0, dev = s->device, sms = 0;
+    MARS_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, search_kernel, kThreads, smem));
+    MARS_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    const int grid = std::max(1, std::min(nq, std::max(nb, 1) * sms));
+    search_kernel<<<grid, kThreads, smem, st>>>(a);
+    MARS_CUDA_TRY(cudaGetLastError());
+    return MARS_OK;
+}
+
+}  // extern "C"

@@ -15,7 +15,7 @@
 namespace mars {
 
 constexpr int kWarp = 32;
-constexpr int kMaxTopK = 128;
+constexpr int kMaxTopK = 256;
 
 // ---------------------------------------------------------------------------
 // Streaming 128-bit load: read-only path, no L1 allocation (each embedding

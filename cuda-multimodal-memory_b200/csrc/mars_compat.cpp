@@ -9,6 +9,7 @@
 
 #include <algorithm>
 #include <cstdio>
+#include <cstring>
 #include <cstdlib>
 #include <mutex>
 #include <stdexcept>
@@ -18,6 +19,7 @@
 
 #include "mars_b200.h"
 #include "mars_internal.h"
+#include "cmng.cuh"
 #include "memory_cuda.cuh"
 
 namespace {
@@ -337,4 +339,136 @@ int32_t maintain_graph(DeviceMemoryGraph& dg, int32_t min_hits, int32_t window_q
     for (int32_t v : h) low += v <= min_hits ? 1 : 0;
     CUDA_CHECK(cudaMemset(dg.d_edge_hits, 0, h.size() * 4));
     return low;
+}
+
+// ===========================================================================
+// include/cmng.cuh
+CMNGGraph build_cmng(const float* h_embeddings, const int32_t* h_modalities, const float* h_timestamps,
+                     int32_t N, int32_t D, int32_t degree, int32_t degree_cross) {
+    mars_store* s = nullptr;
+    check(mars_store_create(current_device(), N, std::max(D, 1), 0, &s), "build_cmng");
+    check(mars_store_upload(s, N, h_embeddings, h_modalities, h_timestamps, nullptr, nullptr, nullptr, 0),
+          "build_cmng");
+    CMNGGraph g;
+    g.N = N;
+    g.D = D;
+    g.degree = degree;
+    g.degree_cross = degree_cross;
+    CUDA_CHECK(cudaMalloc(&g.d_neighbors, (size_t)std::max(N, 1) * degree * sizeof(int32_t)));
+    // the reference selects bridges for MOD_COUNT = 3 modalities (src/cmng_build.cu:234)
+    check(mars_cmng_build(s, degree, degree_cross, 3, g.d_neighbors, &g.build_time_ms), "build_cmng");
+    g.d_embeddings = s->d_E;
+    g.d_modalities = s->d_mod;
+    g.d_timestamps = s->d_ts;
+    Registry& r = reg();
+    std::lock_guard<std::mutex> lk(r.mu);
+    r.stores[s->d_E] = s;
+    return g;
+}
+
+void cmng_upload_fp16(CMNGGraph& g) {
+    if (g.N <= 0 || g.d_embeddings == nullptr) return;
+    DeviceMemoryGraph dg;
+    dg.num_nodes = g.N;
+    dg.embedding_dim = g.D;
+    dg.d_embeddings = g.d_embeddings;
+    upload_fp16_embeddings(dg);
+    g.d_embeddings_fp16 = dg.d_embeddings_fp16;
+}
+
+void free_cmng(CMNGGraph& g) {
+    if (g.d_neighbors) cudaFree(g.d_neighbors);
+    if (g.d_embeddings_fp16) cudaFree(g.d_embeddings_fp16);
+    DeviceMemoryGraph dg;
+    dg.d_embeddings = g.d_embeddings;
+    free_device(dg);
+    g = CMNGGraph{};
+}
+
+CMNGSearchContext create_cmng_context(int32_t D, int32_t max_beam, int32_t max_k) {
+    CMNGSearchContext ctx;
+    ctx.max_D = D;
+    ctx.max_K = max_k;
+    ctx.max_beam = max_beam;
+    CUDA_CHECK(cudaMalloc(&ctx.d_result_ids, (size_t)std::max(max_k, 1) * sizeof(int32_t)));
+    CUDA_CHECK(cudaMalloc(&ctx.d_result_scores, (size_t)std::max(max_k, 1) * sizeof(float)));
+    CUDA_CHECK(cudaMalloc(&ctx.d_result_mods, (size_t)std::max(max_k, 1) * sizeof(int32_t)));
+    CUDA_CHECK(cudaMalloc(&ctx.d_result_count, sizeof(int32_t)));
+    CUDA_CHECK(cudaMalloc(&ctx.d_query, (size_t)((D + 3) & ~3) * sizeof(float)));
+    CUDA_CHECK(cudaMemset(ctx.d_query, 0, (size_t)((D + 3) & ~3) * sizeof(float)));
+    CUDA_CHECK(cudaMallocHost(&ctx.h_query_pinned, (size_t)std::max(D, 1) * sizeof(float)));
+    CUDA_CHECK(cudaEventCreate(&ctx.e_start));
+    CUDA_CHECK(cudaEventCreate(&ctx.e_end));
+    CUDA_CHECK(cudaStreamCreateWithFlags(&ctx.stream, cudaStreamNonBlocking));
+    ctx.valid = true;
+    return ctx;
+}
+
+void destroy_cmng_context(CMNGSearchContext& ctx) {
+    if (!ctx.valid) return;
+    cudaStreamSynchronize(ctx.stream);
+    cudaFree(ctx.d_result_ids);
+    cudaFree(ctx.d_result_scores);
+    cudaFree(ctx.d_result_mods);
+    cudaFree(ctx.d_result_count);
+    cudaFree(ctx.d_query);
+    cudaFreeHost(ctx.h_query_pinned);
+    cudaEventDestroy(ctx.e_start);
+    cudaEventDestroy(ctx.e_end);
+    cudaStreamDestroy(ctx.stream);
+    ctx = CMNGSearchContext{};
+}
+
+std::vector<QueryResult> cmng_search(const CMNGGraph& g, CMNGSearchContext& ctx, const float* h_query,
+                                     float query_timestamp, const CMNGSearchConfig& cfg,
+                                     RetrievalStats& stats) {
+    if (!ctx.valid) die(MARS_ERR_INVALID, "cmng_search (invalid context)");
+    DeviceMemoryGraph dg;
+    dg.num_nodes = g.N;
+    dg.embedding_dim = g.D;
+    dg.d_embeddings = g.d_embeddings;
+    dg.d_modalities = g.d_modalities;
+    dg.d_timestamps = g.d_timestamps;
+    StoreRef sr(dg);
+    const int32_t K = std::min(cfg.K, ctx.max_K);   // src/cmng_search.cu:355
+    if (K <= 0) return {};
+    std::memcpy(ctx.h_query_pinned, h_query, (size_t)g.D * sizeof(float));
+    CUDA_CHECK(cudaMemcpyAsync(ctx.d_query, ctx.h_query_pinned, (size_t)g.D * sizeof(float),
+                               cudaMemcpyHostToDevice, ctx.stream));
+    mars_cmng_config c{};
+    c.K = K;
+    c.beam_width = cfg.beam_width;
+    c.max_iterations = cfg.max_iterations;
+    c.num_parents = cfg.num_parents;
+    c.time_decay_lambda = cfg.time_decay_lambda;
+    c.modality_filter = cfg.modality_filter;
+    c.use_fp16 = cfg.use_fp16 ? 1 : 0;
+    CUDA_CHECK(cudaEventRecord(ctx.e_start, ctx.stream));
+    check(mars_cmng_search_batch(sr.s, g.d_neighbors, g.degree, ctx.d_query, (g.D + 3) & ~3, 1, query_timestamp,
+                                 &c, ctx.d_result_ids, ctx.d_result_scores, ctx.d_result_mods,
+                                 ctx.d_result_count, nullptr, nullptr, ctx.stream),
+          "cmng_search");
+    CUDA_CHECK(cudaEventRecord(ctx.e_end, ctx.stream));
+    int32_t count = 0;
+    CUDA_CHECK(cudaMemcpyAsync(&count, ctx.d_result_count, sizeof(int32_t), cudaMemcpyDeviceToHost, ctx.stream));
+    CUDA_CHECK(cudaStreamSynchronize(ctx.stream));
+    count = std::min(count, K);
+    std::vector<int32_t> ids((size_t)std::max(count, 0)), mods((size_t)std::max(count, 0));
+    std::vector<float> scores((size_t)std::max(count, 0));
+    if (count > 0) {
+        CUDA_CHECK(cudaMemcpy(ids.data(), ctx.d_result_ids, (size_t)count * 4, cudaMemcpyDeviceToHost));
+        CUDA_CHECK(cudaMemcpy(scores.data(), ctx.d_result_scores, (size_t)count * 4, cudaMemcpyDeviceToHost));
+        CUDA_CHECK(cudaMemcpy(mods.data(), ctx.d_result_mods, (size_t)count * 4, cudaMemcpyDeviceToHost));
+    }
+    std::vector<QueryResult> out;
+    out.reserve((size_t)count);
+    for (int32_t i = 0; i < count; ++i) out.push_back({ids[i], scores[i], mods[i], 0});
+    cudaEventElapsedTime(&stats.gpu_ms_total, ctx.e_start, ctx.e_end);
+    stats.gpu_ms_similarity = stats.gpu_ms_total;
+    stats.gpu_ms_topk = 0;
+    stats.gpu_ms_bfs = 0;
+    stats.gpu_ms_rerank = 0;
+    stats.nodes_scanned = 0;
+    stats.bfs_waves = 0;
+    return out;
 }

@@ -9,10 +9,26 @@
 
 #include "mars_b200.h"
 
+struct mars_store;
+struct mars_query_ctx;
+
 // ---- error plumbing ------------------------------------------------------
 namespace mars {
 
 void set_error(const std::string& msg);
+
+// mars_query_batch_topk where query b leaves out row self_base + b
+// (self_base < 0: none); used by the kNN-graph build.
+int batch_topk(const mars_store* s, struct mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
+               int32_t B, float t_q, float lambda, int32_t modality_filter, int32_t use_importance,
+               int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
+               int32_t* d_counts, void* stream);
+
+// mars_scan_topk that leaves out one local row (exclude_row < 0: none).
+int scan_topk_excluding(const mars_store* s, mars_query_ctx* c, const float* d_query, float t_q,
+                        float lambda, int32_t modality_filter, int32_t use_importance, int32_t K,
+                        int32_t row_offset, int32_t exclude_row, int32_t* d_ids, float* d_vals,
+                        int32_t* d_count, void* stream);
 int fail(int status, const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what, const char* file, int line);
 

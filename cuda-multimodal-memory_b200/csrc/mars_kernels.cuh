@@ -26,7 +26,8 @@ struct MarsQueryDesc {
     int32_t  hops;
     uint32_t epoch;
     int32_t  row_offset;
-    int32_t  reserved[7];
+    int32_t  exclude_plus1;   // 1 + local row to leave out (0: none)
+    int32_t  reserved[6];
 };
 constexpr size_t kDescQueryOffset = 64;
 static_assert(sizeof(MarsQueryDesc) <= kDescQueryOffset, "descriptor too large");

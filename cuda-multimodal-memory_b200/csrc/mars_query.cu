@@ -60,7 +60,7 @@ int check_cfg(const mars_query_ctx* c, int K, int hops, const char* fn) {
     return MARS_OK;
 }
 
-int kpl_class(int K) { return K <= 32 ? 32 : (K <= 64 ? 64 : 128); }
+int kpl_class(int K) { return K <= 32 ? 32 : (K <= 64 ? 64 : (K <= 128 ? 128 : 256)); }
 
 uint32_t next_epoch(mars_query_ctx* c, cudaStream_t st, int* status) {
     *status = MARS_OK;
@@ -376,6 +376,16 @@ int mars_query_once(const mars_store* s, const float* query, float t_q,
 int mars_scan_topk(const mars_store* s, mars_query_ctx* c, const float* d_query, float t_q, float lambda,
                    int32_t modality_filter, int32_t use_importance, int32_t K, int32_t row_offset,
                    int32_t* d_ids, float* d_vals, int32_t* d_count, void* stream) {
+    return mars::scan_topk_excluding(s, c, d_query, t_q, lambda, modality_filter, use_importance, K,
+                                     row_offset, -1, d_ids, d_vals, d_count, stream);
+}
+
+}  // extern "C"
+
+int mars::scan_topk_excluding(const mars_store* s, mars_query_ctx* c, const float* d_query, float t_q,
+                              float lambda, int32_t modality_filter, int32_t use_importance, int32_t K,
+                              int32_t row_offset, int32_t exclude_row, int32_t* d_ids, float* d_vals,
+                              int32_t* d_count, void* stream) {
     MARS_TRY(check_store_ctx(s, c, "mars_scan_topk"));
     if (d_query == nullptr || d_ids == nullptr || d_vals == nullptr)
         return fail(MARS_ERR_INVALID, "mars_scan_topk: NULL argument");
@@ -395,6 +405,7 @@ int mars_scan_topk(const mars_store* s, mars_query_ctx* c, const float* d_query,
     sa.d.use_imp = use_importance;
     sa.d.K = K;
     sa.d.row_offset = row_offset;
+    sa.d.exclude_plus1 = exclude_row + 1;
     sa.dyn = nullptr;
     sa.q = reinterpret_cast<const float4*>(d_query);
     sa.part_val = c->d_part_val;
@@ -406,6 +417,8 @@ int mars_scan_topk(const mars_store* s, mars_query_ctx* c, const float* d_query,
     MARS_CUDA_TRY(launch_scan_topk(sa, K, c->scan_blocks, st));
     return MARS_OK;
 }
+
+extern "C" {
 
 int mars_topk_merge(mars_query_ctx* c, const int32_t* d_ids_in, const float* d_vals_in, int32_t n_lists,
                     int32_t K, int32_t* d_ids_out, float* d_vals_out, int32_t* d_count, void* stream) {

@@ -81,7 +81,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_topk_kernel(const ScanAr
         const float t = __shfl_sync(MARS_FULL_MASK, ts_w, src);
         const float im = __shfl_sync(MARS_FULL_MASK, imp_w, src);
         const int32_t m = __shfl_sync(MARS_FULL_MASK, mod_w, src);
-        if (filter >= 0 && m != filter) {
+        if ((filter >= 0 && m != filter) || row + 1 == d.exclude_plus1) {
             if (ALL && lane == 0) a.all_scores[row] = -FLT_MAX;
             return;
         }
@@ -280,7 +280,8 @@ cudaError_t launch_scan_topk(const ScanArgs& a, int k_max, int grid, cudaStream_
     const bool all = a.all_scores != nullptr;
     if (k_max <= 32) return all ? launch_scan_kpl<1, true>(a, grid, st) : launch_scan_kpl<1, false>(a, grid, st);
     if (k_max <= 64) return all ? launch_scan_kpl<2, true>(a, grid, st) : launch_scan_kpl<2, false>(a, grid, st);
-    return all ? launch_scan_kpl<4, true>(a, grid, st) : launch_scan_kpl<4, false>(a, grid, st);
+    if (k_max <= 128) return all ? launch_scan_kpl<4, true>(a, grid, st) : launch_scan_kpl<4, false>(a, grid, st);
+    return all ? launch_scan_kpl<8, true>(a, grid, st) : launch_scan_kpl<8, false>(a, grid, st);
 }
 
 cudaError_t launch_topk_merge(const int32_t* ids_in, const float* vals_in, int n_lists, int K, int Q,
@@ -289,8 +290,10 @@ cudaError_t launch_topk_merge(const int32_t* ids_in, const float* vals_in, int n
         topk_merge_kernel<1><<<Q, kScanThreads, 0, st>>>(ids_in, vals_in, n_lists, K, Q, ids_out, vals_out, cnt);
     else if (K <= 64)
         topk_merge_kernel<2><<<Q, kScanThreads, 0, st>>>(ids_in, vals_in, n_lists, K, Q, ids_out, vals_out, cnt);
-    else
+    else if (K <= 128)
         topk_merge_kernel<4><<<Q, kScanThreads, 0, st>>>(ids_in, vals_in, n_lists, K, Q, ids_out, vals_out, cnt);
+    else
+        topk_merge_kernel<8><<<Q, kScanThreads, 0, st>>>(ids_in, vals_in, n_lists, K, Q, ids_out, vals_out, cnt);
     return cudaGetLastError();
 }
 
@@ -300,7 +303,7 @@ int scan_blocks_per_sm(int nc, int k_max) {
     cudaError_t e = cudaErrorInvalidValue;
 #define MARS_OCC(KPL_, CPL_) \
     e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, scan_topk_kernel<KPL_, CPL_, false>, kScanThreads, 0)
-    const int kpl = k_max <= 32 ? 1 : (k_max <= 64 ? 2 : 4);
+    const int kpl = k_max <= 32 ? 1 : (k_max <= 64 ? 2 : (k_max <= 128 ? 4 : 8));
     if (kpl == 1) {
         switch (cpl) { case 1: MARS_OCC(1, 1); break; case 2: MARS_OCC(1, 2); break; case 3: MARS_OCC(1, 3); break;
                        case 4: MARS_OCC(1, 4); break; case 5: MARS_OCC(1, 5); break; case 6: MARS_OCC(1, 6); break;
@@ -309,10 +312,14 @@ int scan_blocks_per_sm(int nc, int k_max) {
         switch (cpl) { case 1: MARS_OCC(2, 1); break; case 2: MARS_OCC(2, 2); break; case 3: MARS_OCC(2, 3); break;
                        case 4: MARS_OCC(2, 4); break; case 5: MARS_OCC(2, 5); break; case 6: MARS_OCC(2, 6); break;
                        case 7: MARS_OCC(2, 7); break; default: MARS_OCC(2, 8); break; }
-    } else {
+    } else if (kpl == 4) {
         switch (cpl) { case 1: MARS_OCC(4, 1); break; case 2: MARS_OCC(4, 2); break; case 3: MARS_OCC(4, 3); break;
                        case 4: MARS_OCC(4, 4); break; case 5: MARS_OCC(4, 5); break; case 6: MARS_OCC(4, 6); break;
                        case 7: MARS_OCC(4, 7); break; default: MARS_OCC(4, 8); break; }
+    } else {
+        switch (cpl) { case 1: MARS_OCC(8, 1); break; case 2: MARS_OCC(8, 2); break; case 3: MARS_OCC(8, 3); break;
+                       case 4: MARS_OCC(8, 4); break; case 5: MARS_OCC(8, 5); break; case 6: MARS_OCC(8, 6); break;
+                       case 7: MARS_OCC(8, 7); break; default: MARS_OCC(8, 8); break; }
     }
 #undef MARS_OCC
     return (e == cudaSuccess && nb > 0) ? nb : 1;

@@ -81,6 +81,18 @@ class BatchStats(C.Structure):
         return {k: getattr(self, k) for k, _ in self._fields_}
 
 
+class CmngConfig(C.Structure):
+    """mars_cmng_config (CMNGSearchConfig, include/cmng.cuh:54-62)."""
+    _fields_ = [("K", C.c_int32), ("beam_width", C.c_int32), ("max_iterations", C.c_int32),
+                ("num_parents", C.c_int32), ("time_decay_lambda", C.c_float),
+                ("modality_filter", C.c_int32), ("use_fp16", C.c_int32)]
+
+    def __init__(self, K=10, beam_width=128, max_iterations=64, num_parents=1,
+                 time_decay_lambda=1e-8, modality_filter=-1, use_fp16=False):
+        super().__init__(K, beam_width, max_iterations, num_parents, time_decay_lambda,
+                         modality_filter, int(use_fp16))
+
+
 _VP = C.c_void_p
 _I32 = C.c_int32
 _F32 = C.c_float
@@ -115,6 +127,10 @@ _SIGS = {
     "mars_query_batch_topk": [_VP, _VP, _VP, _I32, _I32, _F32, _F32, _I32, _I32, _I32, _I32, _VP,
                               _VP, _VP, _VP],
     "mars_batch_last_stats": [_VP, C.POINTER(BatchStats)],
+    "mars_cmng_build": [_VP, _I32, _I32, _I32, _VP, C.POINTER(C.c_float)],
+    "mars_cmng_knn": [_VP, _I32, _VP, _VP, _VP],
+    "mars_cmng_search_batch": [_VP, _VP, _I32, _VP, _I32, _I32, _F32, C.POINTER(CmngConfig), _VP,
+                               _VP, _VP, _VP, _VP, _VP, _VP],
     "mars_scan_topk_noalloc": [_VP, _I32, _VP, _VP, _VP, _I32, _I32, _VP, _F32, _F32, _I32, _I32,
                                _I32, _I32, _VP, _VP, _VP, _VP],
 }
@@ -367,6 +383,28 @@ class BatchContext:
             self.close()
         except Exception:
             pass
+
+
+def cmng_build(store: Store, degree, degree_cross, num_modalities, d_neighbors) -> float:
+    """build_cmng over the store's rows into d_neighbors (N x degree, device)."""
+    ms = C.c_float()
+    _check(lib().mars_cmng_build(store.handle, degree, degree_cross, num_modalities,
+                                 _ptr(d_neighbors), C.byref(ms)))
+    return ms.value
+
+
+def cmng_knn(store: Store, k, d_ids, d_vals, d_counts=None):
+    _check(lib().mars_cmng_knn(store.handle, k, _ptr(d_ids), _ptr(d_vals), _ptr(d_counts)))
+
+
+def cmng_search_batch(store: Store, d_neighbors, degree, d_queries, nq, t_q, cfg: CmngConfig,
+                      d_ids, d_scores, d_counts, d_mods=None, d_iters=None, d_scored=None,
+                      query_pitch=None, stream=None):
+    pitch = query_pitch if query_pitch is not None else (store.dim + 3) // 4 * 4
+    _check(lib().mars_cmng_search_batch(store.handle, _ptr(d_neighbors), degree, _ptr(d_queries),
+                                        pitch, nq, float(t_q), C.byref(cfg), _ptr(d_ids),
+                                        _ptr(d_scores), _ptr(d_mods), _ptr(d_counts),
+                                        _ptr(d_iters), _ptr(d_scored), stream))
 
 
 def scan_topk_noalloc(d_embeddings, row_pitch, d_timestamps, d_importance, d_modalities, n, dim,

@@ -28,7 +28,7 @@ extern "C" {
 #endif
 
 #define MARS_B200_ABI_VERSION 1
-#define MARS_MAX_TOP_K 128      /* reference: MAX_TOP_K = 64 (src/memory_cuda.cu:38) */
+#define MARS_MAX_TOP_K 256      /* reference: MAX_TOP_K = 64 (src/memory_cuda.cu:38) */
 #define MARS_MAX_BFS_HOPS 14
 
 /* ---- status ------------------------------------------------------------ */
@@ -281,6 +281,46 @@ int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx,
                           float* d_vals, int32_t* d_counts, void* stream);
 
 int mars_batch_last_stats(const mars_batch_ctx* ctx, mars_batch_stats* out);
+
+/* ---- CMNG kNN graph (include/cmng.cuh) --------------------------------- */
+
+/* CMNGSearchConfig, include/cmng.cuh:54-62 (bools widened to int32). */
+typedef struct mars_cmng_config {
+    int32_t K;
+    int32_t beam_width;
+    int32_t max_iterations;
+    int32_t num_parents;
+    float   time_decay_lambda;
+    int32_t modality_filter;   /* accepted, unused (as in the reference) */
+    int32_t use_fp16;          /* accepted, unused: fp32 rows are scored */
+} mars_cmng_config;
+
+/* build_cmng (include/cmng.cuh:91-96, src/cmng_build.cu:135-255) over the
+ * store's rows: for every row the k_init = 2*degree nearest other rows by
+ * dot product (exact fp32, ties by id), then the first degree-degree_cross of
+ * them and, for every modality m < num_modalities other than the row's own,
+ * the nearest kNN entry of modality m (or -1); -1 padding.  The reference
+ * fixes num_modalities = 3 (src/cmng_build.cu:234).  d_neighbors: device
+ * N x degree int32.  build_ms (may be NULL) receives the device time. */
+int mars_cmng_build(const mars_store* s, int32_t degree, int32_t degree_cross,
+                    int32_t num_modalities, int32_t* d_neighbors, float* build_ms);
+
+/* The exact k nearest other rows of every row (the kNN lists of the build):
+ * d_ids / d_vals: N x k (dot desc, id asc), d_counts: N (may be NULL). */
+int mars_cmng_knn(const mars_store* s, int32_t k, int32_t* d_ids, float* d_vals,
+                  int32_t* d_counts);
+
+/* cmng_search (include/cmng.cuh:112-118, src/cmng_search.cu:110-308) for nq
+ * queries at once (the reference answers one per launch).  d_queries: nq
+ * rows of query_pitch floats; outputs [nq][K] ids, decayed scores, modalities
+ * (d_mods may be NULL), d_counts[nq]; d_iters / d_scored (may be NULL)
+ * receive the expansions and distinct rows scored per query. */
+int mars_cmng_search_batch(const mars_store* s, const int32_t* d_neighbors,
+                           int32_t degree, const float* d_queries,
+                           int32_t query_pitch, int32_t nq, float query_timestamp,
+                           const mars_cmng_config* cfg, int32_t* d_ids,
+                           float* d_scores, int32_t* d_mods, int32_t* d_counts,
+                           int32_t* d_iters, int32_t* d_scored, void* stream);
 
 /* Fused scan top-K that allocates nothing.  No counterpart in the reference:
  * it exists for callers that may not call cudaMalloc -- processes that

@@ -1,0 +1,153 @@
+"""CMNG on the GPU: the kNN lists and the built graph against the oracle's
+exact kNN + neighbour selection (bit-exact, ties by id), the beam search
+against the oracle's step-by-step restatement of the reference kernel (same
+warp dot order: identical beams), and both against the reference's own GPU
+code when oracle/_ref is built."""
+import ctypes as C
+import os
+
+import numpy as np
+import pytest
+
+import oracle as O
+from _util import assert_ranked_equivalent
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+REF_LIB = os.path.join(ROOT, "oracle", "_ref", "libmars_ref_gpu.so")
+
+
+@pytest.fixture(scope="module")
+def torch_mod():
+    import torch
+    assert torch.cuda.is_available()
+    return torch
+
+
+@pytest.fixture(scope="module")
+def clustered():
+    from mars_b200 import datagen
+    N, D = 6000, 768
+    E, mod, ts, lab = datagen.cluster_corpus(N, D, 60, 0.3, seed=11, n_mod=4, ts_max=10.0)
+    return E, mod, ts
+
+
+def _store(mb, E, mod, ts):
+    st = mb.Store(E.shape[0], E.shape[1])
+    st.upload(E, mod, ts)
+    return st
+
+
+@pytest.mark.parametrize("k", [32, 64, 128])
+def test_knn_lists_bit_exact(torch_mod, clustered, k):
+    import mars_b200 as mb
+    torch = torch_mod
+    E, mod, ts = clustered
+    N = E.shape[0]
+    st = _store(mb, E, mod, ts)
+    ids = torch.empty((N, k), dtype=torch.int32, device="cuda")
+    vals = torch.empty((N, k), dtype=torch.float32, device="cuda")
+    mb.cmng_knn(st, k, ids, vals)
+    torch.cuda.synchronize()
+    rows = np.arange(0, N, 37, dtype=np.int32)
+    rid, rv = O.knn(O.Corpus(E=E, ts=ts, mod=mod), rows, k)
+    got_i = ids.cpu().numpy()[rows]
+    got_v = vals.cpu().numpy()[rows]
+    assert np.array_equal(got_i, rid)
+    assert np.array_equal(got_v.view(np.uint32), rv.view(np.uint32))
+
+
+@pytest.mark.parametrize("degree,degree_cross,nmod", [(32, 0, 4), (36, 4, 4), (64, 4, 3)])
+def test_cmng_build_matches_oracle(torch_mod, clustered, degree, degree_cross, nmod):
+    import mars_b200 as mb
+    torch = torch_mod
+    E, mod, ts = clustered
+    N = E.shape[0]
+    st = _store(mb, E, mod, ts)
+    nb = torch.empty((N, degree), dtype=torch.int32, device="cuda")
+    ms = mb.cmng_build(st, degree, degree_cross, nmod, nb)
+    torch.cuda.synchronize()
+    assert ms > 0
+    rows = np.arange(0, N, 53, dtype=np.int32)
+    k_init = 2 * degree
+    rid, _ = O.knn(O.Corpus(E=E, ts=ts, mod=mod), rows, k_init)
+    ref = O.cmng_select(rid, mod, rows, degree, degree_cross, nmod)
+    assert np.array_equal(nb.cpu().numpy()[rows], ref)
+
+
+def _graph(mb, torch, E, mod, ts, degree=32):
+    st = _store(mb, E, mod, ts)
+    nb = torch.empty((E.shape[0], degree), dtype=torch.int32, device="cuda")
+    mb.cmng_build(st, degree, 0, 4, nb)
+    torch.cuda.synchronize()
+    return st, nb
+
+
+@pytest.mark.parametrize("beam,iters,K", [(64, 64, 10), (128, 32, 20), (16, 100, 16), (8, 5, 10)])
+def test_cmng_search_matches_oracle(torch_mod, clustered, beam, iters, K):
+    import mars_b200 as mb
+    from mars_b200 import datagen
+    torch = torch_mod
+    E, mod, ts = clustered
+    st, nb = _graph(mb, torch, E, mod, ts)
+    nbh = nb.cpu().numpy()
+    nq = 24
+    Q = datagen.queries(nq, E.shape[1], seed=beam + iters)
+    Q[: nq // 2] = E[np.arange(nq // 2) * 97] + 0.05 * Q[: nq // 2]   # some queries near clusters
+    Qd = torch.from_numpy(np.ascontiguousarray(Q)).cuda()
+    ids = torch.empty((nq, K), dtype=torch.int32, device="cuda")
+    sc = torch.empty((nq, K), dtype=torch.float32, device="cuda")
+    cnt = torch.empty(nq, dtype=torch.int32, device="cuda")
+    its = torch.empty(nq, dtype=torch.int32, device="cuda")
+    scored = torch.empty(nq, dtype=torch.int32, device="cuda")
+    cfg = mb.CmngConfig(K=K, beam_width=beam, max_iterations=iters, time_decay_lambda=0.05)
+    mb.cmng_search_batch(st, nb, 32, Qd, nq, 10.0, cfg, ids, sc, cnt, d_iters=its, d_scored=scored)
+    torch.cuda.synchronize()
+    c = O.Corpus(E=E, ts=ts, mod=mod)
+    for q in range(nq):
+        res, stats = O.cmng_search(c, nbh, Q[q], 10.0, K=K, beam_width=beam, max_iterations=iters,
+                                   lam=0.05, dot_order=O.DOT_REF_WARP)
+        n = int(cnt[q].item())
+        assert n == len(res)
+        assert int(its[q].item()) == stats["iterations"]
+        assert int(scored[q].item()) == stats["rows_scored"]
+        assert_ranked_equivalent(ids[q, :n].cpu().numpy(), sc[q, :n].cpu().numpy(),
+                                 res["node_id"], res["score"], rtol=2e-6, what=f"q{q}")
+
+
+def test_cmng_search_matches_reference_kernel(torch_mod, clustered):
+    if not os.path.exists(REF_LIB):
+        pytest.skip("oracle/_ref not built")
+    import mars_b200 as mb
+    from mars_b200 import datagen
+    torch = torch_mod
+    E, mod, ts = clustered
+    st, nb = _graph(mb, torch, E, mod, ts)
+    nbh = np.ascontiguousarray(nb.cpu().numpy())
+    nq, K, beam, iters = 16, 10, 64, 64
+    Q = datagen.queries(nq, E.shape[1], seed=4)
+    L = C.CDLL(REF_LIB)
+    P = C.c_void_p
+    L.ref_cmng_search.argtypes = [P, P, P, C.c_int32, C.c_int32, P, C.c_int32, P, C.c_int32,
+                                  C.c_float, C.c_int32, C.c_int32, C.c_int32, C.c_int32, C.c_float,
+                                  P, P, P, P]
+    rid = np.full((nq, K), -1, np.int32)
+    rsc = np.zeros((nq, K), np.float32)
+    rcnt = np.zeros(nq, np.int32)
+    L.ref_cmng_search(E.ctypes.data, mod.ctypes.data, ts.ctypes.data, E.shape[0], E.shape[1],
+                      nbh.ctypes.data, 32, Q.ctypes.data, nq, 10.0, K, beam, iters, 1, 0.05,
+                      rid.ctypes.data, rsc.ctypes.data, rcnt.ctypes.data, None)
+    Qd = torch.from_numpy(Q).cuda()
+    ids = torch.empty((nq, K), dtype=torch.int32, device="cuda")
+    sc = torch.empty((nq, K), dtype=torch.float32, device="cuda")
+    cnt = torch.empty(nq, dtype=torch.int32, device="cuda")
+    mb.cmng_search_batch(st, nb, 32, Qd, nq, 10.0,
+                         mb.CmngConfig(K=K, beam_width=beam, max_iterations=iters, time_decay_lambda=0.05),
+                         ids, sc, cnt)
+    torch.cuda.synchronize()
+    for q in range(nq):
+        n = int(cnt[q].item())
+        assert n == rcnt[q]
+        assert np.array_equal(ids[q, :n].cpu().numpy(), rid[q, :n])
+        assert np.array_equal(sc[q, :n].cpu().numpy().view(np.uint32), rsc[q, :n].view(np.uint32))
