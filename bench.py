@@ -56,7 +56,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
     ap.add_argument("--batch", type=int, default=1024)
-    ap.add_argument("--workload", choices=["scan", "c0", "c1", "c2"], default="scan",
+    ap.add_argument("--queries", type=int, default=10000)
+    ap.add_argument("--workload", choices=["scan", "c0", "c1", "c2", "c3", "c4"], default="scan",
                     help="scan: the headline (default); c0: single-query latency at N=2400 "
                          "with BFS depth 1; c1: streaming loop (append 10 rows + query per frame)")
     ap.add_argument("--frames", type=int, default=10000)
@@ -592,9 +593,147 @@ def run_batch(a):
         dist.destroy_process_group()
 
 
+def run_knn_build(a):
+    """c3: cmng_build of an exact out-degree-32 kNN graph.  N = 100,000 rows
+    (100 isotropic Gaussian clusters, centres N(0,1), sigma 0.3, normalised),
+    degree 32, no bridges.  A step is one full build (tensor-core kNN with
+    exact rescoring + neighbour selection), timed with CUDA events."""
+    import torch
+    import mars_b200 as mb
+    import oracle as O
+    from mars_b200 import datagen
+
+    N = a.n if a.n != 1_000_000 else 100_000
+    D, deg = a.dim, 32
+    E, mod, ts, _ = datagen.cluster_corpus(N, D, 100, 0.3, seed=a.seed, n_mod=4, ts_max=10.0)
+    if a.impl == "reference":
+        c = O.Corpus(E=E, ts=ts, mod=mod)
+        rows = np.arange(0, N, max(1, N // 200), dtype=np.int32)
+        t0 = time.perf_counter()
+        O.knn(c, rows, 2 * deg, dot_order=O.DOT_FAST)
+        dt = time.perf_counter() - t0
+        full = dt * N / rows.shape[0]
+        print(json.dumps({"impl": "reference", "workload": "c3", "metric": "cmng_build ms", "value": full * 1e3,
+                          "unit": "ms", "higher_is_better": False,
+                          "cpu_baseline": {"value": full * 1e3, "unit": "ms", "cores": os.cpu_count(),
+                                           "kind": "port", "sample": f"exact kNN of {rows.shape[0]} rows "
+                                           f"against all {N}, extrapolated x{N / rows.shape[0]:.0f}"}}))
+        return
+    st = mb.Store(N, D)
+    st.upload(E, mod, ts)
+    nb = torch.empty((N, deg), dtype=torch.int32, device="cuda")
+    for _ in range(max(1, a.warmup)):
+        mb.cmng_build(st, deg, 0, 4, nb)
+    times = [mb.cmng_build(st, deg, 0, 4, nb) for _ in range(a.steps)]
+    torch.cuda.synchronize()
+    # spot check against the exact oracle kNN
+    rows = np.arange(0, N, N // 64, dtype=np.int32)
+    rid, _ = O.knn(O.Corpus(E=E, ts=ts, mod=mod), rows, 2 * deg)
+    ref = O.cmng_select(rid, mod, rows, deg, 0, 4)
+    exact = bool(np.array_equal(nb.cpu().numpy()[rows], ref))
+    ms = statistics.median(times)
+    flops = 2.0 * N * N * D
+    peaks = {}
+    try:
+        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+    except Exception:
+        pass
+    bf16 = float(peaks.get("bf16_tflops", 1590.0))
+    print(json.dumps({"workload": "c3", "metric": f"cmng_build ms (N={N}, D={D}, degree {deg})",
+                      "value": ms, "unit": "ms", "higher_is_better": False, "steps": a.steps,
+                      "tflops_effective": flops / (ms * 1e-3) / 1e12,
+                      "roofline": {"bound": "tensor", "flops_per_build": flops,
+                                   "frac_of_tf32_nominal": flops / (ms * 1e-3) / 1e12 / (bf16 / 2)},
+                      "spot_check_rows": int(rows.shape[0]), "neighbours_bit_exact": exact}),
+          flush=True)
+
+
+def run_cmng_bfs(a):
+    """c4: cmng_search + cross-modal BFS.  N = 1,000,000 rows from a 1,000
+    cluster mixture (sigma 0.3, 4 modalities, normalised); graph = degree-32
+    kNN + 4 cross-modal bridges (degree 36, built once, untimed); 10,000
+    queries, beam 64, K = 10, lambda = 0.05, BFS depth 2."""
+    import torch
+    import mars_b200 as mb
+    import oracle as O
+    from mars_b200 import datagen
+
+    N, D, deg, K, nq = a.n, a.dim, 36, 10, a.queries
+    E, mod, ts, _ = datagen.cluster_corpus(N, D, 1000, 0.3, seed=a.seed, n_mod=4, ts_max=10.0)
+    Q = datagen.queries(nq, D, seed=a.seed + 5)
+    st = mb.Store(N, D)
+    st.upload(E, mod, ts)
+    nb = torch.empty((N, deg), dtype=torch.int32, device="cuda")
+    build_ms = mb.cmng_build(st, deg, 4, 4, nb)
+    if a.impl == "reference":
+        nbh = nb.cpu().numpy()
+        c = O.Corpus(E=E, ts=ts, mod=mod, fixed_nbrs=nbh)
+        sample = min(nq, 50)
+        t0 = time.perf_counter()
+        for q in range(sample):
+            res, _ = O.cmng_search(c, nbh, Q[q], 10.0, K=K, beam_width=64, max_iterations=64, lam=0.05,
+                                   dot_order=O.DOT_FAST)
+            O.bfs(c, res["node_id"], res["score"], None, 2, 0.5, q=Q[q], t_q=10.0, lam=0.05,
+                  dot_order=O.DOT_FAST)
+        dt = time.perf_counter() - t0
+        v = sample / dt
+        print(json.dumps({"impl": "reference", "workload": "c4", "metric": "queries/s", "value": v,
+                          "unit": "queries/s",
+                          "cpu_baseline": {"value": v, "unit": "queries/s", "cores": 1, "kind": "port",
+                                           "sample": f"{sample} queries, oracle beam search + BFS, 1 thread"}}))
+        return
+    Qd = torch.from_numpy(Q).cuda()
+    cfg = mb.CmngConfig(K=K, beam_width=64, max_iterations=64, time_decay_lambda=0.05)
+    ctx = mb.CmngContext(nq, K, deg, 2, N)
+    ids = torch.empty((nq, K), dtype=torch.int32, device="cuda")
+    sc = torch.empty((nq, K), dtype=torch.float32, device="cuda")
+    cnt = torch.empty(nq, dtype=torch.int32, device="cuda")
+    vis = torch.empty(nq, dtype=torch.int32, device="cuda")
+    bits = torch.empty(nq, dtype=torch.int32, device="cuda")
+    bscored = torch.empty(nq, dtype=torch.int32, device="cuda")
+    stream = torch.cuda.Stream()       # a real stream: NULL would mean the store's own stream
+    torch.cuda.set_stream(stream)
+    for _ in range(max(1, a.warmup)):
+        ctx.search_bfs(st, nb, deg, Qd, nq, 10.0, cfg, 2, 0.5, ids, sc, cnt, d_visited=vis,
+                       stream=stream.cuda_stream)
+    e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
+    torch.cuda.synchronize()
+    e0.record(stream)
+    for _ in range(a.steps):
+        ctx.search_bfs(st, nb, deg, Qd, nq, 10.0, cfg, 2, 0.5, ids, sc, cnt, d_visited=vis,
+                       stream=stream.cuda_stream)
+    e1.record(stream)
+    for _ in range(a.steps):
+        mb.cmng_search_batch(st, nb, deg, Qd, nq, 10.0, cfg, ids, sc, cnt, d_iters=bits,
+                             d_scored=bscored, stream=stream.cuda_stream)
+    e2.record(stream)
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / a.steps
+    ms_beam = e1.elapsed_time(e2) / a.steps
+    rows_bfs = float(vis.double().mean().item())
+    rows_beam = float(bscored.double().mean().item())
+    # rows read per query: beam-scored rows + the BFS levels >= 1 (seeds are beam rows)
+    bytes_q = (rows_beam + rows_bfs) * D * 4
+    peak, _ = measured_peak()
+    achieved = bytes_q * nq / (ms * 1e-3) / 1e9
+    print(json.dumps({"workload": "c4", "metric": f"queries/s (cmng_search + BFS depth 2, N={N}, K={K})",
+                      "value": nq / (ms * 1e-3), "unit": "queries/s", "ms_per_batch": ms,
+                      "beam_only_queries_per_s": nq / (ms_beam * 1e-3), "graph_build_ms": build_ms,
+                      "mean_rows_scored_beam": rows_beam, "mean_nodes_visited_bfs": rows_bfs,
+                      "mean_iterations": float(bits.double().mean().item()),
+                      "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                                   "frac": achieved / peak,
+                                   "note": "row gathers: (beam-scored + BFS-visited rows) x D x 4 bytes"}}),
+          flush=True)
+
+
 def main():
     a = parse_args()
-    if a.workload == "c2":
+    if a.workload == "c3":
+        run_knn_build(a)
+    elif a.workload == "c4":
+        run_cmng_bfs(a)
+    elif a.workload == "c2":
         run_batch(a)
     elif a.workload in ("c0", "c1"):
         run_latency(a)

@@ -308,6 +308,207 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// BFS from each query's beam-search results over the CMNG adjacency
+// (the canonical BFS of the scan pipeline: level-synchronous, a node's score is
+// the best fmaxf(parent * decay, own * 0.8f) over its parents one level up,
+// seeds keep their beam score, no frontier cap), then the top-K of all visited
+// nodes by (score desc, id asc).  One block per query; the visited set is a
+// per-block open-addressing table in global memory whose entries carry the
+// block's query epoch, so nothing is cleared between queries:
+//   tag[slot]   = (epoch << 32) | node
+//   state[slot] = ((epoch << 4 | (15 - level)) << 32) | key(best parent score)
+// One atomicMax on state both claims the node for a level and keeps its best
+// parent; the thread that sees an older state appends the node to the level.
+struct BfsArgs2 {
+    const int32_t* nbrs;
+    int32_t degree;
+    const float* E;
+    const float* ts;
+    const float* imp;
+    const int32_t* mod;
+    int64_t pitch4;
+    int32_t nc, N;
+    const float* Q;
+    int64_t qpitch;
+    int32_t nq;
+    float t_q, lambda, hop_decay;
+    int32_t use_imp, hops, K;
+    const int32_t* seed_ids;      // nq x seed_stride
+    const float* seed_scores;
+    const int32_t* seed_cnt;
+    int32_t seed_stride;
+    unsigned long long* tags;     // gridDim x table
+    unsigned long long* states;
+    int32_t* lists;               // gridDim x vcap
+    uint32_t* epochs;             // gridDim
+    int32_t table, vcap;
+    int32_t* out_ids;             // nq x K
+    float* out_scores;
+    int32_t* out_mods;
+    int32_t* out_hops;
+    int32_t* out_cnt;
+    int32_t* out_visited;         // nq (may be null)
+    int* err;
+};
+
+__device__ __forceinline__ int table_find_or_claim(unsigned long long* tags, uint32_t mask, uint32_t epoch,
+                                                   int32_t v) {
+    const unsigned long long want = ((unsigned long long)epoch << 32) | (uint32_t)v;
+    uint32_t s = hash32(v) & mask;
+    for (uint32_t probe = 0; probe <= mask; ++probe) {
+        unsigned long long cur = __ldcg(tags + s);
+        while ((uint32_t)(cur >> 32) != epoch) {          // stale slot: try to take it
+            const unsigned long long prev = atomicCAS(tags + s, cur, want);
+            if (prev == cur) return (int)s;
+            cur = prev;
+        }
+        if (cur == want) return (int)s;
+        s = (s + 1) & mask;
+    }
+    return -1;   // unreachable: the table is sized to at most half full
+}
+
+__device__ __forceinline__ float bfs_own_score(const BfsArgs2& a, const float4* q4, int32_t u, int lane) {
+    const float4* row = reinterpret_cast<const float4*>(a.E) + (int64_t)u * a.pitch4;
+    const float dot = warp_dot_canonical(row, q4, a.nc, lane);
+    float f = fused_weight_apply(dot, __ldg(a.ts + u), a.t_q, a.lambda);
+    if (a.use_imp && a.imp != nullptr) f = f * __ldg(a.imp + u);
+    return f;
+}
+
+template <int KPL>
+__global__ void __launch_bounds__(kThreads) bfs_kernel(const BfsArgs2 a) {
+    __shared__ int s_lvl[16];       // level offsets; [15] = tail
+    __shared__ float   s_val[kWarps][kMaxTopK];
+    __shared__ int32_t s_idx[kWarps][kMaxTopK];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const uint32_t mask = (uint32_t)a.table - 1u;
+    unsigned long long* tags = a.tags + (int64_t)blockIdx.x * a.table;
+    unsigned long long* states = a.states + (int64_t)blockIdx.x * a.table;
+    int32_t* list = a.lists + (int64_t)blockIdx.x * a.vcap;
+    float* lscore = reinterpret_cast<float*>(list + a.vcap / 2);   // second half: scores
+    const int vcap = a.vcap / 2;
+
+    for (int qi = blockIdx.x; qi < a.nq; qi += gridDim.x) {
+        uint32_t epoch = 0;
+        if (tid == 0) {
+            epoch = a.epochs[blockIdx.x] + 1;
+            if (epoch >= (1u << 27)) epoch = 1;   // wraps after 2^27 queries per block (tables reset below)
+            a.epochs[blockIdx.x] = epoch;
+            s_lvl[0] = 0;
+        }
+        __syncthreads();
+        epoch = a.epochs[blockIdx.x];
+        if (epoch == 1) {   // first use or wrap: clear this block's table
+            for (int i = tid; i < a.table; i += kThreads) { tags[i] = 0ull; states[i] = 0ull; }
+            __syncthreads();
+        }
+        const float4* q4 = reinterpret_cast<const float4*>(a.Q + (int64_t)qi * a.qpitch);
+        // ---- level 0: the seeds with their beam scores ----
+        const int ns = min(a.seed_cnt[qi], a.seed_stride);
+        const unsigned long long st0 = (unsigned long long)((epoch << 4) | 15u) << 32;
+        if (tid == 0) {
+            int n0 = 0;
+            for (int i = 0; i < ns; ++i) {
+                const int32_t u = a.seed_ids[(int64_t)qi * a.seed_stride + i];
+                if (u < 0 || u >= a.N) continue;
+                const int slot = table_find_or_claim(tags, mask, epoch, u);
+                const unsigned long long old = atomicMax(states + slot,
+                    st0 | f2key(a.seed_scores[(int64_t)qi * a.seed_stride + i]));
+                if ((uint32_t)(old >> 32) < (epoch << 4)) {
+                    list[n0] = u;
+                    lscore[n0] = a.seed_scores[(int64_t)qi * a.seed_stride + i];
+                    ++n0;
+                }
+            }
+            s_lvl[1] = n0;
+            s_lvl[15] = n0;
+        }
+        __syncthreads();
+        bool overflow = false;
+        for (int h = 0; h <= a.hops; ++h) {
+            const int beg = s_lvl[h], end = s_lvl[h + 1];
+            const unsigned long long nst = (unsigned long long)((epoch << 4) | (uint32_t)(15 - (h + 1))) << 32;
+            for (int idx = beg + warp; idx < end; idx += kWarps) {
+                const int32_t u = list[idx];
+                float su;
+                if (h == 0) {
+                    su = lscore[idx];
+                } else {
+                    const float own = bfs_own_score(a, q4, u, lane);
+                    const int slot = table_find_or_claim(tags, mask, epoch, u);
+                    const float best = key2f((uint32_t)(__ldcg(states + slot) & 0xffffffffull));
+                    su = fmaxf(best, own * 0.8f);
+                    if (lane == 0) lscore[idx] = su;
+                }
+                if (h == a.hops) continue;           // last level: scored, not expanded
+                const unsigned long long word = nst | f2key(su * a.hop_decay);
+                const int32_t* nb = a.nbrs + (int64_t)u * a.degree;
+                for (int e = lane; e < a.degree; e += 32) {
+                    const int32_t v = __ldg(nb + e);
+                    if (v < 0 || v >= a.N) continue;
+                    const int slot = table_find_or_claim(tags, mask, epoch, v);
+                    const unsigned long long old = atomicMax(states + slot, word);
+                    if ((uint32_t)(old >> 32) < (epoch << 4)) {
+                        const int pos = atomicAdd(&s_lvl[15], 1);
+                        if (pos < vcap) list[pos] = v; else overflow = true;
+                    }
+                }
+            }
+            __syncthreads();
+            if (tid == 0 && h + 2 < 15) s_lvl[h + 2] = min(s_lvl[15], vcap);
+            __syncthreads();
+        }
+        if (overflow) atomicCAS(a.err, 0, 7);
+        // ---- top-K of every visited node ----
+        const int total = min(s_lvl[15], vcap);
+        WarpTopK<KPL> top;
+        top.init(a.K);
+        for (int base = warp * 32; base < total; base += kThreads) {
+            const int j = base + lane;
+            float sv = -INFINITY;
+            int32_t id = INT32_MAX;
+            if (j < total) { sv = lscore[j]; id = list[j]; }
+            top.offer_lanes(sv, id, j < total, lane);
+        }
+        top.store(s_val[warp], s_idx[warp], lane);
+        __syncthreads();
+        if (warp == 0) {
+            for (int w = 1; w < kWarps; ++w) top.offer_sorted(s_val[w], s_idx[w], a.K, lane);
+            int cnt = 0;
+#pragma unroll
+            for (int sl = 0; sl < KPL; ++sl) {
+                const int p = sl * 32 + lane;
+                const bool valid = p < a.K && top.i[sl] != INT32_MAX;
+                cnt += __popc(__ballot_sync(0xffffffffu, valid));
+                if (p < a.K) {
+                    const int64_t o = (int64_t)qi * a.K + p;
+                    if (valid) {
+                        const int32_t u = top.i[sl];
+                        const int slot = table_find_or_claim(tags, mask, epoch, u);
+                        const uint32_t stamp = (uint32_t)(__ldcg(states + slot) >> 32);
+                        a.out_ids[o] = u;
+                        a.out_scores[o] = top.v[sl];
+                        if (a.out_mods) a.out_mods[o] = __ldg(a.mod + u);
+                        if (a.out_hops) a.out_hops[o] = 15 - (int)(stamp & 15u);
+                    } else {
+                        a.out_ids[o] = -1;
+                        a.out_scores[o] = -INFINITY;
+                        if (a.out_mods) a.out_mods[o] = -1;
+                        if (a.out_hops) a.out_hops[o] = -1;
+                    }
+                }
+            }
+            if (lane == 0) {
+                a.out_cnt[qi] = cnt;
+                if (a.out_visited) a.out_visited[qi] = total;
+            }
+        }
+        __syncthreads();
+    }
+}
+
 }  // namespace cmng
 }  // namespace mars
 
@@ -455,6 +656,143 @@ int mars_cmng_search_batch(const mars_store* s, const int32_t* d_neighbors, int3
     MARS_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int grid = std::max(1, std::min(nq, std::max(nb, 1) * sms));
     search_kernel<<<grid, kThreads, smem, st>>>(a);
+    MARS_CUDA_TRY(cudaGetLastError());
+    return MARS_OK;
+}
+
+}  // extern "C"
+
+// ---------------------------------------------------------------------------
+struct mars_cmng_ctx {
+    int32_t device = 0;
+    int32_t max_queries = 0, K = 0, degree = 0, hops = 0;
+    int32_t grid = 0, table = 0, vcap = 0;
+    int32_t* d_seed_ids = nullptr;
+    float* d_seed_scores = nullptr;
+    int32_t* d_seed_cnt = nullptr;
+    unsigned long long* d_tags = nullptr;
+    unsigned long long* d_states = nullptr;
+    int32_t* d_lists = nullptr;
+    uint32_t* d_epochs = nullptr;
+    int* d_err = nullptr;
+};
+
+extern "C" {
+
+int mars_cmng_ctx_create(int32_t device, int32_t max_queries, int32_t K, int32_t degree, int32_t bfs_hops,
+                         int32_t max_nodes, mars_cmng_ctx** out) {
+    if (out == nullptr) return fail(MARS_ERR_INVALID, "mars_cmng_ctx_create: out is NULL");
+    *out = nullptr;
+    if (max_queries <= 0 || K <= 0 || K > MARS_MAX_TOP_K || degree <= 0 || degree > kMaxDegree ||
+        bfs_hops < 0 || bfs_hops > 13 || max_nodes <= 0)
+        return fail(MARS_ERR_INVALID, "mars_cmng_ctx_create: bad sizes");
+    MarsDeviceGuard g(device);
+    // visited nodes per query: K * (1 + d + d^2 + ...) capped at max_nodes
+    int64_t v = K, lvl = K;
+    for (int h = 0; h < bfs_hops; ++h) { lvl = std::min<int64_t>(lvl * degree, max_nodes); v += lvl; }
+    v = std::min<int64_t>(v, (int64_t)max_nodes);
+    if (v > (1 << 24)) return fail(MARS_ERR_UNSUPPORTED, "mars_cmng_ctx_create: BFS too large");
+    int64_t t = 256;
+    while (t < 2 * v) t <<= 1;
+    auto* c = new mars_cmng_ctx();
+    c->device = device;
+    c->max_queries = max_queries;
+    c->K = K;
+    c->degree = degree;
+    c->hops = bfs_hops;
+    c->table = (int32_t)t;
+    c->vcap = (int32_t)(2 * v);          // ids + scores
+    int sms = 0, nb = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, bfs_kernel<1>, kThreads, 0);
+    c->grid = std::max(1, std::min(max_queries, sms * std::max(1, std::min(nb, 4))));
+    int rc = MARS_OK;
+    auto T = [&](cudaError_t e, const char* w) { if (rc == MARS_OK && e != cudaSuccess) rc = cuda_fail(e, w, __FILE__, __LINE__); };
+    T(cudaMalloc(&c->d_seed_ids, (size_t)max_queries * K * 4), "seeds");
+    T(cudaMalloc(&c->d_seed_scores, (size_t)max_queries * K * 4), "seeds");
+    T(cudaMalloc(&c->d_seed_cnt, (size_t)max_queries * 4), "seeds");
+    T(cudaMalloc(&c->d_tags, (size_t)c->grid * t * 8), "visited tables");
+    T(cudaMalloc(&c->d_states, (size_t)c->grid * t * 8), "visited tables");
+    T(cudaMalloc(&c->d_lists, (size_t)c->grid * c->vcap * 4), "level lists");
+    T(cudaMalloc(&c->d_epochs, (size_t)c->grid * 4), "epochs");
+    T(cudaMalloc(&c->d_err, sizeof(int)), "error word");
+    if (rc == MARS_OK) T(cudaMemset(c->d_epochs, 0, (size_t)c->grid * 4), "memset");
+    if (rc == MARS_OK) T(cudaMemset(c->d_err, 0, sizeof(int)), "memset");
+    if (rc != MARS_OK) { mars_cmng_ctx_destroy(c); return rc; }
+    *out = c;
+    return MARS_OK;
+}
+
+int mars_cmng_ctx_destroy(mars_cmng_ctx* c) {
+    if (c == nullptr) return MARS_OK;
+    MarsDeviceGuard g(c->device);
+    cudaFree(c->d_seed_ids); cudaFree(c->d_seed_scores); cudaFree(c->d_seed_cnt);
+    cudaFree(c->d_tags); cudaFree(c->d_states); cudaFree(c->d_lists); cudaFree(c->d_epochs);
+    cudaFree(c->d_err);
+    delete c;
+    return MARS_OK;
+}
+
+int mars_cmng_search_bfs_batch(const mars_store* s, mars_cmng_ctx* c, const int32_t* d_neighbors, int32_t degree,
+                               const float* d_queries, int32_t query_pitch, int32_t nq, float t_q,
+                               const mars_cmng_config* cfg, int32_t bfs_hops, float bfs_score_decay,
+                               int32_t use_importance, int32_t* d_ids, float* d_scores, int32_t* d_mods,
+                               int32_t* d_hops, int32_t* d_counts, int32_t* d_visited, void* stream) {
+    if (s == nullptr || c == nullptr || cfg == nullptr || d_ids == nullptr || d_scores == nullptr ||
+        d_counts == nullptr)
+        return fail(MARS_ERR_INVALID, "mars_cmng_search_bfs_batch: NULL argument");
+    if (nq > c->max_queries || cfg->K != c->K || degree != c->degree || bfs_hops != c->hops)
+        return fail(MARS_ERR_INVALID, "mars_cmng_search_bfs_batch: arguments do not match the context");
+    if ((s->dim & 3) != 0 || (query_pitch & 3) != 0 || (reinterpret_cast<uintptr_t>(d_queries) & 15u) != 0)
+        return fail(MARS_ERR_INVALID, "mars_cmng_search_bfs_batch: dim and query rows must be float4 aligned");
+    if (nq == 0) return MARS_OK;
+    MarsDeviceGuard g(s->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : s->stream;
+    // 1. beam search into the context's seed buffers
+    MARS_TRY(mars_cmng_search_batch(s, d_neighbors, degree, d_queries, query_pitch, nq, t_q, cfg, c->d_seed_ids,
+                                    c->d_seed_scores, nullptr, c->d_seed_cnt, nullptr, nullptr, st));
+    // 2. BFS + final top-K
+    BfsArgs2 a{};
+    a.nbrs = d_neighbors;
+    a.degree = degree;
+    a.E = s->d_E;
+    a.ts = s->d_ts;
+    a.imp = s->d_imp;
+    a.mod = s->d_mod;
+    a.pitch4 = s->pitch / 4;
+    a.nc = (s->dim + 3) / 4;
+    a.N = s->n;
+    a.Q = d_queries;
+    a.qpitch = query_pitch;
+    a.nq = nq;
+    a.t_q = t_q;
+    a.lambda = cfg->time_decay_lambda;
+    a.hop_decay = bfs_score_decay;
+    a.use_imp = use_importance;
+    a.hops = bfs_hops;
+    a.K = cfg->K;
+    a.seed_ids = c->d_seed_ids;
+    a.seed_scores = c->d_seed_scores;
+    a.seed_cnt = c->d_seed_cnt;
+    a.seed_stride = cfg->K;
+    a.tags = c->d_tags;
+    a.states = c->d_states;
+    a.lists = c->d_lists;
+    a.epochs = c->d_epochs;
+    a.table = c->table;
+    a.vcap = c->vcap;
+    a.out_ids = d_ids;
+    a.out_scores = d_scores;
+    a.out_mods = d_mods;
+    a.out_hops = d_hops;
+    a.out_cnt = d_counts;
+    a.out_visited = d_visited;
+    a.err = c->d_err;
+    const int grid = std::min(c->grid, nq);
+    if (cfg->K <= 32) bfs_kernel<1><<<grid, kThreads, 0, st>>>(a);
+    else if (cfg->K <= 64) bfs_kernel<2><<<grid, kThreads, 0, st>>>(a);
+    else if (cfg->K <= 128) bfs_kernel<4><<<grid, kThreads, 0, st>>>(a);
+    else bfs_kernel<8><<<grid, kThreads, 0, st>>>(a);
     MARS_CUDA_TRY(cudaGetLastError());
     return MARS_OK;
 }

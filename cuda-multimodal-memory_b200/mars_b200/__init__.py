@@ -131,6 +131,10 @@ _SIGS = {
     "mars_cmng_knn": [_VP, _I32, _VP, _VP, _VP],
     "mars_cmng_search_batch": [_VP, _VP, _I32, _VP, _I32, _I32, _F32, C.POINTER(CmngConfig), _VP,
                                _VP, _VP, _VP, _VP, _VP, _VP],
+    "mars_cmng_ctx_create": [_I32, _I32, _I32, _I32, _I32, _I32, C.POINTER(_VP)],
+    "mars_cmng_ctx_destroy": [_VP],
+    "mars_cmng_search_bfs_batch": [_VP, _VP, _VP, _I32, _VP, _I32, _I32, _F32, C.POINTER(CmngConfig),
+                                   _I32, _F32, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _VP],
     "mars_scan_topk_noalloc": [_VP, _I32, _VP, _VP, _VP, _I32, _I32, _VP, _F32, _F32, _I32, _I32,
                                _I32, _I32, _VP, _VP, _VP, _VP],
 }
@@ -405,6 +409,38 @@ def cmng_search_batch(store: Store, d_neighbors, degree, d_queries, nq, t_q, cfg
                                         pitch, nq, float(t_q), C.byref(cfg), _ptr(d_ids),
                                         _ptr(d_scores), _ptr(d_mods), _ptr(d_counts),
                                         _ptr(d_iters), _ptr(d_scored), stream))
+
+
+class CmngContext:
+    """Scratch for cmng_search + BFS batches (mars_cmng_search_bfs_batch)."""
+
+    def __init__(self, max_queries, K, degree, bfs_hops, max_nodes, device=0):
+        h = C.c_void_p()
+        _check(lib().mars_cmng_ctx_create(device, max_queries, K, degree, bfs_hops, max_nodes,
+                                          C.byref(h)))
+        self.handle = h
+
+    def search_bfs(self, store: Store, d_neighbors, degree, d_queries, nq, t_q, cfg: CmngConfig,
+                   bfs_hops, bfs_score_decay, d_ids, d_scores, d_counts, d_mods=None, d_hops=None,
+                   d_visited=None, use_importance=False, query_pitch=None, stream=None):
+        pitch = query_pitch if query_pitch is not None else (store.dim + 3) // 4 * 4
+        _check(lib().mars_cmng_search_bfs_batch(store.handle, self.handle, _ptr(d_neighbors), degree,
+                                                _ptr(d_queries), pitch, nq, float(t_q), C.byref(cfg),
+                                                bfs_hops, float(bfs_score_decay),
+                                                int(use_importance), _ptr(d_ids), _ptr(d_scores),
+                                                _ptr(d_mods), _ptr(d_hops), _ptr(d_counts),
+                                                _ptr(d_visited), stream))
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().mars_cmng_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def scan_topk_noalloc(d_embeddings, row_pitch, d_timestamps, d_importance, d_modalities, n, dim,

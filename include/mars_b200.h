@@ -322,6 +322,29 @@ int mars_cmng_search_batch(const mars_store* s, const int32_t* d_neighbors,
                            float* d_scores, int32_t* d_mods, int32_t* d_counts,
                            int32_t* d_iters, int32_t* d_scored, void* stream);
 
+/* cmng_search followed by a cross-modal BFS (no reference counterpart: the
+ * reference's cmng_search stops at the beam, src/cmng_search.cu:110-308).
+ * The beam's top-K (decayed scores) seed a BFS of bfs_hops levels over the
+ * CMNG adjacency with the canonical rule of mars_query: a node's score is the
+ * best fmaxf(parent * bfs_score_decay, own * 0.8f) over its parents one level
+ * up, own = dot x __expf(-lambda * age) [x importance]; the result is the
+ * top-K of all visited nodes by (score desc, id asc).  The context holds the
+ * per-block visited tables (sized for K x (1 + degree + ... + degree^hops)). */
+typedef struct mars_cmng_ctx mars_cmng_ctx;
+
+int mars_cmng_ctx_create(int32_t device, int32_t max_queries, int32_t K, int32_t degree,
+                         int32_t bfs_hops, int32_t max_nodes, mars_cmng_ctx** out);
+int mars_cmng_ctx_destroy(mars_cmng_ctx* ctx);
+
+int mars_cmng_search_bfs_batch(const mars_store* s, mars_cmng_ctx* ctx,
+                               const int32_t* d_neighbors, int32_t degree,
+                               const float* d_queries, int32_t query_pitch, int32_t nq,
+                               float query_timestamp, const mars_cmng_config* cfg,
+                               int32_t bfs_hops, float bfs_score_decay,
+                               int32_t use_importance, int32_t* d_ids, float* d_scores,
+                               int32_t* d_mods, int32_t* d_hops, int32_t* d_counts,
+                               int32_t* d_visited, void* stream);
+
 /* Fused scan top-K that allocates nothing.  No counterpart in the reference:
  * it exists for callers that may not call cudaMalloc -- processes that
  * reserve all GPU memory up front (for example a real-time loop whose memory

@@ -151,3 +151,50 @@ def test_cmng_search_matches_reference_kernel(torch_mod, clustered):
         assert n == rcnt[q]
         assert np.array_equal(ids[q, :n].cpu().numpy(), rid[q, :n])
         assert np.array_equal(sc[q, :n].cpu().numpy().view(np.uint32), rsc[q, :n].view(np.uint32))
+
+
+@pytest.mark.parametrize("hops", [0, 1, 2])
+def test_cmng_search_bfs_matches_oracle(torch_mod, clustered, hops):
+    """Beam search then the canonical BFS over the CMNG adjacency: with the
+    device's beam as seeds, the oracle's BFS gives the same answer (the own
+    scores differ only by __expf vs expf, so ranks are compared tie-aware)."""
+    import mars_b200 as mb
+    from mars_b200 import datagen
+    torch = torch_mod
+    E, mod, ts = clustered
+    N, D = E.shape
+    deg = 36
+    st = _store(mb, E, mod, ts)
+    nb = torch.empty((N, deg), dtype=torch.int32, device="cuda")
+    mb.cmng_build(st, deg, 4, 4, nb)
+    nbh = nb.cpu().numpy()
+    nq, K = 20, 10
+    Q = datagen.queries(nq, D, seed=50 + hops)
+    Q[:8] = E[np.arange(8) * 311] + 0.05 * Q[:8]
+    Qd = torch.from_numpy(np.ascontiguousarray(Q)).cuda()
+    cfg = mb.CmngConfig(K=K, beam_width=64, max_iterations=64, time_decay_lambda=0.05)
+    ctx = mb.CmngContext(nq, K, deg, hops, N)
+    ids = torch.empty((nq, K), dtype=torch.int32, device="cuda")
+    sc = torch.empty((nq, K), dtype=torch.float32, device="cuda")
+    hp = torch.empty((nq, K), dtype=torch.int32, device="cuda")
+    cnt = torch.empty(nq, dtype=torch.int32, device="cuda")
+    vis = torch.empty(nq, dtype=torch.int32, device="cuda")
+    ctx.search_bfs(st, nb, deg, Qd, nq, 10.0, cfg, hops, 0.5, ids, sc, cnt, d_hops=hp, d_visited=vis)
+    # beam results alone, as the BFS seeds
+    bids = torch.empty((nq, K), dtype=torch.int32, device="cuda")
+    bsc = torch.empty((nq, K), dtype=torch.float32, device="cuda")
+    bcnt = torch.empty(nq, dtype=torch.int32, device="cuda")
+    mb.cmng_search_batch(st, nb, deg, Qd, nq, 10.0, cfg, bids, bsc, bcnt)
+    torch.cuda.synchronize()
+    oc = O.Corpus(E=E, ts=ts, mod=mod, fixed_nbrs=nbh)
+    for q in range(nq):
+        n0 = int(bcnt[q].item())
+        visited = O.bfs(oc, bids[q, :n0].cpu().numpy(), bsc[q, :n0].cpu().numpy(), None, hops, 0.5,
+                        q=Q[q], t_q=10.0, lam=0.05)
+        assert int(vis[q].item()) == visited.shape[0]
+        ref = O.finalize(visited, K)
+        n = int(cnt[q].item())
+        assert n == ref.shape[0]
+        assert_ranked_equivalent(ids[q, :n].cpu().numpy(), sc[q, :n].cpu().numpy(), ref["node_id"],
+                                 ref["score"], hp[q, :n].cpu().numpy(), ref["hops"], rtol=2e-6,
+                                 what=f"q{q}")
