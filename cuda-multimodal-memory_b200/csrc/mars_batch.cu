@@ -104,6 +104,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
     uint64_t* tfull = empty + kStages;
     uint64_t* tempty = tfull + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    float* s_w = reinterpret_cast<float*>(smem + kStages * kStageBytes + 256);   // [kBN] row weights
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -186,14 +187,20 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
         const int row_in_tile = sub * 32 + lane;    // query row of this thread
         int buf = 0;
         uint32_t bphase = 0;
+        const int et = threadIdx.x - 64;           // 0..127 among the epilogue threads
         for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
             int qt, row0;
             tile_coords(a, t, MODE, qt, row0);
             const int q = qt * kBM + row_in_tile;
             const bool qv = q < a.B;
             const int32_t self_row = a.self_base >= 0 ? a.self_base + q : -1;
+            // per-tile operands fetched while the tensor cores still work on
+            // this tile: the row weights go to shared memory in one round trip
             const float th = (MODE == kCandidates && qv) ? __ldg(a.theta + q) : 0.f;
             const float mg = qv ? __ldg(a.margin + q) : 0.f;
+            asm volatile("bar.sync 1, 128;" ::: "memory");   // previous tile's reads of s_w done
+            for (int i = et; i < kBN; i += 128) s_w[i] = (row0 + i < a.n) ? __ldg(a.wts + row0 + i) : NAN;
+            asm volatile("bar.sync 1, 128;" ::: "memory");
             if (!sm100::mbar_wait(tfull + buf, bphase, a.err, 5)) break;
             sm100::tc_fence_after();
             float best[kJ];
@@ -208,15 +215,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                 const int rbase = row0 + c * 32;
 #pragma unroll
                 for (int j4 = 0; j4 < 8; ++j4) {
-                    float4 w4 = make_float4(NAN, NAN, NAN, NAN);
-                    if (rbase + 4 * j4 + 3 < a.n) {
-                        w4 = __ldg(reinterpret_cast<const float4*>(a.wts + rbase) + j4);
-                    } else {
-                        float* wp = &w4.x;
-#pragma unroll
-                        for (int u = 0; u < 4; ++u)
-                            if (rbase + 4 * j4 + u < a.n) wp[u] = __ldg(a.wts + rbase + 4 * j4 + u);
-                    }
+                    const float4 w4 = reinterpret_cast<const float4*>(s_w + c * 32)[j4];
                     const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
@@ -527,7 +526,8 @@ int make_map(CUtensorMap* m, const float* base, int64_t rows, int64_t cols, int6
     return MARS_OK;
 }
 
-constexpr size_t kGemmSmem = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/;
+constexpr size_t kGemmSmem = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
+                             kBN * sizeof(float) /*row weights*/;
 
 }  // namespace
 

@@ -1,0 +1,108 @@
+"""Host-side logic of the row-sharded path with world_size 2 on CPU (gloo).
+
+Each rank builds its shard with mars_b200.datagen.gaussian_rows, computes the
+shard's top-K with the oracle (standing in for mars_scan_topk on the GPU),
+offsets ids by the shard start, all-gathers the [Q][K] lists into the
+rank-major [world][Q][K] layout that mars_topk_merge_batch reads, and merges.
+The merged lists must equal the single-process top-K over the whole corpus.
+"""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+N, D, K, Q = 3001, 64, 7, 5
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    return port
+
+
+def _merge_rank_major(gids, gvals, world, Qn, K):
+    """CPU statement of mars_topk_merge_batch: list l of query q at (l*Q+q)*K."""
+    out_i = np.full((Qn, K), -1, np.int32)
+    out_v = np.full((Qn, K), -np.inf, np.float32)
+    for q in range(Qn):
+        cand = []
+        for l in range(world):
+            for k in range(K):
+                i = int(gids[l, q, k])
+                if i >= 0:
+                    cand.append((-float(gvals[l, q, k]), i))
+        cand.sort()
+        for j, (nv, i) in enumerate(cand[:K]):
+            out_i[q, j] = i
+            out_v[q, j] = -nv
+    return out_i, out_v
+
+
+def _worker(rank, world, port, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "cuda-multimodal-memory_b200"))
+    sys.path.insert(0, os.path.join(root, "oracle"))
+    import oracle as O
+    from mars_b200 import datagen
+    lo, hi = N * rank // world, N * (rank + 1) // world
+    E, mod, ts, imp = datagen.gaussian_rows(lo, hi, D, seed=9, ts_max=600.0)
+    Qm = datagen.queries(Q, D, seed=10)
+    c = O.Corpus(E=E, ts=ts, mod=mod, imp=imp)
+    ids = np.full((Q, K), -1, np.int32)
+    vals = np.full((Q, K), -np.inf, np.float32)
+    for q in range(Q):
+        s = O.fused_scores(c, Qm[q], 600.0, 0.01, use_importance=True)
+        i, v = O.topk(s, mod, -1, K)
+        ids[q, :len(i)] = i + lo        # global ids
+        vals[q, :len(v)] = v
+    # gloo has no all_gather_into_tensor; the stacked list is the same
+    # rank-major [world][Q][K] layout NCCL's all_gather_into_tensor produces
+    gl_i = [torch.empty((Q, K), dtype=torch.int32) for _ in range(world)]
+    gl_v = [torch.empty((Q, K), dtype=torch.float32) for _ in range(world)]
+    dist.all_gather(gl_i, torch.from_numpy(ids))
+    dist.all_gather(gl_v, torch.from_numpy(vals))
+    gids = torch.stack(gl_i).numpy()
+    gvals = torch.stack(gl_v).numpy()
+    mi, mv = _merge_rank_major(gids, gvals, world, Q, K)
+    if rank == 0:
+        np.savez(out_path, ids=mi, vals=mv)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2])
+def test_sharded_topk_merge_equals_whole_corpus(tmp_path, world):
+    out = str(tmp_path / "merged.npz")
+    mp.start_processes(_worker, args=(world, _free_port(), out), nprocs=world, join=True,
+                       start_method="spawn")
+    z = np.load(out)
+    import oracle as O
+    from mars_b200 import datagen
+    E, mod, ts, imp = datagen.gaussian_rows(0, N, D, seed=9, ts_max=600.0)
+    Qm = datagen.queries(Q, D, seed=10)
+    c = O.Corpus(E=E, ts=ts, mod=mod, imp=imp)
+    for q in range(Q):
+        s = O.fused_scores(c, Qm[q], 600.0, 0.01, use_importance=True)
+        i, v = O.topk(s, mod, -1, K)
+        assert np.array_equal(z["ids"][q], i)
+        assert np.array_equal(z["vals"][q], v)
+
+
+def test_shards_union_equals_whole_corpus():
+    from mars_b200 import datagen
+    full = datagen.gaussian_rows(0, 70_000, 16, seed=3)
+    for world in (2, 3, 8):
+        parts = [datagen.gaussian_rows(70_000 * r // world, 70_000 * (r + 1) // world, 16, seed=3)
+                 for r in range(world)]
+        for k in range(4):
+            assert np.array_equal(np.concatenate([p[k] for p in parts]), full[k])
