@@ -547,14 +547,15 @@ def run_batch(a):
     for _ in range(a.warmup):
         step()
     torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
     sampler = ClockSampler(local) if rank == 0 else None
     if sampler:
         sampler.start()
         time.sleep(0.3)
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()        # after the sampler started: no rank waits inside the timed region
     torch.cuda.synchronize()
     e0.record(stream)
     for _ in range(a.steps):
@@ -568,6 +569,24 @@ def run_batch(a):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     stats = bc.last_stats()
+    # phase breakdown (outside the timed region): batch alone, exchange alone
+    phases = {}
+    for name, fn in (("batch_ms", lambda: bc.query_batch_topk(store, Qd, B, a.ts_max, a.lam, K, ids, vals,
+                                                              use_importance=True, row_offset=lo,
+                                                              stream=ctx.stream)),
+                     ("exchange_merge_ms", (lambda: (dist.all_gather_into_tensor(gids, ids),
+                                                     dist.all_gather_into_tensor(gvals, vals),
+                                                     ctx.topk_merge_batch(gids, gvals, world, K, B, mids, mvals,
+                                                                          stream=ctx.stream)))
+                      if world > 1 else None)):
+        if fn is None:
+            continue
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        phases[name] = (time.perf_counter() - t0) / 3 * 1e3
     if rank == 0:
         peaks = {}
         try:
@@ -586,7 +605,7 @@ def run_batch(a):
                              "tf32_nominal": bf16 / 2,
                              "frac_of_tf32_nominal": achieved / (bf16 / 2),
                              "flops_per_batch": flops},
-                "batch_stats_rank0": stats, "clocks": clocks}
+                "batch_stats_rank0": stats, "phases_rank0_wall": phases, "clocks": clocks}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
