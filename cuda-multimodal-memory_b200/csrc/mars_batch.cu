@@ -280,7 +280,7 @@ __global__ void prep_rows_kernel(const float* __restrict__ ts, const float* __re
 }
 
 __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch, int32_t B, int32_t nc,
-                                    float max_row_norm, float* __restrict__ margin,
+                                    const unsigned int* __restrict__ norm_bits, float* __restrict__ margin,
                                     int32_t* __restrict__ cand_cnt) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= B) return;
@@ -293,7 +293,7 @@ __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch,
     s = warp_butterfly_sum(s);
     if (lane == 0) {
         // 1.0001: covers the fp32 rounding of this norm itself
-        margin[warp] = kMarginRel * sqrtf(s) * 1.0001f * max_row_norm;
+        margin[warp] = kMarginRel * sqrtf(s) * 1.0001f * __uint_as_float(*norm_bits);
         cand_cnt[warp] = 0;
     }
 }
@@ -629,6 +629,8 @@ int mars::batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d_quer
         return fail(MARS_ERR_INVALID, "mars_query_batch_topk: queries must be 16-byte aligned rows with pitch >= the store's");
     if (s->n > c->max_nodes)
         return fail(MARS_ERR_CAPACITY, "mars_query_batch_topk: store larger than the context");
+    if (s->d_norm_bits == nullptr)
+        return fail(MARS_ERR_UNSUPPORTED, "mars_query_batch_topk: store has no row-norm bound (a view of caller memory)");
     c->last = mars_batch_stats{};
     if (B == 0) return MARS_OK;
     MarsDeviceGuard g(c->device);
@@ -682,7 +684,7 @@ int mars::batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d_quer
                                               use_importance, c->d_wts);
     MARS_CUDA_TRY(cudaGetLastError());
     prep_queries_kernel<<<(B * 32 + 255) / 256, 256, 0, st>>>(d_queries, query_pitch, B, (s->dim + 3) / 4,
-                                                              s->max_row_norm, c->d_margin, c->d_cand_cnt);
+                                                              s->d_norm_bits, c->d_margin, c->d_cand_cnt);
     MARS_CUDA_TRY(cudaGetLastError());
     MARS_CUDA_TRY(cudaMemsetAsync(c->d_err, 0, sizeof(int), st));
 

@@ -186,6 +186,28 @@ struct WarpTopK {
         }
     }
 
+    // Merge a ranked list of n <= 32 entries into this one without serial
+    // inserts (KPL == 1): the element-wise better of this list and the other
+    // list reversed is a bitonic sequence holding the 32 best entries of
+    // both, and five half-cleaner steps sort it.
+    __device__ __forceinline__ void merge_sorted32(const float* vals, const int32_t* ids, int n,
+                                                   int lane) {
+        static_assert(KPL == 1, "merge_sorted32 needs one slot per lane");
+        const int j = 31 - lane;
+        float bv = -INFINITY;
+        int32_t bi = INT32_MAX;
+        if (j < n) { bv = vals[j]; bi = ids[j]; }
+        if (better(bv, bi, v[0], i[0])) { v[0] = bv; i[0] = bi; }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            const float ov = __shfl_xor_sync(MARS_FULL_MASK, v[0], off);
+            const int32_t oi = __shfl_xor_sync(MARS_FULL_MASK, i[0], off);
+            const bool ob = better(ov, oi, v[0], i[0]);
+            if (((lane & off) == 0) == ob) { v[0] = ov; i[0] = oi; }
+        }
+        refresh_threshold();
+    }
+
     // Offer unsorted candidates held one per lane (warp-collective).
     __device__ __forceinline__ void offer_lanes(float s, int32_t id, bool valid, int lane) {
         unsigned m = __ballot_sync(MARS_FULL_MASK, valid && admits(s, id));

@@ -92,12 +92,25 @@ struct mars_store {
     cudaStream_t stream = nullptr;
     cudaEvent_t written = nullptr;  // last write to the store
 
-    // largest row norm (bounds the error of the tensor-core short list)
-    float max_row_norm = 0.0f;
+    // largest row norm, as the bits of a non-negative float (bounds the
+    // error of the tensor-core short list; kernels read it on the device)
     unsigned int* d_norm_bits = nullptr;
 
     // raw view of a caller-owned DeviceMemoryGraph (compat layer)
     void* compat_key = nullptr;
+
+    // pinned, device-mapped staging for small appends: the caller's host
+    // arrays are packed here and read by the append kernel directly, so an
+    // append is one launch and returns without waiting for the device.  Two
+    // buffers alternate; each is reused only after its last kernel finished.
+    struct HostStage {
+        char* h = nullptr;        // host address
+        char* d = nullptr;        // device view of the same memory
+        size_t cap = 0;
+        cudaEvent_t done = nullptr;
+    };
+    HostStage stage[2];
+    int stage_next = 0;
 };
 
 // ---- query context (QueryContext) ----------------------------------------
@@ -140,6 +153,15 @@ struct mars_query_ctx {
     int32_t* d_result_cnt = nullptr;
     mars_query_result* h_results = nullptr;    // pinned
     int32_t* h_result_cnt = nullptr;           // pinned [2]: count, visited
+
+    // single-launch path (mars_fastq.cu): every row's fused score for the
+    // in-kernel BFS, and device views of the host-mapped result buffers
+    bool use_fused = true;
+    float* d_all_scores = nullptr;              // max_nodes
+    mars_query_result* dm_results = nullptr;    // = h_results, device view
+    int32_t* dm_result_cnt = nullptr;           // = h_result_cnt, device view
+    uint64_t fused_queries = 0;                 // answered by the single launch
+    uint64_t fused_reruns = 0;                  // BFS outgrew the last CTA
 
     // graph replay of the whole query (H2D desc -> kernels -> D2H)
     bool use_graph = true;

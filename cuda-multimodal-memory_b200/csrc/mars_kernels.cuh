@@ -83,6 +83,17 @@ struct BfsArgs {
     int32_t* result_cnt;              // [0] count, [1] visited
 };
 
+// Single-launch query (mars_fastq.cu): the scan arguments, the result
+// destination (device or host-mapped memory) and, when a.q is null, the query
+// vector itself (nc <= kFusedMaxChunks float4 chunks, i.e. D <= 1024).
+constexpr int kFusedMaxChunks = 256;
+struct FusedQueryArgs {
+    ScanArgs a;
+    void*    out;        // mars_query_result[K]
+    int32_t* out_cnt;    // [0] count (-1: the BFS outgrew the last CTA), [1] visited
+    float4   qbuf[kFusedMaxChunks];
+};
+
 __device__ __forceinline__ float desc_tq(const MarsQueryDesc& d, const MarsQueryDesc* dyn) {
     return dyn != nullptr ? dyn->t_q : d.t_q;
 }
@@ -95,6 +106,7 @@ cudaError_t launch_scan_topk(const ScanArgs& a, int k_max, int grid, cudaStream_
 cudaError_t launch_bfs_hop(const BfsArgs& a, int hop, int grid, cudaStream_t st);
 cudaError_t launch_bfs_finalize(const BfsArgs& a, int last_level, int k_max, int grid,
                                 cudaStream_t st);
+cudaError_t launch_query_fused(const FusedQueryArgs& p, int grid, cudaStream_t st);
 cudaError_t launch_topk_merge(const int32_t* ids_in, const float* vals_in, int n_lists, int K, int Q,
                               int32_t* ids_out, float* vals_out, int32_t* cnt, cudaStream_t st);
 int scan_blocks_per_sm(int nc, int k_max);

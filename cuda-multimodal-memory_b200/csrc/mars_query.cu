@@ -148,6 +148,70 @@ uint64_t graph_key(const mars_store* s, const mars_retrieval_config* cfg) {
     return h | 1ull;   // never 0 (0 = no graph)
 }
 
+constexpr int kFusedMaxK = 64;
+constexpr int kFusedTicket = 4;
+
+// One query as a single kernel launch (mars_fastq.cu).  *done = 0 when the
+// kernel reported that the BFS outgrew its last CTA (nothing written to out).
+int query_single_launch(const mars_store* s, mars_query_ctx* c, const float* query, float t_q,
+                        uint32_t epoch, const mars_retrieval_config* cfg, mars_query_result* out,
+                        int32_t* n_out, mars_retrieval_stats* stats, int* done) {
+    *done = 0;
+    cudaStream_t st = c->stream;
+    FusedQueryArgs p{};
+    ScanArgs& a = p.a;
+    a.s = make_view(s);
+    a.d = make_desc(cfg, t_q, epoch);
+    a.dyn = nullptr;
+    a.part_val = c->d_part_val;
+    a.part_idx = c->d_part_idx;
+    a.ticket = c->d_ticket + kFusedTicket;
+    a.all_scores = cfg->bfs_max_hops > 0 ? c->d_all_scores : nullptr;
+    a.stamp = c->d_stamp;
+    p.out = c->dm_results;
+    p.out_cnt = c->dm_result_cnt;
+    // the query rides in the parameter block; a device-resident query is
+    // read in place when its layout allows float4 loads
+    cudaPointerAttributes pa{};
+    const bool on_device = cudaPointerGetAttributes(&pa, query) == cudaSuccess &&
+                           pa.type == cudaMemoryTypeDevice;
+    (void)cudaGetLastError();
+    if (on_device) {
+        if ((s->dim & 3) != 0 || (reinterpret_cast<uintptr_t>(query) & 15u) != 0) {
+            MARS_CUDA_TRY(cudaMemcpy(p.qbuf, query, (size_t)s->dim * sizeof(float), cudaMemcpyDeviceToHost));
+        } else {
+            a.q = reinterpret_cast<const float4*>(query);
+        }
+    } else {
+        std::memcpy(p.qbuf, query, (size_t)s->dim * sizeof(float));
+    }
+    c->h_result_cnt[0] = -2;
+    if (stats) MARS_CUDA_TRY(cudaEventRecord(c->ev[0], st));
+    MARS_CUDA_TRY(launch_query_fused(p, c->scan_blocks, st));
+    if (stats) MARS_CUDA_TRY(cudaEventRecord(c->ev[2], st));
+    MARS_CUDA_TRY(cudaStreamSynchronize(st));
+    const int32_t got = c->h_result_cnt[0];
+    if (got < 0) return MARS_OK;
+    const int32_t cnt = std::min(got, cfg->top_k);
+    std::memcpy(out, c->h_results, (size_t)cnt * sizeof(mars_query_result));
+    *n_out = cnt;
+    if (stats) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, c->ev[0], c->ev[2]);
+        stats->gpu_ms_similarity = ms;   // one kernel: scan, selection and BFS together
+        stats->gpu_ms_topk = 0.f;
+        stats->gpu_ms_rerank = 0.f;
+        stats->gpu_ms_bfs = 0.f;
+        stats->gpu_ms_total = ms;
+        stats->nodes_scanned = s->n;
+        stats->bfs_waves = cfg->bfs_max_hops;
+        stats->nodes_visited = c->h_result_cnt[1];
+    }
+    ++c->fused_queries;
+    *done = 1;
+    return MARS_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -200,8 +264,17 @@ int mars_query_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     T(cudaMalloc(&c->d_seed_cnt, sizeof(int32_t)), "seeds");
     T(cudaMalloc(&c->d_results, MARS_MAX_TOP_K * sizeof(mars_query_result)), "results");
     T(cudaMalloc(&c->d_result_cnt, 2 * sizeof(int32_t)), "results");
-    T(cudaMallocHost(&c->h_results, MARS_MAX_TOP_K * sizeof(mars_query_result)), "pinned results");
-    T(cudaMallocHost(&c->h_result_cnt, 2 * sizeof(int32_t)), "pinned results");
+    T(cudaMalloc(&c->d_all_scores, nmax * sizeof(float)), "row scores");
+    // results land in mapped pinned memory: the single-launch path writes
+    // them from the kernel, the pipeline copies them there
+    T(cudaHostAlloc(&c->h_results, MARS_MAX_TOP_K * sizeof(mars_query_result), cudaHostAllocMapped),
+      "pinned results");
+    T(cudaHostAlloc(&c->h_result_cnt, 2 * sizeof(int32_t), cudaHostAllocMapped), "pinned results");
+    if (rc == MARS_OK) {
+        T(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->dm_results), c->h_results, 0), "mapped results");
+        T(cudaHostGetDevicePointer(reinterpret_cast<void**>(&c->dm_result_cnt), c->h_result_cnt, 0),
+          "mapped results");
+    }
     if (rc == MARS_OK) {
         T(cudaMemsetAsync(c->d_ticket, 0, kTickets * sizeof(unsigned int), c->stream), "memset");
         T(cudaMemsetAsync(c->d_stamp, 0, nmax * sizeof(unsigned long long), c->stream), "memset");
@@ -236,6 +309,7 @@ int mars_query_ctx_destroy(mars_query_ctx* c) {
     cudaFree(c->d_seed_cnt);
     cudaFree(c->d_results);
     cudaFree(c->d_result_cnt);
+    cudaFree(c->d_all_scores);
     cudaFreeHost(c->h_results);
     cudaFreeHost(c->h_result_cnt);
     for (int i = 0; i < 5; ++i)
@@ -250,6 +324,19 @@ void* mars_query_ctx_stream(mars_query_ctx* c) { return c ? (void*)c->stream : n
 int mars_query_ctx_use_graph(mars_query_ctx* c, int32_t enable) {
     if (c == nullptr) return fail(MARS_ERR_INVALID, "mars_query_ctx_use_graph: NULL context");
     c->use_graph = enable != 0;
+    return MARS_OK;
+}
+
+int mars_query_ctx_use_fused(mars_query_ctx* c, int32_t enable) {
+    if (c == nullptr) return fail(MARS_ERR_INVALID, "mars_query_ctx_use_fused: NULL context");
+    c->use_fused = enable != 0;
+    return MARS_OK;
+}
+
+int mars_query_ctx_path_counts(const mars_query_ctx* c, uint64_t* fused, uint64_t* reruns) {
+    if (c == nullptr) return fail(MARS_ERR_INVALID, "mars_query_ctx_path_counts: NULL context");
+    if (fused) *fused = c->fused_queries;
+    if (reruns) *reruns = c->fused_reruns;
     return MARS_OK;
 }
 
@@ -269,8 +356,18 @@ int mars_query(const mars_store* s, mars_query_ctx* c, const float* query, float
         return MARS_OK;
     }
     int rc = MARS_OK;
-    const uint32_t epoch = next_epoch(c, st, &rc);
+    uint32_t epoch = next_epoch(c, st, &rc);
     MARS_TRY(rc);
+
+    if (c->use_fused && cfg->top_k <= kFusedMaxK && (s->dim + 3) / 4 <= kFusedMaxChunks) {
+        int done = 0;
+        MARS_TRY(query_single_launch(s, c, query, t_q, epoch, cfg, out, n_out, stats, &done));
+        if (done) return MARS_OK;
+        // the BFS outgrew the last CTA: answer with the multi-kernel pipeline
+        ++c->fused_reruns;
+        epoch = next_epoch(c, st, &rc);
+        MARS_TRY(rc);
+    }
 
     // stage descriptor + query in pinned memory (the previous query has
     // completed: this call is synchronous)

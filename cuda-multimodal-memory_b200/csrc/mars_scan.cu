@@ -5,183 +5,34 @@
 // radix sort of N pairs) with a single streaming kernel that never writes a
 // score array:
 //
-//  * each warp owns a contiguous range of rows (balanced to +-1 row) and
-//    streams them with 128-bit read-only loads, two rows in flight per warp;
-//  * the query lives in registers (lane l holds float4 chunks l, l+32, ...);
-//  * the row's fused score is formed in registers and offered to a
-//    warp-resident ranked list (WarpTopK) -- almost every row is rejected by a
-//    single compare against the list's threshold;
-//  * warps merge into a CTA list in shared memory, CTAs write their list to a
-//    small partial buffer, and the last CTA to finish (ticket counter, no
-//    spinning) merges all partial lists and, for the query pipeline, seeds the
-//    BFS state.
+//  * the streaming part (mars_scan_body.cuh) keeps a warp-resident ranked
+//    list per warp, merges them per CTA and writes one partial list per CTA;
+//  * the last CTA to finish (ticket counter, no spinning) merges the partial
+//    lists, writes the top-K and, for the multi-kernel query pipeline, seeds
+//    the BFS state.
 //
 // HBM traffic per row: pitch*4 bytes of embedding + 4 B timestamp
 // (+4 B importance, +4 B modality when used); nothing else scales with N.
-#include "mars_common.cuh"
-#include "mars_kernels.cuh"
+#include "mars_scan_body.cuh"
 
 namespace mars {
 
-constexpr int kStageEntries = 3072;   // 24 KB of staged (score, id) pairs
-
 template <int KPL, int CPL, bool ALL>
 __global__ void __launch_bounds__(kScanThreads, 2) scan_topk_kernel(const ScanArgs a) {
-    __shared__ float   s_val[kScanWarps][kMaxTopK];
-    __shared__ int32_t s_idx[kScanWarps][kMaxTopK];
-    __shared__ float   s_stage_v[kStageEntries];
-    __shared__ int32_t s_stage_i[kStageEntries];
-    __shared__ bool    s_last;
-
-    const int lane = threadIdx.x & 31;
-    const int warp = threadIdx.x >> 5;
+    __shared__ ScanShared sm;
     const MarsQueryDesc& d = a.d;
-    const float t_q = desc_tq(d, a.dyn), lambda = d.lambda;
-    const int32_t filter = d.filter;
-    const bool use_imp = d.use_imp != 0 && a.s.imp != nullptr;
-    const int K = d.K;
-    const int32_t id_off = d.row_offset;
-    const int32_t n = *a.s.d_n;
-    const int nc = a.s.nc;
-
-    // query chunks in registers
-    float4 qv[CPL];
-#pragma unroll
-    for (int j = 0; j < CPL; ++j) {
-        const int c = lane + 32 * j;
-        qv[j] = c < nc ? a.q[c] : make_float4(0.f, 0.f, 0.f, 0.f);
-    }
-
-    WarpTopK<KPL> top;
-    top.init(K);
-
-    // balanced contiguous row range of this warp
-    const int64_t W = (int64_t)gridDim.x * kScanWarps;
-    const int64_t w = (int64_t)blockIdx.x * kScanWarps + warp;
-    const int32_t r0 = (int32_t)((int64_t)n * w / W);
-    const int32_t r1 = (int32_t)((int64_t)n * (w + 1) / W);
-
-    // metadata window: lane l holds row wbase + l
-    int32_t wbase = r0;
-    float ts_w = 0.f, imp_w = 1.f;
-    int32_t mod_w = 0;
-    auto load_meta = [&](int32_t base) {
-        const int32_t r = base + lane;
-        if (r < r1) {
-            ts_w = __ldg(a.s.ts + r);
-            if (use_imp) imp_w = __ldg(a.s.imp + r);
-            if (filter >= 0) mod_w = __ldg(a.s.mod + r);
-        }
-    };
-    load_meta(wbase);
-
-    auto process = [&](int32_t row, float dot) {
-        if (row - wbase >= 32) { wbase += 32; load_meta(wbase); }
-        const int src = row - wbase;
-        const float t = __shfl_sync(MARS_FULL_MASK, ts_w, src);
-        const float im = __shfl_sync(MARS_FULL_MASK, imp_w, src);
-        const int32_t m = __shfl_sync(MARS_FULL_MASK, mod_w, src);
-        if ((filter >= 0 && m != filter) || row + 1 == d.exclude_plus1) {
-            if (ALL && lane == 0) a.all_scores[row] = -FLT_MAX;
-            return;
-        }
-        float f = fused_weight_apply(dot, t, t_q, lambda);
-        if (use_imp) f = f * im;
-        if (ALL && lane == 0) a.all_scores[row] = f;
-        top.push(f, row + id_off, lane);
-    };
-
-    const float4* __restrict__ E4 = reinterpret_cast<const float4*>(a.s.E);
-    int32_t r = r0;
-    for (; r + 1 < r1; r += 2) {
-        const float4* p0 = E4 + (int64_t)r * a.s.pitch4;
-        const float4* p1 = p0 + a.s.pitch4;
-        float4 e0[CPL], e1[CPL];
-#pragma unroll
-        for (int j = 0; j < CPL; ++j) {
-            const int c = lane + 32 * j;
-            if (c < nc) { e0[j] = ldg_stream(p0 + c); e1[j] = ldg_stream(p1 + c); }
-        }
-        float acc0 = 0.f, acc1 = 0.f;
-#pragma unroll
-        for (int j = 0; j < CPL; ++j) {
-            const int c = lane + 32 * j;
-            if (c < nc) { acc0 = fma4(e0[j], qv[j], acc0); acc1 = fma4(e1[j], qv[j], acc1); }
-        }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-            const float x0 = __shfl_xor_sync(MARS_FULL_MASK, acc0, off);
-            const float x1 = __shfl_xor_sync(MARS_FULL_MASK, acc1, off);
-            acc0 = __fadd_rn(acc0, x0);
-            acc1 = __fadd_rn(acc1, x1);
-        }
-        process(r, acc0);
-        process(r + 1, acc1);
-    }
-    if (r < r1) {
-        const float4* p0 = E4 + (int64_t)r * a.s.pitch4;
-        float acc0 = 0.f;
-#pragma unroll
-        for (int j = 0; j < CPL; ++j) {
-            const int c = lane + 32 * j;
-            if (c < nc) acc0 = fma4(ldg_stream(p0 + c), qv[j], acc0);
-        }
-        process(r, warp_butterfly_sum(acc0));
-    }
-
-    // ---- CTA merge ---------------------------------------------------------
-    top.store(s_val[warp], s_idx[warp], lane);
-    __syncthreads();
-    if (warp == 0) {
-        for (int ww = 1; ww < kScanWarps; ++ww) top.offer_sorted(s_val[ww], s_idx[ww], K, lane);
-        top.store(a.part_val + (int64_t)blockIdx.x * K, a.part_idx + (int64_t)blockIdx.x * K, lane);
-        __threadfence();
-        __syncwarp();
-        if (lane == 0) s_last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
-        __syncwarp();
-    }
-    __syncthreads();
-    if (!s_last) return;
+    if (!scan_rows<KPL, CPL, ALL>(a, a.q, desc_tq(d, a.dyn), sm)) return;
 
     // ---- last CTA: merge every CTA's list ----------------------------------
-    // Stage the lists in shared memory with all threads' loads in flight at
-    // once (one memory round trip per batch instead of one per list), then
-    // let each warp merge a subset of the staged lists.
-    __threadfence();
-    top.init(K);
-    const int lists_per_batch = kStageEntries / K;
-    for (int b0 = 0; b0 < (int)gridDim.x; b0 += lists_per_batch) {
-        const int nl = min(lists_per_batch, (int)gridDim.x - b0);
-        const int ne = nl * K;
-        const float* pv = a.part_val + (int64_t)b0 * K;
-        const int32_t* pi = a.part_idx + (int64_t)b0 * K;
-#pragma unroll 4
-        for (int j = threadIdx.x; j < ne; j += kScanThreads) {
-            s_stage_v[j] = __ldcg(pv + j);   // written by other SMs: bypass L1
-            s_stage_i[j] = __ldcg(pi + j);
-        }
-        __syncthreads();
-        for (int l = warp; l < nl; l += kScanWarps)
-            top.offer_sorted(s_stage_v + l * K, s_stage_i + l * K, K, lane);
-        __syncthreads();
+    const int cnt = final_merge<KPL>(a, sm);
+    const int K = d.K;
+    const int32_t id_off = d.row_offset;
+    for (int p = threadIdx.x; p < K; p += kScanThreads) {
+        const bool valid = p < cnt;
+        a.out_val[p] = valid ? key_score(sm.keys()[p]) : -INFINITY;
+        a.out_idx[p] = valid ? key_id(sm.keys()[p]) : -1;
     }
-    top.store(s_val[warp], s_idx[warp], lane);
-    __syncthreads();
-    if (warp != 0) return;
-    for (int ww = 1; ww < kScanWarps; ++ww) top.offer_sorted(s_val[ww], s_idx[ww], K, lane);
-
-    int cnt = 0;
-#pragma unroll
-    for (int sl = 0; sl < KPL; ++sl) {
-        const int p = sl * 32 + lane;
-        const bool valid = p < K && top.i[sl] != INT32_MAX;
-        cnt += __popc(__ballot_sync(MARS_FULL_MASK, valid));
-        if (p < K) {
-            a.out_val[p] = valid ? top.v[sl] : -INFINITY;
-            a.out_idx[p] = valid ? top.i[sl] : -1;
-        }
-    }
-    if (lane == 0) {
+    if (threadIdx.x == 0) {
         *a.out_cnt = cnt;
         *a.ticket = 0u;   // re-arm for the next launch
     }
@@ -189,17 +40,15 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_topk_kernel(const ScanAr
         // seed the BFS: level 0 = the top-K, stamp (epoch, level 0)
         const unsigned long long st0 =
             (unsigned long long)((desc_epoch(d, a.dyn) << 4) | 15u) << 32;
-#pragma unroll
-        for (int sl = 0; sl < KPL; ++sl) {
-            const int p = sl * 32 + lane;
-            if (p < cnt) {
-                const int32_t u = top.i[sl] - id_off;
-                a.stamp[u] = st0 | f2key(top.v[sl]);
-                a.vis_ids[p] = u;
-                a.vis_score[p] = top.v[sl];
-            }
+        for (int p = threadIdx.x; p < cnt; p += kScanThreads) {
+            const unsigned long long k = sm.keys()[p];
+            const float v = key_score(k);
+            const int32_t u = key_id(k) - id_off;
+            a.stamp[u] = st0 | f2key(v);
+            a.vis_ids[p] = u;
+            a.vis_score[p] = v;
         }
-        if (lane == 0) {
+        if (threadIdx.x == 0) {
             a.lvl[0] = 0;
             a.lvl[1] = cnt;
             a.lvl[16] = cnt;

@@ -76,6 +76,62 @@ __global__ void row_norm_max_kernel(const float* __restrict__ E, int64_t pitch, 
     if (lane == 0) atomicMax(out_bits, __float_as_uint(sqrtf(s) * 1.0001f));
 }
 
+// Small appends in one launch: one warp per row copies the row from the
+// (host-mapped) staging area into E, normalises it with exactly the rule of
+// normalize_rows_kernel when asked, folds its norm into the store's bound,
+// copies the row's metadata and publishes the new row count.  Kernels that
+// read the store run after this one (the store's `written` event).
+constexpr int kAppendWarps = 8;
+struct AppendArgs {
+    float* E;
+    int64_t pitch;
+    int32_t first, count, dim, normalize;
+    const float* rows;        // count x dim, packed
+    const int32_t* mod;
+    const float* ts;
+    const float* imp;         // may be null: importance 1
+    int32_t* d_mod;
+    float* d_ts;
+    float* d_imp;
+    unsigned int* norm_bits;
+    int32_t* d_n;
+    int32_t new_n;
+};
+
+__global__ void __launch_bounds__(kAppendWarps * 32) append_rows_kernel(const AppendArgs a) {
+    __shared__ float s_row[kAppendWarps][1024];
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int r = blockIdx.x * kAppendWarps + w;
+    if (blockIdx.x == 0 && threadIdx.x == 0) *a.d_n = a.new_n;
+    if (r >= a.count) return;
+    const float* src = a.rows + (int64_t)r * a.dim;
+    float* dst = a.E + (int64_t)(a.first + r) * a.pitch;
+    for (int d = lane; d < a.dim; d += 32) s_row[w][d] = src[d];
+    __syncwarp();
+    float norm = 1.0f;
+    if (a.normalize) {
+        if (lane == 0) {
+            float acc = 0.0f;
+            for (int d = 0; d < a.dim; ++d) acc = __fadd_rn(acc, __fmul_rn(s_row[w][d], s_row[w][d]));
+            norm = __fadd_rn(__fsqrt_rn(acc), 1e-8f);
+        }
+        norm = __shfl_sync(0xffffffffu, norm, 0);
+    }
+    float ss = 0.f;
+    for (int d = lane; d < a.dim; d += 32) {
+        const float x = a.normalize ? __fdiv_rn(s_row[w][d], norm) : s_row[w][d];
+        dst[d] = x;
+        ss = fmaf(x, x, ss);
+    }
+    for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    if (lane == 0) {
+        atomicMax(a.norm_bits, __float_as_uint(sqrtf(ss) * 1.0001f));
+        a.d_mod[a.first + r] = a.mod[r];
+        a.d_ts[a.first + r] = a.ts[r];
+        a.d_imp[a.first + r] = a.imp != nullptr ? a.imp[r] : 1.0f;
+    }
+}
+
 __global__ void fill_f32_kernel(float* p, int64_t n, float v) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) p[i] = v;
@@ -162,9 +218,58 @@ static void release_store(mars_store* s) {
     cudaFree(s->d_norm_bits);
     cudaFree(s->d_extra);
     cudaFree(s->d_extra_cnt);
+    for (auto& sg : s->stage) {
+        if (sg.done) {
+            cudaEventSynchronize(sg.done);
+            cudaEventDestroy(sg.done);
+        }
+        if (sg.h) cudaFreeHost(sg.h);
+    }
     if (s->written) cudaEventDestroy(s->written);
     if (s->stream) cudaStreamDestroy(s->stream);
 }
+
+namespace {
+
+constexpr size_t kStageBytes = 4u << 20;
+
+bool on_host(const void* p) {
+    if (p == nullptr) return true;
+    cudaPointerAttributes pa{};
+    if (cudaPointerGetAttributes(&pa, p) != cudaSuccess) {
+        (void)cudaGetLastError();
+        return true;
+    }
+    return pa.type != cudaMemoryTypeDevice;
+}
+
+// The next staging buffer with room for `bytes`, after its previous user
+// finished; nullptr when the request is larger than a buffer.
+mars_store::HostStage* stage_acquire(mars_store* s, size_t bytes, int* rc) {
+    *rc = MARS_OK;
+    if (bytes > kStageBytes) return nullptr;
+    mars_store::HostStage& sg = s->stage[s->stage_next];
+    if (sg.h == nullptr) {
+        cudaError_t e = cudaHostAlloc(reinterpret_cast<void**>(&sg.h), kStageBytes, cudaHostAllocMapped);
+        if (e == cudaSuccess) e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&sg.d), sg.h, 0);
+        if (e == cudaSuccess) e = cudaEventCreateWithFlags(&sg.done, cudaEventDisableTiming);
+        if (e != cudaSuccess) {
+            *rc = cuda_fail(e, "append staging", __FILE__, __LINE__);
+            return nullptr;
+        }
+        sg.cap = kStageBytes;
+    } else {
+        const cudaError_t e = cudaEventSynchronize(sg.done);
+        if (e != cudaSuccess) {
+            *rc = cuda_fail(e, "append staging wait", __FILE__, __LINE__);
+            return nullptr;
+        }
+    }
+    s->stage_next ^= 1;
+    return &sg;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -276,15 +381,12 @@ int mars_store_upload(mars_store* s, int32_t n, const float* embeddings, const i
     }
     MARS_CUDA_TRY(cudaMemcpyAsync(s->d_n, &n, sizeof(int32_t), cudaMemcpyHostToDevice, st));
     MARS_CUDA_TRY(cudaMemsetAsync(s->d_norm_bits, 0, sizeof(unsigned int), st));
-    unsigned int norm_bits = 0;
     if (n > 0) {
         row_norm_max_kernel<<<(unsigned)(((int64_t)n * 32 + 255) / 256), 256, 0, st>>>(
             s->d_E, (int64_t)P, 0, n, s->dim, s->d_norm_bits);
         MARS_CUDA_TRY(cudaGetLastError());
-        MARS_CUDA_TRY(cudaMemcpyAsync(&norm_bits, s->d_norm_bits, 4, cudaMemcpyDeviceToHost, st));
     }
     MARS_CUDA_TRY(cudaStreamSynchronize(st));   // n lives on this stack frame
-    std::memcpy(&s->max_row_norm, &norm_bits, 4);
     s->n = n;
     MARS_CUDA_TRY(cudaEventRecord(s->written, st));
     return MARS_OK;
@@ -307,6 +409,46 @@ int mars_store_append(mars_store* s, int32_t n, const float* embeddings, const i
     cudaStream_t st = s->stream;
     const size_t D = (size_t)s->dim, P = (size_t)s->pitch;
     const int32_t first = s->n;
+
+    // small host-side appends: pack into mapped staging, one launch, no wait
+    const size_t row_bytes = (size_t)n * D * sizeof(float);
+    const size_t bytes = row_bytes + (size_t)n * 12;
+    if (bytes <= kStageBytes && on_host(embeddings) && on_host(modalities) && on_host(timestamps) &&
+        on_host(importance)) {
+        int rc = MARS_OK;
+        mars_store::HostStage* sg = stage_acquire(s, bytes, &rc);
+        MARS_TRY(rc);
+        if (sg != nullptr) {
+            std::memcpy(sg->h, embeddings, row_bytes);
+            std::memcpy(sg->h + row_bytes, modalities, (size_t)n * 4);
+            std::memcpy(sg->h + row_bytes + (size_t)n * 4, timestamps, (size_t)n * 4);
+            if (importance) std::memcpy(sg->h + row_bytes + (size_t)n * 8, importance, (size_t)n * 4);
+            AppendArgs aa{};
+            aa.E = s->d_E;
+            aa.pitch = (int64_t)P;
+            aa.first = first;
+            aa.count = n;
+            aa.dim = s->dim;
+            aa.normalize = normalize != 0;
+            aa.rows = reinterpret_cast<const float*>(sg->d);
+            aa.mod = reinterpret_cast<const int32_t*>(sg->d + row_bytes);
+            aa.ts = reinterpret_cast<const float*>(sg->d + row_bytes + (size_t)n * 4);
+            aa.imp = importance ? reinterpret_cast<const float*>(sg->d + row_bytes + (size_t)n * 8) : nullptr;
+            aa.d_mod = s->d_mod;
+            aa.d_ts = s->d_ts;
+            aa.d_imp = s->d_imp;
+            aa.norm_bits = s->d_norm_bits;
+            aa.d_n = s->d_n;
+            aa.new_n = first + n;
+            append_rows_kernel<<<(n + kAppendWarps - 1) / kAppendWarps, kAppendWarps * 32, 0, st>>>(aa);
+            MARS_CUDA_TRY(cudaGetLastError());
+            MARS_CUDA_TRY(cudaEventRecord(sg->done, st));
+            MARS_CUDA_TRY(cudaEventRecord(s->written, st));
+            s->n = first + n;
+            return MARS_OK;
+        }
+    }
+
     MARS_CUDA_TRY(cudaMemcpy2DAsync(s->d_E + (size_t)first * P, P * sizeof(float), embeddings,
                                     D * sizeof(float), D * sizeof(float), (size_t)n,
                                     cudaMemcpyDefault, st));
@@ -323,13 +465,10 @@ int mars_store_append(mars_store* s, int32_t n, const float* embeddings, const i
     row_norm_max_kernel<<<(unsigned)(((int64_t)n * 32 + 255) / 256), 256, 0, st>>>(
         s->d_E, (int64_t)P, first, n, s->dim, s->d_norm_bits);
     MARS_CUDA_TRY(cudaGetLastError());
-    unsigned int norm_bits = 0;
-    MARS_CUDA_TRY(cudaMemcpyAsync(&norm_bits, s->d_norm_bits, 4, cudaMemcpyDeviceToHost, st));
     // publish the new count after the rows (same stream)
     const int32_t new_n = first + n;
     MARS_CUDA_TRY(cudaMemcpyAsync(s->d_n, &new_n, sizeof(int32_t), cudaMemcpyHostToDevice, st));
     MARS_CUDA_TRY(cudaStreamSynchronize(st));   // new_n and caller buffers live on the host
-    std::memcpy(&s->max_row_norm, &norm_bits, 4);
     s->n = new_n;
     MARS_CUDA_TRY(cudaEventRecord(s->written, st));
     return MARS_OK;
@@ -342,25 +481,55 @@ int mars_store_append_edges(mars_store* s, int32_t n, const int32_t* src, const 
     if (n == 0) return MARS_OK;
     if (s->edge_slack <= 0)
         return fail(MARS_ERR_CAPACITY, "mars_store_append_edges: store was created with edge_slack 0");
-    // plan on the host (deterministic slot order = call order), then scatter
-    std::vector<int32_t> slot(n), fin(n), cnt_after;
-    std::vector<int32_t> local = s->h_extra_cnt;
+    // plan on the host (deterministic slot order = call order), then scatter;
+    // the host counts are advanced in place and rolled back on failure
+    std::vector<int32_t> slot(n), fin(n);
+    int32_t* cnt = s->h_extra_cnt.data();
+    auto rollback = [&](int32_t upto) {
+        for (int32_t j = 0; j < upto; ++j) cnt[src[j]] -= 1;
+    };
     for (int32_t i = 0; i < n; ++i) {
         const int32_t u = src[i], v = dst[i];
-        if (u < 0 || u >= s->n || v < 0 || v >= s->n)
+        if (u < 0 || u >= s->n || v < 0 || v >= s->n) {
+            rollback(i);
             return fail(MARS_ERR_INVALID, "mars_store_append_edges: endpoint out of range");
-        if (local[u] >= s->edge_slack)
+        }
+        if (cnt[u] >= s->edge_slack) {
+            rollback(i);
             return fail(MARS_ERR_CAPACITY, "mars_store_append_edges: node " + std::to_string(u) +
                                                " has no free neighbour slot");
-        slot[i] = u * s->edge_slack + local[u];
-        local[u] += 1;
+        }
+        slot[i] = u * s->edge_slack + cnt[u];
+        cnt[u] += 1;
     }
-    for (int32_t i = 0; i < n; ++i) fin[i] = local[src[i]];
+    for (int32_t i = 0; i < n; ++i) fin[i] = cnt[src[i]];
     MarsDeviceGuard g(s->device);
     cudaStream_t st = s->stream;
-    int32_t* d_tmp = nullptr;
-    MARS_CUDA_TRY(cudaMallocAsync(&d_tmp, (size_t)n * 4 * 4, st));
     int rc = MARS_OK;
+    {   // small batches: mapped staging, one launch, no wait
+        mars_store::HostStage* sg = stage_acquire(s, (size_t)n * 16, &rc);
+        if (rc != MARS_OK) { rollback(n); return rc; }
+        if (sg != nullptr) {
+            int32_t* h = reinterpret_cast<int32_t*>(sg->h);
+            const int32_t* d = reinterpret_cast<const int32_t*>(sg->d);
+            std::memcpy(h, slot.data(), (size_t)n * 4);
+            std::memcpy(h + n, dst, (size_t)n * 4);
+            std::memcpy(h + 2 * (size_t)n, src, (size_t)n * 4);
+            std::memcpy(h + 3 * (size_t)n, fin.data(), (size_t)n * 4);
+            scatter_edges_kernel<<<(n + 255) / 256, 256, 0, st>>>(s->d_extra, s->d_extra_cnt, d, d + n,
+                                                                   d + 2 * (size_t)n, d + 3 * (size_t)n, n);
+            const cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess) { rollback(n); return cuda_fail(e, "scatter_edges_kernel", __FILE__, __LINE__); }
+            MARS_CUDA_TRY(cudaEventRecord(sg->done, st));
+            MARS_CUDA_TRY(cudaEventRecord(s->written, st));
+            return MARS_OK;
+        }
+    }
+    int32_t* d_tmp = nullptr;
+    if (cudaMallocAsync(&d_tmp, (size_t)n * 4 * 4, st) != cudaSuccess) {
+        rollback(n);
+        return fail(MARS_ERR_OOM, "mars_store_append_edges: scratch allocation failed");
+    }
     do {
         if (cudaMemcpyAsync(d_tmp, slot.data(), (size_t)n * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
             cudaMemcpyAsync(d_tmp + n, dst, (size_t)n * 4, cudaMemcpyHostToDevice, st) != cudaSuccess ||
@@ -375,8 +544,7 @@ int mars_store_append_edges(mars_store* s, int32_t n, const int32_t* src, const 
     } while (0);
     cudaFreeAsync(d_tmp, st);
     MARS_CUDA_TRY(cudaStreamSynchronize(st));
-    if (rc != MARS_OK) return rc;
-    s->h_extra_cnt.swap(local);
+    if (rc != MARS_OK) { rollback(n); return rc; }
     MARS_CUDA_TRY(cudaEventRecord(s->written, st));
     return MARS_OK;
 }

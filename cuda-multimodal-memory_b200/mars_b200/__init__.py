@@ -113,6 +113,8 @@ _SIGS = {
     "mars_query_ctx_create": [_I32, _I32, _I32, _I32, C.POINTER(_VP)],
     "mars_query_ctx_destroy": [_VP],
     "mars_query_ctx_use_graph": [_VP, _I32],
+    "mars_query_ctx_use_fused": [_VP, _I32],
+    "mars_query_ctx_path_counts": [_VP, C.POINTER(C.c_uint64), C.POINTER(C.c_uint64)],
     "mars_query": [_VP, _VP, _VP, _F32, C.POINTER(RetrievalConfig), _VP, C.POINTER(_I32),
                    C.POINTER(RetrievalStats)],
     "mars_query_device": [_VP, _VP, _VP, _F32, C.POINTER(RetrievalConfig), _VP, _VP, _VP],
@@ -286,7 +288,7 @@ class QueryContext:
     """Query scratch (QueryContext) bound to a device."""
 
     def __init__(self, max_nodes: int, dim: int, max_k: int = 64, device: int = 0,
-                 use_graph: bool = True):
+                 use_graph: bool = True, use_fused: bool = True):
         h = C.c_void_p()
         _check(lib().mars_query_ctx_create(device, max_nodes, dim, max_k, C.byref(h)))
         self.handle = h
@@ -294,6 +296,18 @@ class QueryContext:
         self.dim = dim
         if not use_graph:
             _check(lib().mars_query_ctx_use_graph(self.handle, 0))
+        if not use_fused:
+            _check(lib().mars_query_ctx_use_fused(self.handle, 0))
+
+    def set_fused(self, enable: bool) -> None:
+        """Single-launch mars_query (True) or the multi-kernel pipeline (False)."""
+        _check(lib().mars_query_ctx_use_fused(self.handle, int(bool(enable))))
+
+    def path_counts(self) -> tuple[int, int]:
+        """(queries answered by the single launch, of those re-run by the pipeline)."""
+        f, r = C.c_uint64(), C.c_uint64()
+        _check(lib().mars_query_ctx_path_counts(self.handle, C.byref(f), C.byref(r)))
+        return f.value, r.value
 
     @property
     def stream(self) -> int:

@@ -384,6 +384,20 @@ int mars_debug_fused_scores(const mars_store* s, mars_query_ctx* ctx,
  * timings are real. */
 int mars_query_ctx_use_graph(mars_query_ctx* ctx, int32_t enable);
 
+/* Answer mars_query with one kernel launch when top_k <= 64 and dim <= 1024
+ * (default on): the query vector travels in the launch's parameter block,
+ * the last CTA of the scan also runs the BFS and ranks the visited set, and
+ * the results are written straight into mapped host memory.  This replaces
+ * the 6-9 launches and copies of src/memory_cuda.cu:1069-1158 for one query.
+ * A query whose BFS outgrows that CTA (more than 3072 visited nodes or 1024
+ * nodes in one level) is answered again by the multi-kernel pipeline; the
+ * results are the same either way.  enable = 0 always uses the pipeline. */
+int mars_query_ctx_use_fused(mars_query_ctx* ctx, int32_t enable);
+
+/* Number of mars_query calls answered by the single launch, and of those
+ * that had to be answered again by the pipeline.  Either pointer may be NULL. */
+int mars_query_ctx_path_counts(const mars_query_ctx* ctx, uint64_t* fused, uint64_t* reruns);
+
 /* The context's CUDA stream (cudaStream_t as void*). */
 void* mars_query_ctx_stream(mars_query_ctx* ctx);
 
