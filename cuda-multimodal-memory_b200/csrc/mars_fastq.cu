@@ -24,6 +24,13 @@
 
 namespace mars {
 
+// Store with release semantics at system scope: every write this thread
+// made or observed (through the preceding barrier) becomes visible to the
+// host no later than the stored value.
+__device__ __forceinline__ void store_release_sys(int32_t* p, int32_t v) {
+    asm volatile("st.release.sys.global.s32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
 constexpr int kTailCap = kStageEntries;   // visited nodes held by the last CTA
 constexpr int kLevelCap = 1024;           // nodes of one BFS level
 
@@ -172,9 +179,9 @@ __global__ void __launch_bounds__(kScanThreads, 2) query_fused_kernel(const __gr
         __syncthreads();
         if (sm.misc[1] != 0) {
             if (threadIdx.x == 0) {
-                p.out_cnt[0] = -1;
-                p.out_cnt[1] = 0;
                 *a.ticket = 0u;
+                p.out_cnt[1] = 0;
+                store_release_sys(p.out_cnt, -1);
             }
             return;
         }
@@ -212,10 +219,13 @@ __global__ void __launch_bounds__(kScanThreads, 2) query_fused_kernel(const __gr
         r.hops_from_seed = ALL ? 15 - (int)((uint32_t)(__ldcg(a.stamp + u) >> 32) & 15u) : 0;
         out[i] = r;
     }
+    // the count is written last, by a system-scope release store: a host
+    // that polls it sees every result (and the visited count) once it changes
+    __syncthreads();
     if (threadIdx.x == 0) {
-        p.out_cnt[0] = cnt;
-        p.out_cnt[1] = total;
         *a.ticket = 0u;   // re-arm for the next launch
+        p.out_cnt[1] = total;
+        store_release_sys(p.out_cnt, cnt);
     }
 }
 

@@ -10,6 +10,8 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
+#include <chrono>
 #include <cstring>
 #include <string>
 
@@ -150,6 +152,8 @@ uint64_t graph_key(const mars_store* s, const mars_retrieval_config* cfg) {
 
 constexpr int kFusedMaxK = 64;
 constexpr int kFusedTicket = 4;
+constexpr int32_t kCountPending = -2;
+constexpr int kPollMs = 200;
 
 // One query as a single kernel launch (mars_fastq.cu).  *done = 0 when the
 // kernel reported that the BFS outgrew its last CTA (nothing written to out).
@@ -185,12 +189,28 @@ int query_single_launch(const mars_store* s, mars_query_ctx* c, const float* que
     } else {
         std::memcpy(p.qbuf, query, (size_t)s->dim * sizeof(float));
     }
-    c->h_result_cnt[0] = -2;
+    volatile int32_t* flag = c->h_result_cnt;
+    flag[0] = kCountPending;
     if (stats) MARS_CUDA_TRY(cudaEventRecord(c->ev[0], st));
     MARS_CUDA_TRY(launch_query_fused(p, c->scan_blocks, st));
-    if (stats) MARS_CUDA_TRY(cudaEventRecord(c->ev[2], st));
-    MARS_CUDA_TRY(cudaStreamSynchronize(st));
-    const int32_t got = c->h_result_cnt[0];
+    if (stats) {
+        MARS_CUDA_TRY(cudaEventRecord(c->ev[2], st));
+        MARS_CUDA_TRY(cudaStreamSynchronize(st));
+    } else {
+        // the kernel writes the count last (after a system-scope fence), so
+        // the results can be taken as soon as it changes, without waiting
+        // for the kernel to retire; a bounded spin, then the stream's own
+        // synchronisation (which also reports any launch failure)
+        const auto t0 = std::chrono::steady_clock::now();
+        for (uint32_t i = 0; flag[0] == kCountPending; ++i) {
+            if ((i & 1023u) == 1023u &&
+                std::chrono::steady_clock::now() - t0 > std::chrono::milliseconds(kPollMs)) break;
+        }
+        if (flag[0] == kCountPending) MARS_CUDA_TRY(cudaStreamSynchronize(st));
+        std::atomic_thread_fence(std::memory_order_acquire);
+    }
+    const int32_t got = flag[0];
+    if (got == kCountPending) return fail(MARS_ERR_DEVICE, "mars_query: the query kernel did not report");
     if (got < 0) return MARS_OK;
     const int32_t cnt = std::min(got, cfg->top_k);
     std::memcpy(out, c->h_results, (size_t)cnt * sizeof(mars_query_result));
@@ -205,7 +225,7 @@ int query_single_launch(const mars_store* s, mars_query_ctx* c, const float* que
         stats->gpu_ms_total = ms;
         stats->nodes_scanned = s->n;
         stats->bfs_waves = cfg->bfs_max_hops;
-        stats->nodes_visited = c->h_result_cnt[1];
+        stats->nodes_visited = flag[1];
     }
     ++c->fused_queries;
     *done = 1;

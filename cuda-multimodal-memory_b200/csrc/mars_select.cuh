@@ -47,6 +47,80 @@ __device__ __forceinline__ void block_bitonic_desc(unsigned long long* keys, int
     }
 }
 
+// Sort keys[0, M) (M <= 32) in descending order within warp 0, in
+// registers (no block barriers); every thread calls it, it ends with a
+// __syncthreads().
+__device__ __forceinline__ void warp0_sort32_desc(unsigned long long* keys, int M) {
+    if (threadIdx.x < 32) {
+        const int lane = threadIdx.x;
+        unsigned long long v = lane < M ? keys[lane] : 0ull;
+#pragma unroll
+        for (int k = 2; k <= 32; k <<= 1) {
+#pragma unroll
+            for (int j = k >> 1; j > 0; j >>= 1) {
+                const unsigned long long o = __shfl_xor_sync(MARS_FULL_MASK, v, j);
+                const bool lower = (lane & j) == 0;
+                const bool desc = (lane & k) == 0;
+                // the lower lane of a descending pair keeps the larger key
+                const bool take = (lower == desc) ? (o > v) : (o < v);
+                if (take) v = o;
+            }
+        }
+        if (lane < M) keys[lane] = v;
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ float4 ld_cg_f4(const float4* p) {
+    float4 v;
+    asm volatile("ld.global.cg.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ int4 ld_cg_i4(const int4* p) {
+    int4 v;
+    asm volatile("ld.global.cg.v4.s32 {%0,%1,%2,%3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
+
+// Append `key` to list[] at a shared counter, one shared atomic per warp.
+// Warp-collective: every lane of the warp calls it.
+__device__ __forceinline__ void warp_append(bool take, unsigned long long key, unsigned long long* list,
+                                            int* counter, int cap) {
+    const unsigned m = __ballot_sync(MARS_FULL_MASK, take);
+    if (m == 0) return;
+    const int lane = threadIdx.x & 31;
+    int base = 0;
+    if (lane == __ffs(m) - 1) base = atomicAdd(counter, __popc(m));
+    base = __shfl_sync(MARS_FULL_MASK, base, __ffs(m) - 1);
+    const int pos = base + __popc(m & ((1u << lane) - 1u));
+    if (take && pos < cap) list[pos] = key;
+}
+
+// Exclusive prefix sum of one int per thread over the block; *total gets
+// the sum.  s_warp: NT / 32 + 1 ints.  Starts and ends with __syncthreads().
+template <int NT>
+__device__ __forceinline__ int block_exclusive_scan1(int x, int* total, int* s_warp) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    int inc = x;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const int y = __shfl_up_sync(MARS_FULL_MASK, inc, off);
+        if (lane >= off) inc += y;
+    }
+    __syncthreads();
+    if (lane == 31) s_warp[warp] = inc;
+    __syncthreads();
+    int before = inc - x, sum = 0;
+#pragma unroll
+    for (int w = 0; w < NT / 32; ++w) {
+        if (w < warp) before += s_warp[w];
+        sum += s_warp[w];
+    }
+    *total = sum;
+    __syncthreads();
+    return before;
+}
+
 __host__ __device__ __forceinline__ int next_pow2(int x) {
     int p = 1;
     while (p < x) p <<= 1;
@@ -121,7 +195,9 @@ __device__ int block_select_topk(unsigned long long* cand, int M, int K, int* hi
             prefix |= (unsigned long long)bsel << shift;
             pmask |= (unsigned long long)(nb - 1) << shift;
             __syncthreads();
-            if (in_bucket <= 32 || shift == 0) break;
+            // stop once the keys to keep fit one warp's sort (K <= 32) or
+            // the bucket is down to 32 keys
+            if ((K <= 32 ? (K - need) + in_bucket <= 32 : in_bucket <= 32) || shift == 0) break;
         }
         // keep the keys at or above the selected prefix (K - need above the
         // bucket plus the bucket): gathered in the histogram's space, then
@@ -130,16 +206,21 @@ __device__ int block_select_topk(unsigned long long* cand, int M, int K, int* hi
         int* s_cnt = s_scan + kW + 3;
         if (threadIdx.x == 0) *s_cnt = 0;
         __syncthreads();
-        for (int i = threadIdx.x; i < M; i += NT) {
-            const unsigned long long k = cand[i];
-            if ((k & pmask) >= prefix) kept[atomicAdd(s_cnt, 1)] = k;
+        for (int i0 = 0; i0 < M; i0 += NT) {
+            const int i = i0 + threadIdx.x;
+            const unsigned long long k = i < M ? cand[i] : 0ull;
+            warp_append(i < M && (k & pmask) >= prefix, k, kept, s_cnt, 1024);
         }
         __syncthreads();
         M = *s_cnt;
         for (int i = threadIdx.x; i < M; i += NT) cand[i] = kept[i];
         __syncthreads();
     }
-    const int P = next_pow2(max(M, 2));
+    if (M <= 32) {
+        warp0_sort32_desc(cand, M);
+        return min(M, K);
+    }
+    const int P = next_pow2(M);
     for (int j = M + threadIdx.x; j < P; j += NT) cand[j] = 0ull;
     block_bitonic_desc<NT>(cand, P);
     return min(M, K);
@@ -162,30 +243,57 @@ __device__ int merge_ranked_lists(const float* __restrict__ vals, const int32_t*
                                   int nl, int K, unsigned long long* cand, int cap, int* hist,
                                   int* s_misc, unsigned long long* s_red) {
     constexpr int kWarps = NT / 32;
-    constexpr int kBatch = 16;
+    constexpr int kG = 4;                   // 16-byte groups per thread and batch
+    constexpr int kBatch = NT * kG * 4;     // entries per batch
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int total = nl * K;
-    int* s_cnt = s_misc + 15;
+    // 16-byte loads need 16-byte aligned arrays (the partial buffers are);
+    // otherwise every entry is read on its own
+    const bool vec = ((reinterpret_cast<uintptr_t>(vals) | reinterpret_cast<uintptr_t>(ids)) & 15u) == 0;
 
-    // the first batch goes to registers with every load in flight; when the
-    // whole input fits in it, the K-th entries (the bound) are among them
-    unsigned long long key[kBatch];
-    unsigned long long t = 0;
-    const bool one_batch = total <= NT * kBatch;
+    // one batch of entries in registers: group g holds entries 4g .. 4g+3
+    float4 v4[kG];
+    int4 i4[kG];
+    auto load_batch = [&](int b0) {
 #pragma unroll
-    for (int u = 0; u < kBatch; ++u) {
-        const int j = u * NT + threadIdx.x;
-        key[u] = 0ull;
-        if (j < total) {
-            const int32_t id = __ldcg(ids + j);
-            const float v = __ldcg(vals + j);
-            if (id != INT32_MAX) {
-                key[u] = rank_key(v, id);
-                if (one_batch && (j % K) == K - 1) t = key[u] > t ? key[u] : t;
+        for (int u = 0; u < kG; ++u) {
+            const int e = b0 + (u * NT + threadIdx.x) * 4;
+            v4[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+            i4[u] = make_int4(INT32_MAX, INT32_MAX, INT32_MAX, INT32_MAX);
+            if (vec && e + 3 < total) {
+                v4[u] = ld_cg_f4(reinterpret_cast<const float4*>(vals + e));
+                i4[u] = ld_cg_i4(reinterpret_cast<const int4*>(ids + e));
+            } else {
+                if (e + 0 < total) { v4[u].x = __ldcg(vals + e + 0); i4[u].x = __ldcg(ids + e + 0); }
+                if (e + 1 < total) { v4[u].y = __ldcg(vals + e + 1); i4[u].y = __ldcg(ids + e + 1); }
+                if (e + 2 < total) { v4[u].z = __ldcg(vals + e + 2); i4[u].z = __ldcg(ids + e + 2); }
+                if (e + 3 < total) { v4[u].w = __ldcg(vals + e + 3); i4[u].w = __ldcg(ids + e + 3); }
             }
         }
-    }
-    if (!one_batch) {
+    };
+    auto key_of = [&](int u, int c) -> unsigned long long {
+        const float v = c == 0 ? v4[u].x : c == 1 ? v4[u].y : c == 2 ? v4[u].z : v4[u].w;
+        const int32_t id = c == 0 ? i4[u].x : c == 1 ? i4[u].y : c == 2 ? i4[u].z : i4[u].w;
+        return id != INT32_MAX ? rank_key(v, id) : 0ull;
+    };
+
+    // the bound: the largest K-th entry over the lists (taken from the
+    // first batch when it holds everything)
+    unsigned long long t = 0;
+    load_batch(0);
+    if (total <= kBatch) {
+#pragma unroll
+        for (int u = 0; u < kG; ++u) {
+            const int e = (u * NT + threadIdx.x) * 4;
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if ((e + c) % K == K - 1) {
+                    const unsigned long long k = key_of(u, c);
+                    t = k > t ? k : t;
+                }
+            }
+        }
+    } else {
         for (int l = threadIdx.x; l < nl; l += NT) {
             const int32_t id = __ldcg(ids + (int64_t)l * K + K - 1);
             const float v = __ldcg(vals + (int64_t)l * K + K - 1);
@@ -196,37 +304,41 @@ __device__ int merge_ranked_lists(const float* __restrict__ vals, const int32_t*
         }
     }
     t = warp_max_u64(t);
-    if (threadIdx.x == 0) *s_cnt = 0;
     if (lane == 0) s_red[warp] = t;
     __syncthreads();
     t = s_red[0];
 #pragma unroll
     for (int w = 1; w < kWarps; ++w) t = s_red[w] > t ? s_red[w] : t;
 
-    // gather every valid entry ranked at or above the bound
-    for (int b0 = 0; b0 < total; b0 += NT * kBatch) {
-        if (b0 > 0) {
+    // gather every valid entry ranked at or above the bound: per-thread
+    // counts, one block prefix sum, then every thread writes its own
+    int n = 0;
+    for (int b0 = 0; b0 < total; b0 += kBatch) {
+        if (b0 > 0) load_batch(b0);
+        unsigned pass = 0u;
+        int mine = 0;
 #pragma unroll
-            for (int u = 0; u < kBatch; ++u) {
-                const int j = b0 + u * NT + threadIdx.x;
-                key[u] = 0ull;
-                if (j < total) {
-                    const int32_t id = __ldcg(ids + j);
-                    const float v = __ldcg(vals + j);
-                    if (id != INT32_MAX) key[u] = rank_key(v, id);
+        for (int u = 0; u < kG; ++u) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                const unsigned long long k = key_of(u, c);
+                if (k != 0ull && k >= t) { pass |= 1u << (u * 4 + c); ++mine; }
+            }
+        }
+        int batch_n = 0;
+        int pos = n + block_exclusive_scan1<NT>(mine, &batch_n, s_misc);
+#pragma unroll
+        for (int u = 0; u < kG; ++u) {
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+                if (pass & (1u << (u * 4 + c))) {
+                    if (pos < cap) cand[pos] = key_of(u, c);
+                    ++pos;
                 }
             }
         }
-#pragma unroll
-        for (int u = 0; u < kBatch; ++u) {
-            if (key[u] != 0ull && key[u] >= t) {
-                const int pos = atomicAdd(s_cnt, 1);
-                if (pos < cap) cand[pos] = key[u];
-            }
-        }
+        n += batch_n;
     }
-    __syncthreads();
-    const int n = *s_cnt;
     __syncthreads();
     if (n > cap) return -1;
     return block_select_topk<NT>(cand, n, K, hist, s_misc);
