@@ -179,7 +179,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) query_fused_kernel(const __gr
         __syncthreads();
         if (sm.misc[1] != 0) {
             if (threadIdx.x == 0) {
-                *a.ticket = 0u;
+                rearm(a);
                 p.out_cnt[1] = 0;
                 store_release_sys(p.out_cnt, -1);
             }
@@ -223,7 +223,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) query_fused_kernel(const __gr
     // that polls it sees every result (and the visited count) once it changes
     __syncthreads();
     if (threadIdx.x == 0) {
-        *a.ticket = 0u;   // re-arm for the next launch
+        rearm(a);
         p.out_cnt[1] = total;
         store_release_sys(p.out_cnt, cnt);
     }

@@ -57,6 +57,7 @@ struct ScanArgs {
     float*   part_val;                // gridDim.x * K
     int32_t* part_idx;
     unsigned int* ticket;
+    unsigned int* cursor;             // dynamic row hand-out (may be null: static split only)
     float*   out_val;                 // K
     int32_t* out_idx;
     int32_t* out_cnt;

@@ -7,7 +7,7 @@
 // library pointers it owns and forbids it from growing the footprint.  The
 // regular entry points need a store and a query context, and both allocate.
 // mars_scan_topk_noalloc takes the caller's own device arrays and keeps its
-// working memory (per-block partial lists and a completion counter) in the
+// working memory (per-block partial lists and two counters) in the
 // file-scope device array below, which exists once per GPU that loads the
 // library and lives until the process exits.
 //
@@ -16,7 +16,7 @@
 //    cudaGetSymbolAddress (and the device's SM count); make that first call
 //    before any stream capture on that device;
 //  * every call shares the one array and finds it as the previous call left
-//    it; the counter that must start at zero is cleared by each call;
+//    it; the counters that must start at zero are cleared by each call;
 //  * calls whose work overlaps on the GPU (two streams, or two host threads)
 //    race on the array: serialise them;
 //  * K <= 128 (MARS_NOALLOC_MAX_K); larger K is rejected.
@@ -38,7 +38,8 @@ constexpr int kNoallocMaxK = MARS_NOALLOC_MAX_K;
 struct NoallocScratch {
     unsigned int ticket;          // completion counter of the scan's blocks
     int32_t      n;               // row count read by the scan kernel
-    int32_t      pad[62];
+    unsigned int cursor;          // rows handed out dynamically by the scan
+    int32_t      pad[61];
     float        part_val[kNoallocMaxBlocks * kNoallocMaxK];
     int32_t      part_idx[kNoallocMaxBlocks * kNoallocMaxK];
     int32_t      count;           // used when the caller passes no d_count
@@ -50,6 +51,7 @@ static __device__ __align__(256) NoallocScratch g_noalloc_scratch;
 
 __global__ void noalloc_prepare_kernel(int32_t n) {
     g_noalloc_scratch.ticket = 0u;
+    g_noalloc_scratch.cursor = 0u;
     g_noalloc_scratch.n = n;
 }
 
@@ -132,6 +134,7 @@ extern "C" int mars_scan_topk_noalloc(const float* d_embeddings, int32_t row_pit
     sa.part_val = ds->scratch->part_val;
     sa.part_idx = ds->scratch->part_idx;
     sa.ticket = &ds->scratch->ticket;
+    sa.cursor = &ds->scratch->cursor;
     sa.out_val = d_vals;
     sa.out_idx = d_ids;
     sa.out_cnt = d_count ? d_count : &ds->scratch->count;

@@ -86,6 +86,7 @@ int enqueue_pipeline(const mars_store* s, mars_query_ctx* c, const MarsQueryDesc
     sa.part_val = c->d_part_val;
     sa.part_idx = c->d_part_idx;
     sa.ticket = c->d_ticket + 0;
+    sa.cursor = c->d_ticket + kTickets + 0;
     sa.out_val = c->d_seed_val;
     sa.out_idx = c->d_seed_idx;
     sa.out_cnt = c->d_seed_cnt;
@@ -170,6 +171,7 @@ int query_single_launch(const mars_store* s, mars_query_ctx* c, const float* que
     a.part_val = c->d_part_val;
     a.part_idx = c->d_part_idx;
     a.ticket = c->d_ticket + kFusedTicket;
+    a.cursor = c->d_ticket + kTickets + kFusedTicket;
     a.all_scores = cfg->bfs_max_hops > 0 ? c->d_all_scores : nullptr;
     a.stamp = c->d_stamp;
     p.out = c->dm_results;
@@ -274,7 +276,8 @@ int mars_query_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     T(cudaMalloc(&c->d_desc, c->desc_bytes), "desc");
     T(cudaMalloc(&c->d_part_val, (size_t)c->scan_blocks * MARS_MAX_TOP_K * sizeof(float)), "partials");
     T(cudaMalloc(&c->d_part_idx, (size_t)c->scan_blocks * MARS_MAX_TOP_K * sizeof(int32_t)), "partials");
-    T(cudaMalloc(&c->d_ticket, kTickets * sizeof(unsigned int)), "tickets");
+    // [0, kTickets) completion tickets, [kTickets, 2 kTickets) row counters
+    T(cudaMalloc(&c->d_ticket, 2 * kTickets * sizeof(unsigned int)), "tickets");
     T(cudaMalloc(&c->d_stamp, nmax * sizeof(unsigned long long)), "stamps");
     T(cudaMalloc(&c->d_vis_ids, nmax * sizeof(int32_t)), "visited");
     T(cudaMalloc(&c->d_vis_score, nmax * sizeof(float)), "visited");
@@ -296,7 +299,7 @@ int mars_query_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
           "mapped results");
     }
     if (rc == MARS_OK) {
-        T(cudaMemsetAsync(c->d_ticket, 0, kTickets * sizeof(unsigned int), c->stream), "memset");
+        T(cudaMemsetAsync(c->d_ticket, 0, 2 * kTickets * sizeof(unsigned int), c->stream), "memset");
         T(cudaMemsetAsync(c->d_stamp, 0, nmax * sizeof(unsigned long long), c->stream), "memset");
         T(cudaMemsetAsync(c->d_desc, 0, c->desc_bytes, c->stream), "memset");
         std::memset(c->h_desc, 0, c->desc_bytes);
@@ -528,6 +531,7 @@ int mars::scan_topk_excluding(const mars_store* s, mars_query_ctx* c, const floa
     sa.part_val = c->d_part_val;
     sa.part_idx = c->d_part_idx;
     sa.ticket = c->d_ticket + 3;
+    sa.cursor = c->d_ticket + kTickets + 3;
     sa.out_val = d_vals;
     sa.out_idx = d_ids;
     sa.out_cnt = d_count ? d_count : c->d_seed_cnt;
@@ -577,6 +581,7 @@ int mars_novelty(const mars_store* s, mars_query_ctx* c, const float* d_query, f
     sa.part_val = c->d_part_val;
     sa.part_idx = c->d_part_idx;
     sa.ticket = c->d_ticket + 5;
+    sa.cursor = c->d_ticket + kTickets + 5;
     sa.out_val = d_max;
     sa.out_idx = c->d_seed_idx;
     sa.out_cnt = c->d_seed_cnt;
@@ -605,6 +610,7 @@ int mars_debug_fused_scores(const mars_store* s, mars_query_ctx* c, const float*
     sa.part_val = c->d_part_val;
     sa.part_idx = c->d_part_idx;
     sa.ticket = c->d_ticket + 4;
+    sa.cursor = c->d_ticket + kTickets + 4;
     sa.out_val = c->d_seed_val;
     sa.out_idx = c->d_seed_idx;
     sa.out_cnt = c->d_seed_cnt;

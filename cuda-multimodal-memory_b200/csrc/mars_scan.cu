@@ -34,7 +34,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_topk_kernel(const ScanAr
     }
     if (threadIdx.x == 0) {
         *a.out_cnt = cnt;
-        *a.ticket = 0u;   // re-arm for the next launch
+        rearm(a);
     }
     if (a.vis_ids != nullptr) {
         // seed the BFS: level 0 = the top-K, stamp (epoch, level 0)

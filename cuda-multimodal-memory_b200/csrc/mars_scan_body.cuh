@@ -2,8 +2,9 @@
 // scan kernel (mars_scan.cu) and the single-launch query kernel
 // (mars_fastq.cu).
 //
-//  * each warp owns a contiguous range of rows (balanced to +-1 row) and
-//    streams them with 128-bit read-only loads, two rows in flight per warp;
+//  * each warp owns a contiguous range of the rows (balanced to +-1 row); for
+//    large row counts the last sixteenth is handed out from a counter; rows
+//    stream with 128-bit read-only loads, two rows in flight per warp;
 //  * the query lives in registers (lane l holds float4 chunks l, l+32, ...);
 //  * the row's fused score (src/memory_cuda.cu:292-310 applied to the
 //    similarity of :50-93) is formed in registers and offered to a
@@ -77,11 +78,24 @@ __device__ __forceinline__ bool scan_rows(const ScanArgs& a, const float4* __res
     WarpTopK<KPL> top;
     top.init(K);
 
-    // balanced contiguous row range of this warp
+    // Rows [0, n_st) are split statically: a balanced contiguous range per
+    // warp.  With at least 32 rows per warp, the last sixteenth, [n_st, n),
+    // is handed out from a counter in grabs of `grab` rows (even, 2..16,
+    // about a quarter of a warp's share of that part), so that warps on
+    // faster-served SMs take more of it and the CTAs finish together.  The
+    // order in which rows are offered does not change the result: the
+    // ranking is total.
     const int64_t W = (int64_t)gridDim.x * kScanWarps;
+    int32_t grab = 0, n_dyn = 0;
+    if (a.cursor != nullptr && (int64_t)n >= 32 * W) {
+        const int64_t gq = ((int64_t)(n >> 4) / (W * 4)) & ~1ll;
+        grab = (int32_t)(gq < 2 ? 2 : (gq > 16 ? 16 : gq));
+        n_dyn = ((n >> 4) / grab) * grab;
+    }
+    const int32_t n_st = n - n_dyn;
     const int64_t w = (int64_t)blockIdx.x * kScanWarps + warp;
-    const int32_t r0 = (int32_t)((int64_t)n * w / W);
-    const int32_t r1 = (int32_t)((int64_t)n * (w + 1) / W);
+    const int32_t r0 = (int32_t)((int64_t)n_st * w / W);
+    const int32_t r1 = (int32_t)((int64_t)n_st * (w + 1) / W);
 
     // metadata window: lane l holds row wbase + l
     int32_t wbase = r0;
@@ -97,12 +111,7 @@ __device__ __forceinline__ bool scan_rows(const ScanArgs& a, const float4* __res
     };
     load_meta(wbase);
 
-    auto process = [&](int32_t row, float dot) {
-        if (row - wbase >= 32) { wbase += 32; load_meta(wbase); }
-        const int src = row - wbase;
-        const float t = __shfl_sync(MARS_FULL_MASK, ts_w, src);
-        const float im = __shfl_sync(MARS_FULL_MASK, imp_w, src);
-        const int32_t m = __shfl_sync(MARS_FULL_MASK, mod_w, src);
+    auto offer = [&](int32_t row, float dot, float t, float im, int32_t m) {
         if ((filter >= 0 && m != filter) || row + 1 == d.exclude_plus1) {
             if (ALL && lane == 0) a.all_scores[row] = -FLT_MAX;
             return;
@@ -111,6 +120,14 @@ __device__ __forceinline__ bool scan_rows(const ScanArgs& a, const float4* __res
         if (use_imp) f = f * im;
         if (ALL && lane == 0) a.all_scores[row] = f;
         top.push(f, row + id_off, lane);
+    };
+    auto process = [&](int32_t row, float dot) {
+        if (row - wbase >= 32) { wbase += 32; load_meta(wbase); }
+        const int src = row - wbase;
+        const float t = __shfl_sync(MARS_FULL_MASK, ts_w, src);
+        const float im = __shfl_sync(MARS_FULL_MASK, imp_w, src);
+        const int32_t m = __shfl_sync(MARS_FULL_MASK, mod_w, src);
+        offer(row, dot, t, im, m);
     };
 
     const float4* __restrict__ E4 = reinterpret_cast<const float4*>(a.s.E);
@@ -150,6 +167,54 @@ __device__ __forceinline__ bool scan_rows(const ScanArgs& a, const float4* __res
         }
         process(r, warp_butterfly_sum(acc0));
     }
+    if (n_dyn > 0) {
+        // grabs of `grab` rows from the counter, scored two rows at a time;
+        // the next grab is requested while the current one is scored
+        int32_t g = 0;
+        if (lane == 0) g = (int32_t)atomicAdd(a.cursor, (unsigned)grab);
+        g = __shfl_sync(MARS_FULL_MASK, g, 0);
+        while (g < n_dyn) {
+            int32_t nxt = 0;
+            if (lane == 0) nxt = (int32_t)atomicAdd(a.cursor, (unsigned)grab);
+            for (int32_t pp = 0; pp < grab; pp += 2) {
+                // rr + 1 < n: n_dyn is a multiple of the even grab
+                const int32_t rr = n_st + g + pp;
+                float tm = 0.f, im = 1.f;
+                int32_t mm = 0;
+                if (lane < 2) {
+                    tm = __ldg(a.s.ts + rr + lane);
+                    if (use_imp) im = __ldg(a.s.imp + rr + lane);
+                    if (filter >= 0) mm = __ldg(a.s.mod + rr + lane);
+                }
+                const float4* p0 = E4 + (int64_t)rr * a.s.pitch4;
+                const float4* p1 = p0 + a.s.pitch4;
+                float4 e0[CPL], e1[CPL];
+#pragma unroll
+                for (int j = 0; j < CPL; ++j) {
+                    const int c = lane + 32 * j;
+                    if (c < nc) { e0[j] = ldg_stream(p0 + c); e1[j] = ldg_stream(p1 + c); }
+                }
+                float acc0 = 0.f, acc1 = 0.f;
+#pragma unroll
+                for (int j = 0; j < CPL; ++j) {
+                    const int c = lane + 32 * j;
+                    if (c < nc) { acc0 = fma4(e0[j], qv[j], acc0); acc1 = fma4(e1[j], qv[j], acc1); }
+                }
+#pragma unroll
+                for (int off = 16; off >= 1; off >>= 1) {
+                    const float x0 = __shfl_xor_sync(MARS_FULL_MASK, acc0, off);
+                    const float x1 = __shfl_xor_sync(MARS_FULL_MASK, acc1, off);
+                    acc0 = __fadd_rn(acc0, x0);
+                    acc1 = __fadd_rn(acc1, x1);
+                }
+                offer(rr, acc0, __shfl_sync(MARS_FULL_MASK, tm, 0), __shfl_sync(MARS_FULL_MASK, im, 0),
+                      __shfl_sync(MARS_FULL_MASK, mm, 0));
+                offer(rr + 1, acc1, __shfl_sync(MARS_FULL_MASK, tm, 1), __shfl_sync(MARS_FULL_MASK, im, 1),
+                      __shfl_sync(MARS_FULL_MASK, mm, 1));
+            }
+            g = __shfl_sync(MARS_FULL_MASK, nxt, 0);
+        }
+    }
     // per-row scores written by every warp are published before the ticket
     if (ALL) __threadfence();
 
@@ -172,6 +237,13 @@ __device__ __forceinline__ bool scan_rows(const ScanArgs& a, const float4* __res
     if (!sm.last) return false;
     __threadfence();
     return true;
+}
+
+// In the last CTA, once its reads of the shared counters are done: make the
+// ticket and the row counter ready for the next launch.
+__device__ __forceinline__ void rearm(const ScanArgs& a) {
+    *a.ticket = 0u;
+    if (a.cursor != nullptr) *a.cursor = 0u;
 }
 
 // In the last CTA: merge the gridDim.x partial lists into the top-K.  On
