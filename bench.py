@@ -612,20 +612,70 @@ def run_batch(a):
         dist.destroy_process_group()
 
 
+def _init_dist(local, world):
+    """NCCL process group for torchrun launches (None on one GPU)."""
+    if world <= 1:
+        return None
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    return dist
+
+
+def _sharded_graph(mb, st, N, deg, deg_cross, n_mod, rank, world, dist):
+    """cmng_build split by row blocks: rank r builds rows [r*N/G, (r+1)*N/G)
+    against the whole (replicated) store, then one NCCL all-gather of the
+    equal-sized padded blocks gives every rank the full N x deg graph.
+    Returns (graph, device ms of the build + gather, max over ranks)."""
+    import torch
+    lo, hi = N * rank // world, N * (rank + 1) // world
+    rows_max = (N + world - 1) // world
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+        torch.cuda.synchronize()
+    e0.record()
+    if world == 1:
+        nb = torch.empty((N, deg), dtype=torch.int32, device="cuda")
+        mb.cmng_build_rows(st, 0, N, deg, deg_cross, n_mod, nb)
+    else:
+        block = torch.full((rows_max, deg), -1, dtype=torch.int32, device="cuda")
+        mb.cmng_build_rows(st, lo, hi - lo, deg, deg_cross, n_mod, block)
+        allb = torch.empty((world * rows_max, deg), dtype=torch.int32, device="cuda")
+        dist.all_gather_into_tensor(allb, block)
+        nb = torch.cat([allb[r * rows_max: r * rows_max + (N * (r + 1) // world - N * r // world)]
+                        for r in range(world)])
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1)
+    if dist is not None:
+        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return nb, ms
+
+
 def run_knn_build(a):
     """c3: cmng_build of an exact out-degree-32 kNN graph.  N = 100,000 rows
     (100 isotropic Gaussian clusters, centres N(0,1), sigma 0.3, normalised),
     degree 32, no bridges.  A step is one full build (tensor-core kNN with
-    exact rescoring + neighbour selection), timed with CUDA events."""
+    exact rescoring + neighbour selection), device-timed.  Under torchrun
+    every rank holds the whole corpus and builds one row block; an NCCL
+    all-gather of the blocks completes the step (strong scaling)."""
     import torch
     import mars_b200 as mb
     import oracle as O
     from mars_b200 import datagen
 
+    rank, world, local = dist_env()
     N = a.n if a.n != 1_000_000 else 100_000
     D, deg = a.dim, 32
     E, mod, ts, _ = datagen.cluster_corpus(N, D, 100, 0.3, seed=a.seed, n_mod=4, ts_max=10.0)
     if a.impl == "reference":
+        if rank != 0:
+            return
         c = O.Corpus(E=E, ts=ts, mod=mod)
         rows = np.arange(0, N, max(1, N // 200), dtype=np.int32)
         t0 = time.perf_counter()
@@ -638,52 +688,72 @@ def run_knn_build(a):
                                            "kind": "port", "sample": f"exact kNN of {rows.shape[0]} rows "
                                            f"against all {N}, extrapolated x{N / rows.shape[0]:.0f}"}}))
         return
-    st = mb.Store(N, D)
+    torch.cuda.set_device(local)
+    dist = _init_dist(local, world)
+    st = mb.Store(N, D, device=local)
     st.upload(E, mod, ts)
-    nb = torch.empty((N, deg), dtype=torch.int32, device="cuda")
     for _ in range(max(1, a.warmup)):
-        mb.cmng_build(st, deg, 0, 4, nb)
-    times = [mb.cmng_build(st, deg, 0, 4, nb) for _ in range(a.steps)]
-    torch.cuda.synchronize()
-    # spot check against the exact oracle kNN
-    rows = np.arange(0, N, N // 64, dtype=np.int32)
-    rid, _ = O.knn(O.Corpus(E=E, ts=ts, mod=mod), rows, 2 * deg)
-    ref = O.cmng_select(rid, mod, rows, deg, 0, 4)
-    exact = bool(np.array_equal(nb.cpu().numpy()[rows], ref))
-    ms = statistics.median(times)
-    flops = 2.0 * N * N * D
-    peaks = {}
-    try:
-        peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-    except Exception:
-        pass
-    bf16 = float(peaks.get("bf16_tflops", 1590.0))
-    print(json.dumps({"workload": "c3", "metric": f"cmng_build ms (N={N}, D={D}, degree {deg})",
-                      "value": ms, "unit": "ms", "higher_is_better": False, "steps": a.steps,
-                      "tflops_effective": flops / (ms * 1e-3) / 1e12,
-                      "roofline": {"bound": "tensor", "flops_per_build": flops,
-                                   "frac_of_tf32_nominal": flops / (ms * 1e-3) / 1e12 / (bf16 / 2)},
-                      "spot_check_rows": int(rows.shape[0]), "neighbours_bit_exact": exact}),
-          flush=True)
+        nb, _ = _sharded_graph(mb, st, N, deg, 0, 4, rank, world, dist)
+    times = []
+    for _ in range(a.steps):
+        nb, ms = _sharded_graph(mb, st, N, deg, 0, 4, rank, world, dist)
+        times.append(ms)
+    if rank == 0:
+        # spot check of the gathered graph against the exact oracle kNN
+        rows = np.arange(0, N, N // 64, dtype=np.int32)
+        rid, _ = O.knn(O.Corpus(E=E, ts=ts, mod=mod), rows, 2 * deg)
+        ref = O.cmng_select(rid, mod, rows, deg, 0, 4)
+        exact = bool(np.array_equal(nb.cpu().numpy()[rows], ref))
+        ms = statistics.median(times)
+        flops = 2.0 * N * N * D
+        peaks = {}
+        try:
+            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        except Exception:
+            pass
+        bf16 = float(peaks.get("bf16_tflops", 1590.0))
+        print(json.dumps({"workload": "c3", "metric": f"cmng_build ms (N={N}, D={D}, degree {deg})",
+                          "value": ms, "unit": "ms", "higher_is_better": False, "n_gpus": world,
+                          "steps": a.steps, "scaling": "strong",
+                          "parallelism": f"row blocks x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+                          "tflops_effective": flops / (ms * 1e-3) / 1e12,
+                          "roofline": {"bound": "tensor", "flops_per_build": flops,
+                                       "frac_of_tf32_nominal_per_gpu":
+                                           flops / world / (ms * 1e-3) / 1e12 / (bf16 / 2)},
+                          "spot_check_rows": int(rows.shape[0]), "neighbours_bit_exact": exact}),
+              flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_cmng_bfs(a):
     """c4: cmng_search + cross-modal BFS.  N = 1,000,000 rows from a 1,000
     cluster mixture (sigma 0.3, 4 modalities, normalised); graph = degree-32
     kNN + 4 cross-modal bridges (degree 36, built once, untimed); 10,000
-    queries, beam 64, K = 10, lambda = 0.05, BFS depth 2."""
+    queries, beam 64, K = 10, lambda = 0.05, BFS depth 2.  Under torchrun:
+    replicas (every rank holds the corpus; the graph is built by row blocks
+    and all-gathered), the queries split across ranks, and an NCCL
+    all-gather of the per-rank results ends each step."""
     import torch
     import mars_b200 as mb
     import oracle as O
     from mars_b200 import datagen
 
+    rank, world, local = dist_env()
     N, D, deg, K, nq = a.n, a.dim, 36, 10, a.queries
+    if a.impl == "reference" and rank != 0:
+        return
+    torch.cuda.set_device(local)
     E, mod, ts, _ = datagen.cluster_corpus(N, D, 1000, 0.3, seed=a.seed, n_mod=4, ts_max=10.0)
     Q = datagen.queries(nq, D, seed=a.seed + 5)
-    st = mb.Store(N, D)
+    dist = _init_dist(local, world) if a.impl != "reference" else None
+    st = mb.Store(N, D, device=local)
     st.upload(E, mod, ts)
-    nb = torch.empty((N, deg), dtype=torch.int32, device="cuda")
-    build_ms = mb.cmng_build(st, deg, 4, 4, nb)
+    if a.impl == "reference":   # rank 0 alone: the graph is built locally
+        nb, build_ms = _sharded_graph(mb, st, N, deg, 4, 4, 0, 1, None)
+    else:
+        nb, build_ms = _sharded_graph(mb, st, N, deg, 4, 4, rank, world, dist)
     if a.impl == "reference":
         nbh = nb.cpu().numpy()
         c = O.Corpus(E=E, ts=ts, mod=mod, fixed_nbrs=nbh)
@@ -701,49 +771,75 @@ def run_cmng_bfs(a):
                           "cpu_baseline": {"value": v, "unit": "queries/s", "cores": 1, "kind": "port",
                                            "sample": f"{sample} queries, oracle beam search + BFS, 1 thread"}}))
         return
-    Qd = torch.from_numpy(Q).cuda()
+    q0, q1 = nq * rank // world, nq * (rank + 1) // world
+    nql = q1 - q0
+    qmax = (nq + world - 1) // world
+    Qd = torch.from_numpy(np.ascontiguousarray(Q[q0:q1])).cuda()
     cfg = mb.CmngConfig(K=K, beam_width=64, max_iterations=64, time_decay_lambda=0.05)
-    ctx = mb.CmngContext(nq, K, deg, 2, N)
-    ids = torch.empty((nq, K), dtype=torch.int32, device="cuda")
-    sc = torch.empty((nq, K), dtype=torch.float32, device="cuda")
-    cnt = torch.empty(nq, dtype=torch.int32, device="cuda")
-    vis = torch.empty(nq, dtype=torch.int32, device="cuda")
-    bits = torch.empty(nq, dtype=torch.int32, device="cuda")
-    bscored = torch.empty(nq, dtype=torch.int32, device="cuda")
+    ctx = mb.CmngContext(qmax, K, deg, 2, N, device=local)
+    ids = torch.full((qmax, K), -1, dtype=torch.int32, device="cuda")
+    sc = torch.zeros((qmax, K), dtype=torch.float32, device="cuda")
+    cnt = torch.zeros(qmax, dtype=torch.int32, device="cuda")
+    vis = torch.zeros(qmax, dtype=torch.int32, device="cuda")
+    bits = torch.zeros(qmax, dtype=torch.int32, device="cuda")
+    bscored = torch.zeros(qmax, dtype=torch.int32, device="cuda")
+    if world > 1:
+        all_ids = torch.empty((world * qmax, K), dtype=torch.int32, device="cuda")
+        all_sc = torch.empty((world * qmax, K), dtype=torch.float32, device="cuda")
     stream = torch.cuda.Stream()       # a real stream: NULL would mean the store's own stream
     torch.cuda.set_stream(stream)
-    for _ in range(max(1, a.warmup)):
-        ctx.search_bfs(st, nb, deg, Qd, nq, 10.0, cfg, 2, 0.5, ids, sc, cnt, d_visited=vis,
+
+    def step():
+        ctx.search_bfs(st, nb, deg, Qd, nql, 10.0, cfg, 2, 0.5, ids, sc, cnt, d_visited=vis,
                        stream=stream.cuda_stream)
+        if world > 1:
+            dist.all_gather_into_tensor(all_ids, ids)
+            dist.all_gather_into_tensor(all_sc, sc)
+
+    for _ in range(max(1, a.warmup)):
+        step()
     e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+        torch.cuda.synchronize()
     e0.record(stream)
     for _ in range(a.steps):
-        ctx.search_bfs(st, nb, deg, Qd, nq, 10.0, cfg, 2, 0.5, ids, sc, cnt, d_visited=vis,
-                       stream=stream.cuda_stream)
+        step()
     e1.record(stream)
     for _ in range(a.steps):
-        mb.cmng_search_batch(st, nb, deg, Qd, nq, 10.0, cfg, ids, sc, cnt, d_iters=bits,
+        mb.cmng_search_batch(st, nb, deg, Qd, nql, 10.0, cfg, ids, sc, cnt, d_iters=bits,
                              d_scored=bscored, stream=stream.cuda_stream)
     e2.record(stream)
     torch.cuda.synchronize()
     ms = e0.elapsed_time(e1) / a.steps
     ms_beam = e1.elapsed_time(e2) / a.steps
-    rows_bfs = float(vis.double().mean().item())
-    rows_beam = float(bscored.double().mean().item())
+    if world > 1:
+        t = torch.tensor([ms, ms_beam], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms, ms_beam = float(t[0].item()), float(t[1].item())
+    rows_bfs = float(vis[:nql].double().mean().item())
+    rows_beam = float(bscored[:nql].double().mean().item())
     # rows read per query: beam-scored rows + the BFS levels >= 1 (seeds are beam rows)
     bytes_q = (rows_beam + rows_bfs) * D * 4
     peak, _ = measured_peak()
-    achieved = bytes_q * nq / (ms * 1e-3) / 1e9
-    print(json.dumps({"workload": "c4", "metric": f"queries/s (cmng_search + BFS depth 2, N={N}, K={K})",
-                      "value": nq / (ms * 1e-3), "unit": "queries/s", "ms_per_batch": ms,
-                      "beam_only_queries_per_s": nq / (ms_beam * 1e-3), "graph_build_ms": build_ms,
-                      "mean_rows_scored_beam": rows_beam, "mean_nodes_visited_bfs": rows_bfs,
-                      "mean_iterations": float(bits.double().mean().item()),
-                      "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                                   "frac": achieved / peak,
-                                   "note": "row gathers: (beam-scored + BFS-visited rows) x D x 4 bytes"}}),
-          flush=True)
+    achieved = bytes_q * nql / (ms * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({"workload": "c4", "metric": f"queries/s (cmng_search + BFS depth 2, N={N}, K={K})",
+                          "value": nq / (ms * 1e-3), "unit": "queries/s", "n_gpus": world,
+                          "scaling": "strong", "ms_per_batch": ms,
+                          "parallelism": f"replicas x{world}, queries split" +
+                                         (" + NCCL all-gather of results" if world > 1 else ""),
+                          "beam_only_queries_per_s": nq / (ms_beam * 1e-3), "graph_build_ms": build_ms,
+                          "mean_rows_scored_beam": rows_beam, "mean_nodes_visited_bfs": rows_bfs,
+                          "mean_iterations": float(bits[:nql].double().mean().item()),
+                          "roofline": {"bound": "hbm", "achieved_per_gpu": achieved, "peak": peak,
+                                       "unit": "GB/s", "frac": achieved / peak,
+                                       "note": "row gathers: (beam-scored + BFS-visited rows) x D x 4 bytes"}}),
+              flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():

@@ -56,18 +56,21 @@ constexpr int kMaxDegree = 128;    // reference MAX_DEGREE (src/cmng_search.cu:2
 
 // ---------------------------------------------------------------------------
 // Neighbour selection with cross-modal bridges (src/cmng_build.cu:75-132).
+// Rows first .. first + count - 1; knn, knn_cnt and out are indexed from
+// the first of them.
 __global__ void select_kernel(const int32_t* __restrict__ knn, const int32_t* __restrict__ knn_cnt,
-                              int32_t k_init, const int32_t* __restrict__ mod, int32_t N, int32_t degree,
-                              int32_t degree_cross, int32_t num_modalities, int32_t* __restrict__ out) {
+                              int32_t k_init, const int32_t* __restrict__ mod, int32_t first, int32_t count,
+                              int32_t degree, int32_t degree_cross, int32_t num_modalities,
+                              int32_t* __restrict__ out) {
     const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
     const int lane = threadIdx.x & 31;
-    if (row >= N) return;
+    if (row >= count) return;
     const int32_t* kr = knn + row * k_init;
     const int32_t cnt = min(knn_cnt[row], k_init);
     int32_t* o = out + row * degree;
     const int32_t intra = degree - degree_cross;
     for (int j = lane; j < intra; j += 32) o[j] = j < cnt ? kr[j] : -1;
-    const int32_t my_mod = mod[row];
+    const int32_t my_mod = mod[first + row];
     int32_t b = intra;
     for (int32_t m = 0; m < num_modalities && b < degree; ++m) {
         if (m == my_mod) continue;
@@ -536,37 +539,50 @@ extern "C" {
 
 int mars_cmng_build(const mars_store* s, int32_t degree, int32_t degree_cross, int32_t num_modalities,
                     int32_t* d_neighbors, float* build_ms) {
+    if (s == nullptr) return fail(MARS_ERR_INVALID, "mars_cmng_build: NULL argument");
+    return mars_cmng_build_rows(s, 0, s->n, degree, degree_cross, num_modalities, d_neighbors, build_ms);
+}
+
+int mars_cmng_build_rows(const mars_store* s, int32_t first, int32_t count, int32_t degree,
+                         int32_t degree_cross, int32_t num_modalities, int32_t* d_neighbors,
+                         float* build_ms) {
     if (s == nullptr || d_neighbors == nullptr) return fail(MARS_ERR_INVALID, "mars_cmng_build: NULL argument");
     if (degree <= 0 || degree > kMaxDegree || degree_cross < 0 || degree_cross > degree || num_modalities < 0)
         return fail(MARS_ERR_INVALID, "mars_cmng_build: need 0 < degree <= 128, 0 <= degree_cross <= degree");
     const int32_t N = s->n;
     if (N < 2) return fail(MARS_ERR_INVALID, "mars_cmng_build: need at least 2 rows");
+    if (first < 0 || count < 0 || (int64_t)first + count > N)
+        return fail(MARS_ERR_INVALID, "mars_cmng_build_rows: rows outside the store");
+    if (build_ms) *build_ms = 0.f;
+    if (count == 0) return MARS_OK;
     const int32_t k_init = std::min(2 * degree, std::min(N - 1, (int32_t)MARS_MAX_TOP_K));
     MarsDeviceGuard g(s->device);
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     MARS_CUDA_TRY(cudaEventCreate(&e0));
     MARS_CUDA_TRY(cudaEventCreate(&e1));
-    const int32_t chunk = std::min(N, 4096);
+    const int32_t chunk = std::min(count, 4096);
     mars_batch_ctx* bc = nullptr;
     int rc = mars_batch_ctx_create(s->device, N, s->dim, chunk, k_init, &bc);
     int32_t* d_knn = nullptr;
     int32_t* d_cnt = nullptr;
     float* d_vals = nullptr;
     cudaStream_t st = s->stream;
-    if (rc == MARS_OK && (cudaMalloc(&d_knn, (size_t)N * k_init * 4) != cudaSuccess ||
-                          cudaMalloc(&d_vals, (size_t)N * k_init * 4) != cudaSuccess ||
-                          cudaMalloc(&d_cnt, (size_t)N * 4) != cudaSuccess))
+    if (rc == MARS_OK && (cudaMalloc(&d_knn, (size_t)count * k_init * 4) != cudaSuccess ||
+                          cudaMalloc(&d_vals, (size_t)count * k_init * 4) != cudaSuccess ||
+                          cudaMalloc(&d_cnt, (size_t)count * 4) != cudaSuccess))
         rc = fail(MARS_ERR_OOM, "mars_cmng_build: kNN buffers");
     if (rc == MARS_OK) cudaEventRecord(e0, st);
-    for (int32_t c0 = 0; rc == MARS_OK && c0 < N; c0 += chunk) {
-        const int32_t b = std::min(chunk, N - c0);
-        // rows as queries; plain dot products (lambda = 0: weight exactly 1)
+    for (int32_t c0 = first; rc == MARS_OK && c0 < first + count; c0 += chunk) {
+        const int32_t b = std::min(chunk, first + count - c0);
+        const size_t o = (size_t)(c0 - first);
+        // rows as queries, each leaving itself out; plain dot products
+        // (lambda = 0: weight exactly 1)
         rc = mars::batch_topk(s, bc, s->d_E + (size_t)c0 * s->pitch, s->pitch, b, 0.0f, 0.0f, -1, 0, k_init, 0,
-                              c0, d_knn + (size_t)c0 * k_init, d_vals + (size_t)c0 * k_init, d_cnt + c0, st);
+                              c0, d_knn + o * k_init, d_vals + o * k_init, d_cnt + o, st);
     }
     if (rc == MARS_OK) {
-        select_kernel<<<(unsigned)(((int64_t)N * 32 + 255) / 256), 256, 0, st>>>(
-            d_knn, d_cnt, k_init, s->d_mod, N, degree, degree_cross, num_modalities, d_neighbors);
+        select_kernel<<<(unsigned)(((int64_t)count * 32 + 255) / 256), 256, 0, st>>>(
+            d_knn, d_cnt, k_init, s->d_mod, first, count, degree, degree_cross, num_modalities, d_neighbors);
         if (cudaGetLastError() != cudaSuccess) rc = fail(MARS_ERR_CUDA, "mars_cmng_build: select launch");
     }
     if (rc == MARS_OK) {

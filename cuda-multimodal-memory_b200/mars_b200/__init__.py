@@ -130,6 +130,7 @@ _SIGS = {
                               _VP, _VP, _VP],
     "mars_batch_last_stats": [_VP, C.POINTER(BatchStats)],
     "mars_cmng_build": [_VP, _I32, _I32, _I32, _VP, C.POINTER(C.c_float)],
+    "mars_cmng_build_rows": [_VP, _I32, _I32, _I32, _I32, _I32, _VP, C.POINTER(C.c_float)],
     "mars_cmng_knn": [_VP, _I32, _VP, _VP, _VP],
     "mars_cmng_search_batch": [_VP, _VP, _I32, _VP, _I32, _I32, _F32, C.POINTER(CmngConfig), _VP,
                                _VP, _VP, _VP, _VP, _VP, _VP],
@@ -408,6 +409,15 @@ def cmng_build(store: Store, degree, degree_cross, num_modalities, d_neighbors) 
     ms = C.c_float()
     _check(lib().mars_cmng_build(store.handle, degree, degree_cross, num_modalities,
                                  _ptr(d_neighbors), C.byref(ms)))
+    return ms.value
+
+
+def cmng_build_rows(store: Store, first, count, degree, degree_cross, num_modalities,
+                    d_neighbors) -> float:
+    """Neighbour lists of rows first .. first+count-1 into d_neighbors (count x degree)."""
+    ms = C.c_float()
+    _check(lib().mars_cmng_build_rows(store.handle, first, count, degree, degree_cross, num_modalities,
+                                      _ptr(d_neighbors), C.byref(ms)))
     return ms.value
 
 

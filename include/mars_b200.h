@@ -305,6 +305,15 @@ typedef struct mars_cmng_config {
 int mars_cmng_build(const mars_store* s, int32_t degree, int32_t degree_cross,
                     int32_t num_modalities, int32_t* d_neighbors, float* build_ms);
 
+/* The same neighbour lists for rows first .. first + count - 1 only (each
+ * still searched against every row of the store), written to d_neighbors as
+ * count x degree.  Row blocks built on several GPUs that each hold the whole
+ * store, then gathered, equal mars_cmng_build: the N x N product of
+ * src/cmng_build.cu:203-246 split by row blocks. */
+int mars_cmng_build_rows(const mars_store* s, int32_t first, int32_t count, int32_t degree,
+                         int32_t degree_cross, int32_t num_modalities, int32_t* d_neighbors,
+                         float* build_ms);
+
 /* The exact k nearest other rows of every row (the kNN lists of the build):
  * d_ids / d_vals: N x k (dot desc, id asc), d_counts: N (may be NULL). */
 int mars_cmng_knn(const mars_store* s, int32_t k, int32_t* d_ids, float* d_vals,

@@ -76,6 +76,30 @@ def test_cmng_build_matches_oracle(torch_mod, clustered, degree, degree_cross, n
     assert np.array_equal(nb.cpu().numpy()[rows], ref)
 
 
+@pytest.mark.parametrize("world", [2, 3, 8])
+def test_row_block_builds_equal_the_whole_build(torch_mod, clustered, world):
+    """The sharded build: row blocks [r*N/G, (r+1)*N/G) built separately
+    (as G GPUs each holding the whole store would) and concatenated equal the
+    single build bit for bit."""
+    import mars_b200 as mb
+    torch = torch_mod
+    E, mod, ts = clustered
+    N, degree = E.shape[0], 36
+    st = _store(mb, E, mod, ts)
+    whole = torch.empty((N, degree), dtype=torch.int32, device="cuda")
+    mb.cmng_build(st, degree, 4, 4, whole)
+    parts = []
+    for r in range(world):
+        lo, hi = N * r // world, N * (r + 1) // world
+        part = torch.empty((hi - lo, degree), dtype=torch.int32, device="cuda")
+        mb.cmng_build_rows(st, lo, hi - lo, degree, 4, 4, part)
+        parts.append(part)
+    torch.cuda.synchronize()
+    assert torch.equal(torch.cat(parts), whole)
+    with pytest.raises(mb.MarsError):
+        mb.cmng_build_rows(st, N - 10, 11, degree, 4, 4, whole)
+
+
 def _graph(mb, torch, E, mod, ts, degree=32):
     st = _store(mb, E, mod, ts)
     nb = torch.empty((E.shape[0], degree), dtype=torch.int32, device="cuda")

@@ -106,3 +106,60 @@ def test_shards_union_equals_whole_corpus():
                  for r in range(world)]
         for k in range(4):
             assert np.array_equal(np.concatenate([p[k] for p in parts]), full[k])
+
+
+# ---------------------------------------------------------------------------
+# Row-block kNN-graph build (bench.py _sharded_graph): rank r builds rows
+# [r*N/G, (r+1)*N/G) against all rows, pads its block to ceil(N/G) rows and
+# all-gathers; trimming the padding reproduces the whole graph.
+NG, DG, DEG = 301, 32, 6
+
+
+def _graph_worker(rank, world, port, out_path):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "cuda-multimodal-memory_b200"))
+    sys.path.insert(0, os.path.join(root, "oracle"))
+    import oracle as O
+    from mars_b200 import datagen
+    E, mod, ts, _ = datagen.cluster_corpus(NG, DG, 7, 0.3, seed=4, n_mod=4, ts_max=10.0)
+    lo, hi = NG * rank // world, NG * (rank + 1) // world
+    rows_max = (NG + world - 1) // world
+    rows = np.arange(lo, hi, dtype=np.int32)
+    rid, _ = O.knn(O.Corpus(E=E, ts=ts, mod=mod), rows, 2 * DEG)
+    block = np.full((rows_max, DEG), -1, np.int32)
+    block[:hi - lo] = O.cmng_select(rid, mod, rows, DEG, 2, 4)
+    got = [torch.empty((rows_max, DEG), dtype=torch.int32) for _ in range(world)]
+    dist.all_gather(got, torch.from_numpy(block))
+    allb = torch.cat(got)
+    nb = torch.cat([allb[r * rows_max: r * rows_max + (NG * (r + 1) // world - NG * r // world)]
+                    for r in range(world)])
+    if rank == 0:
+        np.save(out_path, nb.numpy())
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_row_block_graph_equals_whole_graph(tmp_path, world):
+    out = str(tmp_path / "graph.npy")
+    mp.start_processes(_graph_worker, args=(world, _free_port(), out), nprocs=world, join=True,
+                       start_method="spawn")
+    got = np.load(out)
+    import oracle as O
+    from mars_b200 import datagen
+    E, mod, ts, _ = datagen.cluster_corpus(NG, DG, 7, 0.3, seed=4, n_mod=4, ts_max=10.0)
+    rows = np.arange(NG, dtype=np.int32)
+    rid, _ = O.knn(O.Corpus(E=E, ts=ts, mod=mod), rows, 2 * DEG)
+    assert np.array_equal(got, O.cmng_select(rid, mod, rows, DEG, 2, 4))
+
+
+def test_query_split_covers_every_query_once():
+    for nq in (1, 7, 10000, 10001):
+        for world in (1, 2, 3, 8):
+            seen = np.concatenate([np.arange(nq * r // world, nq * (r + 1) // world) for r in range(world)])
+            assert np.array_equal(seen, np.arange(nq))
+            assert max(nq * (r + 1) // world - nq * r // world for r in range(world)) <= (nq + world - 1) // world
