@@ -557,21 +557,46 @@ int mars_cmng_build_rows(const mars_store* s, int32_t first, int32_t count, int3
     if (count == 0) return MARS_OK;
     const int32_t k_init = std::min(2 * degree, std::min(N - 1, (int32_t)MARS_MAX_TOP_K));
     MarsDeviceGuard g(s->device);
+    const int32_t chunk = std::min(count, 4096);
+    // scratch kept on the store between builds (the store is used by one
+    // host thread at a time)
+    auto& bcache = const_cast<mars_store*>(s)->build;
+    int rc = MARS_OK;
+    if (bcache.bc == nullptr || bcache.bc_nodes < N || bcache.bc_chunk < chunk || bcache.bc_k < k_init) {
+        if (bcache.bc) mars_batch_ctx_destroy(bcache.bc);
+        bcache.bc = nullptr;
+        rc = mars_batch_ctx_create(s->device, N, s->dim, chunk, k_init, &bcache.bc);
+        if (rc != MARS_OK) return rc;
+        bcache.bc_nodes = N;
+        bcache.bc_chunk = chunk;
+        bcache.bc_k = k_init;
+    }
+    const size_t entries = (size_t)count * k_init;
+    if (bcache.entries < entries || bcache.rows < count) {
+        cudaFree(bcache.d_knn);
+        cudaFree(bcache.d_vals);
+        cudaFree(bcache.d_cnt);
+        bcache.d_knn = nullptr;
+        bcache.d_vals = nullptr;
+        bcache.d_cnt = nullptr;
+        bcache.entries = 0;
+        bcache.rows = 0;
+        if (cudaMalloc(&bcache.d_knn, entries * 4) != cudaSuccess ||
+            cudaMalloc(&bcache.d_vals, entries * 4) != cudaSuccess ||
+            cudaMalloc(&bcache.d_cnt, (size_t)count * 4) != cudaSuccess)
+            return fail(MARS_ERR_OOM, "mars_cmng_build: kNN buffers");
+        bcache.entries = entries;
+        bcache.rows = count;
+    }
+    int32_t* d_knn = bcache.d_knn;
+    int32_t* d_cnt = bcache.d_cnt;
+    float* d_vals = bcache.d_vals;
+    mars_batch_ctx* bc = bcache.bc;
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     MARS_CUDA_TRY(cudaEventCreate(&e0));
     MARS_CUDA_TRY(cudaEventCreate(&e1));
-    const int32_t chunk = std::min(count, 4096);
-    mars_batch_ctx* bc = nullptr;
-    int rc = mars_batch_ctx_create(s->device, N, s->dim, chunk, k_init, &bc);
-    int32_t* d_knn = nullptr;
-    int32_t* d_cnt = nullptr;
-    float* d_vals = nullptr;
     cudaStream_t st = s->stream;
-    if (rc == MARS_OK && (cudaMalloc(&d_knn, (size_t)count * k_init * 4) != cudaSuccess ||
-                          cudaMalloc(&d_vals, (size_t)count * k_init * 4) != cudaSuccess ||
-                          cudaMalloc(&d_cnt, (size_t)count * 4) != cudaSuccess))
-        rc = fail(MARS_ERR_OOM, "mars_cmng_build: kNN buffers");
-    if (rc == MARS_OK) cudaEventRecord(e0, st);
+    cudaEventRecord(e0, st);
     for (int32_t c0 = first; rc == MARS_OK && c0 < first + count; c0 += chunk) {
         const int32_t b = std::min(chunk, first + count - c0);
         const size_t o = (size_t)(c0 - first);
@@ -592,10 +617,6 @@ int mars_cmng_build_rows(const mars_store* s, int32_t first, int32_t count, int3
         cudaEventElapsedTime(&ms, e0, e1);
         if (build_ms) *build_ms = ms;
     }
-    cudaFree(d_knn);
-    cudaFree(d_vals);
-    cudaFree(d_cnt);
-    mars_batch_ctx_destroy(bc);
     cudaEventDestroy(e0);
     cudaEventDestroy(e1);
     return rc;

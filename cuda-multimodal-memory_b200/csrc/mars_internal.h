@@ -111,6 +111,19 @@ struct mars_store {
     };
     HostStage stage[2];
     int stage_next = 0;
+
+    // scratch of the kNN-graph build, kept between builds (freed with the
+    // store): the batched top-K context and the per-row candidate lists
+    struct BuildCache {
+        struct mars_batch_ctx* bc = nullptr;
+        int32_t bc_nodes = 0, bc_chunk = 0, bc_k = 0;
+        int32_t* d_knn = nullptr;
+        float* d_vals = nullptr;
+        int32_t* d_cnt = nullptr;
+        size_t entries = 0;           // capacity of d_knn / d_vals
+        int32_t rows = 0;             // capacity of d_cnt
+    };
+    BuildCache build;
 };
 
 // ---- query context (QueryContext) ----------------------------------------

@@ -106,6 +106,53 @@ __global__ void __launch_bounds__(kScanThreads) topk_merge_kernel(const int32_t*
     if (lane == 0 && cnt_out) *cnt_out = cnt;
 }
 
+// The same merge when all of a query's entries fit the key buffer
+// (n_lists * K <= kMergeKeys): every valid entry becomes a 64-bit rank key in
+// shared memory and the block's radix selection picks the top-K; no serial
+// inserts.
+__global__ void __launch_bounds__(kScanThreads) topk_merge_select_kernel(const int32_t* __restrict__ ids_in,
+                                                                         const float* __restrict__ vals_in,
+                                                                         int n_lists, int K, int Q,
+                                                                         int32_t* ids_out, float* vals_out,
+                                                                         int32_t* cnt_out) {
+    __shared__ unsigned long long s_keys[kMergeKeys];
+    __shared__ int s_hist[2048];
+    __shared__ int s_misc[16];
+    constexpr int kPer = kMergeKeys / kScanThreads;
+    const int qi = blockIdx.x;
+    const int total = n_lists * K;
+    if (threadIdx.x == 0) s_misc[15] = 0;
+    int32_t id[kPer];
+    float v[kPer];
+#pragma unroll
+    for (int u = 0; u < kPer; ++u) {
+        const int j = u * kScanThreads + threadIdx.x;
+        id[u] = -1;
+        if (j < total) {
+            const int l = j / K, e = j - l * K;
+            const int64_t p = ((int64_t)l * Q + qi) * K + e;
+            id[u] = __ldg(ids_in + p);
+            v[u] = __ldg(vals_in + p);
+        }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int u = 0; u < kPer; ++u)
+        warp_append(id[u] >= 0, id[u] >= 0 ? rank_key(v[u], id[u]) : 0ull, s_keys, &s_misc[15], kMergeKeys);
+    __syncthreads();
+    const int M = s_misc[15];
+    __syncthreads();
+    const int cnt = block_select_topk<kScanThreads>(s_keys, M, K, s_hist, s_misc);
+    ids_out += (int64_t)qi * K;
+    vals_out += (int64_t)qi * K;
+    for (int p = threadIdx.x; p < K; p += kScanThreads) {
+        const bool valid = p < cnt;
+        vals_out[p] = valid ? key_score(s_keys[p]) : -INFINITY;
+        ids_out[p] = valid ? key_id(s_keys[p]) : -1;
+    }
+    if (threadIdx.x == 0 && cnt_out) cnt_out[qi] = cnt;
+}
+
 // ---------------------------------------------------------------------------
 // Dispatch.  CPL: float4 chunks per lane (D = 128 * CPL covers 768 with 6).
 template <int KPL, bool ALL>
@@ -135,6 +182,10 @@ cudaError_t launch_scan_topk(const ScanArgs& a, int k_max, int grid, cudaStream_
 
 cudaError_t launch_topk_merge(const int32_t* ids_in, const float* vals_in, int n_lists, int K, int Q,
                               int32_t* ids_out, float* vals_out, int32_t* cnt, cudaStream_t st) {
+    if ((int64_t)n_lists * K <= kMergeKeys) {
+        topk_merge_select_kernel<<<Q, kScanThreads, 0, st>>>(ids_in, vals_in, n_lists, K, Q, ids_out, vals_out, cnt);
+        return cudaGetLastError();
+    }
     if (K <= 32)
         topk_merge_kernel<1><<<Q, kScanThreads, 0, st>>>(ids_in, vals_in, n_lists, K, Q, ids_out, vals_out, cnt);
     else if (K <= 64)

@@ -212,7 +212,8 @@ __device__ int block_select_topk(unsigned long long* cand, int M, int K, int* hi
             warp_append(i < M && (k & pmask) >= prefix, k, kept, s_cnt, 1024);
         }
         __syncthreads();
-        M = *s_cnt;
+        // (more than 1024 only if keys repeat; the copies beyond are dropped)
+        M = min(*s_cnt, 1024);
         for (int i = threadIdx.x; i < M; i += NT) cand[i] = kept[i];
         __syncthreads();
     }

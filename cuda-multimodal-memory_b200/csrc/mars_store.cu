@@ -132,6 +132,21 @@ __global__ void __launch_bounds__(kAppendWarps * 32) append_rows_kernel(const Ap
     }
 }
 
+// Tombstones (src/engine_server.cu:178-185): the row's embedding becomes
+// zero and its timestamp -1.  One warp per id; ids outside [0, n) are ignored.
+__global__ void delete_rows_kernel(float* __restrict__ E, int64_t pitch, float* __restrict__ ts,
+                                   const int32_t* __restrict__ ids, int32_t count, const int32_t* __restrict__ d_n,
+                                   int32_t dim) {
+    const int64_t w = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int lane = threadIdx.x & 31;
+    if (w >= count) return;
+    const int32_t u = ids[w];
+    if (u < 0 || u >= *d_n) return;
+    float* row = E + (int64_t)u * pitch;
+    for (int d = lane; d < dim; d += 32) row[d] = 0.0f;
+    if (lane == 0) ts[u] = -1.0f;
+}
+
 __global__ void fill_f32_kernel(float* p, int64_t n, float v) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i < n) p[i] = v;
@@ -218,6 +233,10 @@ static void release_store(mars_store* s) {
     cudaFree(s->d_norm_bits);
     cudaFree(s->d_extra);
     cudaFree(s->d_extra_cnt);
+    if (s->build.bc) mars_batch_ctx_destroy(s->build.bc);
+    cudaFree(s->build.d_knn);
+    cudaFree(s->build.d_vals);
+    cudaFree(s->build.d_cnt);
     for (auto& sg : s->stage) {
         if (sg.done) {
             cudaEventSynchronize(sg.done);
@@ -545,6 +564,39 @@ int mars_store_append_edges(mars_store* s, int32_t n, const int32_t* src, const 
     cudaFreeAsync(d_tmp, st);
     MARS_CUDA_TRY(cudaStreamSynchronize(st));
     if (rc != MARS_OK) { rollback(n); return rc; }
+    MARS_CUDA_TRY(cudaEventRecord(s->written, st));
+    return MARS_OK;
+}
+
+int mars_store_delete(mars_store* s, int32_t n, const int32_t* ids) {
+    if (s == nullptr || n < 0 || (n > 0 && ids == nullptr))
+        return fail(MARS_ERR_INVALID, "mars_store_delete: bad arguments");
+    if (!s->owns) return fail(MARS_ERR_INVALID, "mars_store_delete: store wraps caller memory");
+    if (n == 0) return MARS_OK;
+    MarsDeviceGuard g(s->device);
+    cudaStream_t st = s->stream;
+    int rc = MARS_OK;
+    mars_store::HostStage* sg = stage_acquire(s, (size_t)n * 4, &rc);
+    MARS_TRY(rc);
+    const int32_t* d_ids = nullptr;
+    int32_t* d_tmp = nullptr;
+    if (sg != nullptr) {
+        std::memcpy(sg->h, ids, (size_t)n * 4);
+        d_ids = reinterpret_cast<const int32_t*>(sg->d);
+    } else {
+        MARS_CUDA_TRY(cudaMallocAsync(&d_tmp, (size_t)n * 4, st));
+        MARS_CUDA_TRY(cudaMemcpyAsync(d_tmp, ids, (size_t)n * 4, cudaMemcpyHostToDevice, st));
+        d_ids = d_tmp;
+    }
+    delete_rows_kernel<<<(unsigned)(((int64_t)n * 32 + 255) / 256), 256, 0, st>>>(
+        s->d_E, (int64_t)s->pitch, s->d_ts, d_ids, n, s->d_n, s->dim);
+    MARS_CUDA_TRY(cudaGetLastError());
+    if (sg != nullptr) {
+        MARS_CUDA_TRY(cudaEventRecord(sg->done, st));
+    } else {
+        MARS_CUDA_TRY(cudaFreeAsync(d_tmp, st));
+        MARS_CUDA_TRY(cudaStreamSynchronize(st));   // the caller's ids were copied synchronously above
+    }
     MARS_CUDA_TRY(cudaEventRecord(s->written, st));
     return MARS_OK;
 }

@@ -103,6 +103,7 @@ _SIGS = {
     "mars_store_upload": [_VP, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _I32],
     "mars_store_append": [_VP, _I32, _VP, _VP, _VP, _VP, _I32, C.POINTER(_I32)],
     "mars_store_append_edges": [_VP, _I32, _VP, _VP],
+    "mars_store_delete": [_VP, _I32, _VP],
     "mars_store_set_importance": [_VP, _I32, _I32, _VP],
     "mars_store_info_get": [_VP, C.POINTER(StoreInfo)],
     "mars_importance_fill": [_VP, _F32],
@@ -240,6 +241,11 @@ class Store:
         src = _host(src, np.int32)
         dst = _host(dst, np.int32)
         _check(lib().mars_store_append_edges(self.handle, src.shape[0], _ptr(src), _ptr(dst)))
+
+    def delete(self, ids):
+        """Tombstone rows: zero embedding, timestamp -1 (engine_server DELETE)."""
+        a = _host(ids, np.int32)
+        _check(lib().mars_store_delete(self.handle, int(a.shape[0]), a.ctypes.data))
 
     def set_importance(self, first, importance):
         imp = importance if hasattr(importance, "data_ptr") else _host(importance, np.float32)

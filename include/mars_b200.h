@@ -131,6 +131,13 @@ int mars_store_append(mars_store* s, int32_t n, const float* embeddings,
                       const float* importance, int32_t normalize,
                       int32_t* first_id);
 
+/* Tombstone delete (engine_server DELETE, src/engine_server.cu:178-185):
+ * each listed row's embedding becomes zero and its timestamp -1, as the
+ * reference does; ids outside [0, N) are ignored.  ids: host array.  Like
+ * the reference, the row keeps its id and its edges (its fused score is 0,
+ * and a BFS can still reach it).  Asynchronous like mars_store_append. */
+int mars_store_delete(mars_store* s, int32_t n, const int32_t* ids);
+
 /* Append n directed edges src[i] -> dst[i] (host arrays) to the per-node
  * slack lists; MARS_ERR_CAPACITY if a node's slack is full (nothing is
  * written then).  Replaces the periodic NSN rebuild of

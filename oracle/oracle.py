@@ -139,6 +139,17 @@ class Corpus:
                 setattr(self, name, np.ascontiguousarray(v, dtype=np.int32))
         if self.D is None:
             self.D = self.E.shape[1]
+        # the C restatement indexes these arrays by row without checks
+        N = self.E.shape[0]
+        if self.row_offsets is not None:
+            if self.row_offsets.shape[0] != N + 1 or self.col_indices is None:
+                raise ValueError(f"row_offsets needs N + 1 = {N + 1} entries and col_indices")
+            if self.col_indices.shape[0] < int(self.row_offsets[-1]):
+                raise ValueError("col_indices shorter than row_offsets[-1]")
+        for name in ("ts", "mod", "imp", "extra_cnt", "fixed_nbrs", "extra_nbrs"):
+            v = getattr(self, name)
+            if v is not None and v.shape[0] != N:
+                raise ValueError(f"{name} needs {N} rows, has {v.shape[0]}")
 
     def struct(self) -> _Corpus:
         s = _Corpus()

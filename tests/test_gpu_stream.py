@@ -147,3 +147,75 @@ def test_sharded_scan_merge_equals_single(torch_mod, mb, shards):
     ref = O.fused_scores(O.Corpus(E=E, ts=ts, mod=mod, imp=imp), q, 600.0, 0.01,
                          use_importance=True)
     assert_topk_matches_scores(mids.cpu().numpy(), mvals.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("n_lists,K,Q", [(8, 100, 64), (2, 10, 5), (3, 256, 4), (40, 100, 3), (1, 1, 7)])
+def test_topk_merge_batch_against_numpy(torch_mod, mb, n_lists, K, Q):
+    """mars_topk_merge_batch on rank-major [n_lists][Q][K] ranked lists, with
+    tied scores, short lists (-1 padding) and, for 40 x 100 entries, more
+    entries than the one-CTA selection holds (the list-by-list path)."""
+    torch = torch_mod
+    rng = np.random.default_rng(n_lists * 1000 + K)
+    ids = np.full((n_lists, Q, K), -1, np.int32)
+    vals = np.full((n_lists, Q, K), -np.inf, np.float32)
+    for l in range(n_lists):
+        for q in range(Q):
+            n = K if (l + q) % 3 else K // 2            # some short lists
+            s = np.round(rng.standard_normal(n), 1).astype(np.float32)   # many ties
+            i = (rng.permutation(100000)[:n] * n_lists + l).astype(np.int32)   # unique across lists
+            o = np.lexsort((i, -s))
+            ids[l, q, :n], vals[l, q, :n] = i[o], s[o]
+    ctx = mb.QueryContext(16, 8, max_k=256)
+    di, dv = torch.from_numpy(ids).cuda(), torch.from_numpy(vals).cuda()
+    mi = torch.empty((Q, K), dtype=torch.int32, device="cuda")
+    mv = torch.empty((Q, K), dtype=torch.float32, device="cuda")
+    mc = torch.empty(Q, dtype=torch.int32, device="cuda")
+    ctx.topk_merge_batch(di, dv, n_lists, K, Q, mi, mv, mc)
+    torch.cuda.synchronize()
+    for q in range(Q):
+        valid = ids[:, q, :] >= 0
+        ai, av = ids[:, q, :][valid], vals[:, q, :][valid]
+        o = np.lexsort((ai, -av))[:K]
+        n = o.shape[0]
+        assert int(mc[q].item()) == n
+        assert np.array_equal(mi[q, :n].cpu().numpy(), ai[o])
+        assert np.array_equal(mv[q, :n].cpu().numpy(), av[o])
+        assert np.all(mi[q, n:].cpu().numpy() == -1)
+
+
+def test_tombstone_delete_matches_reference_rule(torch_mod, mb):
+    """mars_store_delete zeroes the row and sets its timestamp to -1 (the
+    reference's engine_server DELETE); queries then equal the oracle on a
+    corpus edited the same way, BFS included (edges stay)."""
+    from mars_b200 import datagen
+    E, mod, ts, imp = datagen.gaussian_corpus(3000, 768, seed=77, ts_max=10.0)
+    ro, ci = datagen.random_bridges(mod, 4, seed=78)
+    st = mb.Store(3200, 768, edge_slack=4)
+    st.upload(E, mod, ts, imp, ro, ci)
+    rows, m2, t2, w2 = datagen.gaussian_corpus(50, 768, seed=79, ts_max=10.0)
+    first = st.append(rows, m2, t2, w2, normalize=False)
+    E = np.concatenate([E, rows]); mod = np.concatenate([mod, m2])
+    ts = np.concatenate([ts, t2]); imp = np.concatenate([imp, w2])
+    ctx = mb.QueryContext(3200, 768, max_k=64)
+    q = E[first + 3] + E[17]                     # close to rows that get deleted
+    cfg = mb.RetrievalConfig(top_k=20, bfs_max_hops=1, time_decay_lambda=0.1, use_importance=True)
+    before = ctx.query(st, q, 10.0, cfg)
+    dead = np.array([17, first + 3, 5000, -1, int(before["node_id"][2])], np.int32)   # two ignored
+    st.delete(dead)
+    for u in dead:
+        if 0 <= u < E.shape[0]:
+            E[u] = 0.0
+            ts[u] = -1.0
+    got = ctx.query(st, q, 10.0, cfg)
+    ctx.set_fused(False)
+    got_pipe = ctx.query(st, q, 10.0, cfg)
+    assert got.tobytes() == got_pipe.tobytes()
+    # the oracle's CSR covers every row: appended rows have no edges
+    ro_all = np.concatenate([ro, np.full(E.shape[0] - (ro.shape[0] - 1), ro[-1], ro.dtype)])
+    oc = O.Corpus(E=E, ts=ts, mod=mod, imp=imp, row_offsets=ro_all, col_indices=ci)
+    ref = O.query(oc, q, 10.0, top_k=20, bfs_max_hops=1, lam=0.1, bfs_score_decay=0.5, use_importance=True)
+    assert_ranked_equivalent(got["node_id"], got["score"], ref["node_id"], ref["score"], got["hops"],
+                             ref["hops"], what="after delete")
+    Er, mr, tr, ir = st.read(0, E.shape[0])
+    assert np.array_equal(Er[17], np.zeros(768, np.float32)) and tr[17] == -1.0
+    assert np.array_equal(tr, ts)
