@@ -77,9 +77,10 @@ __global__ void __launch_bounds__(kScanThreads, 2) query_fused_kernel(const __gr
     const ScanArgs& a = p.a;
     const MarsQueryDesc& d = a.d;
     const float4* q = a.q != nullptr ? a.q : p.qbuf;
-    if (!scan_rows<KPL, CPL, ALL>(a, q, d.t_q, sm)) return;
+    const SlotOne sl{a};
+    if (!scan_rows<KPL, CPL, ALL>(a, sl, q, d.t_q, sm)) return;
 
-    int cnt = final_merge<KPL>(a, sm);
+    int cnt = final_merge<KPL>(a, sl, sm);
     const int K = d.K;
     const int32_t id_off = d.row_offset;
     int total = cnt;
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) query_fused_kernel(const __gr
         __syncthreads();
         if (sm.misc[1] != 0) {
             if (threadIdx.x == 0) {
-                rearm(a);
+                rearm(sl);
                 p.out_cnt[1] = 0;
                 store_release_sys(p.out_cnt, -1);
             }
@@ -223,7 +224,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) query_fused_kernel(const __gr
     // that polls it sees every result (and the visited count) once it changes
     __syncthreads();
     if (threadIdx.x == 0) {
-        rearm(a);
+        rearm(sl);
         p.out_cnt[1] = total;
         store_release_sys(p.out_cnt, cnt);
     }

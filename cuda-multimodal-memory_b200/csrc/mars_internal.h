@@ -150,6 +150,7 @@ struct mars_query_ctx {
     float* d_part_val = nullptr;    // scan_blocks * kMaxTopK
     int32_t* d_part_idx = nullptr;
     unsigned int* d_ticket = nullptr;   // [4] tickets for scan / bfs / finalize / merge
+    unsigned int* d_multi = nullptr;    // tickets + row counters of the multi-query scan
 
     // BFS scratch
     unsigned long long* d_stamp = nullptr;  // max_nodes

@@ -107,6 +107,8 @@ cudaError_t launch_scan_topk(const ScanArgs& a, int k_max, int grid, cudaStream_
 cudaError_t launch_bfs_hop(const BfsArgs& a, int hop, int grid, cudaStream_t st);
 cudaError_t launch_bfs_finalize(const BfsArgs& a, int last_level, int k_max, int grid,
                                 cudaStream_t st);
+cudaError_t launch_scan_multi(const ScanArgs& a, const float* Q, int64_t qpitch, int nq, int grid,
+                              cudaStream_t st);
 cudaError_t launch_query_fused(const FusedQueryArgs& p, int grid, cudaStream_t st);
 cudaError_t launch_topk_merge(const int32_t* ids_in, const float* vals_in, int n_lists, int K, int Q,
                               int32_t* ids_out, float* vals_out, int32_t* cnt, cudaStream_t st);

@@ -24,6 +24,7 @@ using namespace mars;
 namespace {
 
 constexpr int kTickets = 8;   // scan, hop, finalize, merge, spare
+constexpr int kMultiMax = 256; // queries per launch of the multi-query scan
 constexpr uint32_t kMaxEpoch = (1u << 28) - 1;
 
 StoreView make_view(const mars_store* s) {
@@ -278,6 +279,7 @@ int mars_query_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     T(cudaMalloc(&c->d_part_idx, (size_t)c->scan_blocks * MARS_MAX_TOP_K * sizeof(int32_t)), "partials");
     // [0, kTickets) completion tickets, [kTickets, 2 kTickets) row counters
     T(cudaMalloc(&c->d_ticket, 2 * kTickets * sizeof(unsigned int)), "tickets");
+    T(cudaMalloc(&c->d_multi, 2 * kMultiMax * sizeof(unsigned int)), "multi-query tickets");
     T(cudaMalloc(&c->d_stamp, nmax * sizeof(unsigned long long)), "stamps");
     T(cudaMalloc(&c->d_vis_ids, nmax * sizeof(int32_t)), "visited");
     T(cudaMalloc(&c->d_vis_score, nmax * sizeof(float)), "visited");
@@ -300,6 +302,7 @@ int mars_query_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     }
     if (rc == MARS_OK) {
         T(cudaMemsetAsync(c->d_ticket, 0, 2 * kTickets * sizeof(unsigned int), c->stream), "memset");
+        T(cudaMemsetAsync(c->d_multi, 0, 2 * kMultiMax * sizeof(unsigned int), c->stream), "memset");
         T(cudaMemsetAsync(c->d_stamp, 0, nmax * sizeof(unsigned long long), c->stream), "memset");
         T(cudaMemsetAsync(c->d_desc, 0, c->desc_bytes, c->stream), "memset");
         std::memset(c->h_desc, 0, c->desc_bytes);
@@ -323,6 +326,7 @@ int mars_query_ctx_destroy(mars_query_ctx* c) {
     cudaFree(c->d_part_val);
     cudaFree(c->d_part_idx);
     cudaFree(c->d_ticket);
+    cudaFree(c->d_multi);
     cudaFree(c->d_stamp);
     cudaFree(c->d_vis_ids);
     cudaFree(c->d_vis_score);
@@ -501,6 +505,49 @@ int mars_scan_topk(const mars_store* s, mars_query_ctx* c, const float* d_query,
 }
 
 }  // extern "C"
+
+extern "C" int mars_scan_topk_multi(const mars_store* s, mars_query_ctx* c, const float* d_queries,
+                                    int32_t query_pitch, int32_t nq, float t_q, float lambda,
+                                    int32_t modality_filter, int32_t use_importance, int32_t K,
+                                    int32_t row_offset, int32_t* d_ids, float* d_vals, int32_t* d_counts,
+                                    void* stream) {
+    MARS_TRY(check_store_ctx(s, c, "mars_scan_topk_multi"));
+    if (d_queries == nullptr || d_ids == nullptr || d_vals == nullptr || nq < 0)
+        return fail(MARS_ERR_INVALID, "mars_scan_topk_multi: NULL argument or nq < 0");
+    if ((reinterpret_cast<uintptr_t>(d_queries) & 15u) != 0 || query_pitch < s->pitch || (query_pitch & 3) != 0)
+        return fail(MARS_ERR_INVALID, "mars_scan_topk_multi: queries must be 16-byte aligned rows, pitch >= the store's");
+    if ((s->dim & 3) != 0)
+        return fail(MARS_ERR_UNSUPPORTED, "mars_scan_topk_multi: device queries need dim % 4 == 0");
+    MARS_TRY(check_cfg(c, K, 0, "mars_scan_topk_multi"));
+    if (nq == 0) return MARS_OK;
+    MarsDeviceGuard g(c->device);
+    cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
+    MARS_CUDA_TRY(cudaStreamWaitEvent(st, s->written, 0));
+    ScanArgs sa{};
+    sa.s = make_view(s);
+    sa.d.t_q = t_q;
+    sa.d.lambda = lambda;
+    sa.d.filter = modality_filter;
+    sa.d.use_imp = use_importance;
+    sa.d.K = K;
+    sa.d.row_offset = row_offset;
+    sa.dyn = nullptr;
+    sa.part_val = c->d_part_val;
+    sa.part_idx = c->d_part_idx;
+    sa.ticket = c->d_multi;
+    sa.cursor = c->d_multi + kMultiMax;
+    // the partial buffers hold MARS_MAX_TOP_K entries per CTA: that many
+    // entries' worth of queries per launch
+    const int32_t per = std::max(1, std::min(kMultiMax, (int)MARS_MAX_TOP_K / K));
+    for (int32_t q0 = 0; q0 < nq; q0 += per) {
+        const int32_t n = std::min(per, nq - q0);
+        sa.out_val = d_vals + (size_t)q0 * K;
+        sa.out_idx = d_ids + (size_t)q0 * K;
+        sa.out_cnt = d_counts ? d_counts + q0 : nullptr;
+        MARS_CUDA_TRY(launch_scan_multi(sa, d_queries + (size_t)q0 * query_pitch, query_pitch, n, c->scan_blocks, st));
+    }
+    return MARS_OK;
+}
 
 int mars::scan_topk_excluding(const mars_store* s, mars_query_ctx* c, const float* d_query, float t_q,
                               float lambda, int32_t modality_filter, int32_t use_importance, int32_t K,

@@ -21,10 +21,11 @@ template <int KPL, int CPL, bool ALL>
 __global__ void __launch_bounds__(kScanThreads, 2) scan_topk_kernel(const ScanArgs a) {
     __shared__ ScanShared sm;
     const MarsQueryDesc& d = a.d;
-    if (!scan_rows<KPL, CPL, ALL>(a, a.q, desc_tq(d, a.dyn), sm)) return;
+    const SlotOne sl{a};
+    if (!scan_rows<KPL, CPL, ALL>(a, sl, a.q, desc_tq(d, a.dyn), sm)) return;
 
     // ---- last CTA: merge every CTA's list ----------------------------------
-    const int cnt = final_merge<KPL>(a, sm);
+    const int cnt = final_merge<KPL>(a, sl, sm);
     const int K = d.K;
     const int32_t id_off = d.row_offset;
     for (int p = threadIdx.x; p < K; p += kScanThreads) {
@@ -34,7 +35,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_topk_kernel(const ScanAr
     }
     if (threadIdx.x == 0) {
         *a.out_cnt = cnt;
-        rearm(a);
+        rearm(sl);
     }
     if (a.vis_ids != nullptr) {
         // seed the BFS: level 0 = the top-K, stamp (epoch, level 0)
@@ -53,6 +54,35 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_topk_kernel(const ScanAr
             a.lvl[1] = cnt;
             a.lvl[16] = cnt;
         }
+    }
+}
+
+// ---------------------------------------------------------------------------
+// Several queries' scans in one launch: a 2-D grid, blockIdx.y = query.  The
+// block scheduler starts query i + 1's CTAs as query i's finish, so the last
+// CTA of query i merges while the others already stream the next query, and
+// there is one launch instead of nq.  Each query has its own slot (partial
+// lists, ticket, row counter); query i's results are those of a
+// scan_topk_kernel launch for it alone.
+template <int KPL, int CPL>
+__global__ void __launch_bounds__(kScanThreads, 2) scan_multi_kernel(const __grid_constant__ ScanArgs a,
+                                                                      const float* __restrict__ Q,
+                                                                      int64_t qpitch) {
+    __shared__ ScanShared sm;
+    const int qi = blockIdx.y;
+    const SlotMulti sl{a, qi};
+    const float4* q = reinterpret_cast<const float4*>(Q + qi * qpitch);
+    if (!scan_rows<KPL, CPL, false>(a, sl, q, a.d.t_q, sm)) return;
+    const int K = a.d.K;
+    const int cnt = final_merge<KPL>(a, sl, sm);
+    for (int p = threadIdx.x; p < K; p += kScanThreads) {
+        const bool valid = p < cnt;
+        a.out_val[(int64_t)qi * K + p] = valid ? key_score(sm.keys()[p]) : -INFINITY;
+        a.out_idx[(int64_t)qi * K + p] = valid ? key_id(sm.keys()[p]) : -1;
+    }
+    if (threadIdx.x == 0) {
+        if (a.out_cnt != nullptr) a.out_cnt[qi] = cnt;
+        rearm(sl);
     }
 }
 
@@ -178,6 +208,32 @@ cudaError_t launch_scan_topk(const ScanArgs& a, int k_max, int grid, cudaStream_
     if (k_max <= 64) return all ? launch_scan_kpl<2, true>(a, grid, st) : launch_scan_kpl<2, false>(a, grid, st);
     if (k_max <= 128) return all ? launch_scan_kpl<4, true>(a, grid, st) : launch_scan_kpl<4, false>(a, grid, st);
     return all ? launch_scan_kpl<8, true>(a, grid, st) : launch_scan_kpl<8, false>(a, grid, st);
+}
+
+template <int KPL>
+static cudaError_t launch_multi_kpl(const ScanArgs& a, const float* Q, int64_t qpitch, int nq, int grid,
+                                    cudaStream_t st) {
+    switch ((a.s.nc + 31) / 32) {
+    case 1: scan_multi_kernel<KPL, 1><<<dim3(grid, nq), kScanThreads, 0, st>>>(a, Q, qpitch); break;
+    case 2: scan_multi_kernel<KPL, 2><<<dim3(grid, nq), kScanThreads, 0, st>>>(a, Q, qpitch); break;
+    case 3: scan_multi_kernel<KPL, 3><<<dim3(grid, nq), kScanThreads, 0, st>>>(a, Q, qpitch); break;
+    case 4: scan_multi_kernel<KPL, 4><<<dim3(grid, nq), kScanThreads, 0, st>>>(a, Q, qpitch); break;
+    case 5: scan_multi_kernel<KPL, 5><<<dim3(grid, nq), kScanThreads, 0, st>>>(a, Q, qpitch); break;
+    case 6: scan_multi_kernel<KPL, 6><<<dim3(grid, nq), kScanThreads, 0, st>>>(a, Q, qpitch); break;
+    case 7: scan_multi_kernel<KPL, 7><<<dim3(grid, nq), kScanThreads, 0, st>>>(a, Q, qpitch); break;
+    case 8: scan_multi_kernel<KPL, 8><<<dim3(grid, nq), kScanThreads, 0, st>>>(a, Q, qpitch); break;
+    default: return cudaErrorInvalidValue;
+    }
+    return cudaGetLastError();
+}
+
+cudaError_t launch_scan_multi(const ScanArgs& a, const float* Q, int64_t qpitch, int nq, int grid,
+                              cudaStream_t st) {
+    const int K = a.d.K;
+    if (K <= 32) return launch_multi_kpl<1>(a, Q, qpitch, nq, grid, st);
+    if (K <= 64) return launch_multi_kpl<2>(a, Q, qpitch, nq, grid, st);
+    if (K <= 128) return launch_multi_kpl<4>(a, Q, qpitch, nq, grid, st);
+    return launch_multi_kpl<8>(a, Q, qpitch, nq, grid, st);
 }
 
 cudaError_t launch_topk_merge(const int32_t* ids_in, const float* vals_in, int n_lists, int K, int Q,

@@ -50,12 +50,33 @@ struct ScanShared {
 static_assert(2 * kScanWarps * kMaxTopK * 4 <= 2048 * 8, "warp lists must fit their region");
 static_assert(2048 * 8 + 2 * kStageEntries * 4 <= 5120 * 8, "staging must fit its region");
 
+// Where one query's per-CTA lists, completion ticket and row counter live.
+// The addresses are formed on use from the launch's parameters (and, for the
+// multi-query kernel, the query's index), so no pointer stays in a register
+// across the row loop.
+struct SlotOne {     // one query per launch
+    const ScanArgs& a;
+    __device__ float* part_val() const { return a.part_val; }
+    __device__ int32_t* part_idx() const { return a.part_idx; }
+    __device__ unsigned int* ticket() const { return a.ticket; }
+    __device__ unsigned int* cursor() const { return a.cursor; }
+};
+struct SlotMulti {   // query qi of a multi-query launch (gridDim.x CTAs per query)
+    const ScanArgs& a;
+    int qi;
+    __device__ int64_t off() const { return (int64_t)qi * gridDim.x * a.d.K; }
+    __device__ float* part_val() const { return a.part_val + off(); }
+    __device__ int32_t* part_idx() const { return a.part_idx + off(); }
+    __device__ unsigned int* ticket() const { return a.ticket + qi; }
+    __device__ unsigned int* cursor() const { return a.cursor != nullptr ? a.cursor + qi : nullptr; }
+};
+
 // Stream this CTA's rows and leave the CTA's ranked list in the partial
 // buffer.  Returns true in the last CTA to finish (all partial lists and,
 // with ALL, all per-row scores are then visible to it).
-template <int KPL, int CPL, bool ALL>
-__device__ __forceinline__ bool scan_rows(const ScanArgs& a, const float4* __restrict__ q, float t_q,
-                                          ScanShared& sm) {
+template <int KPL, int CPL, bool ALL, class Slot>
+__device__ __forceinline__ bool scan_rows(const ScanArgs& a, const Slot& sl, const float4* __restrict__ q,
+                                          float t_q, ScanShared& sm) {
     const int lane = threadIdx.x & 31;
     const int warp = threadIdx.x >> 5;
     const MarsQueryDesc& d = a.d;
@@ -87,7 +108,7 @@ __device__ __forceinline__ bool scan_rows(const ScanArgs& a, const float4* __res
     // ranking is total.
     const int64_t W = (int64_t)gridDim.x * kScanWarps;
     int32_t grab = 0, n_dyn = 0;
-    if (a.cursor != nullptr && (int64_t)n >= 32 * W) {
+    if (sl.cursor() != nullptr && (int64_t)n >= 32 * W) {
         const int64_t gq = ((int64_t)(n >> 4) / (W * 4)) & ~1ll;
         grab = (int32_t)(gq < 2 ? 2 : (gq > 16 ? 16 : gq));
         n_dyn = ((n >> 4) / grab) * grab;
@@ -171,11 +192,11 @@ __device__ __forceinline__ bool scan_rows(const ScanArgs& a, const float4* __res
         // grabs of `grab` rows from the counter, scored two rows at a time;
         // the next grab is requested while the current one is scored
         int32_t g = 0;
-        if (lane == 0) g = (int32_t)atomicAdd(a.cursor, (unsigned)grab);
+        if (lane == 0) g = (int32_t)atomicAdd(sl.cursor(), (unsigned)grab);
         g = __shfl_sync(MARS_FULL_MASK, g, 0);
         while (g < n_dyn) {
             int32_t nxt = 0;
-            if (lane == 0) nxt = (int32_t)atomicAdd(a.cursor, (unsigned)grab);
+            if (lane == 0) nxt = (int32_t)atomicAdd(sl.cursor(), (unsigned)grab);
             for (int32_t pp = 0; pp < grab; pp += 2) {
                 // rr + 1 < n: n_dyn is a multiple of the even grab
                 const int32_t rr = n_st + g + pp;
@@ -227,10 +248,10 @@ __device__ __forceinline__ bool scan_rows(const ScanArgs& a, const float4* __res
         } else {
             for (int ww = 1; ww < kScanWarps; ++ww) top.offer_sorted(sm.warp_val(ww), sm.warp_idx(ww), K, lane);
         }
-        top.store(a.part_val + (int64_t)blockIdx.x * K, a.part_idx + (int64_t)blockIdx.x * K, lane);
+        top.store(sl.part_val() + (int64_t)blockIdx.x * K, sl.part_idx() + (int64_t)blockIdx.x * K, lane);
         __threadfence();
         __syncwarp();
-        if (lane == 0) sm.last = atomicAdd(a.ticket, 1u) == gridDim.x - 1;
+        if (lane == 0) sm.last = atomicAdd(sl.ticket(), 1u) == gridDim.x - 1;
         __syncwarp();
     }
     __syncthreads();
@@ -241,19 +262,20 @@ __device__ __forceinline__ bool scan_rows(const ScanArgs& a, const float4* __res
 
 // In the last CTA, once its reads of the shared counters are done: make the
 // ticket and the row counter ready for the next launch.
-__device__ __forceinline__ void rearm(const ScanArgs& a) {
-    *a.ticket = 0u;
-    if (a.cursor != nullptr) *a.cursor = 0u;
+template <class Slot>
+__device__ __forceinline__ void rearm(const Slot& sl) {
+    *sl.ticket() = 0u;
+    if (sl.cursor() != nullptr) *sl.cursor() = 0u;
 }
 
 // In the last CTA: merge the gridDim.x partial lists into the top-K.  On
 // return (all threads) sm.keys()[0, cnt) holds it in rank order as
 // rank_key() keys; returns cnt.
-template <int KPL>
-__device__ __forceinline__ int final_merge(const ScanArgs& a, ScanShared& sm) {
+template <int KPL, class Slot>
+__device__ __forceinline__ int final_merge(const ScanArgs& a, const Slot& sl, ScanShared& sm) {
     const int K = a.d.K;
     const int nl = (int)gridDim.x;
-    int cnt = merge_ranked_lists<kScanThreads>(a.part_val, a.part_idx, nl, K, sm.keys(), kMergeKeys, sm.hist(),
+    int cnt = merge_ranked_lists<kScanThreads>(sl.part_val(), sl.part_idx(), nl, K, sm.keys(), kMergeKeys, sm.hist(),
                                                sm.misc, sm.red);
     if (cnt >= 0) return cnt;
 
@@ -269,8 +291,8 @@ __device__ __forceinline__ int final_merge(const ScanArgs& a, ScanShared& sm) {
     for (int b0 = 0; b0 < nl; b0 += lists_per_batch) {
         const int nb = min(lists_per_batch, nl - b0);
         const int ne = nb * K;
-        const float* pv = a.part_val + (int64_t)b0 * K;
-        const int32_t* pi = a.part_idx + (int64_t)b0 * K;
+        const float* pv = sl.part_val() + (int64_t)b0 * K;
+        const int32_t* pi = sl.part_idx() + (int64_t)b0 * K;
         float rv[kPer];
         int32_t ri[kPer];
 #pragma unroll

@@ -122,6 +122,8 @@ _SIGS = {
     "mars_query_once": [_VP, _VP, _F32, C.POINTER(RetrievalConfig), _VP, C.POINTER(_I32),
                         C.POINTER(RetrievalStats)],
     "mars_scan_topk": [_VP, _VP, _VP, _F32, _F32, _I32, _I32, _I32, _I32, _VP, _VP, _VP, _VP],
+    "mars_scan_topk_multi": [_VP, _VP, _VP, _I32, _I32, _F32, _F32, _I32, _I32, _I32, _I32, _VP, _VP, _VP,
+                             _VP],
     "mars_topk_merge": [_VP, _VP, _VP, _I32, _I32, _VP, _VP, _VP, _VP],
     "mars_topk_merge_batch": [_VP, _VP, _VP, _I32, _I32, _I32, _VP, _VP, _VP, _VP],
     "mars_debug_fused_scores": [_VP, _VP, _VP, _F32, _F32, _I32, _I32, _VP, _VP],
@@ -343,6 +345,15 @@ class QueryContext:
         _check(lib().mars_scan_topk(store.handle, self.handle, _ptr(d_query), float(t_q),
                                     float(lam), modality_filter, int(use_importance), K,
                                     row_offset, _ptr(d_ids), _ptr(d_vals), _ptr(d_count), stream))
+
+    def scan_topk_multi(self, store: Store, d_queries, nq, t_q, lam, K, d_ids, d_vals, d_counts=None,
+                        modality_filter=-1, use_importance=False, row_offset=0, stream=None, query_pitch=None):
+        """nq fused scans in one launch; d_queries: [nq][pitch] float32 on the device."""
+        pitch = query_pitch if query_pitch is not None else (d_queries.stride(0) if hasattr(d_queries, "stride")
+                                                             else store.dim)
+        _check(lib().mars_scan_topk_multi(store.handle, self.handle, _ptr(d_queries), int(pitch), int(nq),
+                                          float(t_q), float(lam), modality_filter, int(use_importance), K,
+                                          row_offset, _ptr(d_ids), _ptr(d_vals), _ptr(d_counts), stream))
 
     def topk_merge(self, d_ids_in, d_vals_in, n_lists, K, d_ids_out, d_vals_out, d_count=None,
                    stream=None):

@@ -227,6 +227,21 @@ int mars_scan_topk(const mars_store* s, mars_query_ctx* ctx,
                    int32_t row_offset, int32_t* d_ids, float* d_vals,
                    int32_t* d_count, void* stream);
 
+/* nq queries of mars_scan_topk in one launch (results identical to nq
+ * separate calls).  d_queries: nq rows of query_pitch floats on the device
+ * (16-byte aligned, pitch >= the store's row pitch); d_ids / d_vals:
+ * nq x K, d_counts: nq (may be NULL).  The queries are the rows of one 2-D
+ * grid: while the last CTA of one query merges its partial lists, the CTAs
+ * of the next query already stream, so the per-query selection tail and the
+ * launch gaps overlap with streaming.  Every query still reads every row.
+ * The reference answers one query per pipeline (src/memory_cuda.cu:924-1067);
+ * this entry point has no counterpart there. */
+int mars_scan_topk_multi(const mars_store* s, mars_query_ctx* ctx, const float* d_queries,
+                         int32_t query_pitch, int32_t nq, float query_timestamp, float lambda,
+                         int32_t modality_filter, int32_t use_importance, int32_t K,
+                         int32_t row_offset, int32_t* d_ids, float* d_vals, int32_t* d_counts,
+                         void* stream);
+
 /* Merge `n_lists` ranked lists of K (id, score) pairs that sit back to back
  * in device memory (e.g. the gather buffer of an all-gather of per-shard
  * mars_scan_topk results) into one ranked list of K.  Ties by id. */

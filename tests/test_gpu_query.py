@@ -251,3 +251,32 @@ def test_errors_are_reported_not_fatal(torch_mod, mb):
     # still usable afterwards
     r = ctx.query(st, E[0], 1.0, mb.RetrievalConfig(top_k=4, bfs_max_hops=0))
     assert r["node_id"][0] == 0
+
+
+@pytest.mark.parametrize("N,K,nq", [(100003, 10, 16), (5000, 64, 9), (77, 100, 3), (250000, 1, 40)])
+def test_scan_topk_multi_equals_single_scans(torch_mod, mb, N, K, nq):
+    """mars_scan_topk_multi: the queries of one launch give exactly the
+    results of separate mars_scan_topk calls (ids, score bits, counts)."""
+    torch = torch_mod
+    from mars_b200 import datagen
+    D = 768
+    E, mod, ts, imp = datagen.gaussian_corpus(N, D, seed=N % 97, ts_max=10.0)
+    st = mb.Store(N, D)
+    st.upload(E, mod, ts, imp)
+    ctx = mb.QueryContext(N, D, max_k=max(K, 10))
+    Q = torch.from_numpy(datagen.queries(nq, D, seed=K)).cuda()
+    ids = torch.empty((nq, K), dtype=torch.int32, device="cuda")
+    vals = torch.empty((nq, K), dtype=torch.float32, device="cuda")
+    cnt = torch.empty(nq, dtype=torch.int32, device="cuda")
+    for rep in range(2):   # tickets and counters re-armed between launches
+        ctx.scan_topk_multi(st, Q, nq, 10.0, 0.3, K, ids, vals, cnt, use_importance=True, row_offset=7)
+        torch.cuda.synchronize()
+        for i in range(nq):
+            i1 = torch.empty(K, dtype=torch.int32, device="cuda")
+            v1 = torch.empty(K, dtype=torch.float32, device="cuda")
+            c1 = torch.empty(1, dtype=torch.int32, device="cuda")
+            ctx.scan_topk(st, Q[i], 10.0, 0.3, K, i1, v1, c1, use_importance=True, row_offset=7)
+            torch.cuda.synchronize()
+            assert int(cnt[i].item()) == int(c1.item())
+            assert np.array_equal(ids[i].cpu().numpy(), i1.cpu().numpy()), (rep, i)
+            assert np.array_equal(vals[i].cpu().numpy().view(np.uint32), v1.cpu().numpy().view(np.uint32))
