@@ -35,6 +35,7 @@
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
 
 #include <algorithm>
 #include <cmath>
@@ -63,6 +64,7 @@ constexpr int kThreads = 192;
 constexpr int kTmemCols = 512;
 constexpr int kJ = 16;                // sampled lower bounds kept per (query, tile)
 constexpr float kMarginRel = 2.6e-3f;
+constexpr float kF16Max = 60000.0f;   // |component| bound for the fp16 operands
 
 enum Mode { kSample = 0, kCandidates = 1 };
 
@@ -93,10 +95,15 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int t, int mode, 
     }
 }
 
-template <int MODE>
+// F16: operands are fp16 copies of the queries and rows (kind::f16, 64
+// elements per 128-byte row of a stage); otherwise fp32 read as TF32
+// (kind::tf32, 32 elements).  Both keep 10 mantissa bits; the stage layout in
+// bytes is the same.
+template <int MODE, bool F16>
 __global__ void __launch_bounds__(kThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_e,
             const GemmArgs a) {
+    constexpr int kElemsK = F16 ? 64 : 32;      // elements per 128-byte k-block
     extern __shared__ uint8_t smem_raw[];
     uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
@@ -139,8 +146,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                     if (!sm100::mbar_wait(empty + stage, phase ^ 1u, a.err, 1)) { ok = false; break; }
                     uint8_t* sa = smem + stage * kStageBytes;
                     sm100::mbar_arrive_expect_tx(full + stage, kStageBytes);
-                    sm100::tma_load_2d(sa, &tmap_q, full + stage, kb * kBK, qt * kBM);
-                    sm100::tma_load_2d(sa + kStageA, &tmap_e, full + stage, kb * kBK, row0);
+                    sm100::tma_load_2d(sa, &tmap_q, full + stage, kb * kElemsK, qt * kBM);
+                    sm100::tma_load_2d(sa + kStageA, &tmap_e, full + stage, kb * kElemsK, row0);
                     issued[stage] = true;
                     issued_phase[stage] = phase;
                     if (++stage == kStages) { stage = 0; phase ^= 1u; }
@@ -153,7 +160,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t idesc = sm100::idesc_tf32(kBM, kBN);
+            constexpr uint32_t idesc = F16 ? sm100::idesc_f16(kBM, kBN) : sm100::idesc_tf32(kBM, kBN);
             int stage = 0;
             uint32_t phase = 0;
             int buf = 0;
@@ -170,9 +177,14 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                     const uint64_t da = sm100::smem_desc_sw128(sa);
                     const uint64_t db = sm100::smem_desc_sw128(sa + kStageA);
 #pragma unroll
-                    for (int k = 0; k < kBK / 8; ++k)   // 8 tf32 (32 bytes) per MMA
-                        sm100::mma_tf32(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
-                                        (kb > 0 || k > 0) ? 1u : 0u);
+                    for (int k = 0; k < 4; ++k) {      // 32 bytes of K per MMA: 8 tf32 or 16 fp16
+                        if constexpr (F16)
+                            sm100::mma_f16(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
+                                           (kb > 0 || k > 0) ? 1u : 0u);
+                        else
+                            sm100::mma_tf32(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
+                                            (kb > 0 || k > 0) ? 1u : 0u);
+                    }
                     sm100::mma_commit(empty + stage);   // stage reusable when these MMAs finish
                     if (++stage == kStages) { stage = 0; phase ^= 1u; }
                 }
@@ -279,9 +291,38 @@ __global__ void prep_rows_kernel(const float* __restrict__ ts, const float* __re
     }
 }
 
+// fp16 copy of rows [r0, r1) (row pitch `pitch16` halves, pad zero).
+__global__ void to_f16_rows_kernel(const float* __restrict__ E, int64_t pitch, int32_t r0, int32_t r1, int32_t dim,
+                                   __half* __restrict__ E16, int64_t pitch16) {
+    const int64_t total = (int64_t)(r1 - r0) * pitch16;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = r0 + i / pitch16;
+        const int64_t d = i % pitch16;
+        E16[r * pitch16 + d] = d < dim ? __float2half_rn(E[r * pitch + d]) : __float2half_rn(0.0f);
+    }
+}
+
+// fp16 copies of the queries; *bad is set when a component is outside the
+// fp16 range that the error margin covers.
+__global__ void to_f16_queries_kernel(const float* __restrict__ Q, int64_t qpitch, int32_t B, int32_t dim,
+                                      __half* __restrict__ Q16, int64_t pitch16, int* __restrict__ bad) {
+    const int64_t total = (int64_t)B * pitch16;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t b = i / pitch16, d = i % pitch16;
+        float x = 0.0f;
+        if (d < dim) {
+            x = Q[b * qpitch + d];
+            if (!(fabsf(x) <= kF16Max)) atomicExch(bad, 1);
+        }
+        Q16[b * pitch16 + d] = __float2half_rn(x);
+    }
+}
+
 __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch, int32_t B, int32_t nc,
-                                    const unsigned int* __restrict__ norm_bits, float* __restrict__ margin,
-                                    int32_t* __restrict__ cand_cnt) {
+                                    const unsigned int* __restrict__ norm_bits, int32_t f16,
+                                    float* __restrict__ margin, int32_t* __restrict__ cand_cnt) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= B) return;
     const float4* q = reinterpret_cast<const float4*>(Q + (int64_t)warp * qpitch);
@@ -293,7 +334,14 @@ __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch,
     s = warp_butterfly_sum(s);
     if (lane == 0) {
         // 1.0001: covers the fp32 rounding of this norm itself
-        margin[warp] = kMarginRel * sqrtf(s) * 1.0001f * __uint_as_float(*norm_bits);
+        const float qn = sqrtf(s) * 1.0001f, en = __uint_as_float(*norm_bits);
+        float mg = kMarginRel * qn * en;
+        // fp16 operands: components below the normal range are rounded to a
+        // multiple of 2^-24, an absolute error of at most 2^-25 each; over D
+        // <= 4 nc components the dot changes by at most
+        // 2^-25 (||q||_1 + ||e||_1 + ...) <= 2^-24 sqrt(4 nc) (||q|| + ||e||)
+        if (f16) mg += 5.9604645e-8f * sqrtf(4.0f * nc) * (qn + en) * 1.0001f;
+        margin[warp] = mg;
         cand_cnt[warp] = 0;
     }
 }
@@ -488,6 +536,11 @@ struct mars_batch_ctx {
     int32_t* d_sample_rt = nullptr;
     int32_t sample_tiles_cap = 0;
     int* d_err = nullptr;
+    __half* d_q16 = nullptr;         // max_batch x q16_pitch: fp16 queries
+    int32_t q16_pitch = 0;
+    int* d_bad = nullptr;            // a query component outside the fp16 range
+    int* h_bad = nullptr;            // pinned
+    int32_t precision = 0;           // 0: fp16 when in range, 1: TF32 always
     int32_t* h_fallback = nullptr;   // pinned
     int32_t* h_cand_cnt = nullptr;   // pinned
     int* h_err = nullptr;
@@ -510,16 +563,20 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
     return fn;
 }
 
-// 2D fp32 tensor [rows][cols] with a row stride of `pitch` floats; box
-// (32 cols x box_rows), 128-byte swizzle, out-of-range elements read as 0.
-int make_map(CUtensorMap* m, const float* base, int64_t rows, int64_t cols, int64_t pitch, int box_rows) {
+// 2D tensor [rows][cols] (fp32, or fp16 when f16) with a row stride of
+// `pitch` elements; box (128 bytes of cols x box_rows), 128-byte swizzle,
+// out-of-range elements read as 0.
+int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64_t pitch, int box_rows,
+             bool f16 = false) {
     auto enc = get_encode();
     if (enc == nullptr) return fail(MARS_ERR_CUDA, "cuTensorMapEncodeTiled is unavailable");
+    const int64_t esz = f16 ? 2 : 4;
     cuuint64_t gdim[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t gstride[1] = {(cuuint64_t)(pitch * 4)};
-    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    cuuint64_t gstride[1] = {(cuuint64_t)(pitch * esz)};
+    cuuint32_t box[2] = {(cuuint32_t)(128 / esz), (cuuint32_t)box_rows};
     cuuint32_t estride[2] = {1, 1};
-    CUresult r = enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), gdim, gstride, box,
+    CUresult r = enc(m, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2,
+                     const_cast<void*>(base), gdim, gstride, box,
                      estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return fail(MARS_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
@@ -569,18 +626,30 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     T(cudaMallocHost(&c->h_fallback, (size_t)max_batch * 4), "pinned flags");
     T(cudaMallocHost(&c->h_cand_cnt, (size_t)max_batch * 4), "pinned counts");
     T(cudaMallocHost(&c->h_err, sizeof(int)), "pinned error");
+    c->q16_pitch = (dim + 7) & ~7;
+    T(cudaMalloc(&c->d_q16, (size_t)max_batch * c->q16_pitch * sizeof(__half)), "fp16 queries");
+    T(cudaMalloc(&c->d_bad, sizeof(int)), "range flag");
+    T(cudaMallocHost(&c->h_bad, sizeof(int)), "pinned range flag");
     if (rc == MARS_OK) T(cudaMemset(c->d_err, 0, sizeof(int)), "memset");
     if (rc == MARS_OK) {
         static bool attr_done[64] = {};
         if (device < 64 && !attr_done[device]) {
-            T(cudaFuncSetAttribute(gemm_kernel<kSample>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem), "smem attr");
-            T(cudaFuncSetAttribute(gemm_kernel<kCandidates>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem), "smem attr");
+            T(cudaFuncSetAttribute(gemm_kernel<kSample, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem), "smem attr");
+            T(cudaFuncSetAttribute(gemm_kernel<kCandidates, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem), "smem attr");
+            T(cudaFuncSetAttribute(gemm_kernel<kSample, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem), "smem attr");
+            T(cudaFuncSetAttribute(gemm_kernel<kCandidates, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem), "smem attr");
             attr_done[device] = rc == MARS_OK;
         }
     }
     if (rc == MARS_OK) rc = mars_query_ctx_create(device, max_nodes, dim, max_k, &c->scan_ctx);
     if (rc != MARS_OK) { mars_batch_ctx_destroy(c); return rc; }
     *out = c;
+    return MARS_OK;
+}
+
+int mars_batch_ctx_set_precision(mars_batch_ctx* c, int32_t tf32_only) {
+    if (c == nullptr) return fail(MARS_ERR_INVALID, "mars_batch_ctx_set_precision: NULL context");
+    c->precision = tf32_only != 0 ? 1 : 0;
     return MARS_OK;
 }
 
@@ -593,6 +662,7 @@ int mars_batch_ctx_destroy(mars_batch_ctx* c) {
     cudaFree(c->d_cand_cnt); cudaFree(c->d_fallback); cudaFree(c->d_sample); cudaFree(c->d_sample_rt);
     cudaFree(c->d_err);
     cudaFreeHost(c->h_fallback); cudaFreeHost(c->h_cand_cnt); cudaFreeHost(c->h_err);
+    cudaFree(c->d_q16); cudaFree(c->d_bad); cudaFreeHost(c->h_bad);
     mars_query_ctx_destroy(c->scan_ctx);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
@@ -615,10 +685,70 @@ int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d
 
 }  // extern "C"
 
+int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
+                    int32_t B, float t_q, float lambda, int32_t modality_filter, int32_t use_importance,
+                    int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
+                    int32_t* d_counts, void* stream, bool allow_f16, bool* redo);
+
+namespace {
+
+// Bring the store's fp16 copy of the rows up to date on stream st (after the
+// store's writes).  *ok: the copy may be used (every component within the
+// range the error margin covers).
+int ensure_f16_rows(const mars_store* cs, cudaStream_t st, bool* ok) {
+    auto* s = const_cast<mars_store*>(cs);   // the copy is a cache of the rows
+    *ok = false;
+    const int32_t n = s->n;
+    if (s->e16_rows < n) {
+        unsigned int bits = 0;
+        MARS_CUDA_TRY(cudaMemcpyAsync(&bits, s->d_norm_bits, sizeof(bits), cudaMemcpyDeviceToHost, st));
+        MARS_CUDA_TRY(cudaStreamSynchronize(st));
+        float bound;
+        std::memcpy(&bound, &bits, sizeof(bound));
+        s->e16_in_range = bound <= kF16Max;   // |component| <= row norm
+        if (!s->e16_in_range) return MARS_OK;
+        if (s->d_E16 == nullptr) {
+            s->e16_pitch = (s->dim + 7) & ~7;
+            MARS_CUDA_TRY(cudaMalloc(&s->d_E16, (size_t)s->capacity * s->e16_pitch * sizeof(__half)));
+        }
+        if (s->e16_ready == nullptr) MARS_CUDA_TRY(cudaEventCreateWithFlags(&s->e16_ready, cudaEventDisableTiming));
+        const int32_t r0 = s->e16_rows;
+        const int64_t total = (int64_t)(n - r0) * s->e16_pitch;
+        const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+        to_f16_rows_kernel<<<grid, 256, 0, st>>>(s->d_E, s->pitch, r0, n, s->dim,
+                                                 static_cast<__half*>(s->d_E16), s->e16_pitch);
+        MARS_CUDA_TRY(cudaGetLastError());
+        MARS_CUDA_TRY(cudaEventRecord(s->e16_ready, st));
+        s->e16_rows = n;
+    } else if (s->e16_ready != nullptr) {
+        // another stream may still be converting the last rows
+        MARS_CUDA_TRY(cudaStreamWaitEvent(st, s->e16_ready, 0));
+    }
+    *ok = s->e16_in_range;
+    return MARS_OK;
+}
+
+}  // namespace
+
 int mars::batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
                      int32_t B, float t_q, float lambda, int32_t modality_filter, int32_t use_importance,
                      int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
                      int32_t* d_counts, void* stream) {
+    bool redo = false;
+    MARS_TRY(batch_topk_pass(s, c, d_queries, query_pitch, B, t_q, lambda, modality_filter, use_importance, K,
+                             row_offset, self_base, d_ids, d_vals, d_counts, stream, c != nullptr && c->precision == 0,
+                             &redo));
+    if (!redo) return MARS_OK;
+    // a query component outside the fp16 range: the same batch on TF32
+    return batch_topk_pass(s, c, d_queries, query_pitch, B, t_q, lambda, modality_filter, use_importance, K,
+                           row_offset, self_base, d_ids, d_vals, d_counts, stream, false, &redo);
+}
+
+int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
+                    int32_t B, float t_q, float lambda, int32_t modality_filter, int32_t use_importance,
+                    int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
+                    int32_t* d_counts, void* stream, bool allow_f16, bool* redo) {
+    *redo = false;
     if (s == nullptr || c == nullptr || d_queries == nullptr || d_ids == nullptr || d_vals == nullptr)
         return fail(MARS_ERR_INVALID, "mars_query_batch_topk: NULL argument");
     if (s->device != c->device || s->dim != c->dim)
@@ -639,7 +769,7 @@ int mars::batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d_quer
     const int32_t n = s->n;
     const int32_t rtiles = (n + kBN - 1) / kBN;
     const int32_t qtiles = (B + kBM - 1) / kBM;
-    const int32_t nkb = (s->pitch + kBK - 1) / kBK;
+    int32_t nkb = (s->pitch + kBK - 1) / kBK;
 
     // sample size: about mu = 2 expected true top-K members in the sample
     int32_t n_sample = (int32_t)std::ceil(2.0 * (double)n / ((double)K * kBN));
@@ -675,16 +805,32 @@ int mars::batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d_quer
     for (int32_t i = 0; i < n_sample; ++i) srt[i] = (int32_t)(((int64_t)i * rtiles) / n_sample);
     MARS_CUDA_TRY(cudaMemcpyAsync(c->d_sample_rt, srt.data(), (size_t)n_sample * 4, cudaMemcpyHostToDevice, st));
 
+    // operands: fp16 copies (twice the tensor-core rate, half the bytes,
+    // the same 10 mantissa bits as TF32) when every value is in range
+    bool f16 = false;
+    if (allow_f16) MARS_TRY(ensure_f16_rows(s, st, &f16));
     CUtensorMap mq, me;
-    MARS_TRY(make_map(&mq, d_queries, B, s->pitch, query_pitch, kBM));
-    MARS_TRY(make_map(&me, s->d_E, n, s->pitch, s->pitch, kBN));
+    if (f16) {
+        MARS_CUDA_TRY(cudaMemsetAsync(c->d_bad, 0, sizeof(int), st));
+        const int64_t total = (int64_t)B * c->q16_pitch;
+        to_f16_queries_kernel<<<(int)std::min<int64_t>((total + 255) / 256, 148 * 8), 256, 0, st>>>(
+            d_queries, query_pitch, B, s->dim, c->d_q16, c->q16_pitch, c->d_bad);
+        MARS_CUDA_TRY(cudaGetLastError());
+        MARS_TRY(make_map(&mq, c->d_q16, B, c->q16_pitch, c->q16_pitch, kBM, true));
+        MARS_TRY(make_map(&me, s->d_E16, n, s->e16_pitch, s->e16_pitch, kBN, true));
+        nkb = (s->e16_pitch + 63) / 64;
+    } else {
+        MARS_TRY(make_map(&mq, d_queries, B, s->pitch, query_pitch, kBM));
+        MARS_TRY(make_map(&me, s->d_E, n, s->pitch, s->pitch, kBN));
+    }
 
     const int wblocks = std::min((n + 255) / 256, c->num_sms * 8);
     prep_rows_kernel<<<wblocks, 256, 0, st>>>(s->d_ts, s->d_imp, s->d_mod, n, t_q, lambda, modality_filter,
                                               use_importance, c->d_wts);
     MARS_CUDA_TRY(cudaGetLastError());
     prep_queries_kernel<<<(B * 32 + 255) / 256, 256, 0, st>>>(d_queries, query_pitch, B, (s->dim + 3) / 4,
-                                                              s->d_norm_bits, c->d_margin, c->d_cand_cnt);
+                                                              s->d_norm_bits, f16 ? 1 : 0, c->d_margin,
+                                                              c->d_cand_cnt);
     MARS_CUDA_TRY(cudaGetLastError());
     MARS_CUDA_TRY(cudaMemsetAsync(c->d_err, 0, sizeof(int), st));
 
@@ -708,14 +854,20 @@ int mars::batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d_quer
 
     // 2. sample
     ga.n_tiles = n_sample * qtiles;
-    gemm_kernel<kSample><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
+    if (f16)
+        gemm_kernel<kSample, true><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
+    else
+        gemm_kernel<kSample, false><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
     MARS_CUDA_TRY(cudaGetLastError());
     // 3. thresholds
     threshold_kernel<<<(B * 32 + 255) / 256, 256, 0, st>>>(c->d_sample, n_sample, B, j, c->d_theta);
     MARS_CUDA_TRY(cudaGetLastError());
     // 4. candidates
     ga.n_tiles = rtiles * qtiles;
-    gemm_kernel<kCandidates><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
+    if (f16)
+        gemm_kernel<kCandidates, true><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
+    else
+        gemm_kernel<kCandidates, false><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
     MARS_CUDA_TRY(cudaGetLastError());
     // 5. rescore
     StoreView v{};
@@ -731,7 +883,13 @@ int mars::batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d_quer
     MARS_CUDA_TRY(cudaMemcpyAsync(c->h_cand_cnt, c->d_cand_cnt, (size_t)B * 4, cudaMemcpyDeviceToHost, st));
     MARS_CUDA_TRY(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
     MARS_CUDA_TRY(cudaMemcpyAsync(c->h_rescored, c->d_rescored, (size_t)B * 4, cudaMemcpyDeviceToHost, st));
+    *c->h_bad = 0;
+    if (f16) MARS_CUDA_TRY(cudaMemcpyAsync(c->h_bad, c->d_bad, sizeof(int), cudaMemcpyDeviceToHost, st));
     MARS_CUDA_TRY(cudaStreamSynchronize(st));
+    if (f16 && *c->h_bad != 0) {
+        *redo = true;
+        return MARS_OK;
+    }
     if (*c->h_err != 0)
         return fail(MARS_ERR_TIMEOUT, "mars_query_batch_topk: a tensor-core pipeline wait gave up (code " +
                                           std::to_string(*c->h_err) + ")");
@@ -749,7 +907,7 @@ int mars::batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d_quer
                                                d_vals + (int64_t)b * K, d_counts ? d_counts + b : nullptr, st));
         }
     }
-    c->last.path = 1;
+    c->last.path = f16 ? 2 : 1;
     c->last.fallbacks = fb;
     c->last.candidates = total;
     c->last.max_candidates = maxc;

@@ -124,6 +124,15 @@ struct mars_store {
         int32_t rows = 0;             // capacity of d_cnt
     };
     BuildCache build;
+
+    // fp16 copy of the rows for the batched tensor-core short list (made on
+    // the first batched query; rows [0, e16_rows) are current: appends extend
+    // it, uploads and deletes reset it)
+    void* d_E16 = nullptr;
+    int32_t e16_pitch = 0;      // halves per row (dim rounded up to 8)
+    int32_t e16_rows = 0;
+    bool e16_in_range = false;  // every component within the fp16 range covered
+    cudaEvent_t e16_ready = nullptr;   // the last conversion into d_E16
 };
 
 // ---- query context (QueryContext) ----------------------------------------

@@ -233,6 +233,8 @@ static void release_store(mars_store* s) {
     cudaFree(s->d_norm_bits);
     cudaFree(s->d_extra);
     cudaFree(s->d_extra_cnt);
+    cudaFree(s->d_E16);
+    if (s->e16_ready) cudaEventDestroy(s->e16_ready);
     if (s->build.bc) mars_batch_ctx_destroy(s->build.bc);
     cudaFree(s->build.d_knn);
     cudaFree(s->build.d_vals);
@@ -407,6 +409,7 @@ int mars_store_upload(mars_store* s, int32_t n, const float* embeddings, const i
     }
     MARS_CUDA_TRY(cudaStreamSynchronize(st));   // n lives on this stack frame
     s->n = n;
+    s->e16_rows = 0;
     MARS_CUDA_TRY(cudaEventRecord(s->written, st));
     return MARS_OK;
 }
@@ -588,6 +591,7 @@ int mars_store_delete(mars_store* s, int32_t n, const int32_t* ids) {
         MARS_CUDA_TRY(cudaMemcpyAsync(d_tmp, ids, (size_t)n * 4, cudaMemcpyHostToDevice, st));
         d_ids = d_tmp;
     }
+    s->e16_rows = 0;   // rows change in place: the fp16 copy is rebuilt on next use
     delete_rows_kernel<<<(unsigned)(((int64_t)n * 32 + 255) / 256), 256, 0, st>>>(
         s->d_E, (int64_t)s->pitch, s->d_ts, d_ids, n, s->d_n, s->dim);
     MARS_CUDA_TRY(cudaGetLastError());

@@ -278,7 +278,8 @@ int mars_novelty(const mars_store* s, mars_query_ctx* ctx, const float* d_query,
 typedef struct mars_batch_ctx mars_batch_ctx;
 
 typedef struct mars_batch_stats {
-    int32_t path;            /* 1: tensor-core path, 0: per-query scans (small N) */
+    int32_t path;            /* 2: tensor cores, fp16 operands; 1: tensor cores, TF32;
+                                0: per-query scans (small N) */
     int32_t fallbacks;       /* queries recomputed exactly                         */
     int64_t candidates;      /* short-listed (query, row) pairs                    */
     int32_t max_candidates;  /* largest short list of one query                    */
@@ -290,6 +291,16 @@ typedef struct mars_batch_stats {
 int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim,
                           int32_t max_batch, int32_t max_k, mars_batch_ctx** out);
 int mars_batch_ctx_destroy(mars_batch_ctx* ctx);
+
+/* Operand precision of the batched tensor-core short list.  By default the
+ * GEMM runs on fp16 copies of the rows and queries (kind::f16: twice the
+ * TF32 rate and half the bytes, the same 10 mantissa bits, so the same
+ * proven error margin plus an absolute term for values below the fp16
+ * normal range); stores or queries with a component beyond 60000 use TF32.
+ * tf32_only != 0 always uses TF32 operands.  Either way the final scores are
+ * exact fp32 and the results identical.  The fp16 copy of a store is made on
+ * its first batched query (2 bytes per value) and kept current. */
+int mars_batch_ctx_set_precision(mars_batch_ctx* ctx, int32_t tf32_only);
 
 /* d_queries: B rows of query_pitch floats (16-byte aligned; values past dim
  * must be zero).  One query time t_q for the whole batch.  Outputs d_ids /

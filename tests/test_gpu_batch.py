@@ -18,17 +18,24 @@ def torch_mod():
     return torch
 
 
-def _run(torch, N, D, B, K, filt=-1, use_imp=True, lam=0.01, t_q=600.0, seed=0, check_oracle=2):
+def _run(torch, N, D, B, K, filt=-1, use_imp=True, lam=0.01, t_q=600.0, seed=0, check_oracle=2,
+         tf32_only=False, scale_row=None, scale_query=None):
     import mars_b200 as mb
     from mars_b200 import datagen
     E, mod, ts, imp = datagen.gaussian_corpus(N, D, seed=seed, ts_max=600.0)
     Q = datagen.queries(B, D, seed=seed + 1)
     pitch = (D + 3) // 4 * 4
+    if scale_row is not None:            # a row beyond the fp16 range
+        E[scale_row[0]] *= scale_row[1]
+    if scale_query is not None:          # a query beyond the fp16 range
+        Q[scale_query[0]] *= scale_query[1]
     Qp = np.zeros((B, pitch), np.float32)
     Qp[:, :D] = Q
     st = mb.Store(N, D)
     st.upload(E, mod, ts, imp)
     bc = mb.BatchContext(N, D, max_batch=B, max_k=K)
+    if tf32_only:
+        bc.set_precision(True)
     ctx = mb.QueryContext(N, D, max_k=K)
     Qd = torch.from_numpy(Qp).cuda()
     ids = torch.full((B, K), -7, dtype=torch.int32, device="cuda")
@@ -60,20 +67,71 @@ def _run(torch, N, D, B, K, filt=-1, use_imp=True, lam=0.01, t_q=600.0, seed=0, 
 
 def test_batch_small_smoke(torch_mod):
     stats = _run(torch_mod, N=8192, D=768, B=128, K=10)
-    assert stats["path"] == 1
+    assert stats["path"] == 2
 
 
+@pytest.mark.parametrize("tf32_only", [False, True])
 @pytest.mark.parametrize("N,D,B,K", [(100_003, 768, 200, 100), (60_000, 768, 256, 10),
                                      (50_000, 64, 130, 32), (40_000, 100, 64, 50)])
-def test_batch_matches_single_query_scans(torch_mod, N, D, B, K):
-    stats = _run(torch_mod, N, D, B, K, seed=N % 97)
-    assert stats["path"] == 1
+def test_batch_matches_single_query_scans(torch_mod, N, D, B, K, tf32_only):
+    """fp16 operands (default) and TF32 operands give the same results."""
+    stats = _run(torch_mod, N, D, B, K, seed=N % 97, tf32_only=tf32_only)
+    assert stats["path"] == (1 if tf32_only else 2)
     assert stats["fallbacks"] <= max(2, B // 50), stats
 
 
 def test_batch_with_modality_filter(torch_mod):
     stats = _run(torch_mod, 70_000, 768, 128, 20, filt=2, seed=5)
+    assert stats["path"] == 2
+
+
+def test_batch_out_of_fp16_range_uses_tf32(torch_mod):
+    """A row or a query with a component beyond the fp16 range covered by
+    the error margin moves the batch to TF32 operands; results unchanged."""
+    stats = _run(torch_mod, 30_000, 768, 64, 10, seed=8, scale_row=(123, 1e6))
     assert stats["path"] == 1
+    stats = _run(torch_mod, 30_000, 768, 64, 10, seed=9, scale_query=(5, 1e6))
+    assert stats["path"] == 1
+
+
+def test_batch_fp16_copy_follows_appends_and_deletes(torch_mod):
+    """The store's fp16 copy is extended after appends and rebuilt after a
+    delete: batched results keep matching the exact scans."""
+    import mars_b200 as mb
+    from mars_b200 import datagen
+    torch = torch_mod
+    N0, D, B, K = 20_000, 768, 64, 10
+    E, mod, ts, imp = datagen.gaussian_corpus(N0, D, seed=21, ts_max=600.0)
+    st = mb.Store(N0 + 5000, D)
+    st.upload(E, mod, ts, imp)
+    bc = mb.BatchContext(N0 + 5000, D, max_batch=B, max_k=K)
+    ctx = mb.QueryContext(N0 + 5000, D, max_k=K)
+    Q = torch.from_numpy(datagen.queries(B, D, seed=22)).cuda()
+
+    def check():
+        ids = torch.empty((B, K), dtype=torch.int32, device="cuda")
+        vals = torch.empty((B, K), dtype=torch.float32, device="cuda")
+        bc.query_batch_topk(st, Q, B, 600.0, 0.01, K, ids, vals, use_importance=True)
+        torch.cuda.synchronize()
+        assert bc.last_stats()["path"] == 2
+        for b in range(0, B, 7):
+            i1 = torch.empty(K, dtype=torch.int32, device="cuda")
+            v1 = torch.empty(K, dtype=torch.float32, device="cuda")
+            ctx.scan_topk(st, Q[b], 600.0, 0.01, K, i1, v1, use_importance=True)
+            torch.cuda.synchronize()
+            assert np.array_equal(ids[b].cpu().numpy(), i1.cpu().numpy())
+            assert np.array_equal(vals[b].cpu().numpy().view(np.uint32), v1.cpu().numpy().view(np.uint32))
+        return ids
+
+    check()
+    # rows close to the queries appended: they must reach the fp16 copy
+    rows = Q[:40].cpu().numpy() * 3.0
+    st.append(rows, np.zeros(40, np.int32), np.full(40, 600.0, np.float32), np.ones(40, np.float32),
+              normalize=False)
+    ids = check()
+    assert int(ids[0, 0].item()) >= N0
+    st.delete(ids[:, 0].cpu().numpy())
+    check()
 
 
 def test_batch_small_corpus_uses_scans(torch_mod):
