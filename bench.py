@@ -616,9 +616,13 @@ def run_batch(a):
                 "value": B * a.steps / (ms * 1e-3), "unit": "queries/s", "n_gpus": world,
                 "steps": a.steps, "ms_per_step": ms / a.steps, "scaling": "strong",
                 "roofline": {"bound": "tensor", "achieved": achieved, "unit": "TFLOP/s per GPU",
-                             "peak_bf16_measured": bf16, "frac_of_bf16": achieved / bf16,
-                             "tf32_nominal": bf16 / 2,
-                             "frac_of_tf32_nominal": achieved / (bf16 / 2),
+                             "operands": {2: "fp16 (kind::f16)", 1: "tf32 (kind::tf32)"}.get(
+                                 stats.get("path"), "scan"),
+                             # fp16 runs at the bf16 rate; TF32 at half of it
+                             "peak": bf16 if stats.get("path") == 2 else bf16 / 2,
+                             "peak_kind": ("measured bf16 GEMM" if "bf16_tflops" in peaks else "fallback")
+                                          + (" (same rate as fp16)" if stats.get("path") == 2 else " / 2 (TF32)"),
+                             "frac": achieved / (bf16 if stats.get("path") == 2 else bf16 / 2),
                              "flops_per_batch": flops},
                 "batch_stats_rank0": stats, "phases_rank0_wall": phases, "clocks": clocks}
         print(json.dumps(line), flush=True)
