@@ -64,7 +64,6 @@ constexpr int kThreads = 192;
 constexpr int kTmemCols = 512;
 constexpr int kJ = 16;                // sampled lower bounds kept per (query, tile)
 constexpr float kMarginRel = 2.6e-3f;
-constexpr float kF16Max = 60000.0f;   // |component| bound for the fp16 operands
 
 enum Mode { kSample = 0, kCandidates = 1 };
 
@@ -288,18 +287,6 @@ __global__ void prep_rows_kernel(const float* __restrict__ ts, const float* __re
             if (use_imp) w = w * imp[i];
         }
         wts[i] = w;
-    }
-}
-
-// fp16 copy of rows [r0, r1) (row pitch `pitch16` halves, pad zero).
-__global__ void to_f16_rows_kernel(const float* __restrict__ E, int64_t pitch, int32_t r0, int32_t r1, int32_t dim,
-                                   __half* __restrict__ E16, int64_t pitch16) {
-    const int64_t total = (int64_t)(r1 - r0) * pitch16;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = r0 + i / pitch16;
-        const int64_t d = i % pitch16;
-        E16[r * pitch16 + d] = d < dim ? __float2half_rn(E[r * pitch + d]) : __float2half_rn(0.0f);
     }
 }
 
@@ -690,46 +677,6 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
                     int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
                     int32_t* d_counts, void* stream, bool allow_f16, bool* redo);
 
-namespace {
-
-// Bring the store's fp16 copy of the rows up to date on stream st (after the
-// store's writes).  *ok: the copy may be used (every component within the
-// range the error margin covers).
-int ensure_f16_rows(const mars_store* cs, cudaStream_t st, bool* ok) {
-    auto* s = const_cast<mars_store*>(cs);   // the copy is a cache of the rows
-    *ok = false;
-    const int32_t n = s->n;
-    if (s->e16_rows < n) {
-        unsigned int bits = 0;
-        MARS_CUDA_TRY(cudaMemcpyAsync(&bits, s->d_norm_bits, sizeof(bits), cudaMemcpyDeviceToHost, st));
-        MARS_CUDA_TRY(cudaStreamSynchronize(st));
-        float bound;
-        std::memcpy(&bound, &bits, sizeof(bound));
-        s->e16_in_range = bound <= kF16Max;   // |component| <= row norm
-        if (!s->e16_in_range) return MARS_OK;
-        if (s->d_E16 == nullptr) {
-            s->e16_pitch = (s->dim + 7) & ~7;
-            MARS_CUDA_TRY(cudaMalloc(&s->d_E16, (size_t)s->capacity * s->e16_pitch * sizeof(__half)));
-        }
-        if (s->e16_ready == nullptr) MARS_CUDA_TRY(cudaEventCreateWithFlags(&s->e16_ready, cudaEventDisableTiming));
-        const int32_t r0 = s->e16_rows;
-        const int64_t total = (int64_t)(n - r0) * s->e16_pitch;
-        const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
-        to_f16_rows_kernel<<<grid, 256, 0, st>>>(s->d_E, s->pitch, r0, n, s->dim,
-                                                 static_cast<__half*>(s->d_E16), s->e16_pitch);
-        MARS_CUDA_TRY(cudaGetLastError());
-        MARS_CUDA_TRY(cudaEventRecord(s->e16_ready, st));
-        s->e16_rows = n;
-    } else if (s->e16_ready != nullptr) {
-        // another stream may still be converting the last rows
-        MARS_CUDA_TRY(cudaStreamWaitEvent(st, s->e16_ready, 0));
-    }
-    *ok = s->e16_in_range;
-    return MARS_OK;
-}
-
-}  // namespace
-
 int mars::batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
                      int32_t B, float t_q, float lambda, int32_t modality_filter, int32_t use_importance,
                      int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
@@ -808,7 +755,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     // operands: fp16 copies (twice the tensor-core rate, half the bytes,
     // the same 10 mantissa bits as TF32) when every value is in range
     bool f16 = false;
-    if (allow_f16) MARS_TRY(ensure_f16_rows(s, st, &f16));
+    if (allow_f16) MARS_TRY(mars::store_f16_rows(s, st, &f16));
     CUtensorMap mq, me;
     if (f16) {
         MARS_CUDA_TRY(cudaMemsetAsync(c->d_bad, 0, sizeof(int), st));

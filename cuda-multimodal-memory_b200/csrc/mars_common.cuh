@@ -65,10 +65,12 @@ __device__ __forceinline__ int warp_reduce_sum_int(int v) {
 // The one definition of the temporal decay (src/memory_cuda.cu:292-310:
 // final = sim * __expf(-lambda * max(0, t_q - ts))), shared by the scan and
 // the BFS kernels so a node's score is bit-identical whichever computes it.
-__device__ __forceinline__ float fused_weight_apply(float dot, float ts, float t_q, float lambda) {
+__device__ __forceinline__ float fused_weight(float ts, float t_q, float lambda) {
     const float age = fmaxf(0.0f, t_q - ts);
-    const float w = __expf(-lambda * age);
-    return dot * w;
+    return __expf(-lambda * age);
+}
+__device__ __forceinline__ float fused_weight_apply(float dot, float ts, float t_q, float lambda) {
+    return dot * fused_weight(ts, t_q, lambda);
 }
 
 // ---------------------------------------------------------------------------

@@ -29,6 +29,20 @@ int scan_topk_excluding(const mars_store* s, mars_query_ctx* c, const float* d_q
                         float lambda, int32_t modality_filter, int32_t use_importance, int32_t K,
                         int32_t row_offset, int32_t exclude_row, int32_t* d_ids, float* d_vals,
                         int32_t* d_count, void* stream);
+// Largest |component| the fp16 copies of rows and queries may hold: within
+// it the fp16 rounding error bounds used by the batched short list and the
+// fp16-filtered scan hold.
+constexpr float kF16Max = 60000.0f;
+
+// Bring the store's fp16 copy of the rows up to date on stream st; *ok says
+// whether it may be used (every component within kF16Max).
+int store_f16_rows(const mars_store* s, cudaStream_t st, bool* ok);
+
+// fp16-filtered scan: queries per launch and candidate rows kept per query
+constexpr int kF16Slots = 16;
+constexpr int kF16CandCap = 65536;
+int query_ctx_f16_buffers(mars_query_ctx* c);
+
 int fail(int status, const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what, const char* file, int line);
 
@@ -185,6 +199,16 @@ struct mars_query_ctx {
     int32_t* dm_result_cnt = nullptr;           // = h_result_cnt, device view
     uint64_t fused_queries = 0;                 // answered by the single launch
     uint64_t fused_reruns = 0;                  // BFS outgrew the last CTA
+
+    // fp16-filtered scan (mars_scan16.cu), allocated on first use
+    unsigned int* d_f16_ticket = nullptr;       // kF16Slots
+    unsigned long long* d_f16_cand = nullptr;   // kF16Slots x kF16CandCap
+    int32_t* d_f16_cnt = nullptr;               // kF16Slots
+    int32_t* d_f16_overflow = nullptr;          // kF16Slots flags, then kF16Slots x (candidates, survivors)
+    int32_t* h_f16_overflow = nullptr;          // pinned copy
+    uint64_t f16_reruns = 0;                    // queries re-run on the fp32 scan
+    int32_t f16_max_cand = 0;                   // largest candidate list of the last call
+    int32_t f16_max_surv = 0;                   // largest survivor count of the last call (-1: overflow)
 
     // graph replay of the whole query (H2D desc -> kernels -> D2H)
     bool use_graph = true;

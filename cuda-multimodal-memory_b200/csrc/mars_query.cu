@@ -327,6 +327,11 @@ int mars_query_ctx_destroy(mars_query_ctx* c) {
     cudaFree(c->d_part_idx);
     cudaFree(c->d_ticket);
     cudaFree(c->d_multi);
+    cudaFree(c->d_f16_ticket);
+    cudaFree(c->d_f16_cnt);
+    cudaFree(c->d_f16_overflow);
+    cudaFree(c->d_f16_cand);
+    cudaFreeHost(c->h_f16_overflow);
     cudaFree(c->d_stamp);
     cudaFree(c->d_vis_ids);
     cudaFree(c->d_vis_score);
@@ -505,6 +510,19 @@ int mars_scan_topk(const mars_store* s, mars_query_ctx* c, const float* d_query,
 }
 
 }  // extern "C"
+
+int mars::query_ctx_f16_buffers(mars_query_ctx* c) {
+    if (c->d_f16_cand != nullptr) return MARS_OK;
+    MARS_CUDA_TRY(cudaMalloc(&c->d_f16_ticket, kF16Slots * sizeof(unsigned int)));
+    MARS_CUDA_TRY(cudaMalloc(&c->d_f16_cnt, kF16Slots * sizeof(int32_t)));
+    MARS_CUDA_TRY(cudaMalloc(&c->d_f16_overflow, 3 * kF16Slots * sizeof(int32_t)));
+    MARS_CUDA_TRY(cudaMallocHost(&c->h_f16_overflow, 3 * kF16Slots * sizeof(int32_t)));
+    MARS_CUDA_TRY(cudaMemset(c->d_f16_ticket, 0, kF16Slots * sizeof(unsigned int)));
+    MARS_CUDA_TRY(cudaMemset(c->d_f16_cnt, 0, kF16Slots * sizeof(int32_t)));
+    MARS_CUDA_TRY(cudaMemset(c->d_f16_overflow, 0, 3 * kF16Slots * sizeof(int32_t)));
+    MARS_CUDA_TRY(cudaMalloc(&c->d_f16_cand, (size_t)kF16Slots * kF16CandCap * sizeof(unsigned long long)));
+    return MARS_OK;
+}
 
 extern "C" int mars_scan_topk_multi(const mars_store* s, mars_query_ctx* c, const float* d_queries,
                                     int32_t query_pitch, int32_t nq, float t_q, float lambda,

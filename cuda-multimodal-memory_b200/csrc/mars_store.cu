@@ -13,6 +13,7 @@
 // engine_server's add_node + ensure_device (src/engine_server.cu:154-213),
 // which grows host vectors and re-uploads the whole corpus on the next query.
 #include <cuda_runtime.h>
+#include <cuda_fp16.h>
 
 #include <algorithm>
 #include <cstdio>
@@ -145,6 +146,18 @@ __global__ void delete_rows_kernel(float* __restrict__ E, int64_t pitch, float* 
     float* row = E + (int64_t)u * pitch;
     for (int d = lane; d < dim; d += 32) row[d] = 0.0f;
     if (lane == 0) ts[u] = -1.0f;
+}
+
+// fp16 copy of rows [r0, r1) (row pitch `pitch16` halves, pad zero).
+__global__ void to_f16_rows_kernel(const float* __restrict__ E, int64_t pitch, int32_t r0, int32_t r1, int32_t dim,
+                                   __half* __restrict__ E16, int64_t pitch16) {
+    const int64_t total = (int64_t)(r1 - r0) * pitch16;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = r0 + i / pitch16;
+        const int64_t d = i % pitch16;
+        E16[r * pitch16 + d] = d < dim ? __float2half_rn(E[r * pitch + d]) : __float2half_rn(0.0f);
+    }
 }
 
 __global__ void fill_f32_kernel(float* p, int64_t n, float v) {
@@ -291,6 +304,44 @@ mars_store::HostStage* stage_acquire(mars_store* s, size_t bytes, int* rc) {
 }
 
 }  // namespace
+
+
+// Bring the store's fp16 copy of the rows up to date on stream st (after the
+// store's writes).  *ok: the copy may be used, i.e. every component is
+// within kF16Max (the row-norm bound says so).
+int mars::store_f16_rows(const mars_store* cs, cudaStream_t st, bool* ok) {
+    auto* s = const_cast<mars_store*>(cs);   // the copy is a cache of the rows
+    *ok = false;
+    if (!s->owns || s->d_norm_bits == nullptr) return MARS_OK;
+    const int32_t n = s->n;
+    if (s->e16_rows < n) {
+        unsigned int bits = 0;
+        MARS_CUDA_TRY(cudaMemcpyAsync(&bits, s->d_norm_bits, sizeof(bits), cudaMemcpyDeviceToHost, st));
+        MARS_CUDA_TRY(cudaStreamSynchronize(st));
+        float bound;
+        std::memcpy(&bound, &bits, sizeof(bound));
+        s->e16_in_range = bound <= kF16Max;   // |component| <= row norm
+        if (!s->e16_in_range) return MARS_OK;
+        if (s->d_E16 == nullptr) {
+            s->e16_pitch = (s->dim + 7) & ~7;
+            MARS_CUDA_TRY(cudaMalloc(&s->d_E16, (size_t)s->capacity * s->e16_pitch * sizeof(__half)));
+        }
+        if (s->e16_ready == nullptr) MARS_CUDA_TRY(cudaEventCreateWithFlags(&s->e16_ready, cudaEventDisableTiming));
+        const int32_t r0 = s->e16_rows;
+        const int64_t total = (int64_t)(n - r0) * s->e16_pitch;
+        const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+        to_f16_rows_kernel<<<grid, 256, 0, st>>>(s->d_E, s->pitch, r0, n, s->dim,
+                                                 static_cast<__half*>(s->d_E16), s->e16_pitch);
+        MARS_CUDA_TRY(cudaGetLastError());
+        MARS_CUDA_TRY(cudaEventRecord(s->e16_ready, st));
+        s->e16_rows = n;
+    } else if (s->e16_ready != nullptr) {
+        // another stream may still be converting the last rows
+        MARS_CUDA_TRY(cudaStreamWaitEvent(st, s->e16_ready, 0));
+    }
+    *ok = s->e16_in_range;
+    return MARS_OK;
+}
 
 extern "C" {
 

@@ -124,6 +124,8 @@ _SIGS = {
     "mars_scan_topk": [_VP, _VP, _VP, _F32, _F32, _I32, _I32, _I32, _I32, _VP, _VP, _VP, _VP],
     "mars_scan_topk_multi": [_VP, _VP, _VP, _I32, _I32, _F32, _F32, _I32, _I32, _I32, _I32, _VP, _VP, _VP,
                              _VP],
+    "mars_scan_topk_f16": [_VP, _VP, _VP, _I32, _I32, _F32, _F32, _I32, _I32, _I32, _I32, _VP, _VP, _VP, _VP],
+    "mars_query_ctx_f16_stats": [_VP, _VP, _VP, _VP],
     "mars_topk_merge": [_VP, _VP, _VP, _I32, _I32, _VP, _VP, _VP, _VP],
     "mars_topk_merge_batch": [_VP, _VP, _VP, _I32, _I32, _I32, _VP, _VP, _VP, _VP],
     "mars_debug_fused_scores": [_VP, _VP, _VP, _F32, _F32, _I32, _I32, _VP, _VP],
@@ -197,6 +199,39 @@ def _host(a, dtype):
     return None if a is None else np.ascontiguousarray(a, dtype=dtype)
 
 
+_STREAM_LEGACY = 1   # cudaStreamLegacy: the legacy default stream, named explicitly
+
+
+def _cuda_tensors(arrays):
+    return [a for a in arrays if getattr(a, "is_cuda", False)]
+
+
+def _stream(stream, *arrays):
+    """The stream a device call runs on.  An explicit stream is used as given.
+    Without one, a call that reads or writes torch CUDA tensors runs on
+    torch's current stream of their device, so it follows the work that made
+    its inputs and precedes the work that reads its outputs, as a torch op
+    would (cudaStreamLegacy names torch's default stream, since NULL means
+    the library object's own stream).  Otherwise NULL."""
+    if stream is not None:
+        return stream
+    t = _cuda_tensors(arrays)
+    if not t:
+        return None
+    import torch
+    h = torch.cuda.current_stream(t[0].device).cuda_stream
+    return h if h != 0 else _STREAM_LEGACY
+
+
+def _settle(*arrays):
+    """Store writes run on the store's own stream and return when done: torch
+    CUDA inputs must be complete before the library reads them."""
+    t = _cuda_tensors(arrays)
+    if t:
+        import torch
+        torch.cuda.current_stream(t[0].device).synchronize()
+
+
 class Store:
     """Device store (DeviceMemoryGraph) with in-place streaming append."""
 
@@ -222,6 +257,7 @@ class Store:
             return _ptr(a)
         n = int(E.shape[0])
         ne = 0 if col_indices is None else int(col_indices.shape[0])
+        _settle(E, modalities, timestamps, importance, row_offsets, col_indices)
         _check(lib().mars_store_upload(self.handle, n, prep(E, np.float32),
                                        prep(modalities, np.int32), prep(timestamps, np.float32),
                                        prep(importance, np.float32),
@@ -236,6 +272,7 @@ class Store:
         if imp is not None and not hasattr(imp, "data_ptr"):
             imp = _host(imp, np.float32)
         first = C.c_int32()
+        _settle(E, mod, ts, imp)
         _check(lib().mars_store_append(self.handle, int(E.shape[0]), _ptr(E), _ptr(mod), _ptr(ts),
                                        _ptr(imp), int(normalize), C.byref(first)))
         return first.value
@@ -252,6 +289,7 @@ class Store:
 
     def set_importance(self, first, importance):
         imp = importance if hasattr(importance, "data_ptr") else _host(importance, np.float32)
+        _settle(imp)
         _check(lib().mars_store_set_importance(self.handle, first, int(imp.shape[0]), _ptr(imp)))
 
     def read(self, first=0, n=None):
@@ -271,7 +309,7 @@ class Store:
     def importance_update(self, d_ids, n, boost=0.1, decay_rate=0.001, max_importance=5.0,
                           stream=None):
         _check(lib().mars_importance_update(self.handle, _ptr(d_ids), n, boost, decay_rate,
-                                            max_importance, stream))
+                                            max_importance, _stream(stream, d_ids)))
 
     def info(self) -> StoreInfo:
         i = StoreInfo()
@@ -319,6 +357,17 @@ class QueryContext:
         _check(lib().mars_query_ctx_path_counts(self.handle, C.byref(f), C.byref(r)))
         return f.value, r.value
 
+    def f16_stats(self) -> dict:
+        """scan_topk_f16's filter: re-runs on the fp32 scan (context life), largest
+        candidate list and rescored-row count of one query in the last call."""
+        r, mc, ms = C.c_uint64(), C.c_int32(), C.c_int32()
+        _check(lib().mars_query_ctx_f16_stats(self.handle, C.byref(r), C.byref(mc), C.byref(ms)))
+        return {"reruns": r.value, "max_candidates": mc.value, "max_survivors": ms.value}
+
+    def f16_reruns(self) -> int:
+        """Queries of scan_topk_f16 answered again by the fp32 scan (candidate overflow)."""
+        return self.f16_stats()["reruns"]
+
     @property
     def stream(self) -> int:
         return lib().mars_query_ctx_stream(self.handle)
@@ -339,13 +388,15 @@ class QueryContext:
 
     def query_device(self, store: Store, d_query, t_q, cfg, d_out, d_count, stream=None):
         _check(lib().mars_query_device(store.handle, self.handle, _ptr(d_query), float(t_q),
-                                       C.byref(cfg), _ptr(d_out), _ptr(d_count), stream))
+                                       C.byref(cfg), _ptr(d_out), _ptr(d_count),
+                                       _stream(stream, d_query, d_out, d_count)))
 
     def scan_topk(self, store: Store, d_query, t_q, lam, K, d_ids, d_vals, d_count=None,
                   modality_filter=-1, use_importance=False, row_offset=0, stream=None):
         _check(lib().mars_scan_topk(store.handle, self.handle, _ptr(d_query), float(t_q),
                                     float(lam), modality_filter, int(use_importance), K,
-                                    row_offset, _ptr(d_ids), _ptr(d_vals), _ptr(d_count), stream))
+                                    row_offset, _ptr(d_ids), _ptr(d_vals), _ptr(d_count),
+                                    _stream(stream, d_query, d_ids, d_vals, d_count)))
 
     def scan_topk_multi(self, store: Store, d_queries, nq, t_q, lam, K, d_ids, d_vals, d_counts=None,
                         modality_filter=-1, use_importance=False, row_offset=0, stream=None, query_pitch=None):
@@ -354,27 +405,41 @@ class QueryContext:
                                                              else store.dim)
         _check(lib().mars_scan_topk_multi(store.handle, self.handle, _ptr(d_queries), int(pitch), int(nq),
                                           float(t_q), float(lam), modality_filter, int(use_importance), K,
-                                          row_offset, _ptr(d_ids), _ptr(d_vals), _ptr(d_counts), stream))
+                                          row_offset, _ptr(d_ids), _ptr(d_vals), _ptr(d_counts),
+                                          _stream(stream, d_queries, d_ids, d_vals, d_counts)))
+
+    def scan_topk_f16(self, store: Store, d_queries, nq, t_q, lam, K, d_ids, d_vals, d_counts=None,
+                      modality_filter=-1, use_importance=False, row_offset=0, stream=None, query_pitch=None):
+        """scan_topk_multi's results from the store's fp16 copy (exact: fp16 only filters)."""
+        pitch = query_pitch if query_pitch is not None else (d_queries.stride(0) if hasattr(d_queries, "stride")
+                                                             else store.dim)
+        _check(lib().mars_scan_topk_f16(store.handle, self.handle, _ptr(d_queries), int(pitch), int(nq),
+                                        float(t_q), float(lam), modality_filter, int(use_importance), K,
+                                        row_offset, _ptr(d_ids), _ptr(d_vals), _ptr(d_counts),
+                                        _stream(stream, d_queries, d_ids, d_vals, d_counts)))
 
     def topk_merge(self, d_ids_in, d_vals_in, n_lists, K, d_ids_out, d_vals_out, d_count=None,
                    stream=None):
         _check(lib().mars_topk_merge(self.handle, _ptr(d_ids_in), _ptr(d_vals_in), n_lists, K,
-                                     _ptr(d_ids_out), _ptr(d_vals_out), _ptr(d_count), stream))
+                                     _ptr(d_ids_out), _ptr(d_vals_out), _ptr(d_count),
+                                     _stream(stream, d_ids_in, d_vals_in, d_ids_out, d_vals_out, d_count)))
 
     def topk_merge_batch(self, d_ids_in, d_vals_in, n_lists, K, Q, d_ids_out, d_vals_out,
                          d_counts=None, stream=None):
         _check(lib().mars_topk_merge_batch(self.handle, _ptr(d_ids_in), _ptr(d_vals_in), n_lists,
                                            K, Q, _ptr(d_ids_out), _ptr(d_vals_out),
-                                           _ptr(d_counts), stream))
+                                           _ptr(d_counts),
+                                           _stream(stream, d_ids_in, d_vals_in, d_ids_out, d_vals_out, d_counts)))
 
     def novelty(self, store: Store, d_query, d_max, stream=None):
-        _check(lib().mars_novelty(store.handle, self.handle, _ptr(d_query), _ptr(d_max), stream))
+        _check(lib().mars_novelty(store.handle, self.handle, _ptr(d_query), _ptr(d_max),
+        _stream(stream, d_query, d_max)))
 
     def debug_fused_scores(self, store: Store, d_query, t_q, lam, d_out, modality_filter=-1,
                            use_importance=False, stream=None):
         _check(lib().mars_debug_fused_scores(store.handle, self.handle, _ptr(d_query), float(t_q),
                                              float(lam), modality_filter, int(use_importance),
-                                             _ptr(d_out), stream))
+                                             _ptr(d_out), _stream(stream, d_query, d_out)))
 
     def close(self):
         if getattr(self, "handle", None):
@@ -407,7 +472,8 @@ class BatchContext:
         _check(lib().mars_query_batch_topk(store.handle, self.handle, _ptr(d_queries), pitch, B,
                                            float(t_q), float(lam), modality_filter,
                                            int(use_importance), K, row_offset, _ptr(d_ids),
-                                           _ptr(d_vals), _ptr(d_counts), stream))
+                                           _ptr(d_vals), _ptr(d_counts),
+                                           _stream(stream, d_queries, d_ids, d_vals, d_counts)))
 
     def last_stats(self):
         st = BatchStats()
@@ -454,7 +520,8 @@ def cmng_search_batch(store: Store, d_neighbors, degree, d_queries, nq, t_q, cfg
     _check(lib().mars_cmng_search_batch(store.handle, _ptr(d_neighbors), degree, _ptr(d_queries),
                                         pitch, nq, float(t_q), C.byref(cfg), _ptr(d_ids),
                                         _ptr(d_scores), _ptr(d_mods), _ptr(d_counts),
-                                        _ptr(d_iters), _ptr(d_scored), stream))
+                                        _ptr(d_iters), _ptr(d_scored),
+                                        _stream(stream, d_neighbors, d_queries, d_ids, d_scores, d_mods, d_counts, d_iters, d_scored)))
 
 
 class CmngContext:
@@ -475,7 +542,8 @@ class CmngContext:
                                                 bfs_hops, float(bfs_score_decay),
                                                 int(use_importance), _ptr(d_ids), _ptr(d_scores),
                                                 _ptr(d_mods), _ptr(d_hops), _ptr(d_counts),
-                                                _ptr(d_visited), stream))
+                                                _ptr(d_visited),
+                                                _stream(stream, d_neighbors, d_queries, d_ids, d_scores, d_mods, d_hops, d_counts, d_visited)))
 
     def close(self):
         if getattr(self, "handle", None):
@@ -498,7 +566,8 @@ def scan_topk_noalloc(d_embeddings, row_pitch, d_timestamps, d_importance, d_mod
                                         _ptr(d_importance), _ptr(d_modalities), n, dim,
                                         _ptr(d_query), float(t_q), float(lam), modality_filter,
                                         int(use_importance), K, row_offset, _ptr(d_ids),
-                                        _ptr(d_vals), _ptr(d_count), stream))
+                                        _ptr(d_vals), _ptr(d_count),
+                                        _stream(stream, d_embeddings, d_timestamps, d_importance, d_modalities, d_query, d_ids, d_vals, d_count)))
 
 
 def query_once(store: Store, q, t_q, cfg: RetrievalConfig | None = None):

@@ -242,6 +242,31 @@ int mars_scan_topk_multi(const mars_store* s, mars_query_ctx* ctx, const float* 
                          int32_t row_offset, int32_t* d_ids, float* d_vals, int32_t* d_counts,
                          void* stream);
 
+/* The same results as mars_scan_topk_multi, bit for bit, from the store's
+ * fp16 copy of its rows (2 bytes per value instead of 4).  The fp16 pass only
+ * filters: with a proven error margin it brackets every row's fused score,
+ * keeps the rows whose upper bound reaches the K-th best lower bound, and
+ * scores those exactly in fp32 with the scan's arithmetic.  The fp16 copy is
+ * made on first use (2 bytes per value of the store) and kept current.
+ * K <= 64, D <= 1024 with D % 4 == 0; otherwise, or when a value exceeds
+ * 60000, it runs mars_scan_topk_multi.  Blocks until done: queries whose
+ * candidate list overflows are answered again by the fp32 scan.  The
+ * reference's FP16 path (src/memory_cuda.cu:113-156) changes the scores; this
+ * one does not. */
+int mars_scan_topk_f16(const mars_store* s, mars_query_ctx* ctx, const float* d_queries,
+                       int32_t query_pitch, int32_t nq, float query_timestamp, float lambda,
+                       int32_t modality_filter, int32_t use_importance, int32_t K,
+                       int32_t row_offset, int32_t* d_ids, float* d_vals, int32_t* d_counts,
+                       void* stream);
+/* mars_scan_topk_f16's filter: *reruns = queries answered again with the
+ * fp32 scan because their candidate list overflowed (heavy ties, or a query
+ * too large for the bound), over the context's life; *max_candidates and
+ * *max_survivors = the largest candidate list and the largest number of rows
+ * rescored in fp32 for one query of the last call (-1: overflow).  Any
+ * pointer may be NULL. */
+int mars_query_ctx_f16_stats(const mars_query_ctx* ctx, uint64_t* reruns, int32_t* max_candidates,
+                             int32_t* max_survivors);
+
 /* Merge `n_lists` ranked lists of K (id, score) pairs that sit back to back
  * in device memory (e.g. the gather buffer of an all-gather of per-shard
  * mars_scan_topk results) into one ranked list of K.  Ties by id. */
