@@ -333,21 +333,82 @@ __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch,
     }
 }
 
-// theta[q] = the j-th best sampled lower bound of query q.
-__global__ void threshold_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tiles,
-                                 int32_t B, int32_t j, float* __restrict__ theta) {
-    const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-    if (warp >= B) return;
-    WarpTopK<1> top;
-    top.init(j);
+// theta[q] = the j-th best sampled lower bound of query q (-inf when fewer
+// than j exist).  One block per query: a radix selection on the
+// order-preserving keys of the n_sample_tiles * kJ sampled bounds (11, 11 and
+// 10 bits from the top), each pass a shared histogram of the keys that share
+// the prefix chosen so far.
+constexpr int kThrThreads = 256;
+
+__global__ void __launch_bounds__(kThrThreads)
+threshold_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tiles, int32_t B, int32_t j,
+                 float* __restrict__ theta) {
+    __shared__ int hist[2048];
+    __shared__ uint32_t s_prefix;
+    __shared__ int s_rem, s_valid;
+    const int q = blockIdx.x;
+    const int lane = threadIdx.x & 31;
     const int total = n_sample_tiles * kJ;
-    for (int base = 0; base < total; base += 32) {
-        const int i = base + lane;
-        float v = -INFINITY;
-        if (i < total) v = sample_buf[((int64_t)(i / kJ) * B + warp) * kJ + (i % kJ)];
-        top.offer_lanes(v, i, i < total && v > -INFINITY, lane);
+    uint32_t prefix = 0, pmask = 0;
+    int rem = j;
+    if (threadIdx.x == 0) s_valid = 0;
+#pragma unroll 1
+    for (int pass = 0; pass < 3; ++pass) {
+        const int sh = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
+        const int nb = pass == 2 ? 1024 : 2048;
+        for (int i = threadIdx.x; i < nb; i += kThrThreads) hist[i] = 0;
+        __syncthreads();
+        int valid = 0;
+        for (int i = threadIdx.x; i < total; i += kThrThreads) {
+            const float v = sample_buf[((int64_t)(i / kJ) * B + q) * kJ + (i % kJ)];
+            if (!(v > -INFINITY)) continue;   // empty slot
+            ++valid;
+            const uint32_t k = f2key(v);
+            if ((k & pmask) == prefix) atomicAdd(&hist[(k >> sh) & (nb - 1)], 1);
+        }
+        if (pass == 0) {
+            valid = warp_reduce_sum_int(valid);
+            if (lane == 0) atomicAdd(&s_valid, valid);
+        }
+        __syncthreads();
+        if (s_valid < j) {
+            if (threadIdx.x == 0) theta[q] = -INFINITY;
+            return;
+        }
+        // the bucket holding the rem-th largest key: warp 0, lane l sums the
+        // l-th group of nb / 32 buckets counted from the top
+        if (threadIdx.x < 32) {
+            const int per = nb / 32;
+            const int top = nb - lane * per;
+            int sum = 0;
+            for (int b = top - 1; b >= top - per; --b) sum += hist[b];
+            int incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += t;
+            }
+            const int excl = incl - sum;
+            const unsigned mine = __ballot_sync(0xffffffffu, excl < rem && rem <= incl);
+            if (lane == __ffs(mine) - 1) {
+                int acc = excl;
+                for (int b = top - 1; b >= top - per; --b) {
+                    if (acc + hist[b] >= rem) {
+                        s_prefix = prefix | ((uint32_t)b << sh);
+                        s_rem = rem - acc;
+                        break;
+                    }
+                    acc += hist[b];
+                }
+            }
+        }
+        __syncthreads();
+        prefix = s_prefix;
+        rem = s_rem;
+        pmask |= (uint32_t)(nb - 1) << sh;
+        __syncthreads();
     }
-    if (lane == 0) theta[warp] = top.thr_v;   // -inf when fewer than j values exist
+    if (threadIdx.x == 0) theta[q] = key2f(prefix);
 }
 
 // Exact rescoring of candidates: one block per query.
@@ -718,8 +779,13 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     const int32_t qtiles = (B + kBM - 1) / kBM;
     int32_t nkb = (s->pitch + kBK - 1) / kBK;
 
-    // sample size: about mu = 2 expected true top-K members in the sample
-    int32_t n_sample = (int32_t)std::ceil(2.0 * (double)n / ((double)K * kBN));
+    // sample size: one row tile in 48.  The threshold is the j-th best
+    // sampled lower bound, about the level of the 48 j best rows of the
+    // whole store, so a few hundred candidates per query whatever K is (the
+    // rescore sorts up to kSortCap); mu, the expected number of true top-K
+    // members in the sample, sets j so the threshold stays below the K-th
+    // score with high probability (else the query is rescanned exactly).
+    int32_t n_sample = (int32_t)std::ceil((double)n / (48.0 * kBN));
     n_sample = std::max(1, std::min(n_sample, rtiles));
     const double mu = (double)K * std::min<int64_t>((int64_t)n_sample * kBN, n) / std::max(n, 1);
     const int32_t j = (int32_t)std::ceil(mu + 5.0 * std::sqrt(mu) + 3.0);
@@ -807,7 +873,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         gemm_kernel<kSample, false><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
     MARS_CUDA_TRY(cudaGetLastError());
     // 3. thresholds
-    threshold_kernel<<<(B * 32 + 255) / 256, 256, 0, st>>>(c->d_sample, n_sample, B, j, c->d_theta);
+    threshold_kernel<<<B, kThrThreads, 0, st>>>(c->d_sample, n_sample, B, j, c->d_theta);
     MARS_CUDA_TRY(cudaGetLastError());
     // 4. candidates
     ga.n_tiles = rtiles * qtiles;

@@ -562,7 +562,11 @@ extern "C" int mars_scan_topk_multi(const mars_store* s, mars_query_ctx* c, cons
         sa.out_val = d_vals + (size_t)q0 * K;
         sa.out_idx = d_ids + (size_t)q0 * K;
         sa.out_cnt = d_counts ? d_counts + q0 : nullptr;
-        MARS_CUDA_TRY(launch_scan_multi(sa, d_queries + (size_t)q0 * query_pitch, query_pitch, n, c->scan_blocks, st));
+        // one wave for the whole launch: the queries' CTAs are all resident
+        // and walk the same rows in step, so each row comes from HBM about
+        // once and the other queries read it from L2
+        const int gx = std::max(1, c->scan_blocks / n);
+        MARS_CUDA_TRY(launch_scan_multi(sa, d_queries + (size_t)q0 * query_pitch, query_pitch, n, gx, st));
     }
     return MARS_OK;
 }

@@ -448,7 +448,11 @@ extern "C" int mars_scan_topk_f16(const mars_store* s, mars_query_ctx* c, const 
         a.out_val = d_vals + (size_t)q0 * K;
         a.out_idx = d_ids + (size_t)q0 * K;
         a.out_cnt = d_counts ? d_counts + q0 : nullptr;
-        MARS_CUDA_TRY(launch_scan16(p, c->scan_blocks, n, st));
+        // one wave (two CTAs per SM) for the whole launch: the queries walk
+        // the same rows in step and share them through L2, and each warp's
+        // longer row range lets its threshold settle (fewer candidates)
+        const int gx = std::max(1, std::min(c->scan_blocks, 2 * c->num_sms / n));
+        MARS_CUDA_TRY(launch_scan16(p, gx, n, st));
         MARS_CUDA_TRY(cudaMemcpyAsync(c->h_f16_overflow, c->d_f16_overflow, 3 * kF16Slots * sizeof(int32_t),
                                       cudaMemcpyDeviceToHost, st));
         MARS_CUDA_TRY(cudaStreamSynchronize(st));
