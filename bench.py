@@ -1,22 +1,28 @@
 #!/usr/bin/env python
-"""MARS B200 benchmark: fused score x decay x importance -> top-K scan.
+"""MARS B200 benchmark: exact retrieval top-K (cosine x decay x importance).
 
 Workload (the metric of BASELINE.json: queries/s + p99 at N=1M, D=768, K=10,
 HBM GB/s vs peak):
   * corpus N = 1,000,000 rows x D = 768 fp32, i.i.d. Gaussian rows divided by
     (||v|| + 1e-8), timestamps U[0, 600] s, importance U[0, 1], 4 modalities;
     seeded synthetic data (no dataset is involved);
-  * every query is one fused scan (dot x exp(-lambda * age) x importance) over
-    all N rows with top-K = 10, lambda = 0.01; a step is 16 such queries;
+  * a step is 16 concurrent queries, each the exact top-K = 10 of
+    dot x exp(-lambda * age) x importance over all N rows, lambda = 0.01,
+    answered by mars_query_batch_topk (an fp16 tensor-core short list with a
+    proven error margin, then an exact fp32 rescore: the results are those of
+    the fp32 fused scan bit for bit, which the run checks);
   * N GPUs: the corpus is row-sharded (strong scaling: total N fixed); each
-    GPU scans its shard, the per-query local top-K lists are all-gathered over
-    NCCL and merged on every GPU.
+    GPU answers the step's queries on its shard, the per-query local top-K
+    lists are all-gathered over NCCL and merged on every GPU.
 
 `value` is queries/s with queries and corpus resident in HBM, timed with CUDA
-events on the scan stream (max over ranks).  `e2e` goes through the C ABI with
-host buffers: queries copied host->device and results device->host inside the
-timed region.  `--impl reference` times the CPU implementation of the same
-path (the oracle port) on the host cores.
+events on the query stream (max over ranks).  `e2e` goes through the public
+API with host buffers: queries copied host->device and results device->host
+inside the timed region.  `latency_us` is the single-query p50/p99 of
+mars_query (host in, host out).  `fused_scan` reports the fp32 fused scan
+kernel, one query per launch, against the HBM roofline.  `--impl reference`
+times the CPU implementation of the same path (the oracle port) on the host
+cores.
 """
 from __future__ import annotations
 
@@ -72,19 +78,21 @@ def dist_env():
 
 
 def metric_name(a):
-    return (f"queries/s (fused score*decay*importance top-K scan, N={a.n}, D={a.dim}, "
-            f"K={a.k})")
+    return (f"queries/s (exact top-K of cosine*exp(-lambda*age)*importance over all rows, "
+            f"N={a.n}, D={a.dim}, K={a.k})")
 
 
 def config_dict(a, world):
     return {
-        "workload": f"fused_scan_topk N={a.n} D={a.dim} K={a.k}: one scan of all rows per query, "
-                    f"{a.queries_per_step} queries per step (one multi-query launch)",
+        "workload": f"retrieval N={a.n} D={a.dim} K={a.k}: {a.queries_per_step} concurrent queries "
+                    f"per step, each the exact top-K over all rows (mars_query_batch_topk: "
+                    f"fp16 tensor-core short list + exact fp32 rescore; results bit-identical "
+                    f"to the fp32 fused scan)",
         "n_rows": a.n, "dim": a.dim, "top_k": a.k, "queries_per_step": a.queries_per_step,
         "lambda": a.lam, "importance": True, "shards": world,
         "parallelism": f"row-shard x{world}" + (" + NCCL all-gather + merge" if world > 1 else ""),
-        "l2": "inputs larger than L2: each query streams "
-              f"{a.n // world * (a.dim * 4 + 8) / 1e9:.3f} GB per GPU (L2 126 MB)",
+        "l2": "inputs larger than L2: each step streams the fp16 rows, "
+              f"{a.n // world * ((a.dim + 7) // 8 * 16 + 4) / 1e9:.3f} GB per GPU (L2 126 MB)",
     }
 
 
@@ -99,8 +107,8 @@ def measured_peak():
 
 
 def committed_traffic():
-    """dram bytes per scan launch from the committed ncu summary (or None)."""
-    p = os.path.join(ROOT, "profiles", "scan_topk_traffic.json")
+    """dram bytes per candidates-pass launch from the committed ncu summary (or None)."""
+    p = os.path.join(ROOT, "profiles", "batch_gemm_traffic.json")
     try:
         with open(p) as f:
             return json.load(f)
@@ -239,9 +247,10 @@ def run_mars(a):
     store = mb.Store(n_local, a.dim, device=local)
     store.upload(E, mod, ts, imp)
     ctx = mb.QueryContext(n_local, a.dim, max_k=a.k, device=local)
+    K, Q = a.k, a.queries_per_step
+    bc = mb.BatchContext(n_local, a.dim, max_batch=Q, max_k=K, device=local)
     stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
     torch.cuda.set_stream(stream)
-    K, Q = a.k, a.queries_per_step
     Qd = torch.from_numpy(Qh).cuda()
     ids = torch.empty((Q, K), dtype=torch.int32, device="cuda")
     vals = torch.empty((Q, K), dtype=torch.float32, device="cuda")
@@ -253,27 +262,23 @@ def run_mars(a):
     n_ev = a.steps + a.warmup
     ev_a = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
     ev_b = [torch.cuda.Event(enable_timing=True) for _ in range(n_ev)]
-    st_a = [torch.cuda.Event(enable_timing=True) for _ in range(a.steps + a.warmup)]
-    st_b = [torch.cuda.Event(enable_timing=True) for _ in range(a.steps + a.warmup)]
 
-    def step(i, timed_events=True):
-        # one step: Q single-query scans of all rows, issued as one
-        # multi-query launch (every query still reads every row)
-        if timed_events:
-            st_a[i].record(stream)
+    def batch(q, out_ids, out_vals):
+        bc.query_batch_topk(store, q, Q, a.ts_max, a.lam, K, out_ids, out_vals, use_importance=True,
+                            row_offset=lo, stream=ctx.stream)
+
+    def step(i):
+        # one step: Q concurrent queries, each the exact top-K of the fused
+        # score over every row of the shard (mars_query_batch_topk: fp16
+        # tensor-core short list, exact fp32 rescore)
         base = (i * Q) % (Qd.shape[0] - Q + 1)
-        if timed_events:
-            ev_a[i].record(stream)
-        ctx.scan_topk_multi(store, Qd[base:base + Q], Q, a.ts_max, a.lam, K, ids, vals,
-                            use_importance=True, row_offset=lo, stream=ctx.stream)
-        if timed_events:
-            ev_b[i].record(stream)
+        ev_a[i].record(stream)
+        batch(Qd[base:base + Q], ids, vals)
         if world > 1:
             dist.all_gather_into_tensor(gids, ids)
             dist.all_gather_into_tensor(gvals, vals)
             ctx.topk_merge_batch(gids, gvals, world, K, Q, mids, mvals, stream=ctx.stream)
-        if timed_events:
-            st_b[i].record(stream)
+        ev_b[i].record(stream)
 
     def barrier():
         torch.cuda.synchronize()
@@ -298,110 +303,144 @@ def run_mars(a):
     barrier()
     clocks = sampler.stop() if sampler else None
     elapsed_ms = t_start.elapsed_time(t_end)
-    multi_ms = [ev_a[i].elapsed_time(ev_b[i]) for i in range(a.steps)]
-    # single-query latency: one query per launch, outside the timed region
-    scan_ms = []
-    l0, l1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    for j in range(64):
-        l0.record(stream)
-        ctx.scan_topk(store, Qd[j % Qd.shape[0]], a.ts_max, a.lam, K, ids[0], vals[0],
-                      use_importance=True, row_offset=lo, stream=ctx.stream)
-        l1.record(stream)
-        l1.synchronize()
-        scan_ms.append(l0.elapsed_time(l1))
-    step_ms = [st_a[i].elapsed_time(st_b[i]) for i in range(a.steps)]
+    step_ms = [ev_a[i].elapsed_time(ev_b[i]) for i in range(a.steps)]
     if world > 1:
         t = torch.tensor([elapsed_ms], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         elapsed_ms = float(t.item())
 
-    # correctness spot check of the last step against a local recompute (rank 0)
-    ok = True
-    if world > 1:
+    # ---- outside the timed region ------------------------------------------
+    # the dominant kernel (the candidates pass) timed by the library's CUDA
+    # events on the call's stream
+    gemm_ms, bstats = [], None
+    for j in range(10):
+        batch(Qd[:Q], ids, vals)
+        bstats = bc.last_stats()
+        gemm_ms.append(bstats["gemm_ms"])
+    # exactness: the step's answers against the fp32 fused scan, bit for bit
+    ref_ids = torch.empty_like(ids)
+    ref_vals = torch.empty_like(vals)
+    exact = True
+    for base in (0, 16, 48):
+        q = Qd[base:base + Q]
+        batch(q, ids, vals)
+        ctx.scan_topk_multi(store, q, Q, a.ts_max, a.lam, K, ref_ids, ref_vals, use_importance=True,
+                            row_offset=lo, stream=ctx.stream)
         torch.cuda.synchronize()
+        exact = exact and torch.equal(ids, ref_ids) and torch.equal(vals.view(torch.int32),
+                                                                    ref_vals.view(torch.int32))
+    if world > 1:
+        t = torch.tensor([1 if exact else 0], dtype=torch.int32, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MIN)
+        exact = bool(t.item())
 
-    # ---- end to end through the C ABI with host buffers ---------------------
-    e2e = None
-    pitch = (a.dim + 3) // 4 * 4
-    if world == 1:
-        cfg = mb.RetrievalConfig(top_k=K, bfs_max_hops=0, time_decay_lambda=a.lam,
-                                 use_importance=True)
-        for i in range(3):
-            ctx.query(store, Qh[i], a.ts_max, cfg)
-        lat = []
-        t0 = time.perf_counter()
-        for s in range(a.steps):
-            for j in range(Q):
-                c0 = time.perf_counter()
-                ctx.query(store, Qh[(s * Q + j) % 64], a.ts_max, cfg)
-                lat.append(time.perf_counter() - c0)
-        dt = time.perf_counter() - t0
-        e2e = {"value": a.steps * Q / dt, "unit": "queries/s",
-               "h2d_bytes_per_step": Q * (64 + pitch * 4), "d2h_bytes_per_step": Q * (K * 16 + 8),
-               "p50_us": float(np.percentile(lat, 50) * 1e6),
-               "p99_us": float(np.percentile(lat, 99) * 1e6),
-               "path": "mars_query (C ABI) per query: query in the launch's parameter block, "
-                       "one kernel (scan + selection), K results read from mapped host memory"}
-    else:
-        Qpin = torch.from_numpy(Qh).pin_memory()
-        qbuf = torch.empty((Q, a.dim), dtype=torch.float32, device="cuda")
-        out_ids = torch.empty((Q, K), dtype=torch.int32).pin_memory()
-        out_vals = torch.empty((Q, K), dtype=torch.float32).pin_memory()
-        barrier()
-        t0 = time.perf_counter()
-        for s in range(a.steps):
-            base = (s * Q) % (64 - Q + 1)
-            qbuf.copy_(Qpin[base:base + Q], non_blocking=True)
-            ctx.scan_topk_multi(store, qbuf, Q, a.ts_max, a.lam, K, ids, vals,
-                                use_importance=True, row_offset=lo, stream=ctx.stream)
+    # the fused scan: one query per launch (the HBM-bound kernel), the
+    # multi-query launch of the step's queries, and its fp16-filtered form
+    def timed(fn, reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        out = []
+        for _ in range(reps):
+            e0.record(stream)
+            fn()
+            e1.record(stream)
+            e1.synchronize()
+            out.append(e0.elapsed_time(e1))
+        return out
+    scan_ms = timed(lambda: ctx.scan_topk(store, Qd[0], a.ts_max, a.lam, K, ids[0], vals[0],
+                                          use_importance=True, row_offset=lo, stream=ctx.stream), 64)
+    multi_ms = timed(lambda: ctx.scan_topk_multi(store, Qd[:Q], Q, a.ts_max, a.lam, K, ids, vals,
+                                                 use_importance=True, row_offset=lo, stream=ctx.stream), 8)
+    f16_ms = timed(lambda: ctx.scan_topk_f16(store, Qd[:Q], Q, a.ts_max, a.lam, K, ids, vals,
+                                             use_importance=True, row_offset=lo, stream=ctx.stream), 8)
+
+    # ---- end to end through the public API with host buffers --------------
+    Qpin = torch.from_numpy(Qh).pin_memory()
+    qbuf = torch.empty((Q, a.dim), dtype=torch.float32, device="cuda")
+    out_ids = torch.empty((Q, K), dtype=torch.int32).pin_memory()
+    out_vals = torch.empty((Q, K), dtype=torch.float32).pin_memory()
+    res_ids, res_vals = (mids, mvals) if world > 1 else (ids, vals)
+    barrier()
+    t0 = time.perf_counter()
+    for s in range(a.steps):
+        base = (s * Q) % (64 - Q + 1)
+        qbuf.copy_(Qpin[base:base + Q], non_blocking=True)
+        batch(qbuf, ids, vals)
+        if world > 1:
             dist.all_gather_into_tensor(gids, ids)
             dist.all_gather_into_tensor(gvals, vals)
             ctx.topk_merge_batch(gids, gvals, world, K, Q, mids, mvals, stream=ctx.stream)
-            out_ids.copy_(mids, non_blocking=True)
-            out_vals.copy_(mvals, non_blocking=True)
-            stream.synchronize()
-        dt = time.perf_counter() - t0
+        out_ids.copy_(res_ids, non_blocking=True)
+        out_vals.copy_(res_vals, non_blocking=True)
+        stream.synchronize()
+    dt = time.perf_counter() - t0
+    if world > 1:
         t = torch.tensor([dt], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = float(t.item())
-        e2e = {"value": a.steps * Q / dt, "unit": "queries/s",
-               "h2d_bytes_per_step": Q * a.dim * 4, "d2h_bytes_per_step": Q * K * 8,
-               "path": "pinned H2D of queries, mars_scan_topk_multi per shard, NCCL all-gather, "
-                       "mars_topk_merge_batch, D2H of merged top-K"}
+    e2e = {"value": a.steps * Q / dt, "unit": "queries/s",
+           "h2d_bytes_per_step": Q * a.dim * 4, "d2h_bytes_per_step": Q * K * 8,
+           "path": "pinned H2D of the step's queries, mars_query_batch_topk"
+                   + (" per shard, NCCL all-gather, mars_topk_merge_batch" if world > 1 else "")
+                   + ", D2H of the top-K ids and scores, stream synchronize"}
+    latency = None
+    if world == 1:
+        # single-query latency through mars_query (host query in, host results out)
+        cfg = mb.RetrievalConfig(top_k=K, bfs_max_hops=0, time_decay_lambda=a.lam, use_importance=True)
+        for i in range(3):
+            ctx.query(store, Qh[i], a.ts_max, cfg)
+        lat = []
+        for j in range(256):
+            c0 = time.perf_counter()
+            ctx.query(store, Qh[j % 64], a.ts_max, cfg)
+            lat.append(time.perf_counter() - c0)
+        latency = {"path": "mars_query (C ABI), one query, host in / host out, N=%d" % n_local,
+                   "p50_us": float(np.percentile(lat, 50) * 1e6),
+                   "p99_us": float(np.percentile(lat, 99) * 1e6)}
 
     if rank == 0:
         peak, peak_kind = measured_peak()
-        # the dominant kernel: the multi-query scan, Q queries per launch
-        bytes_per_launch = Q * n_local * (a.dim * 4 + 4 + 4)
-        mean_multi_ms = statistics.mean(multi_ms)
-        achieved = bytes_per_launch / (mean_multi_ms * 1e-3) / 1e9
+        pitch16 = (a.dim + 7) // 8 * 8
+        qtiles = (Q + 127) // 128
+        gemm_bytes = qtiles * n_local * (pitch16 * 2 + 4)
+        mean_gemm = statistics.mean(gemm_ms)
+        achieved = gemm_bytes / (mean_gemm * 1e-3) / 1e9
         tr = committed_traffic()
         traffic = None
         if tr and tr.get("n_rows") and tr.get("dram_bytes"):
-            traffic = tr["dram_bytes"] * Q * n_local / tr["n_rows"]
+            traffic = tr["dram_bytes"] * n_local / tr["n_rows"]
+        scan_bytes = n_local * (a.dim * 4 + 4 + 4)
+        scan_med = float(np.median(scan_ms))
         qps = a.steps * Q / (elapsed_ms * 1e-3)
         line = {
             "metric": metric_name(a), "value": qps, "unit": "queries/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": elapsed_ms / a.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "f32 results (exact; fp16 tensor-core short list, fp32 rescore)",
             "data": "synthetic (seeded Gaussian corpus and queries)",
             "config": config_dict(a, world),
-            "latency_us": {
-                "note": "scan_kernel_*: one query per launch (event-timed, outside the timed "
-                        "region); multi_launch_*: the step's launch of Q queries",
-                "scan_kernel_p50": float(np.percentile(scan_ms, 50) * 1e3),
-                "scan_kernel_p99": float(np.percentile(scan_ms, 99) * 1e3),
-                "multi_launch_p50": float(np.percentile(multi_ms, 50) * 1e3),
-                "multi_launch_p99": float(np.percentile(multi_ms, 99) * 1e3),
-                "step_p50": float(np.percentile(step_ms, 50) * 1e3),
-                "step_p99": float(np.percentile(step_ms, 99) * 1e3)},
+            "exact_vs_fp32_scan": exact,
+            "latency_us": latency,
+            "step_ms_p50": float(np.percentile(step_ms, 50)),
+            "step_ms_p99": float(np.percentile(step_ms, 99)),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "peak_kind": peak_kind,
-                         "traffic": traffic,
-                         "kernel": f"scan_multi_kernel ({Q} queries per launch)",
-                         "algorithmic_bytes_per_launch": bytes_per_launch},
+                         "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
+                         "kernel": "batch::gemm_kernel<kCandidates, f16> (the candidates pass)",
+                         "kernel_ms": mean_gemm,
+                         "algorithmic_bytes_per_launch": gemm_bytes,
+                         "bytes_note": "fp16 rows (pitch %d halves) once per 128-query tile plus a 4-byte "
+                                       "row weight" % pitch16},
+            "batch_stats": bstats,
+            "fused_scan": {
+                "note": "the fp32 fused scan (score x decay x importance -> top-K), event-timed "
+                        "outside the timed region",
+                "single_query_kernel_ms_p50": scan_med,
+                "single_query_kernel_ms_p99": float(np.percentile(scan_ms, 99)),
+                "single_query_hbm_gbs": scan_bytes / (scan_med * 1e-3) / 1e9,
+                "single_query_hbm_frac": scan_bytes / (scan_med * 1e-3) / 1e9 / peak,
+                "multi_query_launch_qps": Q / (float(np.median(multi_ms)) * 1e-3),
+                "f16_filtered_launch_qps": Q / (float(np.median(f16_ms)) * 1e-3)},
             "e2e": e2e,
-            "gpu_launches": a.steps * (1 + (1 if world > 1 else 0)),
+            "gpu_launches": a.steps * (7 + (1 if world > 1 else 0)),
             "clocks": clocks,
         }
         if world == 1 and not a.no_cpu_baseline:
@@ -410,7 +449,6 @@ def run_mars(a):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
-    del ok
 
 
 # ---------------------------------------------------------------------------

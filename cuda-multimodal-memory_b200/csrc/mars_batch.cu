@@ -594,6 +594,7 @@ struct mars_batch_ctx {
     int* h_err = nullptr;
     mars_query_ctx* scan_ctx = nullptr;   // exact single-query scans for fallbacks
     mars_batch_stats last{};
+    cudaEvent_t ev_gemm[2] = {nullptr, nullptr};   // around the candidates pass
 };
 
 namespace {
@@ -661,6 +662,8 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     int rc = MARS_OK;
     auto T = [&](cudaError_t e, const char* w) { if (rc == MARS_OK && e != cudaSuccess) rc = cuda_fail(e, w, __FILE__, __LINE__); };
     T(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
+    T(cudaEventCreate(&c->ev_gemm[0]), "event");
+    T(cudaEventCreate(&c->ev_gemm[1]), "event");
     T(cudaMalloc(&c->d_wts, (size_t)max_nodes * 4 + 16), "weights");
     T(cudaMalloc(&c->d_margin, (size_t)max_batch * 4), "margins");
     T(cudaMalloc(&c->d_theta, (size_t)max_batch * 4), "thresholds");
@@ -712,6 +715,8 @@ int mars_batch_ctx_destroy(mars_batch_ctx* c) {
     cudaFreeHost(c->h_fallback); cudaFreeHost(c->h_cand_cnt); cudaFreeHost(c->h_err);
     cudaFree(c->d_q16); cudaFree(c->d_bad); cudaFreeHost(c->h_bad);
     mars_query_ctx_destroy(c->scan_ctx);
+    for (cudaEvent_t e : c->ev_gemm)
+        if (e) cudaEventDestroy(e);
     if (c->stream) cudaStreamDestroy(c->stream);
     delete c;
     return MARS_OK;
@@ -877,11 +882,13 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     MARS_CUDA_TRY(cudaGetLastError());
     // 4. candidates
     ga.n_tiles = rtiles * qtiles;
+    MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
     if (f16)
         gemm_kernel<kCandidates, true><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
     else
         gemm_kernel<kCandidates, false><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
     MARS_CUDA_TRY(cudaGetLastError());
+    MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[1], st));
     // 5. rescore
     StoreView v{};
     v.E = s->d_E; v.ts = s->d_ts; v.imp = s->d_imp; v.mod = s->d_mod; v.d_n = s->d_n;
@@ -920,6 +927,9 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
                                                d_vals + (int64_t)b * K, d_counts ? d_counts + b : nullptr, st));
         }
     }
+    float gms = 0.f;
+    MARS_CUDA_TRY(cudaEventElapsedTime(&gms, c->ev_gemm[0], c->ev_gemm[1]));
+    c->last.gemm_ms = gms;
     c->last.path = f16 ? 2 : 1;
     c->last.fallbacks = fb;
     c->last.candidates = total;

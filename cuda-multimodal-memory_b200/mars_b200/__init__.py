@@ -75,7 +75,7 @@ class StoreInfo(C.Structure):
 class BatchStats(C.Structure):
     _fields_ = [("path", C.c_int32), ("fallbacks", C.c_int32), ("candidates", C.c_int64),
                 ("max_candidates", C.c_int32), ("sample_tiles", C.c_int32),
-                ("sample_rank", C.c_int32), ("rescored", C.c_int64)]
+                ("sample_rank", C.c_int32), ("rescored", C.c_int64), ("gemm_ms", C.c_float)]
 
     def as_dict(self):
         return {k: getattr(self, k) for k, _ in self._fields_}

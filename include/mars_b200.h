@@ -311,6 +311,8 @@ typedef struct mars_batch_stats {
     int32_t sample_tiles;    /* 256-row tiles in the threshold sample              */
     int32_t sample_rank;     /* rank of the sampled bound used as threshold        */
     int64_t rescored;        /* candidates rescored exactly after pruning          */
+    float   gemm_ms;         /* device time of the candidates pass (CUDA events on
+                                the call's stream; 0 on the scan path)             */
 } mars_batch_stats;
 
 int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim,
