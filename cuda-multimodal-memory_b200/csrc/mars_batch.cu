@@ -48,6 +48,7 @@
 #include "mars_common.cuh"
 #include "mars_internal.h"
 #include "mars_kernels.cuh"
+#include "mars_select.cuh"
 #include "mars_sm100.cuh"
 
 namespace mars {
@@ -290,36 +291,42 @@ __global__ void prep_rows_kernel(const float* __restrict__ ts, const float* __re
     }
 }
 
-// fp16 copies of the queries; *bad is set when a component is outside the
-// fp16 range that the error margin covers.
+// fp16 copies of the queries (prep_queries_kernel flags a query with a
+// component outside the fp16 range that the error margin covers).
 __global__ void to_f16_queries_kernel(const float* __restrict__ Q, int64_t qpitch, int32_t B, int32_t dim,
-                                      __half* __restrict__ Q16, int64_t pitch16, int* __restrict__ bad) {
+                                      __half* __restrict__ Q16, int64_t pitch16) {
     const int64_t total = (int64_t)B * pitch16;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t b = i / pitch16, d = i % pitch16;
-        float x = 0.0f;
-        if (d < dim) {
-            x = Q[b * qpitch + d];
-            if (!(fabsf(x) <= kF16Max)) atomicExch(bad, 1);
-        }
-        Q16[b * pitch16 + d] = __float2half_rn(x);
+        Q16[b * pitch16 + d] = __float2half_rn(d < dim ? Q[b * qpitch + d] : 0.0f);
     }
 }
 
+// Per query: the error margin, the fp16 range flag, and the per-call
+// counters zeroed (candidate count, rescored count; the error word by query 0).
 __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch, int32_t B, int32_t nc,
                                     const unsigned int* __restrict__ norm_bits, int32_t f16,
-                                    float* __restrict__ margin, int32_t* __restrict__ cand_cnt) {
+                                    float* __restrict__ margin, int32_t* __restrict__ cand_cnt,
+                                    int32_t* __restrict__ rescored, int32_t* __restrict__ bad,
+                                    int32_t* __restrict__ err) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= B) return;
     const float4* q = reinterpret_cast<const float4*>(Q + (int64_t)warp * qpitch);
     float s = 0.f;
+    bool out = false;
     for (int c = lane; c < nc; c += 32) {
         const float4 v = q[c];
         s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        out = out || !(fabsf(v.x) <= kF16Max) || !(fabsf(v.y) <= kF16Max) || !(fabsf(v.z) <= kF16Max) ||
+              !(fabsf(v.w) <= kF16Max);
     }
     s = warp_butterfly_sum(s);
+    out = __any_sync(0xffffffffu, out);
     if (lane == 0) {
+        bad[warp] = out ? 1 : 0;
+        rescored[warp] = 0;
+        if (warp == 0) *err = 0;
         // 1.0001: covers the fp32 rounding of this norm itself
         const float qn = sqrtf(s) * 1.0001f, en = __uint_as_float(*norm_bits);
         float mg = kMarginRel * qn * en;
@@ -334,81 +341,35 @@ __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch,
 }
 
 // theta[q] = the j-th best sampled lower bound of query q (-inf when fewer
-// than j exist).  One block per query: a radix selection on the
-// order-preserving keys of the n_sample_tiles * kJ sampled bounds (11, 11 and
-// 10 bits from the top), each pass a shared histogram of the keys that share
-// the prefix chosen so far.
+// than j exist): one block per query, a radix selection
+// (block_kth_largest_key) over the n_sample_tiles * per_tile sampled bounds
+// (layout [tile][query][per_tile]), empty slots (-inf) left out.
 constexpr int kThrThreads = 256;
 
 __global__ void __launch_bounds__(kThrThreads)
 threshold_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tiles, int32_t B, int32_t j,
-                 float* __restrict__ theta) {
+                 int32_t per_tile, float* __restrict__ theta) {
     __shared__ int hist[2048];
-    __shared__ uint32_t s_prefix;
-    __shared__ int s_rem, s_valid;
+    __shared__ uint32_t s_sel[2];
+    __shared__ int s_valid;
     const int q = blockIdx.x;
-    const int lane = threadIdx.x & 31;
-    const int total = n_sample_tiles * kJ;
-    uint32_t prefix = 0, pmask = 0;
-    int rem = j;
+    const int total = n_sample_tiles * per_tile;
+    auto at = [&](int i) { return sample_buf[((int64_t)(i / per_tile) * B + q) * per_tile + (i % per_tile)]; };
     if (threadIdx.x == 0) s_valid = 0;
-#pragma unroll 1
-    for (int pass = 0; pass < 3; ++pass) {
-        const int sh = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
-        const int nb = pass == 2 ? 1024 : 2048;
-        for (int i = threadIdx.x; i < nb; i += kThrThreads) hist[i] = 0;
-        __syncthreads();
-        int valid = 0;
-        for (int i = threadIdx.x; i < total; i += kThrThreads) {
-            const float v = sample_buf[((int64_t)(i / kJ) * B + q) * kJ + (i % kJ)];
-            if (!(v > -INFINITY)) continue;   // empty slot
-            ++valid;
-            const uint32_t k = f2key(v);
-            if ((k & pmask) == prefix) atomicAdd(&hist[(k >> sh) & (nb - 1)], 1);
-        }
-        if (pass == 0) {
-            valid = warp_reduce_sum_int(valid);
-            if (lane == 0) atomicAdd(&s_valid, valid);
-        }
-        __syncthreads();
-        if (s_valid < j) {
-            if (threadIdx.x == 0) theta[q] = -INFINITY;
-            return;
-        }
-        // the bucket holding the rem-th largest key: warp 0, lane l sums the
-        // l-th group of nb / 32 buckets counted from the top
-        if (threadIdx.x < 32) {
-            const int per = nb / 32;
-            const int top = nb - lane * per;
-            int sum = 0;
-            for (int b = top - 1; b >= top - per; --b) sum += hist[b];
-            int incl = sum;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const int t = __shfl_up_sync(0xffffffffu, incl, o);
-                if (lane >= o) incl += t;
-            }
-            const int excl = incl - sum;
-            const unsigned mine = __ballot_sync(0xffffffffu, excl < rem && rem <= incl);
-            if (lane == __ffs(mine) - 1) {
-                int acc = excl;
-                for (int b = top - 1; b >= top - per; --b) {
-                    if (acc + hist[b] >= rem) {
-                        s_prefix = prefix | ((uint32_t)b << sh);
-                        s_rem = rem - acc;
-                        break;
-                    }
-                    acc += hist[b];
-                }
-            }
-        }
-        __syncthreads();
-        prefix = s_prefix;
-        rem = s_rem;
-        pmask |= (uint32_t)(nb - 1) << sh;
-        __syncthreads();
+    __syncthreads();
+    int valid = 0;
+    for (int i = threadIdx.x; i < total; i += kThrThreads) valid += at(i) > -INFINITY ? 1 : 0;
+    valid = warp_reduce_sum_int(valid);
+    if ((threadIdx.x & 31) == 0) atomicAdd(&s_valid, valid);
+    __syncthreads();
+    if (s_valid < j) {
+        if (threadIdx.x == 0) theta[q] = -INFINITY;
+        return;
     }
-    if (threadIdx.x == 0) theta[q] = key2f(prefix);
+    // empty slots map to key 0, below every valid bound
+    const uint32_t key = block_kth_largest_key<kThrThreads>(
+        [&](int i) { const float v = at(i); return v > -INFINITY ? f2key(v) : 0u; }, total, j, hist, s_sel);
+    if (threadIdx.x == 0) theta[q] = key2f(key);
 }
 
 // Exact rescoring of candidates: one block per query.
@@ -467,6 +428,8 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     __shared__ float   s_key[kSortCap];
     __shared__ int32_t s_id[kSortCap];
     __shared__ int     s_ge, s_n2;
+    __shared__ int     s_hist[2048];
+    __shared__ uint32_t s_sel[2];
     const int qi = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int kWarps = kRescoreThreads / 32;
@@ -485,18 +448,11 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     const float* cf = cand_f + (int64_t)qi * cap;
 
     // ---- pass 1: lower bounds, completeness, K-th largest lower bound -------
-    const int n1 = pow2_at_least(nc_);
     int ge = 0;
-    for (int i = threadIdx.x; i < n1; i += kRescoreThreads) {
-        float lo = -INFINITY;
-        int32_t id = INT32_MAX;
-        if (i < nc_) {
-            lo = cf[i] - m * fabsf(__ldg(wts + ci[i]));
-            id = i;
-            ge += (lo >= th) ? 1 : 0;
-        }
+    for (int i = threadIdx.x; i < nc_; i += kRescoreThreads) {
+        const float lo = cf[i] - m * fabsf(__ldg(wts + ci[i]));
+        ge += (lo >= th) ? 1 : 0;
         s_key[i] = lo;
-        s_id[i] = id;
     }
     ge = warp_reduce_sum_int(ge);
     if (lane == 0) atomicAdd(&s_ge, ge);
@@ -505,9 +461,8 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         if (threadIdx.x == 0) { fallback[qi] = 1; rescored[qi] = 0; if (out_cnt) out_cnt[qi] = 0; }
         return;
     }
-    block_bitonic_desc(s_key, s_id, n1);
-    const float th2 = s_key[K - 1];
-    __syncthreads();
+    const float th2 = key2f(block_kth_largest_key<kRescoreThreads>(
+        [&](int i) { return f2key(s_key[i]); }, nc_, K, s_hist, s_sel));
 
     // ---- pass 2: exact scores of the candidates that can still place -------
     const float4* q4 = reinterpret_cast<const float4*>(Q + (int64_t)qi * qpitch);
@@ -554,6 +509,192 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     }
 }
 
+// ---------------------------------------------------------------------------
+// Small batches (B <= kSmallMaxB queries, fp16 operands): the roles of the
+// operands swap.  A tile is 128 rows (UMMA M) x NQ queries (UMMA N = B
+// rounded up to 16), so the tensor cores do no work for absent queries, the
+// queries' fp16 k-blocks stay in shared memory for the whole kernel (loaded
+// once), and the rest of shared memory is a ring of row stages (16 KB each,
+// up to kSmallMaxStages) -- more row bytes in flight per SM than the
+// 128 x 256 tile's ring, whose stages also carry a 128-row query tile.
+// TMEM holds D[row][query] (lanes = rows, columns = queries), double
+// buffered; epilogue thread t owns row t of the tile.
+//
+// Candidates mode appends (query, row) when the row's upper bound reaches the
+// query's threshold, as gemm_kernel does.  Sample mode writes every lower
+// bound of the sampled tiles: sample_buf[tile][query][128].
+constexpr int kSmallMaxB = 64;
+constexpr int kSmallRows = 128;
+constexpr int kSmallStage = kSmallRows * 128;      // 16 KB: 128 rows x 64 halves
+constexpr int kSmallMaxStages = 12;
+
+struct SmallArgs {
+    int32_t B, NQ;                   // queries, MMA N (B rounded up to 16)
+    int32_t n, nkb;                  // rows, 64-half k-blocks
+    int32_t n_tiles;                 // 128-row tiles of this launch
+    int32_t stages;                  // row stages in the ring
+    uint32_t tmem_cols;              // columns allocated (power of two >= 2 NQ, >= 32)
+    const int32_t* sample_rt;        // sample mode: 128-row tile of sample tile i
+    const float* wts;
+    const float* theta;
+    const float* margin;
+    float* sample_buf;               // sample mode: [n_tiles][B][128]
+    int32_t* cand;
+    float* cand_f;
+    int32_t* cand_cnt;
+    int32_t cap;
+    int32_t self_base;
+    int* err;
+};
+
+__host__ __device__ constexpr size_t small_smem_bytes(int nkb, int NQ, int stages) {
+    return 1024 /*align*/ + (size_t)nkb * NQ * 128 + (size_t)stages * kSmallStage + 512 /*barriers*/;
+}
+
+template <int MODE>
+__global__ void __launch_bounds__(kThreads, 1)
+gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_e,
+                  const SmallArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int qkb_bytes = a.NQ * 128;                          // one query k-block
+    uint8_t* qs = smem;                                        // nkb query k-blocks
+    uint8_t* rs = smem + (size_t)a.nkb * qkb_bytes;            // row stages
+    uint64_t* full = reinterpret_cast<uint64_t*>(rs + (size_t)a.stages * kSmallStage);
+    uint64_t* empty = full + kSmallMaxStages;
+    uint64_t* qfull = empty + kSmallMaxStages;
+    uint64_t* tfull = qfull + 1;
+    uint64_t* tempty = tfull + 2;
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < a.stages; ++s) { sm100::mbar_init(full + s, 1); sm100::mbar_init(empty + s, 1); }
+        sm100::mbar_init(qfull, 1);
+        for (int b = 0; b < 2; ++b) { sm100::mbar_init(tfull + b, 1); sm100::mbar_init(tempty + b, 128); }
+        sm100::fence_mbar_init();
+        sm100::prefetch_tmap(&tmap_q);
+        sm100::prefetch_tmap(&tmap_e);
+    }
+    if (warp == 1) {
+        sm100::tmem_alloc(tmem_slot, a.tmem_cols);
+        sm100::tmem_relinquish();
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    sm100::tc_fence_after();
+    const uint32_t tmem_base = *tmem_slot;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            // the queries, once
+            sm100::mbar_arrive_expect_tx(qfull, (uint32_t)(a.nkb * qkb_bytes));
+            for (int kb = 0; kb < a.nkb; ++kb)
+                sm100::tma_load_2d(qs + (size_t)kb * qkb_bytes, &tmap_q, qfull, kb * 64, 0);
+            int stage = 0;
+            uint32_t phase = 0;
+            uint32_t issued_phase[kSmallMaxStages];
+            bool issued[kSmallMaxStages];
+            for (int s = 0; s < kSmallMaxStages; ++s) { issued[s] = false; issued_phase[s] = 0; }
+            bool ok = true;
+            for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
+                const int row0 = (MODE == kSample ? a.sample_rt[t] : t) * kSmallRows;
+                for (int kb = 0; kb < a.nkb; ++kb) {
+                    if (!sm100::mbar_wait(empty + stage, phase ^ 1u, a.err, 11)) { ok = false; break; }
+                    sm100::mbar_arrive_expect_tx(full + stage, kSmallStage);
+                    sm100::tma_load_2d(rs + (size_t)stage * kSmallStage, &tmap_e, full + stage, kb * 64, row0);
+                    issued[stage] = true;
+                    issued_phase[stage] = phase;
+                    if (++stage == a.stages) { stage = 0; phase ^= 1u; }
+                }
+            }
+            // every copy this thread started has landed before the CTA may exit
+            sm100::mbar_wait(qfull, 0, a.err, 12);
+            for (int s = 0; s < a.stages; ++s)
+                if (issued[s]) sm100::mbar_wait(full + s, issued_phase[s], a.err, 12);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            const uint32_t idesc = sm100::idesc_f16(kSmallRows, a.NQ);
+            bool ok = sm100::mbar_wait(qfull, 0, a.err, 13);
+            sm100::tc_fence_after();
+            const uint32_t qs_addr = sm100::smem_u32(qs);
+            int stage = 0;
+            uint32_t phase = 0;
+            int buf = 0;
+            uint32_t bphase = 0;
+            for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
+                if (!sm100::mbar_wait(tempty + buf, bphase ^ 1u, a.err, 14)) break;
+                sm100::tc_fence_after();
+                const uint32_t d = tmem_base + (uint32_t)(buf * a.NQ);
+                for (int kb = 0; kb < a.nkb; ++kb) {
+                    if (!sm100::mbar_wait(full + stage, phase, a.err, 15)) { ok = false; break; }
+                    sm100::tc_fence_after();
+                    const uint64_t da = sm100::smem_desc_sw128(sm100::smem_u32(rs + (size_t)stage * kSmallStage));
+                    const uint64_t db = sm100::smem_desc_sw128(qs_addr + (uint32_t)(kb * qkb_bytes));
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)      // 32 bytes of K (16 halves) per MMA
+                        sm100::mma_f16(d, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
+                                       (kb > 0 || k > 0) ? 1u : 0u);
+                    sm100::mma_commit(empty + stage);   // stage reusable when these MMAs finish
+                    if (++stage == a.stages) { stage = 0; phase ^= 1u; }
+                }
+                if (!ok) break;
+                sm100::mma_commit(tfull + buf);         // accumulator ready
+                if (++buf == 2) { buf = 0; bphase ^= 1u; }
+            }
+        }
+    } else {
+        // ---------------- epilogue (warps 2..5): thread = row ----------------
+        const int sub = warp & 3;                   // TMEM lane quarter of this warp
+        const int rt = sub * 32 + lane;             // row within the tile
+        int buf = 0;
+        uint32_t bphase = 0;
+        for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
+            const int row = (MODE == kSample ? a.sample_rt[t] : t) * kSmallRows + rt;
+            const float w = row < a.n ? __ldg(a.wts + row) : NAN;   // NaN: never a candidate
+            if (!sm100::mbar_wait(tfull + buf, bphase, a.err, 16)) break;
+            sm100::tc_fence_after();
+            for (int q0 = 0; q0 < a.NQ; q0 += 16) {
+                uint32_t r[16];
+                sm100::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(buf * a.NQ + q0), r);
+                sm100::tmem_ld_wait();
+#pragma unroll
+                for (int u = 0; u < 16; ++u) {
+                    const int q = q0 + u;
+                    if (q >= a.B) break;
+                    const float wq = (a.self_base >= 0 && row == a.self_base + q) ? NAN : w;
+                    const float f = __uint_as_float(r[u]) * wq;
+                    const float slack = __ldg(a.margin + q) * fabsf(wq);
+                    if (MODE == kCandidates) {
+                        if (f + slack >= __ldg(a.theta + q)) {   // NaN weights never pass
+                            const int pos = atomicAdd(a.cand_cnt + q, 1);
+                            if (pos < a.cap) {
+                                a.cand[(int64_t)q * a.cap + pos] = row;
+                                a.cand_f[(int64_t)q * a.cap + pos] = f;
+                            }
+                        }
+                    } else {
+                        const float lo = f - slack;
+                        a.sample_buf[((int64_t)t * a.B + q) * kSmallRows + rt] = (lo == lo) ? lo : -INFINITY;
+                    }
+                }
+            }
+            sm100::tc_fence_before();
+            sm100::mbar_arrive(tempty + buf);
+            if (++buf == 2) { buf = 0; bphase ^= 1u; }
+        }
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        sm100::tc_fence_after();
+        sm100::tmem_dealloc(tmem_base, a.tmem_cols);
+    }
+}
+
 }  // namespace batch
 }  // namespace mars
 
@@ -562,6 +703,16 @@ using namespace mars::batch;
 
 // ---------------------------------------------------------------------------
 // Host side
+
+// A tensor map and the arguments it was encoded for.
+struct MapCache {
+    const void* base = nullptr;
+    int64_t rows = -1, cols = -1, pitch = -1;
+    int box = 0;
+    bool f16 = false;
+    CUtensorMap map{};
+};
+
 struct mars_batch_ctx {
     int32_t device = 0;
     int32_t max_batch = 0;
@@ -576,22 +727,30 @@ struct mars_batch_ctx {
     float* d_theta = nullptr;
     int32_t* d_cand = nullptr;       // max_batch * cap
     float* d_cand_f = nullptr;       // max_batch * cap
-    int32_t* d_rescored = nullptr;   // max_batch
-    int32_t* h_rescored = nullptr;   // pinned
-    int32_t* d_cand_cnt = nullptr;
+    // the call's status words, one block read back with one copy:
+    // [err, pad, fallback[max_batch], cand_cnt[max_batch], rescored[max_batch], bad[max_batch]]
+    int32_t* d_status = nullptr;
+    int32_t* h_status = nullptr;     // pinned mirror
+    int32_t* d_err = nullptr;        // views into d_status / h_status
     int32_t* d_fallback = nullptr;
+    int32_t* d_cand_cnt = nullptr;
+    int32_t* d_rescored = nullptr;
+    int32_t* d_bad = nullptr;        // a query component outside the fp16 range
+    int32_t* h_err = nullptr;
+    int32_t* h_fallback = nullptr;
+    int32_t* h_cand_cnt = nullptr;
+    int32_t* h_rescored = nullptr;
+    int32_t* h_bad = nullptr;
     float* d_sample = nullptr;       // sample_tiles_cap * max_batch * kJ
     int32_t* d_sample_rt = nullptr;
     int32_t sample_tiles_cap = 0;
-    int* d_err = nullptr;
+    size_t sample_floats_cap = 0;
+    int32_t sample_rt_n = -1, sample_rt_rtiles = -1, sample_rt_rows = -1;   // the row-tile list on the device
+    int32_t max_smem = 0;            // opt-in shared memory per block
     __half* d_q16 = nullptr;         // max_batch x q16_pitch: fp16 queries
     int32_t q16_pitch = 0;
-    int* d_bad = nullptr;            // a query component outside the fp16 range
-    int* h_bad = nullptr;            // pinned
     int32_t precision = 0;           // 0: fp16 when in range, 1: TF32 always
-    int32_t* h_fallback = nullptr;   // pinned
-    int32_t* h_cand_cnt = nullptr;   // pinned
-    int* h_err = nullptr;
+    MapCache map_q, map_e;           // tensor maps of the last call's operands
     mars_query_ctx* scan_ctx = nullptr;   // exact single-query scans for fallbacks
     mars_batch_stats last{};
     cudaEvent_t ev_gemm[2] = {nullptr, nullptr};   // around the candidates pass
@@ -632,6 +791,22 @@ int make_map(CUtensorMap* m, const void* base, int64_t rows, int64_t cols, int64
     return MARS_OK;
 }
 
+// make_map through a cache: the same operands as the last call reuse its map.
+int cached_map(MapCache& mc, const void* base, int64_t rows, int64_t cols, int64_t pitch, int box_rows, bool f16) {
+    if (mc.base == base && mc.rows == rows && mc.cols == cols && mc.pitch == pitch && mc.box == box_rows &&
+        mc.f16 == f16)
+        return MARS_OK;
+    mc.base = nullptr;
+    MARS_TRY(make_map(&mc.map, base, rows, cols, pitch, box_rows, f16));
+    mc.base = base;
+    mc.rows = rows;
+    mc.cols = cols;
+    mc.pitch = pitch;
+    mc.box = box_rows;
+    mc.f16 = f16;
+    return MARS_OK;
+}
+
 constexpr size_t kGemmSmem = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
                              kBN * sizeof(float) /*row weights*/;
 
@@ -658,6 +833,7 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     c->max_nodes = max_nodes;
     c->cap = 16384;
     c->num_sms = prop.multiProcessorCount;
+    c->max_smem = (int32_t)prop.sharedMemPerBlockOptin;
     c->sample_tiles_cap = 0;
     int rc = MARS_OK;
     auto T = [&](cudaError_t e, const char* w) { if (rc == MARS_OK && e != cudaSuccess) rc = cuda_fail(e, w, __FILE__, __LINE__); };
@@ -669,19 +845,24 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     T(cudaMalloc(&c->d_theta, (size_t)max_batch * 4), "thresholds");
     T(cudaMalloc(&c->d_cand, (size_t)max_batch * c->cap * 4), "candidates");
     T(cudaMalloc(&c->d_cand_f, (size_t)max_batch * c->cap * 4), "candidate scores");
-    T(cudaMalloc(&c->d_rescored, (size_t)max_batch * 4), "rescore counts");
-    T(cudaMallocHost(&c->h_rescored, (size_t)max_batch * 4), "pinned rescore counts");
-    T(cudaMalloc(&c->d_cand_cnt, (size_t)max_batch * 4), "candidate counts");
-    T(cudaMalloc(&c->d_fallback, (size_t)max_batch * 4), "fallback flags");
-    T(cudaMalloc(&c->d_err, sizeof(int)), "error word");
-    T(cudaMallocHost(&c->h_fallback, (size_t)max_batch * 4), "pinned flags");
-    T(cudaMallocHost(&c->h_cand_cnt, (size_t)max_batch * 4), "pinned counts");
-    T(cudaMallocHost(&c->h_err, sizeof(int)), "pinned error");
+    const size_t status_words = 2 + 4 * (size_t)max_batch;
+    T(cudaMalloc(&c->d_status, status_words * 4), "status words");
+    T(cudaMallocHost(&c->h_status, status_words * 4), "pinned status words");
+    if (rc == MARS_OK) {
+        c->d_err = c->d_status;
+        c->d_fallback = c->d_status + 2;
+        c->d_cand_cnt = c->d_fallback + max_batch;
+        c->d_rescored = c->d_cand_cnt + max_batch;
+        c->d_bad = c->d_rescored + max_batch;
+        c->h_err = c->h_status;
+        c->h_fallback = c->h_status + 2;
+        c->h_cand_cnt = c->h_fallback + max_batch;
+        c->h_rescored = c->h_cand_cnt + max_batch;
+        c->h_bad = c->h_rescored + max_batch;
+        T(cudaMemset(c->d_status, 0, status_words * 4), "memset");
+    }
     c->q16_pitch = (dim + 7) & ~7;
     T(cudaMalloc(&c->d_q16, (size_t)max_batch * c->q16_pitch * sizeof(__half)), "fp16 queries");
-    T(cudaMalloc(&c->d_bad, sizeof(int)), "range flag");
-    T(cudaMallocHost(&c->h_bad, sizeof(int)), "pinned range flag");
-    if (rc == MARS_OK) T(cudaMemset(c->d_err, 0, sizeof(int)), "memset");
     if (rc == MARS_OK) {
         static bool attr_done[64] = {};
         if (device < 64 && !attr_done[device]) {
@@ -689,6 +870,8 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
             T(cudaFuncSetAttribute(gemm_kernel<kCandidates, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem), "smem attr");
             T(cudaFuncSetAttribute(gemm_kernel<kSample, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem), "smem attr");
             T(cudaFuncSetAttribute(gemm_kernel<kCandidates, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem), "smem attr");
+            T(cudaFuncSetAttribute(gemm_small_kernel<kSample>, cudaFuncAttributeMaxDynamicSharedMemorySize, c->max_smem), "smem attr");
+            T(cudaFuncSetAttribute(gemm_small_kernel<kCandidates>, cudaFuncAttributeMaxDynamicSharedMemorySize, c->max_smem), "smem attr");
             attr_done[device] = rc == MARS_OK;
         }
     }
@@ -709,11 +892,9 @@ int mars_batch_ctx_destroy(mars_batch_ctx* c) {
     MarsDeviceGuard g(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     cudaFree(c->d_wts); cudaFree(c->d_margin); cudaFree(c->d_theta); cudaFree(c->d_cand);
-    cudaFree(c->d_cand_f); cudaFree(c->d_rescored); cudaFreeHost(c->h_rescored);
-    cudaFree(c->d_cand_cnt); cudaFree(c->d_fallback); cudaFree(c->d_sample); cudaFree(c->d_sample_rt);
-    cudaFree(c->d_err);
-    cudaFreeHost(c->h_fallback); cudaFreeHost(c->h_cand_cnt); cudaFreeHost(c->h_err);
-    cudaFree(c->d_q16); cudaFree(c->d_bad); cudaFreeHost(c->h_bad);
+    cudaFree(c->d_cand_f); cudaFree(c->d_sample); cudaFree(c->d_sample_rt);
+    cudaFree(c->d_status); cudaFreeHost(c->h_status);
+    cudaFree(c->d_q16);
     mars_query_ctx_destroy(c->scan_ctx);
     for (cudaEvent_t e : c->ev_gemm)
         if (e) cudaEventDestroy(e);
@@ -793,7 +974,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     int32_t n_sample = (int32_t)std::ceil((double)n / (48.0 * kBN));
     n_sample = std::max(1, std::min(n_sample, rtiles));
     const double mu = (double)K * std::min<int64_t>((int64_t)n_sample * kBN, n) / std::max(n, 1);
-    const int32_t j = (int32_t)std::ceil(mu + 5.0 * std::sqrt(mu) + 3.0);
+    int32_t j = (int32_t)std::ceil(mu + 5.0 * std::sqrt(mu) + 3.0);
     const bool use_gemm = n >= 4 * kBN && K >= 3 && n_sample < rtiles && j <= kJ;
     if (!use_gemm) {
         // small corpora: exact single-query scans, one per query
@@ -807,40 +988,67 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         return MARS_OK;
     }
 
-    if (c->d_sample == nullptr || n_sample > c->sample_tiles_cap) {
-        // sized for this call's sample (about 2N / (256 K) row tiles)
+    // operands: fp16 copies (twice the tensor-core rate, half the bytes,
+    // the same 10 mantissa bits as TF32) when every value is in range
+    bool f16 = false;
+    if (allow_f16) MARS_TRY(mars::store_f16_rows(s, st, &f16));
+    // small batches on fp16 operands: rows as the MMA's M (gemm_small_kernel)
+    const int32_t NQ = (B + 15) & ~15;
+    int32_t stages = 0;
+    if (f16 && B <= kSmallMaxB) {
+        const size_t fixed = small_smem_bytes((s->e16_pitch + 63) / 64, NQ, 0);
+        if (fixed < (size_t)c->max_smem)
+            stages = (int32_t)std::min<size_t>(kSmallMaxStages, ((size_t)c->max_smem - fixed) / kSmallStage);
+    }
+    const bool small = stages >= 2;
+    const int32_t tile_rows = small ? kSmallRows : kBN;
+    const int32_t all_tiles = small ? (n + kSmallRows - 1) / kSmallRows : rtiles;
+    if (small) {   // the same one-in-48 rule over 128-row tiles
+        n_sample = (int32_t)std::ceil((double)n / (48.0 * kSmallRows));
+        n_sample = std::max(1, std::min(n_sample, all_tiles - 1));
+        const double mu_s = (double)K * std::min<int64_t>((int64_t)n_sample * kSmallRows, n) / std::max(n, 1);
+        j = (int32_t)std::ceil(mu_s + 5.0 * std::sqrt(mu_s) + 3.0);
+    }
+    const int32_t per_tile = small ? kSmallRows : kJ;
+    const size_t sample_floats = (size_t)n_sample * (small ? B : c->max_batch) * per_tile;
+    if (c->d_sample == nullptr || n_sample > c->sample_tiles_cap || sample_floats > c->sample_floats_cap) {
         MARS_CUDA_TRY(cudaStreamSynchronize(st));
         cudaFree(c->d_sample);
         cudaFree(c->d_sample_rt);
         c->d_sample = nullptr;
         c->d_sample_rt = nullptr;
         c->sample_tiles_cap = std::max(n_sample, 16);
-        MARS_CUDA_TRY(cudaMalloc(&c->d_sample, (size_t)c->sample_tiles_cap * c->max_batch * kJ * 4));
+        c->sample_floats_cap = std::max(sample_floats, (size_t)c->sample_tiles_cap * c->max_batch * kJ);
+        MARS_CUDA_TRY(cudaMalloc(&c->d_sample, c->sample_floats_cap * 4));
         MARS_CUDA_TRY(cudaMalloc(&c->d_sample_rt, (size_t)c->sample_tiles_cap * 4));
+        c->sample_rt_n = -1;
     }
-    // strided sample of row tiles
-    std::vector<int32_t> srt(n_sample);
-    for (int32_t i = 0; i < n_sample; ++i) srt[i] = (int32_t)(((int64_t)i * rtiles) / n_sample);
-    MARS_CUDA_TRY(cudaMemcpyAsync(c->d_sample_rt, srt.data(), (size_t)n_sample * 4, cudaMemcpyHostToDevice, st));
+    // strided sample of row tiles (uploaded again only when it changes)
+    if (c->sample_rt_n != n_sample || c->sample_rt_rtiles != all_tiles || c->sample_rt_rows != tile_rows) {
+        std::vector<int32_t> srt(n_sample);
+        for (int32_t i = 0; i < n_sample; ++i) srt[i] = (int32_t)(((int64_t)i * all_tiles) / n_sample);
+        MARS_CUDA_TRY(cudaMemcpyAsync(c->d_sample_rt, srt.data(), (size_t)n_sample * 4, cudaMemcpyHostToDevice,
+                                      st));
+        MARS_CUDA_TRY(cudaStreamSynchronize(st));   // srt lives on this stack frame
+        c->sample_rt_n = n_sample;
+        c->sample_rt_rtiles = all_tiles;
+        c->sample_rt_rows = tile_rows;
+    }
 
-    // operands: fp16 copies (twice the tensor-core rate, half the bytes,
-    // the same 10 mantissa bits as TF32) when every value is in range
-    bool f16 = false;
-    if (allow_f16) MARS_TRY(mars::store_f16_rows(s, st, &f16));
-    CUtensorMap mq, me;
     if (f16) {
-        MARS_CUDA_TRY(cudaMemsetAsync(c->d_bad, 0, sizeof(int), st));
         const int64_t total = (int64_t)B * c->q16_pitch;
         to_f16_queries_kernel<<<(int)std::min<int64_t>((total + 255) / 256, 148 * 8), 256, 0, st>>>(
-            d_queries, query_pitch, B, s->dim, c->d_q16, c->q16_pitch, c->d_bad);
+            d_queries, query_pitch, B, s->dim, c->d_q16, c->q16_pitch);
         MARS_CUDA_TRY(cudaGetLastError());
-        MARS_TRY(make_map(&mq, c->d_q16, B, c->q16_pitch, c->q16_pitch, kBM, true));
-        MARS_TRY(make_map(&me, s->d_E16, n, s->e16_pitch, s->e16_pitch, kBN, true));
+        MARS_TRY(cached_map(c->map_q, c->d_q16, B, c->q16_pitch, c->q16_pitch, small ? NQ : kBM, true));
+        MARS_TRY(cached_map(c->map_e, s->d_E16, n, s->e16_pitch, s->e16_pitch, tile_rows, true));
         nkb = (s->e16_pitch + 63) / 64;
     } else {
-        MARS_TRY(make_map(&mq, d_queries, B, s->pitch, query_pitch, kBM));
-        MARS_TRY(make_map(&me, s->d_E, n, s->pitch, s->pitch, kBN));
+        MARS_TRY(cached_map(c->map_q, d_queries, B, s->pitch, query_pitch, kBM, false));
+        MARS_TRY(cached_map(c->map_e, s->d_E, n, s->pitch, s->pitch, kBN, false));
     }
+    const CUtensorMap& mq = c->map_q.map;
+    const CUtensorMap& me = c->map_e.map;
 
     const int wblocks = std::min((n + 255) / 256, c->num_sms * 8);
     prep_rows_kernel<<<wblocks, 256, 0, st>>>(s->d_ts, s->d_imp, s->d_mod, n, t_q, lambda, modality_filter,
@@ -848,67 +1056,103 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     MARS_CUDA_TRY(cudaGetLastError());
     prep_queries_kernel<<<(B * 32 + 255) / 256, 256, 0, st>>>(d_queries, query_pitch, B, (s->dim + 3) / 4,
                                                               s->d_norm_bits, f16 ? 1 : 0, c->d_margin,
-                                                              c->d_cand_cnt);
+                                                              c->d_cand_cnt, c->d_rescored, c->d_bad,
+                                                              c->d_err);
     MARS_CUDA_TRY(cudaGetLastError());
-    MARS_CUDA_TRY(cudaMemsetAsync(c->d_err, 0, sizeof(int), st));
 
-    GemmArgs ga{};
-    ga.B = B;
-    ga.n = n;
-    ga.nkb = nkb;
-    ga.qtiles = qtiles;
-    ga.rtiles = rtiles;
-    ga.sample_rt = c->d_sample_rt;
-    ga.wts = c->d_wts;
-    ga.theta = c->d_theta;
-    ga.margin = c->d_margin;
-    ga.sample_buf = c->d_sample;
-    ga.cand = c->d_cand;
-    ga.cand_f = c->d_cand_f;
-    ga.cand_cnt = c->d_cand_cnt;
-    ga.cap = c->cap;
-    ga.self_base = self_base;
-    ga.err = c->d_err;
+    if (small) {
+        SmallArgs sa{};
+        sa.B = B;
+        sa.NQ = NQ;
+        sa.n = n;
+        sa.nkb = nkb;
+        sa.stages = stages;
+        uint32_t cols = 32;
+        while (cols < 2u * (uint32_t)NQ) cols <<= 1;
+        sa.tmem_cols = cols;
+        sa.sample_rt = c->d_sample_rt;
+        sa.wts = c->d_wts;
+        sa.theta = c->d_theta;
+        sa.margin = c->d_margin;
+        sa.sample_buf = c->d_sample;
+        sa.cand = c->d_cand;
+        sa.cand_f = c->d_cand_f;
+        sa.cand_cnt = c->d_cand_cnt;
+        sa.cap = c->cap;
+        sa.self_base = self_base;
+        sa.err = c->d_err;
+        const size_t smem = small_smem_bytes(nkb, NQ, stages);
+        // 2. sample, 3. thresholds, 4. candidates
+        sa.n_tiles = n_sample;
+        gemm_small_kernel<kSample><<<std::min(n_sample, c->num_sms), kThreads, smem, st>>>(mq, me, sa);
+        MARS_CUDA_TRY(cudaGetLastError());
+        threshold_kernel<<<B, kThrThreads, 0, st>>>(c->d_sample, n_sample, B, j, kSmallRows, c->d_theta);
+        MARS_CUDA_TRY(cudaGetLastError());
+        sa.n_tiles = all_tiles;
+        MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
+        gemm_small_kernel<kCandidates><<<std::min(all_tiles, c->num_sms), kThreads, smem, st>>>(mq, me, sa);
+        MARS_CUDA_TRY(cudaGetLastError());
+        MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[1], st));
+    } else {
+        GemmArgs ga{};
+        ga.B = B;
+        ga.n = n;
+        ga.nkb = nkb;
+        ga.qtiles = qtiles;
+        ga.rtiles = rtiles;
+        ga.sample_rt = c->d_sample_rt;
+        ga.wts = c->d_wts;
+        ga.theta = c->d_theta;
+        ga.margin = c->d_margin;
+        ga.sample_buf = c->d_sample;
+        ga.cand = c->d_cand;
+        ga.cand_f = c->d_cand_f;
+        ga.cand_cnt = c->d_cand_cnt;
+        ga.cap = c->cap;
+        ga.self_base = self_base;
+        ga.err = c->d_err;
 
-    // 2. sample
-    ga.n_tiles = n_sample * qtiles;
-    if (f16)
-        gemm_kernel<kSample, true><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
-    else
-        gemm_kernel<kSample, false><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
-    MARS_CUDA_TRY(cudaGetLastError());
-    // 3. thresholds
-    threshold_kernel<<<B, kThrThreads, 0, st>>>(c->d_sample, n_sample, B, j, c->d_theta);
-    MARS_CUDA_TRY(cudaGetLastError());
-    // 4. candidates
-    ga.n_tiles = rtiles * qtiles;
-    MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
-    if (f16)
-        gemm_kernel<kCandidates, true><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
-    else
-        gemm_kernel<kCandidates, false><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
-    MARS_CUDA_TRY(cudaGetLastError());
-    MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[1], st));
+        // 2. sample
+        ga.n_tiles = n_sample * qtiles;
+        if (f16)
+            gemm_kernel<kSample, true><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
+        else
+            gemm_kernel<kSample, false><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
+        MARS_CUDA_TRY(cudaGetLastError());
+        // 3. thresholds
+        threshold_kernel<<<B, kThrThreads, 0, st>>>(c->d_sample, n_sample, B, j, kJ, c->d_theta);
+        MARS_CUDA_TRY(cudaGetLastError());
+        // 4. candidates
+        ga.n_tiles = rtiles * qtiles;
+        MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
+        if (f16)
+            gemm_kernel<kCandidates, true><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me,
+                                                                                                            ga);
+        else
+            gemm_kernel<kCandidates, false><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me,
+                                                                                                             ga);
+        MARS_CUDA_TRY(cudaGetLastError());
+        MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[1], st));
+    }
     // 5. rescore
     StoreView v{};
     v.E = s->d_E; v.ts = s->d_ts; v.imp = s->d_imp; v.mod = s->d_mod; v.d_n = s->d_n;
     v.pitch4 = s->pitch / 4; v.nc = (s->dim + 3) / 4;
-    MARS_CUDA_TRY(cudaMemsetAsync(c->d_rescored, 0, (size_t)B * 4, st));
     rescore_kernel<<<B, kRescoreThreads, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, use_importance, K,
                                                   row_offset, c->d_theta, c->d_margin, c->d_wts, c->d_cand,
                                                   c->d_cand_f, c->d_cand_cnt, c->cap, d_ids, d_vals, d_counts,
                                                   c->d_fallback, c->d_rescored);
     MARS_CUDA_TRY(cudaGetLastError());
-    MARS_CUDA_TRY(cudaMemcpyAsync(c->h_fallback, c->d_fallback, (size_t)B * 4, cudaMemcpyDeviceToHost, st));
-    MARS_CUDA_TRY(cudaMemcpyAsync(c->h_cand_cnt, c->d_cand_cnt, (size_t)B * 4, cudaMemcpyDeviceToHost, st));
-    MARS_CUDA_TRY(cudaMemcpyAsync(c->h_err, c->d_err, sizeof(int), cudaMemcpyDeviceToHost, st));
-    MARS_CUDA_TRY(cudaMemcpyAsync(c->h_rescored, c->d_rescored, (size_t)B * 4, cudaMemcpyDeviceToHost, st));
-    *c->h_bad = 0;
-    if (f16) MARS_CUDA_TRY(cudaMemcpyAsync(c->h_bad, c->d_bad, sizeof(int), cudaMemcpyDeviceToHost, st));
+    MARS_CUDA_TRY(cudaMemcpyAsync(c->h_status, c->d_status, (2 + 4 * (size_t)c->max_batch) * 4,
+                                  cudaMemcpyDeviceToHost, st));
     MARS_CUDA_TRY(cudaStreamSynchronize(st));
-    if (f16 && *c->h_bad != 0) {
-        *redo = true;
-        return MARS_OK;
+    if (f16) {
+        for (int32_t b = 0; b < B; ++b) {
+            if (c->h_bad[b] != 0) {
+                *redo = true;
+                return MARS_OK;
+            }
+        }
     }
     if (*c->h_err != 0)
         return fail(MARS_ERR_TIMEOUT, "mars_query_batch_topk: a tensor-core pipeline wait gave up (code " +
@@ -930,7 +1174,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     float gms = 0.f;
     MARS_CUDA_TRY(cudaEventElapsedTime(&gms, c->ev_gemm[0], c->ev_gemm[1]));
     c->last.gemm_ms = gms;
-    c->last.path = f16 ? 2 : 1;
+    c->last.path = small ? 3 : (f16 ? 2 : 1);
     c->last.fallbacks = fb;
     c->last.candidates = total;
     c->last.max_candidates = maxc;

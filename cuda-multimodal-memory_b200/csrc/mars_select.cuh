@@ -227,6 +227,64 @@ __device__ int block_select_topk(unsigned long long* cand, int M, int K, int* hi
     return min(M, K);
 }
 
+// The k-th largest of n 32-bit keys (1 <= k <= n), key i = load(i), by MSD
+// radix selection: 11, 11 and 10 bits, each pass a shared histogram of the
+// keys that share the prefix chosen so far.  Every thread of the block calls
+// it; hist: 2048 ints, s_sel: 2 words of shared scratch.  Starts and ends
+// with __syncthreads().
+template <int NT, class Load>
+__device__ uint32_t block_kth_largest_key(Load load, int n, int k, int* hist, uint32_t* s_sel) {
+    const int lane = threadIdx.x & 31;
+    uint32_t prefix = 0, pmask = 0;
+    int rem = k;
+    __syncthreads();
+#pragma unroll 1
+    for (int pass = 0; pass < 3; ++pass) {
+        const int sh = pass == 0 ? 21 : (pass == 1 ? 10 : 0);
+        const int nb = pass == 2 ? 1024 : 2048;
+        for (int i = threadIdx.x; i < nb; i += NT) hist[i] = 0;
+        __syncthreads();
+        for (int i = threadIdx.x; i < n; i += NT) {
+            const uint32_t key = load(i);
+            if ((key & pmask) == prefix) atomicAdd(&hist[(key >> sh) & (nb - 1)], 1);
+        }
+        __syncthreads();
+        // the bucket holding the rem-th largest key: warp 0, lane l sums the
+        // l-th group of nb / 32 buckets counted from the top
+        if (threadIdx.x < 32) {
+            const int per = nb / 32;
+            const int top = nb - lane * per;
+            int sum = 0;
+            for (int b = top - 1; b >= top - per; --b) sum += hist[b];
+            int incl = sum;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int t = __shfl_up_sync(0xffffffffu, incl, o);
+                if (lane >= o) incl += t;
+            }
+            const int excl = incl - sum;
+            const unsigned mine = __ballot_sync(0xffffffffu, excl < rem && rem <= incl);
+            if (lane == __ffs(mine) - 1) {
+                int acc = excl;
+                for (int b = top - 1; b >= top - per; --b) {
+                    if (acc + hist[b] >= rem) {
+                        s_sel[0] = prefix | ((uint32_t)b << sh);
+                        s_sel[1] = (uint32_t)(rem - acc);
+                        break;
+                    }
+                    acc += hist[b];
+                }
+            }
+        }
+        __syncthreads();
+        prefix = s_sel[0];
+        rem = (int)s_sel[1];
+        pmask |= (uint32_t)(nb - 1) << sh;
+        __syncthreads();
+    }
+    return prefix;
+}
+
 // Merge nl ranked lists of K entries each (list l at vals/ids + l * K, rank
 // order, empty slots id == INT32_MAX) into their top-K.
 //

@@ -303,8 +303,10 @@ int mars_novelty(const mars_store* s, mars_query_ctx* ctx, const float* d_query,
 typedef struct mars_batch_ctx mars_batch_ctx;
 
 typedef struct mars_batch_stats {
-    int32_t path;            /* 2: tensor cores, fp16 operands; 1: tensor cores, TF32;
-                                0: per-query scans (small N) */
+    int32_t path;            /* 3: tensor cores, fp16 operands, small-batch tiles
+                                (128 rows x B queries, B <= 64); 2: tensor cores,
+                                fp16 operands (128 queries x 256 rows); 1: tensor
+                                cores, TF32; 0: per-query scans (small N) */
     int32_t fallbacks;       /* queries recomputed exactly                         */
     int64_t candidates;      /* short-listed (query, row) pairs                    */
     int32_t max_candidates;  /* largest short list of one query                    */

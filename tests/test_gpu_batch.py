@@ -76,7 +76,7 @@ def test_batch_small_smoke(torch_mod):
 def test_batch_matches_single_query_scans(torch_mod, N, D, B, K, tf32_only):
     """fp16 operands (default) and TF32 operands give the same results."""
     stats = _run(torch_mod, N, D, B, K, seed=N % 97, tf32_only=tf32_only)
-    assert stats["path"] == (1 if tf32_only else 2)
+    assert stats["path"] == (1 if tf32_only else (3 if B <= 64 else 2))
     assert stats["fallbacks"] <= max(2, B // 50), stats
 
 
@@ -113,7 +113,7 @@ def test_batch_fp16_copy_follows_appends_and_deletes(torch_mod):
         vals = torch.empty((B, K), dtype=torch.float32, device="cuda")
         bc.query_batch_topk(st, Q, B, 600.0, 0.01, K, ids, vals, use_importance=True)
         torch.cuda.synchronize()
-        assert bc.last_stats()["path"] == 2
+        assert bc.last_stats()["path"] == 3      # B = 64: the small-batch tiles
         for b in range(0, B, 7):
             i1 = torch.empty(K, dtype=torch.int32, device="cuda")
             v1 = torch.empty(K, dtype=torch.float32, device="cuda")
@@ -132,6 +132,24 @@ def test_batch_fp16_copy_follows_appends_and_deletes(torch_mod):
     assert int(ids[0, 0].item()) >= N0
     st.delete(ids[:, 0].cpu().numpy())
     check()
+
+
+@pytest.mark.parametrize("B", [1, 5, 16, 17, 48, 64])
+@pytest.mark.parametrize("K", [3, 10, 64])
+def test_batch_small_batches(torch_mod, B, K):
+    """B <= 64 on fp16 operands: 128-row x B-query tiles with the queries
+    resident in shared memory (gemm_small_kernel); results equal the scans."""
+    stats = _run(torch_mod, 100_003, 768, B, K, seed=B * 7 + K, check_oracle=1)
+    assert stats["path"] == 3
+    assert stats["fallbacks"] == 0, stats
+
+
+@pytest.mark.parametrize("N,D,B,K,filt", [(60_001, 1024, 33, 10, -1), (30_000, 100, 16, 25, 1),
+                                          (20_000, 64, 64, 100, -1), (1_000_000, 768, 16, 10, 2)])
+def test_batch_small_batches_shapes(torch_mod, N, D, B, K, filt):
+    stats = _run(torch_mod, N, D, B, K, filt=filt, seed=N % 101, check_oracle=1)
+    assert stats["path"] == 3
+    assert stats["fallbacks"] == 0, stats
 
 
 def test_batch_small_corpus_uses_scans(torch_mod):
