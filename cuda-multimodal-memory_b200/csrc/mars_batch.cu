@@ -340,36 +340,54 @@ __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch,
     }
 }
 
-// theta[q] = the j-th best sampled lower bound of query q (-inf when fewer
-// than j exist): one block per query, a radix selection
-// (block_kth_largest_key) over the n_sample_tiles * per_tile sampled bounds
-// (layout [tile][query][per_tile]), empty slots (-inf) left out.
+// theta[q] = the j-th largest of query q's sampled values (-inf when fewer
+// than j exist; j <= kThrKeep), over n_sample_tiles * per_tile values laid out
+// [tile][query][per_tile], empty slots -inf.  One warp per query: each lane
+// keeps its kThrKeep largest values sorted in registers while the warp
+// streams the values, then the warp takes the largest lane head j times (a
+// max butterfly; the lowest lane holding it drops it).  No block barrier, no
+// shared memory: the problem is a few thousand values per query.
 constexpr int kThrThreads = 256;
+constexpr int kThrKeep = 32;
 
 __global__ void __launch_bounds__(kThrThreads)
 threshold_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tiles, int32_t B, int32_t j,
                  int32_t per_tile, float* __restrict__ theta) {
-    __shared__ int hist[2048];
-    __shared__ uint32_t s_sel[2];
-    __shared__ int s_valid;
-    const int q = blockIdx.x;
+    const int q = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (q >= B) return;
     const int total = n_sample_tiles * per_tile;
-    auto at = [&](int i) { return sample_buf[((int64_t)(i / per_tile) * B + q) * per_tile + (i % per_tile)]; };
-    if (threadIdx.x == 0) s_valid = 0;
-    __syncthreads();
+    float keep[kThrKeep];
+#pragma unroll
+    for (int s = 0; s < kThrKeep; ++s) keep[s] = -INFINITY;
     int valid = 0;
-    for (int i = threadIdx.x; i < total; i += kThrThreads) valid += at(i) > -INFINITY ? 1 : 0;
-    valid = warp_reduce_sum_int(valid);
-    if ((threadIdx.x & 31) == 0) atomicAdd(&s_valid, valid);
-    __syncthreads();
-    if (s_valid < j) {
-        if (threadIdx.x == 0) theta[q] = -INFINITY;
-        return;
+    for (int i = lane; i < total; i += 32) {
+        float x = sample_buf[((int64_t)(i / per_tile) * B + q) * per_tile + (i % per_tile)];
+        if (!(x > -INFINITY)) continue;   // empty slot
+        ++valid;
+        if (x > keep[kThrKeep - 1]) {
+#pragma unroll
+            for (int s = 0; s < kThrKeep; ++s)
+                if (x > keep[s]) { const float t = keep[s]; keep[s] = x; x = t; }
+        }
     }
-    // empty slots map to key 0, below every valid bound
-    const uint32_t key = block_kth_largest_key<kThrThreads>(
-        [&](int i) { const float v = at(i); return v > -INFINITY ? f2key(v) : 0u; }, total, j, hist, s_sel);
-    if (threadIdx.x == 0) theta[q] = key2f(key);
+    valid = warp_reduce_sum_int(valid);
+    float th = -INFINITY;
+    if (valid >= j) {
+        for (int r = 0; r < j; ++r) {
+            float m = keep[0];
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+            const unsigned who = __ballot_sync(0xffffffffu, keep[0] == m);
+            if (lane == __ffs(who) - 1) {
+#pragma unroll
+                for (int s = 0; s < kThrKeep - 1; ++s) keep[s] = keep[s + 1];
+                keep[kThrKeep - 1] = -INFINITY;
+            }
+            th = m;
+        }
+    }
+    if (lane == 0) theta[q] = th;
 }
 
 // Exact rescoring of candidates: one block per query.
@@ -424,10 +442,10 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
                const float* __restrict__ cand_f, const int32_t* __restrict__ cand_cnt, int32_t cap,
                int32_t* __restrict__ out_ids, float* __restrict__ out_vals,
                int32_t* __restrict__ out_cnt, int32_t* __restrict__ fallback,
-               int32_t* __restrict__ rescored) {
+               int32_t* __restrict__ rescored, const int32_t* __restrict__ bad) {
     __shared__ float   s_key[kSortCap];
     __shared__ int32_t s_id[kSortCap];
-    __shared__ int     s_ge, s_n2;
+    __shared__ int     s_ge, s_n2, s_nk;
     __shared__ int     s_hist[2048];
     __shared__ uint32_t s_sel[2];
     const int qi = blockIdx.x;
@@ -437,8 +455,9 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     const int nc_ = min(ncand, cap);
     if (threadIdx.x == 0) { s_ge = 0; s_n2 = 0; }
     __syncthreads();
-    if (ncand > kSortCap || nc_ < K) {
-        // too many candidates to sort here, or too few to be complete
+    if (ncand > kSortCap || nc_ < K || (bad != nullptr && bad[qi] != 0)) {
+        // too many candidates to sort here, too few to be complete, or a
+        // query outside the fp16 range (its short list is meaningless)
         if (threadIdx.x == 0) { fallback[qi] = 1; rescored[qi] = 0; if (out_cnt) out_cnt[qi] = 0; }
         return;
     }
@@ -465,29 +484,66 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         [&](int i) { return f2key(s_key[i]); }, nc_, K, s_hist, s_sel));
 
     // ---- pass 2: exact scores of the candidates that can still place -------
+    // Their rows are listed first (in the histogram's space, free now) and
+    // dealt to the warps in turn, one row per warp at a time.
     const float4* q4 = reinterpret_cast<const float4*>(Q + (int64_t)qi * qpitch);
     const bool use_w = use_imp != 0 && s.imp != nullptr;
-    for (int base = warp * 32; base < nc_; base += kWarps * 32) {
-        const int i = base + lane;
-        bool keep = false;
+    int32_t* s_rows = s_hist;
+    constexpr int kRowsCap = 2048;
+    if (threadIdx.x == 0) s_nk = 0;
+    __syncthreads();
+    for (int i0 = warp * 32; i0 < nc_; i0 += kWarps * 32) {
+        const int i = i0 + lane;
         int32_t r = 0;
+        bool keep = false;
         if (i < nc_) {
             r = ci[i];
             keep = cf[i] + m * fabsf(__ldg(wts + r)) >= th2;
         }
-        unsigned mk = __ballot_sync(0xffffffffu, keep);
-        while (mk) {
-            const int src = __ffs(mk) - 1;
-            mk &= mk - 1;
-            const int32_t rr = __shfl_sync(0xffffffffu, r, src);
-            const float4* row = reinterpret_cast<const float4*>(s.E) + (int64_t)rr * s.pitch4;
-            const float dot = warp_dot_canonical(row, q4, s.nc, lane);
-            float f = fused_weight_apply(dot, __ldg(s.ts + rr), t_q, lambda);
-            if (use_w) f = f * __ldg(s.imp + rr);
-            if (lane == 0) {
-                const int pos = atomicAdd(&s_n2, 1);
-                s_key[pos] = f;
-                s_id[pos] = rr + row_offset;
+        const unsigned mk = __ballot_sync(0xffffffffu, keep);
+        int base = 0;
+        if (lane == 0 && mk != 0u) base = atomicAdd(&s_nk, __popc(mk));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        const int pos = base + __popc(mk & ((1u << lane) - 1u));
+        if (keep && pos < kRowsCap) s_rows[pos] = r;
+    }
+    __syncthreads();
+    const int nk = min(s_nk, kRowsCap);
+    auto score_row = [&](int32_t rr) {
+        const float4* row = reinterpret_cast<const float4*>(s.E) + (int64_t)rr * s.pitch4;
+        const float dot = warp_dot_canonical(row, q4, s.nc, lane);
+        float f = fused_weight_apply(dot, __ldg(s.ts + rr), t_q, lambda);
+        if (use_w) f = f * __ldg(s.imp + rr);
+        if (lane == 0) {
+            const int pos = atomicAdd(&s_n2, 1);
+            s_key[pos] = f;
+            s_id[pos] = rr + row_offset;
+        }
+    };
+    for (int t = warp; t < nk; t += kWarps) score_row(s_rows[t]);
+    if (s_nk > kRowsCap) {
+        // more rows than the list holds: the rest in candidate order
+        __syncthreads();
+        for (int i0 = warp * 32; i0 < nc_; i0 += kWarps * 32) {
+            const int i = i0 + lane;
+            int32_t r = 0;
+            bool keep = false;
+            if (i < nc_) {
+                r = ci[i];
+                keep = cf[i] + m * fabsf(__ldg(wts + r)) >= th2;
+            }
+            // the first kRowsCap kept rows (in list order) are done; ranks are
+            // not known here, so every kept row not in the list is scored by
+            // membership test against the list
+            unsigned mk = __ballot_sync(0xffffffffu, keep);
+            while (mk) {
+                const int src = __ffs(mk) - 1;
+                mk &= mk - 1;
+                const int32_t rr = __shfl_sync(0xffffffffu, r, src);
+                bool listed = false;
+                for (int t = lane; t < kRowsCap && !listed; t += 32) listed = s_rows[t] == rr;
+                if (__any_sync(0xffffffffu, listed)) continue;
+                score_row(rr);
             }
         }
     }
@@ -521,12 +577,16 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
 // buffered; epilogue thread t owns row t of the tile.
 //
 // Candidates mode appends (query, row) when the row's upper bound reaches the
-// query's threshold, as gemm_kernel does.  Sample mode writes every lower
-// bound of the sampled tiles: sample_buf[tile][query][128].
+// query's threshold, as gemm_kernel does.  Sample mode writes, per sampled
+// tile and query, each epilogue warp's largest lower bound (of its 32 rows):
+// sample_buf[tile][query][kSmallWarps].  The j-th largest of these is at most
+// the j-th largest sampled bound (j of them are the maxima of j distinct
+// row sets), so the threshold stays as safe.
 constexpr int kSmallMaxB = 64;
 constexpr int kSmallRows = 128;
 constexpr int kSmallStage = kSmallRows * 128;      // 16 KB: 128 rows x 64 halves
 constexpr int kSmallMaxStages = 12;
+constexpr int kSmallWarps = 4;                       // epilogue warps: 32 rows each
 
 struct SmallArgs {
     int32_t B, NQ;                   // queries, MMA N (B rounded up to 16)
@@ -538,7 +598,7 @@ struct SmallArgs {
     const float* wts;
     const float* theta;
     const float* margin;
-    float* sample_buf;               // sample mode: [n_tiles][B][128]
+    float* sample_buf;               // sample mode: [n_tiles][B][kSmallWarps]
     int32_t* cand;
     float* cand_f;
     int32_t* cand_cnt;
@@ -677,8 +737,13 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                             }
                         }
                     } else {
-                        const float lo = f - slack;
-                        a.sample_buf[((int64_t)t * a.B + q) * kSmallRows + rt] = (lo == lo) ? lo : -INFINITY;
+                        // the warp's largest lower bound (its 32 rows) for query q
+                        float lo = f - slack;
+                        if (!(lo == lo)) lo = -INFINITY;
+#pragma unroll
+                        for (int off = 16; off >= 1; off >>= 1)
+                            lo = fmaxf(lo, __shfl_xor_sync(0xffffffffu, lo, off));
+                        if (lane == 0) a.sample_buf[((int64_t)t * a.B + q) * kSmallWarps + sub] = lo;
                     }
                 }
             }
@@ -754,7 +819,20 @@ struct mars_batch_ctx {
     mars_query_ctx* scan_ctx = nullptr;   // exact single-query scans for fallbacks
     mars_batch_stats last{};
     cudaEvent_t ev_gemm[2] = {nullptr, nullptr};   // around the candidates pass
+    // exact rescans of the queries the rescore could not certify, on the
+    // device (a multi-query scan that skips unflagged queries)
+    int32_t fb_grid = 1;                // CTAs per query at max_batch queries
+    float* d_fb_val = nullptr;          // max_batch * fb_grid * max_k
+    int32_t* d_fb_idx = nullptr;
+    unsigned int* d_fb_slots = nullptr; // tickets [max_batch], row counters [max_batch]
+    // the last call's status block, read when asked for
+    cudaStream_t last_stream = nullptr;
+    cudaEvent_t ev_status = nullptr;    // after the status copy
+    bool status_pending = false;
+    int32_t last_B = 0;
 };
+
+int batch_collect_stats(mars_batch_ctx* c);
 
 namespace {
 
@@ -863,6 +941,12 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     }
     c->q16_pitch = (dim + 7) & ~7;
     T(cudaMalloc(&c->d_q16, (size_t)max_batch * c->q16_pitch * sizeof(__half)), "fp16 queries");
+    c->fb_grid = std::max(1, std::min(2 * c->num_sms, 2 * c->num_sms / max_batch));
+    T(cudaMalloc(&c->d_fb_val, (size_t)max_batch * c->fb_grid * max_k * 4), "rescan partials");
+    T(cudaMalloc(&c->d_fb_idx, (size_t)max_batch * c->fb_grid * max_k * 4), "rescan partials");
+    T(cudaMalloc(&c->d_fb_slots, (size_t)max_batch * 2 * sizeof(unsigned int)), "rescan slots");
+    if (rc == MARS_OK) T(cudaMemset(c->d_fb_slots, 0, (size_t)max_batch * 2 * sizeof(unsigned int)), "memset");
+    T(cudaEventCreateWithFlags(&c->ev_status, cudaEventDisableTiming), "event");
     if (rc == MARS_OK) {
         static bool attr_done[64] = {};
         if (device < 64 && !attr_done[device]) {
@@ -895,6 +979,8 @@ int mars_batch_ctx_destroy(mars_batch_ctx* c) {
     cudaFree(c->d_cand_f); cudaFree(c->d_sample); cudaFree(c->d_sample_rt);
     cudaFree(c->d_status); cudaFreeHost(c->h_status);
     cudaFree(c->d_q16);
+    cudaFree(c->d_fb_val); cudaFree(c->d_fb_idx); cudaFree(c->d_fb_slots);
+    if (c->ev_status) cudaEventDestroy(c->ev_status);
     mars_query_ctx_destroy(c->scan_ctx);
     for (cudaEvent_t e : c->ev_gemm)
         if (e) cudaEventDestroy(e);
@@ -905,8 +991,9 @@ int mars_batch_ctx_destroy(mars_batch_ctx* c) {
 
 int mars_batch_last_stats(const mars_batch_ctx* c, mars_batch_stats* out) {
     if (c == nullptr || out == nullptr) return fail(MARS_ERR_INVALID, "mars_batch_last_stats: NULL argument");
+    const int rc = batch_collect_stats(const_cast<mars_batch_ctx*>(c));   // the statistics are a cache
     *out = c->last;
-    return MARS_OK;
+    return rc;
 }
 
 int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
@@ -922,27 +1009,62 @@ int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d
 int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
                     int32_t B, float t_q, float lambda, int32_t modality_filter, int32_t use_importance,
                     int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
-                    int32_t* d_counts, void* stream, bool allow_f16, bool* redo);
+                    int32_t* d_counts, void* stream, bool allow_f16);
 
+// The previous call's pipeline error word, if its status copy has landed
+// (never waits).
+int batch_prev_status(const mars_batch_ctx* c) {
+    if (!c->status_pending || cudaEventQuery(c->ev_status) != cudaSuccess) return MARS_OK;
+    if (*c->h_err != 0)
+        return fail(MARS_ERR_TIMEOUT, "mars_query_batch_topk: a tensor-core pipeline wait gave up (code " +
+                                          std::to_string(*c->h_err) + ")");
+    return MARS_OK;
+}
+
+// Fill c->last from the last call's status words (waits for the call).
+int batch_collect_stats(mars_batch_ctx* c) {
+    if (!c->status_pending) return MARS_OK;
+    MarsDeviceGuard g(c->device);
+    MARS_CUDA_TRY(cudaEventSynchronize(c->ev_status));
+    c->status_pending = false;
+    int64_t total = 0, rescored = 0;
+    int32_t fb = 0, maxc = 0;
+    for (int32_t b = 0; b < c->last_B; ++b) {
+        total += c->h_cand_cnt[b];
+        rescored += c->h_rescored[b];
+        maxc = std::max(maxc, c->h_cand_cnt[b]);
+        fb += c->h_fallback[b] != 0 ? 1 : 0;
+    }
+    float gms = 0.f;
+    MARS_CUDA_TRY(cudaEventElapsedTime(&gms, c->ev_gemm[0], c->ev_gemm[1]));
+    c->last.gemm_ms = gms;
+    c->last.fallbacks = fb;
+    c->last.candidates = total;
+    c->last.max_candidates = maxc;
+    c->last.rescored = rescored;
+    if (*c->h_err != 0)
+        return fail(MARS_ERR_TIMEOUT, "mars_query_batch_topk: a tensor-core pipeline wait gave up (code " +
+                                          std::to_string(*c->h_err) + ")");
+    return MARS_OK;
+}
+
+// Asynchronous on the stream: queries that the rescore cannot certify (and
+// queries outside the fp16 range) are rescanned exactly on the device, so no
+// step waits for the host.  The statistics of the call are read when
+// mars_batch_last_stats asks for them.
 int mars::batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
                      int32_t B, float t_q, float lambda, int32_t modality_filter, int32_t use_importance,
                      int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
                      int32_t* d_counts, void* stream) {
-    bool redo = false;
-    MARS_TRY(batch_topk_pass(s, c, d_queries, query_pitch, B, t_q, lambda, modality_filter, use_importance, K,
-                             row_offset, self_base, d_ids, d_vals, d_counts, stream, c != nullptr && c->precision == 0,
-                             &redo));
-    if (!redo) return MARS_OK;
-    // a query component outside the fp16 range: the same batch on TF32
     return batch_topk_pass(s, c, d_queries, query_pitch, B, t_q, lambda, modality_filter, use_importance, K,
-                           row_offset, self_base, d_ids, d_vals, d_counts, stream, false, &redo);
+                           row_offset, self_base, d_ids, d_vals, d_counts, stream,
+                           c != nullptr && c->precision == 0);
 }
 
 int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
                     int32_t B, float t_q, float lambda, int32_t modality_filter, int32_t use_importance,
                     int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
-                    int32_t* d_counts, void* stream, bool allow_f16, bool* redo) {
-    *redo = false;
+                    int32_t* d_counts, void* stream, bool allow_f16) {
     if (s == nullptr || c == nullptr || d_queries == nullptr || d_ids == nullptr || d_vals == nullptr)
         return fail(MARS_ERR_INVALID, "mars_query_batch_topk: NULL argument");
     if (s->device != c->device || s->dim != c->dim)
@@ -955,7 +1077,9 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         return fail(MARS_ERR_CAPACITY, "mars_query_batch_topk: store larger than the context");
     if (s->d_norm_bits == nullptr)
         return fail(MARS_ERR_UNSUPPORTED, "mars_query_batch_topk: store has no row-norm bound (a view of caller memory)");
+    MARS_TRY(batch_prev_status(c));
     c->last = mars_batch_stats{};
+    c->status_pending = false;
     if (B == 0) return MARS_OK;
     MarsDeviceGuard g(c->device);
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : c->stream;
@@ -1000,16 +1124,21 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         if (fixed < (size_t)c->max_smem)
             stages = (int32_t)std::min<size_t>(kSmallMaxStages, ((size_t)c->max_smem - fixed) / kSmallStage);
     }
-    const bool small = stages >= 2;
+    bool small = stages >= 2;
+    if (small) {   // the same one-in-48 rule over 128-row tiles
+        const int32_t tiles128 = (n + kSmallRows - 1) / kSmallRows;
+        const int32_t ns = std::max(1, std::min((int32_t)std::ceil((double)n / (48.0 * kSmallRows)), tiles128 - 1));
+        const double mu_s = (double)K * std::min<int64_t>((int64_t)ns * kSmallRows, n) / std::max(n, 1);
+        const int32_t js = (int32_t)std::ceil(mu_s + 5.0 * std::sqrt(mu_s) + 3.0);
+        small = js <= kThrKeep;
+        if (small) {
+            n_sample = ns;
+            j = js;
+        }
+    }
     const int32_t tile_rows = small ? kSmallRows : kBN;
     const int32_t all_tiles = small ? (n + kSmallRows - 1) / kSmallRows : rtiles;
-    if (small) {   // the same one-in-48 rule over 128-row tiles
-        n_sample = (int32_t)std::ceil((double)n / (48.0 * kSmallRows));
-        n_sample = std::max(1, std::min(n_sample, all_tiles - 1));
-        const double mu_s = (double)K * std::min<int64_t>((int64_t)n_sample * kSmallRows, n) / std::max(n, 1);
-        j = (int32_t)std::ceil(mu_s + 5.0 * std::sqrt(mu_s) + 3.0);
-    }
-    const int32_t per_tile = small ? kSmallRows : kJ;
+    const int32_t per_tile = small ? kSmallWarps : kJ;
     const size_t sample_floats = (size_t)n_sample * (small ? B : c->max_batch) * per_tile;
     if (c->d_sample == nullptr || n_sample > c->sample_tiles_cap || sample_floats > c->sample_floats_cap) {
         MARS_CUDA_TRY(cudaStreamSynchronize(st));
@@ -1086,7 +1215,8 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         sa.n_tiles = n_sample;
         gemm_small_kernel<kSample><<<std::min(n_sample, c->num_sms), kThreads, smem, st>>>(mq, me, sa);
         MARS_CUDA_TRY(cudaGetLastError());
-        threshold_kernel<<<B, kThrThreads, 0, st>>>(c->d_sample, n_sample, B, j, kSmallRows, c->d_theta);
+        threshold_kernel<<<(B * 32 + kThrThreads - 1) / kThrThreads, kThrThreads, 0, st>>>(
+            c->d_sample, n_sample, B, j, kSmallWarps, c->d_theta);
         MARS_CUDA_TRY(cudaGetLastError());
         sa.n_tiles = all_tiles;
         MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
@@ -1120,7 +1250,8 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
             gemm_kernel<kSample, false><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
         MARS_CUDA_TRY(cudaGetLastError());
         // 3. thresholds
-        threshold_kernel<<<B, kThrThreads, 0, st>>>(c->d_sample, n_sample, B, j, kJ, c->d_theta);
+        threshold_kernel<<<(B * 32 + kThrThreads - 1) / kThrThreads, kThrThreads, 0, st>>>(
+            c->d_sample, n_sample, B, j, kJ, c->d_theta);
         MARS_CUDA_TRY(cudaGetLastError());
         // 4. candidates
         ga.n_tiles = rtiles * qtiles;
@@ -1141,46 +1272,42 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     rescore_kernel<<<B, kRescoreThreads, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, use_importance, K,
                                                   row_offset, c->d_theta, c->d_margin, c->d_wts, c->d_cand,
                                                   c->d_cand_f, c->d_cand_cnt, c->cap, d_ids, d_vals, d_counts,
-                                                  c->d_fallback, c->d_rescored);
+                                                  c->d_fallback, c->d_rescored, f16 ? c->d_bad : nullptr);
     MARS_CUDA_TRY(cudaGetLastError());
+    // 6. exact rescans of the flagged queries (every CTA of an unflagged
+    // query leaves at once)
+    ScanArgs fa{};
+    fa.s = StoreView{};
+    fa.s.E = s->d_E; fa.s.ts = s->d_ts; fa.s.imp = s->d_imp; fa.s.mod = s->d_mod; fa.s.d_n = s->d_n;
+    fa.s.pitch4 = s->pitch / 4; fa.s.nc = (s->dim + 3) / 4;
+    fa.d.t_q = t_q;
+    fa.d.lambda = lambda;
+    fa.d.filter = modality_filter;
+    fa.d.use_imp = use_importance;
+    fa.d.K = K;
+    fa.d.row_offset = row_offset;
+    fa.part_val = c->d_fb_val;
+    fa.part_idx = c->d_fb_idx;
+    fa.ticket = c->d_fb_slots;
+    fa.cursor = c->d_fb_slots + c->max_batch;
+    fa.out_val = d_vals;
+    fa.out_idx = d_ids;
+    fa.out_cnt = d_counts;
+    fa.only = c->d_fallback;
+    fa.exclude_base1 = self_base >= 0 ? self_base + 1 : 0;
+    const int fgx = std::max(1, std::min(c->fb_grid, 2 * c->num_sms / B));
+    MARS_CUDA_TRY(launch_scan_multi(fa, d_queries, query_pitch, B, fgx, st));
+    // the status words, read by mars_batch_last_stats (and checked for a
+    // pipeline error by the next call)
     MARS_CUDA_TRY(cudaMemcpyAsync(c->h_status, c->d_status, (2 + 4 * (size_t)c->max_batch) * 4,
                                   cudaMemcpyDeviceToHost, st));
-    MARS_CUDA_TRY(cudaStreamSynchronize(st));
-    if (f16) {
-        for (int32_t b = 0; b < B; ++b) {
-            if (c->h_bad[b] != 0) {
-                *redo = true;
-                return MARS_OK;
-            }
-        }
-    }
-    if (*c->h_err != 0)
-        return fail(MARS_ERR_TIMEOUT, "mars_query_batch_topk: a tensor-core pipeline wait gave up (code " +
-                                          std::to_string(*c->h_err) + ")");
-    int64_t total = 0, rescored = 0;
-    int32_t fb = 0, maxc = 0;
-    for (int32_t b = 0; b < B; ++b) {
-        total += c->h_cand_cnt[b];
-        rescored += c->h_rescored[b];
-        maxc = std::max(maxc, c->h_cand_cnt[b]);
-        if (c->h_fallback[b]) {
-            ++fb;
-            MARS_TRY(mars::scan_topk_excluding(s, c->scan_ctx, d_queries + (int64_t)b * query_pitch, t_q,
-                                               lambda, modality_filter, use_importance, K, row_offset,
-                                               self_base >= 0 ? self_base + b : -1, d_ids + (int64_t)b * K,
-                                               d_vals + (int64_t)b * K, d_counts ? d_counts + b : nullptr, st));
-        }
-    }
-    float gms = 0.f;
-    MARS_CUDA_TRY(cudaEventElapsedTime(&gms, c->ev_gemm[0], c->ev_gemm[1]));
-    c->last.gemm_ms = gms;
+    MARS_CUDA_TRY(cudaEventRecord(c->ev_status, st));
+    c->status_pending = true;
+    c->last_stream = st;
+    c->last_B = B;
     c->last.path = small ? 3 : (f16 ? 2 : 1);
-    c->last.fallbacks = fb;
-    c->last.candidates = total;
-    c->last.max_candidates = maxc;
     c->last.sample_tiles = n_sample;
     c->last.sample_rank = j;
-    c->last.rescored = rescored;
     return MARS_OK;
 }
 

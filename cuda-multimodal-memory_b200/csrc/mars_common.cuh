@@ -51,8 +51,22 @@ __device__ __forceinline__ float warp_butterfly_sum(float v) {
 __device__ __forceinline__ float warp_dot_canonical(const float4* __restrict__ row,
                                                     const float4* __restrict__ q,
                                                     int nc, int lane) {
+    // chunk c = lane + 32 k in increasing k, one fused multiply-add chain per
+    // lane; the loads of up to 8 chunks are issued before the first FMA so a
+    // lone row (a BFS node, a rescored candidate) costs one memory latency,
+    // not one per chunk.  The arithmetic is the same as the streaming scan's.
     float acc = 0.0f;
-    for (int c = lane; c < nc; c += kWarp) acc = fma4(ldg_stream(row + c), q[c], acc);
+    for (int c0 = lane; c0 < nc; c0 += 8 * kWarp) {
+        float4 e[8], qv[8];
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            const int c = c0 + k * kWarp;
+            if (c < nc) { e[k] = ldg_stream(row + c); qv[k] = q[c]; }
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+            if (c0 + k * kWarp < nc) acc = fma4(e[k], qv[k], acc);
+    }
     return warp_butterfly_sum(acc);
 }
 

@@ -67,6 +67,10 @@ struct ScanArgs {
     int32_t* vis_ids;
     float*   vis_score;
     int32_t* lvl;                     // [0..15] level offsets, [16] tail
+    // multi-query launches
+    const int32_t* only;              // only[qi] == 0: query qi is skipped (null: every query)
+    int32_t  exclude_base1;           // 1 + the row query 0 leaves out; query qi leaves out
+                                      // row exclude_base1 - 1 + qi (0: none)
 };
 
 struct BfsArgs {

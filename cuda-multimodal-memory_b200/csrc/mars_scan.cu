@@ -70,6 +70,7 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan_multi_kernel(const __gri
                                                                       int64_t qpitch) {
     __shared__ ScanShared sm;
     const int qi = blockIdx.y;
+    if (a.only != nullptr && a.only[qi] == 0) return;   // every CTA of the query leaves
     const SlotMulti sl{a, qi};
     const float4* q = reinterpret_cast<const float4*>(Q + qi * qpitch);
     if (!scan_rows<KPL, CPL, false>(a, sl, q, a.d.t_q, sm)) return;

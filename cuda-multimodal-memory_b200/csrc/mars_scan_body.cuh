@@ -60,6 +60,7 @@ struct SlotOne {     // one query per launch
     __device__ int32_t* part_idx() const { return a.part_idx; }
     __device__ unsigned int* ticket() const { return a.ticket; }
     __device__ unsigned int* cursor() const { return a.cursor; }
+    __device__ bool excluded(int32_t) const { return false; }
 };
 struct SlotMulti {   // query qi of a multi-query launch (gridDim.x CTAs per query)
     const ScanArgs& a;
@@ -69,6 +70,7 @@ struct SlotMulti {   // query qi of a multi-query launch (gridDim.x CTAs per que
     __device__ int32_t* part_idx() const { return a.part_idx + off(); }
     __device__ unsigned int* ticket() const { return a.ticket + qi; }
     __device__ unsigned int* cursor() const { return a.cursor != nullptr ? a.cursor + qi : nullptr; }
+    __device__ bool excluded(int32_t row) const { return a.exclude_base1 != 0 && row == a.exclude_base1 - 1 + qi; }
 };
 
 // Stream this CTA's rows and leave the CTA's ranked list in the partial
@@ -133,7 +135,7 @@ __device__ __forceinline__ bool scan_rows(const ScanArgs& a, const Slot& sl, con
     load_meta(wbase);
 
     auto offer = [&](int32_t row, float dot, float t, float im, int32_t m) {
-        if ((filter >= 0 && m != filter) || row + 1 == d.exclude_plus1) {
+        if ((filter >= 0 && m != filter) || row + 1 == d.exclude_plus1 || sl.excluded(row)) {
             if (ALL && lane == 0) a.all_scores[row] = -FLT_MAX;
             return;
         }

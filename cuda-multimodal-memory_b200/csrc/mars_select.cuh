@@ -244,9 +244,15 @@ __device__ uint32_t block_kth_largest_key(Load load, int n, int k, int* hist, ui
         const int nb = pass == 2 ? 1024 : 2048;
         for (int i = threadIdx.x; i < nb; i += NT) hist[i] = 0;
         __syncthreads();
-        for (int i = threadIdx.x; i < n; i += NT) {
-            const uint32_t key = load(i);
-            if ((key & pmask) == prefix) atomicAdd(&hist[(key >> sh) & (nb - 1)], 1);
+        // keys crowd into few buckets (one exponent range): lanes that hit
+        // the same bucket add their count with one atomic
+        for (int i0 = threadIdx.x - (threadIdx.x & 31); i0 < n; i0 += NT) {
+            const int i = i0 + (threadIdx.x & 31);
+            const uint32_t key = i < n ? load(i) : 0u;
+            const bool in = i < n && (key & pmask) == prefix;
+            const int bucket = in ? (int)((key >> sh) & (uint32_t)(nb - 1)) : -1;
+            const unsigned peers = __match_any_sync(0xffffffffu, bucket);
+            if (in && (threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[bucket], __popc(peers));
         }
         __syncthreads();
         // the bucket holding the rem-th largest key: warp 0, lane l sums the

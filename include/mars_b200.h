@@ -334,7 +334,11 @@ int mars_batch_ctx_set_precision(mars_batch_ctx* ctx, int32_t tf32_only);
 /* d_queries: B rows of query_pitch floats (16-byte aligned; values past dim
  * must be zero).  One query time t_q for the whole batch.  Outputs d_ids /
  * d_vals: [B][K] (ids offset by row_offset), d_counts: [B] (may be NULL).
- * Synchronises with the host once per call (to run fallbacks). */
+ * Asynchronous on `stream`: a query whose short list cannot be proven
+ * complete, or with a component outside the fp16 range, is rescanned exactly
+ * on the device in the same stream (mars_batch_stats.fallbacks).  A
+ * pipeline error of a call (a bounded wait that gave up) is returned by
+ * mars_batch_last_stats or by the next call. */
 int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx,
                           const float* d_queries, int32_t query_pitch, int32_t B,
                           float query_timestamp, float lambda,
@@ -342,6 +346,7 @@ int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx,
                           int32_t K, int32_t row_offset, int32_t* d_ids,
                           float* d_vals, int32_t* d_counts, void* stream);
 
+/* Statistics of the last mars_query_batch_topk call (waits for it). */
 int mars_batch_last_stats(const mars_batch_ctx* ctx, mars_batch_stats* out);
 
 /* ---- CMNG kNN graph (include/cmng.cuh) --------------------------------- */

@@ -85,13 +85,35 @@ def test_batch_with_modality_filter(torch_mod):
     assert stats["path"] == 2
 
 
-def test_batch_out_of_fp16_range_uses_tf32(torch_mod):
-    """A row or a query with a component beyond the fp16 range covered by
-    the error margin moves the batch to TF32 operands; results unchanged."""
+def test_batch_out_of_fp16_range(torch_mod):
+    """A row beyond the fp16 range covered by the error margin moves the
+    batch to TF32 operands; a query beyond it is rescanned exactly on the
+    device.  Results unchanged either way."""
     stats = _run(torch_mod, 30_000, 768, 64, 10, seed=8, scale_row=(123, 1e6))
     assert stats["path"] == 1
     stats = _run(torch_mod, 30_000, 768, 64, 10, seed=9, scale_query=(5, 1e6))
-    assert stats["path"] == 1
+    assert stats["path"] == 3 and stats["fallbacks"] >= 1, stats
+    stats = _run(torch_mod, 30_000, 768, 100, 10, seed=10, scale_query=(70, 1e6))
+    assert stats["path"] == 2 and stats["fallbacks"] >= 1, stats
+
+
+def test_batch_device_rescans_ties(torch_mod):
+    """Every row identical: no short list can be proven complete, so every
+    query is rescanned on the device; the answer is the K smallest ids."""
+    import mars_b200 as mb
+    torch = torch_mod
+    N, D, B, K = 50_000, 64, 8, 10
+    E = np.tile(np.random.default_rng(0).standard_normal((1, D)).astype(np.float32), (N, 1))
+    st = mb.Store(N, D)
+    st.upload(E, np.zeros(N, np.int32), np.zeros(N, np.float32), None)
+    bc = mb.BatchContext(N, D, max_batch=B, max_k=K)
+    Q = torch.from_numpy(np.random.default_rng(1).standard_normal((B, D)).astype(np.float32)).cuda()
+    ids = torch.full((B, K), -7, dtype=torch.int32, device="cuda")
+    vals = torch.zeros((B, K), dtype=torch.float32, device="cuda")
+    bc.query_batch_topk(st, Q, B, 0.0, 0.0, K, ids, vals)
+    stats = bc.last_stats()
+    assert stats["fallbacks"] == B, stats
+    assert np.array_equal(ids.cpu().numpy(), np.tile(np.arange(K, dtype=np.int32), (B, 1)))
 
 
 def test_batch_fp16_copy_follows_appends_and_deletes(torch_mod):
