@@ -11,9 +11,13 @@ HBM GB/s vs peak):
     answered by mars_query_batch_topk (an fp16 tensor-core short list with a
     proven error margin, then an exact fp32 rescore: the results are those of
     the fp32 fused scan bit for bit, which the run checks);
-  * N GPUs: the corpus is row-sharded (strong scaling: total N fixed); each
-    GPU answers the step's queries on its shard, the per-query local top-K
-    lists are all-gathered over NCCL and merged on every GPU.
+  * N GPUs (`--shard replicas`, the default): the 1M-row corpus (4.6 GB with
+    its fp16 copy) fits every GPU, so every GPU holds it and answers its own
+    16 queries per step, with no data-path collective (weak scaling: 16 N
+    queries per step).  `--shard rows`: the corpus is row-sharded (strong
+    scaling), every GPU answers the same queries on its shard, and the
+    per-query local top-K lists are all-gathered over NCCL and merged on
+    every GPU.
 
 `value` is queries/s with queries and corpus resident in HBM, timed with CUDA
 events on the query stream (max over ranks).  `e2e` goes through the public
@@ -63,6 +67,10 @@ def parse_args():
     ap.add_argument("--cpu-budget-s", type=float, default=10.0)
     ap.add_argument("--batch", type=int, default=1024)
     ap.add_argument("--queries", type=int, default=10000)
+    ap.add_argument("--shard", choices=["replicas", "rows"], default="replicas",
+                    help="headline on several GPUs: replicas (every GPU holds the whole corpus and answers "
+                         "its own queries; weak scaling) or rows (the corpus row-sharded, every GPU answers "
+                         "the same queries on its shard, NCCL all-gather + merge; strong scaling)")
     ap.add_argument("--workload", choices=["scan", "c0", "c1", "c2", "c3", "c4"], default="scan",
                     help="scan: the headline (default); c0: single-query latency at N=2400 "
                          "with BFS depth 1; c1: streaming loop (append 10 rows + query per frame)")
@@ -83,16 +91,21 @@ def metric_name(a):
 
 
 def config_dict(a, world):
+    rows = world > 1 and a.shard == "rows"
+    per_gpu = a.n // world if rows else a.n
     return {
         "workload": f"retrieval N={a.n} D={a.dim} K={a.k}: {a.queries_per_step} concurrent queries "
                     f"per step, each the exact top-K over all rows (mars_query_batch_topk: "
                     f"fp16 tensor-core short list + exact fp32 rescore; results bit-identical "
                     f"to the fp32 fused scan)",
         "n_rows": a.n, "dim": a.dim, "top_k": a.k, "queries_per_step": a.queries_per_step,
-        "lambda": a.lam, "importance": True, "shards": world,
-        "parallelism": f"row-shard x{world}" + (" + NCCL all-gather + merge" if world > 1 else ""),
+        "lambda": a.lam, "importance": True, "gpus": world,
+        "parallelism": (f"row-shard x{world} + NCCL all-gather + merge" if rows else
+                        (f"replicas x{world}: every GPU holds all {a.n} rows and answers its own "
+                         f"{a.queries_per_step} queries per step, no data-path collective" if world > 1
+                         else "one GPU")),
         "l2": "inputs larger than L2: each step streams the fp16 rows, "
-              f"{a.n // world * ((a.dim + 7) // 8 * 16 + 4) / 1e9:.3f} GB per GPU (L2 126 MB)",
+              f"{per_gpu * ((a.dim + 7) // 8 * 16 + 8) / 1e9:.3f} GB per GPU (L2 126 MB)",
     }
 
 
@@ -240,10 +253,13 @@ def run_mars(a):
         dist = dist_mod
         dist.init_process_group("nccl", timeout=timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
-    lo, hi = a.n * rank // world, a.n * (rank + 1) // world
+    # rows: shard r holds rows [r N / G, (r + 1) N / G) and answers every
+    # query; replicas: every rank holds all rows and answers its own queries
+    sharded = world > 1 and a.shard == "rows"
+    lo, hi = (a.n * rank // world, a.n * (rank + 1) // world) if sharded else (0, a.n)
     n_local = hi - lo
     E, mod, ts, imp = datagen.gaussian_rows(lo, hi, a.dim, seed=a.seed, ts_max=a.ts_max)
-    Qh = datagen.queries(64, a.dim, seed=a.seed + 1)
+    Qh = datagen.queries(64, a.dim, seed=a.seed + 1 + (0 if sharded else 1000 * rank))
     store = mb.Store(n_local, a.dim, device=local)
     store.upload(E, mod, ts, imp)
     ctx = mb.QueryContext(n_local, a.dim, max_k=a.k, device=local)
@@ -254,7 +270,7 @@ def run_mars(a):
     Qd = torch.from_numpy(Qh).cuda()
     ids = torch.empty((Q, K), dtype=torch.int32, device="cuda")
     vals = torch.empty((Q, K), dtype=torch.float32, device="cuda")
-    if world > 1:
+    if sharded:
         gids = torch.empty((world, Q, K), dtype=torch.int32, device="cuda")
         gvals = torch.empty((world, Q, K), dtype=torch.float32, device="cuda")
         mids = torch.empty((Q, K), dtype=torch.int32, device="cuda")
@@ -274,7 +290,7 @@ def run_mars(a):
         base = (i * Q) % (Qd.shape[0] - Q + 1)
         ev_a[i].record(stream)
         batch(Qd[base:base + Q], ids, vals)
-        if world > 1:
+        if sharded:
             dist.all_gather_into_tensor(gids, ids)
             dist.all_gather_into_tensor(gvals, vals)
             ctx.topk_merge_batch(gids, gvals, world, K, Q, mids, mvals, stream=ctx.stream)
@@ -358,14 +374,14 @@ def run_mars(a):
     qbuf = torch.empty((Q, a.dim), dtype=torch.float32, device="cuda")
     out_ids = torch.empty((Q, K), dtype=torch.int32).pin_memory()
     out_vals = torch.empty((Q, K), dtype=torch.float32).pin_memory()
-    res_ids, res_vals = (mids, mvals) if world > 1 else (ids, vals)
+    res_ids, res_vals = (mids, mvals) if sharded else (ids, vals)
     barrier()
     t0 = time.perf_counter()
     for s in range(a.steps):
         base = (s * Q) % (64 - Q + 1)
         qbuf.copy_(Qpin[base:base + Q], non_blocking=True)
         batch(qbuf, ids, vals)
-        if world > 1:
+        if sharded:
             dist.all_gather_into_tensor(gids, ids)
             dist.all_gather_into_tensor(gvals, vals)
             ctx.topk_merge_batch(gids, gvals, world, K, Q, mids, mvals, stream=ctx.stream)
@@ -377,10 +393,12 @@ def run_mars(a):
         t = torch.tensor([dt], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = float(t.item())
-    e2e = {"value": a.steps * Q / dt, "unit": "queries/s",
+    q_all = Q * (1 if sharded else world)   # queries answered per step by the whole job
+    e2e = {"value": a.steps * q_all / dt, "unit": "queries/s",
            "h2d_bytes_per_step": Q * a.dim * 4, "d2h_bytes_per_step": Q * K * 8,
            "path": "pinned H2D of the step's queries, mars_query_batch_topk"
-                   + (" per shard, NCCL all-gather, mars_topk_merge_batch" if world > 1 else "")
+                   + (" per shard, NCCL all-gather, mars_topk_merge_batch" if sharded else
+                      (" on every replica" if world > 1 else ""))
                    + ", D2H of the top-K ids and scores, stream synchronize"}
     latency = None
     if world == 1:
@@ -400,8 +418,10 @@ def run_mars(a):
     if rank == 0:
         peak, peak_kind = measured_peak()
         pitch16 = (a.dim + 7) // 8 * 8
-        qtiles = (Q + 127) // 128
-        gemm_bytes = qtiles * n_local * (pitch16 * 2 + 4)
+        # small batches (path 3) read each row once; the 128-query tiles once
+        # per query tile; rows carry a timestamp and an importance (4 + 4 B)
+        qtiles = 1 if bstats and bstats.get("path") == 3 else (Q + 127) // 128
+        gemm_bytes = qtiles * n_local * (pitch16 * 2 + 8)
         mean_gemm = statistics.mean(gemm_ms)
         achieved = gemm_bytes / (mean_gemm * 1e-3) / 1e9
         tr = committed_traffic()
@@ -410,11 +430,12 @@ def run_mars(a):
             traffic = tr["dram_bytes"] * n_local / tr["n_rows"]
         scan_bytes = n_local * (a.dim * 4 + 4 + 4)
         scan_med = float(np.median(scan_ms))
-        qps = a.steps * Q / (elapsed_ms * 1e-3)
+        qps = a.steps * q_all / (elapsed_ms * 1e-3)
         line = {
             "metric": metric_name(a), "value": qps, "unit": "queries/s", "n_gpus": world,
             "steps": a.steps, "warmup": a.warmup, "ms_per_step": elapsed_ms / a.steps,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "higher_is_better": True, "scaling": "strong" if sharded or world == 1 else "weak",
+            "vs_baseline": None,
             "dtype": "f32 results (exact; fp16 tensor-core short list, fp32 rescore)",
             "data": "synthetic (seeded Gaussian corpus and queries)",
             "config": config_dict(a, world),
@@ -424,11 +445,13 @@ def run_mars(a):
             "step_ms_p99": float(np.percentile(step_ms, 99)),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
-                         "kernel": "batch::gemm_kernel<kCandidates, f16> (the candidates pass)",
+                         "kernel": ("batch::gemm_small_kernel<kCandidates> (the candidates pass, 128 rows x "
+                                    f"{Q} queries per tile)" if bstats and bstats.get("path") == 3 else
+                                    "batch::gemm_kernel<kCandidates> (the candidates pass)"),
                          "kernel_ms": mean_gemm,
                          "algorithmic_bytes_per_launch": gemm_bytes,
-                         "bytes_note": "fp16 rows (pitch %d halves) once per 128-query tile plus a 4-byte "
-                                       "row weight" % pitch16},
+                         "bytes_note": "fp16 rows (pitch %d halves) plus a timestamp and an importance "
+                                       "per row, once per query tile (one tile at B <= 64)" % pitch16},
             "batch_stats": bstats,
             "fused_scan": {
                 "note": "the fp32 fused scan (score x decay x importance -> top-K), event-timed "
@@ -440,7 +463,9 @@ def run_mars(a):
                 "multi_query_launch_qps": Q / (float(np.median(multi_ms)) * 1e-3),
                 "f16_filtered_launch_qps": Q / (float(np.median(f16_ms)) * 1e-3)},
             "e2e": e2e,
-            "gpu_launches": a.steps * (7 + (1 if world > 1 else 0)),
+            # per step and GPU: query prep, sample pass, threshold, candidates
+            # pass, rescore, device rescan (+ the merge when sharded); all GPUs
+            "gpu_launches": a.steps * world * (6 + (1 if sharded else 0)),
             "clocks": clocks,
         }
         if world == 1 and not a.no_cpu_baseline:

@@ -68,12 +68,31 @@ constexpr float kMarginRel = 2.6e-3f;
 
 enum Mode { kSample = 0, kCandidates = 1 };
 
+// What a row's fused score multiplies its dot product by: the decay
+// exp(-lambda * max(0, t_q - ts)), times the importance when asked, NaN for a
+// row of another modality than the filter's (never a candidate).  The same
+// expression as the exact score's, computed where it is needed.
+struct RowMeta {
+    const float* ts;
+    const float* imp;
+    const int32_t* mod;
+    float t_q, lambda;
+    int32_t filter, use_imp;
+};
+
+__device__ __forceinline__ float row_weight(const RowMeta& m, int32_t row) {
+    if (m.filter >= 0 && __ldg(m.mod + row) != m.filter) return NAN;
+    float w = __expf(-m.lambda * fmaxf(0.0f, m.t_q - __ldg(m.ts + row)));
+    if (m.use_imp) w = w * __ldg(m.imp + row);
+    return w;
+}
+
 struct GemmArgs {
     int32_t B, n, nkb;               // queries, rows, K blocks
     int32_t qtiles, rtiles;          // tiles along queries / rows
     int32_t n_tiles;                 // total tiles of this launch
     const int32_t* sample_rt;        // sample mode: row tile of sample tile i
-    const float* wts;                // n row weights (NaN = rejected)
+    RowMeta meta;                    // row weights
     const float* theta;              // B thresholds (candidate mode)
     const float* margin;             // B margins
     float* sample_buf;               // [n_tiles][B][kJ]
@@ -211,7 +230,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
             const float th = (MODE == kCandidates && qv) ? __ldg(a.theta + q) : 0.f;
             const float mg = qv ? __ldg(a.margin + q) : 0.f;
             asm volatile("bar.sync 1, 128;" ::: "memory");   // previous tile's reads of s_w done
-            for (int i = et; i < kBN; i += 128) s_w[i] = (row0 + i < a.n) ? __ldg(a.wts + row0 + i) : NAN;
+            for (int i = et; i < kBN; i += 128) s_w[i] = (row0 + i < a.n) ? row_weight(a.meta, row0 + i) : NAN;
             asm volatile("bar.sync 1, 128;" ::: "memory");
             if (!sm100::mbar_wait(tfull + buf, bphase, a.err, 5)) break;
             sm100::tc_fence_after();
@@ -274,45 +293,19 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
 }
 
 // ---------------------------------------------------------------------------
-// Row weights and per-query margins.
-__global__ void prep_rows_kernel(const float* __restrict__ ts, const float* __restrict__ imp,
-                                 const int32_t* __restrict__ mod, int32_t n, float t_q, float lambda,
-                                 int32_t filter, int32_t use_imp, float* __restrict__ wts) {
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        float w;
-        if (filter >= 0 && mod[i] != filter) {
-            w = NAN;
-        } else {
-            w = __expf(-lambda * fmaxf(0.0f, t_q - ts[i]));
-            if (use_imp) w = w * imp[i];
-        }
-        wts[i] = w;
-    }
-}
-
-// fp16 copies of the queries (prep_queries_kernel flags a query with a
-// component outside the fp16 range that the error margin covers).
-__global__ void to_f16_queries_kernel(const float* __restrict__ Q, int64_t qpitch, int32_t B, int32_t dim,
-                                      __half* __restrict__ Q16, int64_t pitch16) {
-    const int64_t total = (int64_t)B * pitch16;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t b = i / pitch16, d = i % pitch16;
-        Q16[b * pitch16 + d] = __float2half_rn(d < dim ? Q[b * qpitch + d] : 0.0f);
-    }
-}
-
-// Per query: the error margin, the fp16 range flag, and the per-call
-// counters zeroed (candidate count, rescored count; the error word by query 0).
+// Per query (one warp): the error margin, the fp16 range flag, the fp16 copy
+// of the query when q16 is given (rows of pitch16 halves, zero padded), and
+// the per-call counters zeroed (candidate count, rescored count; the error
+// word by query 0).
 __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch, int32_t B, int32_t nc,
                                     const unsigned int* __restrict__ norm_bits, int32_t f16,
                                     float* __restrict__ margin, int32_t* __restrict__ cand_cnt,
                                     int32_t* __restrict__ rescored, int32_t* __restrict__ bad,
-                                    int32_t* __restrict__ err) {
+                                    int32_t* __restrict__ err, __half* __restrict__ q16, int32_t pitch16) {
     const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
     if (warp >= B) return;
     const float4* q = reinterpret_cast<const float4*>(Q + (int64_t)warp * qpitch);
+    __half2* h = q16 != nullptr ? reinterpret_cast<__half2*>(q16 + (int64_t)warp * pitch16) : nullptr;
     float s = 0.f;
     bool out = false;
     for (int c = lane; c < nc; c += 32) {
@@ -320,7 +313,13 @@ __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch,
         s += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
         out = out || !(fabsf(v.x) <= kF16Max) || !(fabsf(v.y) <= kF16Max) || !(fabsf(v.z) <= kF16Max) ||
               !(fabsf(v.w) <= kF16Max);
+        if (h != nullptr) {
+            h[2 * c] = __floats2half2_rn(v.x, v.y);
+            h[2 * c + 1] = __floats2half2_rn(v.z, v.w);
+        }
     }
+    if (h != nullptr)
+        for (int p = 2 * nc + lane; p < pitch16 / 2; p += 32) h[p] = __floats2half2_rn(0.0f, 0.0f);
     s = warp_butterfly_sum(s);
     out = __any_sync(0xffffffffu, out);
     if (lane == 0) {
@@ -438,7 +437,7 @@ __global__ void __launch_bounds__(kRescoreThreads)
 rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t B, float t_q,
                float lambda, int32_t use_imp, int32_t K, int32_t row_offset,
                const float* __restrict__ theta, const float* __restrict__ margin,
-               const float* __restrict__ wts, const int32_t* __restrict__ cand,
+               const RowMeta meta, const int32_t* __restrict__ cand,
                const float* __restrict__ cand_f, const int32_t* __restrict__ cand_cnt, int32_t cap,
                int32_t* __restrict__ out_ids, float* __restrict__ out_vals,
                int32_t* __restrict__ out_cnt, int32_t* __restrict__ fallback,
@@ -469,7 +468,7 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     // ---- pass 1: lower bounds, completeness, K-th largest lower bound -------
     int ge = 0;
     for (int i = threadIdx.x; i < nc_; i += kRescoreThreads) {
-        const float lo = cf[i] - m * fabsf(__ldg(wts + ci[i]));
+        const float lo = cf[i] - m * fabsf(row_weight(meta, ci[i]));
         ge += (lo >= th) ? 1 : 0;
         s_key[i] = lo;
     }
@@ -498,7 +497,7 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         bool keep = false;
         if (i < nc_) {
             r = ci[i];
-            keep = cf[i] + m * fabsf(__ldg(wts + r)) >= th2;
+            keep = cf[i] + m * fabsf(row_weight(meta, r)) >= th2;
         }
         const unsigned mk = __ballot_sync(0xffffffffu, keep);
         int base = 0;
@@ -530,7 +529,7 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
             bool keep = false;
             if (i < nc_) {
                 r = ci[i];
-                keep = cf[i] + m * fabsf(__ldg(wts + r)) >= th2;
+                keep = cf[i] + m * fabsf(row_weight(meta, r)) >= th2;
             }
             // the first kRowsCap kept rows (in list order) are done; ranks are
             // not known here, so every kept row not in the list is scored by
@@ -595,7 +594,7 @@ struct SmallArgs {
     int32_t stages;                  // row stages in the ring
     uint32_t tmem_cols;              // columns allocated (power of two >= 2 NQ, >= 32)
     const int32_t* sample_rt;        // sample mode: 128-row tile of sample tile i
-    const float* wts;
+    RowMeta meta;
     const float* theta;
     const float* margin;
     float* sample_buf;               // sample mode: [n_tiles][B][kSmallWarps]
@@ -714,7 +713,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
         uint32_t bphase = 0;
         for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
             const int row = (MODE == kSample ? a.sample_rt[t] : t) * kSmallRows + rt;
-            const float w = row < a.n ? __ldg(a.wts + row) : NAN;   // NaN: never a candidate
+            const float w = row < a.n ? row_weight(a.meta, row) : NAN;   // NaN: never a candidate
             if (!sm100::mbar_wait(tfull + buf, bphase, a.err, 16)) break;
             sm100::tc_fence_after();
             for (int q0 = 0; q0 < a.NQ; q0 += 16) {
@@ -787,7 +786,6 @@ struct mars_batch_ctx {
     int32_t cap = 0;
     int32_t num_sms = 0;
     cudaStream_t stream = nullptr;
-    float* d_wts = nullptr;          // max_nodes
     float* d_margin = nullptr;       // max_batch
     float* d_theta = nullptr;
     int32_t* d_cand = nullptr;       // max_batch * cap
@@ -918,7 +916,6 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     T(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
     T(cudaEventCreate(&c->ev_gemm[0]), "event");
     T(cudaEventCreate(&c->ev_gemm[1]), "event");
-    T(cudaMalloc(&c->d_wts, (size_t)max_nodes * 4 + 16), "weights");
     T(cudaMalloc(&c->d_margin, (size_t)max_batch * 4), "margins");
     T(cudaMalloc(&c->d_theta, (size_t)max_batch * 4), "thresholds");
     T(cudaMalloc(&c->d_cand, (size_t)max_batch * c->cap * 4), "candidates");
@@ -975,7 +972,7 @@ int mars_batch_ctx_destroy(mars_batch_ctx* c) {
     if (c == nullptr) return MARS_OK;
     MarsDeviceGuard g(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
-    cudaFree(c->d_wts); cudaFree(c->d_margin); cudaFree(c->d_theta); cudaFree(c->d_cand);
+    cudaFree(c->d_margin); cudaFree(c->d_theta); cudaFree(c->d_cand);
     cudaFree(c->d_cand_f); cudaFree(c->d_sample); cudaFree(c->d_sample_rt);
     cudaFree(c->d_status); cudaFreeHost(c->h_status);
     cudaFree(c->d_q16);
@@ -1125,9 +1122,10 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
             stages = (int32_t)std::min<size_t>(kSmallMaxStages, ((size_t)c->max_smem - fixed) / kSmallStage);
     }
     bool small = stages >= 2;
-    if (small) {   // the same one-in-48 rule over 128-row tiles
+    if (small) {   // the same one-in-48 rule over 128-row tiles, at most one wave of them
         const int32_t tiles128 = (n + kSmallRows - 1) / kSmallRows;
-        const int32_t ns = std::max(1, std::min((int32_t)std::ceil((double)n / (48.0 * kSmallRows)), tiles128 - 1));
+        const int32_t ns = std::max(1, std::min({(int32_t)std::ceil((double)n / (48.0 * kSmallRows)), tiles128 - 1,
+                                                 c->num_sms}));
         const double mu_s = (double)K * std::min<int64_t>((int64_t)ns * kSmallRows, n) / std::max(n, 1);
         const int32_t js = (int32_t)std::ceil(mu_s + 5.0 * std::sqrt(mu_s) + 3.0);
         small = js <= kThrKeep;
@@ -1165,10 +1163,6 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     }
 
     if (f16) {
-        const int64_t total = (int64_t)B * c->q16_pitch;
-        to_f16_queries_kernel<<<(int)std::min<int64_t>((total + 255) / 256, 148 * 8), 256, 0, st>>>(
-            d_queries, query_pitch, B, s->dim, c->d_q16, c->q16_pitch);
-        MARS_CUDA_TRY(cudaGetLastError());
         MARS_TRY(cached_map(c->map_q, c->d_q16, B, c->q16_pitch, c->q16_pitch, small ? NQ : kBM, true));
         MARS_TRY(cached_map(c->map_e, s->d_E16, n, s->e16_pitch, s->e16_pitch, tile_rows, true));
         nkb = (s->e16_pitch + 63) / 64;
@@ -1179,14 +1173,18 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     const CUtensorMap& mq = c->map_q.map;
     const CUtensorMap& me = c->map_e.map;
 
-    const int wblocks = std::min((n + 255) / 256, c->num_sms * 8);
-    prep_rows_kernel<<<wblocks, 256, 0, st>>>(s->d_ts, s->d_imp, s->d_mod, n, t_q, lambda, modality_filter,
-                                              use_importance, c->d_wts);
-    MARS_CUDA_TRY(cudaGetLastError());
+    RowMeta meta{};
+    meta.ts = s->d_ts;
+    meta.imp = s->d_imp;
+    meta.mod = s->d_mod;
+    meta.t_q = t_q;
+    meta.lambda = lambda;
+    meta.filter = modality_filter;
+    meta.use_imp = use_importance;
     prep_queries_kernel<<<(B * 32 + 255) / 256, 256, 0, st>>>(d_queries, query_pitch, B, (s->dim + 3) / 4,
                                                               s->d_norm_bits, f16 ? 1 : 0, c->d_margin,
                                                               c->d_cand_cnt, c->d_rescored, c->d_bad,
-                                                              c->d_err);
+                                                              c->d_err, f16 ? c->d_q16 : nullptr, c->q16_pitch);
     MARS_CUDA_TRY(cudaGetLastError());
 
     if (small) {
@@ -1200,7 +1198,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         while (cols < 2u * (uint32_t)NQ) cols <<= 1;
         sa.tmem_cols = cols;
         sa.sample_rt = c->d_sample_rt;
-        sa.wts = c->d_wts;
+        sa.meta = meta;
         sa.theta = c->d_theta;
         sa.margin = c->d_margin;
         sa.sample_buf = c->d_sample;
@@ -1231,7 +1229,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         ga.qtiles = qtiles;
         ga.rtiles = rtiles;
         ga.sample_rt = c->d_sample_rt;
-        ga.wts = c->d_wts;
+        ga.meta = meta;
         ga.theta = c->d_theta;
         ga.margin = c->d_margin;
         ga.sample_buf = c->d_sample;
@@ -1270,7 +1268,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     v.E = s->d_E; v.ts = s->d_ts; v.imp = s->d_imp; v.mod = s->d_mod; v.d_n = s->d_n;
     v.pitch4 = s->pitch / 4; v.nc = (s->dim + 3) / 4;
     rescore_kernel<<<B, kRescoreThreads, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, use_importance, K,
-                                                  row_offset, c->d_theta, c->d_margin, c->d_wts, c->d_cand,
+                                                  row_offset, c->d_theta, c->d_margin, meta, c->d_cand,
                                                   c->d_cand_f, c->d_cand_cnt, c->cap, d_ids, d_vals, d_counts,
                                                   c->d_fallback, c->d_rescored, f16 ? c->d_bad : nullptr);
     MARS_CUDA_TRY(cudaGetLastError());
