@@ -42,6 +42,12 @@ int store_f16_rows(const mars_store* s, cudaStream_t st, bool* ok);
 constexpr int kF16Slots = 16;
 constexpr int kF16CandCap = 65536;
 int query_ctx_f16_buffers(mars_query_ctx* c);
+// mars_query through the fp16-filtered scan (hop-free queries over large
+// stores); *done = 0 when the caller must answer with the fp32 kernel.
+constexpr int32_t kF16QueryRows = 1 << 18;
+int query_f16(const mars_store* s, mars_query_ctx* c, const float* query, float t_q,
+              const mars_retrieval_config* cfg, mars_query_result* out, int32_t* n_out,
+              mars_retrieval_stats* stats, int* done);
 
 int fail(int status, const std::string& msg);
 int cuda_fail(cudaError_t e, const char* what, const char* file, int line);
@@ -207,6 +213,8 @@ struct mars_query_ctx {
     int32_t* d_f16_overflow = nullptr;          // kF16Slots flags, then kF16Slots x (candidates, survivors)
     int32_t* h_f16_overflow = nullptr;          // pinned copy
     uint64_t f16_reruns = 0;                    // queries re-run on the fp32 scan
+    int32_t* d_f16_qout = nullptr;              // one query's packed results (mars_query):
+    int32_t* h_f16_qout = nullptr;              //   [overflow, count, -, -, ids K, scores K, modalities K]
     int32_t f16_max_cand = 0;                   // largest candidate list of the last call
     int32_t f16_max_surv = 0;                   // largest survivor count of the last call (-1: overflow)
 

@@ -332,6 +332,8 @@ int mars_query_ctx_destroy(mars_query_ctx* c) {
     cudaFree(c->d_f16_overflow);
     cudaFree(c->d_f16_cand);
     cudaFreeHost(c->h_f16_overflow);
+    cudaFree(c->d_f16_qout);
+    cudaFreeHost(c->h_f16_qout);
     cudaFree(c->d_stamp);
     cudaFree(c->d_vis_ids);
     cudaFree(c->d_vis_score);
@@ -391,6 +393,14 @@ int mars_query(const mars_store* s, mars_query_ctx* c, const float* query, float
     uint32_t epoch = next_epoch(c, st, &rc);
     MARS_TRY(rc);
 
+    if (c->use_fused && cfg->bfs_max_hops == 0 && s->n >= kF16QueryRows && cfg->top_k <= 64 &&
+        (s->dim & 3) == 0) {
+        // a hop-free query over a large store: streaming the fp16 copy halves
+        // the bytes, with the same results
+        int done = 0;
+        MARS_TRY(query_f16(s, c, query, t_q, cfg, out, n_out, stats, &done));
+        if (done) return MARS_OK;
+    }
     if (c->use_fused && cfg->top_k <= kFusedMaxK && (s->dim + 3) / 4 <= kFusedMaxChunks) {
         int done = 0;
         MARS_TRY(query_single_launch(s, c, query, t_q, epoch, cfg, out, n_out, stats, &done));
@@ -521,6 +531,8 @@ int mars::query_ctx_f16_buffers(mars_query_ctx* c) {
     MARS_CUDA_TRY(cudaMemset(c->d_f16_cnt, 0, kF16Slots * sizeof(int32_t)));
     MARS_CUDA_TRY(cudaMemset(c->d_f16_overflow, 0, 3 * kF16Slots * sizeof(int32_t)));
     MARS_CUDA_TRY(cudaMalloc(&c->d_f16_cand, (size_t)kF16Slots * kF16CandCap * sizeof(unsigned long long)));
+    MARS_CUDA_TRY(cudaMalloc(&c->d_f16_qout, (4 + 3 * (size_t)c->max_k) * sizeof(int32_t)));
+    MARS_CUDA_TRY(cudaMallocHost(&c->h_f16_qout, (4 + 3 * (size_t)c->max_k) * sizeof(int32_t)));
     return MARS_OK;
 }
 

@@ -52,6 +52,7 @@ struct Scan16Args {
     int32_t cand_cap;
     int32_t* overflow;                // [nq]: 1 = the candidate list overflowed
     int32_t* stats;                   // [nq][2]: candidates, survivors of the last CTA's filter
+    int32_t* out_mod;                 // [nq][K] modality of each result (may be null)
 };
 
 __device__ __forceinline__ uint4 ldg_stream_u4(const void* p) {
@@ -346,6 +347,8 @@ __global__ void __launch_bounds__(kScanThreads, 2) scan16_kernel(const __grid_co
         const bool valid = pp < cnt;
         a.out_val[(int64_t)qi * K + pp] = valid ? key_score(keys[pp]) : -INFINITY;
         a.out_idx[(int64_t)qi * K + pp] = valid ? key_id(keys[pp]) : -1;
+        if (p.out_mod != nullptr)
+            p.out_mod[(int64_t)qi * K + pp] = valid ? __ldg(a.s.mod + (key_id(keys[pp]) - id_off)) : -1;
     }
     if (threadIdx.x == 0) {
         if (a.out_cnt != nullptr) a.out_cnt[qi] = cnt;
@@ -478,5 +481,99 @@ extern "C" int mars_query_ctx_f16_stats(const mars_query_ctx* c, uint64_t* rerun
     if (reruns != nullptr) *reruns = c->f16_reruns;
     if (max_candidates != nullptr) *max_candidates = c->f16_max_cand;
     if (max_survivors != nullptr) *max_survivors = c->f16_max_surv;
+    return MARS_OK;
+}
+
+int mars::query_f16(const mars_store* s, mars_query_ctx* c, const float* query, float t_q,
+                    const mars_retrieval_config* cfg, mars_query_result* out, int32_t* n_out,
+                    mars_retrieval_stats* stats, int* done) {
+    *done = 0;
+    cudaStream_t st = c->stream;
+    bool ok = false;
+    MARS_TRY(store_f16_rows(s, st, &ok));
+    if (!ok) return MARS_OK;   // values beyond the fp16 range
+    MARS_TRY(query_ctx_f16_buffers(c));
+    const int K = cfg->top_k;
+    // the query on the device: in place when aligned, else through the
+    // context's descriptor buffer
+    const float* dq = nullptr;
+    cudaPointerAttributes pa{};
+    const bool on_device = cudaPointerGetAttributes(&pa, query) == cudaSuccess && pa.type == cudaMemoryTypeDevice;
+    (void)cudaGetLastError();
+    float* d_slot = reinterpret_cast<float*>(static_cast<char*>(c->d_desc) + kDescQueryOffset);
+    if (on_device && (reinterpret_cast<uintptr_t>(query) & 15u) == 0) {
+        dq = query;
+    } else if (on_device) {
+        MARS_CUDA_TRY(cudaMemcpyAsync(d_slot, query, (size_t)s->dim * sizeof(float), cudaMemcpyDeviceToDevice, st));
+        dq = d_slot;
+    } else {
+        float* h_slot = reinterpret_cast<float*>(static_cast<char*>(c->h_desc) + kDescQueryOffset);
+        std::memcpy(h_slot, query, (size_t)s->dim * sizeof(float));
+        MARS_CUDA_TRY(cudaMemcpyAsync(d_slot, h_slot, (size_t)s->dim * sizeof(float), cudaMemcpyHostToDevice, st));
+        dq = d_slot;
+    }
+    Scan16Args p{};
+    ScanArgs& a = p.a;
+    a.s.E = s->d_E;
+    a.s.ts = s->d_ts;
+    a.s.imp = s->d_imp;
+    a.s.mod = s->d_mod;
+    a.s.d_n = s->d_n;
+    a.s.pitch4 = s->pitch / 4;
+    a.s.nc = (s->dim + 3) / 4;
+    a.d.t_q = t_q;
+    a.d.lambda = cfg->time_decay_lambda;
+    a.d.filter = cfg->modality_filter;
+    a.d.use_imp = cfg->use_importance;
+    a.d.K = K;
+    a.part_val = c->d_part_val;
+    a.part_idx = c->d_part_idx;
+    a.ticket = c->d_f16_ticket;
+    int32_t* qo = c->d_f16_qout;
+    a.out_cnt = qo + 1;
+    a.out_idx = qo + 4;
+    a.out_val = reinterpret_cast<float*>(qo + 4 + K);
+    p.out_mod = qo + 4 + 2 * K;
+    p.Q = dq;
+    p.qpitch = s->dim;
+    p.E16 = static_cast<const __half*>(s->d_E16);
+    p.pitch16 = s->e16_pitch;
+    p.nc16 = (s->dim + 7) / 8;
+    p.norm_bits = s->d_norm_bits;
+    p.cand = c->d_f16_cand;
+    p.cand_cnt = c->d_f16_cnt;
+    p.cand_cap = kF16CandCap;
+    p.overflow = qo;
+    p.stats = c->d_f16_overflow + kF16Slots;
+    if (stats) MARS_CUDA_TRY(cudaEventRecord(c->ev[0], st));
+    MARS_CUDA_TRY(launch_scan16(p, std::min(c->scan_blocks, 2 * c->num_sms), 1, st));
+    if (stats) MARS_CUDA_TRY(cudaEventRecord(c->ev[2], st));
+    MARS_CUDA_TRY(cudaMemcpyAsync(c->h_f16_qout, qo, (4 + 3 * (size_t)K) * sizeof(int32_t), cudaMemcpyDeviceToHost,
+                                  st));
+    MARS_CUDA_TRY(cudaStreamSynchronize(st));
+    const int32_t* h = c->h_f16_qout;
+    if (h[0] != 0) {   // the candidate list overflowed
+        ++c->f16_reruns;
+        return MARS_OK;
+    }
+    const int32_t cnt = std::min(h[1], K);
+    for (int32_t i = 0; i < cnt; ++i) {
+        out[i].node_id = h[4 + i];
+        std::memcpy(&out[i].score, h + 4 + K + i, sizeof(float));
+        out[i].modality = h[4 + 2 * K + i];
+        out[i].hops_from_seed = 0;
+    }
+    *n_out = cnt;
+    if (stats) {
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, c->ev[0], c->ev[2]);
+        *stats = mars_retrieval_stats{};
+        stats->gpu_ms_similarity = ms;
+        stats->gpu_ms_total = ms;
+        stats->nodes_scanned = s->n;
+        stats->nodes_visited = cnt;
+    }
+    ++c->fused_queries;
+    *done = 1;
     return MARS_OK;
 }

@@ -191,7 +191,11 @@ int mars_query_ctx_destroy(mars_query_ctx* ctx);
  * top-K seeds -> BFS over the store's graph -> best top_k visited nodes by
  * (score desc, id asc).  query: host or device, D floats.  out: host array
  * of cfg->top_k entries; *n_out receives the count.  stats may be NULL.
- * Blocks until the results are on the host (like the reference). */
+ * Blocks until the results are on the host (like the reference).  A query
+ * without BFS hops over a store of at least 2^18 rows (top_k <= 64, D a
+ * multiple of 4, values within the fp16 range) streams the store's fp16 copy
+ * through the exact fp16-filtered scan (mars_scan_topk_f16): same results,
+ * half the bytes. */
 int mars_query(const mars_store* s, mars_query_ctx* ctx, const float* query,
                float query_timestamp, const mars_retrieval_config* cfg,
                mars_query_result* out, int32_t* n_out,
@@ -470,7 +474,8 @@ int mars_query_ctx_use_graph(mars_query_ctx* ctx, int32_t enable);
  * results are the same either way.  enable = 0 always uses the pipeline. */
 int mars_query_ctx_use_fused(mars_query_ctx* ctx, int32_t enable);
 
-/* Number of mars_query calls answered by the single launch, and of those
+/* Number of mars_query calls answered by a single launch (the fused query
+ * kernel, or the fp16-filtered scan for large hop-free queries), and of those
  * that had to be answered again by the pipeline.  Either pointer may be NULL. */
 int mars_query_ctx_path_counts(const mars_query_ctx* ctx, uint64_t* fused, uint64_t* reruns);
 

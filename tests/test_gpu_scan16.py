@@ -191,3 +191,46 @@ def test_f16_scan_falls_back_for_large_k_and_odd_dim(torch_mod, mb):
         with pytest.raises(mb.MarsError) as e:
             fn(st2, Q2, 3, 10.0, 0.3, 10, ids, vals)
         assert e.value.status == mb.MARS_ERR_UNSUPPORTED
+
+
+def test_mars_query_uses_the_f16_scan_for_large_hop_free_queries(torch_mod, mb):
+    """mars_query with no BFS hops over >= 2^18 rows streams the fp16 copy:
+    the results (ids, score bits, modalities, hops) equal the fp32 pipeline's."""
+    torch = torch_mod
+    from mars_b200 import datagen
+    N, D = 300_000, 768
+    E, mod, ts, imp = datagen.gaussian_corpus(N, D, seed=31, ts_max=10.0)
+    st = mb.Store(N, D)
+    st.upload(E, mod, ts, imp)
+    fast = mb.QueryContext(N, D, max_k=64)
+    pipe = mb.QueryContext(N, D, max_k=64, use_fused=False)
+    rng = np.random.default_rng(5)
+    for i, K in enumerate((1, 10, 33, 64)):
+        q = rng.standard_normal(D).astype(np.float32)
+        cfg = mb.RetrievalConfig(top_k=K, bfs_max_hops=0, time_decay_lambda=0.2 * i,
+                                 use_importance=bool(i % 2), modality_filter=(i % 3) - 1)
+        a = fast.query(st, q, 10.0, cfg)
+        b = pipe.query(st, q, 10.0, cfg)
+        assert a.tobytes() == b.tobytes(), K
+        # a device-resident query takes the same route
+        c = fast.query(st, torch.from_numpy(q).cuda(), 10.0, cfg)
+        assert c.tobytes() == b.tobytes(), K
+    assert fast.f16_reruns() == 0
+    assert fast.path_counts()[0] == 8
+
+
+def test_mars_query_f16_overflow_falls_back(torch_mod, mb):
+    """Every row identical: the fp16 candidate list overflows and mars_query
+    answers with the fp32 single-launch kernel (same results)."""
+    N, D = 300_000, 64
+    E = np.tile(np.random.default_rng(0).standard_normal((1, D)).astype(np.float32), (N, 1))
+    st = mb.Store(N, D)
+    st.upload(E, np.zeros(N, np.int32), np.zeros(N, np.float32), None)
+    fast = mb.QueryContext(N, D, max_k=16)
+    pipe = mb.QueryContext(N, D, max_k=16, use_fused=False)
+    q = np.random.default_rng(1).standard_normal(D).astype(np.float32)
+    cfg = mb.RetrievalConfig(top_k=10, bfs_max_hops=0, time_decay_lambda=0.0)
+    a = fast.query(st, q, 0.0, cfg)
+    assert a.tobytes() == pipe.query(st, q, 0.0, cfg).tobytes()
+    assert np.array_equal(a["node_id"], np.arange(10))
+    assert fast.f16_reruns() == 1
