@@ -98,6 +98,7 @@ struct GemmArgs {
     float* sample_buf;               // [n_tiles][B][kJ]
     int32_t* cand;                   // [B][cap] row ids
     float* cand_f;                   // [B][cap] approximate fused scores
+    float* cand_s;                   // [B][cap] their error slack (margin x |weight|)
     int32_t* cand_cnt;               // [B]
     int32_t cap;
     int32_t self_base;               // query b leaves out row self_base + b (-1: none)
@@ -260,6 +261,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                                 if (pos < a.cap) {
                                     a.cand[(int64_t)q * a.cap + pos] = rbase + j;
                                     a.cand_f[(int64_t)q * a.cap + pos] = f;
+                                    a.cand_s[(int64_t)q * a.cap + pos] = slack;
                                 }
                             }
                         } else {
@@ -360,14 +362,23 @@ threshold_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tiles, i
 #pragma unroll
     for (int s = 0; s < kThrKeep; ++s) keep[s] = -INFINITY;
     int valid = 0;
-    for (int i = lane; i < total; i += 32) {
-        float x = sample_buf[((int64_t)(i / per_tile) * B + q) * per_tile + (i % per_tile)];
-        if (!(x > -INFINITY)) continue;   // empty slot
-        ++valid;
-        if (x > keep[kThrKeep - 1]) {
+    for (int i0 = lane; i0 < total; i0 += 8 * 32) {
+        float v[8];   // eight loads in flight per lane
 #pragma unroll
-            for (int s = 0; s < kThrKeep; ++s)
-                if (x > keep[s]) { const float t = keep[s]; keep[s] = x; x = t; }
+        for (int k = 0; k < 8; ++k) {
+            const int i = i0 + 32 * k;
+            v[k] = i < total ? sample_buf[((int64_t)(i / per_tile) * B + q) * per_tile + (i % per_tile)] : -INFINITY;
+        }
+#pragma unroll
+        for (int k = 0; k < 8; ++k) {
+            float x = v[k];
+            if (!(x > -INFINITY)) continue;   // empty slot
+            ++valid;
+            if (x > keep[kThrKeep - 1]) {
+#pragma unroll
+                for (int s = 0; s < kThrKeep; ++s)
+                    if (x > keep[s]) { const float t = keep[s]; keep[s] = x; x = t; }
+            }
         }
     }
     valid = warp_reduce_sum_int(valid);
@@ -438,7 +449,8 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
                float lambda, int32_t use_imp, int32_t K, int32_t row_offset,
                const float* __restrict__ theta, const float* __restrict__ margin,
                const RowMeta meta, const int32_t* __restrict__ cand,
-               const float* __restrict__ cand_f, const int32_t* __restrict__ cand_cnt, int32_t cap,
+               const float* __restrict__ cand_f, const float* __restrict__ cand_s,
+               const int32_t* __restrict__ cand_cnt, int32_t cap,
                int32_t* __restrict__ out_ids, float* __restrict__ out_vals,
                int32_t* __restrict__ out_cnt, int32_t* __restrict__ fallback,
                int32_t* __restrict__ rescored, const int32_t* __restrict__ bad) {
@@ -464,11 +476,12 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     const float m = margin[qi];
     const int32_t* ci = cand + (int64_t)qi * cap;
     const float* cf = cand_f + (int64_t)qi * cap;
+    const float* cs = cand_s + (int64_t)qi * cap;   // slack: the exact score lies in cf -+ cs
 
     // ---- pass 1: lower bounds, completeness, K-th largest lower bound -------
     int ge = 0;
     for (int i = threadIdx.x; i < nc_; i += kRescoreThreads) {
-        const float lo = cf[i] - m * fabsf(row_weight(meta, ci[i]));
+        const float lo = cf[i] - cs[i];
         ge += (lo >= th) ? 1 : 0;
         s_key[i] = lo;
     }
@@ -497,7 +510,7 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         bool keep = false;
         if (i < nc_) {
             r = ci[i];
-            keep = cf[i] + m * fabsf(row_weight(meta, r)) >= th2;
+            keep = cf[i] + cs[i] >= th2;
         }
         const unsigned mk = __ballot_sync(0xffffffffu, keep);
         int base = 0;
@@ -529,7 +542,7 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
             bool keep = false;
             if (i < nc_) {
                 r = ci[i];
-                keep = cf[i] + m * fabsf(row_weight(meta, r)) >= th2;
+                keep = cf[i] + cs[i] >= th2;
             }
             // the first kRowsCap kept rows (in list order) are done; ranks are
             // not known here, so every kept row not in the list is scored by
@@ -600,6 +613,7 @@ struct SmallArgs {
     float* sample_buf;               // sample mode: [n_tiles][B][kSmallWarps]
     int32_t* cand;
     float* cand_f;
+    float* cand_s;
     int32_t* cand_cnt;
     int32_t cap;
     int32_t self_base;
@@ -733,6 +747,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                             if (pos < a.cap) {
                                 a.cand[(int64_t)q * a.cap + pos] = row;
                                 a.cand_f[(int64_t)q * a.cap + pos] = f;
+                                a.cand_s[(int64_t)q * a.cap + pos] = slack;
                             }
                         }
                     } else {
@@ -919,7 +934,7 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     T(cudaMalloc(&c->d_margin, (size_t)max_batch * 4), "margins");
     T(cudaMalloc(&c->d_theta, (size_t)max_batch * 4), "thresholds");
     T(cudaMalloc(&c->d_cand, (size_t)max_batch * c->cap * 4), "candidates");
-    T(cudaMalloc(&c->d_cand_f, (size_t)max_batch * c->cap * 4), "candidate scores");
+    T(cudaMalloc(&c->d_cand_f, (size_t)max_batch * c->cap * 8), "candidate scores and slacks");
     const size_t status_words = 2 + 4 * (size_t)max_batch;
     T(cudaMalloc(&c->d_status, status_words * 4), "status words");
     T(cudaMallocHost(&c->h_status, status_words * 4), "pinned status words");
@@ -1204,6 +1219,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         sa.sample_buf = c->d_sample;
         sa.cand = c->d_cand;
         sa.cand_f = c->d_cand_f;
+        sa.cand_s = c->d_cand_f + (size_t)c->max_batch * c->cap;
         sa.cand_cnt = c->d_cand_cnt;
         sa.cap = c->cap;
         sa.self_base = self_base;
@@ -1235,6 +1251,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         ga.sample_buf = c->d_sample;
         ga.cand = c->d_cand;
         ga.cand_f = c->d_cand_f;
+        ga.cand_s = c->d_cand_f + (size_t)c->max_batch * c->cap;
         ga.cand_cnt = c->d_cand_cnt;
         ga.cap = c->cap;
         ga.self_base = self_base;
@@ -1269,7 +1286,8 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     v.pitch4 = s->pitch / 4; v.nc = (s->dim + 3) / 4;
     rescore_kernel<<<B, kRescoreThreads, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, use_importance, K,
                                                   row_offset, c->d_theta, c->d_margin, meta, c->d_cand,
-                                                  c->d_cand_f, c->d_cand_cnt, c->cap, d_ids, d_vals, d_counts,
+                                                  c->d_cand_f, c->d_cand_f + (size_t)c->max_batch * c->cap,
+                                                  c->d_cand_cnt, c->cap, d_ids, d_vals, d_counts,
                                                   c->d_fallback, c->d_rescored, f16 ? c->d_bad : nullptr);
     MARS_CUDA_TRY(cudaGetLastError());
     // 6. exact rescans of the flagged queries (every CTA of an unflagged
