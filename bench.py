@@ -420,8 +420,11 @@ def run_mars(a):
         pitch16 = (a.dim + 7) // 8 * 8
         # small batches (path 3) read each row once; the 128-query tiles once
         # per query tile; rows carry a timestamp and an importance (4 + 4 B)
-        qtiles = 1 if bstats and bstats.get("path") == 3 else (Q + 127) // 128
+        small = bool(bstats and bstats.get("path") == 3)
+        qtiles = 1 if small else (Q + 127) // 128
         gemm_bytes = qtiles * n_local * (pitch16 * 2 + 8)
+        if small:   # the fused pass also streams its sampled 128-row tiles
+            gemm_bytes += bstats.get("sample_tiles", 0) * 128 * (pitch16 * 2 + 8)
         mean_gemm = statistics.mean(gemm_ms)
         achieved = gemm_bytes / (mean_gemm * 1e-3) / 1e9
         tr = committed_traffic()
@@ -445,8 +448,8 @@ def run_mars(a):
             "step_ms_p99": float(np.percentile(step_ms, 99)),
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
-                         "kernel": ("batch::gemm_small_kernel<kCandidates> (the candidates pass, 128 rows x "
-                                    f"{Q} queries per tile)" if bstats and bstats.get("path") == 3 else
+                         "kernel": ("batch::gemm_small_kernel<kFused> (sample, thresholds and candidates in one "
+                                    f"cooperative launch, 128 rows x {Q} queries per tile)" if small else
                                     "batch::gemm_kernel<kCandidates> (the candidates pass)"),
                          "kernel_ms": mean_gemm,
                          "algorithmic_bytes_per_launch": gemm_bytes,
@@ -463,9 +466,10 @@ def run_mars(a):
                 "multi_query_launch_qps": Q / (float(np.median(multi_ms)) * 1e-3),
                 "f16_filtered_launch_qps": Q / (float(np.median(f16_ms)) * 1e-3)},
             "e2e": e2e,
-            # per step and GPU: query prep, sample pass, threshold, candidates
-            # pass, rescore, device rescan (+ the merge when sharded); all GPUs
-            "gpu_launches": a.steps * world * (6 + (1 if sharded else 0)),
+            # per step and GPU: query prep, the fused sample + threshold +
+            # candidates pass (three launches on the 128-query tiles), rescore,
+            # device rescan (+ the merge when sharded); all GPUs
+            "gpu_launches": a.steps * world * ((4 if small else 6) + (1 if sharded else 0)),
             "clocks": clocks,
         }
         if world == 1 and not a.no_cpu_baseline:

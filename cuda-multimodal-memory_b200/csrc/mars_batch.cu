@@ -66,7 +66,7 @@ constexpr int kTmemCols = 512;
 constexpr int kJ = 16;                // sampled lower bounds kept per (query, tile)
 constexpr float kMarginRel = 2.6e-3f;
 
-enum Mode { kSample = 0, kCandidates = 1 };
+enum Mode { kSample = 0, kCandidates = 1, kFused = 2 };
 
 // What a row's fused score multiplies its dot product by: the decay
 // exp(-lambda * max(0, t_q - ts)), times the importance when asked, NaN for a
@@ -351,23 +351,21 @@ __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch,
 constexpr int kThrThreads = 256;
 constexpr int kThrKeep = 32;
 
-__global__ void __launch_bounds__(kThrThreads)
-threshold_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tiles, int32_t B, int32_t j,
-                 int32_t per_tile, float* __restrict__ theta) {
-    const int q = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
-    const int lane = threadIdx.x & 31;
-    if (q >= B) return;
+// The j-th largest of query q's values for one warp (see threshold_kernel).
+__device__ float warp_threshold(const float* __restrict__ sample_buf, int32_t n_sample_tiles, int32_t B, int q,
+                                int32_t j, int32_t per_tile, int lane) {
     const int total = n_sample_tiles * per_tile;
     float keep[kThrKeep];
 #pragma unroll
     for (int s = 0; s < kThrKeep; ++s) keep[s] = -INFINITY;
     int valid = 0;
     for (int i0 = lane; i0 < total; i0 += 8 * 32) {
-        float v[8];   // eight loads in flight per lane
+        float v[8];   // eight loads in flight per lane (L2: other CTAs may have written them)
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
             const int i = i0 + 32 * k;
-            v[k] = i < total ? sample_buf[((int64_t)(i / per_tile) * B + q) * per_tile + (i % per_tile)] : -INFINITY;
+            v[k] = i < total ? __ldcg(sample_buf + ((int64_t)(i / per_tile) * B + q) * per_tile + (i % per_tile))
+                             : -INFINITY;
         }
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -397,6 +395,16 @@ threshold_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tiles, i
             th = m;
         }
     }
+    return th;
+}
+
+__global__ void __launch_bounds__(kThrThreads)
+threshold_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tiles, int32_t B, int32_t j,
+                 int32_t per_tile, float* __restrict__ theta) {
+    const int q = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (q >= B) return;
+    const float th = warp_threshold(sample_buf, n_sample_tiles, B, q, j, per_tile, lane);
     if (lane == 0) theta[q] = th;
 }
 
@@ -599,6 +607,7 @@ constexpr int kSmallRows = 128;
 constexpr int kSmallStage = kSmallRows * 128;      // 16 KB: 128 rows x 64 halves
 constexpr int kSmallMaxStages = 12;
 constexpr int kSmallWarps = 4;                       // epilogue warps: 32 rows each
+constexpr int kSmallStaticSmem = 1024;               // bound on the kernel's static shared memory
 
 struct SmallArgs {
     int32_t B, NQ;                   // queries, MMA N (B rounded up to 16)
@@ -618,7 +627,53 @@ struct SmallArgs {
     int32_t cap;
     int32_t self_base;
     int* err;
+    // kFused: CTA b < n_sample first runs sample tile sample_rt[b]; after
+    // every CTA's sample maxima are written (grid counter), each CTA takes
+    // the thresholds itself; CTA 0 also stores them in theta_out
+    int32_t n_sample, j;
+    unsigned long long* grid_sync;   // monotone arrival counter
+    unsigned long long sync_target;  // its value once every CTA of this launch arrived
+    float* theta_out;
 };
+
+// The it-th tile of this CTA: first row, sample or candidates, and (sample)
+// its index in sample_buf; false past the CTA's last tile.  kFused: the
+// CTA's sample tile (if it has one), then its candidate tiles.
+struct SmallTile {
+    int row0;
+    bool sample;
+    int sidx;
+};
+template <int MODE>
+__device__ __forceinline__ bool small_tile(const SmallArgs& a, int it, SmallTile& tl) {
+    if (MODE == kFused) {
+        const int hs = (int)blockIdx.x < a.n_sample ? 1 : 0;
+        if (it < hs) {
+            tl.row0 = a.sample_rt[blockIdx.x] * kSmallRows;
+            tl.sample = true;
+            tl.sidx = blockIdx.x;
+            return true;
+        }
+        const int t = blockIdx.x + (it - hs) * gridDim.x;
+        if (t >= a.n_tiles) return false;
+        tl.row0 = t * kSmallRows;
+        tl.sample = false;
+        tl.sidx = 0;
+        return true;
+    }
+    const int t = blockIdx.x + it * gridDim.x;
+    if (t >= a.n_tiles) return false;
+    tl.row0 = (MODE == kSample ? a.sample_rt[t] : t) * kSmallRows;
+    tl.sample = MODE == kSample;
+    tl.sidx = t;
+    return true;
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
 
 __host__ __device__ constexpr size_t small_smem_bytes(int nkb, int NQ, int stages) {
     return 1024 /*align*/ + (size_t)nkb * NQ * 128 + (size_t)stages * kSmallStage + 512 /*barriers*/;
@@ -640,6 +695,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     uint64_t* tempty = tfull + 2;
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
+    __shared__ float s_theta[kSmallMaxB];   // kFused: this launch's thresholds
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.stages; ++s) { sm100::mbar_init(full + s, 1); sm100::mbar_init(empty + s, 1); }
@@ -671,8 +727,9 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
             bool issued[kSmallMaxStages];
             for (int s = 0; s < kSmallMaxStages; ++s) { issued[s] = false; issued_phase[s] = 0; }
             bool ok = true;
-            for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
-                const int row0 = (MODE == kSample ? a.sample_rt[t] : t) * kSmallRows;
+            SmallTile tl;
+            for (int it = 0; ok && small_tile<MODE>(a, it, tl); ++it) {
+                const int row0 = tl.row0;
                 for (int kb = 0; kb < a.nkb; ++kb) {
                     if (!sm100::mbar_wait(empty + stage, phase ^ 1u, a.err, 11)) { ok = false; break; }
                     sm100::mbar_arrive_expect_tx(full + stage, kSmallStage);
@@ -698,7 +755,8 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
             uint32_t phase = 0;
             int buf = 0;
             uint32_t bphase = 0;
-            for (int t = blockIdx.x; t < a.n_tiles && ok; t += gridDim.x) {
+            SmallTile tl;
+            for (int it = 0; ok && small_tile<MODE>(a, it, tl); ++it) {
                 if (!sm100::mbar_wait(tempty + buf, bphase ^ 1u, a.err, 14)) break;
                 sm100::tc_fence_after();
                 const uint32_t d = tmem_base + (uint32_t)(buf * a.NQ);
@@ -725,8 +783,36 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
         const int rt = sub * 32 + lane;             // row within the tile
         int buf = 0;
         uint32_t bphase = 0;
-        for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
-            const int row = (MODE == kSample ? a.sample_rt[t] : t) * kSmallRows + rt;
+        bool have_theta = MODE != kFused;
+        SmallTile tl;
+        for (int it = 0; small_tile<MODE>(a, it, tl); ++it) {
+            if (MODE == kFused && !tl.sample && !have_theta) {
+                // every CTA's sample maxima written: a grid-wide arrival count
+                // (the launch is cooperative, so every CTA is resident and the
+                // wait ends; it is bounded all the same)
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (rt == 0) {
+                    __threadfence();
+                    atomicAdd(a.grid_sync, 1ull);
+                    uint32_t spins = 0;
+                    while (ld_acquire_u64(a.grid_sync) < a.sync_target) {
+                        if (++spins > sm100::kSpinLimit) { atomicExch(a.err, 17); break; }
+                        __nanosleep(128);
+                    }
+                    __threadfence();
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                for (int q = sub; q < a.B; q += kSmallWarps) {
+                    const float th = warp_threshold(a.sample_buf, a.n_sample, a.B, q, a.j, kSmallWarps, lane);
+                    if (lane == 0) {
+                        s_theta[q] = th;
+                        if (blockIdx.x == 0) a.theta_out[q] = th;
+                    }
+                }
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                have_theta = true;
+            }
+            const int row = tl.row0 + rt;
             const float w = row < a.n ? row_weight(a.meta, row) : NAN;   // NaN: never a candidate
             if (!sm100::mbar_wait(tfull + buf, bphase, a.err, 16)) break;
             sm100::tc_fence_after();
@@ -741,8 +827,9 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                     const float wq = (a.self_base >= 0 && row == a.self_base + q) ? NAN : w;
                     const float f = __uint_as_float(r[u]) * wq;
                     const float slack = __ldg(a.margin + q) * fabsf(wq);
-                    if (MODE == kCandidates) {
-                        if (f + slack >= __ldg(a.theta + q)) {   // NaN weights never pass
+                    if (!tl.sample) {
+                        const float th = MODE == kFused ? s_theta[q] : __ldg(a.theta + q);
+                        if (f + slack >= th) {   // NaN weights never pass
                             const int pos = atomicAdd(a.cand_cnt + q, 1);
                             if (pos < a.cap) {
                                 a.cand[(int64_t)q * a.cap + pos] = row;
@@ -757,7 +844,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
 #pragma unroll
                         for (int off = 16; off >= 1; off >>= 1)
                             lo = fmaxf(lo, __shfl_xor_sync(0xffffffffu, lo, off));
-                        if (lane == 0) a.sample_buf[((int64_t)t * a.B + q) * kSmallWarps + sub] = lo;
+                        if (lane == 0) a.sample_buf[((int64_t)tl.sidx * a.B + q) * kSmallWarps + sub] = lo;
                     }
                 }
             }
@@ -825,6 +912,8 @@ struct mars_batch_ctx {
     size_t sample_floats_cap = 0;
     int32_t sample_rt_n = -1, sample_rt_rtiles = -1, sample_rt_rows = -1;   // the row-tile list on the device
     int32_t max_smem = 0;            // opt-in shared memory per block
+    unsigned long long* d_grid_sync = nullptr;   // the small-batch launch's arrival counter (monotone)
+    unsigned long long grid_sync_count = 0;      // its value after the launches issued so far
     __half* d_q16 = nullptr;         // max_batch x q16_pitch: fp16 queries
     int32_t q16_pitch = 0;
     int32_t precision = 0;           // 0: fp16 when in range, 1: TF32 always
@@ -959,6 +1048,8 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     T(cudaMalloc(&c->d_fb_slots, (size_t)max_batch * 2 * sizeof(unsigned int)), "rescan slots");
     if (rc == MARS_OK) T(cudaMemset(c->d_fb_slots, 0, (size_t)max_batch * 2 * sizeof(unsigned int)), "memset");
     T(cudaEventCreateWithFlags(&c->ev_status, cudaEventDisableTiming), "event");
+    T(cudaMalloc(&c->d_grid_sync, sizeof(unsigned long long)), "grid counter");
+    if (rc == MARS_OK) T(cudaMemset(c->d_grid_sync, 0, sizeof(unsigned long long)), "memset");
     if (rc == MARS_OK) {
         static bool attr_done[64] = {};
         if (device < 64 && !attr_done[device]) {
@@ -966,8 +1057,9 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
             T(cudaFuncSetAttribute(gemm_kernel<kCandidates, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem), "smem attr");
             T(cudaFuncSetAttribute(gemm_kernel<kSample, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem), "smem attr");
             T(cudaFuncSetAttribute(gemm_kernel<kCandidates, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kGemmSmem), "smem attr");
-            T(cudaFuncSetAttribute(gemm_small_kernel<kSample>, cudaFuncAttributeMaxDynamicSharedMemorySize, c->max_smem), "smem attr");
-            T(cudaFuncSetAttribute(gemm_small_kernel<kCandidates>, cudaFuncAttributeMaxDynamicSharedMemorySize, c->max_smem), "smem attr");
+            T(cudaFuncSetAttribute(gemm_small_kernel<kSample>, cudaFuncAttributeMaxDynamicSharedMemorySize, c->max_smem - kSmallStaticSmem), "smem attr");
+            T(cudaFuncSetAttribute(gemm_small_kernel<kCandidates>, cudaFuncAttributeMaxDynamicSharedMemorySize, c->max_smem - kSmallStaticSmem), "smem attr");
+            T(cudaFuncSetAttribute(gemm_small_kernel<kFused>, cudaFuncAttributeMaxDynamicSharedMemorySize, c->max_smem - kSmallStaticSmem), "smem attr");
             attr_done[device] = rc == MARS_OK;
         }
     }
@@ -992,6 +1084,7 @@ int mars_batch_ctx_destroy(mars_batch_ctx* c) {
     cudaFree(c->d_status); cudaFreeHost(c->h_status);
     cudaFree(c->d_q16);
     cudaFree(c->d_fb_val); cudaFree(c->d_fb_idx); cudaFree(c->d_fb_slots);
+    cudaFree(c->d_grid_sync);
     if (c->ev_status) cudaEventDestroy(c->ev_status);
     mars_query_ctx_destroy(c->scan_ctx);
     for (cudaEvent_t e : c->ev_gemm)
@@ -1133,8 +1226,8 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     int32_t stages = 0;
     if (f16 && B <= kSmallMaxB) {
         const size_t fixed = small_smem_bytes((s->e16_pitch + 63) / 64, NQ, 0);
-        if (fixed < (size_t)c->max_smem)
-            stages = (int32_t)std::min<size_t>(kSmallMaxStages, ((size_t)c->max_smem - fixed) / kSmallStage);
+        const size_t room = (size_t)c->max_smem - kSmallStaticSmem;   // the kernel's static array aside
+        if (fixed < room) stages = (int32_t)std::min<size_t>(kSmallMaxStages, (room - fixed) / kSmallStage);
     }
     bool small = stages >= 2;
     if (small) {   // the same one-in-48 rule over 128-row tiles, at most one wave of them
@@ -1225,17 +1318,23 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         sa.self_base = self_base;
         sa.err = c->d_err;
         const size_t smem = small_smem_bytes(nkb, NQ, stages);
-        // 2. sample, 3. thresholds, 4. candidates
-        sa.n_tiles = n_sample;
-        gemm_small_kernel<kSample><<<std::min(n_sample, c->num_sms), kThreads, smem, st>>>(mq, me, sa);
-        MARS_CUDA_TRY(cudaGetLastError());
-        threshold_kernel<<<(B * 32 + kThrThreads - 1) / kThrThreads, kThrThreads, 0, st>>>(
-            c->d_sample, n_sample, B, j, kSmallWarps, c->d_theta);
-        MARS_CUDA_TRY(cudaGetLastError());
+        // 2.-4. sample, thresholds and candidates in one cooperative launch
+        // (one CTA per SM, every CTA resident): CTA b < n_sample first runs
+        // sample tile b; the epilogue warps meet on a grid-wide counter,
+        // take the thresholds, and go on with the candidate tiles that the
+        // producer and MMA warps have kept streaming meanwhile
+        const int grid = std::min(all_tiles, c->num_sms);
         sa.n_tiles = all_tiles;
+        sa.n_sample = n_sample;
+        sa.j = j;
+        sa.grid_sync = c->d_grid_sync;
+        sa.sync_target = c->grid_sync_count + (unsigned long long)grid;
+        sa.theta_out = c->d_theta;
+        void* args[] = {const_cast<CUtensorMap*>(&mq), const_cast<CUtensorMap*>(&me), &sa};
         MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
-        gemm_small_kernel<kCandidates><<<std::min(all_tiles, c->num_sms), kThreads, smem, st>>>(mq, me, sa);
-        MARS_CUDA_TRY(cudaGetLastError());
+        MARS_CUDA_TRY(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&gemm_small_kernel<kFused>),
+                                                  dim3(grid), dim3(kThreads), args, smem, st));
+        c->grid_sync_count += (unsigned long long)grid;
         MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[1], st));
     } else {
         GemmArgs ga{};
