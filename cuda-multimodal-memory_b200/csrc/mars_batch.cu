@@ -914,6 +914,8 @@ struct mars_batch_ctx {
     int32_t max_smem = 0;            // opt-in shared memory per block
     unsigned long long* d_grid_sync = nullptr;   // the small-batch launch's arrival counter (monotone)
     unsigned long long grid_sync_count = 0;      // its value after the launches issued so far
+    bool coop = false;               // the device runs cooperative launches
+    bool single_launch = false;      // small batches: sample + thresholds + candidates in one launch
     __half* d_q16 = nullptr;         // max_batch x q16_pitch: fp16 queries
     int32_t q16_pitch = 0;
     int32_t precision = 0;           // 0: fp16 when in range, 1: TF32 always
@@ -1014,6 +1016,8 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     c->cap = 16384;
     c->num_sms = prop.multiProcessorCount;
     c->max_smem = (int32_t)prop.sharedMemPerBlockOptin;
+    c->coop = prop.cooperativeLaunch != 0;
+    c->single_launch = c->coop;
     c->sample_tiles_cap = 0;
     int rc = MARS_OK;
     auto T = [&](cudaError_t e, const char* w) { if (rc == MARS_OK && e != cudaSuccess) rc = cuda_fail(e, w, __FILE__, __LINE__); };
@@ -1072,6 +1076,12 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
 int mars_batch_ctx_set_precision(mars_batch_ctx* c, int32_t tf32_only) {
     if (c == nullptr) return fail(MARS_ERR_INVALID, "mars_batch_ctx_set_precision: NULL context");
     c->precision = tf32_only != 0 ? 1 : 0;
+    return MARS_OK;
+}
+
+int mars_batch_ctx_set_single_launch(mars_batch_ctx* c, int32_t enable) {
+    if (c == nullptr) return fail(MARS_ERR_INVALID, "mars_batch_ctx_set_single_launch: NULL context");
+    c->single_launch = enable != 0 && c->coop;
     return MARS_OK;
 }
 
@@ -1318,24 +1328,39 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         sa.self_base = self_base;
         sa.err = c->d_err;
         const size_t smem = small_smem_bytes(nkb, NQ, stages);
-        // 2.-4. sample, thresholds and candidates in one cooperative launch
-        // (one CTA per SM, every CTA resident): CTA b < n_sample first runs
-        // sample tile b; the epilogue warps meet on a grid-wide counter,
-        // take the thresholds, and go on with the candidate tiles that the
-        // producer and MMA warps have kept streaming meanwhile
         const int grid = std::min(all_tiles, c->num_sms);
         sa.n_tiles = all_tiles;
         sa.n_sample = n_sample;
         sa.j = j;
-        sa.grid_sync = c->d_grid_sync;
-        sa.sync_target = c->grid_sync_count + (unsigned long long)grid;
-        sa.theta_out = c->d_theta;
-        void* args[] = {const_cast<CUtensorMap*>(&mq), const_cast<CUtensorMap*>(&me), &sa};
-        MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
-        MARS_CUDA_TRY(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&gemm_small_kernel<kFused>),
-                                                  dim3(grid), dim3(kThreads), args, smem, st));
-        c->grid_sync_count += (unsigned long long)grid;
-        MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[1], st));
+        if (c->single_launch) {
+            // 2.-4. sample, thresholds and candidates in one cooperative launch
+            // (one CTA per SM, every CTA resident): CTA b < n_sample first runs
+            // sample tile b; the epilogue warps meet on a grid-wide counter,
+            // take the thresholds, and go on with the candidate tiles that the
+            // producer and MMA warps have kept streaming meanwhile
+            sa.grid_sync = c->d_grid_sync;
+            sa.sync_target = c->grid_sync_count + (unsigned long long)grid;
+            sa.theta_out = c->d_theta;
+            void* args[] = {const_cast<CUtensorMap*>(&mq), const_cast<CUtensorMap*>(&me), &sa};
+            MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
+            MARS_CUDA_TRY(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&gemm_small_kernel<kFused>),
+                                                      dim3(grid), dim3(kThreads), args, smem, st));
+            c->grid_sync_count += (unsigned long long)grid;
+            MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[1], st));
+        } else {
+            // the same three steps as separate launches (no cooperative launch)
+            sa.n_tiles = n_sample;
+            gemm_small_kernel<kSample><<<n_sample, kThreads, smem, st>>>(mq, me, sa);
+            MARS_CUDA_TRY(cudaGetLastError());
+            threshold_kernel<<<(B * 32 + kThrThreads - 1) / kThrThreads, kThrThreads, 0, st>>>(
+                c->d_sample, n_sample, B, j, kSmallWarps, c->d_theta);
+            MARS_CUDA_TRY(cudaGetLastError());
+            sa.n_tiles = all_tiles;
+            MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
+            gemm_small_kernel<kCandidates><<<grid, kThreads, smem, st>>>(mq, me, sa);
+            MARS_CUDA_TRY(cudaGetLastError());
+            MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[1], st));
+        }
     } else {
         GemmArgs ga{};
         ga.B = B;

@@ -132,6 +132,7 @@ _SIGS = {
     "mars_batch_ctx_create": [_I32, _I32, _I32, _I32, _I32, C.POINTER(_VP)],
     "mars_batch_ctx_destroy": [_VP],
     "mars_batch_ctx_set_precision": [_VP, _I32],
+    "mars_batch_ctx_set_single_launch": [_VP, _I32],
     "mars_query_batch_topk": [_VP, _VP, _VP, _I32, _I32, _F32, _F32, _I32, _I32, _I32, _I32, _VP,
                               _VP, _VP, _VP],
     "mars_batch_last_stats": [_VP, C.POINTER(BatchStats)],
@@ -464,6 +465,10 @@ class BatchContext:
     def set_precision(self, tf32_only: bool) -> None:
         """TF32 operands always (True) or fp16 when in range (False, the default)."""
         _check(lib().mars_batch_ctx_set_precision(self.handle, int(bool(tf32_only))))
+
+    def set_single_launch(self, enable: bool) -> None:
+        """Small batches: sample, thresholds and candidates as one cooperative launch (default) or three."""
+        _check(lib().mars_batch_ctx_set_single_launch(self.handle, int(bool(enable))))
 
     def query_batch_topk(self, store: Store, d_queries, B, t_q, lam, K, d_ids, d_vals, d_counts=None,
                          modality_filter=-1, use_importance=False, row_offset=0, query_pitch=None,

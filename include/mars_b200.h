@@ -335,6 +335,12 @@ int mars_batch_ctx_destroy(mars_batch_ctx* ctx);
  * its first batched query (2 bytes per value) and kept current. */
 int mars_batch_ctx_set_precision(mars_batch_ctx* ctx, int32_t tf32_only);
 
+/* Small batches (B <= 64 on fp16 operands): enable != 0 (the default on
+ * devices with cooperative launch) runs the sample pass, the thresholds and
+ * the candidates pass as one cooperative launch; 0 runs them as three
+ * launches.  The results are the same. */
+int mars_batch_ctx_set_single_launch(mars_batch_ctx* ctx, int32_t enable);
+
 /* d_queries: B rows of query_pitch floats (16-byte aligned; values past dim
  * must be zero).  One query time t_q for the whole batch.  Outputs d_ids /
  * d_vals: [B][K] (ids offset by row_offset), d_counts: [B] (may be NULL).

@@ -19,7 +19,7 @@ def torch_mod():
 
 
 def _run(torch, N, D, B, K, filt=-1, use_imp=True, lam=0.01, t_q=600.0, seed=0, check_oracle=2,
-         tf32_only=False, scale_row=None, scale_query=None):
+         tf32_only=False, scale_row=None, scale_query=None, single_launch=True):
     import mars_b200 as mb
     from mars_b200 import datagen
     E, mod, ts, imp = datagen.gaussian_corpus(N, D, seed=seed, ts_max=600.0)
@@ -36,6 +36,7 @@ def _run(torch, N, D, B, K, filt=-1, use_imp=True, lam=0.01, t_q=600.0, seed=0, 
     bc = mb.BatchContext(N, D, max_batch=B, max_k=K)
     if tf32_only:
         bc.set_precision(True)
+    bc.set_single_launch(single_launch)
     ctx = mb.QueryContext(N, D, max_k=K)
     Qd = torch.from_numpy(Qp).cuda()
     ids = torch.full((B, K), -7, dtype=torch.int32, device="cuda")
@@ -162,6 +163,15 @@ def test_batch_small_batches(torch_mod, B, K):
     """B <= 64 on fp16 operands: 128-row x B-query tiles with the queries
     resident in shared memory (gemm_small_kernel); results equal the scans."""
     stats = _run(torch_mod, 100_003, 768, B, K, seed=B * 7 + K, check_oracle=1)
+    assert stats["path"] == 3
+    assert stats["fallbacks"] == 0, stats
+
+
+@pytest.mark.parametrize("B,K", [(5, 10), (16, 64), (64, 3)])
+def test_batch_small_batches_three_launches(torch_mod, B, K):
+    """The small-batch sample, thresholds and candidates as three launches
+    (devices without cooperative launch) give the scans' results too."""
+    stats = _run(torch_mod, 200_003, 768, B, K, seed=B + K, check_oracle=1, single_launch=False)
     assert stats["path"] == 3
     assert stats["fallbacks"] == 0, stats
 
