@@ -64,7 +64,15 @@ constexpr int kStageBytes = kStageA + kStageB;
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 512;
 constexpr int kJ = 16;                // sampled lower bounds kept per (query, tile)
+// Relative error margin of a short-listed score, times ||q|| max||e||.
+// TF32 operands: the tensor cores may truncate each fp32 operand to 10
+// mantissa bits (2^-10 relative each, 1.95e-3 for the product's two
+// factors), plus the fp32 accumulation.  fp16 operands: both copies are
+// rounded to nearest here (2^-11 each, 9.8e-4 together; products of fp16
+// values are exact in fp32), plus the accumulation over at most 64 16-wide
+// steps, far below the remaining 6e-4.
 constexpr float kMarginRel = 2.6e-3f;
+constexpr float kMarginRelF16 = 1.6e-3f;
 
 enum Mode { kSample = 0, kCandidates = 1, kFused = 2 };
 
@@ -330,7 +338,7 @@ __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch,
         if (warp == 0) *err = 0;
         // 1.0001: covers the fp32 rounding of this norm itself
         const float qn = sqrtf(s) * 1.0001f, en = __uint_as_float(*norm_bits);
-        float mg = kMarginRel * qn * en;
+        float mg = (f16 ? kMarginRelF16 : kMarginRel) * qn * en;
         // fp16 operands: components below the normal range are rounded to a
         // multiple of 2^-24, an absolute error of at most 2^-25 each; over D
         // <= 4 nc components the dot changes by at most
