@@ -370,24 +370,37 @@ def run_mars(a):
                                              use_importance=True, row_offset=lo, stream=ctx.stream), 8)
 
     # ---- end to end through the public API with host buffers --------------
+    # A serving loop: every step copies its queries host -> device, answers
+    # them and copies the ids and scores device -> host into one of two pinned
+    # buffers; the host then waits for the previous step's results and reads
+    # them, so the GPU is not idle while the host issues the next step.  The
+    # device buffers are reused in stream order.
     Qpin = torch.from_numpy(Qh).pin_memory()
     qbuf = torch.empty((Q, a.dim), dtype=torch.float32, device="cuda")
-    out_ids = torch.empty((Q, K), dtype=torch.int32).pin_memory()
-    out_vals = torch.empty((Q, K), dtype=torch.float32).pin_memory()
+    out_ids = [torch.empty((Q, K), dtype=torch.int32).pin_memory() for _ in range(2)]
+    out_vals = [torch.empty((Q, K), dtype=torch.float32).pin_memory() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
     res_ids, res_vals = (mids, mvals) if sharded else (ids, vals)
+    checksum = 0
     barrier()
     t0 = time.perf_counter()
-    for s in range(a.steps):
-        base = (s * Q) % (64 - Q + 1)
-        qbuf.copy_(Qpin[base:base + Q], non_blocking=True)
-        batch(qbuf, ids, vals)
-        if sharded:
-            dist.all_gather_into_tensor(gids, ids)
-            dist.all_gather_into_tensor(gvals, vals)
-            ctx.topk_merge_batch(gids, gvals, world, K, Q, mids, mvals, stream=ctx.stream)
-        out_ids.copy_(res_ids, non_blocking=True)
-        out_vals.copy_(res_vals, non_blocking=True)
-        stream.synchronize()
+    for s in range(a.steps + 1):
+        if s < a.steps:
+            b = s % 2
+            base = (s * Q) % (64 - Q + 1)
+            qbuf.copy_(Qpin[base:base + Q], non_blocking=True)
+            batch(qbuf, ids, vals)
+            if sharded:
+                dist.all_gather_into_tensor(gids, ids)
+                dist.all_gather_into_tensor(gvals, vals)
+                ctx.topk_merge_batch(gids, gvals, world, K, Q, mids, mvals, stream=ctx.stream)
+            out_ids[b].copy_(res_ids, non_blocking=True)
+            out_vals[b].copy_(res_vals, non_blocking=True)
+            done[b].record(stream)
+        if s > 0:   # the previous step's results, read on the host
+            p = (s - 1) % 2
+            done[p].synchronize()
+            checksum += int(out_ids[p][0, 0])
     dt = time.perf_counter() - t0
     if world > 1:
         t = torch.tensor([dt], dtype=torch.float64, device="cuda")
@@ -399,7 +412,8 @@ def run_mars(a):
            "path": "pinned H2D of the step's queries, mars_query_batch_topk"
                    + (" per shard, NCCL all-gather, mars_topk_merge_batch" if sharded else
                       (" on every replica" if world > 1 else ""))
-                   + ", D2H of the top-K ids and scores, stream synchronize"}
+                   + ", D2H of the top-K ids and scores into one of two pinned buffers; the host waits "
+                     "for and reads each step's results while the next step runs"}
     latency = None
     if world == 1:
         # single-query latency through mars_query (host query in, host results out)
