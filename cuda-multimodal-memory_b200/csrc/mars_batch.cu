@@ -464,7 +464,7 @@ __global__ void __launch_bounds__(kRescoreThreads)
 rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t B, float t_q,
                float lambda, int32_t use_imp, int32_t K, int32_t row_offset,
                const float* __restrict__ theta, const float* __restrict__ margin,
-               const RowMeta meta, const int32_t* __restrict__ cand,
+               const int32_t* __restrict__ cand,
                const float* __restrict__ cand_f, const float* __restrict__ cand_s,
                const int32_t* __restrict__ cand_cnt, int32_t cap,
                int32_t* __restrict__ out_ids, float* __restrict__ out_vals,
@@ -1417,7 +1417,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     v.E = s->d_E; v.ts = s->d_ts; v.imp = s->d_imp; v.mod = s->d_mod; v.d_n = s->d_n;
     v.pitch4 = s->pitch / 4; v.nc = (s->dim + 3) / 4;
     rescore_kernel<<<B, kRescoreThreads, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, use_importance, K,
-                                                  row_offset, c->d_theta, c->d_margin, meta, c->d_cand,
+                                                  row_offset, c->d_theta, c->d_margin, c->d_cand,
                                                   c->d_cand_f, c->d_cand_f + (size_t)c->max_batch * c->cap,
                                                   c->d_cand_cnt, c->cap, d_ids, d_vals, d_counts,
                                                   c->d_fallback, c->d_rescored, f16 ? c->d_bad : nullptr);
