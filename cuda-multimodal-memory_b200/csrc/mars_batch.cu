@@ -1134,13 +1134,26 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
                     int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
                     int32_t* d_counts, void* stream, bool allow_f16);
 
+// After a wait that gave up, some CTAs of the small-batch launch may not
+// have counted their arrival: once the stream is idle, the grid counter and
+// its expected value start again from zero.
+void batch_reset_grid_sync(mars_batch_ctx* c) {
+    if (c->last_stream != nullptr) cudaStreamSynchronize(c->last_stream);
+    if (cudaMemset(c->d_grid_sync, 0, sizeof(unsigned long long)) == cudaSuccess) c->grid_sync_count = 0;
+}
+
 // The previous call's pipeline error word, if its status copy has landed
 // (never waits).
-int batch_prev_status(const mars_batch_ctx* c) {
+int batch_prev_status(mars_batch_ctx* c) {
     if (!c->status_pending || cudaEventQuery(c->ev_status) != cudaSuccess) return MARS_OK;
-    if (*c->h_err != 0)
+    if (*c->h_err != 0) {
+        const int code = *c->h_err;
+        *c->h_err = 0;
+        c->status_pending = false;
+        batch_reset_grid_sync(c);
         return fail(MARS_ERR_TIMEOUT, "mars_query_batch_topk: a tensor-core pipeline wait gave up (code " +
-                                          std::to_string(*c->h_err) + ")");
+                                          std::to_string(code) + ")");
+    }
     return MARS_OK;
 }
 
@@ -1165,9 +1178,13 @@ int batch_collect_stats(mars_batch_ctx* c) {
     c->last.candidates = total;
     c->last.max_candidates = maxc;
     c->last.rescored = rescored;
-    if (*c->h_err != 0)
+    if (*c->h_err != 0) {
+        const int code = *c->h_err;
+        *c->h_err = 0;
+        batch_reset_grid_sync(c);
         return fail(MARS_ERR_TIMEOUT, "mars_query_batch_topk: a tensor-core pipeline wait gave up (code " +
-                                          std::to_string(*c->h_err) + ")");
+                                          std::to_string(code) + ")");
+    }
     return MARS_OK;
 }
 
