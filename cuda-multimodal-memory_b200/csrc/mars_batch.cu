@@ -606,16 +606,17 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
 //
 // Candidates mode appends (query, row) when the row's upper bound reaches the
 // query's threshold, as gemm_kernel does.  Sample mode writes, per sampled
-// tile and query, each epilogue warp's largest lower bound (of its 32 rows):
-// sample_buf[tile][query][kSmallWarps].  The j-th largest of these is at most
-// the j-th largest sampled bound (j of them are the maxima of j distinct
-// row sets), so the threshold stays as safe.
+// tile and query, the tile's largest lower bound (of its 128 rows), or each
+// epilogue warp's (of its 32 rows) when the sample has few tiles:
+// sample_buf[tile][query][1 or kSmallWarps].  The j-th largest of these is at
+// most the j-th largest sampled bound (j of them are the maxima of j
+// distinct row sets), so the threshold stays as safe.
 constexpr int kSmallMaxB = 64;
 constexpr int kSmallRows = 128;
 constexpr int kSmallStage = kSmallRows * 128;      // 16 KB: 128 rows x 64 halves
 constexpr int kSmallMaxStages = 12;
 constexpr int kSmallWarps = 4;                       // epilogue warps: 32 rows each
-constexpr int kSmallStaticSmem = 1024;               // bound on the kernel's static shared memory
+constexpr int kSmallStaticSmem = 2048;               // bound on the kernel's static shared memory
 
 struct SmallArgs {
     int32_t B, NQ;                   // queries, MMA N (B rounded up to 16)
@@ -627,7 +628,7 @@ struct SmallArgs {
     RowMeta meta;
     const float* theta;
     const float* margin;
-    float* sample_buf;               // sample mode: [n_tiles][B][kSmallWarps]
+    float* sample_buf;               // sample mode: [n_tiles][B][sample_per_tile] maxima
     int32_t* cand;
     float* cand_f;
     float* cand_s;
@@ -639,6 +640,8 @@ struct SmallArgs {
     // every CTA's sample maxima are written (grid counter), each CTA takes
     // the thresholds itself; CTA 0 also stores them in theta_out
     int32_t n_sample, j;
+    int32_t sample_per_tile;         // values per sampled tile and query: 1 (the tile's
+                                     // maximum) or kSmallWarps (each epilogue warp's)
     unsigned long long* grid_sync;   // monotone arrival counter
     unsigned long long sync_target;  // its value once every CTA of this launch arrived
     float* theta_out;
@@ -704,6 +707,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
 
     __shared__ float s_theta[kSmallMaxB];   // kFused: this launch's thresholds
+    __shared__ float s_wmax[kSmallWarps][kSmallMaxB];   // sample tile: each epilogue warp's maxima
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.stages; ++s) { sm100::mbar_init(full + s, 1); sm100::mbar_init(empty + s, 1); }
@@ -811,7 +815,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                 }
                 asm volatile("bar.sync 1, 128;" ::: "memory");
                 for (int q = sub; q < a.B; q += kSmallWarps) {
-                    const float th = warp_threshold(a.sample_buf, a.n_sample, a.B, q, a.j, kSmallWarps, lane);
+                    const float th = warp_threshold(a.sample_buf, a.n_sample, a.B, q, a.j, a.sample_per_tile, lane);
                     if (lane == 0) {
                         s_theta[q] = th;
                         if (blockIdx.x == 0) a.theta_out[q] = th;
@@ -852,13 +856,24 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
 #pragma unroll
                         for (int off = 16; off >= 1; off >>= 1)
                             lo = fmaxf(lo, __shfl_xor_sync(0xffffffffu, lo, off));
-                        if (lane == 0) a.sample_buf[((int64_t)tl.sidx * a.B + q) * kSmallWarps + sub] = lo;
+                        if (lane == 0) {
+                            if (a.sample_per_tile == 1) s_wmax[sub][q] = lo;
+                            else a.sample_buf[((int64_t)tl.sidx * a.B + q) * kSmallWarps + sub] = lo;
+                        }
                     }
                 }
             }
             sm100::tc_fence_before();
             sm100::mbar_arrive(tempty + buf);
             if (++buf == 2) { buf = 0; bphase ^= 1u; }
+            if (tl.sample && a.sample_per_tile == 1) {
+                // the tile's largest lower bound per query: sample_buf[tile][query]
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (rt < a.B)
+                    a.sample_buf[(int64_t)tl.sidx * a.B + rt] =
+                        fmaxf(fmaxf(s_wmax[0][rt], s_wmax[1][rt]), fmaxf(s_wmax[2][rt], s_wmax[3][rt]));
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+            }
         }
     }
     sm100::tc_fence_before();
@@ -1279,7 +1294,9 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     }
     const int32_t tile_rows = small ? kSmallRows : kBN;
     const int32_t all_tiles = small ? (n + kSmallRows - 1) / kSmallRows : rtiles;
-    const int32_t per_tile = small ? kSmallWarps : kJ;
+    // small tiles: one maximum per sampled tile and query when the sample has
+    // plenty of tiles for the j-th largest, else one per epilogue warp
+    const int32_t per_tile = small ? (n_sample >= 4 * j ? 1 : kSmallWarps) : kJ;
     const size_t sample_floats = (size_t)n_sample * (small ? B : c->max_batch) * per_tile;
     if (c->d_sample == nullptr || n_sample > c->sample_tiles_cap || sample_floats > c->sample_floats_cap) {
         MARS_CUDA_TRY(cudaStreamSynchronize(st));
@@ -1357,6 +1374,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         sa.n_tiles = all_tiles;
         sa.n_sample = n_sample;
         sa.j = j;
+        sa.sample_per_tile = per_tile;
         if (c->single_launch) {
             // 2.-4. sample, thresholds and candidates in one cooperative launch
             // (one CTA per SM, every CTA resident): CTA b < n_sample first runs
@@ -1378,7 +1396,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
             gemm_small_kernel<kSample><<<n_sample, kThreads, smem, st>>>(mq, me, sa);
             MARS_CUDA_TRY(cudaGetLastError());
             threshold_kernel<<<(B * 32 + kThrThreads - 1) / kThrThreads, kThrThreads, 0, st>>>(
-                c->d_sample, n_sample, B, j, kSmallWarps, c->d_theta);
+                c->d_sample, n_sample, B, j, sa.sample_per_tile, c->d_theta);
             MARS_CUDA_TRY(cudaGetLastError());
             sa.n_tiles = all_tiles;
             MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
