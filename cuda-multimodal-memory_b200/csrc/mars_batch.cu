@@ -473,6 +473,9 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     __shared__ float   s_key[kSortCap];
     __shared__ int32_t s_id[kSortCap];
     __shared__ int     s_ge, s_n2, s_nk;
+    __shared__ float   s_wv[kRescoreThreads];      // K <= 32: each warp's K best lower bounds
+    __shared__ int32_t s_wi[kRescoreThreads];
+    __shared__ float   s_th2;
     __shared__ int     s_hist[2048];
     __shared__ uint32_t s_sel[2];
     const int qi = blockIdx.x;
@@ -495,21 +498,41 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     const float* cs = cand_s + (int64_t)qi * cap;   // slack: the exact score lies in cf -+ cs
 
     // ---- pass 1: lower bounds, completeness, K-th largest lower bound -------
+    // K <= 32: every warp keeps its K best lower bounds (ranked by value, then
+    // candidate index) and warp 0 merges the eight lists; larger K: a radix
+    // selection over all of them.  Either way th2 is the K-th largest.
+    const bool warp_lists = K <= 32;
+    WarpTopK<1> top;
+    top.init(warp_lists ? K : 1);
     int ge = 0;
-    for (int i = threadIdx.x; i < nc_; i += kRescoreThreads) {
-        const float lo = cf[i] - cs[i];
-        ge += (lo >= th) ? 1 : 0;
-        s_key[i] = lo;
+    for (int i0 = warp * 32; i0 < nc_; i0 += kRescoreThreads) {
+        const int i = i0 + lane;
+        const bool in = i < nc_;
+        const float lo = in ? cf[i] - cs[i] : -INFINITY;
+        ge += (in && lo >= th) ? 1 : 0;
+        if (warp_lists) top.offer_lanes(lo, i, in, lane);
+        else if (in) s_key[i] = lo;
     }
     ge = warp_reduce_sum_int(ge);
     if (lane == 0) atomicAdd(&s_ge, ge);
+    if (warp_lists) top.store(s_wv + warp * 32, s_wi + warp * 32, lane);
     __syncthreads();
     if (s_ge < K) {
         if (threadIdx.x == 0) { fallback[qi] = 1; rescored[qi] = 0; if (out_cnt) out_cnt[qi] = 0; }
         return;
     }
-    const float th2 = key2f(block_kth_largest_key<kRescoreThreads>(
-        [&](int i) { return f2key(s_key[i]); }, nc_, K, s_hist, s_sel));
+    float th2;
+    if (warp_lists) {
+        if (warp == 0) {
+            for (int ww = 1; ww < kWarps; ++ww) top.merge_sorted32(s_wv + ww * 32, s_wi + ww * 32, K, lane);
+            if (lane == 0) s_th2 = top.thr_v;
+        }
+        __syncthreads();
+        th2 = s_th2;
+    } else {
+        th2 = key2f(block_kth_largest_key<kRescoreThreads>(
+            [&](int i) { return f2key(s_key[i]); }, nc_, K, s_hist, s_sel));
+    }
 
     // ---- pass 2: exact scores of the candidates that can still place -------
     // Their rows are listed first (in the histogram's space, free now) and
@@ -577,10 +600,23 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     }
     __syncthreads();
     const int n2 = s_n2;
-    const int p2 = pow2_at_least(n2);
-    for (int i = n2 + threadIdx.x; i < p2; i += kRescoreThreads) { s_key[i] = -INFINITY; s_id[i] = INT32_MAX; }
-    __syncthreads();
-    block_bitonic_desc(s_key, s_id, p2);
+    if (n2 <= 32) {
+        // few rows: ranked in warp 0's registers (score desc, id asc)
+        unsigned long long* keys = reinterpret_cast<unsigned long long*>(s_hist);   // the row list is done
+        if (threadIdx.x < 32) keys[threadIdx.x] = threadIdx.x < n2 ? rank_key(s_key[threadIdx.x], s_id[threadIdx.x]) : 0ull;
+        __syncthreads();
+        warp0_sort32_desc(keys, n2);
+        for (int p = threadIdx.x; p < n2; p += kRescoreThreads) {
+            s_key[p] = key_score(keys[p]);
+            s_id[p] = key_id(keys[p]);
+        }
+        __syncthreads();
+    } else {
+        const int p2 = pow2_at_least(n2);
+        for (int i = n2 + threadIdx.x; i < p2; i += kRescoreThreads) { s_key[i] = -INFINITY; s_id[i] = INT32_MAX; }
+        __syncthreads();
+        block_bitonic_desc(s_key, s_id, p2);
+    }
     for (int p = threadIdx.x; p < K; p += kRescoreThreads) {
         const bool valid = p < n2;
         out_vals[(int64_t)qi * K + p] = valid ? s_key[p] : -INFINITY;
