@@ -1,8 +1,8 @@
 #!/usr/bin/env python
 """MARS B200 benchmark: exact retrieval top-K (cosine x decay x importance).
 
-Workload (the metric of BASELINE.json: queries/s + p99 at N=1M, D=768, K=10,
-HBM GB/s vs peak):
+Workload (the headline metric: queries/s + p99 at N=1M, D=768, K=10, HBM GB/s
+vs peak):
   * corpus N = 1,000,000 rows x D = 768 fp32, i.i.d. Gaussian rows divided by
     (||v|| + 1e-8), timestamps U[0, 600] s, importance U[0, 1], 4 modalities;
     seeded synthetic data (no dataset is involved);
@@ -41,7 +41,8 @@ import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-for _p in (os.path.join(ROOT, "cuda-multimodal-memory_b200"), os.path.join(ROOT, "oracle")):
+for _p in (os.path.join(ROOT, "cuda-multimodal-memory_b200"), os.path.join(ROOT, "oracle"),
+           os.path.join(ROOT, "tests")):
     if _p not in sys.path:
         sys.path.insert(0, _p)
 
@@ -229,14 +230,27 @@ def cpu_baseline(a, E, mod, ts, imp, Qh):
     O.scan_topk_fast(c, Qh[0], a.ts_max, a.lam, a.k, use_importance=True, n_threads=threads)
     t1 = time.perf_counter() - t0
     n = int(max(2, min(32, math.ceil(a.cpu_budget_s / max(t1, 1e-3)))))
+    answers = []
     t0 = time.perf_counter()
     for i in range(n):
-        O.scan_topk_fast(c, Qh[i % Qh.shape[0]], a.ts_max, a.lam, a.k, use_importance=True,
-                         n_threads=threads)
+        answers.append(O.scan_topk_fast(c, Qh[i % Qh.shape[0]], a.ts_max, a.lam, a.k, use_importance=True,
+                                        n_threads=threads))
     dt = time.perf_counter() - t0
     return {"value": n / dt, "unit": "queries/s", "cores": threads, "kind": "port",
             "sample": f"{n} queries, each scanning all {a.n} rows (same corpus, same K/lambda), "
-                      f"oracle/mars_oracle.c orc_scan_topk_fast with {threads} OpenMP threads"}
+                      f"oracle/mars_oracle.c orc_scan_topk_fast with {threads} OpenMP threads"}, answers
+
+
+def compare_with_oracle(gpu_ids, gpu_vals, answers):
+    """Tie-aware comparison of the GPU answers of queries 0.. with the oracle's
+    (ids identical wherever scores are separated by more than 1e-5 relative)."""
+    from _util import assert_ranked_equivalent
+    try:
+        for i, (oi, ov) in enumerate(answers):
+            assert_ranked_equivalent(gpu_ids[i], gpu_vals[i], oi, ov, what=f"query {i}")
+        return True
+    except AssertionError:
+        return False
 
 
 def run_mars(a):
@@ -349,6 +363,15 @@ def run_mars(a):
         t = torch.tensor([1 if exact else 0], dtype=torch.int32, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MIN)
         exact = bool(t.item())
+    # the step's answers for queries 0..31 (two steps), compared with the
+    # oracle's answers on the same queries (computed by the CPU baseline)
+    ans_ids, ans_vals = [], []
+    for base in (0, Q):
+        batch(Qd[base:base + Q], ids, vals)
+        torch.cuda.synchronize()
+        ans_ids.append(ids.cpu().numpy().copy())
+        ans_vals.append(vals.cpu().numpy().copy())
+    ans_ids, ans_vals = np.concatenate(ans_ids), np.concatenate(ans_vals)
 
     # the fused scan: one query per launch (the HBM-bound kernel), the
     # multi-query launch of the step's queries, and its fp16-filtered form
@@ -379,9 +402,13 @@ def run_mars(a):
     qbuf = torch.empty((Q, a.dim), dtype=torch.float32, device="cuda")
     out_ids = [torch.empty((Q, K), dtype=torch.int32).pin_memory() for _ in range(2)]
     out_vals = [torch.empty((Q, K), dtype=torch.float32).pin_memory() for _ in range(2)]
+    out_cnt = [torch.empty(Q, dtype=torch.int32).pin_memory() for _ in range(2)]
+    cnt = torch.empty(Q, dtype=torch.int32, device="cuda")
+    mcnt = torch.empty(Q, dtype=torch.int32, device="cuda")
     done = [torch.cuda.Event() for _ in range(2)]
     res_ids, res_vals = (mids, mvals) if sharded else (ids, vals)
     checksum = 0
+    e2e_valid = True
     barrier()
     t0 = time.perf_counter()
     for s in range(a.steps + 1):
@@ -389,31 +416,37 @@ def run_mars(a):
             b = s % 2
             base = (s * Q) % (64 - Q + 1)
             qbuf.copy_(Qpin[base:base + Q], non_blocking=True)
-            batch(qbuf, ids, vals)
+            bc.query_batch_topk(store, qbuf, Q, a.ts_max, a.lam, K, ids, vals, cnt, use_importance=True,
+                                row_offset=lo, stream=ctx.stream)
             if sharded:
                 dist.all_gather_into_tensor(gids, ids)
                 dist.all_gather_into_tensor(gvals, vals)
-                ctx.topk_merge_batch(gids, gvals, world, K, Q, mids, mvals, stream=ctx.stream)
+                ctx.topk_merge_batch(gids, gvals, world, K, Q, mids, mvals, mcnt, stream=ctx.stream)
             out_ids[b].copy_(res_ids, non_blocking=True)
             out_vals[b].copy_(res_vals, non_blocking=True)
+            out_cnt[b].copy_(mcnt if sharded else cnt, non_blocking=True)
             done[b].record(stream)
-        if s > 0:   # the previous step's results, read on the host
+        if s > 0:   # the previous step's results, read and checked on the host
             p = (s - 1) % 2
             done[p].synchronize()
+            e2e_valid = e2e_valid and bool((out_cnt[p] == K).all())
             checksum += int(out_ids[p][0, 0])
     dt = time.perf_counter() - t0
+    bc.last_stats()      # raises if the last step's pipeline reported an error
     if world > 1:
         t = torch.tensor([dt], dtype=torch.float64, device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         dt = float(t.item())
     q_all = Q * (1 if sharded else world)   # queries answered per step by the whole job
     e2e = {"value": a.steps * q_all / dt, "unit": "queries/s",
-           "h2d_bytes_per_step": Q * a.dim * 4, "d2h_bytes_per_step": Q * K * 8,
+           "h2d_bytes_per_step": Q * a.dim * 4, "d2h_bytes_per_step": Q * K * 8 + Q * 4,
+           "every_step_valid": e2e_valid,
            "path": "pinned H2D of the step's queries, mars_query_batch_topk"
                    + (" per shard, NCCL all-gather, mars_topk_merge_batch" if sharded else
                       (" on every replica" if world > 1 else ""))
-                   + ", D2H of the top-K ids and scores into one of two pinned buffers; the host waits "
-                     "for and reads each step's results while the next step runs"}
+                   + ", D2H of the top-K ids, scores and counts into one of two pinned buffers; the host "
+                     "waits for and reads each step's results (checking every count) while the next step "
+                     "runs"}
     latency = None
     if world == 1:
         # single-query latency through mars_query (host query in, host results out)
@@ -437,8 +470,9 @@ def run_mars(a):
         small = bool(bstats and bstats.get("path") == 3)
         qtiles = 1 if small else (Q + 127) // 128
         gemm_bytes = qtiles * n_local * (pitch16 * 2 + 8)
-        if small:   # the fused pass also streams its sampled 128-row tiles
-            gemm_bytes += bstats.get("sample_tiles", 0) * 128 * (pitch16 * 2 + 8)
+        # the fused pass also streams its sampled 128-row tiles a second time:
+        # reported apart, not counted as algorithmic bytes
+        overhead_bytes = bstats.get("sample_tiles", 0) * 128 * (pitch16 * 2 + 8) if small else 0
         mean_gemm = statistics.mean(gemm_ms)
         achieved = gemm_bytes / (mean_gemm * 1e-3) / 1e9
         tr = committed_traffic()
@@ -467,6 +501,7 @@ def run_mars(a):
                                     "batch::gemm_kernel<kCandidates> (the candidates pass)"),
                          "kernel_ms": mean_gemm,
                          "algorithmic_bytes_per_launch": gemm_bytes,
+                         "overhead_bytes_per_launch": overhead_bytes,
                          "bytes_note": "fp16 rows (pitch %d halves) plus a timestamp and an importance "
                                        "per row, once per query tile (one tile at B <= 64)" % pitch16},
             "batch_stats": bstats,
@@ -487,7 +522,10 @@ def run_mars(a):
             "clocks": clocks,
         }
         if world == 1 and not a.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(a, E, mod, ts, imp, Qh)
+            line["cpu_baseline"], answers = cpu_baseline(a, E, mod, ts, imp, Qh)
+            n_cmp = min(len(answers), ans_ids.shape[0])
+            line["exact_vs_oracle"] = compare_with_oracle(ans_ids, ans_vals, answers[:n_cmp])
+            line["oracle_checked_queries"] = n_cmp
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

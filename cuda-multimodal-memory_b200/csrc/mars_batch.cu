@@ -138,13 +138,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
     uint64_t* empty = full + kStages;
     uint64_t* tfull = empty + kStages;
     uint64_t* tempty = tfull + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint64_t* mdrain = tempty + 2;      // the MMA issuer's last commit
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdrain + 1);
     float* s_w = reinterpret_cast<float*>(smem + kStages * kStageBytes + 256);   // [kBN] row weights
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) { sm100::mbar_init(full + s, 1); sm100::mbar_init(empty + s, 1); }
         for (int b = 0; b < 2; ++b) { sm100::mbar_init(tfull + b, 1); sm100::mbar_init(tempty + b, 128); }
+        sm100::mbar_init(mdrain, 1);
         sm100::fence_mbar_init();
         sm100::prefetch_tmap(&tmap_q);
         sm100::prefetch_tmap(&tmap_e);
@@ -182,8 +184,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                 }
             }
             // every copy this thread started has landed before the CTA may exit
+            // (also after a wait gave up: the drain does not stop at the error word)
             for (int s = 0; s < kStages; ++s)
-                if (issued[s]) sm100::mbar_wait(full + s, issued_phase[s], a.err, 2);
+                if (issued[s]) sm100::mbar_wait_drain(full + s, issued_phase[s], a.err, 2);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
@@ -220,6 +223,10 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                 sm100::mma_commit(tfull + buf);         // accumulator ready
                 if (++buf == 2) { buf = 0; bphase ^= 1u; }
             }
+            // every MMA this thread issued has finished before TMEM is freed
+            // (also when a wait gave up and the loop ended early)
+            sm100::mma_commit(mdrain);
+            sm100::mbar_wait_drain(mdrain, 0, a.err, 6);
         }
     } else {
         // ---------------- epilogue (warps 2..5) ----------------
@@ -335,7 +342,7 @@ __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch,
     if (lane == 0) {
         bad[warp] = out ? 1 : 0;
         rescored[warp] = 0;
-        if (warp == 0) *err = 0;
+        if (warp == 0) { err[0] = 0; err[1] = 0; }   // the pipeline's and the arrival wait's words
         // 1.0001: covers the fp32 rounding of this norm itself
         const float qn = sqrtf(s) * 1.0001f, en = __uint_as_float(*norm_bits);
         float mg = (f16 ? kMarginRelF16 : kMarginRel) * qn * en;
@@ -469,7 +476,8 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
                const int32_t* __restrict__ cand_cnt, int32_t cap,
                int32_t* __restrict__ out_ids, float* __restrict__ out_vals,
                int32_t* __restrict__ out_cnt, int32_t* __restrict__ fallback,
-               int32_t* __restrict__ rescored, const int32_t* __restrict__ bad) {
+               int32_t* __restrict__ rescored, const int32_t* __restrict__ bad,
+               const int32_t* __restrict__ status) {
     __shared__ float   s_key[kSortCap];
     __shared__ int32_t s_id[kSortCap];
     __shared__ int     s_ge, s_n2, s_nk;
@@ -481,6 +489,16 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     const int qi = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int kWarps = kRescoreThreads / 32;
+    if (status[0] != 0 || status[1] != 0) {
+        // a bounded wait of this call's GEMM gave up: the short lists and the
+        // thresholds may be incomplete, so no result of the call is served
+        for (int p = threadIdx.x; p < K; p += kRescoreThreads) {
+            out_vals[(int64_t)qi * K + p] = -INFINITY;
+            out_ids[(int64_t)qi * K + p] = -1;
+        }
+        if (threadIdx.x == 0) { if (out_cnt) out_cnt[qi] = -1; fallback[qi] = 0; rescored[qi] = 0; }
+        return;
+    }
     const int ncand = cand_cnt[qi];
     const int nc_ = min(ncand, cap);
     if (threadIdx.x == 0) { s_ge = 0; s_n2 = 0; }
@@ -492,7 +510,6 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         return;
     }
     const float th = theta[qi];
-    const float m = margin[qi];
     const int32_t* ci = cand + (int64_t)qi * cap;
     const float* cf = cand_f + (int64_t)qi * cap;
     const float* cs = cand_s + (int64_t)qi * cap;   // slack: the exact score lies in cf -+ cs
@@ -680,6 +697,8 @@ struct SmallArgs {
                                      // maximum) or kSmallWarps (each epilogue warp's)
     unsigned long long* grid_sync;   // monotone arrival counter
     unsigned long long sync_target;  // its value once every CTA of this launch arrived
+    uint32_t sync_spin_limit;        // polls of the arrival wait before it gives up
+    int* sync_err;                   // set (17) when the arrival wait gave up
     float* theta_out;
 };
 
@@ -740,7 +759,8 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     uint64_t* qfull = empty + kSmallMaxStages;
     uint64_t* tfull = qfull + 1;
     uint64_t* tempty = tfull + 2;
-    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+    uint64_t* mdrain = tempty + 2;      // the MMA issuer's last commit
+    uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdrain + 1);
 
     __shared__ float s_theta[kSmallMaxB];   // kFused: this launch's thresholds
     __shared__ float s_wmax[kSmallWarps][kSmallMaxB];   // sample tile: each epilogue warp's maxima
@@ -749,6 +769,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
         for (int s = 0; s < a.stages; ++s) { sm100::mbar_init(full + s, 1); sm100::mbar_init(empty + s, 1); }
         sm100::mbar_init(qfull, 1);
         for (int b = 0; b < 2; ++b) { sm100::mbar_init(tfull + b, 1); sm100::mbar_init(tempty + b, 128); }
+        sm100::mbar_init(mdrain, 1);
         sm100::fence_mbar_init();
         sm100::prefetch_tmap(&tmap_q);
         sm100::prefetch_tmap(&tmap_e);
@@ -788,9 +809,10 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                 }
             }
             // every copy this thread started has landed before the CTA may exit
-            sm100::mbar_wait(qfull, 0, a.err, 12);
+            // (also after a wait gave up: the drain does not stop at the error word)
+            sm100::mbar_wait_drain(qfull, 0, a.err, 12);
             for (int s = 0; s < a.stages; ++s)
-                if (issued[s]) sm100::mbar_wait(full + s, issued_phase[s], a.err, 12);
+                if (issued[s]) sm100::mbar_wait_drain(full + s, issued_phase[s], a.err, 12);
         }
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
@@ -824,6 +846,10 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                 sm100::mma_commit(tfull + buf);         // accumulator ready
                 if (++buf == 2) { buf = 0; bphase ^= 1u; }
             }
+            // every MMA this thread issued has finished before TMEM is freed
+            // (also when a wait gave up and the loop ended early)
+            sm100::mma_commit(mdrain);
+            sm100::mbar_wait_drain(mdrain, 0, a.err, 18);
         }
     } else {
         // ---------------- epilogue (warps 2..5): thread = row ----------------
@@ -844,7 +870,12 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                     atomicAdd(a.grid_sync, 1ull);
                     uint32_t spins = 0;
                     while (ld_acquire_u64(a.grid_sync) < a.sync_target) {
-                        if (++spins > sm100::kSpinLimit) { atomicExch(a.err, 17); break; }
+                        // a CTA whose pipeline wait gave up may never arrive
+                        if (*((volatile int*)a.err) != 0) break;
+                        // given up: recorded in its own word, so the pipeline
+                        // runs on and drains normally; the rescore then marks
+                        // every result of the call invalid
+                        if (++spins > a.sync_spin_limit) { atomicCAS(a.sync_err, 0, 17); break; }
                         __nanosleep(128);
                     }
                     __threadfence();
@@ -952,7 +983,8 @@ struct mars_batch_ctx {
     int32_t* d_cand = nullptr;       // max_batch * cap
     float* d_cand_f = nullptr;       // max_batch * cap
     // the call's status words, one block read back with one copy:
-    // [err, pad, fallback[max_batch], cand_cnt[max_batch], rescored[max_batch], bad[max_batch]]
+    // [err, sync_err, fallback[max_batch], cand_cnt[max_batch], rescored[max_batch], bad[max_batch]]
+    // (err: a pipeline wait gave up; sync_err: the grid-wide arrival wait gave up)
     int32_t* d_status = nullptr;
     int32_t* h_status = nullptr;     // pinned mirror
     int32_t* d_err = nullptr;        // views into d_status / h_status
@@ -993,6 +1025,10 @@ struct mars_batch_ctx {
     cudaEvent_t ev_status = nullptr;    // after the status copy
     bool status_pending = false;
     int32_t last_B = 0;
+    // test hook (mars_batch_ctx_debug_wait): polls of the arrival wait (0:
+    // the default) and arrivals the next call waits for beyond its CTAs'
+    uint32_t dbg_spin_limit = 0;
+    int32_t dbg_extra_arrivals = 0;
 };
 
 int batch_collect_stats(mars_batch_ctx* c);
@@ -1144,6 +1180,14 @@ int mars_batch_ctx_set_single_launch(mars_batch_ctx* c, int32_t enable) {
     return MARS_OK;
 }
 
+int mars_batch_ctx_debug_wait(mars_batch_ctx* c, uint32_t spin_limit, int32_t extra_arrivals) {
+    if (c == nullptr || extra_arrivals < 0)
+        return fail(MARS_ERR_INVALID, "mars_batch_ctx_debug_wait: NULL context or negative arrivals");
+    c->dbg_spin_limit = spin_limit;
+    c->dbg_extra_arrivals = extra_arrivals;
+    return MARS_OK;
+}
+
 int mars_batch_ctx_destroy(mars_batch_ctx* c) {
     if (c == nullptr) return MARS_OK;
     MarsDeviceGuard g(c->device);
@@ -1197,9 +1241,9 @@ void batch_reset_grid_sync(mars_batch_ctx* c) {
 // (never waits).
 int batch_prev_status(mars_batch_ctx* c) {
     if (!c->status_pending || cudaEventQuery(c->ev_status) != cudaSuccess) return MARS_OK;
-    if (*c->h_err != 0) {
-        const int code = *c->h_err;
-        *c->h_err = 0;
+    if (c->h_err[0] != 0 || c->h_err[1] != 0) {
+        const int code = c->h_err[0] != 0 ? c->h_err[0] : c->h_err[1];
+        c->h_err[0] = c->h_err[1] = 0;
         c->status_pending = false;
         batch_reset_grid_sync(c);
         return fail(MARS_ERR_TIMEOUT, "mars_query_batch_topk: a tensor-core pipeline wait gave up (code " +
@@ -1229,9 +1273,9 @@ int batch_collect_stats(mars_batch_ctx* c) {
     c->last.candidates = total;
     c->last.max_candidates = maxc;
     c->last.rescored = rescored;
-    if (*c->h_err != 0) {
-        const int code = *c->h_err;
-        *c->h_err = 0;
+    if (c->h_err[0] != 0 || c->h_err[1] != 0) {
+        const int code = c->h_err[0] != 0 ? c->h_err[0] : c->h_err[1];
+        c->h_err[0] = c->h_err[1] = 0;
         batch_reset_grid_sync(c);
         return fail(MARS_ERR_TIMEOUT, "mars_query_batch_topk: a tensor-core pipeline wait gave up (code " +
                                           std::to_string(code) + ")");
@@ -1269,6 +1313,8 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     if (s->d_norm_bits == nullptr)
         return fail(MARS_ERR_UNSUPPORTED, "mars_query_batch_topk: store has no row-norm bound (a view of caller memory)");
     MARS_TRY(batch_prev_status(c));
+    const int32_t dbg_extra = c->dbg_extra_arrivals;   // the test hook holds for one call
+    c->dbg_extra_arrivals = 0;
     c->last = mars_batch_stats{};
     c->status_pending = false;
     if (B == 0) return MARS_OK;
@@ -1418,7 +1464,9 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
             // take the thresholds, and go on with the candidate tiles that the
             // producer and MMA warps have kept streaming meanwhile
             sa.grid_sync = c->d_grid_sync;
-            sa.sync_target = c->grid_sync_count + (unsigned long long)grid;
+            sa.sync_target = c->grid_sync_count + (unsigned long long)grid + (unsigned long long)dbg_extra;
+            sa.sync_spin_limit = c->dbg_spin_limit != 0 ? c->dbg_spin_limit : sm100::kSpinLimit;
+            sa.sync_err = c->d_status + 1;
             sa.theta_out = c->d_theta;
             void* args[] = {const_cast<CUtensorMap*>(&mq), const_cast<CUtensorMap*>(&me), &sa};
             MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
@@ -1491,7 +1539,8 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
                                                   row_offset, c->d_theta, c->d_margin, c->d_cand,
                                                   c->d_cand_f, c->d_cand_f + (size_t)c->max_batch * c->cap,
                                                   c->d_cand_cnt, c->cap, d_ids, d_vals, d_counts,
-                                                  c->d_fallback, c->d_rescored, f16 ? c->d_bad : nullptr);
+                                                  c->d_fallback, c->d_rescored, f16 ? c->d_bad : nullptr,
+                                                  c->d_status);
     MARS_CUDA_TRY(cudaGetLastError());
     // 6. exact rescans of the flagged queries (every CTA of an unflagged
     // query leaves at once)

@@ -117,5 +117,8 @@ cudaError_t launch_query_fused(const FusedQueryArgs& p, int grid, cudaStream_t s
 cudaError_t launch_topk_merge(const int32_t* ids_in, const float* vals_in, int n_lists, int K, int Q,
                               int32_t* ids_out, float* vals_out, int32_t* cnt, cudaStream_t st);
 int scan_blocks_per_sm(int nc, int k_max);
+// Loads the scan_topk_kernel variants for K <= 128, D <= 1024 on the current
+// device; returns 0 or the cudaError_t value.
+int preload_scan_topk_kernels();
 
 }  // namespace mars

@@ -12,9 +12,15 @@
 // library and lives until the process exits.
 //
 // Rules of use:
-//  * the first call on a device looks up the array's device address with
-//    cudaGetSymbolAddress (and the device's SM count); make that first call
-//    before any stream capture on that device;
+//  * the first call on a device sets that device up: it looks up the array's
+//    device address with cudaGetSymbolAddress (which loads this file's code
+//    and commits the array), reads the SM count, and loads every scan kernel
+//    variant this entry point can launch (K <= 128, D <= 1024).  With lazy
+//    module loading (the CUDA default) that is the only point where the
+//    entry point grows the process's device memory.  Make that first call
+//    -- any K, any D -- before reserving the rest of the device memory and
+//    before any stream capture on that device, or run the process with
+//    CUDA_MODULE_LOADING=EAGER;
 //  * every call shares the one array and finds it as the previous call left
 //    it; the counters that must start at zero are cleared by each call;
 //  * calls whose work overlaps on the GPU (two streams, or two host threads)
@@ -73,6 +79,11 @@ int setup_device(int dev, DeviceSetup** out) {
         MARS_CUDA_TRY(cudaGetSymbolAddress(&p, g_noalloc_scratch));
         int sms = 0;
         MARS_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        // the kernels' code too, so no later call loads a module
+        cudaFuncAttributes fa;
+        MARS_CUDA_TRY(cudaFuncGetAttributes(&fa, noalloc_prepare_kernel));
+        const int le = mars::preload_scan_topk_kernels();
+        if (le != 0) return mars::cuda_fail(static_cast<cudaError_t>(le), "preload_scan_topk_kernels", __FILE__, __LINE__);
         s.scratch = static_cast<NoallocScratch*>(p);
         s.num_sms = sms;
         s.ready = true;

@@ -254,6 +254,28 @@ cudaError_t launch_topk_merge(const int32_t* ids_in, const float* vals_in, int n
     return cudaGetLastError();
 }
 
+// Load every scan_topk_kernel variant for K <= 128 and D <= 1024 into the
+// current device now (with lazy module loading a kernel's code is otherwise
+// placed in device memory at its first launch).
+int preload_scan_topk_kernels() {
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaSuccess;
+#define MARS_LOAD(KPL_)                                                                               \
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, scan_topk_kernel<KPL_, 1, false>);           \
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, scan_topk_kernel<KPL_, 2, false>);           \
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, scan_topk_kernel<KPL_, 3, false>);           \
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, scan_topk_kernel<KPL_, 4, false>);           \
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, scan_topk_kernel<KPL_, 5, false>);           \
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, scan_topk_kernel<KPL_, 6, false>);           \
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, scan_topk_kernel<KPL_, 7, false>);           \
+    if (e == cudaSuccess) e = cudaFuncGetAttributes(&fa, scan_topk_kernel<KPL_, 8, false>)
+    MARS_LOAD(1);
+    MARS_LOAD(2);
+    MARS_LOAD(4);
+#undef MARS_LOAD
+    return e == cudaSuccess ? 0 : (int)e;
+}
+
 int scan_blocks_per_sm(int nc, int k_max) {
     int nb = 0;
     const int cpl = (nc + 31) / 32;

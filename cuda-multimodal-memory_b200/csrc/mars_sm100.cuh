@@ -58,6 +58,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, int* e
     return false;
 }
 
+// Bounded wait that does not stop early when another role gave up: a thread
+// that issued copies or MMAs waits with it for them to land before its CTA
+// may exit.  Returns false after kSpinLimit polls (recording `code` if the
+// error word is still clear).
+__device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity, int* err, int code) {
+    for (uint32_t i = 0; i < kSpinLimit; ++i)
+        if (mbar_try_wait(bar, parity)) return true;
+    atomicCAS(err, 0, code);
+    return false;
+}
+
 // ---- TMA --------------------------------------------------------------------
 __device__ __forceinline__ void tma_load_2d(void* smem_dst, const void* tmap, uint64_t* bar,
                                             int32_t x, int32_t y) {

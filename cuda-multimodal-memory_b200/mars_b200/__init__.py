@@ -27,7 +27,8 @@ MARS_ERR_UNSUPPORTED = 5
 MARS_ERR_TIMEOUT = 6
 MARS_ERR_NO_DEVICE = 7
 MARS_ERR_DEVICE = 8
-MAX_TOP_K = 128
+MAX_TOP_K = 256          # MARS_MAX_TOP_K
+NOALLOC_MAX_K = 128      # MARS_NOALLOC_MAX_K: K limit of scan_topk_noalloc
 MAX_BFS_HOPS = 14
 
 RESULT_DTYPE = np.dtype([("node_id", "<i4"), ("score", "<f4"), ("modality", "<i4"),
@@ -136,6 +137,7 @@ _SIGS = {
     "mars_query_batch_topk": [_VP, _VP, _VP, _I32, _I32, _F32, _F32, _I32, _I32, _I32, _I32, _VP,
                               _VP, _VP, _VP],
     "mars_batch_last_stats": [_VP, C.POINTER(BatchStats)],
+    "mars_batch_ctx_debug_wait": [_VP, C.c_uint32, _I32],
     "mars_cmng_build": [_VP, _I32, _I32, _I32, _VP, C.POINTER(C.c_float)],
     "mars_cmng_build_rows": [_VP, _I32, _I32, _I32, _I32, _I32, _VP, C.POINTER(C.c_float)],
     "mars_cmng_knn": [_VP, _I32, _VP, _VP, _VP],
@@ -484,6 +486,11 @@ class BatchContext:
         st = BatchStats()
         _check(lib().mars_batch_last_stats(self.handle, C.byref(st)))
         return st.as_dict()
+
+    def debug_wait(self, spin_limit: int, extra_arrivals: int) -> None:
+        """Test hook: bound the grid-wide arrival wait to spin_limit polls and make
+        the next call wait for extra_arrivals arrivals that never come."""
+        _check(lib().mars_batch_ctx_debug_wait(self.handle, int(spin_limit), int(extra_arrivals)))
 
     def close(self):
         if getattr(self, "handle", None):

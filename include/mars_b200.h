@@ -347,8 +347,10 @@ int mars_batch_ctx_set_single_launch(mars_batch_ctx* ctx, int32_t enable);
  * Asynchronous on `stream`: a query whose short list cannot be proven
  * complete, or with a component outside the fp16 range, is rescanned exactly
  * on the device in the same stream (mars_batch_stats.fallbacks).  A
- * pipeline error of a call (a bounded wait that gave up) is returned by
- * mars_batch_last_stats or by the next call. */
+ * pipeline error of a call (a bounded device-side wait that gave up) is
+ * returned as MARS_ERR_TIMEOUT by mars_batch_last_stats or by the next call;
+ * the failed call's results are not served: every count is -1, every id -1
+ * and every score -inf. */
 int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx,
                           const float* d_queries, int32_t query_pitch, int32_t B,
                           float query_timestamp, float lambda,
@@ -358,6 +360,15 @@ int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx,
 
 /* Statistics of the last mars_query_batch_topk call (waits for it). */
 int mars_batch_last_stats(const mars_batch_ctx* ctx, mars_batch_stats* out);
+
+/* Test hook for the bounded grid-wide wait of the single-launch small-batch
+ * path (no reference counterpart).  spin_limit bounds the polls of that wait
+ * (0: the default, about 2^26 polls of >= 128 ns); extra_arrivals > 0 makes
+ * the next call wait for that many arrivals more than its CTAs make, so its
+ * wait cannot end and gives up after spin_limit polls.  That call's results
+ * are then marked invalid and its status is MARS_ERR_TIMEOUT; the call after
+ * it runs normally. */
+int mars_batch_ctx_debug_wait(mars_batch_ctx* ctx, uint32_t spin_limit, int32_t extra_arrivals);
 
 /* ---- CMNG kNN graph (include/cmng.cuh) --------------------------------- */
 
@@ -442,9 +453,14 @@ int mars_cmng_search_bfs_batch(const mars_store* s, mars_cmng_ctx* ctx,
  * mars_scan_topk's.  Working memory is a library-owned device array of
  * MARS_NOALLOC_SCRATCH_BYTES that every GPU loading the library holds until
  * exit; K above MARS_NOALLOC_MAX_K is rejected with MARS_ERR_CAPACITY.  The
- * first call on a device looks the array up (cudaGetSymbolAddress): make it
- * before any stream capture.  All calls share the array, so calls that
- * overlap on the GPU race; serialise them.  Works on the current device. */
+ * first call on a device sets it up: it looks the array up
+ * (cudaGetSymbolAddress) and loads every kernel this entry point can launch,
+ * which is when the library's code and the array take their place in device
+ * memory under lazy module loading (the CUDA default).  Make that first call
+ * (any K, any D) before reserving the rest of the device memory and before
+ * any stream capture, or run with CUDA_MODULE_LOADING=EAGER; later calls
+ * load nothing.  All calls share the array, so calls that overlap on the
+ * GPU race; serialise them.  Works on the current device. */
 #define MARS_NOALLOC_MAX_K 128
 #define MARS_NOALLOC_SCRATCH_BYTES 524548
 int mars_scan_topk_noalloc(const float* d_embeddings, int32_t row_pitch,

@@ -37,8 +37,11 @@ DECAYS = ((1e-8, 1e7), (2e-7, 1e7))
 
 def main() -> None:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("MARS_REFERENCE_ROOT", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("MARS_REFERENCE_ROOT"),
+                    help="root of the reference checkout (or MARS_REFERENCE_ROOT)")
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("give --ref or set MARS_REFERENCE_ROOT to the reference checkout")
     sys.path.insert(0, os.path.join(args.ref, "scripts"))
     import bench_cpu  # the reference's own module
 

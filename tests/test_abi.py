@@ -62,3 +62,13 @@ def test_calls_fail_cleanly_without_a_device():
     with pytest.raises(mars_b200.MarsError) as e:
         mars_b200.Store(16, 8)
     assert e.value.status in (mars_b200.MARS_ERR_NO_DEVICE, mars_b200.MARS_ERR_CUDA)
+
+
+def test_python_limits_match_the_header():
+    import mars_b200
+    text = open(HEADER).read()
+    defines = {m.group(1): int(m.group(2))
+               for m in re.finditer(r"#define\s+(MARS_[A-Z0-9_]+)\s+(\d+)", text)}
+    assert mars_b200.MAX_TOP_K == defines["MARS_MAX_TOP_K"]
+    assert mars_b200.NOALLOC_MAX_K == defines["MARS_NOALLOC_MAX_K"]
+    assert mars_b200.MAX_BFS_HOPS == defines["MARS_MAX_BFS_HOPS"]
