@@ -260,6 +260,34 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                 sm100::tmem_ld_wait();
                 if (!qv) continue;
                 const int rbase = row0 + c * 32;
+                if (MODE == kCandidates) {
+                    // which of the 32 rows pass; one atomic per chunk for all
+                    // of them (clustered data can make a query's candidates
+                    // dense in a few tiles), then the writes
+                    uint32_t pass = 0u;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) {
+                        const float w = (rbase + j == self_row) ? NAN : s_w[c * 32 + j];
+                        const float f = __uint_as_float(r[j]) * w;
+                        if (f + mg * fabsf(w) >= th) pass |= 1u << j;   // NaN weights never pass
+                    }
+                    if (pass != 0u) {
+                        int pos = atomicAdd(a.cand_cnt + q, __popc(pass));
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (pass & (1u << j)) {
+                                if (pos < a.cap) {
+                                    const float w = s_w[c * 32 + j];
+                                    a.cand[(int64_t)q * a.cap + pos] = rbase + j;
+                                    a.cand_f[(int64_t)q * a.cap + pos] = __uint_as_float(r[j]) * w;
+                                    a.cand_s[(int64_t)q * a.cap + pos] = mg * fabsf(w);
+                                }
+                                ++pos;
+                            }
+                        }
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int j4 = 0; j4 < 8; ++j4) {
                     const float4 w4 = reinterpret_cast<const float4*>(s_w + c * 32)[j4];
@@ -270,22 +298,12 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                         const float w = (rbase + j == self_row) ? NAN : wv[u];
                         const float f = __uint_as_float(r[j]) * w;
                         const float slack = mg * fabsf(w);
-                        if (MODE == kCandidates) {
-                            if (f + slack >= th) {      // NaN weights never pass
-                                const int pos = atomicAdd(a.cand_cnt + q, 1);
-                                if (pos < a.cap) {
-                                    a.cand[(int64_t)q * a.cap + pos] = rbase + j;
-                                    a.cand_f[(int64_t)q * a.cap + pos] = f;
-                                    a.cand_s[(int64_t)q * a.cap + pos] = slack;
-                                }
-                            }
-                        } else {
-                            float lo = f - slack;
-                            if (lo > best[kJ - 1]) {    // NaN never passes
+                        // sample mode: the tile's kJ best lower bounds of query q
+                        float lo = f - slack;
+                        if (lo > best[kJ - 1]) {    // NaN never passes
 #pragma unroll
-                                for (int s = 0; s < kJ; ++s) {
-                                    if (lo > best[s]) { const float tmp = best[s]; best[s] = lo; lo = tmp; }
-                                }
+                            for (int s = 0; s < kJ; ++s) {
+                                if (lo > best[s]) { const float tmp = best[s]; best[s] = lo; lo = tmp; }
                             }
                         }
                     }
@@ -435,6 +453,12 @@ threshold_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tiles, i
 //  * Pruning: with theta2 the K-th largest lo_c, a candidate with
 //    hi_c < theta2 cannot enter the top-K, so only candidates with
 //    hi_c >= theta2 are rescored exactly (typically K plus a few).
+//  * Row shards: with bound_out the kernel stops after pass 1 and writes
+//    theta2 (-inf when the query is not certified).  K rows of this shard
+//    score at least theta2, so the largest theta2 over all shards is a lower
+//    bound of the global K-th score; a later launch with bound_in prunes with
+//    max(theta2, bound_in[q]) and keeps only rows that can still enter the
+//    global top-K (about K / shards + a few per shard instead of K + a few).
 // Both selections are block-wide bitonic sorts in shared memory ranked by
 // (score desc, id asc).
 constexpr int kSortCap = 4096;
@@ -477,7 +501,8 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
                int32_t* __restrict__ out_ids, float* __restrict__ out_vals,
                int32_t* __restrict__ out_cnt, int32_t* __restrict__ fallback,
                int32_t* __restrict__ rescored, const int32_t* __restrict__ bad,
-               const int32_t* __restrict__ status) {
+               const int32_t* __restrict__ status, float* __restrict__ bound_out,
+               const float* __restrict__ bound_in) {
     __shared__ float   s_key[kSortCap];
     __shared__ int32_t s_id[kSortCap];
     __shared__ int     s_ge, s_n2, s_nk;
@@ -489,6 +514,11 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     const int qi = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int kWarps = kRescoreThreads / 32;
+    if (bound_out != nullptr && threadIdx.x == 0) {
+        bound_out[qi] = -INFINITY;   // until certified
+        // element B: 1 when this shard's call failed (its results are not served)
+        if (qi == 0) bound_out[gridDim.x] = (status[0] != 0 || status[1] != 0) ? 1.0f : 0.0f;
+    }
     if (status[0] != 0 || status[1] != 0) {
         // a bounded wait of this call's GEMM gave up: the short lists and the
         // thresholds may be incomplete, so no result of the call is served
@@ -550,6 +580,11 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         th2 = key2f(block_kth_largest_key<kRescoreThreads>(
             [&](int i) { return f2key(s_key[i]); }, nc_, K, s_hist, s_sel));
     }
+    if (bound_out != nullptr) {      // shard pass 1: this shard's certified bound only
+        if (threadIdx.x == 0) bound_out[qi] = th2;
+        return;
+    }
+    if (bound_in != nullptr) th2 = fmaxf(th2, __ldcg(bound_in + qi));
 
     // ---- pass 2: exact scores of the candidates that can still place -------
     // Their rows are listed first (in the histogram's space, free now) and
@@ -980,6 +1015,7 @@ struct mars_batch_ctx {
     cudaStream_t stream = nullptr;
     float* d_margin = nullptr;       // max_batch
     float* d_theta = nullptr;
+    float* d_bound = nullptr;        // max_batch + 1: certified K-th lower bounds and a failure flag (row shards)
     int32_t* d_cand = nullptr;       // max_batch * cap
     float* d_cand_f = nullptr;       // max_batch * cap
     // the call's status words, one block read back with one copy:
@@ -1121,6 +1157,7 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     T(cudaEventCreate(&c->ev_gemm[1]), "event");
     T(cudaMalloc(&c->d_margin, (size_t)max_batch * 4), "margins");
     T(cudaMalloc(&c->d_theta, (size_t)max_batch * 4), "thresholds");
+    T(cudaMalloc(&c->d_bound, ((size_t)max_batch + 1) * 4), "shard bounds + failure flag");
     T(cudaMalloc(&c->d_cand, (size_t)max_batch * c->cap * 4), "candidates");
     T(cudaMalloc(&c->d_cand_f, (size_t)max_batch * c->cap * 8), "candidate scores and slacks");
     const size_t status_words = 2 + 4 * (size_t)max_batch;
@@ -1192,7 +1229,7 @@ int mars_batch_ctx_destroy(mars_batch_ctx* c) {
     if (c == nullptr) return MARS_OK;
     MarsDeviceGuard g(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
-    cudaFree(c->d_margin); cudaFree(c->d_theta); cudaFree(c->d_cand);
+    cudaFree(c->d_margin); cudaFree(c->d_theta); cudaFree(c->d_bound); cudaFree(c->d_cand);
     cudaFree(c->d_cand_f); cudaFree(c->d_sample); cudaFree(c->d_sample_rt);
     cudaFree(c->d_status); cudaFreeHost(c->h_status);
     cudaFree(c->d_q16);
@@ -1227,7 +1264,7 @@ int mars_query_batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d
 int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
                     int32_t B, float t_q, float lambda, int32_t modality_filter, int32_t use_importance,
                     int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
-                    int32_t* d_counts, void* stream, bool allow_f16);
+                    int32_t* d_counts, void* stream, bool allow_f16, mars::BoundExchange* xchg);
 
 // After a wait that gave up, some CTAs of the small-batch launch may not
 // have counted their arrival: once the stream is idle, the grid counter and
@@ -1293,13 +1330,24 @@ int mars::batch_topk(const mars_store* s, mars_batch_ctx* c, const float* d_quer
                      int32_t* d_counts, void* stream) {
     return batch_topk_pass(s, c, d_queries, query_pitch, B, t_q, lambda, modality_filter, use_importance, K,
                            row_offset, self_base, d_ids, d_vals, d_counts, stream,
-                           c != nullptr && c->precision == 0);
+                           c != nullptr && c->precision == 0, nullptr);
+}
+
+cudaStream_t mars::batch_ctx_stream(const mars_batch_ctx* c) { return c->stream; }
+
+int mars::batch_topk_sharded(const mars_store* s, mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
+                             int32_t B, float t_q, float lambda, int32_t modality_filter, int32_t use_importance,
+                             int32_t K, int32_t row_offset, int32_t* d_ids, float* d_vals, int32_t* d_counts,
+                             void* stream, BoundExchange* xchg) {
+    return batch_topk_pass(s, c, d_queries, query_pitch, B, t_q, lambda, modality_filter, use_importance, K,
+                           row_offset, -1, d_ids, d_vals, d_counts, stream, c != nullptr && c->precision == 0,
+                           xchg);
 }
 
 int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
                     int32_t B, float t_q, float lambda, int32_t modality_filter, int32_t use_importance,
                     int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
-                    int32_t* d_counts, void* stream, bool allow_f16) {
+                    int32_t* d_counts, void* stream, bool allow_f16, mars::BoundExchange* xchg) {
     if (s == nullptr || c == nullptr || d_queries == nullptr || d_ids == nullptr || d_vals == nullptr)
         return fail(MARS_ERR_INVALID, "mars_query_batch_topk: NULL argument");
     if (s->device != c->device || s->dim != c->dim)
@@ -1535,13 +1583,25 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     StoreView v{};
     v.E = s->d_E; v.ts = s->d_ts; v.imp = s->d_imp; v.mod = s->d_mod; v.d_n = s->d_n;
     v.pitch4 = s->pitch / 4; v.nc = (s->dim + 3) / 4;
-    rescore_kernel<<<B, kRescoreThreads, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, use_importance, K,
-                                                  row_offset, c->d_theta, c->d_margin, c->d_cand,
-                                                  c->d_cand_f, c->d_cand_f + (size_t)c->max_batch * c->cap,
-                                                  c->d_cand_cnt, c->cap, d_ids, d_vals, d_counts,
-                                                  c->d_fallback, c->d_rescored, f16 ? c->d_bad : nullptr,
-                                                  c->d_status);
-    MARS_CUDA_TRY(cudaGetLastError());
+    auto rescore = [&](float* bound_out, const float* bound_in) {
+        rescore_kernel<<<B, kRescoreThreads, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, use_importance, K,
+                                                      row_offset, c->d_theta, c->d_margin, c->d_cand,
+                                                      c->d_cand_f, c->d_cand_f + (size_t)c->max_batch * c->cap,
+                                                      c->d_cand_cnt, c->cap, d_ids, d_vals, d_counts,
+                                                      c->d_fallback, c->d_rescored, f16 ? c->d_bad : nullptr,
+                                                      c->d_status, bound_out, bound_in);
+        return cudaGetLastError();
+    };
+    if (xchg != nullptr) {
+        // row shards: certified bounds, their maximum over the shards, then
+        // the rescore against it
+        MARS_CUDA_TRY(rescore(c->d_bound, nullptr));
+        xchg->done = true;
+        MARS_TRY(xchg->fn(xchg->arg, c->d_bound, B, st));
+        MARS_CUDA_TRY(rescore(nullptr, c->d_bound));
+    } else {
+        MARS_CUDA_TRY(rescore(nullptr, nullptr));
+    }
     // 6. exact rescans of the flagged queries (every CTA of an unflagged
     // query leaves at once)
     ScanArgs fa{};

@@ -24,6 +24,28 @@ int batch_topk(const mars_store* s, struct mars_batch_ctx* c, const float* d_que
                int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
                int32_t* d_counts, void* stream);
 
+// Row shards: between the two rescore passes of a batched call, the
+// certified K-th lower bounds of the B queries (d_bound[0, B), device
+// floats, -inf where uncertified) and a failure flag (d_bound[B]: 1 when the
+// shard's call failed) are replaced on every shard by their maximum over the
+// shards.  fn enqueues that exchange of B + 1 floats on `st`; `done` records
+// that the batched call reached it (every rank runs it exactly once per
+// call).
+struct BoundExchange {
+    int (*fn)(void* arg, float* d_bound, int32_t B, cudaStream_t st);
+    void* arg;
+    bool done;
+};
+
+// The stream a batched call with stream == NULL runs on.
+cudaStream_t batch_ctx_stream(const struct mars_batch_ctx* c);
+
+// mars_query_batch_topk over one row shard with the bound exchange above.
+int batch_topk_sharded(const mars_store* s, struct mars_batch_ctx* c, const float* d_queries,
+                       int32_t query_pitch, int32_t B, float t_q, float lambda, int32_t modality_filter,
+                       int32_t use_importance, int32_t K, int32_t row_offset, int32_t* d_ids, float* d_vals,
+                       int32_t* d_counts, void* stream, BoundExchange* xchg);
+
 // mars_scan_topk that leaves out one local row (exclude_row < 0: none).
 int scan_topk_excluding(const mars_store* s, mars_query_ctx* c, const float* d_query, float t_q,
                         float lambda, int32_t modality_filter, int32_t use_importance, int32_t K,

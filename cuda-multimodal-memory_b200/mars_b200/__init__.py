@@ -138,6 +138,15 @@ _SIGS = {
                               _VP, _VP, _VP],
     "mars_batch_last_stats": [_VP, C.POINTER(BatchStats)],
     "mars_batch_ctx_debug_wait": [_VP, C.c_uint32, _I32],
+    "mars_shard_unique_id": [_VP],
+    "mars_shard_comm_create": [_I32, _I32, _I32, _VP, _I32, _I32, C.POINTER(_VP)],
+    "mars_shard_comm_destroy": [_VP],
+    "mars_shard_comm_status": [_VP],
+    "mars_shard_comm_abort": [_VP],
+    "mars_shard_comm_set_timing": [_VP, _I32],
+    "mars_shard_last_times": [_VP, C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(C.c_float)],
+    "mars_shard_query_batch_topk": [_VP, _VP, _VP, _VP, _I32, _I32, _F32, _F32, _I32, _I32, _I32, _I32,
+                                    _VP, _VP, _VP, _VP],
     "mars_cmng_build": [_VP, _I32, _I32, _I32, _VP, C.POINTER(C.c_float)],
     "mars_cmng_build_rows": [_VP, _I32, _I32, _I32, _I32, _I32, _VP, C.POINTER(C.c_float)],
     "mars_cmng_knn": [_VP, _I32, _VP, _VP, _VP],
@@ -495,6 +504,63 @@ class BatchContext:
     def close(self):
         if getattr(self, "handle", None):
             lib().mars_batch_ctx_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+SHARD_ID_BYTES = 128
+
+
+def shard_unique_id() -> bytes:
+    """A fresh NCCL unique id (make it on rank 0 and give it to every rank)."""
+    buf = C.create_string_buffer(SHARD_ID_BYTES)
+    _check(lib().mars_shard_unique_id(buf))
+    return buf.raw
+
+
+class ShardComm:
+    """Row-shard communicator (one per rank and GPU; NCCL owned by the library)."""
+
+    def __init__(self, device: int, rank: int, world: int, unique_id: bytes, max_batch: int, max_k: int):
+        assert len(unique_id) == SHARD_ID_BYTES
+        h = C.c_void_p()
+        buf = C.create_string_buffer(unique_id, SHARD_ID_BYTES)
+        _check(lib().mars_shard_comm_create(device, rank, world, buf, max_batch, max_k, C.byref(h)))
+        self.handle = h
+        self.rank, self.world = rank, world
+
+    def query_batch_topk(self, store: Store, bc: "BatchContext", d_queries, B, t_q, lam, K, d_ids, d_vals,
+                         d_counts=None, modality_filter=-1, use_importance=False, row_offset=0,
+                         query_pitch=None, stream=None):
+        """The global top-K of every query over all ranks' shards (collective)."""
+        pitch = query_pitch if query_pitch is not None else (store.dim + 3) // 4 * 4
+        _check(lib().mars_shard_query_batch_topk(store.handle, bc.handle, self.handle, _ptr(d_queries), pitch, B,
+                                                 float(t_q), float(lam), modality_filter, int(use_importance),
+                                                 K, row_offset, _ptr(d_ids), _ptr(d_vals), _ptr(d_counts),
+                                                 _stream(stream, d_queries, d_ids, d_vals, d_counts)))
+
+    def set_timing(self, enable: bool) -> None:
+        _check(lib().mars_shard_comm_set_timing(self.handle, int(bool(enable))))
+
+    def last_times(self) -> dict:
+        a, b, m = C.c_float(), C.c_float(), C.c_float()
+        _check(lib().mars_shard_last_times(self.handle, C.byref(a), C.byref(b), C.byref(m)))
+        return {"local_ms": a.value, "gather_ms": b.value, "merge_ms": m.value}
+
+    def status(self) -> None:
+        _check(lib().mars_shard_comm_status(self.handle))
+
+    def abort(self) -> None:
+        _check(lib().mars_shard_comm_abort(self.handle))
+
+    def close(self):
+        if getattr(self, "handle", None):
+            lib().mars_shard_comm_destroy(self.handle)
             self.handle = None
 
     def __del__(self):

@@ -370,6 +370,57 @@ int mars_batch_last_stats(const mars_batch_ctx* ctx, mars_batch_stats* out);
  * it runs normally. */
 int mars_batch_ctx_debug_wait(mars_batch_ctx* ctx, uint32_t spin_limit, int32_t extra_arrivals);
 
+/* ---- row shards across GPUs ---------------------------------------------
+ * No reference counterpart: the reference runs on one GPU and lists
+ * multi-GPU sharding as future work (NEXT_STEPS.md:31).  One process per GPU;
+ * rank r holds rows [offset_r, offset_r + n_r) of the corpus in its own
+ * store.  The library owns an NCCL communicator (libnccl.so.2, loaded at run
+ * time: the copy already in the process, else the system's).  Rank 0 makes a
+ * unique id with mars_shard_unique_id and the caller hands its
+ * MARS_SHARD_ID_BYTES bytes to every rank (any channel), then every rank
+ * creates its communicator. */
+#define MARS_SHARD_ID_BYTES 128
+typedef struct mars_shard_comm mars_shard_comm;
+
+int mars_shard_unique_id(void* id_out);
+/* Collective over the `world` ranks (blocks until all have joined).  Calls
+ * on it take B <= max_batch queries and K <= max_k; world x max_k <= 4096. */
+int mars_shard_comm_create(int32_t device, int32_t rank, int32_t world, const void* unique_id,
+                           int32_t max_batch, int32_t max_k, mars_shard_comm** out);
+/* Waits for the device, then frees the communicator.  NULL is accepted. */
+int mars_shard_comm_destroy(mars_shard_comm* comm);
+/* MARS_OK, or the communicator's asynchronous NCCL error (a peer that failed
+ * or left); after an error, mars_shard_comm_abort ends the communicator so
+ * that no rank waits for the others any longer, then destroy it. */
+int mars_shard_comm_status(mars_shard_comm* comm);
+int mars_shard_comm_abort(mars_shard_comm* comm);
+/* Optional: record events around the call's three phases (local pipeline
+ * with the bound exchange / all-gather / merge); mars_shard_last_times waits
+ * for the last call and returns their device times in ms. */
+int mars_shard_comm_set_timing(mars_shard_comm* comm, int32_t enable);
+int mars_shard_last_times(mars_shard_comm* comm, float* local_ms, float* gather_ms, float* merge_ms);
+
+/* mars_query_batch_topk over a row-sharded corpus, called by every rank with
+ * the same queries, B, K, t_q, lambda, filter and use_importance (a
+ * collective).  s: this rank's shard; row_offset: its first global row.
+ * Outputs on every rank: the global top-K [B][K] (global ids), d_counts [B].
+ * Each shard runs the batched tensor-core pipeline; between its two rescore
+ * passes one NCCL all-reduce (max) of the B certified K-th lower bounds gives
+ * every shard a bound of the global K-th score, so a shard rescores only
+ * rows that can still place; then one NCCL all-gather of B x K packed 64-bit
+ * keys (score, then id) and a per-query selection on every rank.  The
+ * results equal mars_query_batch_topk over the whole corpus on one GPU, bit
+ * for bit.  Asynchronous on `stream` (NULL: the batch context's stream).  If
+ * any rank's call fails (an argument, or a bounded device wait that gave
+ * up), every rank's results of that call are marked invalid (counts -1, ids
+ * -1) and the failing rank returns the error; ranks still take every
+ * collective step. */
+int mars_shard_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx, mars_shard_comm* comm,
+                                const float* d_queries, int32_t query_pitch, int32_t B,
+                                float query_timestamp, float lambda, int32_t modality_filter,
+                                int32_t use_importance, int32_t K, int32_t row_offset,
+                                int32_t* d_ids, float* d_vals, int32_t* d_counts, void* stream);
+
 /* ---- CMNG kNN graph (include/cmng.cuh) --------------------------------- */
 
 /* CMNGSearchConfig, include/cmng.cuh:54-62 (bools widened to int32). */

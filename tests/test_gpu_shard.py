@@ -1,0 +1,111 @@
+"""Row-sharded batched top-K (mars_shard_query_batch_topk) with the NCCL
+communicator owned by the library.
+
+* One rank on one GPU (world 1, real NCCL): the call equals
+  mars_query_batch_topk on the same store bit for bit, for the small-batch
+  tiles (B <= 64), the 128 x 256 tiles and K = 256, with a row offset.
+* A bounded device wait that gives up on a rank (the batch context's test
+  hook) marks that call's merged results invalid (counts -1) and the call
+  after it is exact again.
+* Two ranks on two GPUs (tests/shard_worker.py under torchrun, when two GPUs
+  are visible): every rank's merged answer is the same, equals the single-GPU
+  answer over the whole corpus bit for bit, and matches the CPU oracle.
+"""
+import json
+import os
+import subprocess
+import sys
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def env():
+    import torch
+
+    import mars_b200 as mb
+    from mars_b200 import datagen
+    N, D = 150_000, 768
+    E, mod, ts, imp = datagen.gaussian_corpus(N, D, seed=31, ts_max=600.0)
+    st = mb.Store(N, D)
+    st.upload(E, mod, ts, imp)
+    comm = mb.ShardComm(0, 0, 1, mb.shard_unique_id(), max_batch=256, max_k=256)
+    Qd = torch.from_numpy(datagen.queries(256, D, seed=32)).cuda()
+    yield st, comm, Qd, N, D
+    comm.close()
+
+
+def _answers(fn, B, K):
+    import torch
+    ids = torch.full((B, K), -7, dtype=torch.int32, device="cuda")
+    vals = torch.zeros((B, K), dtype=torch.float32, device="cuda")
+    cnt = torch.full((B,), -7, dtype=torch.int32, device="cuda")
+    fn(ids, vals, cnt)
+    torch.cuda.synchronize()
+    return ids.cpu().numpy(), vals.cpu().numpy(), cnt.cpu().numpy()
+
+
+@pytest.mark.parametrize("B,K", [(16, 10), (200, 100), (64, 256)])
+def test_world1_equals_unsharded_call(env, B, K):
+    import mars_b200 as mb
+    st, comm, Qd, N, D = env
+    bc = mb.BatchContext(N, D, max_batch=256, max_k=256)
+    off = 1_000_000
+    ref = _answers(lambda i, v, c: bc.query_batch_topk(st, Qd[:B], B, 600.0, 0.01, K, i, v, c, use_importance=True,
+                                                       row_offset=off), B, K)
+    got = _answers(lambda i, v, c: comm.query_batch_topk(st, bc, Qd[:B], B, 600.0, 0.01, K, i, v, c,
+                                                         use_importance=True, row_offset=off), B, K)
+    assert np.array_equal(got[2], ref[2])
+    assert np.array_equal(got[0], ref[0])
+    assert np.array_equal(got[1].view(np.int32), ref[1].view(np.int32))
+    comm.set_timing(True)
+    _answers(lambda i, v, c: comm.query_batch_topk(st, bc, Qd[:B], B, 600.0, 0.01, K, i, v, c,
+                                                   use_importance=True, row_offset=off), B, K)
+    t = comm.last_times()
+    comm.set_timing(False)
+    assert t["local_ms"] > 0 and t["gather_ms"] >= 0 and t["merge_ms"] > 0
+    comm.status()
+
+
+def test_failed_rank_invalidates_merged_results(env):
+    import mars_b200 as mb
+    st, comm, Qd, N, D = env
+    B, K = 16, 10
+    bc = mb.BatchContext(N, D, max_batch=256, max_k=256)
+    ref = _answers(lambda i, v, c: bc.query_batch_topk(st, Qd[:B], B, 600.0, 0.01, K, i, v, c,
+                                                       use_importance=True), B, K)
+    bc.debug_wait(4096, 1)          # this call's grid-wide wait cannot end
+    ids, vals, cnt = _answers(lambda i, v, c: comm.query_batch_topk(st, bc, Qd[:B], B, 600.0, 0.01, K, i, v, c,
+                                                                    use_importance=True), B, K)
+    assert np.all(cnt == -1) and np.all(ids == -1) and np.all(np.isneginf(vals))
+    # the failing rank reports the timeout on its next call (which joins the
+    # collectives with neutral data, so its results are invalid too) ...
+    with pytest.raises(mb.MarsError) as e:
+        _answers(lambda i, v, c: comm.query_batch_topk(st, bc, Qd[:B], B, 600.0, 0.01, K, i, v, c,
+                                                       use_importance=True), B, K)
+    assert e.value.status == mb.MARS_ERR_TIMEOUT
+    # ... and the one after is exact again
+    got = _answers(lambda i, v, c: comm.query_batch_topk(st, bc, Qd[:B], B, 600.0, 0.01, K, i, v, c,
+                                                         use_importance=True), B, K)
+    assert np.array_equal(got[0], ref[0]) and np.array_equal(got[2], ref[2])
+
+
+def test_two_ranks_on_two_gpus(tmp_path):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    out = str(tmp_path / "shard.json")
+    cmd = ["timeout", "-k", "30", "600", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29517",
+           os.path.join(ROOT, "tests", "shard_worker.py"), out]
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    rep = json.load(open(out))
+    assert rep["world"] == 2
+    assert rep["ranks_agree"] and rep["equal_to_single_gpu"] and rep["oracle_ok"], rep

@@ -163,3 +163,112 @@ def test_query_split_covers_every_query_once():
             seen = np.concatenate([np.arange(nq * r // world, nq * (r + 1) // world) for r in range(world)])
             assert np.array_equal(seen, np.arange(nq))
             assert max(nq * (r + 1) // world - nq * r // world for r in range(world)) <= (nq + world - 1) // world
+
+
+# ---------------------------------------------------------------------------
+# Row shards with a shared pruning bound (mars_shard_query_batch_topk):
+# every rank certifies a lower bound of its shard's K-th score (here the
+# approximate scores' K-th lower bound, approximate = exact + noise within a
+# stated margin), one all-reduce (max) gives a bound of the global K-th score,
+# every rank keeps only rows whose upper bound reaches it, packs its local
+# top-K as 64-bit rank keys (score, then id), and one all-gather + a per-query
+# selection gives the global answer.  A rank that flags a failure makes every
+# rank's answer invalid (count -1).
+NS, DS, KS, QS, MARGIN = 4001, 32, 9, 6, 2e-3
+
+
+def _f2key(v):
+    u = np.asarray(v, np.float32).view(np.uint32).astype(np.uint64)
+    return np.where(u & 0x80000000, (~u) & 0xFFFFFFFF, u | 0x80000000)
+
+
+def _rank_keys(ids, vals):
+    k = (_f2key(vals) << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - ids.astype(np.int64).astype(np.uint64))
+    return np.where(ids >= 0, k, np.uint64(0)).astype(np.uint64)
+
+
+def _key_decode(k):
+    hi = (k >> np.uint64(32)).astype(np.uint32)
+    u = np.where(hi & 0x80000000, hi & 0x7FFFFFFF, ~hi).astype(np.uint32)
+    ids = (np.uint64(0xFFFFFFFF) - (k & np.uint64(0xFFFFFFFF))).astype(np.int64).astype(np.int32)
+    return ids, u.view(np.float32)
+
+
+def _bound_worker(rank, world, port, out_path, fail_rank):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "cuda-multimodal-memory_b200"))
+    sys.path.insert(0, os.path.join(root, "oracle"))
+    import oracle as O
+    from mars_b200 import datagen
+    lo, hi = NS * rank // world, NS * (rank + 1) // world
+    E, mod, ts, imp = datagen.gaussian_rows(lo, hi, DS, seed=21, ts_max=600.0)
+    Qm = datagen.queries(QS, DS, seed=22)
+    c = O.Corpus(E=E, ts=ts, mod=mod, imp=imp)
+    rng = np.random.default_rng(100 + rank)
+    exact = np.stack([O.fused_scores(c, Qm[q], 600.0, 0.01, use_importance=True) for q in range(QS)])
+    approx = exact + rng.uniform(-MARGIN, MARGIN, exact.shape).astype(np.float32)
+    # pass 1: the K-th largest lower bound of the shard, and the failure flag
+    bound = np.sort(approx - MARGIN, axis=1)[:, -KS].astype(np.float32)
+    flag = np.float32(1.0 if rank == fail_rank else 0.0)
+    t = torch.from_numpy(np.concatenate([bound, [flag]]).astype(np.float32))
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    gbound, failed = t[:QS].numpy(), float(t[QS])
+    # pass 2: exact scores of the rows whose upper bound reaches the global bound
+    ids = np.full((QS, KS), -1, np.int32)
+    vals = np.full((QS, KS), -np.inf, np.float32)
+    kept = 0
+    for q in range(QS):
+        rows = np.nonzero(approx[q] + MARGIN >= max(gbound[q], bound[q]))[0]
+        kept += rows.size
+        order = sorted(rows.tolist(), key=lambda r: (-float(exact[q, r]), r))[:KS]
+        ids[q, :len(order)] = np.asarray(order, np.int32) + lo
+        vals[q, :len(order)] = exact[q, order]
+    keys = torch.from_numpy(_rank_keys(ids, vals).view(np.int64))
+    got = [torch.empty_like(keys) for _ in range(world)]
+    dist.all_gather(got, keys)
+    allk = torch.stack(got).numpy().view(np.uint64)           # [world][Q][K]
+    out_i = np.full((QS, KS), -1, np.int32)
+    out_v = np.full((QS, KS), -np.inf, np.float32)
+    cnt = np.zeros(QS, np.int32)
+    for q in range(QS):
+        if failed > 0:
+            cnt[q] = -1
+            continue
+        k = np.sort(allk[:, q, :].ravel())[::-1]
+        k = k[k != 0][:KS]
+        out_i[q, :k.size], out_v[q, :k.size] = _key_decode(k)
+        cnt[q] = k.size
+    kept_all = torch.tensor([kept], dtype=torch.int64)
+    dist.all_reduce(kept_all)
+    if rank == 0:
+        np.savez(out_path, ids=out_i, vals=out_v, cnt=cnt, kept=int(kept_all))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,fail_rank", [(2, -1), (3, -1), (2, 1)])
+def test_shared_bound_shards_equal_whole_corpus(tmp_path, world, fail_rank):
+    out = str(tmp_path / "bound.npz")
+    mp.start_processes(_bound_worker, args=(world, _free_port(), out, fail_rank), nprocs=world, join=True,
+                       start_method="spawn")
+    z = np.load(out)
+    if fail_rank >= 0:
+        assert np.all(z["cnt"] == -1) and np.all(z["ids"] == -1)
+        return
+    import oracle as O
+    from mars_b200 import datagen
+    E, mod, ts, imp = datagen.gaussian_rows(0, NS, DS, seed=21, ts_max=600.0)
+    Qm = datagen.queries(QS, DS, seed=22)
+    c = O.Corpus(E=E, ts=ts, mod=mod, imp=imp)
+    for q in range(QS):
+        s = O.fused_scores(c, Qm[q], 600.0, 0.01, use_importance=True)
+        i, v = O.topk(s, mod, -1, KS)
+        assert np.array_equal(z["ids"][q], i)
+        assert np.array_equal(z["vals"][q], v)
+        assert z["cnt"][q] == KS
+    # the shared bound prunes: far fewer rows than world x K per query survive
+    assert z["kept"] < world * KS * QS
