@@ -73,9 +73,15 @@ def parse_args():
                          "its own queries; weak scaling) or rows (the corpus row-sharded, every GPU answers "
                          "the same queries on its shard, NCCL all-gather + merge; strong scaling)")
     ap.add_argument("--workload", choices=["scan", "c0", "c1", "c2", "c3", "c4"], default="scan",
-                    help="scan: the headline (default); c0: single-query latency at N=2400 "
-                         "with BFS depth 1; c1: streaming loop (append 10 rows + query per frame)")
+                    help="scan: the headline (default; its line also carries every config under "
+                         "`configs`); c0: single-query latency at N=2400 with BFS depth 1; c1: streaming "
+                         "loop (append 10 rows + query per frame); c2: batched top-K B=1024 K=100, rows "
+                         "sharded; c3: kNN-graph build; c4: graph search + BFS")
     ap.add_argument("--frames", type=int, default=10000)
+    ap.add_argument("--c4-n", type=int, default=1_000_000, help="rows of the c4 corpus")
+    ap.add_argument("--skip-configs", default="",
+                    help="comma-separated configs (c0..c4) left out of the default run's `configs`")
+    ap.add_argument("--no-configs", action="store_true", help="the headline only")
     return ap.parse_args()
 
 
@@ -400,13 +406,14 @@ def run_mars(a):
     # device buffers are reused in stream order.
     Qpin = torch.from_numpy(Qh).pin_memory()
     qbuf = torch.empty((Q, a.dim), dtype=torch.float32, device="cuda")
-    out_ids = [torch.empty((Q, K), dtype=torch.int32).pin_memory() for _ in range(2)]
-    out_vals = [torch.empty((Q, K), dtype=torch.float32).pin_memory() for _ in range(2)]
-    out_cnt = [torch.empty(Q, dtype=torch.int32).pin_memory() for _ in range(2)]
-    cnt = torch.empty(Q, dtype=torch.int32, device="cuda")
-    mcnt = torch.empty(Q, dtype=torch.int32, device="cuda")
+    # one packed result buffer per step (ids | scores | counts): one D2H copy
+    res = torch.empty(2 * Q * K + Q, dtype=torch.int32, device="cuda")
+    r_ids = res[:Q * K].view(Q, K)
+    r_vals = res[Q * K:2 * Q * K].view(torch.float32).view(Q, K)
+    r_cnt = res[2 * Q * K:]
+    outs = [torch.empty(2 * Q * K + Q, dtype=torch.int32).pin_memory() for _ in range(2)]
+    outs_np = [o.numpy() for o in outs]
     done = [torch.cuda.Event() for _ in range(2)]
-    res_ids, res_vals = (mids, mvals) if sharded else (ids, vals)
     checksum = 0
     e2e_valid = True
     barrier()
@@ -416,21 +423,22 @@ def run_mars(a):
             b = s % 2
             base = (s * Q) % (64 - Q + 1)
             qbuf.copy_(Qpin[base:base + Q], non_blocking=True)
-            bc.query_batch_topk(store, qbuf, Q, a.ts_max, a.lam, K, ids, vals, cnt, use_importance=True,
-                                row_offset=lo, stream=ctx.stream)
             if sharded:
+                bc.query_batch_topk(store, qbuf, Q, a.ts_max, a.lam, K, ids, vals, use_importance=True,
+                                    row_offset=lo, stream=ctx.stream)
                 dist.all_gather_into_tensor(gids, ids)
                 dist.all_gather_into_tensor(gvals, vals)
-                ctx.topk_merge_batch(gids, gvals, world, K, Q, mids, mvals, mcnt, stream=ctx.stream)
-            out_ids[b].copy_(res_ids, non_blocking=True)
-            out_vals[b].copy_(res_vals, non_blocking=True)
-            out_cnt[b].copy_(mcnt if sharded else cnt, non_blocking=True)
+                ctx.topk_merge_batch(gids, gvals, world, K, Q, r_ids, r_vals, r_cnt, stream=ctx.stream)
+            else:
+                bc.query_batch_topk(store, qbuf, Q, a.ts_max, a.lam, K, r_ids, r_vals, r_cnt,
+                                    use_importance=True, row_offset=lo, stream=ctx.stream)
+            outs[b].copy_(res, non_blocking=True)
             done[b].record(stream)
         if s > 0:   # the previous step's results, read and checked on the host
             p = (s - 1) % 2
             done[p].synchronize()
-            e2e_valid = e2e_valid and bool((out_cnt[p] == K).all())
-            checksum += int(out_ids[p][0, 0])
+            e2e_valid = e2e_valid and bool(outs_np[p][2 * Q * K:].min() == K)
+            checksum += int(outs_np[p][0])
     dt = time.perf_counter() - t0
     bc.last_stats()      # raises if the last step's pipeline reported an error
     if world > 1:
@@ -439,14 +447,14 @@ def run_mars(a):
         dt = float(t.item())
     q_all = Q * (1 if sharded else world)   # queries answered per step by the whole job
     e2e = {"value": a.steps * q_all / dt, "unit": "queries/s",
-           "h2d_bytes_per_step": Q * a.dim * 4, "d2h_bytes_per_step": Q * K * 8 + Q * 4,
+           "h2d_bytes_per_step": Q * a.dim * 4, "d2h_bytes_per_step": (2 * Q * K + Q) * 4,
            "every_step_valid": e2e_valid,
            "path": "pinned H2D of the step's queries, mars_query_batch_topk"
                    + (" per shard, NCCL all-gather, mars_topk_merge_batch" if sharded else
                       (" on every replica" if world > 1 else ""))
-                   + ", D2H of the top-K ids, scores and counts into one of two pinned buffers; the host "
-                     "waits for and reads each step's results (checking every count) while the next step "
-                     "runs"}
+                   + ", one packed D2H of the top-K ids, scores and counts into one of two pinned buffers; "
+                     "the host waits for and reads each step's results (checking every count) while the "
+                     "next step runs"}
     latency = None
     if world == 1:
         # single-query latency through mars_query (host query in, host results out)
@@ -462,6 +470,12 @@ def run_mars(a):
                    "p50_us": float(np.percentile(lat, 50) * 1e6),
                    "p99_us": float(np.percentile(lat, 99) * 1e6)}
 
+    # every config of the family (c2-c4 on all ranks, c0/c1 on one GPU)
+    configs = None
+    if not a.no_configs and not sharded:
+        env = {"rank": rank, "world": world, "local": local, "dist": dist, "rows": (E, mod, ts, imp),
+               "store": store}
+        configs = run_configs(a, env)
     if rank == 0:
         peak, peak_kind = measured_peak()
         pitch16 = (a.dim + 7) // 8 * 8
@@ -521,6 +535,8 @@ def run_mars(a):
             "gpu_launches": a.steps * world * ((4 if small else 6) + (1 if sharded else 0)),
             "clocks": clocks,
         }
+        if configs is not None:
+            line["configs"] = configs
         if world == 1 and not a.no_cpu_baseline:
             line["cpu_baseline"], answers = cpu_baseline(a, E, mod, ts, imp, Qh)
             n_cmp = min(len(answers), ans_ids.shape[0])
@@ -533,52 +549,96 @@ def run_mars(a):
 
 
 # ---------------------------------------------------------------------------
+# The configurations of the workload family (c0-c4).  Each function runs on
+# every rank (collectives in the same order on all of them) and returns the
+# config's record on rank 0 (None elsewhere).  The default run embeds them in
+# the headline line under "configs"; `--workload cX` prints one of them.
 def _pct(xs, p):
     return float(np.percentile(np.asarray(xs), p))
 
 
-def run_latency(a):
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+def _tensor_peaks():
+    """(sustained, burst, kind): the measured bf16 GEMM rates (fp16 runs at
+    the same rate), else the fallback figures."""
+    p = _peaks()
+    if "bf16_tflops" in p:
+        return float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), float(p["bf16_tflops"]), "measured"
+    return 1400.0, 1590.0, "fallback"
+
+
+def _max_over_ranks(dist, x):
+    if dist is None:
+        return x
+    import torch
+    t = torch.tensor([float(x)], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _all_true(dist, ok):
+    if dist is None:
+        return bool(ok)
+    import torch
+    t = torch.tensor([1 if ok else 0], dtype=torch.int32, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)
+    return bool(t.item())
+
+
+def _barrier(dist):
+    import torch
+    torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+        torch.cuda.synchronize()
+
+
+def _init_dist(local, world):
+    """NCCL process group for torchrun launches (None on one GPU)."""
+    if world <= 1:
+        return None
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
+    return dist
+
+
+def cfg_latency(a, which):
     """c0 / c1: single-query latency through the public API (host query in,
     host results out), one GPU.  c0: N = 2,400, lambda = 0.5, K = 10, BFS
     depth 1 over 4 random cross-modal bridges per node.  c1: start with
     N = 10,000 (same generator); every 1 ms frame appends 10 rows stamped with
     the frame time (normalised on the device) and 2 bridge edges per new row,
     then queries with lambda = 1.0, K = 10, depth 1; latency and freshness
-    (share of the top-K stamped within the last 100 ms) over all frames."""
+    (share of the top-K stamped within the last 100 ms) over all frames.
+    Parity: the answers of sampled frames against the oracle on the same
+    corpus and graph (c1: the store read back, the CSR plus appended edges)."""
     import torch
     import mars_b200 as mb
     import oracle as O
     from mars_b200 import datagen
+    from _util import assert_ranked_equivalent
 
     D, K = a.dim, 10
-    if a.workload == "c0":
-        N0, lam, frames, per = 2400, 0.5, a.frames, 0
+    frames = a.frames
+    if which == "c0":
+        N0, lam, per = 2400, 0.5, 0
     else:
-        N0, lam, frames, per = 10000, 1.0, a.frames, 10
+        N0, lam, per = 10000, 1.0, 10
     E, mod, ts, imp = datagen.gaussian_corpus(N0, D, seed=a.seed, n_mod=4, ts_max=10.0)
     ro, ci = datagen.random_bridges(mod, 4, seed=7)
     cap = N0 + frames * per
     rng = np.random.default_rng(a.seed + 3)
     Q = datagen.queries(256, D, seed=0x5EED0000)
     cfg_kw = dict(top_k=K, bfs_max_hops=1, time_decay_lambda=lam, bfs_score_decay=0.5)
-
-    if a.impl == "reference":
-        oc = O.Corpus(E=E, ts=ts, mod=mod, row_offsets=ro, col_indices=ci)
-        lat = []
-        for f in range(min(frames, 200)):
-            t0 = time.perf_counter()
-            O.query(oc, Q[f % 256], 10.0, top_k=K, bfs_max_hops=1, lam=lam, bfs_score_decay=0.5,
-                    dot_order=O.DOT_FAST)
-            lat.append(time.perf_counter() - t0)
-        v = len(lat) / sum(lat)
-        print(json.dumps({"impl": "reference", "workload": a.workload, "metric": "queries/s",
-                          "value": v, "unit": "queries/s", "p50_us": _pct(lat, 50) * 1e6,
-                          "p99_us": _pct(lat, 99) * 1e6,
-                          "cpu_baseline": {"value": v, "unit": "queries/s", "cores": 1,
-                                           "kind": "port", "sample": f"{len(lat)} queries, "
-                                           "oracle orc_query single thread (corpus fixed)"}}))
-        return
-
     slack = 64 if per else 0
     store = mb.Store(cap, D, edge_slack=slack)
     slack_used = np.zeros(cap, np.int32)
@@ -591,6 +651,9 @@ def run_latency(a):
     q_lat, a_lat, fresh = [], [], []
     ts_host = np.zeros(cap, np.float32)
     ts_host[:N0] = ts
+    extra_src, extra_dst = [], []
+    check_frames = set(range(0, frames, max(1, frames // 8))) | {frames - 1}
+    answers = {}
     t_base = 10.0
     t_all0 = time.perf_counter()
     for f in range(frames):
@@ -610,155 +673,217 @@ def run_latency(a):
                     dst[i] = rng.integers(0, first)
                 slack_used[dst[i]] += 1
                 slack_used[src[i]] += 1
-            store.append_edges(np.concatenate([src, dst]), np.concatenate([dst, src]))
+            s2, d2 = np.concatenate([src, dst]), np.concatenate([dst, src])
+            store.append_edges(s2, d2)
             a_lat.append(time.perf_counter() - t0)
+            extra_src.append(s2)
+            extra_dst.append(d2)
         t0 = time.perf_counter()
         res = ctx.query(store, Q[f % 256], t_now, cfg)
         q_lat.append(time.perf_counter() - t0)
+        if f in check_frames:
+            answers[f] = (res.copy(), store.num_nodes if per else N0)
         if per:
             fresh.append(float(np.mean(ts_host[res["node_id"]] >= np.float32(t_now - 0.1)))
                          if len(res) else 0.0)
     total = time.perf_counter() - t_all0
-    line = {"workload": a.workload, "metric": "single-query latency (mars_query, host in/out)",
-            "n_start": N0, "n_end": N0 + frames * per, "frames": frames, "dim": D, "top_k": K,
-            "lambda": lam, "bfs_max_hops": 1,
-            "query_p50_us": _pct(q_lat, 50) * 1e6, "query_p99_us": _pct(q_lat, 99) * 1e6,
-            "query_max_us": float(np.max(q_lat) * 1e6),
-            "queries_per_s": frames / sum(q_lat)}
+    # parity of the sampled frames: the oracle on the corpus as it was then
+    n_end = store.num_nodes
     if per:
-        line.update({"append_p50_us": _pct(a_lat, 50) * 1e6, "append_p99_us": _pct(a_lat, 99) * 1e6,
-                     "freshness_mean": float(np.mean(fresh)),
-                     "frames_per_s_incl_append": frames / total})
-    print(json.dumps(line), flush=True)
+        Eh, modh, tsh, _ = store.read(0, n_end)
+        es = np.concatenate(extra_src) if extra_src else np.zeros(0, np.int32)
+        ed = np.concatenate(extra_dst) if extra_dst else np.zeros(0, np.int32)
+    exact = True
+    for f, (res, n_f) in sorted(answers.items()):
+        if per:
+            # CSR over the first n_f rows: the uploaded graph plus the bridges appended by then
+            keep = (es < n_f) & (ed < n_f)
+            adj = [[] for _ in range(n_f)]
+            for u in range(N0):
+                adj[u].extend(ci[ro[u]:ro[u + 1]].tolist())
+            for u, v in zip(es[keep].tolist(), ed[keep].tolist()):
+                adj[u].append(v)
+            ro_f = np.zeros(n_f + 1, np.int32)
+            ro_f[1:] = np.cumsum([len(x) for x in adj])
+            ci_f = np.asarray([v for x in adj for v in x], np.int32)
+            oc = O.Corpus(E=Eh[:n_f], ts=tsh[:n_f], mod=modh[:n_f], row_offsets=ro_f, col_indices=ci_f)
+        else:
+            oc = O.Corpus(E=E, ts=ts, mod=mod, row_offsets=ro, col_indices=ci)
+        ref = O.query(oc, Q[f % 256], t_base + f * 1e-3, top_k=K, bfs_max_hops=1, lam=lam, bfs_score_decay=0.5)
+        try:
+            assert_ranked_equivalent(res["node_id"], res["score"], ref["node_id"], ref["score"], res["hops"],
+                                     ref["hops"], what=f"frame {f}")
+        except AssertionError:
+            exact = False
+    # CPU baseline: the oracle port answering the same queries on the final
+    # corpus, one thread (the reference's only CPU path is NumPy)
+    oc = O.Corpus(E=E, ts=ts, mod=mod, row_offsets=ro, col_indices=ci)
+    lat = []
+    for f in range(64):
+        t0 = time.perf_counter()
+        O.query(oc, Q[f % 256], 10.0, top_k=K, bfs_max_hops=1, lam=lam, bfs_score_decay=0.5, dot_order=O.DOT_FAST)
+        lat.append(time.perf_counter() - t0)
+    rec = {"workload": which, "metric": "single-query latency (mars_query, host in/out)",
+           "n_start": N0, "n_end": n_end, "frames": frames, "dim": D, "top_k": K,
+           "lambda": lam, "bfs_max_hops": 1,
+           "query_p50_us": _pct(q_lat, 50) * 1e6, "query_p99_us": _pct(q_lat, 99) * 1e6,
+           "query_max_us": float(np.max(q_lat) * 1e6), "queries_per_s": frames / sum(q_lat),
+           "oracle_checked_frames": len(answers), "exact_vs_oracle": exact,
+           "cpu_baseline": {"value": len(lat) / sum(lat), "unit": "queries/s", "cores": 1, "kind": "port",
+                            "sample": f"{len(lat)} queries over the starting {N0}-row corpus, oracle orc_query "
+                                      "(fast dot order) on one thread",
+                            "p50_us": _pct(lat, 50) * 1e6}}
+    if per:
+        rec.update({"append_p50_us": _pct(a_lat, 50) * 1e6, "append_p99_us": _pct(a_lat, 99) * 1e6,
+                    "freshness_mean": float(np.mean(fresh)),
+                    "frames_per_s_incl_append": frames / total})
+    return rec
 
 
-def run_batch(a):
-    """c2: batched queries on the tensor cores.  N = 1M rows (row-sharded over
-    the ranks), B = 1024 queries per step, K = 100, lambda = 0.01, t_q = 600,
-    importance on.  A step is one mars_query_batch_topk per rank (+ NCCL
-    all-gather of the [B][K] lists and mars_topk_merge_batch when sharded)."""
+def cfg_c2(a, env):
+    """c2: batched top-K over N = 1M rows (the headline's corpus), B = 1024
+    queries per step, K = 100, lambda = 0.01, importance on, row-sharded over
+    the ranks: one mars_shard_query_batch_topk per step and rank (the
+    library's NCCL: bound all-reduce between the rescore passes, one
+    all-gather of packed keys, merge).  Strong scaling (N fixed)."""
     import torch
     import mars_b200 as mb
+    import oracle as O
     from mars_b200 import datagen
-
-    rank, world, local = dist_env()
-    torch.cuda.set_device(local)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist_mod
-        from datetime import timedelta
-        dist = dist_mod
-        dist.init_process_group("nccl", timeout=timedelta(seconds=180),
-                                device_id=torch.device("cuda", local))
-    K, B, D = (a.k if a.k != 10 else 100), a.batch, a.dim
-    lo, hi = a.n * rank // world, a.n * (rank + 1) // world
-    E, mod, ts, imp = datagen.gaussian_rows(lo, hi, D, seed=a.seed, ts_max=a.ts_max)
-    store = mb.Store(hi - lo, D, device=local)
-    store.upload(E, mod, ts, imp)
-    del E
+    from _util import assert_ranked_equivalent
+    rank, world, local, dist = env["rank"], env["world"], env["local"], env["dist"]
+    B, K, D, N = a.batch, 100, a.dim, a.n
+    lo, hi = N * rank // world, N * (rank + 1) // world
+    E, mod, ts, imp = env["rows"]            # every row (the headline holds them all)
+    full = env["store"]
+    if world == 1:
+        st = full
+    else:
+        st = mb.Store(hi - lo, D, device=local)
+        st.upload(E[lo:hi], mod[lo:hi], ts[lo:hi], imp[lo:hi])
     bc = mb.BatchContext(hi - lo, D, max_batch=B, max_k=K, device=local)
-    ctx = mb.QueryContext(hi - lo, D, max_k=K, device=local)
-    Qh = datagen.queries(B, D, seed=a.seed + 1)
+    uid = [mb.shard_unique_id() if rank == 0 else None]
+    if dist is not None:
+        dist.broadcast_object_list(uid, src=0)
+    comm = mb.ShardComm(local, rank, world, uid[0], max_batch=B, max_k=K)
+    Qh = datagen.queries(B, D, seed=a.seed + 7)
     Qd = torch.from_numpy(Qh).cuda()
-    ids = torch.empty((B, K), dtype=torch.int32, device="cuda")
-    vals = torch.empty((B, K), dtype=torch.float32, device="cuda")
-    if world > 1:
-        gids = torch.empty((world, B, K), dtype=torch.int32, device="cuda")
-        gvals = torch.empty((world, B, K), dtype=torch.float32, device="cuda")
-        mids = torch.empty((B, K), dtype=torch.int32, device="cuda")
-        mvals = torch.empty((B, K), dtype=torch.float32, device="cuda")
-    stream = torch.cuda.ExternalStream(ctx.stream, device=torch.device("cuda", local))
-    torch.cuda.set_stream(stream)
+    stream = torch.cuda.Stream()
+    res = torch.empty(2 * B * K + B, dtype=torch.int32, device="cuda")   # ids | scores | counts
+    ids, vals, cnt = res[:B * K].view(B, K), res[B * K:2 * B * K].view(torch.float32).view(B, K), res[2 * B * K:]
 
-    def step():
-        bc.query_batch_topk(store, Qd, B, a.ts_max, a.lam, K, ids, vals, use_importance=True,
-                            row_offset=lo, stream=ctx.stream)
-        if world > 1:
-            dist.all_gather_into_tensor(gids, ids)
-            dist.all_gather_into_tensor(gvals, vals)
-            ctx.topk_merge_batch(gids, gvals, world, K, B, mids, mvals, stream=ctx.stream)
+    def step(q):
+        comm.query_batch_topk(st, bc, q, B, a.ts_max, a.lam, K, ids, vals, cnt, use_importance=True,
+                              row_offset=lo, stream=stream.cuda_stream)
 
-    for _ in range(a.warmup):
-        step()
-    torch.cuda.synchronize()
-    sampler = ClockSampler(local) if rank == 0 else None
-    if sampler:
-        sampler.start()
-        time.sleep(0.3)
-    e0 = torch.cuda.Event(enable_timing=True)
-    e1 = torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()        # after the sampler started: no rank waits inside the timed region
-    torch.cuda.synchronize()
+    for _ in range(max(3, a.warmup)):
+        step(Qd)
+    steps = max(5, min(a.steps, 20))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    _barrier(dist)
     e0.record(stream)
-    for _ in range(a.steps):
-        step()
+    for _ in range(steps):
+        step(Qd)
     e1.record(stream)
-    torch.cuda.synchronize()
-    clocks = sampler.stop() if sampler else None
-    ms = e0.elapsed_time(e1)
-    if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
+    _barrier(dist)
+    ms = _max_over_ranks(dist, e0.elapsed_time(e1) / steps)
+    comm.set_timing(True)
+    step(Qd)
+    phases = comm.last_times()
+    comm.set_timing(False)
     stats = bc.last_stats()
-    # phase breakdown (outside the timed region): batch alone, exchange alone
-    phases = {}
-    for name, fn in (("batch_ms", lambda: bc.query_batch_topk(store, Qd, B, a.ts_max, a.lam, K, ids, vals,
-                                                              use_importance=True, row_offset=lo,
-                                                              stream=ctx.stream)),
-                     ("exchange_merge_ms", (lambda: (dist.all_gather_into_tensor(gids, ids),
-                                                     dist.all_gather_into_tensor(gvals, vals),
-                                                     ctx.topk_merge_batch(gids, gvals, world, K, B, mids, mvals,
-                                                                          stream=ctx.stream)))
-                      if world > 1 else None)):
-        if fn is None:
-            continue
-        torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        for _ in range(3):
-            fn()
-        torch.cuda.synchronize()
-        phases[name] = (time.perf_counter() - t0) / 3 * 1e3
+    gemm_ms = _max_over_ranks(dist, stats["gemm_ms"])
+    phases = {k: _max_over_ranks(dist, v) for k, v in phases.items()}
+    ans = res.cpu().numpy()
+    a_ids, a_vals = ans[:B * K].reshape(B, K), ans[B * K:2 * B * K].view(np.float32).reshape(B, K)
+    valid = bool(np.all(ans[2 * B * K:] == K))
+
+    # end to end: host queries in (pinned), one packed result copy out
+    Qpin = torch.from_numpy(Qh).pin_memory()
+    qbuf = torch.empty((B, D), dtype=torch.float32, device="cuda")
+    outs = [torch.empty(2 * B * K + B, dtype=torch.int32).pin_memory() for _ in range(2)]
+    done = [torch.cuda.Event() for _ in range(2)]
+    e2e_valid = True
+    _barrier(dist)
+    t0 = time.perf_counter()
+    for s in range(steps + 1):
+        if s < steps:
+            b = s % 2
+            with torch.cuda.stream(stream):
+                qbuf.copy_(Qpin, non_blocking=True)
+            step(qbuf)
+            with torch.cuda.stream(stream):
+                outs[b].copy_(res, non_blocking=True)
+            done[b].record(stream)
+        if s > 0:
+            p = (s - 1) % 2
+            done[p].synchronize()
+            e2e_valid = e2e_valid and bool(np.all(outs[p].numpy()[2 * B * K:] == K))
+    dt = _max_over_ranks(dist, time.perf_counter() - t0)
+
+    # exactness: the merged answer equals one GPU's answer over all rows (bit
+    # for bit) and the oracle's (tie-aware) on sampled queries
+    exact_single = None
+    exact_oracle = None
+    cpu = None
     if rank == 0:
-        peaks = {}
+        bcf = mb.BatchContext(N, D, max_batch=B, max_k=K, device=local)
+        fi = torch.empty((B, K), dtype=torch.int32, device="cuda")
+        fv = torch.empty((B, K), dtype=torch.float32, device="cuda")
+        bcf.query_batch_topk(full, Qd, B, a.ts_max, a.lam, K, fi, fv, use_importance=True, stream=stream.cuda_stream)
+        torch.cuda.synchronize()
+        exact_single = bool(np.array_equal(fi.cpu().numpy(), a_ids) and
+                            np.array_equal(fv.cpu().numpy().view(np.int32), a_vals.view(np.int32)))
+        bcf.close()
+        corpus = O.Corpus(E=E, ts=ts, mod=mod, imp=imp)
+        threads = os.cpu_count() or 1
+        sample = 8
+        oi, ov = O.query_batch_topk(corpus, Qh[:4], a.ts_max, a.lam, K, use_importance=True)
         try:
-            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-        except Exception:
-            pass
-        flops = 2.0 * B * a.n * D
-        per_batch_s = ms * 1e-3 / a.steps
-        achieved = flops / per_batch_s / 1e12 / world
-        bf16 = float(peaks.get("bf16_tflops", 1590.0))
-        line = {"workload": "c2", "metric": f"queries/s (batched top-K, N={a.n}, D={D}, B={B}, K={K})",
-                "value": B * a.steps / (ms * 1e-3), "unit": "queries/s", "n_gpus": world,
-                "steps": a.steps, "ms_per_step": ms / a.steps, "scaling": "strong",
-                "roofline": {"bound": "tensor", "achieved": achieved, "unit": "TFLOP/s per GPU",
-                             "operands": {2: "fp16 (kind::f16)", 1: "tf32 (kind::tf32)"}.get(
-                                 stats.get("path"), "scan"),
-                             # fp16 runs at the bf16 rate; TF32 at half of it
-                             "peak": bf16 if stats.get("path") == 2 else bf16 / 2,
-                             "peak_kind": ("measured bf16 GEMM" if "bf16_tflops" in peaks else "fallback")
-                                          + (" (same rate as fp16)" if stats.get("path") == 2 else " / 2 (TF32)"),
-                             "frac": achieved / (bf16 if stats.get("path") == 2 else bf16 / 2),
-                             "flops_per_batch": flops},
-                "batch_stats_rank0": stats, "phases_rank0_wall": phases, "clocks": clocks}
-        print(json.dumps(line), flush=True)
+            for q in range(4):
+                assert_ranked_equivalent(a_ids[q], a_vals[q], oi[q], ov[q], what=f"c2 query {q}")
+            exact_oracle = True
+        except AssertionError:
+            exact_oracle = False
+        if world == 1:
+            t1 = time.perf_counter()
+            for q in range(sample):
+                O.scan_topk_fast(corpus, Qh[q], a.ts_max, a.lam, K, use_importance=True, n_threads=threads)
+            cdt = time.perf_counter() - t1
+            cpu = {"value": sample / cdt, "unit": "queries/s", "cores": threads, "kind": "port",
+                   "sample": f"{sample} of the {B} queries, each scanning all {N} rows (K = {K}), "
+                             f"oracle orc_scan_topk_fast with {threads} OpenMP threads; queries/s of the "
+                             f"sample stands for the batch ({B // sample}x the sample's work)"}
+    exact_all = _all_true(dist, valid and (exact_single is not False))
+    sus, burst, kind = _tensor_peaks()
+    achieved = 2.0 * B * (hi - lo) * D / (gemm_ms * 1e-3) / 1e12
+    comm.close()
+    del bc
     if world > 1:
-        dist.barrier()
-        dist.destroy_process_group()
-
-
-def _init_dist(local, world):
-    """NCCL process group for torchrun launches (None on one GPU)."""
-    if world <= 1:
+        st.close()
+    if rank != 0:
         return None
-    import torch
-    import torch.distributed as dist
-    from datetime import timedelta
-    dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=torch.device("cuda", local))
-    return dist
+    return {"workload": "c2", "metric": f"queries/s (batched exact top-K, N={N}, D={D}, B={B}, K={K})",
+            "value": B / (ms * 1e-3), "unit": "queries/s", "n_gpus": world, "steps": steps,
+            "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+            "parallelism": (f"rows sharded x{world}: mars_shard_query_batch_topk (NCCL bound all-reduce + "
+                            f"one all-gather of packed keys + merge, inside the library)" if world > 1
+                            else "one GPU (mars_shard_query_batch_topk, world 1)"),
+            "phases_ms_max_over_ranks": phases,
+            "exact_vs_single_gpu": exact_single, "exact_vs_oracle": exact_oracle,
+            "oracle_checked_queries": 4, "all_results_valid": exact_all,
+            "e2e": {"value": steps * B / dt, "unit": "queries/s", "h2d_bytes_per_step": B * D * 4,
+                    "d2h_bytes_per_step": (2 * B * K + B) * 4, "every_step_valid": e2e_valid,
+                    "path": "pinned H2D of the batch, mars_shard_query_batch_topk, one packed D2H of ids, "
+                            "scores and counts; the host checks each step's counts while the next runs"},
+            "roofline": {"bound": "tensor", "kernel": "batch::gemm_kernel<kCandidates, fp16> (128 queries x "
+                                                      "256 rows per tcgen05 tile)",
+                         "kernel_ms": gemm_ms, "achieved": achieved, "unit": "TFLOP/s",
+                         "peak": sus, "frac": achieved / sus, "peak_kind": f"{kind} bf16 GEMM, sustained",
+                         "frac_of_burst": achieved / burst,
+                         "flops_per_launch": 2.0 * B * (hi - lo) * D,
+                         "step_tflops_per_gpu": 2.0 * B * N * D / world / (ms * 1e-3) / 1e12},
+            "batch_stats_rank0": stats, "cpu_baseline": cpu}
 
 
 def _sharded_graph(mb, st, N, deg, deg_cross, n_mod, rank, world, dist):
@@ -770,10 +895,7 @@ def _sharded_graph(mb, st, N, deg, deg_cross, n_mod, rank, world, dist):
     lo, hi = N * rank // world, N * (rank + 1) // world
     rows_max = (N + world - 1) // world
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.synchronize()
-    if dist is not None:
-        dist.barrier()
-        torch.cuda.synchronize()
+    _barrier(dist)
     e0.record()
     if world == 1:
         nb = torch.empty((N, deg), dtype=torch.int32, device="cuda")
@@ -787,15 +909,10 @@ def _sharded_graph(mb, st, N, deg, deg_cross, n_mod, rank, world, dist):
                         for r in range(world)])
     e1.record()
     torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1)
-    if dist is not None:
-        t = torch.tensor([ms], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    return nb, ms
+    return nb, _max_over_ranks(dist, e0.elapsed_time(e1))
 
 
-def run_knn_build(a):
+def cfg_c3(a, env):
     """c3: cmng_build of an exact out-degree-32 kNN graph.  N = 100,000 rows
     (100 isotropic Gaussian clusters, centres N(0,1), sigma 0.3, normalised),
     degree 32, no bridges.  A step is one full build (tensor-core kNN with
@@ -806,109 +923,68 @@ def run_knn_build(a):
     import mars_b200 as mb
     import oracle as O
     from mars_b200 import datagen
-
-    rank, world, local = dist_env()
-    N = a.n if a.n != 1_000_000 else 100_000
-    D, deg = a.dim, 32
+    rank, world, local, dist = env["rank"], env["world"], env["local"], env["dist"]
+    N, D, deg = 100_000, a.dim, 32
     E, mod, ts, _ = datagen.cluster_corpus(N, D, 100, 0.3, seed=a.seed, n_mod=4, ts_max=10.0)
-    if a.impl == "reference":
-        if rank != 0:
-            return
-        c = O.Corpus(E=E, ts=ts, mod=mod)
-        rows = np.arange(0, N, max(1, N // 200), dtype=np.int32)
-        t0 = time.perf_counter()
-        O.knn(c, rows, 2 * deg, dot_order=O.DOT_FAST)
-        dt = time.perf_counter() - t0
-        full = dt * N / rows.shape[0]
-        print(json.dumps({"impl": "reference", "workload": "c3", "metric": "cmng_build ms", "value": full * 1e3,
-                          "unit": "ms", "higher_is_better": False,
-                          "cpu_baseline": {"value": full * 1e3, "unit": "ms", "cores": os.cpu_count(),
-                                           "kind": "port", "sample": f"exact kNN of {rows.shape[0]} rows "
-                                           f"against all {N}, extrapolated x{N / rows.shape[0]:.0f}"}}))
-        return
-    torch.cuda.set_device(local)
-    dist = _init_dist(local, world)
     st = mb.Store(N, D, device=local)
     st.upload(E, mod, ts)
-    for _ in range(max(1, a.warmup)):
-        nb, _ = _sharded_graph(mb, st, N, deg, 0, 4, rank, world, dist)
+    nb, _ = _sharded_graph(mb, st, N, deg, 0, 4, rank, world, dist)
     times = []
-    for _ in range(a.steps):
+    for _ in range(3):
         nb, ms = _sharded_graph(mb, st, N, deg, 0, 4, rank, world, dist)
         times.append(ms)
+    rec = None
     if rank == 0:
-        # spot check of the gathered graph against the exact oracle kNN
-        rows = np.arange(0, N, N // 64, dtype=np.int32)
-        rid, _ = O.knn(O.Corpus(E=E, ts=ts, mod=mod), rows, 2 * deg)
+        # bit-exact check of sampled rows against the oracle's exact kNN
+        rows = np.arange(0, N, N // 128, dtype=np.int32)
+        c = O.Corpus(E=E, ts=ts, mod=mod)
+        rid, _ = O.knn(c, rows, 2 * deg)
         ref = O.cmng_select(rid, mod, rows, deg, 0, 4)
         exact = bool(np.array_equal(nb.cpu().numpy()[rows], ref))
+        threads = os.cpu_count() or 1
+        crow = np.arange(0, N, N // 256, dtype=np.int32)
+        t0 = time.perf_counter()
+        O.knn(c, crow, 2 * deg, dot_order=O.DOT_FAST, n_threads=threads)
+        cdt = (time.perf_counter() - t0) * N / crow.shape[0]
         ms = statistics.median(times)
         flops = 2.0 * N * N * D
-        peaks = {}
-        try:
-            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-        except Exception:
-            pass
-        bf16 = float(peaks.get("bf16_tflops", 1590.0))
-        print(json.dumps({"workload": "c3", "metric": f"cmng_build ms (N={N}, D={D}, degree {deg})",
-                          "value": ms, "unit": "ms", "higher_is_better": False, "n_gpus": world,
-                          "steps": a.steps, "scaling": "strong",
-                          "parallelism": f"row blocks x{world}" + (" + NCCL all-gather" if world > 1 else ""),
-                          "tflops_effective": flops / (ms * 1e-3) / 1e12,
-                          "roofline": {"bound": "tensor", "flops_per_build": flops,
-                                       "frac_of_tf32_nominal_per_gpu":
-                                           flops / world / (ms * 1e-3) / 1e12 / (bf16 / 2)},
-                          "spot_check_rows": int(rows.shape[0]), "neighbours_bit_exact": exact}),
-              flush=True)
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+        sus, burst, kind = _tensor_peaks()
+        ach = flops / world / (ms * 1e-3) / 1e12
+        rec = {"workload": "c3", "metric": f"cmng_build ms (N={N}, D={D}, degree {deg})", "value": ms, "unit": "ms",
+               "higher_is_better": False, "n_gpus": world, "steps": len(times), "scaling": "strong",
+               "parallelism": f"row blocks x{world}" + (" + NCCL all-gather" if world > 1 else ""),
+               "tflops_effective": flops / (ms * 1e-3) / 1e12,
+               "roofline": {"bound": "tensor", "flops_per_build": flops, "achieved_per_gpu": ach, "unit": "TFLOP/s",
+                            "peak": sus, "frac": ach / sus, "peak_kind": f"{kind} bf16 GEMM, sustained",
+                            "frac_of_burst": ach / burst},
+               "oracle_checked_rows": int(rows.shape[0]), "neighbours_bit_exact": exact,
+               "cpu_baseline": {"value": cdt * 1e3, "unit": "ms", "cores": threads, "kind": "port",
+                                "sample": f"exact kNN of {crow.shape[0]} rows against all {N} (oracle orc_knn, fast "
+                                          f"dot order, {threads} threads), extrapolated x{N // crow.shape[0]}"}}
+    st.close()
+    return rec
 
 
-def run_cmng_bfs(a):
+def cfg_c4(a, env):
     """c4: cmng_search + cross-modal BFS.  N = 1,000,000 rows from a 1,000
     cluster mixture (sigma 0.3, 4 modalities, normalised); graph = degree-32
-    kNN + 4 cross-modal bridges (degree 36, built once, untimed); 10,000
-    queries, beam 64, K = 10, lambda = 0.05, BFS depth 2.  Under torchrun:
-    replicas (every rank holds the corpus; the graph is built by row blocks
-    and all-gathered), the queries split across ranks, and an NCCL
-    all-gather of the per-rank results ends each step."""
+    kNN + 4 cross-modal bridges (degree 36, built by row blocks, untimed);
+    10,000 queries, beam 64, K = 10, lambda = 0.05, BFS depth 2.  Under
+    torchrun: replicas (every rank holds the corpus and the graph), the
+    queries split across ranks, an NCCL all-gather of the per-rank results
+    ends each step."""
     import torch
     import mars_b200 as mb
     import oracle as O
     from mars_b200 import datagen
-
-    rank, world, local = dist_env()
-    N, D, deg, K, nq = a.n, a.dim, 36, 10, a.queries
-    if a.impl == "reference" and rank != 0:
-        return
-    torch.cuda.set_device(local)
+    from _util import assert_ranked_equivalent
+    rank, world, local, dist = env["rank"], env["world"], env["local"], env["dist"]
+    N, D, deg, K, nq = a.c4_n, a.dim, 36, 10, a.queries
     E, mod, ts, _ = datagen.cluster_corpus(N, D, 1000, 0.3, seed=a.seed, n_mod=4, ts_max=10.0)
     Q = datagen.queries(nq, D, seed=a.seed + 5)
-    dist = _init_dist(local, world) if a.impl != "reference" else None
     st = mb.Store(N, D, device=local)
     st.upload(E, mod, ts)
-    if a.impl == "reference":   # rank 0 alone: the graph is built locally
-        nb, build_ms = _sharded_graph(mb, st, N, deg, 4, 4, 0, 1, None)
-    else:
-        nb, build_ms = _sharded_graph(mb, st, N, deg, 4, 4, rank, world, dist)
-    if a.impl == "reference":
-        nbh = nb.cpu().numpy()
-        c = O.Corpus(E=E, ts=ts, mod=mod, fixed_nbrs=nbh)
-        sample = min(nq, 50)
-        t0 = time.perf_counter()
-        for q in range(sample):
-            res, _ = O.cmng_search(c, nbh, Q[q], 10.0, K=K, beam_width=64, max_iterations=64, lam=0.05,
-                                   dot_order=O.DOT_FAST)
-            O.bfs(c, res["node_id"], res["score"], None, 2, 0.5, q=Q[q], t_q=10.0, lam=0.05,
-                  dot_order=O.DOT_FAST)
-        dt = time.perf_counter() - t0
-        v = sample / dt
-        print(json.dumps({"impl": "reference", "workload": "c4", "metric": "queries/s", "value": v,
-                          "unit": "queries/s",
-                          "cpu_baseline": {"value": v, "unit": "queries/s", "cores": 1, "kind": "port",
-                                           "sample": f"{sample} queries, oracle beam search + BFS, 1 thread"}}))
-        return
+    nb, build_ms = _sharded_graph(mb, st, N, deg, 4, 4, rank, world, dist)
     q0, q1 = nq * rank // world, nq * (rank + 1) // world
     nql = q1 - q0
     qmax = (nq + world - 1) // world
@@ -917,79 +993,210 @@ def run_cmng_bfs(a):
     ctx = mb.CmngContext(qmax, K, deg, 2, N, device=local)
     ids = torch.full((qmax, K), -1, dtype=torch.int32, device="cuda")
     sc = torch.zeros((qmax, K), dtype=torch.float32, device="cuda")
+    hp = torch.zeros((qmax, K), dtype=torch.int32, device="cuda")
     cnt = torch.zeros(qmax, dtype=torch.int32, device="cuda")
     vis = torch.zeros(qmax, dtype=torch.int32, device="cuda")
-    bits = torch.zeros(qmax, dtype=torch.int32, device="cuda")
-    bscored = torch.zeros(qmax, dtype=torch.int32, device="cuda")
+    iters = torch.zeros(qmax, dtype=torch.int32, device="cuda")
+    scored = torch.zeros(qmax, dtype=torch.int32, device="cuda")
+    bids = torch.zeros((qmax, K), dtype=torch.int32, device="cuda")     # beam-only outputs
+    bsc = torch.zeros((qmax, K), dtype=torch.float32, device="cuda")
+    bcnt = torch.zeros(qmax, dtype=torch.int32, device="cuda")
     if world > 1:
         all_ids = torch.empty((world * qmax, K), dtype=torch.int32, device="cuda")
         all_sc = torch.empty((world * qmax, K), dtype=torch.float32, device="cuda")
-    stream = torch.cuda.Stream()       # a real stream: NULL would mean the store's own stream
-    torch.cuda.set_stream(stream)
+    stream = torch.cuda.Stream()
 
     def step():
-        ctx.search_bfs(st, nb, deg, Qd, nql, 10.0, cfg, 2, 0.5, ids, sc, cnt, d_visited=vis,
+        ctx.search_bfs(st, nb, deg, Qd, nql, 10.0, cfg, 2, 0.5, ids, sc, cnt, d_hops=hp, d_visited=vis,
                        stream=stream.cuda_stream)
         if world > 1:
-            dist.all_gather_into_tensor(all_ids, ids)
-            dist.all_gather_into_tensor(all_sc, sc)
+            with torch.cuda.stream(stream):
+                dist.all_gather_into_tensor(all_ids, ids)
+                dist.all_gather_into_tensor(all_sc, sc)
 
-    for _ in range(max(1, a.warmup)):
-        step()
+    step()
+    steps = 3
     e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
-    torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-        torch.cuda.synchronize()
+    _barrier(dist)
     e0.record(stream)
-    for _ in range(a.steps):
+    for _ in range(steps):
         step()
     e1.record(stream)
-    for _ in range(a.steps):
-        mb.cmng_search_batch(st, nb, deg, Qd, nql, 10.0, cfg, ids, sc, cnt, d_iters=bits,
-                             d_scored=bscored, stream=stream.cuda_stream)
+    for _ in range(steps):
+        mb.cmng_search_batch(st, nb, deg, Qd, nql, 10.0, cfg, bids, bsc, bcnt, d_iters=iters, d_scored=scored,
+                             stream=stream.cuda_stream)
     e2.record(stream)
-    torch.cuda.synchronize()
-    ms = e0.elapsed_time(e1) / a.steps
-    ms_beam = e1.elapsed_time(e2) / a.steps
-    if world > 1:
-        t = torch.tensor([ms, ms_beam], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms, ms_beam = float(t[0].item()), float(t[1].item())
+    _barrier(dist)
+    ms = _max_over_ranks(dist, e0.elapsed_time(e1) / steps)
+    ms_beam = _max_over_ranks(dist, e1.elapsed_time(e2) / steps)
     rows_bfs = float(vis[:nql].double().mean().item())
-    rows_beam = float(bscored[:nql].double().mean().item())
-    # rows read per query: beam-scored rows + the BFS levels >= 1 (seeds are beam rows)
+    rows_beam = float(scored[:nql].double().mean().item())
     bytes_q = (rows_beam + rows_bfs) * D * 4
-    peak, _ = measured_peak()
-    achieved = bytes_q * nql / (ms * 1e-3) / 1e9
+    rec = None
     if rank == 0:
-        print(json.dumps({"workload": "c4", "metric": f"queries/s (cmng_search + BFS depth 2, N={N}, K={K})",
-                          "value": nq / (ms * 1e-3), "unit": "queries/s", "n_gpus": world,
-                          "scaling": "strong", "ms_per_batch": ms,
-                          "parallelism": f"replicas x{world}, queries split" +
-                                         (" + NCCL all-gather of results" if world > 1 else ""),
-                          "beam_only_queries_per_s": nq / (ms_beam * 1e-3), "graph_build_ms": build_ms,
-                          "mean_rows_scored_beam": rows_beam, "mean_nodes_visited_bfs": rows_bfs,
-                          "mean_iterations": float(bits[:nql].double().mean().item()),
-                          "roofline": {"bound": "hbm", "achieved_per_gpu": achieved, "peak": peak,
-                                       "unit": "GB/s", "frac": achieved / peak,
-                                       "note": "row gathers: (beam-scored + BFS-visited rows) x D x 4 bytes"}}),
-              flush=True)
-    if world > 1:
+        nbh = nb.cpu().numpy()
+        oc = O.Corpus(E=E, ts=ts, mod=mod, fixed_nbrs=nbh)
+        gi, gs, gh, gc = ids.cpu().numpy(), sc.cpu().numpy(), hp.cpu().numpy(), cnt.cpu().numpy()
+        exact = True
+        n_check = 8
+        for q in range(n_check):
+            beam, _ = O.cmng_search(oc, nbh, Q[q0 + q], 10.0, K=K, beam_width=64, max_iterations=64, lam=0.05)
+            visited = O.bfs(oc, beam["node_id"], beam["score"], None, 2, 0.5, q=Q[q0 + q], t_q=10.0, lam=0.05)
+            ref = O.finalize(visited, K)
+            n = int(gc[q])
+            try:
+                assert n == ref.shape[0]
+                assert_ranked_equivalent(gi[q, :n], gs[q, :n], ref["node_id"], ref["score"], gh[q, :n], ref["hops"],
+                                         rtol=2e-6, what=f"c4 query {q}")
+            except AssertionError:
+                exact = False
+        sample = 16
+        t0 = time.perf_counter()
+        for q in range(sample):
+            beam, _ = O.cmng_search(oc, nbh, Q[q], 10.0, K=K, beam_width=64, max_iterations=64, lam=0.05,
+                                    dot_order=O.DOT_FAST)
+            O.bfs(oc, beam["node_id"], beam["score"], None, 2, 0.5, q=Q[q], t_q=10.0, lam=0.05, dot_order=O.DOT_FAST)
+        cdt = time.perf_counter() - t0
+        peak, peak_kind = measured_peak()
+        achieved = bytes_q * nql / (ms * 1e-3) / 1e9
+        rec = {"workload": "c4", "metric": f"queries/s (cmng_search + BFS depth 2, N={N}, K={K})",
+               "value": nq / (ms * 1e-3), "unit": "queries/s", "n_gpus": world, "steps": steps, "scaling": "strong",
+               "ms_per_batch": ms, "queries_per_batch": nq,
+               "parallelism": f"replicas x{world}, queries split" + (" + NCCL all-gather of results" if world > 1 else ""),
+               "beam_only_queries_per_s": nq / (ms_beam * 1e-3), "graph_build_ms": build_ms,
+               "mean_rows_scored_beam": rows_beam, "mean_nodes_visited_bfs": rows_bfs,
+               "oracle_checked_queries": n_check, "exact_vs_oracle": exact,
+               "roofline": {"bound": "hbm", "achieved_per_gpu": achieved, "peak": peak, "unit": "GB/s",
+                            "frac": achieved / peak, "peak_kind": peak_kind,
+                            "bytes_per_query": bytes_q,
+                            "note": "measured row gathers per query: (beam-scored + BFS-visited rows) x D x 4 bytes"},
+               "cpu_baseline": {"value": sample / cdt, "unit": "queries/s", "cores": 1, "kind": "port",
+                                "sample": f"{sample} queries, oracle beam search + BFS (fast dot order), one thread, "
+                                          "on the same graph"}}
+    st.close()
+    return rec
+
+
+def run_configs(a, env):
+    """Every config of the family, in the same order on every rank."""
+    out = {}
+    import gc
+    for name, fn in (("c2", cfg_c2), ("c3", cfg_c3), ("c4", cfg_c4)):
+        if name in a.skip_configs:
+            continue
+        t0 = time.perf_counter()
+        rec = fn(a, env)
+        gc.collect()
+        if rec is not None:
+            rec["setup_and_run_s"] = time.perf_counter() - t0
+            out[name] = rec
+    if env["world"] == 1:
+        for name in ("c0", "c1"):
+            if name in a.skip_configs:
+                continue
+            t0 = time.perf_counter()
+            out[name] = cfg_latency(a, name)
+            out[name]["setup_and_run_s"] = time.perf_counter() - t0
+    return out
+
+
+def run_workload(a):
+    """`--workload cX`: one config's record as its own JSON line."""
+    import torch
+    rank, world, local = dist_env()
+    if a.workload in ("c0", "c1"):
+        if rank == 0:
+            print(json.dumps(cfg_latency(a, a.workload)), flush=True)
+        return
+    torch.cuda.set_device(local)
+    dist = _init_dist(local, world)
+    env = {"rank": rank, "world": world, "local": local, "dist": dist}
+    if a.workload == "c2":
+        import mars_b200 as mb
+        from mars_b200 import datagen
+        E, mod, ts, imp = datagen.gaussian_rows(0, a.n, a.dim, seed=a.seed, ts_max=a.ts_max)
+        st = mb.Store(a.n, a.dim, device=local)
+        st.upload(E, mod, ts, imp)
+        env.update({"rows": (E, mod, ts, imp), "store": st})
+        rec = cfg_c2(a, env)
+    elif a.workload == "c3":
+        rec = cfg_c3(a, env)
+    else:
+        rec = cfg_c4(a, env)
+    if rank == 0:
+        print(json.dumps(rec), flush=True)
+    if dist is not None:
         dist.barrier()
         dist.destroy_process_group()
 
 
+def run_reference_workload(a):
+    """`--impl reference --workload cX`: the CPU implementation of config X
+    (the oracle port) on the host cores, rank 0 only."""
+    rank, _, _ = dist_env()
+    if rank != 0:
+        return
+    import oracle as O
+    from mars_b200 import datagen
+    if a.workload in ("c0", "c1"):
+        D, K = a.dim, 10
+        N0, lam = (2400, 0.5) if a.workload == "c0" else (10000, 1.0)
+        E, mod, ts, imp = datagen.gaussian_corpus(N0, D, seed=a.seed, n_mod=4, ts_max=10.0)
+        ro, ci = datagen.random_bridges(mod, 4, seed=7)
+        Q = datagen.queries(256, D, seed=0x5EED0000)
+        oc = O.Corpus(E=E, ts=ts, mod=mod, row_offsets=ro, col_indices=ci)
+        lat = []
+        for f in range(min(a.frames, 200)):
+            t0 = time.perf_counter()
+            O.query(oc, Q[f % 256], 10.0, top_k=K, bfs_max_hops=1, lam=lam, bfs_score_decay=0.5,
+                    dot_order=O.DOT_FAST)
+            lat.append(time.perf_counter() - t0)
+        v = len(lat) / sum(lat)
+        rec = {"impl": "reference", "workload": a.workload, "metric": "queries/s", "value": v, "unit": "queries/s",
+               "p50_us": _pct(lat, 50) * 1e6, "p99_us": _pct(lat, 99) * 1e6,
+               "cpu_baseline": {"value": v, "unit": "queries/s", "cores": 1, "kind": "port",
+                                "sample": f"{len(lat)} queries, oracle orc_query single thread (corpus fixed)"}}
+    elif a.workload == "c3":
+        N, deg = 100_000, 32
+        E, mod, ts, _ = datagen.cluster_corpus(N, a.dim, 100, 0.3, seed=a.seed, n_mod=4, ts_max=10.0)
+        c = O.Corpus(E=E, ts=ts, mod=mod)
+        rows = np.arange(0, N, max(1, N // 200), dtype=np.int32)
+        t0 = time.perf_counter()
+        O.knn(c, rows, 2 * deg, dot_order=O.DOT_FAST)
+        full = (time.perf_counter() - t0) * N / rows.shape[0]
+        rec = {"impl": "reference", "workload": "c3", "metric": "cmng_build ms", "value": full * 1e3, "unit": "ms",
+               "higher_is_better": False,
+               "cpu_baseline": {"value": full * 1e3, "unit": "ms", "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"exact kNN of {rows.shape[0]} rows against all {N}, extrapolated "
+                                          f"x{N / rows.shape[0]:.0f}"}}
+    elif a.workload == "c2":
+        B, K = a.batch, 100
+        E, mod, ts, imp = datagen.gaussian_rows(0, a.n, a.dim, seed=a.seed, ts_max=a.ts_max)
+        c = O.Corpus(E=E, ts=ts, mod=mod, imp=imp)
+        Qh = datagen.queries(B, a.dim, seed=a.seed + 7)
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        for q in range(8):
+            O.scan_topk_fast(c, Qh[q], a.ts_max, a.lam, K, use_importance=True, n_threads=threads)
+        v = 8 / (time.perf_counter() - t0)
+        rec = {"impl": "reference", "workload": "c2", "metric": "queries/s", "value": v, "unit": "queries/s",
+               "cpu_baseline": {"value": v, "unit": "queries/s", "cores": threads, "kind": "port",
+                                "sample": f"8 of the {B} queries over all {a.n} rows, K = {K}"}}
+    else:
+        print(json.dumps({"impl": "reference", "workload": a.workload,
+                          "unavailable": "the c4 reference arm runs inside the GPU run (it needs the GPU-built graph)"}))
+        return
+    print(json.dumps(rec), flush=True)
+
+
 def main():
     a = parse_args()
-    if a.workload == "c3":
-        run_knn_build(a)
-    elif a.workload == "c4":
-        run_cmng_bfs(a)
-    elif a.workload == "c2":
-        run_batch(a)
-    elif a.workload in ("c0", "c1"):
-        run_latency(a)
+    a.skip_configs = set(x for x in a.skip_configs.split(",") if x) if isinstance(a.skip_configs, str) else set()
+    if a.workload != "scan":
+        if a.impl == "reference":
+            run_reference_workload(a)
+        else:
+            run_workload(a)
     elif a.impl == "reference":
         run_reference(a)
     else:
