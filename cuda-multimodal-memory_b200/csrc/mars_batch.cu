@@ -72,7 +72,15 @@ constexpr int kJ = 16;                // sampled lower bounds kept per (query, t
 // values are exact in fp32), plus the accumulation over at most 64 16-wide
 // steps, far below the remaining 6e-4.
 constexpr float kMarginRel = 2.6e-3f;
-constexpr float kMarginRelF16 = 1.6e-3f;
+// fp16 operands: the rounding of both copies is bounded exactly instead
+// (|q.e - q16.e16| <= ||q|| ||e - e16|| + ||q - q16|| ||e16||, Cauchy-Schwarz,
+// with ||e - e16|| the store's largest measured row error and ||q - q16||
+// measured per query); this term, times ||q|| max||e||, covers the rest: the
+// fp32 accumulation inside and across the tensor-core steps (D / 16 <= 64
+// steps; fp32 accumulation errs by ~2^-23 of the running magnitude per
+// step, so the budget holds ~2^-19 per step) and the canonical fp32 dot's
+// own rounding (<= (D / 32 + 5) 2^-24).
+constexpr float kAccRelF16 = 2.0e-4f;
 
 enum Mode { kSample = 0, kCandidates = 1, kFused = 2 };
 
@@ -260,7 +268,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                 sm100::tmem_ld_wait();
                 if (!qv) continue;
                 const int rbase = row0 + c * 32;
-                if (MODE == kCandidates) {
+                if constexpr (MODE == kCandidates) {
                     // which of the 32 rows pass; one atomic per chunk for all
                     // of them (clustered data can make a query's candidates
                     // dense in a few tiles), then the writes
@@ -286,8 +294,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                             }
                         }
                     }
-                    continue;
-                }
+                } else {
 #pragma unroll
                 for (int j4 = 0; j4 < 8; ++j4) {
                     const float4 w4 = reinterpret_cast<const float4*>(s_w + c * 32)[j4];
@@ -307,6 +314,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                             }
                         }
                     }
+                }
                 }
             }
             sm100::tc_fence_before();
@@ -341,7 +349,7 @@ __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch,
     if (warp >= B) return;
     const float4* q = reinterpret_cast<const float4*>(Q + (int64_t)warp * qpitch);
     __half2* h = q16 != nullptr ? reinterpret_cast<__half2*>(q16 + (int64_t)warp * pitch16) : nullptr;
-    float s = 0.f;
+    float s = 0.f, dq2 = 0.f;    // ||q||^2 and ||q - fp16(q)||^2
     bool out = false;
     for (int c = lane; c < nc; c += 32) {
         const float4 v = q[c];
@@ -349,26 +357,37 @@ __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch,
         out = out || !(fabsf(v.x) <= kF16Max) || !(fabsf(v.y) <= kF16Max) || !(fabsf(v.z) <= kF16Max) ||
               !(fabsf(v.w) <= kF16Max);
         if (h != nullptr) {
-            h[2 * c] = __floats2half2_rn(v.x, v.y);
-            h[2 * c + 1] = __floats2half2_rn(v.z, v.w);
+            const __half2 a = __floats2half2_rn(v.x, v.y), b = __floats2half2_rn(v.z, v.w);
+            h[2 * c] = a;
+            h[2 * c + 1] = b;
+            const float ex = v.x - __low2float(a), ey = v.y - __high2float(a);   // exact differences
+            const float ez = v.z - __low2float(b), ew = v.w - __high2float(b);
+            dq2 = fmaf(ex, ex, fmaf(ey, ey, fmaf(ez, ez, fmaf(ew, ew, dq2))));
         }
     }
     if (h != nullptr)
         for (int p = 2 * nc + lane; p < pitch16 / 2; p += 32) h[p] = __floats2half2_rn(0.0f, 0.0f);
     s = warp_butterfly_sum(s);
+    dq2 = warp_butterfly_sum(dq2);
     out = __any_sync(0xffffffffu, out);
     if (lane == 0) {
         bad[warp] = out ? 1 : 0;
         rescored[warp] = 0;
         if (warp == 0) { err[0] = 0; err[1] = 0; }   // the pipeline's and the arrival wait's words
         // 1.0001: covers the fp32 rounding of this norm itself
-        const float qn = sqrtf(s) * 1.0001f, en = __uint_as_float(*norm_bits);
-        float mg = (f16 ? kMarginRelF16 : kMarginRel) * qn * en;
-        // fp16 operands: components below the normal range are rounded to a
-        // multiple of 2^-24, an absolute error of at most 2^-25 each; over D
-        // <= 4 nc components the dot changes by at most
-        // 2^-25 (||q||_1 + ||e||_1 + ...) <= 2^-24 sqrt(4 nc) (||q|| + ||e||)
-        if (f16) mg += 5.9604645e-8f * sqrtf(4.0f * nc) * (qn + en) * 1.0001f;
+        const float qn = sqrtf(s) * 1.0001f, en = __uint_as_float(norm_bits[0]);
+        float mg;
+        if (f16) {
+            // measured rounding: the rows' largest ||e - e16|| (norm_bits[1])
+            // and this query's ||q - q16||; ||e16|| <= ||e|| + ||e - e16||.
+            // Components below the fp16 normal range are included: the
+            // differences are taken from the converted values themselves.
+            const float err = __uint_as_float(norm_bits[1]);
+            const float dq = sqrtf(dq2) * 1.001f;
+            mg = (qn * err + dq * (en + err) + kAccRelF16 * qn * en) * 1.001f;
+        } else {
+            mg = kMarginRel * qn * en;
+        }
         margin[warp] = mg;
         cand_cnt[warp] = 0;
     }

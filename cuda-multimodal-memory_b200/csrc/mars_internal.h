@@ -134,8 +134,10 @@ struct mars_store {
     cudaStream_t stream = nullptr;
     cudaEvent_t written = nullptr;  // last write to the store
 
-    // largest row norm, as the bits of a non-negative float (bounds the
-    // error of the tensor-core short list; kernels read it on the device)
+    // [0]: the largest row norm; [1]: the largest fp16 rounding error
+    // ||e - fp16(e)|| of a row of the fp16 copy; both as the bits of
+    // non-negative floats (they bound the error of the tensor-core short
+    // list; kernels read them on the device)
     unsigned int* d_norm_bits = nullptr;
 
     // raw view of a caller-owned DeviceMemoryGraph (compat layer)

@@ -32,6 +32,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstddef>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -44,6 +45,7 @@
 #include "mars_nccl.h"
 #include "mars_scan_body.cuh"
 #include "mars_select.cuh"
+#include "mars_shard_internal.h"
 
 namespace mars {
 
@@ -137,6 +139,46 @@ __global__ void __launch_bounds__(kThreads) merge_keys_kernel(const unsigned lon
     if (threadIdx.x == 0 && cnt_out != nullptr) cnt_out[qi] = cnt;
 }
 
+// Merge for the sharded query's seeds: as merge_keys_kernel, but a rank
+// that failed sends all-ones keys (kFailedKey, never a rank key of a
+// finite score); any such key marks the merge failed (count -1).
+constexpr unsigned long long kFailedKey = ~0ull;
+__global__ void __launch_bounds__(kThreads) merge_keys_flagged_kernel(const unsigned long long* __restrict__ keys,
+                                                                      int world, int K, int B,
+                                                                      int32_t* __restrict__ ids_out,
+                                                                      float* __restrict__ vals_out,
+                                                                      int32_t* __restrict__ cnt_out) {
+    __shared__ unsigned long long s_keys[kMergeKeys];
+    __shared__ int s_hist[2048];
+    __shared__ int s_misc[16];
+    __shared__ int s_failed;
+    const int qi = blockIdx.x;
+    const int total = world * K;
+    if (threadIdx.x == 0) { s_misc[15] = 0; s_failed = 0; }
+    __syncthreads();
+    for (int j0 = 0; j0 < total; j0 += kThreads) {
+        const int j = j0 + threadIdx.x;
+        unsigned long long k = 0ull;
+        if (j < total) {
+            const int r = j / K, e = j - r * K;
+            k = __ldg(keys + ((int64_t)r * B + qi) * K + e);
+            if (k == kFailedKey) { s_failed = 1; k = 0ull; }
+        }
+        warp_append(k != 0ull, k, s_keys, &s_misc[15], kMergeKeys);
+    }
+    __syncthreads();
+    const int M = s_misc[15];
+    const bool failed = s_failed != 0;
+    __syncthreads();
+    const int cnt = failed ? 0 : block_select_topk<kThreads>(s_keys, M, K, s_hist, s_misc);
+    for (int p = threadIdx.x; p < K; p += kThreads) {
+        const bool valid = p < cnt;
+        vals_out[(int64_t)qi * K + p] = valid ? key_score(s_keys[p]) : -INFINITY;
+        ids_out[(int64_t)qi * K + p] = valid ? key_id(s_keys[p]) : -1;
+    }
+    if (threadIdx.x == 0 && cnt_out != nullptr) cnt_out[qi] = failed ? -1 : cnt;
+}
+
 // A shard whose call ended before its exchange: bounds -inf, flag = failed.
 __global__ void neutral_bounds_kernel(float* p, int n, float failed) {
     const int i = blockIdx.x * blockDim.x + threadIdx.x;
@@ -163,6 +205,7 @@ struct mars_shard_comm {
     const float* last_bound = nullptr;      // the exchanged array of the current call
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};   // local / exchange / merge boundaries
     bool timed = false;
+    void* bfs_state = nullptr;              // mars_shard_query's scratch (made on first use)
 };
 
 namespace {
@@ -183,6 +226,56 @@ int exchange_bounds(void* arg, float* d_bound, int32_t B, cudaStream_t st) {
 }
 
 }  // namespace
+
+int mars::shard_comm_view(mars_shard_comm* c, ShardCommView* v) {
+    if (c == nullptr || c->comm == nullptr) return fail(MARS_ERR_INVALID, "NULL or aborted shard communicator");
+    v->device = c->device;
+    v->rank = c->rank;
+    v->world = c->world;
+    v->max_k = c->max_k;
+    v->bfs_state = &c->bfs_state;
+    return MARS_OK;
+}
+
+static mars_shard_comm* comm_of(const ShardCommView& v) {
+    return reinterpret_cast<mars_shard_comm*>(reinterpret_cast<char*>(v.bfs_state) -
+                                              offsetof(mars_shard_comm, bfs_state));
+}
+
+int mars::shard_gather_merge(const ShardCommView& v, const int32_t* d_ids, const float* d_vals, int32_t B, int32_t K,
+                             int32_t* d_ids_out, float* d_vals_out, int32_t* d_counts, bool neutral,
+                             cudaStream_t st) {
+    mars_shard_comm* c = comm_of(v);
+    if (B > c->max_batch || K > c->max_k) return fail(MARS_ERR_INVALID, "shard merge: B or K beyond the communicator");
+    const int64_t n = (int64_t)B * K;
+    if (!neutral && d_ids != nullptr) {
+        shard::pack_keys_kernel<<<(int)std::min<int64_t>((n + 255) / 256, 1024), 256, 0, st>>>(d_ids, d_vals, n,
+                                                                                             c->d_send);
+        MARS_CUDA_TRY(cudaGetLastError());
+    } else {
+        MARS_CUDA_TRY(cudaMemsetAsync(c->d_send, 0xff, (size_t)n * 8, st));   // kFailedKey
+    }
+    const ncclResult_t r = c->nccl->AllGather(c->d_send, c->d_recv, (size_t)n, ncclUint64, c->comm, st);
+    if (r != ncclSuccess) return nccl_fail(c->nccl, r, "shard merge: all-gather");
+    shard::merge_keys_flagged_kernel<<<B, shard::kThreads, 0, st>>>(c->d_recv, c->world, K, B, d_ids_out, d_vals_out,
+                                                                    d_counts);
+    MARS_CUDA_TRY(cudaGetLastError());
+    return MARS_OK;
+}
+
+int mars::shard_allreduce_max_f32(const ShardCommView& v, float* d, int32_t n, cudaStream_t st) {
+    mars_shard_comm* c = comm_of(v);
+    const ncclResult_t r = c->nccl->AllReduce(d, d, (size_t)n, ncclFloat32, ncclMax, c->comm, st);
+    if (r != ncclSuccess) return nccl_fail(c->nccl, r, "shard all-reduce");
+    return MARS_OK;
+}
+
+int mars::shard_allreduce_max_i32(const ShardCommView& v, int32_t* d, int32_t n, cudaStream_t st) {
+    mars_shard_comm* c = comm_of(v);
+    const ncclResult_t r = c->nccl->AllReduce(d, d, (size_t)n, ncclInt32, ncclMax, c->comm, st);
+    if (r != ncclSuccess) return nccl_fail(c->nccl, r, "shard all-reduce");
+    return MARS_OK;
+}
 
 extern "C" {
 
@@ -243,6 +336,7 @@ int mars_shard_comm_destroy(mars_shard_comm* c) {
     if (c == nullptr) return MARS_OK;
     MarsDeviceGuard g(c->device);
     cudaDeviceSynchronize();
+    if (c->bfs_state != nullptr) shard_bfs_state_free(c->bfs_state);
     if (c->comm != nullptr) c->nccl->CommDestroy(c->comm);
     cudaFree(c->d_send);
     cudaFree(c->d_recv);

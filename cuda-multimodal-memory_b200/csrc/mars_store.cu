@@ -148,15 +148,27 @@ __global__ void delete_rows_kernel(float* __restrict__ E, int64_t pitch, float* 
     if (lane == 0) ts[u] = -1.0f;
 }
 
-// fp16 copy of rows [r0, r1) (row pitch `pitch16` halves, pad zero).
+// fp16 copy of rows [r0, r1) (row pitch `pitch16` halves, pad zero), one
+// warp per row.  Each row's rounding error ||e - fp16(e)|| (exact
+// differences, fp32 sum of squares rounded up by 0.1 %) raises *err_bits,
+// the largest over the rows: the batched short list bounds its error with it.
 __global__ void to_f16_rows_kernel(const float* __restrict__ E, int64_t pitch, int32_t r0, int32_t r1, int32_t dim,
-                                   __half* __restrict__ E16, int64_t pitch16) {
-    const int64_t total = (int64_t)(r1 - r0) * pitch16;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = r0 + i / pitch16;
-        const int64_t d = i % pitch16;
-        E16[r * pitch16 + d] = d < dim ? __float2half_rn(E[r * pitch + d]) : __float2half_rn(0.0f);
+                                   __half* __restrict__ E16, int64_t pitch16, unsigned int* __restrict__ err_bits) {
+    const int lane = threadIdx.x & 31;
+    const int64_t w0 = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+    for (int64_t r = r0 + w0; r < r1; r += nw) {
+        float ss = 0.0f;
+        for (int64_t d = lane; d < pitch16; d += 32) {
+            const float x = d < dim ? E[r * pitch + d] : 0.0f;
+            const __half h = __float2half_rn(x);
+            E16[r * pitch16 + d] = h;
+            const float e = x - __half2float(h);    // exact
+            ss = fmaf(e, e, ss);
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+        if (lane == 0 && ss > 0.0f) atomicMax(err_bits, __float_as_uint(sqrtf(ss) * 1.001f));
     }
 }
 
@@ -221,8 +233,10 @@ static int alloc_store(mars_store* s) {
     MARS_CUDA_TRY(cudaMemsetAsync(s->d_mod, 0, rows * sizeof(int32_t), s->stream));
     MARS_CUDA_TRY(cudaMalloc(&s->d_n, sizeof(int32_t)));
     MARS_CUDA_TRY(cudaMemsetAsync(s->d_n, 0, sizeof(int32_t), s->stream));
-    MARS_CUDA_TRY(cudaMalloc(&s->d_norm_bits, sizeof(unsigned int)));
-    MARS_CUDA_TRY(cudaMemsetAsync(s->d_norm_bits, 0, sizeof(unsigned int), s->stream));
+    // [0]: the largest row norm; [1]: the largest fp16 rounding error of a
+    // row of the fp16 copy (both as the bits of non-negative floats)
+    MARS_CUDA_TRY(cudaMalloc(&s->d_norm_bits, 2 * sizeof(unsigned int)));
+    MARS_CUDA_TRY(cudaMemsetAsync(s->d_norm_bits, 0, 2 * sizeof(unsigned int), s->stream));
     if (s->edge_slack > 0) {
         MARS_CUDA_TRY(cudaMalloc(&s->d_extra, rows * (size_t)s->edge_slack * sizeof(int32_t)));
         MARS_CUDA_TRY(cudaMalloc(&s->d_extra_cnt, rows * sizeof(int32_t)));
@@ -328,10 +342,12 @@ int mars::store_f16_rows(const mars_store* cs, cudaStream_t st, bool* ok) {
         }
         if (s->e16_ready == nullptr) MARS_CUDA_TRY(cudaEventCreateWithFlags(&s->e16_ready, cudaEventDisableTiming));
         const int32_t r0 = s->e16_rows;
-        const int64_t total = (int64_t)(n - r0) * s->e16_pitch;
-        const int grid = (int)std::min<int64_t>((total + 255) / 256, 148 * 16);
+        // a rebuilt copy starts its rounding-error bound again
+        if (r0 == 0) MARS_CUDA_TRY(cudaMemsetAsync(s->d_norm_bits + 1, 0, sizeof(unsigned int), st));
+        const int64_t rows = n - r0;
+        const int grid = (int)std::min<int64_t>((rows * 32 + 255) / 256, 148 * 16);
         to_f16_rows_kernel<<<grid, 256, 0, st>>>(s->d_E, s->pitch, r0, n, s->dim,
-                                                 static_cast<__half*>(s->d_E16), s->e16_pitch);
+                                                 static_cast<__half*>(s->d_E16), s->e16_pitch, s->d_norm_bits + 1);
         MARS_CUDA_TRY(cudaGetLastError());
         MARS_CUDA_TRY(cudaEventRecord(s->e16_ready, st));
         s->e16_rows = n;

@@ -145,6 +145,8 @@ _SIGS = {
     "mars_shard_comm_abort": [_VP],
     "mars_shard_comm_set_timing": [_VP, _I32],
     "mars_shard_last_times": [_VP, C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(C.c_float)],
+    "mars_shard_query": [_VP, _VP, _VP, _VP, _VP, _I32, _VP, _F32, C.POINTER(RetrievalConfig), _I32, _VP,
+                         C.POINTER(_I32)],
     "mars_shard_query_batch_topk": [_VP, _VP, _VP, _VP, _I32, _I32, _F32, _F32, _I32, _I32, _I32, _I32,
                                     _VP, _VP, _VP, _VP],
     "mars_cmng_build": [_VP, _I32, _I32, _I32, _VP, C.POINTER(C.c_float)],
@@ -543,6 +545,18 @@ class ShardComm:
                                                  float(t_q), float(lam), modality_filter, int(use_importance),
                                                  K, row_offset, _ptr(d_ids), _ptr(d_vals), _ptr(d_counts),
                                                  _stream(stream, d_queries, d_ids, d_vals, d_counts)))
+
+    def query(self, store: Store, ctx: "QueryContext", d_row_offsets, d_col_indices, n_global, q, t_q,
+              cfg: RetrievalConfig, row_offset=0):
+        """query_memory_fast over all ranks' shards with BFS over the replicated
+        global CSR (collective); numpy results on every rank."""
+        qa = q if hasattr(q, "data_ptr") else _host(q, np.float32)
+        out = np.zeros(max(cfg.top_k, 1), dtype=RESULT_DTYPE)
+        n = C.c_int32()
+        _check(lib().mars_shard_query(store.handle, ctx.handle, self.handle, _ptr(d_row_offsets),
+                                      _ptr(d_col_indices), int(n_global), _ptr(qa), float(t_q), C.byref(cfg),
+                                      int(row_offset), out.ctypes.data, C.byref(n)))
+        return out[:n.value]
 
     def set_timing(self, enable: bool) -> None:
         _check(lib().mars_shard_comm_set_timing(self.handle, int(bool(enable))))

@@ -421,6 +421,26 @@ int mars_shard_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx, mars_s
                                 int32_t use_importance, int32_t K, int32_t row_offset,
                                 int32_t* d_ids, float* d_vals, int32_t* d_counts, void* stream);
 
+/* query_memory_fast (include/memory_cuda.cuh:188-194, src/memory_cuda.cu:
+ * 1069-1158) over a row-sharded corpus, one process per GPU (a collective:
+ * every rank calls it with the same query, t_q and cfg).  s: this rank's rows,
+ * global ids [row_offset, row_offset + N_r); d_row_offsets / d_col_indices:
+ * the CSR over all n_global rows in global ids (device arrays replicated on
+ * every rank; NULL allowed without BFS hops).  The answer -- the same as
+ * mars_query on one GPU holding every row and that graph -- lands in `out`
+ * (host, cfg->top_k entries) on every rank: the local top-K seeds merged with
+ * one all-gather; per BFS level, every rank expands the level over the
+ * replicated graph and one all-reduce gives every node's own score from the
+ * rank that holds its row; the results' modalities come from their owners.
+ * Limits: 16384 nodes per level and in total (MARS_ERR_CAPACITY beyond),
+ * top_k <= the communicator's max_k, D % 4 == 0.  Blocks until the results
+ * are on the host.  A rank whose part fails still takes every collective
+ * step; every rank then returns an error. */
+int mars_shard_query(const mars_store* s, mars_query_ctx* ctx, mars_shard_comm* comm,
+                     const int32_t* d_row_offsets, const int32_t* d_col_indices, int32_t n_global,
+                     const float* query, float query_timestamp, const mars_retrieval_config* cfg,
+                     int32_t row_offset, mars_query_result* out, int32_t* n_out);
+
 /* ---- CMNG kNN graph (include/cmng.cuh) --------------------------------- */
 
 /* CMNGSearchConfig, include/cmng.cuh:54-62 (bools widened to int32). */

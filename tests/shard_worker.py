@@ -37,9 +37,11 @@ def main():
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=torch.device("cuda", local))
     N, D = 300_000, 768
     lo, hi = N * rank // world, N * (rank + 1) // world
-    E, mod, ts, imp = datagen.gaussian_rows(lo, hi, D, seed=5, ts_max=600.0)
+    Ef, modf, tsf, impf = datagen.gaussian_rows(0, N, D, seed=5, ts_max=600.0)
+    E, mod, ts, imp = Ef[lo:hi], modf[lo:hi], tsf[lo:hi], impf[lo:hi]
     st = mb.Store(hi - lo, D, device=local)
     st.upload(E, mod, ts, imp)
+    ro, ci = datagen.random_bridges(modf, 4, seed=7)      # the global graph, replicated
     uid = [mb.shard_unique_id() if rank == 0 else None]
     dist.broadcast_object_list(uid, src=0)
     cases = [(16, 10), (200, 100), (64, 256)]
@@ -63,11 +65,42 @@ def main():
         lst = [torch.empty_like(t) for _ in range(world)]
         dist.all_gather(lst, t)
         same = same and all(torch.equal(lst[0], x) for x in lst)
+    # sharded query + BFS (mars_shard_query) over the replicated global graph
+    qctx = mb.QueryContext(hi - lo, D, max_k=64, device=local)
+    d_ro, d_ci = torch.from_numpy(ro).cuda(), torch.from_numpy(ci).cuda()
+    bfs_cases = [(0, 10, -1), (1, 10, -1), (2, 10, 1), (2, 32, -1)]
+    bfs_got = {}
+    for hops, K, filt in bfs_cases:
+        cfg = mb.RetrievalConfig(top_k=K, bfs_max_hops=hops, time_decay_lambda=0.01, bfs_score_decay=0.5,
+                                 modality_filter=filt, use_importance=True)
+        bfs_got[(hops, K, filt)] = [comm.query(st, qctx, d_ro, d_ci, N, Qh[q], 600.0, cfg, row_offset=lo)
+                                    for q in range(4)]
+    for (hops, K, filt), res in bfs_got.items():
+        flat = np.full((len(res), 4, K), -9, np.int32)     # fixed size on every rank
+        for i, r in enumerate(res):
+            n = len(r)
+            flat[i, :, :n] = np.stack([r["node_id"], r["score"].view(np.int32), r["modality"], r["hops"]])
+        flat = flat.ravel()
+        t = torch.from_numpy(flat).cuda()
+        lst = [torch.empty_like(t) for _ in range(world)]
+        dist.all_gather(lst, t)
+        same = same and all(torch.equal(lst[0], x) for x in lst)
     report = {"world": world, "ranks_agree": bool(same)}
     if rank == 0:
-        Ef, modf, tsf, impf = datagen.gaussian_rows(0, N, D, seed=5, ts_max=600.0)
         full = mb.Store(N, D, device=local)
-        full.upload(Ef, modf, tsf, impf)
+        full.upload(Ef, modf, tsf, impf, ro, ci)
+        fctx = mb.QueryContext(N, D, max_k=64, device=local)
+        bfs_exact = True
+        for (hops, K, filt), res in bfs_got.items():
+            cfg = mb.RetrievalConfig(top_k=K, bfs_max_hops=hops, time_decay_lambda=0.01, bfs_score_decay=0.5,
+                                     modality_filter=filt, use_importance=True)
+            for q in range(4):
+                ref = fctx.query(full, Qh[q], 600.0, cfg)
+                g = res[q]
+                bfs_exact = bfs_exact and len(g) == len(ref) and np.array_equal(g["node_id"], ref["node_id"]) and \
+                    np.array_equal(g["score"].view(np.int32), ref["score"].view(np.int32)) and \
+                    np.array_equal(g["hops"], ref["hops"]) and np.array_equal(g["modality"], ref["modality"])
+        report["bfs_equal_to_single_gpu"] = bool(bfs_exact)
         bcf = mb.BatchContext(N, D, max_batch=256, max_k=256, device=local)
         exact, oracle_ok = True, True
         corpus = O.Corpus(E=Ef, ts=tsf, mod=modf, imp=impf)

@@ -46,7 +46,7 @@ def _script(D, seed=3):
     rng = np.random.default_rng(seed)
     n1, n2 = 1500, 300
     raw = rng.standard_normal((n1 + n2, D)).astype(np.float32)
-    mod = rng.integers(0, 4, n1 + n2).astype(np.int32)
+    mod = rng.integers(0, 3, n1 + n2).astype(np.int32)    # the reference's graph builder knows 3 modalities
     ts = rng.uniform(0.0, 100.0, n1 + n2).astype(np.float32)
     cmds, queries = [], []
 

@@ -7,9 +7,13 @@ communicator owned by the library.
 * A bounded device wait that gives up on a rank (the batch context's test
   hook) marks that call's merged results invalid (counts -1) and the call
   after it is exact again.
+* mars_shard_query (top-K seeds merged over NCCL, then BFS over a replicated
+  global graph with each level's own scores exchanged) on one rank equals
+  mars_query bit for bit, hops 0-3, with and without a modality filter.
 * Two ranks on two GPUs (tests/shard_worker.py under torchrun, when two GPUs
   are visible): every rank's merged answer is the same, equals the single-GPU
-  answer over the whole corpus bit for bit, and matches the CPU oracle.
+  answer over the whole corpus bit for bit (batched top-K and the sharded BFS
+  query), and matches the CPU oracle.
 """
 import json
 import os
@@ -109,3 +113,35 @@ def test_two_ranks_on_two_gpus(tmp_path):
     rep = json.load(open(out))
     assert rep["world"] == 2
     assert rep["ranks_agree"] and rep["equal_to_single_gpu"] and rep["oracle_ok"], rep
+    assert rep["bfs_equal_to_single_gpu"], rep
+
+
+@pytest.mark.parametrize("hops,K,filt", [(0, 10, -1), (1, 10, -1), (2, 10, 2), (3, 16, -1), (2, 64, -1)])
+def test_world1_sharded_bfs_query_equals_mars_query(hops, K, filt):
+    """mars_shard_query (seeds merged over NCCL, own scores of each BFS
+    level exchanged by all-reduce) on one rank equals mars_query over the
+    same rows and graph, bit for bit."""
+    import torch
+
+    import mars_b200 as mb
+    from mars_b200 import datagen
+    N, D = 60_000, 768
+    E, mod, ts, imp = datagen.gaussian_corpus(N, D, seed=41, n_mod=4, ts_max=10.0)
+    ro, ci = datagen.random_bridges(mod, 4, seed=7)
+    st = mb.Store(N, D)
+    st.upload(E, mod, ts, imp, ro, ci)
+    ctx = mb.QueryContext(N, D, max_k=64)
+    comm = mb.ShardComm(0, 0, 1, mb.shard_unique_id(), max_batch=4, max_k=64)
+    d_ro, d_ci = torch.from_numpy(ro).cuda(), torch.from_numpy(ci).cuda()
+    cfg = mb.RetrievalConfig(top_k=K, bfs_max_hops=hops, time_decay_lambda=0.5, bfs_score_decay=0.5,
+                             modality_filter=filt, use_importance=True)
+    Q = datagen.queries(6, D, seed=42)
+    for q in range(Q.shape[0]):
+        ref = ctx.query(st, Q[q], 10.0, cfg)
+        got = comm.query(st, ctx, d_ro, d_ci, N, Q[q], 10.0, cfg, row_offset=0)
+        assert len(got) == len(ref)
+        assert np.array_equal(got["node_id"], ref["node_id"]), (q, got, ref)
+        assert np.array_equal(got["score"].view(np.int32), ref["score"].view(np.int32))
+        assert np.array_equal(got["hops"], ref["hops"])
+        assert np.array_equal(got["modality"], ref["modality"])
+    comm.close()
