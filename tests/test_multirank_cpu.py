@@ -272,3 +272,87 @@ def test_shared_bound_shards_equal_whole_corpus(tmp_path, world, fail_rank):
         assert z["cnt"][q] == KS
     # the shared bound prunes: far fewer rows than world x K per query survive
     assert z["kept"] < world * KS * QS
+
+
+# ---------------------------------------------------------------------------
+# Sharded query with BFS (mars_shard_query): every rank holds a row shard and
+# the whole graph; the seeds are the merged local top-K; every rank expands
+# each level itself over the graph (the level sorted by id), each node's own
+# score comes from the rank that holds its row through an all-reduce (max,
+# -inf elsewhere), and a node scores fmaxf(best parent * decay, own * 0.8).
+# The answer must be the single-process oracle query's.
+NB, DB, KB = 2001, 32, 8
+
+
+def _bfs_worker(rank, world, port, out_path, hops, filt):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, os.path.join(root, "cuda-multimodal-memory_b200"))
+    sys.path.insert(0, os.path.join(root, "oracle"))
+    import oracle as O
+    from mars_b200 import datagen
+    E, mod, ts, imp = datagen.gaussian_rows(0, NB, DB, seed=31, ts_max=10.0)
+    ro, ci = datagen.random_bridges(mod, 3, seed=7)
+    lo, hi = NB * rank // world, NB * (rank + 1) // world
+    shard = O.Corpus(E=E[lo:hi], ts=ts[lo:hi], mod=mod[lo:hi], imp=imp[lo:hi])
+    q = datagen.queries(1, DB, seed=32)[0]
+    own_local = O.fused_scores(shard, q, 10.0, 0.5, modality_filter=filt, use_importance=True)
+    li, lv = O.topk(own_local, mod[lo:hi], filt, KB)
+    keys = np.zeros(KB, np.uint64)
+    keys[:len(li)] = _rank_keys(li.astype(np.int32) + lo, lv)
+    got = [torch.empty(KB, dtype=torch.int64) for _ in range(world)]
+    dist.all_gather(got, torch.from_numpy(keys.view(np.int64)))
+    allk = np.sort(torch.cat(got).numpy().view(np.uint64))[::-1]
+    allk = allk[allk != 0][:KB]
+    seed_ids, seed_vals = _key_decode(allk)
+    score = {int(i): np.float32(v) for i, v in zip(seed_ids, seed_vals)}
+    hop_of = {int(i): 0 for i in seed_ids}
+    frontier = [int(i) for i in seed_ids]
+    decay = np.float32(0.5)
+    for h in range(1, hops + 1):
+        best = {}
+        for p in frontier:
+            for v in ci[ro[p]:ro[p + 1]].tolist():
+                if v in score:
+                    continue
+                c = np.float32(score[p] * decay)
+                best[v] = max(best.get(v, np.float32(-np.inf)), c)
+        level = sorted(best)
+        own = np.full(len(level), -np.inf, np.float32)
+        for j, v in enumerate(level):
+            if lo <= v < hi:
+                own[j] = own_local[v - lo]
+        t = torch.from_numpy(own)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        for j, v in enumerate(level):
+            score[v] = np.float32(max(best[v], np.float32(t[j].item()) * np.float32(0.8)))
+            hop_of[v] = h
+        frontier = level
+    final = sorted(score, key=lambda v: (-float(score[v]), v))[:KB]
+    if rank == 0:
+        np.savez(out_path, ids=np.asarray(final, np.int32),
+                 vals=np.asarray([score[v] for v in final], np.float32),
+                 hops=np.asarray([hop_of[v] for v in final], np.int32))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,hops,filt", [(2, 1, -1), (3, 2, -1), (2, 2, 1)])
+def test_sharded_bfs_query_equals_single_process_query(tmp_path, world, hops, filt):
+    out = str(tmp_path / "sbfs.npz")
+    mp.start_processes(_bfs_worker, args=(world, _free_port(), out, hops, filt), nprocs=world, join=True,
+                       start_method="spawn")
+    z = np.load(out)
+    import oracle as O
+    from mars_b200 import datagen
+    from _util import assert_ranked_equivalent
+    E, mod, ts, imp = datagen.gaussian_rows(0, NB, DB, seed=31, ts_max=10.0)
+    ro, ci = datagen.random_bridges(mod, 3, seed=7)
+    q = datagen.queries(1, DB, seed=32)[0]
+    ref = O.query(O.Corpus(E=E, ts=ts, mod=mod, imp=imp, row_offsets=ro, col_indices=ci), q, 10.0, top_k=KB,
+                  bfs_max_hops=hops, lam=0.5, bfs_score_decay=0.5, modality_filter=filt, use_importance=True)
+    assert_ranked_equivalent(z["ids"], z["vals"], ref["node_id"], ref["score"], z["hops"], ref["hops"],
+                             rtol=0, atol=0, what="sharded BFS")
