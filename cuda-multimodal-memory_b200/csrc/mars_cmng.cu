@@ -99,6 +99,39 @@ __device__ __forceinline__ float warp_dot_ref(const float* __restrict__ a, const
     return __shfl_sync(0xffffffffu, s, 0);
 }
 
+// The same arithmetic with a row's loads issued together: lane l holds
+// elements l, l + 32, ... (at most C of them, D <= 32 C) in registers before
+// the fused multiply-adds run in the reference's order, so a row costs one
+// memory round trip instead of one per unrolled group of the loop.
+template <int C>
+__device__ __forceinline__ float warp_dot_ref_rows(const float* __restrict__ a, const float* __restrict__ b,
+                                                   int D, int lane) {
+    float v[C];
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        const int d = lane + 32 * c;
+        v[c] = d < D ? __ldg(a + d) : 0.0f;
+    }
+    float s = 0.0f;
+#pragma unroll
+    for (int c = 0; c < C; ++c) {
+        const int d = lane + 32 * c;
+        if (d < D) s = __fmaf_rn(v[c], b[d], s);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) s = __fadd_rn(s, __shfl_down_sync(0xffffffffu, s, off));
+    return __shfl_sync(0xffffffffu, s, 0);
+}
+
+__device__ __forceinline__ float warp_dot_ref_fast(const float* __restrict__ a, const float* __restrict__ b, int D,
+                                                   int lane) {
+    if (D <= 256) return warp_dot_ref_rows<8>(a, b, D, lane);
+    if (D <= 512) return warp_dot_ref_rows<16>(a, b, D, lane);
+    if (D <= 768) return warp_dot_ref_rows<24>(a, b, D, lane);
+    if (D <= 1024) return warp_dot_ref_rows<32>(a, b, D, lane);
+    return warp_dot_ref(a, b, D, lane);
+}
+
 struct SearchArgs {
     const int32_t* nbrs;      // N x degree
     const float* E;           // N x pitch
@@ -180,7 +213,7 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
         if (warp < num_seeds && warp < 8) {
             const uint32_t h = __float_as_uint(s_q[0]) ^ __float_as_uint(s_q[1]);
             const int32_t seed = (int32_t)((h + (uint32_t)warp * 7919u) % (uint32_t)a.N);
-            const float sim = warp_dot_ref(a.E + (int64_t)seed * a.pitch, s_q, a.D, lane);
+            const float sim = warp_dot_ref_fast(a.E + (int64_t)seed * a.pitch, s_q, a.D, lane);
             if (lane == 0) {
                 s_bs[warp] = sim;
                 s_bi[warp] = seed;
@@ -221,7 +254,7 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
             for (int j = warp; j < a.degree; j += kWarps) {
                 if (s_dist[j] == -FLT_MAX) continue;                    // warp-uniform
                 const int32_t v = s_nb[j];
-                const float sim = warp_dot_ref(a.E + (int64_t)v * a.pitch, s_q, a.D, lane);
+                const float sim = warp_dot_ref_fast(a.E + (int64_t)v * a.pitch, s_q, a.D, lane);
                 if (lane == 0) s_dist[j] = sim;
             }
             __syncthreads();
