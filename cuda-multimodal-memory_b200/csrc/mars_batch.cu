@@ -261,29 +261,48 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
             float best[kJ];
 #pragma unroll
             for (int j = 0; j < kJ; ++j) best[j] = -INFINITY;
-            for (int c = 0; c < kBN / 32; ++c) {
-                uint32_t r[32];
-                sm100::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(sub * 32) << 16) +
-                                              (uint32_t)(buf * kBN + c * 32), r);
-                sm100::tmem_ld_wait();
-                if (!qv) continue;
-                const int rbase = row0 + c * 32;
-                if constexpr (MODE == kCandidates) {
-                    // which of the 32 rows pass; one atomic per chunk for all
-                    // of them (clustered data can make a query's candidates
-                    // dense in a few tiles), then the writes
-                    uint32_t pass = 0u;
+            if constexpr (MODE == kCandidates) {
+                // pass 1: which of the tile's 256 rows pass, as eight 32-row
+                // masks; then ONE atomic reserves this query's slots for the
+                // whole tile (clustered data can make a query's candidates
+                // dense in every tile, and each atomic is a round trip);
+                // pass 2 reads back only the chunks with hits and writes them
+                uint32_t pass[kBN / 32];
+                int total = 0;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        const float w = (rbase + j == self_row) ? NAN : s_w[c * 32 + j];
-                        const float f = __uint_as_float(r[j]) * w;
-                        if (f + mg * fabsf(w) >= th) pass |= 1u << j;   // NaN weights never pass
-                    }
-                    if (pass != 0u) {
-                        int pos = atomicAdd(a.cand_cnt + q, __popc(pass));
+                for (int c = 0; c < kBN / 32; ++c) {
+                    uint32_t r[32];
+                    sm100::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(sub * 32) << 16) +
+                                                  (uint32_t)(buf * kBN + c * 32), r);
+                    sm100::tmem_ld_wait();
+                    uint32_t m = 0u;
+                    if (qv) {
+                        const int rbase = row0 + c * 32;
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
-                            if (pass & (1u << j)) {
+                            const float w = (rbase + j == self_row) ? NAN : s_w[c * 32 + j];
+                            const float f = __uint_as_float(r[j]) * w;
+                            if (f + mg * fabsf(w) >= th) m |= 1u << j;   // NaN weights never pass
+                        }
+                    }
+                    pass[c] = m;
+                    total += __popc(m);
+                }
+                // the TMEM loads are warp-collective (.sync.aligned): every
+                // branch around them is decided for the whole warp
+                if (__any_sync(0xffffffffu, total > 0)) {
+                    int pos = total > 0 ? atomicAdd(a.cand_cnt + q, total) : 0;
+#pragma unroll
+                    for (int c = 0; c < kBN / 32; ++c) {
+                        if (!__any_sync(0xffffffffu, pass[c] != 0u)) continue;
+                        uint32_t r[32];
+                        sm100::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(sub * 32) << 16) +
+                                                      (uint32_t)(buf * kBN + c * 32), r);
+                        sm100::tmem_ld_wait();
+                        const int rbase = row0 + c * 32;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if (pass[c] & (1u << j)) {
                                 if (pos < a.cap) {
                                     const float w = s_w[c * 32 + j];
                                     a.cand[(int64_t)q * a.cap + pos] = rbase + j;
@@ -294,27 +313,35 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                             }
                         }
                     }
-                } else {
+                }
+            } else {
+                for (int c = 0; c < kBN / 32; ++c) {
+                    uint32_t r[32];
+                    sm100::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(sub * 32) << 16) +
+                                                  (uint32_t)(buf * kBN + c * 32), r);
+                    sm100::tmem_ld_wait();
+                    if (!qv) continue;
+                    const int rbase = row0 + c * 32;
 #pragma unroll
-                for (int j4 = 0; j4 < 8; ++j4) {
-                    const float4 w4 = reinterpret_cast<const float4*>(s_w + c * 32)[j4];
-                    const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
+                    for (int j4 = 0; j4 < 8; ++j4) {
+                        const float4 w4 = reinterpret_cast<const float4*>(s_w + c * 32)[j4];
+                        const float wv[4] = {w4.x, w4.y, w4.z, w4.w};
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int j = 4 * j4 + u;
-                        const float w = (rbase + j == self_row) ? NAN : wv[u];
-                        const float f = __uint_as_float(r[j]) * w;
-                        const float slack = mg * fabsf(w);
-                        // sample mode: the tile's kJ best lower bounds of query q
-                        float lo = f - slack;
-                        if (lo > best[kJ - 1]) {    // NaN never passes
+                        for (int u = 0; u < 4; ++u) {
+                            const int j = 4 * j4 + u;
+                            const float w = (rbase + j == self_row) ? NAN : wv[u];
+                            const float f = __uint_as_float(r[j]) * w;
+                            const float slack = mg * fabsf(w);
+                            // sample mode: the tile's kJ best lower bounds of query q
+                            float lo = f - slack;
+                            if (lo > best[kJ - 1]) {    // NaN never passes
 #pragma unroll
-                            for (int s = 0; s < kJ; ++s) {
-                                if (lo > best[s]) { const float tmp = best[s]; best[s] = lo; lo = tmp; }
+                                for (int s = 0; s < kJ; ++s) {
+                                    if (lo > best[s]) { const float tmp = best[s]; best[s] = lo; lo = tmp; }
+                                }
                             }
                         }
                     }
-                }
                 }
             }
             sm100::tc_fence_before();
@@ -510,7 +537,7 @@ __device__ __forceinline__ int pow2_at_least(int n) {
     return p;
 }
 
-__global__ void __launch_bounds__(kRescoreThreads)
+__global__ void __launch_bounds__(kRescoreThreads, 3)
 rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t B, float t_q,
                float lambda, int32_t use_imp, int32_t K, int32_t row_offset,
                const float* __restrict__ theta, const float* __restrict__ margin,

@@ -414,7 +414,7 @@ __device__ __forceinline__ float bfs_own_score(const BfsArgs2& a, const float4* 
 }
 
 template <int KPL>
-__global__ void __launch_bounds__(kThreads) bfs_kernel(const BfsArgs2 a) {
+__global__ void __launch_bounds__(kThreads, 3) bfs_kernel(const BfsArgs2 a) {
     __shared__ int s_lvl[16];       // level offsets; [15] = tail
     __shared__ float   s_val[kWarps][kMaxTopK];
     __shared__ int32_t s_idx[kWarps][kMaxTopK];

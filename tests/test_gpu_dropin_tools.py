@@ -91,7 +91,7 @@ def _server_rows(raw, ts, deleted, n):
     squares, sqrt + 1e-8, one division per component), tombstones zeroed."""
     x = raw[:n]
     norm2 = np.cumsum(x * x, axis=1, dtype=np.float32)[:, -1]    # sequential, like the server's loop
-    E = x / (np.sqrt(norm2, dtype=np.float32) + np.float32(1e-8))
+    E = x / (np.sqrt(norm2, dtype=np.float32) + np.float32(1e-8))[:, None]
     ts = ts[:n].copy()
     E[deleted] = 0.0
     ts[deleted] = -1.0
