@@ -548,7 +548,20 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
                int32_t* __restrict__ out_cnt, int32_t* __restrict__ fallback,
                int32_t* __restrict__ rescored, const int32_t* __restrict__ bad,
                const int32_t* __restrict__ status, float* __restrict__ bound_out,
-               const float* __restrict__ bound_in) {
+               const float* __restrict__ bound_in, int32_t* __restrict__ status_mirror, int32_t max_batch) {
+    // The call's status words, [err, sync_err, fallback[], cand_cnt[],
+    // rescored[], bad[]] (max_batch each), also go straight to the caller's
+    // host-mapped mirror by the final pass (status_mirror != NULL), so no
+    // device-to-host copy follows the call: block qi publishes its query's
+    // words on its way out, block 0 the two error words.
+    auto publish = [&](int32_t fb, int32_t resc) {
+        if (status_mirror == nullptr || threadIdx.x != 0) return;
+        if (blockIdx.x == 0) { status_mirror[0] = status[0]; status_mirror[1] = status[1]; }
+        status_mirror[2 + blockIdx.x] = fb;
+        status_mirror[2 + max_batch + blockIdx.x] = cand_cnt[blockIdx.x];
+        status_mirror[2 + 2 * max_batch + blockIdx.x] = resc;
+        status_mirror[2 + 3 * max_batch + blockIdx.x] = bad != nullptr ? bad[blockIdx.x] : 0;
+    };
     __shared__ float   s_key[kSortCap];
     __shared__ int32_t s_id[kSortCap];
     __shared__ int     s_ge, s_n2, s_nk;
@@ -573,6 +586,7 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
             out_ids[(int64_t)qi * K + p] = -1;
         }
         if (threadIdx.x == 0) { if (out_cnt) out_cnt[qi] = -1; fallback[qi] = 0; rescored[qi] = 0; }
+        if (bound_out == nullptr) publish(0, 0);
         return;
     }
     const int ncand = cand_cnt[qi];
@@ -583,6 +597,7 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         // too many candidates to sort here, too few to be complete, or a
         // query outside the fp16 range (its short list is meaningless)
         if (threadIdx.x == 0) { fallback[qi] = 1; rescored[qi] = 0; if (out_cnt) out_cnt[qi] = 0; }
+        if (bound_out == nullptr) publish(1, 0);
         return;
     }
     const float th = theta[qi];
@@ -612,6 +627,7 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     __syncthreads();
     if (s_ge < K) {
         if (threadIdx.x == 0) { fallback[qi] = 1; rescored[qi] = 0; if (out_cnt) out_cnt[qi] = 0; }
+        if (bound_out == nullptr) publish(1, 0);
         return;
     }
     float th2;
@@ -725,6 +741,7 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         fallback[qi] = 0;
         rescored[qi] = n2;
     }
+    publish(0, n2);
 }
 
 // ---------------------------------------------------------------------------
@@ -1068,7 +1085,8 @@ struct mars_batch_ctx {
     // [err, sync_err, fallback[max_batch], cand_cnt[max_batch], rescored[max_batch], bad[max_batch]]
     // (err: a pipeline wait gave up; sync_err: the grid-wide arrival wait gave up)
     int32_t* d_status = nullptr;
-    int32_t* h_status = nullptr;     // pinned mirror
+    int32_t* h_status = nullptr;     // pinned, device-mapped mirror (written by the rescore kernel)
+    int32_t* dm_status = nullptr;    // its device address
     int32_t* d_err = nullptr;        // views into d_status / h_status
     int32_t* d_fallback = nullptr;
     int32_t* d_cand_cnt = nullptr;
@@ -1208,7 +1226,8 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     T(cudaMalloc(&c->d_cand_f, (size_t)max_batch * c->cap * 8), "candidate scores and slacks");
     const size_t status_words = 2 + 4 * (size_t)max_batch;
     T(cudaMalloc(&c->d_status, status_words * 4), "status words");
-    T(cudaMallocHost(&c->h_status, status_words * 4), "pinned status words");
+    T(cudaHostAlloc(&c->h_status, status_words * 4, cudaHostAllocMapped), "pinned status words");
+    if (rc == MARS_OK) T(cudaHostGetDevicePointer(&c->dm_status, c->h_status, 0), "mapped status words");
     if (rc == MARS_OK) {
         c->d_err = c->d_status;
         c->d_fallback = c->d_status + 2;
@@ -1635,7 +1654,8 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
                                                       c->d_cand_f, c->d_cand_f + (size_t)c->max_batch * c->cap,
                                                       c->d_cand_cnt, c->cap, d_ids, d_vals, d_counts,
                                                       c->d_fallback, c->d_rescored, f16 ? c->d_bad : nullptr,
-                                                      c->d_status, bound_out, bound_in);
+                                                      c->d_status, bound_out, bound_in,
+                                                      bound_out == nullptr ? c->dm_status : nullptr, c->max_batch);
         return cudaGetLastError();
     };
     if (xchg != nullptr) {
@@ -1671,10 +1691,9 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     fa.exclude_base1 = self_base >= 0 ? self_base + 1 : 0;
     const int fgx = std::max(1, std::min(c->fb_grid, 2 * c->num_sms / B));
     MARS_CUDA_TRY(launch_scan_multi(fa, d_queries, query_pitch, B, fgx, st));
-    // the status words, read by mars_batch_last_stats (and checked for a
-    // pipeline error by the next call)
-    MARS_CUDA_TRY(cudaMemcpyAsync(c->h_status, c->d_status, (2 + 4 * (size_t)c->max_batch) * 4,
-                                  cudaMemcpyDeviceToHost, st));
+    // the status words (read by mars_batch_last_stats and checked for a
+    // pipeline error by the next call) were written to the mapped mirror by
+    // the rescore kernel; they are readable once this event has completed
     MARS_CUDA_TRY(cudaEventRecord(c->ev_status, st));
     c->status_pending = true;
     c->last_stream = st;

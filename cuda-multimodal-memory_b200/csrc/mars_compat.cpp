@@ -28,6 +28,7 @@ struct Registry {
     std::mutex mu;
     std::unordered_map<const void*, mars_store*> stores;        // d_embeddings -> store
     std::unordered_map<const void*, mars_query_ctx*> aux_ctx;   // store -> novelty context
+    std::unordered_map<const void*, float*> dense;              // store -> dense N x D copy (D % 4 != 0)
 };
 
 Registry& reg() {
@@ -135,6 +136,26 @@ __global__ void f32_to_f16_kernel(const float* __restrict__ in, int64_t pitch, h
     out[i] = __float2half(in[r * pitch + c]);
 }
 
+// The embeddings a returned DeviceMemoryGraph / CMNGGraph points at: the
+// reference's layout is dense N x D; the store keeps rows padded to a
+// multiple of 4 floats for its 16-byte loads.  When D % 4 == 0 the two are
+// the same memory; otherwise the caller gets a dense, read-only copy made at
+// upload (the queries keep reading the store's padded rows).  The store is
+// registered under the returned pointer.
+float* expose_rows(mars_store* s, int32_t n, int32_t D) {
+    float* rows = s->d_E;
+    if ((D & 3) != 0 && n > 0) {
+        CUDA_CHECK(cudaMalloc(&rows, (size_t)n * D * sizeof(float)));
+        CUDA_CHECK(cudaMemcpy2D(rows, (size_t)D * sizeof(float), s->d_E, (size_t)s->pitch * sizeof(float),
+                                (size_t)D * sizeof(float), (size_t)n, cudaMemcpyDeviceToDevice));
+    }
+    Registry& r = reg();
+    std::lock_guard<std::mutex> lk(r.mu);
+    r.stores[rows] = s;
+    if (rows != s->d_E) r.dense[s] = rows;
+    return rows;
+}
+
 }  // namespace
 
 DeviceMemoryGraph upload_to_device(const MemoryGraph& h) {
@@ -153,18 +174,16 @@ DeviceMemoryGraph upload_to_device(const MemoryGraph& h) {
     d.embedding_dim = h.embedding_dim;
     d.d_row_offsets = s->d_row_offsets;
     d.d_col_indices = s->d_col_indices;
-    d.d_embeddings = s->d_E;
+    d.d_embeddings = expose_rows(s, h.num_nodes, h.embedding_dim);
     d.d_modalities = s->d_mod;
     d.d_timestamps = s->d_ts;
-    Registry& r = reg();
-    std::lock_guard<std::mutex> lk(r.mu);
-    r.stores[s->d_E] = s;
     return d;
 }
 
 void free_device(DeviceMemoryGraph& d) {
     mars_store* s = nullptr;
     mars_query_ctx* aux = nullptr;
+    float* dense = nullptr;
     {
         Registry& r = reg();
         std::lock_guard<std::mutex> lk(r.mu);
@@ -174,9 +193,12 @@ void free_device(DeviceMemoryGraph& d) {
             r.stores.erase(it);
             auto jt = r.aux_ctx.find(s);
             if (jt != r.aux_ctx.end()) { aux = jt->second; r.aux_ctx.erase(jt); }
+            auto kt = r.dense.find(s);
+            if (kt != r.dense.end()) { dense = kt->second; r.dense.erase(kt); }
         }
     }
     mars_query_ctx_destroy(aux);
+    if (dense) cudaFree(dense);
     if (d.d_embeddings_fp16) cudaFree(d.d_embeddings_fp16);
     if (d.d_edge_hits) cudaFree(d.d_edge_hits);
     mars_store_destroy(s);
@@ -189,7 +211,7 @@ void upload_fp16_embeddings(DeviceMemoryGraph& dg) {
     StoreRef sr(dg);
     CUDA_CHECK(cudaMalloc(&dg.d_embeddings_fp16, n * D * sizeof(half)));
     const int64_t total = n * D;
-    f32_to_f16_kernel<<<(unsigned)((total + 255) / 256), 256>>>(dg.d_embeddings, sr.s->pitch,
+    f32_to_f16_kernel<<<(unsigned)((total + 255) / 256), 256>>>(sr.s->d_E, sr.s->pitch,
                                                                 dg.d_embeddings_fp16, n, (int32_t)D);
     CUDA_CHECK(cudaGetLastError());
     CUDA_CHECK(cudaDeviceSynchronize());
@@ -357,12 +379,9 @@ CMNGGraph build_cmng(const float* h_embeddings, const int32_t* h_modalities, con
     CUDA_CHECK(cudaMalloc(&g.d_neighbors, (size_t)std::max(N, 1) * degree * sizeof(int32_t)));
     // the reference selects bridges for MOD_COUNT = 3 modalities (src/cmng_build.cu:234)
     check(mars_cmng_build(s, degree, degree_cross, 3, g.d_neighbors, &g.build_time_ms), "build_cmng");
-    g.d_embeddings = s->d_E;
+    g.d_embeddings = expose_rows(s, N, D);
     g.d_modalities = s->d_mod;
     g.d_timestamps = s->d_ts;
-    Registry& r = reg();
-    std::lock_guard<std::mutex> lk(r.mu);
-    r.stores[s->d_E] = s;
     return g;
 }
 

@@ -99,22 +99,63 @@ std::vector<QueryResult>
 query_memory(const DeviceMemoryGraph& dg, const float* h_query, float query_timestamp,
              const RetrievalConfig& cfg, RetrievalStats& stats);
 
-// Query scratch.  A value type like the reference's; the library state lives
-// behind `impl` and is released by destroy_query_context.
+// Query scratch.  A value type like the reference's (include/memory_cuda.cuh
+// of the reference, QueryContext): the same members in the same order, so
+// code that names them compiles unchanged.  This library keeps its own state
+// behind `impl` (appended after them) and leaves the reference's scratch
+// pointers, events, graph and cuBLAS/CUB members null or zero: they describe
+// the reference's pipeline, which is not run here.  `stream` is the
+// context's stream, `valid` is set by create_query_context, and
+// use_cuda_graph is honoured; use_fp16 / use_cublas / use_cub_topk are
+// accepted and have no effect (the fused fp32 pipeline always runs).
 struct QueryContext {
     int32_t max_nodes     = 0;
     int32_t embedding_dim = 0;
     int32_t max_k         = 0;
 
+    float*   d_query      = nullptr;
+    float*   d_sim        = nullptr;
+    float*   d_final      = nullptr;
+    float*   d_bfs_score  = nullptr;
+    int32_t* d_hop_count  = nullptr;
+    int32_t* d_top_idx    = nullptr;
+    float*   d_top_val    = nullptr;
+    int32_t* d_front_a    = nullptr;
+    int32_t* d_front_b    = nullptr;
+    int32_t* d_front_cnt  = nullptr;
+    void*    d_compact_out   = nullptr;
+    int32_t* d_compact_count = nullptr;
+    int32_t  max_compact     = 0;
+    int32_t* d_front_cnt_b   = nullptr;
+    float*   h_query_pinned  = nullptr;
+
+    cudaEvent_t e0 = nullptr, e1 = nullptr, e2 = nullptr, e3 = nullptr, e4 = nullptr;
     cudaStream_t stream   = nullptr;   // the context's stream
     bool valid            = false;
+
+    cudaGraph_t      captured_graph   = nullptr;
+    cudaGraphExec_t  graph_exec       = nullptr;
+    bool             graph_captured   = false;
+    int32_t          graph_N          = 0;
+    int32_t          graph_K          = 0;
+    int32_t          graph_bfs_hops   = 0;
+    int32_t          graph_mod_filter = -1;
+    bool             graph_fp16       = false;
 
     bool use_cuda_graph   = false;     // replay the query as one CUDA graph
     bool use_fp16         = false;     // accepted, no effect
     bool use_cublas       = false;     // accepted, no effect
     bool use_cub_topk     = false;     // accepted, no effect
 
-    void* impl            = nullptr;   // mars_query_ctx*
+    void*    cublas_handle    = nullptr;
+    void*    d_sort_temp      = nullptr;
+    size_t   sort_temp_bytes  = 0;
+    float*   d_sort_keys_in   = nullptr;
+    float*   d_sort_keys_out  = nullptr;
+    int32_t* d_sort_vals_in   = nullptr;
+    int32_t* d_sort_vals_out  = nullptr;
+
+    void* impl            = nullptr;   // mars_query_ctx* (this library's state)
 };
 
 QueryContext create_query_context(int32_t max_nodes, int32_t embedding_dim, int32_t max_k = 64);
