@@ -261,48 +261,33 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
             float best[kJ];
 #pragma unroll
             for (int j = 0; j < kJ; ++j) best[j] = -INFINITY;
-            if constexpr (MODE == kCandidates) {
-                // pass 1: which of the tile's 256 rows pass, as eight 32-row
-                // masks; then ONE atomic reserves this query's slots for the
-                // whole tile (clustered data can make a query's candidates
-                // dense in every tile, and each atomic is a round trip);
-                // pass 2 reads back only the chunks with hits and writes them
-                uint32_t pass[kBN / 32];
-                int total = 0;
+            // one 32-row chunk of the accumulator at a time (the chunk loop is
+            // left rolled: the epilogue's code shares the instruction cache
+            // with the producer and MMA warps)
+#pragma unroll 1
+            for (int c = 0; c < kBN / 32; ++c) {
+                uint32_t r[32];
+                sm100::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(sub * 32) << 16) +
+                                              (uint32_t)(buf * kBN + c * 32), r);
+                sm100::tmem_ld_wait();
+                if (!qv) continue;
+                const int rbase = row0 + c * 32;
+                if constexpr (MODE == kCandidates) {
+                    // which of the 32 rows pass; one atomic per chunk for all
+                    // of them (clustered data can make a query's candidates
+                    // dense in a few tiles), then the writes
+                    uint32_t pass = 0u;
 #pragma unroll
-                for (int c = 0; c < kBN / 32; ++c) {
-                    uint32_t r[32];
-                    sm100::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(sub * 32) << 16) +
-                                                  (uint32_t)(buf * kBN + c * 32), r);
-                    sm100::tmem_ld_wait();
-                    uint32_t m = 0u;
-                    if (qv) {
-                        const int rbase = row0 + c * 32;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            const float w = (rbase + j == self_row) ? NAN : s_w[c * 32 + j];
-                            const float f = __uint_as_float(r[j]) * w;
-                            if (f + mg * fabsf(w) >= th) m |= 1u << j;   // NaN weights never pass
-                        }
+                    for (int j = 0; j < 32; ++j) {
+                        const float w = (rbase + j == self_row) ? NAN : s_w[c * 32 + j];
+                        const float f = __uint_as_float(r[j]) * w;
+                        if (f + mg * fabsf(w) >= th) pass |= 1u << j;   // NaN weights never pass
                     }
-                    pass[c] = m;
-                    total += __popc(m);
-                }
-                // the TMEM loads are warp-collective (.sync.aligned): every
-                // branch around them is decided for the whole warp
-                if (__any_sync(0xffffffffu, total > 0)) {
-                    int pos = total > 0 ? atomicAdd(a.cand_cnt + q, total) : 0;
-#pragma unroll
-                    for (int c = 0; c < kBN / 32; ++c) {
-                        if (!__any_sync(0xffffffffu, pass[c] != 0u)) continue;
-                        uint32_t r[32];
-                        sm100::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(sub * 32) << 16) +
-                                                      (uint32_t)(buf * kBN + c * 32), r);
-                        sm100::tmem_ld_wait();
-                        const int rbase = row0 + c * 32;
+                    if (pass != 0u) {
+                        int pos = atomicAdd(a.cand_cnt + q, __popc(pass));
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
-                            if (pass[c] & (1u << j)) {
+                            if (pass & (1u << j)) {
                                 if (pos < a.cap) {
                                     const float w = s_w[c * 32 + j];
                                     a.cand[(int64_t)q * a.cap + pos] = rbase + j;
@@ -313,15 +298,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                             }
                         }
                     }
-                }
-            } else {
-                for (int c = 0; c < kBN / 32; ++c) {
-                    uint32_t r[32];
-                    sm100::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(sub * 32) << 16) +
-                                                  (uint32_t)(buf * kBN + c * 32), r);
-                    sm100::tmem_ld_wait();
-                    if (!qv) continue;
-                    const int rbase = row0 + c * 32;
+                } else {
 #pragma unroll
                     for (int j4 = 0; j4 < 8; ++j4) {
                         const float4 w4 = reinterpret_cast<const float4*>(s_w + c * 32)[j4];
