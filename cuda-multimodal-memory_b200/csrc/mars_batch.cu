@@ -61,7 +61,12 @@ constexpr int kStages = 4;
 constexpr int kStageA = kBM * kBK * 4;    // 16 KB
 constexpr int kStageB = kBN * kBK * 4;    // 32 KB
 constexpr int kStageBytes = kStageA + kStageB;
-constexpr int kThreads = 192;
+constexpr int kThreads = 192;                // small-batch tiles: producer, MMA, 4 epilogue warps
+// 128 x 256 tiles: producer, MMA and 8 epilogue warps -- two per TMEM lane
+// quarter, each taking half of the tile's 256 columns (with 4 the epilogue
+// was the slower half of the pipeline)
+constexpr int kGemmThreads = 320;
+constexpr int kGemmEpi = kGemmThreads - 64;  // epilogue threads
 constexpr int kTmemCols = 512;
 constexpr int kJ = 16;                // sampled lower bounds kept per (query, tile)
 // Relative error margin of a short-listed score, times ||q|| max||e||.
@@ -136,7 +141,7 @@ __device__ __forceinline__ void tile_coords(const GemmArgs& a, int t, int mode, 
 // (kind::tf32, 32 elements).  Both keep 10 mantissa bits; the stage layout in
 // bytes is the same.
 template <int MODE, bool F16>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_e,
             const GemmArgs a) {
     constexpr int kElemsK = F16 ? 64 : 32;      // elements per 128-byte k-block
@@ -153,7 +158,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; ++s) { sm100::mbar_init(full + s, 1); sm100::mbar_init(empty + s, 1); }
-        for (int b = 0; b < 2; ++b) { sm100::mbar_init(tfull + b, 1); sm100::mbar_init(tempty + b, 128); }
+        for (int b = 0; b < 2; ++b) { sm100::mbar_init(tfull + b, 1); sm100::mbar_init(tempty + b, kGemmEpi); }
         sm100::mbar_init(mdrain, 1);
         sm100::fence_mbar_init();
         sm100::prefetch_tmap(&tmap_q);
@@ -237,12 +242,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
             sm100::mbar_wait_drain(mdrain, 0, a.err, 6);
         }
     } else {
-        // ---------------- epilogue (warps 2..5) ----------------
+        // ---------------- epilogue (warps 2..9) ----------------
         const int sub = warp & 3;                   // TMEM lane quarter of this warp
+        const int half = (warp - 2) >> 2;           // columns [128 half, 128 half + 128)
         const int row_in_tile = sub * 32 + lane;    // query row of this thread
         int buf = 0;
         uint32_t bphase = 0;
-        const int et = threadIdx.x - 64;           // 0..127 among the epilogue threads
+        const int et = threadIdx.x - 64;           // 0..255 among the epilogue threads
         for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
             int qt, row0;
             tile_coords(a, t, MODE, qt, row0);
@@ -253,9 +259,9 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
             // this tile: the row weights go to shared memory in one round trip
             const float th = (MODE == kCandidates && qv) ? __ldg(a.theta + q) : 0.f;
             const float mg = qv ? __ldg(a.margin + q) : 0.f;
-            asm volatile("bar.sync 1, 128;" ::: "memory");   // previous tile's reads of s_w done
-            for (int i = et; i < kBN; i += 128) s_w[i] = (row0 + i < a.n) ? row_weight(a.meta, row0 + i) : NAN;
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            asm volatile("bar.sync 1, 256;" ::: "memory");   // previous tile's reads of s_w done
+            for (int i = et; i < kBN; i += kGemmEpi) s_w[i] = (row0 + i < a.n) ? row_weight(a.meta, row0 + i) : NAN;
+            asm volatile("bar.sync 1, 256;" ::: "memory");
             if (!sm100::mbar_wait(tfull + buf, bphase, a.err, 5)) break;
             sm100::tc_fence_after();
             float best[kJ];
@@ -265,7 +271,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
             // left rolled: the epilogue's code shares the instruction cache
             // with the producer and MMA warps)
 #pragma unroll 1
-            for (int c = 0; c < kBN / 32; ++c) {
+            for (int c = half * (kBN / 64); c < (half + 1) * (kBN / 64); ++c) {
                 uint32_t r[32];
                 sm100::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(sub * 32) << 16) +
                                               (uint32_t)(buf * kBN + c * 32), r);
@@ -324,7 +330,8 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
             sm100::tc_fence_before();
             sm100::mbar_arrive(tempty + buf);
             if (MODE == kSample && qv) {
-                float* dst = a.sample_buf + ((int64_t)(t / a.qtiles) * a.B + q) * kJ;
+                // each half's kJ best of its 128 columns: [tile][query][2 kJ]
+                float* dst = a.sample_buf + (((int64_t)(t / a.qtiles) * a.B + q) * 2 + half) * kJ;
 #pragma unroll
                 for (int j = 0; j < kJ; ++j) dst[j] = best[j];
             }
@@ -837,7 +844,8 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     uint64_t* mdrain = tempty + 2;      // the MMA issuer's last commit
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdrain + 1);
 
-    __shared__ float s_theta[kSmallMaxB];   // kFused: this launch's thresholds
+    __shared__ float s_theta[kSmallMaxB];   // this launch's thresholds (kFused: after the grid wait)
+    __shared__ float s_mg[kSmallMaxB];      // the queries' error margins
     __shared__ float s_wmax[kSmallWarps][kSmallMaxB];   // sample tile: each epilogue warp's maxima
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
@@ -933,6 +941,12 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
         int buf = 0;
         uint32_t bphase = 0;
         bool have_theta = MODE != kFused;
+        // per-query values every row compares against, once per CTA
+        for (int q = rt; q < a.B; q += 128) {
+            s_mg[q] = __ldg(a.margin + q);
+            if (MODE == kCandidates) s_theta[q] = __ldg(a.theta + q);
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
         SmallTile tl;
         for (int it = 0; small_tile<MODE>(a, it, tl); ++it) {
             if (MODE == kFused && !tl.sample && !have_theta) {
@@ -980,9 +994,9 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                     if (q >= a.B) break;
                     const float wq = (a.self_base >= 0 && row == a.self_base + q) ? NAN : w;
                     const float f = __uint_as_float(r[u]) * wq;
-                    const float slack = __ldg(a.margin + q) * fabsf(wq);
+                    const float slack = s_mg[q] * fabsf(wq);
                     if (!tl.sample) {
-                        const float th = MODE == kFused ? s_theta[q] : __ldg(a.theta + q);
+                        const float th = s_theta[q];
                         if (f + slack >= th) {   // NaN weights never pass
                             const int pos = atomicAdd(a.cand_cnt + q, 1);
                             if (pos < a.cap) {
@@ -1468,7 +1482,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     const int32_t all_tiles = small ? (n + kSmallRows - 1) / kSmallRows : rtiles;
     // small tiles: one maximum per sampled tile and query when the sample has
     // plenty of tiles for the j-th largest, else one per epilogue warp
-    const int32_t per_tile = small ? (n_sample >= 4 * j ? 1 : kSmallWarps) : kJ;
+    const int32_t per_tile = small ? (n_sample >= 4 * j ? 1 : kSmallWarps) : 2 * kJ;
     const size_t sample_floats = (size_t)n_sample * (small ? B : c->max_batch) * per_tile;
     if (c->d_sample == nullptr || n_sample > c->sample_tiles_cap || sample_floats > c->sample_floats_cap) {
         MARS_CUDA_TRY(cudaStreamSynchronize(st));
@@ -1477,7 +1491,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         c->d_sample = nullptr;
         c->d_sample_rt = nullptr;
         c->sample_tiles_cap = std::max(n_sample, 16);
-        c->sample_floats_cap = std::max(sample_floats, (size_t)c->sample_tiles_cap * c->max_batch * kJ);
+        c->sample_floats_cap = std::max(sample_floats, (size_t)c->sample_tiles_cap * c->max_batch * 2 * kJ);
         MARS_CUDA_TRY(cudaMalloc(&c->d_sample, c->sample_floats_cap * 4));
         MARS_CUDA_TRY(cudaMalloc(&c->d_sample_rt, (size_t)c->sample_tiles_cap * 4));
         c->sample_rt_n = -1;
@@ -1601,22 +1615,22 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         // 2. sample
         ga.n_tiles = n_sample * qtiles;
         if (f16)
-            gemm_kernel<kSample, true><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
+            gemm_kernel<kSample, true><<<std::min(ga.n_tiles, c->num_sms), kGemmThreads, kGemmSmem, st>>>(mq, me, ga);
         else
-            gemm_kernel<kSample, false><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me, ga);
+            gemm_kernel<kSample, false><<<std::min(ga.n_tiles, c->num_sms), kGemmThreads, kGemmSmem, st>>>(mq, me, ga);
         MARS_CUDA_TRY(cudaGetLastError());
         // 3. thresholds
         threshold_kernel<<<(B * 32 + kThrThreads - 1) / kThrThreads, kThrThreads, 0, st>>>(
-            c->d_sample, n_sample, B, j, kJ, c->d_theta);
+            c->d_sample, n_sample, B, j, per_tile, c->d_theta);   // 2 kJ values per tile and query
         MARS_CUDA_TRY(cudaGetLastError());
         // 4. candidates
         ga.n_tiles = rtiles * qtiles;
         MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
         if (f16)
-            gemm_kernel<kCandidates, true><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me,
+            gemm_kernel<kCandidates, true><<<std::min(ga.n_tiles, c->num_sms), kGemmThreads, kGemmSmem, st>>>(mq, me,
                                                                                                             ga);
         else
-            gemm_kernel<kCandidates, false><<<std::min(ga.n_tiles, c->num_sms), kThreads, kGemmSmem, st>>>(mq, me,
+            gemm_kernel<kCandidates, false><<<std::min(ga.n_tiles, c->num_sms), kGemmThreads, kGemmSmem, st>>>(mq, me,
                                                                                                              ga);
         MARS_CUDA_TRY(cudaGetLastError());
         MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[1], st));
