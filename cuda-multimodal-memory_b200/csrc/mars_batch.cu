@@ -751,7 +751,8 @@ constexpr int kSmallRows = 128;
 constexpr int kSmallStage = kSmallRows * 128;      // 16 KB: 128 rows x 64 halves
 constexpr int kSmallMaxStages = 12;
 constexpr int kSmallWarps = 4;                       // epilogue warps: 32 rows each
-constexpr int kSmallStaticSmem = 2048;               // bound on the kernel's static shared memory
+constexpr int kSmallStaticSmem = 6144;               // bound on the kernel's static shared memory
+constexpr int kStageCand = 256;                      // candidates staged in shared memory per CTA
 
 struct SmallArgs {
     int32_t B, NQ;                   // queries, MMA N (B rounded up to 16)
@@ -847,6 +848,14 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     __shared__ float s_theta[kSmallMaxB];   // this launch's thresholds (kFused: after the grid wait)
     __shared__ float s_mg[kSmallMaxB];      // the queries' error margins
     __shared__ float s_wmax[kSmallWarps][kSmallMaxB];   // sample tile: each epilogue warp's maxima
+    // candidates of the candidate tiles, staged in shared memory (a shared
+    // atomic each) and written out in groups with ONE global atomic per
+    // query: a global atomic per candidate is a dependent round trip
+    __shared__ int s_ccnt;
+    __shared__ int16_t s_cq[kStageCand];
+    __shared__ int32_t s_crow[kStageCand];
+    __shared__ float s_cf[kStageCand], s_cs[kStageCand];
+    __shared__ int s_qn[kSmallMaxB], s_qbase[kSmallMaxB];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.stages; ++s) { sm100::mbar_init(full + s, 1); sm100::mbar_init(empty + s, 1); }
@@ -941,12 +950,41 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
         int buf = 0;
         uint32_t bphase = 0;
         bool have_theta = MODE != kFused;
+        bool pipe_ok = true;
         // per-query values every row compares against, once per CTA
         for (int q = rt; q < a.B; q += 128) {
             s_mg[q] = __ldg(a.margin + q);
             if (MODE == kCandidates) s_theta[q] = __ldg(a.theta + q);
+            s_qn[q] = 0;
         }
+        if (rt == 0) s_ccnt = 0;
         asm volatile("bar.sync 1, 128;" ::: "memory");
+        // the staged candidates to the per-query lists: per query one global
+        // atomic reserves its slots; called by all 128 epilogue threads
+        auto flush = [&]() {
+            const int m = min(s_ccnt, kStageCand);
+            for (int i = rt; i < m; i += 128) atomicAdd(&s_qn[s_cq[i]], 1);
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            for (int q = rt; q < a.B; q += 128) {
+                const int c = s_qn[q];
+                s_qbase[q] = c > 0 ? atomicAdd(a.cand_cnt + q, c) : 0;
+                s_qn[q] = 0;
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            for (int i = rt; i < m; i += 128) {
+                const int q = s_cq[i];
+                const int pos = s_qbase[q] + atomicAdd(&s_qn[q], 1);
+                if (pos < a.cap) {
+                    a.cand[(int64_t)q * a.cap + pos] = s_crow[i];
+                    a.cand_f[(int64_t)q * a.cap + pos] = s_cf[i];
+                    a.cand_s[(int64_t)q * a.cap + pos] = s_cs[i];
+                }
+            }
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            for (int q = rt; q < a.B; q += 128) s_qn[q] = 0;
+            if (rt == 0) s_ccnt = 0;
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+        };
         SmallTile tl;
         for (int it = 0; small_tile<MODE>(a, it, tl); ++it) {
             if (MODE == kFused && !tl.sample && !have_theta) {
@@ -982,7 +1020,12 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
             }
             const int row = tl.row0 + rt;
             const float w = row < a.n ? row_weight(a.meta, row) : NAN;   // NaN: never a candidate
-            if (!sm100::mbar_wait(tfull + buf, bphase, a.err, 16)) break;
+            // every epilogue thread runs the same tiles and named barriers:
+            // after a wait gave up, the remaining tiles are skipped, not left
+            // (the TMEM loads are warp-collective, so the warp decides as one)
+            pipe_ok = pipe_ok && sm100::mbar_wait(tfull + buf, bphase, a.err, 16);
+            pipe_ok = __all_sync(0xffffffffu, pipe_ok);
+            if (pipe_ok) {
             sm100::tc_fence_after();
             for (int q0 = 0; q0 < a.NQ; q0 += 16) {
                 uint32_t r[16];
@@ -998,11 +1041,19 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                     if (!tl.sample) {
                         const float th = s_theta[q];
                         if (f + slack >= th) {   // NaN weights never pass
-                            const int pos = atomicAdd(a.cand_cnt + q, 1);
-                            if (pos < a.cap) {
-                                a.cand[(int64_t)q * a.cap + pos] = row;
-                                a.cand_f[(int64_t)q * a.cap + pos] = f;
-                                a.cand_s[(int64_t)q * a.cap + pos] = slack;
+                            const int p = atomicAdd(&s_ccnt, 1);
+                            if (p < kStageCand) {
+                                s_cq[p] = (int16_t)q;
+                                s_crow[p] = row;
+                                s_cf[p] = f;
+                                s_cs[p] = slack;
+                            } else {   // the stage is full: straight to the query's list
+                                const int pos = atomicAdd(a.cand_cnt + q, 1);
+                                if (pos < a.cap) {
+                                    a.cand[(int64_t)q * a.cap + pos] = row;
+                                    a.cand_f[(int64_t)q * a.cap + pos] = f;
+                                    a.cand_s[(int64_t)q * a.cap + pos] = slack;
+                                }
                             }
                         }
                     } else {
@@ -1021,6 +1072,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
             }
             sm100::tc_fence_before();
             sm100::mbar_arrive(tempty + buf);
+            }   // pipe_ok
             if (++buf == 2) { buf = 0; bphase ^= 1u; }
             if (tl.sample && a.sample_per_tile == 1) {
                 // the tile's largest lower bound per query: sample_buf[tile][query]
@@ -1030,7 +1082,13 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                         fmaxf(fmaxf(s_wmax[0][rt], s_wmax[1][rt]), fmaxf(s_wmax[2][rt], s_wmax[3][rt]));
                 asm volatile("bar.sync 1, 128;" ::: "memory");
             }
+            if (!tl.sample) {   // the stage half full: out to the lists
+                asm volatile("bar.sync 1, 128;" ::: "memory");
+                if (s_ccnt >= kStageCand / 2) flush();
+            }
         }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (s_ccnt > 0) flush();
     }
     sm100::tc_fence_before();
     __syncthreads();
