@@ -845,8 +845,10 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     uint64_t* mdrain = tempty + 2;      // the MMA issuer's last commit
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdrain + 1);
 
-    __shared__ float s_theta[kSmallMaxB];   // this launch's thresholds (kFused: after the grid wait)
-    __shared__ float s_mg[kSmallMaxB];      // the queries' error margins
+    // this launch's thresholds (kFused: after the grid wait) and the queries'
+    // error margins; past B: +inf and 0, so those columns never pass
+    __shared__ __align__(16) float s_theta[kSmallMaxB];
+    __shared__ __align__(16) float s_mg[kSmallMaxB];
     __shared__ float s_wmax[kSmallWarps][kSmallMaxB];   // sample tile: each epilogue warp's maxima
     // candidates of the candidate tiles, staged in shared memory (a shared
     // atomic each) and written out in groups with ONE global atomic per
@@ -952,9 +954,9 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
         bool have_theta = MODE != kFused;
         bool pipe_ok = true;
         // per-query values every row compares against, once per CTA
-        for (int q = rt; q < a.B; q += 128) {
-            s_mg[q] = __ldg(a.margin + q);
-            if (MODE == kCandidates) s_theta[q] = __ldg(a.theta + q);
+        for (int q = rt; q < kSmallMaxB; q += 128) {
+            s_mg[q] = q < a.B ? __ldg(a.margin + q) : 0.0f;
+            s_theta[q] = (MODE == kCandidates && q < a.B) ? __ldg(a.theta + q) : INFINITY;
             s_qn[q] = 0;
         }
         if (rt == 0) s_ccnt = 0;
@@ -1027,36 +1029,63 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
             pipe_ok = __all_sync(0xffffffffu, pipe_ok);
             if (pipe_ok) {
             sm100::tc_fence_after();
+            const int selfq = a.self_base >= 0 ? row - a.self_base : -1;   // the query that leaves this row out
             for (int q0 = 0; q0 < a.NQ; q0 += 16) {
                 uint32_t r[16];
                 sm100::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(buf * a.NQ + q0), r);
                 sm100::tmem_ld_wait();
+                if (!tl.sample) {
+                    // the 16 queries' tests without a branch each (columns
+                    // past B carry theta = +inf), then the rare hits
+                    uint32_t pass = 0u;
+#pragma unroll
+                    for (int u4 = 0; u4 < 4; ++u4) {
+                        const float4 th4 = reinterpret_cast<const float4*>(s_theta + q0)[u4];
+                        const float4 mg4 = reinterpret_cast<const float4*>(s_mg + q0)[u4];
+                        const float thv[4] = {th4.x, th4.y, th4.z, th4.w};
+                        const float mgv[4] = {mg4.x, mg4.y, mg4.z, mg4.w};
+#pragma unroll
+                        for (int k = 0; k < 4; ++k) {
+                            const int u = 4 * u4 + k;
+                            const float wq = (q0 + u == selfq) ? NAN : w;
+                            const float f = __uint_as_float(r[u]) * wq;
+                            if (f + mgv[k] * fabsf(wq) >= thv[k]) pass |= 1u << u;   // NaN weights never pass
+                        }
+                    }
+                    if (pass != 0u) {
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) {   // compile-time indices: r[] stays in registers
+                        if (!(pass & (1u << u))) continue;
+                        const int q = q0 + u;
+                        const float wq = (q == selfq) ? NAN : w;
+                        const float f = __uint_as_float(r[u]) * wq;
+                        const float slack = s_mg[q] * fabsf(wq);
+                        const int p = atomicAdd(&s_ccnt, 1);
+                        if (p < kStageCand) {
+                            s_cq[p] = (int16_t)q;
+                            s_crow[p] = row;
+                            s_cf[p] = f;
+                            s_cs[p] = slack;
+                        } else {   // the stage is full: straight to the query's list
+                            const int pos = atomicAdd(a.cand_cnt + q, 1);
+                            if (pos < a.cap) {
+                                a.cand[(int64_t)q * a.cap + pos] = row;
+                                a.cand_f[(int64_t)q * a.cap + pos] = f;
+                                a.cand_s[(int64_t)q * a.cap + pos] = slack;
+                            }
+                        }
+                    }
+                    }
+                    continue;
+                }
 #pragma unroll
                 for (int u = 0; u < 16; ++u) {
                     const int q = q0 + u;
                     if (q >= a.B) break;
-                    const float wq = (a.self_base >= 0 && row == a.self_base + q) ? NAN : w;
+                    const float wq = (q == selfq) ? NAN : w;
                     const float f = __uint_as_float(r[u]) * wq;
                     const float slack = s_mg[q] * fabsf(wq);
-                    if (!tl.sample) {
-                        const float th = s_theta[q];
-                        if (f + slack >= th) {   // NaN weights never pass
-                            const int p = atomicAdd(&s_ccnt, 1);
-                            if (p < kStageCand) {
-                                s_cq[p] = (int16_t)q;
-                                s_crow[p] = row;
-                                s_cf[p] = f;
-                                s_cs[p] = slack;
-                            } else {   // the stage is full: straight to the query's list
-                                const int pos = atomicAdd(a.cand_cnt + q, 1);
-                                if (pos < a.cap) {
-                                    a.cand[(int64_t)q * a.cap + pos] = row;
-                                    a.cand_f[(int64_t)q * a.cap + pos] = f;
-                                    a.cand_s[(int64_t)q * a.cap + pos] = slack;
-                                }
-                            }
-                        }
-                    } else {
+                    {
                         // the warp's largest lower bound (its 32 rows) for query q
                         float lo = f - slack;
                         if (!(lo == lo)) lo = -INFINITY;

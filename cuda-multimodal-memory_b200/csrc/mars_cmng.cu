@@ -201,6 +201,11 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
     const uint32_t mask = (uint32_t)a.hash_size - 1u;
 
     for (int qi = blockIdx.x; qi < a.nq; qi += gridDim.x) {
+        // the beam and its merged successor swap roles every iteration
+        float* bs = s_bs;
+        int32_t* bi = s_bi;
+        float* nbs = s_nbs;
+        int32_t* nbi = s_nbi;
         const float* q = a.Q + (int64_t)qi * a.qpitch;
         for (int d = tid; d < a.D; d += kThreads) s_q[d] = q[d];
         for (int i = tid; i < a.hash_size; i += kThreads) s_hash[i] = -1;
@@ -215,8 +220,8 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
             const int32_t seed = (int32_t)((h + (uint32_t)warp * 7919u) % (uint32_t)a.N);
             const float sim = warp_dot_ref_fast(a.E + (int64_t)seed * a.pitch, s_q, a.D, lane);
             if (lane == 0) {
-                s_bs[warp] = sim;
-                s_bi[warp] = seed;
+                bs[warp] = sim;
+                bi[warp] = seed;
                 if (set_insert(s_hash, mask, seed)) atomicAdd(&s_scored, 1);
             }
         }
@@ -226,9 +231,9 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
             const int ns = min(min(num_seeds, 8), bw);
             for (int i = 0; i < ns - 1; ++i)
                 for (int j = i + 1; j < ns; ++j)
-                    if (s_bs[j] > s_bs[i]) {
-                        const float t = s_bs[i]; s_bs[i] = s_bs[j]; s_bs[j] = t;
-                        const int32_t u = s_bi[i]; s_bi[i] = s_bi[j]; s_bi[j] = u;
+                    if (bs[j] > bs[i]) {
+                        const float t = bs[i]; bs[i] = bs[j]; bs[j] = t;
+                        const int32_t u = bi[i]; bi[i] = bi[j]; bi[j] = u;
                     }
         }
         __syncthreads();
@@ -237,7 +242,7 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
         int iters = 0;
         for (int it = 0; it < a.max_iter; ++it) {
             if (it >= bw) break;
-            const int32_t parent = s_bi[it];
+            const int32_t parent = bi[it];
             if (parent < 0) break;
             ++iters;
             const int32_t* nb = a.nbrs + (int64_t)parent * a.degree;
@@ -262,10 +267,10 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
                 if (s_dist[j] > -FLT_MAX * 0.5f) { set_insert(s_hash, mask, s_nb[j]); atomicAdd(&s_scored, 1); }
             // rank merge: beam entries keep their order and precede equal candidates
             for (int o = tid; o < bw; o += kThreads) {
-                const float so = s_bs[o];
+                const float so = bs[o];
                 int pos = o;
                 for (int j = 0; j < a.degree; ++j) pos += (s_dist[j] > -FLT_MAX * 0.5f && s_dist[j] > so) ? 1 : 0;
-                if (pos < bw) { s_nbs[pos] = so; s_nbi[pos] = s_bi[o]; }
+                if (pos < bw) { nbs[pos] = so; nbi[pos] = bi[o]; }
             }
             for (int j = tid; j < a.degree; j += kThreads) {
                 const float d = s_dist[j];
@@ -275,15 +280,20 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
                     const float dk = s_dist[k];
                     pos += (dk > -FLT_MAX * 0.5f && (dk > d || (dk == d && k < j))) ? 1 : 0;
                 }
-                for (int o = 0; o < bw; ++o) pos += (s_bs[o] >= d) ? 1 : 0;
-                if (pos < bw) { s_nbs[pos] = d; s_nbi[pos] = s_nb[j]; }
+                for (int o = 0; o < bw; ++o) pos += (bs[o] >= d) ? 1 : 0;
+                if (pos < bw) { nbs[pos] = d; nbi[pos] = s_nb[j]; }
             }
             __syncthreads();
-            for (int o = tid; o < bw; o += kThreads) { s_bs[o] = s_nbs[o]; s_bi[o] = s_nbi[o]; }
-            __syncthreads();
+            // the merged beam is the beam of the next iteration
+            float* tf = bs; bs = nbs; nbs = tf;
+            int32_t* ti = bi; bi = nbi; nbi = ti;
         }
 
         // ---- decay (src/cmng_search.cu:275-280) ----
+        if (bs != s_bs) {   // the current beam sits in the second buffer: bring it home
+            for (int o = tid; o < bw; o += kThreads) { s_bs[o] = bs[o]; s_bi[o] = bi[o]; }
+            __syncthreads();
+        }
         for (int o = tid; o < bw; o += kThreads) {
             const int32_t id = s_bi[o];
             if (id >= 0) {
