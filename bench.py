@@ -6,18 +6,22 @@ vs peak):
   * corpus N = 1,000,000 rows x D = 768 fp32, i.i.d. Gaussian rows divided by
     (||v|| + 1e-8), timestamps U[0, 600] s, importance U[0, 1], 4 modalities;
     seeded synthetic data (no dataset is involved);
-  * a step is 16 concurrent queries, each the exact top-K = 10 of
-    dot x exp(-lambda * age) x importance over all N rows, lambda = 0.01,
-    answered by mars_query_batch_topk (an fp16 tensor-core short list with a
-    proven error margin, then an exact fp32 rescore: the results are those of
-    the fp32 fused scan bit for bit, which the run checks);
+  * a step is 64 concurrent queries (`--queries-per-step`), each the exact
+    top-K = 10 of dot x exp(-lambda * age) x importance over all N rows,
+    lambda = 0.01, answered by mars_query_batch_topk (an fp16 tensor-core
+    short list with a proven error margin, then an exact fp32 rescore: the
+    results are those of the fp32 fused scan bit for bit, which the run
+    checks, and the oracle's, which the run checks on 32 queries); 64 is the
+    most the small-batch tiles hold, so a step stays one pass over the rows
+    (the line's `batch_sweep_per_gpu` has the step at 16 / 32 / 48);
   * N GPUs (`--shard replicas`, the default): the 1M-row corpus (4.6 GB with
     its fp16 copy) fits every GPU, so every GPU holds it and answers its own
-    16 queries per step, with no data-path collective (weak scaling: 16 N
+    64 queries per step, with no data-path collective (weak scaling: 64 N
     queries per step).  `--shard rows`: the corpus is row-sharded (strong
     scaling), every GPU answers the same queries on its shard, and the
     per-query local top-K lists are all-gathered over NCCL and merged on
-    every GPU.
+    every GPU.  The line's `configs` carries every config of the family
+    (c0-c4), c2 row-sharded through the library's own NCCL path.
 
 `value` is queries/s with queries and corpus resident in HBM, timed with CUDA
 events on the query stream (max over ranks).  `e2e` goes through the public
@@ -60,7 +64,9 @@ def parse_args():
     ap.add_argument("--n", type=int, default=1_000_000)
     ap.add_argument("--dim", type=int, default=768)
     ap.add_argument("--k", type=int, default=10)
-    ap.add_argument("--queries-per-step", type=int, default=16)
+    ap.add_argument("--queries-per-step", type=int, default=64,
+                    help="concurrent queries answered by one step (one mars_query_batch_topk call); 64 is the "
+                         "most the small-batch tensor-core tiles hold, so the step stays one pass over the rows")
     ap.add_argument("--lam", type=float, default=0.01)
     ap.add_argument("--ts-max", type=float, default=600.0)
     ap.add_argument("--seed", type=int, default=42)
@@ -279,7 +285,8 @@ def run_mars(a):
     lo, hi = (a.n * rank // world, a.n * (rank + 1) // world) if sharded else (0, a.n)
     n_local = hi - lo
     E, mod, ts, imp = datagen.gaussian_rows(lo, hi, a.dim, seed=a.seed, ts_max=a.ts_max)
-    Qh = datagen.queries(64, a.dim, seed=a.seed + 1 + (0 if sharded else 1000 * rank))
+    n_pool = max(64, 2 * a.queries_per_step)     # query pool the steps cycle through
+    Qh = datagen.queries(n_pool, a.dim, seed=a.seed + 1 + (0 if sharded else 1000 * rank))
     store = mb.Store(n_local, a.dim, device=local)
     store.upload(E, mod, ts, imp)
     ctx = mb.QueryContext(n_local, a.dim, max_k=a.k, device=local)
@@ -357,7 +364,7 @@ def run_mars(a):
     ref_ids = torch.empty_like(ids)
     ref_vals = torch.empty_like(vals)
     exact = True
-    for base in (0, 16, 48):
+    for base in sorted({0, Q // 2, n_pool - Q}):
         q = Qd[base:base + Q]
         batch(q, ids, vals)
         ctx.scan_topk_multi(store, q, Q, a.ts_max, a.lam, K, ref_ids, ref_vals, use_importance=True,
@@ -398,6 +405,26 @@ def run_mars(a):
     f16_ms = timed(lambda: ctx.scan_topk_f16(store, Qd[:Q], Q, a.ts_max, a.lam, K, ids, vals,
                                              use_importance=True, row_offset=lo, stream=ctx.stream), 8)
 
+    # the same step with fewer concurrent queries (device time per step, 20
+    # steps each, outside the timed region): how the step's cost grows with
+    # the batch
+    sweep = {}
+    if not sharded:
+        for Bs in (16, 32, 48):
+            if Bs >= Q:
+                continue
+            bcs = mb.BatchContext(n_local, a.dim, max_batch=Bs, max_k=K, device=local)
+            i2 = torch.empty((Bs, K), dtype=torch.int32, device="cuda")
+            v2 = torch.empty((Bs, K), dtype=torch.float32, device="cuda")
+            for _ in range(3):
+                bcs.query_batch_topk(store, Qd[:Bs], Bs, a.ts_max, a.lam, K, i2, v2, use_importance=True,
+                                     row_offset=lo, stream=ctx.stream)
+            t_ms = timed(lambda: [bcs.query_batch_topk(store, Qd[:Bs], Bs, a.ts_max, a.lam, K, i2, v2,
+                                                       use_importance=True, row_offset=lo, stream=ctx.stream)
+                                  for _ in range(20)], 1)[0] / 20
+            sweep[str(Bs)] = {"ms_per_step": t_ms, "queries_per_s": Bs / (t_ms * 1e-3)}
+            bcs.close()
+
     # ---- end to end through the public API with host buffers --------------
     # A serving loop: every step copies its queries host -> device, answers
     # them and copies the ids and scores device -> host into one of two pinned
@@ -421,7 +448,7 @@ def run_mars(a):
     for s in range(a.steps + 1):
         if s < a.steps:
             b = s % 2
-            base = (s * Q) % (64 - Q + 1)
+            base = (s * Q) % (n_pool - Q + 1)
             qbuf.copy_(Qpin[base:base + Q], non_blocking=True)
             if sharded:
                 bc.query_batch_topk(store, qbuf, Q, a.ts_max, a.lam, K, ids, vals, use_importance=True,
@@ -519,6 +546,7 @@ def run_mars(a):
                          "bytes_note": "fp16 rows (pitch %d halves) plus a timestamp and an importance "
                                        "per row, once per query tile (one tile at B <= 64)" % pitch16},
             "batch_stats": bstats,
+            "batch_sweep_per_gpu": sweep,
             "fused_scan": {
                 "note": "the fp32 fused scan (score x decay x importance -> top-K), event-timed "
                         "outside the timed region",
