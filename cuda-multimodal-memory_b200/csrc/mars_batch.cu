@@ -61,7 +61,6 @@ constexpr int kStages = 4;
 constexpr int kStageA = kBM * kBK * 4;    // 16 KB
 constexpr int kStageB = kBN * kBK * 4;    // 32 KB
 constexpr int kStageBytes = kStageA + kStageB;
-constexpr int kThreads = 192;                // small-batch tiles: producer, MMA, 4 epilogue warps
 // 128 x 256 tiles: producer, MMA and 8 epilogue warps -- two per TMEM lane
 // quarter, each taking half of the tile's 256 columns (with 4 the epilogue
 // was the slower half of the pipeline)
@@ -593,7 +592,11 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     // K <= 32: every warp keeps its K best lower bounds (ranked by value, then
     // candidate index) and warp 0 merges the eight lists; larger K: a radix
     // selection over all of them.  Either way th2 is the K-th largest.
-    const bool warp_lists = K <= 32;
+    // Shard pass 2 (bound_in): the exchanged bound is the maximum of every
+    // shard's certified K-th lower bound, this shard's included, so it
+    // replaces the local selection; only the completeness count runs.
+    const bool need_th2 = bound_in == nullptr;
+    const bool warp_lists = need_th2 && K <= 32;
     WarpTopK<1> top;
     top.init(warp_lists ? K : 1);
     int ge = 0;
@@ -603,7 +606,7 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         const float lo = in ? cf[i] - cs[i] : -INFINITY;
         ge += (in && lo >= th) ? 1 : 0;
         if (warp_lists) top.offer_lanes(lo, i, in, lane);
-        else if (in) s_key[i] = lo;
+        else if (need_th2 && in) s_key[i] = lo;
     }
     ge = warp_reduce_sum_int(ge);
     if (lane == 0) atomicAdd(&s_ge, ge);
@@ -615,7 +618,9 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         return;
     }
     float th2;
-    if (warp_lists) {
+    if (!need_th2) {
+        th2 = __ldcg(bound_in + qi);
+    } else if (warp_lists) {
         if (warp == 0) {
             for (int ww = 1; ww < kWarps; ++ww) top.merge_sorted32(s_wv + ww * 32, s_wi + ww * 32, K, lane);
             if (lane == 0) s_th2 = top.thr_v;
@@ -630,7 +635,6 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         if (threadIdx.x == 0) bound_out[qi] = th2;
         return;
     }
-    if (bound_in != nullptr) th2 = fmaxf(th2, __ldcg(bound_in + qi));
 
     // ---- pass 2: exact scores of the candidates that can still place -------
     // Their rows are listed first (in the histogram's space, free now) and
@@ -750,7 +754,12 @@ constexpr int kSmallMaxB = 64;
 constexpr int kSmallRows = 128;
 constexpr int kSmallStage = kSmallRows * 128;      // 16 KB: 128 rows x 64 halves
 constexpr int kSmallMaxStages = 12;
-constexpr int kSmallWarps = 4;                       // epilogue warps: 32 rows each
+constexpr int kSmallWarps = 4;                       // TMEM lane quarters: 32 rows each
+// producer, MMA and 8 epilogue warps: two per lane quarter, taking
+// alternate 16-query column chunks (with one per quarter the epilogue paced
+// the launch at 48-64 queries)
+constexpr int kSmallThreads = 320;
+constexpr int kSmallEpi = kSmallThreads - 64;
 constexpr int kSmallStaticSmem = 6144;               // bound on the kernel's static shared memory
 constexpr int kStageCand = 256;                      // candidates staged in shared memory per CTA
 
@@ -829,7 +838,7 @@ __host__ __device__ constexpr size_t small_smem_bytes(int nkb, int NQ, int stage
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kSmallThreads, 1)
 gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ CUtensorMap tmap_e,
                   const SmallArgs a) {
     extern __shared__ uint8_t smem_raw[];
@@ -862,7 +871,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.stages; ++s) { sm100::mbar_init(full + s, 1); sm100::mbar_init(empty + s, 1); }
         sm100::mbar_init(qfull, 1);
-        for (int b = 0; b < 2; ++b) { sm100::mbar_init(tfull + b, 1); sm100::mbar_init(tempty + b, 128); }
+        for (int b = 0; b < 2; ++b) { sm100::mbar_init(tfull + b, 1); sm100::mbar_init(tempty + b, kSmallEpi); }
         sm100::mbar_init(mdrain, 1);
         sm100::fence_mbar_init();
         sm100::prefetch_tmap(&tmap_q);
@@ -949,31 +958,34 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
         // ---------------- epilogue (warps 2..5): thread = row ----------------
         const int sub = warp & 3;                   // TMEM lane quarter of this warp
         const int rt = sub * 32 + lane;             // row within the tile
+        const int ew = warp - 2;                    // epilogue warp 0..7
+        const int qh = ew >> 2;                     // 16-query column chunks qh, qh + 2, ...
+        const int et = threadIdx.x - 64;            // 0..255 among the epilogue threads
         int buf = 0;
         uint32_t bphase = 0;
         bool have_theta = MODE != kFused;
         bool pipe_ok = true;
         // per-query values every row compares against, once per CTA
-        for (int q = rt; q < kSmallMaxB; q += 128) {
+        for (int q = et; q < kSmallMaxB; q += kSmallEpi) {
             s_mg[q] = q < a.B ? __ldg(a.margin + q) : 0.0f;
             s_theta[q] = (MODE == kCandidates && q < a.B) ? __ldg(a.theta + q) : INFINITY;
             s_qn[q] = 0;
         }
-        if (rt == 0) s_ccnt = 0;
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (et == 0) s_ccnt = 0;
+        asm volatile("bar.sync 1, 256;" ::: "memory");
         // the staged candidates to the per-query lists: per query one global
         // atomic reserves its slots; called by all 128 epilogue threads
         auto flush = [&]() {
             const int m = min(s_ccnt, kStageCand);
-            for (int i = rt; i < m; i += 128) atomicAdd(&s_qn[s_cq[i]], 1);
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            for (int q = rt; q < a.B; q += 128) {
+            for (int i = et; i < m; i += kSmallEpi) atomicAdd(&s_qn[s_cq[i]], 1);
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            for (int q = et; q < a.B; q += kSmallEpi) {
                 const int c = s_qn[q];
                 s_qbase[q] = c > 0 ? atomicAdd(a.cand_cnt + q, c) : 0;
                 s_qn[q] = 0;
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            for (int i = rt; i < m; i += 128) {
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            for (int i = et; i < m; i += kSmallEpi) {
                 const int q = s_cq[i];
                 const int pos = s_qbase[q] + atomicAdd(&s_qn[q], 1);
                 if (pos < a.cap) {
@@ -982,10 +994,10 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                     a.cand_s[(int64_t)q * a.cap + pos] = s_cs[i];
                 }
             }
-            asm volatile("bar.sync 1, 128;" ::: "memory");
-            for (int q = rt; q < a.B; q += 128) s_qn[q] = 0;
-            if (rt == 0) s_ccnt = 0;
-            asm volatile("bar.sync 1, 128;" ::: "memory");
+            asm volatile("bar.sync 1, 256;" ::: "memory");
+            for (int q = et; q < a.B; q += kSmallEpi) s_qn[q] = 0;
+            if (et == 0) s_ccnt = 0;
+            asm volatile("bar.sync 1, 256;" ::: "memory");
         };
         SmallTile tl;
         for (int it = 0; small_tile<MODE>(a, it, tl); ++it) {
@@ -993,8 +1005,8 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                 // every CTA's sample maxima written: a grid-wide arrival count
                 // (the launch is cooperative, so every CTA is resident and the
                 // wait ends; it is bounded all the same)
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (rt == 0) {
+                asm volatile("bar.sync 1, 256;" ::: "memory");
+                if (et == 0) {
                     __threadfence();
                     atomicAdd(a.grid_sync, 1ull);
                     uint32_t spins = 0;
@@ -1009,15 +1021,15 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                     }
                     __threadfence();
                 }
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                for (int q = sub; q < a.B; q += kSmallWarps) {
+                asm volatile("bar.sync 1, 256;" ::: "memory");
+                for (int q = ew; q < a.B; q += 2 * kSmallWarps) {
                     const float th = warp_threshold(a.sample_buf, a.n_sample, a.B, q, a.j, a.sample_per_tile, lane);
                     if (lane == 0) {
                         s_theta[q] = th;
                         if (blockIdx.x == 0) a.theta_out[q] = th;
                     }
                 }
-                asm volatile("bar.sync 1, 128;" ::: "memory");
+                asm volatile("bar.sync 1, 256;" ::: "memory");
                 have_theta = true;
             }
             const int row = tl.row0 + rt;
@@ -1030,7 +1042,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
             if (pipe_ok) {
             sm100::tc_fence_after();
             const int selfq = a.self_base >= 0 ? row - a.self_base : -1;   // the query that leaves this row out
-            for (int q0 = 0; q0 < a.NQ; q0 += 16) {
+            for (int q0 = 16 * qh; q0 < a.NQ; q0 += 32) {
                 uint32_t r[16];
                 sm100::tmem_ld_32x32b_x16(tmem_base + ((uint32_t)(sub * 32) << 16) + (uint32_t)(buf * a.NQ + q0), r);
                 sm100::tmem_ld_wait();
@@ -1105,18 +1117,18 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
             if (++buf == 2) { buf = 0; bphase ^= 1u; }
             if (tl.sample && a.sample_per_tile == 1) {
                 // the tile's largest lower bound per query: sample_buf[tile][query]
-                asm volatile("bar.sync 1, 128;" ::: "memory");
-                if (rt < a.B)
-                    a.sample_buf[(int64_t)tl.sidx * a.B + rt] =
-                        fmaxf(fmaxf(s_wmax[0][rt], s_wmax[1][rt]), fmaxf(s_wmax[2][rt], s_wmax[3][rt]));
-                asm volatile("bar.sync 1, 128;" ::: "memory");
+                asm volatile("bar.sync 1, 256;" ::: "memory");
+                if (et < a.B)
+                    a.sample_buf[(int64_t)tl.sidx * a.B + et] =
+                        fmaxf(fmaxf(s_wmax[0][et], s_wmax[1][et]), fmaxf(s_wmax[2][et], s_wmax[3][et]));
+                asm volatile("bar.sync 1, 256;" ::: "memory");
             }
             if (!tl.sample) {   // the stage half full: out to the lists
-                asm volatile("bar.sync 1, 128;" ::: "memory");
+                asm volatile("bar.sync 1, 256;" ::: "memory");
                 if (s_ccnt >= kStageCand / 2) flush();
             }
         }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        asm volatile("bar.sync 1, 256;" ::: "memory");
         if (s_ccnt > 0) flush();
     }
     sm100::tc_fence_before();
@@ -1662,20 +1674,20 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
             void* args[] = {const_cast<CUtensorMap*>(&mq), const_cast<CUtensorMap*>(&me), &sa};
             MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
             MARS_CUDA_TRY(cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&gemm_small_kernel<kFused>),
-                                                      dim3(grid), dim3(kThreads), args, smem, st));
+                                                      dim3(grid), dim3(kSmallThreads), args, smem, st));
             c->grid_sync_count += (unsigned long long)grid;
             MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[1], st));
         } else {
             // the same three steps as separate launches (no cooperative launch)
             sa.n_tiles = n_sample;
-            gemm_small_kernel<kSample><<<n_sample, kThreads, smem, st>>>(mq, me, sa);
+            gemm_small_kernel<kSample><<<n_sample, kSmallThreads, smem, st>>>(mq, me, sa);
             MARS_CUDA_TRY(cudaGetLastError());
             threshold_kernel<<<(B * 32 + kThrThreads - 1) / kThrThreads, kThrThreads, 0, st>>>(
                 c->d_sample, n_sample, B, j, sa.sample_per_tile, c->d_theta);
             MARS_CUDA_TRY(cudaGetLastError());
             sa.n_tiles = all_tiles;
             MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
-            gemm_small_kernel<kCandidates><<<grid, kThreads, smem, st>>>(mq, me, sa);
+            gemm_small_kernel<kCandidates><<<grid, kSmallThreads, smem, st>>>(mq, me, sa);
             MARS_CUDA_TRY(cudaGetLastError());
             MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[1], st));
         }
