@@ -413,21 +413,20 @@ __global__ void prep_queries_kernel(const float* __restrict__ Q, int64_t qpitch,
 constexpr int kThrThreads = 256;
 constexpr int kThrKeep = 32;
 
-// The j-th largest of query q's values for one warp (see threshold_kernel).
-__device__ float warp_threshold(const float* __restrict__ sample_buf, int32_t n_sample_tiles, int32_t B, int q,
-                                int32_t j, int32_t per_tile, int lane) {
-    const int total = n_sample_tiles * per_tile;
-    float keep[kThrKeep];
+// Streams `total` values (load(i); -inf marks an empty slot) through one
+// warp: each lane keeps its kThrKeep largest sorted in registers.  Returns
+// the warp's count of non-empty values.
+template <class Load>
+__device__ __forceinline__ int warp_keep_largest(Load load, int total, float (&keep)[kThrKeep], int lane) {
 #pragma unroll
     for (int s = 0; s < kThrKeep; ++s) keep[s] = -INFINITY;
     int valid = 0;
     for (int i0 = lane; i0 < total; i0 += 8 * 32) {
-        float v[8];   // eight loads in flight per lane (L2: other CTAs may have written them)
+        float v[8];   // eight loads in flight per lane
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
             const int i = i0 + 32 * k;
-            v[k] = i < total ? __ldcg(sample_buf + ((int64_t)(i / per_tile) * B + q) * per_tile + (i % per_tile))
-                             : -INFINITY;
+            v[k] = i < total ? load(i) : -INFINITY;
         }
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
@@ -441,22 +440,38 @@ __device__ float warp_threshold(const float* __restrict__ sample_buf, int32_t n_
             }
         }
     }
-    valid = warp_reduce_sum_int(valid);
-    float th = -INFINITY;
-    if (valid >= j) {
-        for (int r = 0; r < j; ++r) {
-            float m = keep[0];
+    return warp_reduce_sum_int(valid);
+}
+
+// Takes the warp's largest kept value n times (a max butterfly; the lowest
+// lane holding it drops it); emit(r, m) receives the (r+1)-th largest, -inf
+// once the kept values are used up.
+template <class Emit>
+__device__ __forceinline__ void warp_take_largest(float (&keep)[kThrKeep], int n, int lane, Emit emit) {
+    for (int r = 0; r < n; ++r) {
+        float m = keep[0];
 #pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-            const unsigned who = __ballot_sync(0xffffffffu, keep[0] == m);
-            if (lane == __ffs(who) - 1) {
+        for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        const unsigned who = __ballot_sync(0xffffffffu, keep[0] == m);
+        if (lane == __ffs(who) - 1) {
 #pragma unroll
-                for (int s = 0; s < kThrKeep - 1; ++s) keep[s] = keep[s + 1];
-                keep[kThrKeep - 1] = -INFINITY;
-            }
-            th = m;
+            for (int s = 0; s < kThrKeep - 1; ++s) keep[s] = keep[s + 1];
+            keep[kThrKeep - 1] = -INFINITY;
         }
+        emit(r, m);
     }
+}
+
+// The j-th largest of query q's values for one warp (see threshold_kernel).
+__device__ float warp_threshold(const float* __restrict__ sample_buf, int32_t n_sample_tiles, int32_t B, int q,
+                                int32_t j, int32_t per_tile, int lane) {
+    float keep[kThrKeep];
+    // L2 loads: other CTAs may have written the values
+    const int valid = warp_keep_largest(
+        [&](int i) { return __ldcg(sample_buf + ((int64_t)(i / per_tile) * B + q) * per_tile + (i % per_tile)); },
+        n_sample_tiles * per_tile, keep, lane);
+    float th = -INFINITY;
+    if (valid >= j) warp_take_largest(keep, j, lane, [&](int, float m) { th = m; });
     return th;
 }
 
@@ -468,6 +483,80 @@ threshold_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tiles, i
     if (q >= B) return;
     const float th = warp_threshold(sample_buf, n_sample_tiles, B, q, j, per_tile, lane);
     if (lane == 0) theta[q] = th;
+}
+
+// Row shards, before the candidates pass: query q's kJ largest sampled
+// values (descending, -inf past the valid ones) go to rec[q kJ, (q+1) kJ)
+// and the shard's sampled rows, rows and mode (1: it takes the shared
+// threshold) to rec[B kJ + 0, 1, 2] as int bits -- the record that one
+// all-gather sends to every shard.  kJ >= every shard's own j, so the j-th
+// largest of the shards' union is among their records.
+static_assert(kShardJ == kJ, "the shard threshold record holds kJ values per query");
+__global__ void __launch_bounds__(kThrThreads)
+sample_record_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tiles, int32_t B, int32_t per_tile,
+                     int32_t sample_rows, int32_t rows, float* __restrict__ rec) {
+    const int q = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (q == 0 && lane == 0) {
+        int32_t* h = reinterpret_cast<int32_t*>(rec + (int64_t)B * kJ);
+        h[0] = sample_rows;
+        h[1] = rows;
+        h[2] = 1;
+    }
+    if (q >= B) return;
+    float keep[kThrKeep];
+    warp_keep_largest(
+        [&](int i) { return __ldcg(sample_buf + ((int64_t)(i / per_tile) * B + q) * per_tile + (i % per_tile)); },
+        n_sample_tiles * per_tile, keep, lane);
+    warp_take_largest(keep, kJ, lane, [&](int r, float m) { if (lane == 0) rec[(int64_t)q * kJ + r] = m; });
+}
+
+// Row shards: query q's threshold from every shard's record (rank-major,
+// `stride` floats each).  Over the shards of mode 1, mu = K x (sampled rows)
+// / (rows) and j = ceil(mu + 5 sqrt(mu) + 3) -- one store's rule applied to
+// the union of the samples -- and theta = the j-th largest of their values
+// (-inf when fewer exist).  Every shard computes the same value from the
+// same records.
+__global__ void __launch_bounds__(kThrThreads)
+union_threshold_kernel(const float* __restrict__ recs, int32_t world, int32_t stride, int32_t B, int32_t K,
+                       float* __restrict__ theta) {
+    const int q = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
+    const int lane = threadIdx.x & 31;
+    if (q >= B) return;
+    long long srows = 0, rows = 0;
+    for (int r = 0; r < world; ++r) {
+        const int32_t* h = reinterpret_cast<const int32_t*>(recs + (int64_t)r * stride + (int64_t)B * kJ);
+        if (__ldcg(h + 2) == 1) { srows += __ldcg(h + 0); rows += __ldcg(h + 1); }
+    }
+    const double mu = rows > 0 ? (double)K * (double)srows / (double)rows : 0.0;
+    const int j = max(1, min(kJ, (int)ceil(mu + 5.0 * sqrt(mu) + 3.0)));
+    float keep[kThrKeep];
+    const int valid = warp_keep_largest(
+        [&](int i) {
+            const int r = i / kJ;
+            const float* rec = recs + (int64_t)r * stride;
+            const int32_t mode = __ldcg(reinterpret_cast<const int32_t*>(rec + (int64_t)B * kJ) + 2);
+            return mode == 1 ? __ldcg(rec + (int64_t)q * kJ + (i - r * kJ)) : -INFINITY;
+        },
+        world * kJ, keep, lane);
+    float th = -INFINITY;
+    if (valid >= j) warp_take_largest(keep, j, lane, [&](int, float m) { th = m; });
+    if (lane == 0) theta[q] = th;
+}
+
+// Neutral shard records, for a shard whose call does not reach an exchange
+// with data of its own: no sampled values, mode 0 (threshold record);
+// counts 0, bounds -inf and the failure flag (bound record).
+__global__ void neutral_thr_kernel(float* __restrict__ rec, int32_t B) {
+    const int64_t n = (int64_t)B * kJ;
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n + 3; i += (int64_t)gridDim.x * blockDim.x)
+        rec[i] = i < n ? -INFINITY : 0.0f;   // 0.0f: the int 0 as bits
+}
+
+__global__ void neutral_rec_kernel(float* __restrict__ rec, int32_t B, float failed) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i <= 3 * (int64_t)B;
+         i += (int64_t)gridDim.x * blockDim.x)
+        rec[i] = i < B ? 0.0f : (i < 3 * (int64_t)B ? -INFINITY : failed);
 }
 
 // Exact rescoring of candidates: one block per query.
@@ -482,12 +571,19 @@ threshold_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tiles, i
 //  * Pruning: with theta2 the K-th largest lo_c, a candidate with
 //    hi_c < theta2 cannot enter the top-K, so only candidates with
 //    hi_c >= theta2 are rescored exactly (typically K plus a few).
-//  * Row shards: with bound_out the kernel stops after pass 1 and writes
-//    theta2 (-inf when the query is not certified).  K rows of this shard
-//    score at least theta2, so the largest theta2 over all shards is a lower
-//    bound of the global K-th score; a later launch with bound_in prunes with
-//    max(theta2, bound_in[q]) and keeps only rows that can still enter the
-//    global top-K (about K / shards + a few per shard instead of K + a few).
+//  * Row shards (the record layout is kShardRec*): pass 1 (bound_out) writes
+//    this shard's record and stops: the count of candidates with
+//    lo_c >= theta, the K-th largest lo_c (theta2) and the m-th largest lo_c
+//    (m = ceil(K / world); -inf where fewer exist).  With a threshold shared
+//    by every shard (shard_global) the counts add up: K candidates over all
+//    shards with lo_c >= theta certify every shard's short list; with this
+//    shard's own threshold its own count must reach K.  Pass 2 (bound_in,
+//    every shard's record) prunes with the largest of theta (once certified),
+//    every shard's theta2 (K rows of that shard score at least that much) and
+//    the smallest m-th bound (each of `world` shards has m rows above its
+//    own, world x m >= K rows in all): each is a lower bound of the global
+//    K-th score, so only rows that can still enter the global top-K are
+//    rescored (about K / world + a few per shard).
 // Both selections are block-wide bitonic sorts in shared memory ranked by
 // (score desc, id asc).
 constexpr int kSortCap = 4096;
@@ -520,6 +616,10 @@ __device__ __forceinline__ int pow2_at_least(int n) {
     return p;
 }
 
+// Rank by counting over at most this many lower bounds (shard pass 1):
+// every order statistic from one sweep, cheaper than radix passes.
+constexpr int kCountCap = 512;
+
 __global__ void __launch_bounds__(kRescoreThreads, 3)
 rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t B, float t_q,
                float lambda, int32_t use_imp, int32_t K, int32_t row_offset,
@@ -531,7 +631,8 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
                int32_t* __restrict__ out_cnt, int32_t* __restrict__ fallback,
                int32_t* __restrict__ rescored, const int32_t* __restrict__ bad,
                const int32_t* __restrict__ status, float* __restrict__ bound_out,
-               const float* __restrict__ bound_in, int32_t* __restrict__ status_mirror, int32_t max_batch) {
+               const float* __restrict__ bound_in, int32_t shard_world, int32_t shard_global,
+               int32_t* __restrict__ status_mirror, int32_t max_batch) {
     // The call's status words, [err, sync_err, fallback[], cand_cnt[],
     // rescored[], bad[]] (max_batch each), also go straight to the caller's
     // host-mapped mirror by the final pass (status_mirror != NULL), so no
@@ -550,18 +651,23 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     __shared__ int     s_ge, s_n2, s_nk;
     __shared__ float   s_wv[kRescoreThreads];      // K <= 32: each warp's K best lower bounds
     __shared__ int32_t s_wi[kRescoreThreads];
-    __shared__ float   s_th2;
-    __shared__ int     s_hist[2048];
+    __shared__ float   s_th2, s_mth;
+    __shared__ __align__(16) int s_hist[2048];   // also read as 64-bit keys
     __shared__ uint32_t s_sel[2];
     const int qi = blockIdx.x;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int kWarps = kRescoreThreads / 32;
-    if (bound_out != nullptr && threadIdx.x == 0) {
-        bound_out[qi] = -INFINITY;   // until certified
-        // element B: 1 when this shard's call failed (its results are not served)
-        if (qi == 0) bound_out[gridDim.x] = (status[0] != 0 || status[1] != 0) ? 1.0f : 0.0f;
+    const bool call_failed = status[0] != 0 || status[1] != 0;
+    const bool shard_pass1 = bound_out != nullptr;
+    if (shard_pass1 && threadIdx.x == 0) {
+        // this shard's record, neutral until pass 1 fills it in
+        reinterpret_cast<int32_t*>(bound_out)[qi] = 0;
+        bound_out[B + qi] = -INFINITY;
+        bound_out[2 * B + qi] = -INFINITY;
+        // the flag: 1 when this shard's call failed (no result is served)
+        if (qi == 0) bound_out[3 * B] = call_failed ? 1.0f : 0.0f;
     }
-    if (status[0] != 0 || status[1] != 0) {
+    if (call_failed) {
         // a bounded wait of this call's GEMM gave up: the short lists and the
         // thresholds may be incomplete, so no result of the call is served
         for (int p = threadIdx.x; p < K; p += kRescoreThreads) {
@@ -569,18 +675,22 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
             out_ids[(int64_t)qi * K + p] = -1;
         }
         if (threadIdx.x == 0) { if (out_cnt) out_cnt[qi] = -1; fallback[qi] = 0; rescored[qi] = 0; }
-        if (bound_out == nullptr) publish(0, 0);
+        if (!shard_pass1) publish(0, 0);
         return;
     }
     const int ncand = cand_cnt[qi];
     const int nc_ = min(ncand, cap);
     if (threadIdx.x == 0) { s_ge = 0; s_n2 = 0; }
     __syncthreads();
-    if (ncand > kSortCap || nc_ < K || (bad != nullptr && bad[qi] != 0)) {
-        // too many candidates to sort here, too few to be complete, or a
-        // query outside the fp16 range (its short list is meaningless)
+    // Too many candidates to sort here, or a query outside the fp16 range
+    // (its short list is meaningless): the exact scan answers it.  Fewer
+    // than K candidates only rule out a threshold of this shard's own; with
+    // a shared one the count over all shards decides.
+    const bool unsortable = ncand > kSortCap || (bad != nullptr && bad[qi] != 0);
+    if (unsortable || (nc_ < K && shard_global == 0)) {
+        if (shard_pass1) return;   // the record stays neutral
         if (threadIdx.x == 0) { fallback[qi] = 1; rescored[qi] = 0; if (out_cnt) out_cnt[qi] = 0; }
-        if (bound_out == nullptr) publish(1, 0);
+        publish(1, 0);
         return;
     }
     const float th = theta[qi];
@@ -589,13 +699,12 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     const float* cs = cand_s + (int64_t)qi * cap;   // slack: the exact score lies in cf -+ cs
 
     // ---- pass 1: lower bounds, completeness, K-th largest lower bound -------
-    // K <= 32: every warp keeps its K best lower bounds (ranked by value, then
-    // candidate index) and warp 0 merges the eight lists; larger K: a radix
-    // selection over all of them.  Either way th2 is the K-th largest.
-    // Shard pass 2 (bound_in): the exchanged bound is the maximum of every
-    // shard's certified K-th lower bound, this shard's included, so it
-    // replaces the local selection; only the completeness count runs.
-    const bool need_th2 = bound_in == nullptr;
+    // Unsharded, K <= 32: every warp keeps its K best lower bounds (ranked by
+    // value, then candidate index) and warp 0 merges the eight lists; larger
+    // K: a radix selection over all of them.  Either way th2 is the K-th
+    // largest.  Shard pass 1 writes the record; shard pass 2 takes its
+    // bound from every shard's record, so only the count runs here.
+    const bool need_th2 = bound_in == nullptr && !shard_pass1;
     const bool warp_lists = need_th2 && K <= 32;
     WarpTopK<1> top;
     top.init(warp_lists ? K : 1);
@@ -606,34 +715,81 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         const float lo = in ? cf[i] - cs[i] : -INFINITY;
         ge += (in && lo >= th) ? 1 : 0;
         if (warp_lists) top.offer_lanes(lo, i, in, lane);
-        else if (need_th2 && in) s_key[i] = lo;
+        else if ((need_th2 || shard_pass1) && in) s_key[i] = lo;
     }
     ge = warp_reduce_sum_int(ge);
     if (lane == 0) atomicAdd(&s_ge, ge);
     if (warp_lists) top.store(s_wv + warp * 32, s_wi + warp * 32, lane);
     __syncthreads();
-    if (s_ge < K) {
-        if (threadIdx.x == 0) { fallback[qi] = 1; rescored[qi] = 0; if (out_cnt) out_cnt[qi] = 0; }
-        if (bound_out == nullptr) publish(1, 0);
+    if (shard_pass1) {
+        // the K-th and the m-th largest lower bounds of this shard
+        const int m = (K + shard_world - 1) / shard_world;
+        float kth = -INFINITY, mth = -INFINITY;
+        if (nc_ <= kCountCap) {
+            // candidate i's rank = the lower bounds above it (ties by index)
+            if (threadIdx.x == 0) { s_th2 = -INFINITY; s_mth = -INFINITY; }
+            __syncthreads();
+            for (int i = threadIdx.x; i < nc_; i += kRescoreThreads) {
+                const float v = s_key[i];
+                int r = 0;
+                for (int t = 0; t < nc_; ++t) {
+                    const float u = s_key[t];
+                    r += (u > v || (u == v && t < i)) ? 1 : 0;
+                }
+                if (r == K - 1) s_th2 = v;
+                if (r == m - 1) s_mth = v;
+            }
+            __syncthreads();
+            kth = s_th2;
+            mth = s_mth;
+        } else {
+            auto key = [&](int i) { return f2key(s_key[i]); };
+            if (nc_ >= K) kth = key2f(block_kth_largest_key<kRescoreThreads>(key, nc_, K, s_hist, s_sel));
+            mth = m == K ? kth : key2f(block_kth_largest_key<kRescoreThreads>(key, nc_, m, s_hist, s_sel));
+        }
+        if (threadIdx.x == 0) {
+            reinterpret_cast<int32_t*>(bound_out)[qi] = shard_global ? s_ge : 0;
+            bound_out[B + qi] = kth;
+            bound_out[2 * B + qi] = mth;
+        }
         return;
     }
     float th2;
-    if (!need_th2) {
-        th2 = __ldcg(bound_in + qi);
-    } else if (warp_lists) {
-        if (warp == 0) {
-            for (int ww = 1; ww < kWarps; ++ww) top.merge_sorted32(s_wv + ww * 32, s_wi + ww * 32, K, lane);
-            if (lane == 0) s_th2 = top.thr_v;
+    bool certified;
+    if (bound_in != nullptr) {
+        // every shard's record (rank-major): the completeness count and the
+        // pruning bound, the same on every shard
+        long long total = 0;
+        float best = -INFINITY, mmin = INFINITY;
+        const int64_t stride = 3 * (int64_t)B + 1;
+        for (int r = 0; r < shard_world; ++r) {
+            const float* rec = bound_in + r * stride;
+            total += __ldcg(reinterpret_cast<const int32_t*>(rec) + qi);
+            best = fmaxf(best, __ldcg(rec + B + qi));
+            mmin = fminf(mmin, __ldcg(rec + 2 * B + qi));
         }
-        __syncthreads();
-        th2 = s_th2;
+        certified = shard_global ? total >= K : s_ge >= K;
+        th2 = fmaxf(fmaxf(best, mmin), th);
     } else {
-        th2 = key2f(block_kth_largest_key<kRescoreThreads>(
-            [&](int i) { return f2key(s_key[i]); }, nc_, K, s_hist, s_sel));
+        certified = s_ge >= K;
     }
-    if (bound_out != nullptr) {      // shard pass 1: this shard's certified bound only
-        if (threadIdx.x == 0) bound_out[qi] = th2;
+    if (!certified) {
+        if (threadIdx.x == 0) { fallback[qi] = 1; rescored[qi] = 0; if (out_cnt) out_cnt[qi] = 0; }
+        publish(1, 0);
         return;
+    }
+    if (bound_in == nullptr) {
+        if (warp_lists) {
+            if (warp == 0) {
+                for (int ww = 1; ww < kWarps; ++ww) top.merge_sorted32(s_wv + ww * 32, s_wi + ww * 32, K, lane);
+                if (lane == 0) s_th2 = top.thr_v;
+            }
+            __syncthreads();
+            th2 = s_th2;
+        } else {
+            th2 = key2f(block_kth_largest_key<kRescoreThreads>(
+                [&](int i) { return f2key(s_key[i]); }, nc_, K, s_hist, s_sel));
+        }
     }
 
     // ---- pass 2: exact scores of the candidates that can still place -------
@@ -662,6 +818,14 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     }
     __syncthreads();
     const int nk = min(s_nk, kRowsCap);
+    // each warp requests its next two rows into L2 (one bulk prefetch each)
+    // while it scores the current one: three of its rows travel at a time
+    // instead of one, and L2 holds only rows about to be read
+    const uint32_t row_bytes = (uint32_t)s.nc * 16u;
+    auto prefetch_row = [&](int t) {
+        if (lane == 0 && t < nk)
+            prefetch_l2_bulk(reinterpret_cast<const float4*>(s.E) + (int64_t)s_rows[t] * s.pitch4, row_bytes);
+    };
     auto score_row = [&](int32_t rr) {
         const float4* row = reinterpret_cast<const float4*>(s.E) + (int64_t)rr * s.pitch4;
         const float dot = warp_dot_canonical(row, q4, s.nc, lane);
@@ -673,7 +837,11 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
             s_id[pos] = rr + row_offset;
         }
     };
-    for (int t = warp; t < nk; t += kWarps) score_row(s_rows[t]);
+    prefetch_row(warp + kWarps);
+    for (int t = warp; t < nk; t += kWarps) {
+        prefetch_row(t + 2 * kWarps);
+        score_row(s_rows[t]);
+    }
     if (s_nk > kRowsCap) {
         // more rows than the list holds: the rest in candidate order
         __syncthreads();
@@ -1168,7 +1336,6 @@ struct mars_batch_ctx {
     cudaStream_t stream = nullptr;
     float* d_margin = nullptr;       // max_batch
     float* d_theta = nullptr;
-    float* d_bound = nullptr;        // max_batch + 1: certified K-th lower bounds and a failure flag (row shards)
     int32_t* d_cand = nullptr;       // max_batch * cap
     float* d_cand_f = nullptr;       // max_batch * cap
     // the call's status words, one block read back with one copy:
@@ -1311,7 +1478,6 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     T(cudaEventCreate(&c->ev_gemm[1]), "event");
     T(cudaMalloc(&c->d_margin, (size_t)max_batch * 4), "margins");
     T(cudaMalloc(&c->d_theta, (size_t)max_batch * 4), "thresholds");
-    T(cudaMalloc(&c->d_bound, ((size_t)max_batch + 1) * 4), "shard bounds + failure flag");
     T(cudaMalloc(&c->d_cand, (size_t)max_batch * c->cap * 4), "candidates");
     T(cudaMalloc(&c->d_cand_f, (size_t)max_batch * c->cap * 8), "candidate scores and slacks");
     const size_t status_words = 2 + 4 * (size_t)max_batch;
@@ -1384,7 +1550,7 @@ int mars_batch_ctx_destroy(mars_batch_ctx* c) {
     if (c == nullptr) return MARS_OK;
     MarsDeviceGuard g(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
-    cudaFree(c->d_margin); cudaFree(c->d_theta); cudaFree(c->d_bound); cudaFree(c->d_cand);
+    cudaFree(c->d_margin); cudaFree(c->d_theta); cudaFree(c->d_cand);
     cudaFree(c->d_cand_f); cudaFree(c->d_sample); cudaFree(c->d_sample_rt);
     cudaFree(c->d_status); cudaFreeHost(c->h_status);
     cudaFree(c->d_q16);
@@ -1497,6 +1663,18 @@ int mars::batch_topk_sharded(const mars_store* s, mars_batch_ctx* c, const float
     return batch_topk_pass(s, c, d_queries, query_pitch, B, t_q, lambda, modality_filter, use_importance, K,
                            row_offset, -1, d_ids, d_vals, d_counts, stream, c != nullptr && c->precision == 0,
                            xchg);
+}
+
+int mars::shard_neutral_thr(float* d_rec, int32_t B, cudaStream_t st) {
+    neutral_thr_kernel<<<(shard_thr_floats(B) + 255) / 256, 256, 0, st>>>(d_rec, B);
+    MARS_CUDA_TRY(cudaGetLastError());
+    return MARS_OK;
+}
+
+int mars::shard_neutral_rec(float* d_rec, int32_t B, bool failed, cudaStream_t st) {
+    neutral_rec_kernel<<<(shard_rec_floats(B) + 255) / 256, 256, 0, st>>>(d_rec, B, failed ? 1.0f : 0.0f);
+    MARS_CUDA_TRY(cudaGetLastError());
+    return MARS_OK;
 }
 
 int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queries, int32_t query_pitch,
@@ -1617,6 +1795,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     }
     const CUtensorMap& mq = c->map_q.map;
     const CUtensorMap& me = c->map_e.map;
+    bool shard_global = false;   // row shards: the threshold came from every shard's sample
 
     RowMeta meta{};
     meta.ts = s->d_ts;
@@ -1718,9 +1897,25 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         else
             gemm_kernel<kSample, false><<<std::min(ga.n_tiles, c->num_sms), kGemmThreads, kGemmSmem, st>>>(mq, me, ga);
         MARS_CUDA_TRY(cudaGetLastError());
-        // 3. thresholds
-        threshold_kernel<<<(B * 32 + kThrThreads - 1) / kThrThreads, kThrThreads, 0, st>>>(
-            c->d_sample, n_sample, B, j, per_tile, c->d_theta);   // 2 kJ values per tile and query
+        // 3. thresholds (2 kJ values per tile and query)
+        const int thr_grid = (B * 32 + kThrThreads - 1) / kThrThreads;
+        if (xchg != nullptr) {
+            // row shards: every shard's kJ best sampled bounds per query, one
+            // all-gather, and the same threshold on every shard from their
+            // union (a sample of the whole corpus, so each shard short-lists
+            // about 1 / world of the rows it would list on its own)
+            sample_record_kernel<<<thr_grid, kThrThreads, 0, st>>>(
+                c->d_sample, n_sample, B, per_tile, (int32_t)std::min<int64_t>((int64_t)n_sample * kBN, n), n,
+                xchg->send[0]);
+            MARS_CUDA_TRY(cudaGetLastError());
+            xchg->theta_done = true;
+            MARS_TRY(xchg->gather(xchg->arg, 0, shard_thr_floats(B), st));
+            union_threshold_kernel<<<thr_grid, kThrThreads, 0, st>>>(xchg->recv[0], xchg->world,
+                                                                     shard_thr_floats(B), B, K, c->d_theta);
+            shard_global = true;
+        } else {
+            threshold_kernel<<<thr_grid, kThrThreads, 0, st>>>(c->d_sample, n_sample, B, j, per_tile, c->d_theta);
+        }
         MARS_CUDA_TRY(cudaGetLastError());
         // 4. candidates
         ga.n_tiles = rtiles * qtiles;
@@ -1745,16 +1940,24 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
                                                       c->d_cand_cnt, c->cap, d_ids, d_vals, d_counts,
                                                       c->d_fallback, c->d_rescored, f16 ? c->d_bad : nullptr,
                                                       c->d_status, bound_out, bound_in,
+                                                      xchg != nullptr ? xchg->world : 1, shard_global ? 1 : 0,
                                                       bound_out == nullptr ? c->dm_status : nullptr, c->max_batch);
         return cudaGetLastError();
     };
     if (xchg != nullptr) {
-        // row shards: certified bounds, their maximum over the shards, then
-        // the rescore against it
-        MARS_CUDA_TRY(rescore(c->d_bound, nullptr));
+        // row shards: a small batch took its thresholds inside the fused
+        // launch (its own shard's), so it joins the threshold exchange with a
+        // neutral record; then every shard's bound record, one all-gather,
+        // and the rescore against all of them
+        if (!xchg->theta_done) {
+            MARS_TRY(shard_neutral_thr(xchg->send[0], B, st));
+            xchg->theta_done = true;
+            MARS_TRY(xchg->gather(xchg->arg, 0, shard_thr_floats(B), st));
+        }
+        MARS_CUDA_TRY(rescore(xchg->send[1], nullptr));
         xchg->done = true;
-        MARS_TRY(xchg->fn(xchg->arg, c->d_bound, B, st));
-        MARS_CUDA_TRY(rescore(nullptr, c->d_bound));
+        MARS_TRY(xchg->gather(xchg->arg, 1, shard_rec_floats(B), st));
+        MARS_CUDA_TRY(rescore(nullptr, xchg->recv[1]));
     } else {
         MARS_CUDA_TRY(rescore(nullptr, nullptr));
     }

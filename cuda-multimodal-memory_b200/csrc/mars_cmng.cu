@@ -199,6 +199,7 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int bw = a.beam;
     const uint32_t mask = (uint32_t)a.hash_size - 1u;
+    const uint32_t row_bytes = (uint32_t)((a.D + 3) & ~3) * 4u;   // rows are float4 aligned
 
     for (int qi = blockIdx.x; qi < a.nq; qi += gridDim.x) {
         // the beam and its merged successor swap roles every iteration
@@ -246,8 +247,16 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
             if (parent < 0) break;
             ++iters;
             const int32_t* nb = a.nbrs + (int64_t)parent * a.degree;
-            // candidate slots: valid id, not visited, first occurrence in the list
-            for (int j = tid; j < a.degree; j += kThreads) s_nb[j] = __ldg(nb + j);
+            // candidate slots: valid id, not visited, first occurrence in the
+            // list.  Each neighbour's row is requested into L2 as its id
+            // arrives, so the rows travel during the visited checks and the
+            // warps' dot products below (about degree / 8 rows per warp, one
+            // after another) wait on L2 instead of one DRAM trip per row.
+            for (int j = tid; j < a.degree; j += kThreads) {
+                const int32_t v = __ldg(nb + j);
+                s_nb[j] = v;
+                if (v >= 0 && v < a.N) prefetch_l2_bulk(a.E + (int64_t)v * a.pitch, row_bytes);
+            }
             __syncthreads();
             for (int j = tid; j < a.degree; j += kThreads) {
                 const int32_t v = s_nb[j];
@@ -281,7 +290,14 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
                     pos += (dk > -FLT_MAX * 0.5f && (dk > d || (dk == d && k < j))) ? 1 : 0;
                 }
                 for (int o = 0; o < bw; ++o) pos += (bs[o] >= d) ? 1 : 0;
-                if (pos < bw) { nbs[pos] = d; nbi[pos] = s_nb[j]; }
+                if (pos < bw) {
+                    nbs[pos] = d;
+                    nbi[pos] = s_nb[j];
+                    // a later iteration may expand this position: its
+                    // neighbour list is requested into L2 now
+                    if (pos > it && pos < a.max_iter)
+                        prefetch_l2_span(a.nbrs + (int64_t)s_nb[j] * a.degree, (uint32_t)a.degree * 4u);
+                }
             }
             __syncthreads();
             // the merged beam is the beam of the next iteration
@@ -396,6 +412,11 @@ struct BfsArgs2 {
     int32_t* out_cnt;
     int32_t* out_visited;         // nq (may be null)
     int* err;
+    // queries that the shared-memory kernel could not hold: it appends them,
+    // the global-table kernel then answers only those (NULL: every query)
+    int32_t* redo;
+    int32_t* redo_cnt;
+    int32_t smem_nodes;           // visited nodes the shared table takes per query
 };
 
 __device__ __forceinline__ int table_find_or_claim(unsigned long long* tags, uint32_t mask, uint32_t epoch,
@@ -423,6 +444,57 @@ __device__ __forceinline__ float bfs_own_score(const BfsArgs2& a, const float4* 
     return f;
 }
 
+// The top-K of a query's visited nodes (list / lscore, `total` of them) by
+// (score desc, id asc) into the outputs: per-warp ranked lists merged by warp
+// 0; hop_of(u) gives a listed node's level.
+template <int KPL, class HopOf>
+__device__ __forceinline__ void bfs_emit_topk(const BfsArgs2& a, int qi, const int32_t* list, const float* lscore,
+                                              int total, float (*s_val)[kMaxTopK], int32_t (*s_idx)[kMaxTopK],
+                                              HopOf hop_of) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    WarpTopK<KPL> top;
+    top.init(a.K);
+    for (int base = warp * 32; base < total; base += kThreads) {
+        const int j = base + lane;
+        float sv = -INFINITY;
+        int32_t id = INT32_MAX;
+        if (j < total) { sv = lscore[j]; id = list[j]; }
+        top.offer_lanes(sv, id, j < total, lane);
+    }
+    top.store(s_val[warp], s_idx[warp], lane);
+    __syncthreads();
+    if (warp == 0) {
+        for (int w = 1; w < kWarps; ++w) top.offer_sorted(s_val[w], s_idx[w], a.K, lane);
+        int cnt = 0;
+#pragma unroll
+        for (int sl = 0; sl < KPL; ++sl) {
+            const int p = sl * 32 + lane;
+            const bool valid = p < a.K && top.i[sl] != INT32_MAX;
+            cnt += __popc(__ballot_sync(0xffffffffu, valid));
+            if (p < a.K) {
+                const int64_t o = (int64_t)qi * a.K + p;
+                if (valid) {
+                    const int32_t u = top.i[sl];
+                    a.out_ids[o] = u;
+                    a.out_scores[o] = top.v[sl];
+                    if (a.out_mods) a.out_mods[o] = __ldg(a.mod + u);
+                    if (a.out_hops) a.out_hops[o] = hop_of(u);
+                } else {
+                    a.out_ids[o] = -1;
+                    a.out_scores[o] = -INFINITY;
+                    if (a.out_mods) a.out_mods[o] = -1;
+                    if (a.out_hops) a.out_hops[o] = -1;
+                }
+            }
+        }
+        if (lane == 0) {
+            a.out_cnt[qi] = cnt;
+            if (a.out_visited) a.out_visited[qi] = total;
+        }
+    }
+    __syncthreads();
+}
+
 template <int KPL>
 __global__ void __launch_bounds__(kThreads, 3) bfs_kernel(const BfsArgs2 a) {
     __shared__ int s_lvl[16];       // level offsets; [15] = tail
@@ -436,7 +508,9 @@ __global__ void __launch_bounds__(kThreads, 3) bfs_kernel(const BfsArgs2 a) {
     float* lscore = reinterpret_cast<float*>(list + a.vcap / 2);   // second half: scores
     const int vcap = a.vcap / 2;
 
-    for (int qi = blockIdx.x; qi < a.nq; qi += gridDim.x) {
+    const int nwork = a.redo != nullptr ? __ldcg(a.redo_cnt) : a.nq;
+    for (int wi = blockIdx.x; wi < nwork; wi += gridDim.x) {
+        const int qi = a.redo != nullptr ? __ldcg(a.redo + wi) : wi;
         uint32_t epoch = 0;
         if (tid == 0) {
             epoch = a.epochs[blockIdx.x] + 1;
@@ -507,51 +581,140 @@ __global__ void __launch_bounds__(kThreads, 3) bfs_kernel(const BfsArgs2 a) {
             __syncthreads();
         }
         if (overflow) atomicCAS(a.err, 0, 7);
-        // ---- top-K of every visited node ----
-        const int total = min(s_lvl[15], vcap);
-        WarpTopK<KPL> top;
-        top.init(a.K);
-        for (int base = warp * 32; base < total; base += kThreads) {
-            const int j = base + lane;
-            float sv = -INFINITY;
-            int32_t id = INT32_MAX;
-            if (j < total) { sv = lscore[j]; id = list[j]; }
-            top.offer_lanes(sv, id, j < total, lane);
+        bfs_emit_topk<KPL>(a, qi, list, lscore, min(s_lvl[15], vcap), s_val, s_idx, [&](int32_t u) {
+            const int slot = table_find_or_claim(tags, mask, epoch, u);
+            return 15 - (int)((uint32_t)(__ldcg(states + slot) >> 32) & 15u);
+        });
+    }
+}
+
+// The same BFS with the visited set in shared memory: a table of kBfsSlots
+// node ids and states per block (cleared per query), at most smem_nodes
+// visited nodes per query (half the table or less).  The state word and the
+// rule are the global kernel's -- ((1 << 4 | (15 - level)) << 32) | key(best
+// parent score), one atomicMax both claims a node for a level and keeps its
+// best parent -- and the answer does not depend on the order of the claims.
+// Per level the own scores come first (a warp per node; the node's slot was
+// kept when it was listed), then every (node, edge) pair of the level is
+// handed to its own thread, so a level's claims are shared-memory atomics
+// spread over the whole block.  A query that outgrows the table is appended
+// to a.redo for the global-table kernel.
+constexpr int kBfsSlots = 4096;
+constexpr uint32_t kEmptyTag = 0xffffffffu;
+constexpr size_t kBfsSmemBytes = (size_t)kBfsSlots * (4 + 8) + (size_t)(kBfsSlots / 2) * 2;
+
+// The slot of v (claimed when absent), -1 when the table is full.
+__device__ __forceinline__ int smem_claim(uint32_t* tag, int32_t v) {
+    uint32_t s = hash32(v) & (uint32_t)(kBfsSlots - 1);
+    for (int probe = 0; probe < kBfsSlots; ++probe) {
+        const uint32_t cur = *reinterpret_cast<volatile uint32_t*>(tag + s);
+        if (cur == (uint32_t)v) return (int)s;
+        if (cur == kEmptyTag) {
+            const uint32_t old = atomicCAS(tag + s, kEmptyTag, (uint32_t)v);
+            if (old == kEmptyTag || old == (uint32_t)v) return (int)s;
         }
-        top.store(s_val[warp], s_idx[warp], lane);
+        s = (s + 1) & (uint32_t)(kBfsSlots - 1);
+    }
+    return -1;
+}
+
+__device__ __forceinline__ int smem_find(const uint32_t* tag, int32_t v) {
+    uint32_t s = hash32(v) & (uint32_t)(kBfsSlots - 1);
+    for (int probe = 0; probe < kBfsSlots; ++probe) {
+        const uint32_t cur = tag[s];
+        if (cur == (uint32_t)v) return (int)s;
+        if (cur == kEmptyTag) return -1;
+        s = (s + 1) & (uint32_t)(kBfsSlots - 1);
+    }
+    return -1;
+}
+
+template <int KPL>
+__global__ void __launch_bounds__(kThreads, 3) bfs_smem_kernel(const BfsArgs2 a) {
+    extern __shared__ __align__(16) uint8_t bfs_smem[];
+    unsigned long long* s_state = reinterpret_cast<unsigned long long*>(bfs_smem);
+    uint32_t* s_tag = reinterpret_cast<uint32_t*>(s_state + kBfsSlots);
+    uint16_t* s_lslot = reinterpret_cast<uint16_t*>(s_tag + kBfsSlots);   // the slot of each listed node
+    __shared__ int s_lvl[16];
+    __shared__ int s_tail, s_ovf;
+    __shared__ float   s_val[kWarps][kMaxTopK];
+    __shared__ int32_t s_idx[kWarps][kMaxTopK];
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int32_t* list = a.lists + (int64_t)blockIdx.x * a.vcap;
+    float* lscore = reinterpret_cast<float*>(list + a.vcap / 2);
+    const int limit = min(a.smem_nodes, a.vcap / 2);
+
+    for (int qi = blockIdx.x; qi < a.nq; qi += gridDim.x) {
+        for (int i = tid; i < kBfsSlots; i += kThreads) { s_tag[i] = kEmptyTag; s_state[i] = 0ull; }
+        if (tid == 0) { s_tail = 0; s_ovf = 0; s_lvl[0] = 0; }
         __syncthreads();
-        if (warp == 0) {
-            for (int w = 1; w < kWarps; ++w) top.offer_sorted(s_val[w], s_idx[w], a.K, lane);
-            int cnt = 0;
-#pragma unroll
-            for (int sl = 0; sl < KPL; ++sl) {
-                const int p = sl * 32 + lane;
-                const bool valid = p < a.K && top.i[sl] != INT32_MAX;
-                cnt += __popc(__ballot_sync(0xffffffffu, valid));
-                if (p < a.K) {
-                    const int64_t o = (int64_t)qi * a.K + p;
-                    if (valid) {
-                        const int32_t u = top.i[sl];
-                        const int slot = table_find_or_claim(tags, mask, epoch, u);
-                        const uint32_t stamp = (uint32_t)(__ldcg(states + slot) >> 32);
-                        a.out_ids[o] = u;
-                        a.out_scores[o] = top.v[sl];
-                        if (a.out_mods) a.out_mods[o] = __ldg(a.mod + u);
-                        if (a.out_hops) a.out_hops[o] = 15 - (int)(stamp & 15u);
-                    } else {
-                        a.out_ids[o] = -1;
-                        a.out_scores[o] = -INFINITY;
-                        if (a.out_mods) a.out_mods[o] = -1;
-                        if (a.out_hops) a.out_hops[o] = -1;
-                    }
+        const float4* q4 = reinterpret_cast<const float4*>(a.Q + (int64_t)qi * a.qpitch);
+        // ---- level 0: the seeds with their beam scores, one thread each ----
+        const int ns = min(a.seed_cnt[qi], a.seed_stride);
+        const unsigned long long st0 = (unsigned long long)((1u << 4) | 15u) << 32;
+        for (int i = tid; i < ns; i += kThreads) {
+            const int32_t u = a.seed_ids[(int64_t)qi * a.seed_stride + i];
+            if (u < 0 || u >= a.N) continue;
+            const int slot = smem_claim(s_tag, u);
+            if (slot < 0) { s_ovf = 1; continue; }
+            const unsigned long long old = atomicMax(s_state + slot,
+                                                     st0 | f2key(a.seed_scores[(int64_t)qi * a.seed_stride + i]));
+            if ((old >> 32) == 0ull) {
+                const int pos = atomicAdd(&s_tail, 1);
+                if (pos < limit) { list[pos] = u; s_lslot[pos] = (uint16_t)slot; } else { s_ovf = 1; }
+            }
+        }
+        __syncthreads();
+        if (tid == 0) s_lvl[1] = min(s_tail, limit);
+        __syncthreads();
+        for (int h = 0; h <= a.hops; ++h) {
+            if (s_ovf != 0) break;                 // read after a barrier: the same on every thread
+            const int beg = s_lvl[h], end = s_lvl[h + 1];
+            // the level's scores: seeds keep their beam score (the state's
+            // key), later levels max(best parent x decay, own x 0.8)
+            if (h == 0) {
+                for (int idx = beg + tid; idx < end; idx += kThreads)
+                    lscore[idx] = key2f((uint32_t)(s_state[s_lslot[idx]] & 0xffffffffull));
+            } else {
+                for (int idx = beg + warp; idx < end; idx += kWarps) {
+                    const float own = bfs_own_score(a, q4, list[idx], lane);
+                    const float best = key2f((uint32_t)(s_state[s_lslot[idx]] & 0xffffffffull));
+                    if (lane == 0) lscore[idx] = fmaxf(best, own * 0.8f);
                 }
             }
-            if (lane == 0) {
-                a.out_cnt[qi] = cnt;
-                if (a.out_visited) a.out_visited[qi] = total;
+            if (h == a.hops) break;                // last level: scored, not expanded
+            __syncthreads();
+            const unsigned long long nst = (unsigned long long)((1u << 4) | (uint32_t)(15 - (h + 1))) << 32;
+            const int total = (end - beg) * a.degree;
+            for (int p = tid; p < total; p += kThreads) {
+                const int k = p / a.degree;
+                const int idx = beg + k;
+                const int32_t v = __ldg(a.nbrs + (int64_t)list[idx] * a.degree + (p - k * a.degree));
+                if (v < 0 || v >= a.N) continue;
+                const int slot = smem_claim(s_tag, v);
+                if (slot < 0) { s_ovf = 1; continue; }
+                const unsigned long long old = atomicMax(s_state + slot, nst | f2key(lscore[idx] * a.hop_decay));
+                if ((old >> 32) == 0ull) {
+                    const int pos = atomicAdd(&s_tail, 1);
+                    if (pos < limit) { list[pos] = v; s_lslot[pos] = (uint16_t)slot; } else { s_ovf = 1; }
+                }
             }
+            __syncthreads();
+            if (tid == 0 && h + 2 < 15) s_lvl[h + 2] = min(s_tail, limit);
+            __syncthreads();
         }
         __syncthreads();
+        const bool ovf = s_ovf != 0;
+        const int visited = min(s_tail, limit);
+        __syncthreads();                           // every thread has read the flag before the next query resets it
+        if (ovf) {
+            if (tid == 0) a.redo[atomicAdd(a.redo_cnt, 1)] = qi;
+            continue;
+        }
+        bfs_emit_topk<KPL>(a, qi, list, lscore, visited, s_val, s_idx, [&](int32_t u) {
+            const int slot = smem_find(s_tag, u);
+            return slot < 0 ? -1 : 15 - (int)((uint32_t)(s_state[slot] >> 32) & 15u);
+        });
     }
 }
 
@@ -755,6 +918,8 @@ struct mars_cmng_ctx {
     int32_t* d_lists = nullptr;
     uint32_t* d_epochs = nullptr;
     int* d_err = nullptr;
+    int32_t* d_redo = nullptr;           // max_queries + 1: queries for the global-table BFS, their count
+    int32_t smem_nodes = kBfsSlots / 2;  // visited nodes per query in the shared-memory BFS (0: never)
 };
 
 extern "C" {
@@ -796,10 +961,26 @@ int mars_cmng_ctx_create(int32_t device, int32_t max_queries, int32_t K, int32_t
     T(cudaMalloc(&c->d_lists, (size_t)c->grid * c->vcap * 4), "level lists");
     T(cudaMalloc(&c->d_epochs, (size_t)c->grid * 4), "epochs");
     T(cudaMalloc(&c->d_err, sizeof(int)), "error word");
+    T(cudaMalloc(&c->d_redo, ((size_t)max_queries + 1) * 4), "BFS redo list");
+    if (rc == MARS_OK) {
+        T(cudaFuncSetAttribute(bfs_smem_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBfsSmemBytes), "attribute");
+        T(cudaFuncSetAttribute(bfs_smem_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBfsSmemBytes), "attribute");
+        T(cudaFuncSetAttribute(bfs_smem_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBfsSmemBytes), "attribute");
+        T(cudaFuncSetAttribute(bfs_smem_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBfsSmemBytes), "attribute");
+    }
     if (rc == MARS_OK) T(cudaMemset(c->d_epochs, 0, (size_t)c->grid * 4), "memset");
     if (rc == MARS_OK) T(cudaMemset(c->d_err, 0, sizeof(int)), "memset");
     if (rc != MARS_OK) { mars_cmng_ctx_destroy(c); return rc; }
     *out = c;
+    return MARS_OK;
+}
+
+int mars_cmng_ctx_set_bfs_smem_nodes(mars_cmng_ctx* c, int32_t max_nodes) {
+    if (c == nullptr) return fail(MARS_ERR_INVALID, "mars_cmng_ctx_set_bfs_smem_nodes: NULL context");
+    if (max_nodes < 0 || max_nodes > kBfsSlots / 2)
+        return fail(MARS_ERR_INVALID, "mars_cmng_ctx_set_bfs_smem_nodes: need 0 <= max_nodes <= " +
+                                          std::to_string(kBfsSlots / 2));
+    c->smem_nodes = max_nodes;
     return MARS_OK;
 }
 
@@ -809,6 +990,7 @@ int mars_cmng_ctx_destroy(mars_cmng_ctx* c) {
     cudaFree(c->d_seed_ids); cudaFree(c->d_seed_scores); cudaFree(c->d_seed_cnt);
     cudaFree(c->d_tags); cudaFree(c->d_states); cudaFree(c->d_lists); cudaFree(c->d_epochs);
     cudaFree(c->d_err);
+    cudaFree(c->d_redo);
     delete c;
     return MARS_OK;
 }
@@ -869,10 +1051,24 @@ int mars_cmng_search_bfs_batch(const mars_store* s, mars_cmng_ctx* c, const int3
     a.out_visited = d_visited;
     a.err = c->d_err;
     const int grid = std::min(c->grid, nq);
-    if (cfg->K <= 32) bfs_kernel<1><<<grid, kThreads, 0, st>>>(a);
-    else if (cfg->K <= 64) bfs_kernel<2><<<grid, kThreads, 0, st>>>(a);
-    else if (cfg->K <= 128) bfs_kernel<4><<<grid, kThreads, 0, st>>>(a);
-    else bfs_kernel<8><<<grid, kThreads, 0, st>>>(a);
+    auto launch = [&](auto kfn, size_t smem) { kfn<<<grid, kThreads, smem, st>>>(a); };
+    if (c->smem_nodes > 0) {
+        // shared-memory visited tables first; the queries that outgrow them
+        // go to the global-table kernel, which answers only those
+        a.redo = c->d_redo;
+        a.redo_cnt = c->d_redo + c->max_queries;
+        a.smem_nodes = c->smem_nodes;
+        MARS_CUDA_TRY(cudaMemsetAsync(a.redo_cnt, 0, sizeof(int32_t), st));
+        if (cfg->K <= 32) launch(bfs_smem_kernel<1>, kBfsSmemBytes);
+        else if (cfg->K <= 64) launch(bfs_smem_kernel<2>, kBfsSmemBytes);
+        else if (cfg->K <= 128) launch(bfs_smem_kernel<4>, kBfsSmemBytes);
+        else launch(bfs_smem_kernel<8>, kBfsSmemBytes);
+        MARS_CUDA_TRY(cudaGetLastError());
+    }
+    if (cfg->K <= 32) launch(bfs_kernel<1>, 0);
+    else if (cfg->K <= 64) launch(bfs_kernel<2>, 0);
+    else if (cfg->K <= 128) launch(bfs_kernel<4>, 0);
+    else launch(bfs_kernel<8>, 0);
     MARS_CUDA_TRY(cudaGetLastError());
     return MARS_OK;
 }

@@ -27,6 +27,23 @@ __device__ __forceinline__ float4 ldg_stream(const float4* p) {
     return v;
 }
 
+// Bulk prefetch of `bytes` (a multiple of 16) at a 16-byte aligned global
+// address into L2 (cp.async.bulk.prefetch.L2, sm_90+): one instruction asks
+// for a whole row, so a warp can request the rows it will gather next while
+// it computes on the current one.  Nothing is written and no wait follows.
+__device__ __forceinline__ void prefetch_l2_bulk(const void* p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// L2 prefetch of the 128-byte lines covering [p, p + bytes) at any
+// alignment (prefetch.global.L2, one per line): for short spans such as a
+// graph node's neighbour list.
+__device__ __forceinline__ void prefetch_l2_span(const void* p, uint32_t bytes) {
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(p);
+    for (uintptr_t a = lo & ~(uintptr_t)127; a < lo + bytes; a += 128)
+        asm volatile("prefetch.global.L2 [%0];" ::"l"(a) : "memory");
+}
+
 // ---------------------------------------------------------------------------
 // Canonical dot product.  Lane l owns float4 chunks c = l, l+32, ... of the
 // row (chunks past nc are skipped), accumulates each chunk with fmaf in

@@ -24,18 +24,36 @@ int batch_topk(const mars_store* s, struct mars_batch_ctx* c, const float* d_que
                int32_t K, int32_t row_offset, int32_t self_base, int32_t* d_ids, float* d_vals,
                int32_t* d_counts, void* stream);
 
-// Row shards: between the two rescore passes of a batched call, the
-// certified K-th lower bounds of the B queries (d_bound[0, B), device
-// floats, -inf where uncertified) and a failure flag (d_bound[B]: 1 when the
-// shard's call failed) are replaced on every shard by their maximum over the
-// shards.  fn enqueues that exchange of B + 1 floats on `st`; `done` records
-// that the batched call reached it (every rank runs it exactly once per
-// call).
+// Row shards: a batched call on one shard exchanges two small records with
+// the other shards, each by one all-gather of the same number of floats per
+// rank on `st` (gather(arg, which, count, st): send[which] -> recv[which],
+// world records rank-major):
+//  0. before the candidates pass, the threshold record (kShardThr*): each
+//     query's kShardJ largest sampled lower bounds (descending, -inf padded)
+//     and [sampled rows, rows, mode] as int bits after the B lists; every
+//     shard of mode 1 takes the same short-list threshold from their union;
+//  1. between the rescore passes, the bound record (kShardRec*): per query
+//     the count of candidates whose lower bound reaches the threshold (int
+//     bits), the K-th and the ceil(K / world)-th largest lower bounds, then
+//     one failure flag (1: the shard's call failed; no result is served).
+// theta_done / done record that the call reached each exchange: every rank
+// runs each exactly once per call, with neutral records (mode 0, counts 0,
+// bounds -inf) when its local call ended early.
+constexpr int kShardJ = 16;
+inline int32_t shard_thr_floats(int32_t B) { return B * kShardJ + 3; }
+inline int32_t shard_rec_floats(int32_t B) { return 3 * B + 1; }
 struct BoundExchange {
-    int (*fn)(void* arg, float* d_bound, int32_t B, cudaStream_t st);
+    int (*gather)(void* arg, int which, int32_t count, cudaStream_t st);
     void* arg;
+    int32_t world;
+    float* send[2];
+    const float* recv[2];
+    bool theta_done;
     bool done;
 };
+// Enqueue neutral records of B queries on st.
+int shard_neutral_thr(float* d_rec, int32_t B, cudaStream_t st);
+int shard_neutral_rec(float* d_rec, int32_t B, bool failed, cudaStream_t st);
 
 // The stream a batched call with stream == NULL runs on.
 cudaStream_t batch_ctx_stream(const struct mars_batch_ctx* c);

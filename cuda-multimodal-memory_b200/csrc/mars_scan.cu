@@ -147,7 +147,7 @@ __global__ void __launch_bounds__(kScanThreads) topk_merge_select_kernel(const i
                                                                          int32_t* ids_out, float* vals_out,
                                                                          int32_t* cnt_out) {
     __shared__ unsigned long long s_keys[kMergeKeys];
-    __shared__ int s_hist[2048];
+    __shared__ __align__(16) int s_hist[2048];   // also read as 64-bit keys
     __shared__ int s_misc[16];
     constexpr int kPer = kMergeKeys / kScanThreads;
     const int qi = blockIdx.x;

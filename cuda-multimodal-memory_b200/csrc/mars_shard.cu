@@ -7,36 +7,49 @@
 // [offset_r, offset_r + n_r) in its own store and every rank answers the same
 // B queries.  One call of mars_shard_query_batch_topk on every rank:
 //
-//  1. the local batched pipeline (mars_batch.cu): fp16 tensor-core short
-//     list with proven margins, then rescore pass 1, which writes each
-//     query's certified K-th lower bound on this shard (K rows of the shard
-//     score at least that much);
-//  2. NCCL all-reduce (max) of the B bounds: the largest is a lower bound of
-//     the global K-th score, valid on every shard;
-//  3. rescore pass 2 against that bound: only rows that can still enter the
-//     global top-K are scored exactly (about K / world + a few per shard);
-//     uncertified queries are rescanned exactly on the device;
-//  4. the local lists become 64-bit rank keys (score, then id, in one
+//  1. the local batched pipeline (mars_batch.cu) on the shard's rows: the
+//     sample pass, then ONE ncclAllGather of every shard's best sampled
+//     lower bounds per query (B x 16 floats per rank), from which every
+//     shard takes the same short-list threshold -- the level a sample of the
+//     whole corpus gives, so a shard short-lists about 1 / world of what its
+//     own sample would let through;
+//  2. the fp16 tensor-core candidates pass against that threshold, then
+//     rescore pass 1, which writes each query's record: the candidates whose
+//     lower bound reaches the threshold, the K-th and the ceil(K / world)-th
+//     largest lower bounds;
+//  3. ONE ncclAllGather of the records (3 B + 1 floats per rank): the counts
+//     add up to the completeness check (K of them over all shards certify
+//     every shard's short list), and the largest K-th bound, the smallest
+//     ceil(K / world)-th bound and the threshold are lower bounds of the
+//     global K-th score, valid on every shard;
+//  4. rescore pass 2 against the largest of them: only rows that can still
+//     enter the global top-K are scored exactly (about K / world + a few per
+//     shard); uncertified queries are rescanned exactly on every shard;
+//  5. the local lists become 64-bit rank keys (score, then id, in one
 //     integer; 0 = no entry) and ONE ncclAllGather moves them, B x K x 8
 //     bytes per rank;
-//  5. every rank selects each query's top-K of the world x K keys.
+//  6. every rank selects each query's top-K of the world x K keys.
 //
 // The results equal a single-GPU mars_query_batch_topk over the whole
 // corpus bit for bit: every shard's exact scores are the fp32 scan's, the
 // pruning only drops rows that cannot place, and keys rank by (score desc,
 // id asc).  Every rank takes the same collective steps in the same order in
-// every path: a rank whose local work fails still joins both collectives
-// with neutral data (bounds -inf, no keys) and returns its error after them.
+// every path: a rank whose local work fails still joins all three
+// collectives with neutral data (no samples, bounds -inf, no keys) and
+// returns its error after them.
 #include <cuda_runtime.h>
 #include <dlfcn.h>
 
 #include <algorithm>
 #include <cmath>
 #include <cstddef>
+#include <condition_variable>
 #include <cstring>
 #include <mutex>
-#include <type_traits>
 #include <string>
+#include <thread>
+#include <type_traits>
+#include <vector>
 
 #include "mars_b200.h"
 #include "mars_common.cuh"
@@ -96,18 +109,21 @@ __global__ void pack_keys_kernel(const int32_t* __restrict__ ids, const float* _
 
 // Query qi's top-K of the world x K gathered keys ([rank][B][K] layout): the
 // non-empty keys go to shared memory and the block's radix selection takes
-// the K largest.  world x K <= kMergeKeys.  failed (> 0 when some shard's
-// call failed): no result is served, counts are -1.
+// the K largest.  world x K <= kMergeKeys.  recs: every shard's bound record
+// (rank-major, 3 B + 1 floats each, the last the shard's failure flag); when
+// some shard's call failed no result is served and counts are -1.
 __global__ void __launch_bounds__(kThreads) merge_keys_kernel(const unsigned long long* __restrict__ keys, int world,
-                                                              int K, int B, const float* __restrict__ failed,
+                                                              int K, int B, const float* __restrict__ recs,
                                                               int32_t* __restrict__ ids_out,
                                                               float* __restrict__ vals_out,
                                                               int32_t* __restrict__ cnt_out) {
     __shared__ unsigned long long s_keys[kMergeKeys];
-    __shared__ int s_hist[2048];
+    __shared__ __align__(16) int s_hist[2048];   // also read as 64-bit keys
     __shared__ int s_misc[16];
     const int qi = blockIdx.x;
-    if (__ldcg(failed) > 0.0f) {
+    bool failed = false;
+    for (int r = 0; r < world; ++r) failed = failed || __ldcg(recs + (int64_t)r * (3 * (int64_t)B + 1) + 3 * B) > 0.0f;
+    if (failed) {
         for (int p = threadIdx.x; p < K; p += kThreads) {
             vals_out[(int64_t)qi * K + p] = -INFINITY;
             ids_out[(int64_t)qi * K + p] = -1;
@@ -149,7 +165,7 @@ __global__ void __launch_bounds__(kThreads) merge_keys_flagged_kernel(const unsi
                                                                       float* __restrict__ vals_out,
                                                                       int32_t* __restrict__ cnt_out) {
     __shared__ unsigned long long s_keys[kMergeKeys];
-    __shared__ int s_hist[2048];
+    __shared__ __align__(16) int s_hist[2048];   // also read as 64-bit keys
     __shared__ int s_misc[16];
     __shared__ int s_failed;
     const int qi = blockIdx.x;
@@ -179,13 +195,6 @@ __global__ void __launch_bounds__(kThreads) merge_keys_flagged_kernel(const unsi
     if (threadIdx.x == 0 && cnt_out != nullptr) cnt_out[qi] = failed ? -1 : cnt;
 }
 
-// A shard whose call ended before its exchange: bounds -inf, flag = failed.
-__global__ void neutral_bounds_kernel(float* p, int n, float failed) {
-    const int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < n) p[i] = -INFINITY;
-    if (i == n) p[n] = failed;
-}
-
 }  // namespace shard
 }  // namespace mars
 
@@ -201,8 +210,8 @@ struct mars_shard_comm {
     ncclComm_t comm = nullptr;
     unsigned long long* d_send = nullptr;   // max_batch x max_k keys
     unsigned long long* d_recv = nullptr;   // world x max_batch x max_k keys
-    float* d_bound = nullptr;               // max_batch + 1: bounds and flag when the batched call failed early
-    const float* last_bound = nullptr;      // the exchanged array of the current call
+    float* d_xsend[2] = {nullptr, nullptr};  // this rank's threshold / bound record
+    float* d_xrecv[2] = {nullptr, nullptr};  // every rank's, rank-major
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};   // local / exchange / merge boundaries
     bool timed = false;
     void* bfs_state = nullptr;              // mars_shard_query's scratch (made on first use)
@@ -215,13 +224,15 @@ int nccl_fail(const NcclApi* api, ncclResult_t r, const char* what) {
                                    (api ? api->GetErrorString(r) : "?") + ")");
 }
 
-// max over the shards of the B certified bounds and the failure flag, in
-// place, on st
-int exchange_bounds(void* arg, float* d_bound, int32_t B, cudaStream_t st) {
+// all-gather of one record (`which`: 0 threshold, 1 bound) of `count`
+// floats per rank, on st
+int exchange_records(void* arg, int which, int32_t count, cudaStream_t st) {
     auto* c = static_cast<mars_shard_comm*>(arg);
-    c->last_bound = d_bound;
-    const ncclResult_t r = c->nccl->AllReduce(d_bound, d_bound, (size_t)B + 1, ncclFloat32, ncclMax, c->comm, st);
-    if (r != ncclSuccess) return nccl_fail(c->nccl, r, "mars_shard_query_batch_topk: bound all-reduce");
+    const ncclResult_t r = c->nccl->AllGather(c->d_xsend[which], c->d_xrecv[which], (size_t)count, ncclFloat32,
+                                              c->comm, st);
+    if (r != ncclSuccess)
+        return nccl_fail(c->nccl, r, which == 0 ? "mars_shard_query_batch_topk: threshold all-gather"
+                                                : "mars_shard_query_batch_topk: bound all-gather");
     return MARS_OK;
 }
 
@@ -319,7 +330,11 @@ int mars_shard_comm_create(int32_t device, int32_t rank, int32_t world, const vo
     const size_t keys = (size_t)max_batch * max_k;
     T(cudaMalloc(&c->d_send, keys * 8), "shard send keys");
     T(cudaMalloc(&c->d_recv, keys * 8 * world), "shard gathered keys");
-    T(cudaMalloc(&c->d_bound, ((size_t)max_batch + 1) * 4), "shard bounds + failure flag");
+    const size_t rec[2] = {(size_t)shard_thr_floats(max_batch), (size_t)shard_rec_floats(max_batch)};
+    for (int w = 0; w < 2; ++w) {
+        T(cudaMalloc(&c->d_xsend[w], rec[w] * 4), "shard record");
+        T(cudaMalloc(&c->d_xrecv[w], rec[w] * 4 * world), "shard records of every rank");
+    }
     for (auto& e : c->ev) T(cudaEventCreate(&e), "event");
     if (rc == MARS_OK) {
         ncclUniqueId id;
@@ -340,7 +355,10 @@ int mars_shard_comm_destroy(mars_shard_comm* c) {
     if (c->comm != nullptr) c->nccl->CommDestroy(c->comm);
     cudaFree(c->d_send);
     cudaFree(c->d_recv);
-    cudaFree(c->d_bound);
+    for (int w = 0; w < 2; ++w) {
+        cudaFree(c->d_xsend[w]);
+        cudaFree(c->d_xrecv[w]);
+    }
     for (cudaEvent_t e : c->ev)
         if (e) cudaEventDestroy(e);
     delete c;
@@ -406,10 +424,10 @@ int mars_shard_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx, mars_s
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream)
                              : (ctx != nullptr ? batch_ctx_stream(ctx) : static_cast<cudaStream_t>(nullptr));
     if (c->timed) MARS_CUDA_TRY(cudaEventRecord(c->ev[0], st));
-    c->last_bound = nullptr;
 
-    // 1-3: the local pipeline with the bound exchange between the rescore passes
-    BoundExchange xchg{&exchange_bounds, c, false};
+    // 1-4: the local pipeline with the two record exchanges
+    BoundExchange xchg{&exchange_records, c, c->world, {c->d_xsend[0], c->d_xsend[1]},
+                       {c->d_xrecv[0], c->d_xrecv[1]}, false, false};
     int local_rc = MARS_OK;
     if (s == nullptr || ctx == nullptr || s->device != c->device)
         local_rc = fail(MARS_ERR_INVALID, "mars_shard_query_batch_topk: store and context must be on the "
@@ -418,13 +436,15 @@ int mars_shard_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx, mars_s
         local_rc = batch_topk_sharded(s, ctx, d_queries, query_pitch, B, query_timestamp, lambda, modality_filter,
                                       use_importance, K, row_offset, d_ids, d_vals, d_counts, st, &xchg);
     const std::string local_msg = local_rc != MARS_OK ? std::string(mars_last_error()) : std::string();
+    // the local call ended before an exchange (an error, or the exact
+    // per-query scans of a small shard): join it with a neutral record
+    if (!xchg.theta_done) {
+        MARS_TRY(shard_neutral_thr(c->d_xsend[0], B, st));
+        MARS_TRY(exchange_records(c, 0, shard_thr_floats(B), st));
+    }
     if (!xchg.done) {
-        // the local call ended before its exchange (an error, or the exact
-        // per-query scans of a small shard): join it with no bound
-        shard::neutral_bounds_kernel<<<(B + 256) / 256, 256, 0, st>>>(c->d_bound, B,
-                                                                      local_rc != MARS_OK ? 1.0f : 0.0f);
-        MARS_CUDA_TRY(cudaGetLastError());
-        MARS_TRY(exchange_bounds(c, c->d_bound, B, st));
+        MARS_TRY(shard_neutral_rec(c->d_xsend[1], B, local_rc != MARS_OK, st));
+        MARS_TRY(exchange_records(c, 1, shard_rec_floats(B), st));
     }
     if (c->timed) MARS_CUDA_TRY(cudaEventRecord(c->ev[1], st));
 
@@ -442,7 +462,7 @@ int mars_shard_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx, mars_s
     if (c->timed) MARS_CUDA_TRY(cudaEventRecord(c->ev[2], st));
 
     // 5: every rank merges
-    shard::merge_keys_kernel<<<B, shard::kThreads, 0, st>>>(c->d_recv, c->world, K, B, c->last_bound + B, d_ids,
+    shard::merge_keys_kernel<<<B, shard::kThreads, 0, st>>>(c->d_recv, c->world, K, B, c->d_xrecv[1], d_ids,
                                                             d_vals, d_counts);
     MARS_CUDA_TRY(cudaGetLastError());
     if (c->timed) MARS_CUDA_TRY(cudaEventRecord(c->ev[3], st));
@@ -451,3 +471,179 @@ int mars_shard_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx, mars_s
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// One-GPU emulation of the sharded call (test hook).  Every shard runs
+// batch_topk_sharded on its own host thread and stream; an exchange is two
+// host barriers: after the first every shard's record is ready (its event
+// recorded), and each shard copies all records into its own receive buffer;
+// after the second every copy is enqueued, and each stream waits for all of
+// them before it may write a send buffer again.  No kernel waits on another.
+namespace {
+
+struct EmuShared {
+    int world = 0;
+    std::mutex mu;
+    std::condition_variable cv;
+    int arrived = 0;
+    long generation = 0;
+    std::vector<cudaEvent_t> ready, copied;
+    std::vector<float*> send[2], recv[2];
+
+    void barrier() {
+        std::unique_lock<std::mutex> lock(mu);
+        const long g = generation;
+        if (++arrived == world) {
+            arrived = 0;
+            ++generation;
+            cv.notify_all();
+        } else {
+            cv.wait(lock, [&] { return generation != g; });
+        }
+    }
+};
+
+struct EmuArg {
+    EmuShared* sh;
+    int rank;
+};
+
+int emu_gather(void* arg, int which, int32_t count, cudaStream_t st) {
+    auto* a = static_cast<EmuArg*>(arg);
+    EmuShared& sh = *a->sh;
+    const int r = a->rank;
+    // both barriers are reached whatever fails, so no shard is left waiting
+    cudaError_t e = cudaEventRecord(sh.ready[r], st);
+    sh.barrier();
+    for (int q = 0; q < sh.world && e == cudaSuccess; ++q) {
+        e = cudaStreamWaitEvent(st, sh.ready[q], 0);
+        if (e == cudaSuccess)
+            e = cudaMemcpyAsync(sh.recv[which][r] + (size_t)q * count, sh.send[which][q], (size_t)count * 4,
+                                cudaMemcpyDeviceToDevice, st);
+    }
+    const cudaError_t e2 = cudaEventRecord(sh.copied[r], st);
+    sh.barrier();
+    cudaError_t e3 = cudaSuccess;
+    for (int q = 0; q < sh.world && e3 == cudaSuccess; ++q) e3 = cudaStreamWaitEvent(st, sh.copied[q], 0);
+    if (e != cudaSuccess) return cuda_fail(e, "shard emulation: record copy", __FILE__, __LINE__);
+    if (e2 != cudaSuccess) return cuda_fail(e2, "shard emulation: event", __FILE__, __LINE__);
+    if (e3 != cudaSuccess) return cuda_fail(e3, "shard emulation: event wait", __FILE__, __LINE__);
+    return MARS_OK;
+}
+
+}  // namespace
+
+extern "C" int mars_shard_emulate_query_batch_topk(int32_t world, const mars_store* const* stores,
+                                                   mars_batch_ctx* const* ctxs, const int32_t* row_offsets,
+                                                   const float* d_queries, int32_t query_pitch, int32_t B,
+                                                   float query_timestamp, float lambda, int32_t modality_filter,
+                                                   int32_t use_importance, int32_t K, int32_t* d_ids,
+                                                   float* d_vals, int32_t* d_counts) {
+    if (world <= 0 || world > 16 || stores == nullptr || ctxs == nullptr || row_offsets == nullptr ||
+        d_ids == nullptr || d_vals == nullptr || d_counts == nullptr)
+        return fail(MARS_ERR_INVALID, "mars_shard_emulate_query_batch_topk: bad arguments");
+    if (B <= 0 || K <= 0 || K > MARS_MAX_TOP_K || (int64_t)world * K > kMergeKeys)
+        return fail(MARS_ERR_INVALID, "mars_shard_emulate_query_batch_topk: need B > 0, 0 < K <= 256, world x K <= 4096");
+    for (int r = 0; r < world; ++r)
+        if (stores[r] == nullptr || ctxs[r] == nullptr || stores[r]->device != stores[0]->device)
+            return fail(MARS_ERR_INVALID, "mars_shard_emulate_query_batch_topk: every shard on one device");
+    const int dev = stores[0]->device;
+    MarsDeviceGuard g(dev);
+    if (!g.ok) return fail(MARS_ERR_NO_DEVICE, "mars_shard_emulate_query_batch_topk: cudaSetDevice failed");
+    EmuShared sh;
+    sh.world = world;
+    const size_t n = (size_t)B * K;
+    const int32_t cnt[2] = {shard_thr_floats(B), shard_rec_floats(B)};
+    std::vector<int32_t*> l_ids(world, nullptr), l_cnt(world, nullptr);
+    std::vector<float*> l_vals(world, nullptr);
+    std::vector<unsigned long long*> keys(world, nullptr);
+    std::vector<cudaEvent_t> keys_ready(world, nullptr);
+    unsigned long long* all_keys = nullptr;
+    sh.ready.assign(world, nullptr);
+    sh.copied.assign(world, nullptr);
+    for (int w = 0; w < 2; ++w) {
+        sh.send[w].assign(world, nullptr);
+        sh.recv[w].assign(world, nullptr);
+    }
+    int rc = MARS_OK;
+    auto T = [&](cudaError_t e, const char* what) {
+        if (rc == MARS_OK && e != cudaSuccess) rc = cuda_fail(e, what, __FILE__, __LINE__);
+    };
+    for (int r = 0; r < world; ++r) {
+        T(cudaMalloc(&l_ids[r], n * 4), "emulation buffers");
+        T(cudaMalloc(&l_vals[r], n * 4), "emulation buffers");
+        T(cudaMalloc(&l_cnt[r], (size_t)B * 4), "emulation buffers");
+        T(cudaMalloc(&keys[r], n * 8), "emulation buffers");
+        for (int w = 0; w < 2; ++w) {
+            T(cudaMalloc(&sh.send[w][r], (size_t)cnt[w] * 4), "emulation buffers");
+            T(cudaMalloc(&sh.recv[w][r], (size_t)cnt[w] * 4 * world), "emulation buffers");
+        }
+        T(cudaEventCreateWithFlags(&sh.ready[r], cudaEventDisableTiming), "event");
+        T(cudaEventCreateWithFlags(&sh.copied[r], cudaEventDisableTiming), "event");
+        T(cudaEventCreateWithFlags(&keys_ready[r], cudaEventDisableTiming), "event");
+    }
+    T(cudaMalloc(&all_keys, n * 8 * world), "emulation buffers");
+    T(cudaDeviceSynchronize(), "emulation set-up");
+    std::vector<int> rcs(world, MARS_OK);
+    std::vector<std::string> msgs(world);
+    if (rc == MARS_OK) {
+        std::vector<EmuArg> args(world);
+        std::vector<std::thread> th;
+        for (int r = 0; r < world; ++r) {
+            args[r] = EmuArg{&sh, r};
+            th.emplace_back([&, r] {
+                MarsDeviceGuard tg(dev);
+                cudaStream_t st = batch_ctx_stream(ctxs[r]);
+                BoundExchange x{&emu_gather, &args[r], world, {sh.send[0][r], sh.send[1][r]},
+                                {sh.recv[0][r], sh.recv[1][r]}, false, false};
+                int lrc = tg.ok ? batch_topk_sharded(stores[r], ctxs[r], d_queries, query_pitch, B, query_timestamp,
+                                                     lambda, modality_filter, use_importance, K, row_offsets[r],
+                                                     l_ids[r], l_vals[r], l_cnt[r], st, &x)
+                                : fail(MARS_ERR_NO_DEVICE, "shard emulation: cudaSetDevice failed");
+                if (lrc != MARS_OK) msgs[r] = mars_last_error();
+                // every shard takes both exchanges exactly once
+                if (!x.theta_done) {
+                    shard_neutral_thr(sh.send[0][r], B, st);
+                    emu_gather(&args[r], 0, cnt[0], st);
+                }
+                if (!x.done) {
+                    shard_neutral_rec(sh.send[1][r], B, lrc != MARS_OK, st);
+                    emu_gather(&args[r], 1, cnt[1], st);
+                }
+                if (lrc == MARS_OK)
+                    shard::pack_keys_kernel<<<(int)std::min<size_t>((n + 255) / 256, 1024), 256, 0, st>>>(
+                        l_ids[r], l_vals[r], (int64_t)n, keys[r]);
+                else
+                    cudaMemsetAsync(keys[r], 0, n * 8, st);
+                cudaEventRecord(keys_ready[r], st);
+                rcs[r] = lrc;
+            });
+        }
+        for (auto& t : th) t.join();
+        // the key "all-gather" and the merge, on shard 0's stream
+        cudaStream_t st0 = batch_ctx_stream(ctxs[0]);
+        for (int r = 0; r < world; ++r) {
+            T(cudaStreamWaitEvent(st0, keys_ready[r], 0), "event wait");
+            T(cudaMemcpyAsync(all_keys + (size_t)r * n, keys[r], n * 8, cudaMemcpyDeviceToDevice, st0), "key copy");
+        }
+        if (rc == MARS_OK) {
+            shard::merge_keys_kernel<<<B, shard::kThreads, 0, st0>>>(all_keys, world, K, B, sh.recv[1][0], d_ids,
+                                                                     d_vals, d_counts);
+            T(cudaGetLastError(), "merge");
+        }
+        T(cudaStreamSynchronize(st0), "emulation");
+    }
+    cudaDeviceSynchronize();
+    for (int r = 0; r < world; ++r) {
+        cudaFree(l_ids[r]); cudaFree(l_vals[r]); cudaFree(l_cnt[r]); cudaFree(keys[r]);
+        for (int w = 0; w < 2; ++w) { cudaFree(sh.send[w][r]); cudaFree(sh.recv[w][r]); }
+        if (sh.ready[r]) cudaEventDestroy(sh.ready[r]);
+        if (sh.copied[r]) cudaEventDestroy(sh.copied[r]);
+        if (keys_ready[r]) cudaEventDestroy(keys_ready[r]);
+    }
+    cudaFree(all_keys);
+    if (rc != MARS_OK) return rc;
+    for (int r = 0; r < world; ++r)
+        if (rcs[r] != MARS_OK) return fail(rcs[r], msgs[r]);
+    return MARS_OK;
+}

@@ -149,6 +149,8 @@ _SIGS = {
                          C.POINTER(_I32)],
     "mars_shard_query_batch_topk": [_VP, _VP, _VP, _VP, _I32, _I32, _F32, _F32, _I32, _I32, _I32, _I32,
                                     _VP, _VP, _VP, _VP],
+    "mars_shard_emulate_query_batch_topk": [_I32, _VP, _VP, _VP, _VP, _I32, _I32, _F32, _F32, _I32, _I32, _I32,
+                                            _VP, _VP, _VP],
     "mars_cmng_build": [_VP, _I32, _I32, _I32, _VP, C.POINTER(C.c_float)],
     "mars_cmng_build_rows": [_VP, _I32, _I32, _I32, _I32, _I32, _VP, C.POINTER(C.c_float)],
     "mars_cmng_knn": [_VP, _I32, _VP, _VP, _VP],
@@ -156,6 +158,7 @@ _SIGS = {
                                _VP, _VP, _VP, _VP, _VP, _VP],
     "mars_cmng_ctx_create": [_I32, _I32, _I32, _I32, _I32, _I32, C.POINTER(_VP)],
     "mars_cmng_ctx_destroy": [_VP],
+    "mars_cmng_ctx_set_bfs_smem_nodes": [_VP, _I32],
     "mars_cmng_search_bfs_batch": [_VP, _VP, _VP, _I32, _VP, _I32, _I32, _F32, C.POINTER(CmngConfig),
                                    _I32, _F32, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _VP],
     "mars_scan_topk_noalloc": [_VP, _I32, _VP, _VP, _VP, _I32, _I32, _VP, _F32, _F32, _I32, _I32,
@@ -584,6 +587,23 @@ class ShardComm:
             pass
 
 
+def shard_emulate_query_batch_topk(stores, contexts, row_offsets, d_queries, B, t_q, lam, K, d_ids, d_vals,
+                                   d_counts, modality_filter=-1, use_importance=False, query_pitch=None):
+    """Test hook: the sharded batched top-K over len(stores) row shards that
+    all live on this GPU (each shard's pipeline on its own thread and its
+    context's stream, the all-gathers done as device copies); blocks until
+    the merged answer is written."""
+    w = len(stores)
+    assert len(contexts) == w and len(row_offsets) == w
+    hs = (C.c_void_p * w)(*[s.handle.value for s in stores])
+    hc = (C.c_void_p * w)(*[c.handle.value for c in contexts])
+    offs = (C.c_int32 * w)(*[int(o) for o in row_offsets])
+    pitch = query_pitch if query_pitch is not None else (stores[0].dim + 3) // 4 * 4
+    _check(lib().mars_shard_emulate_query_batch_topk(w, hs, hc, offs, _ptr(d_queries), pitch, B, float(t_q),
+                                                     float(lam), modality_filter, int(use_importance), K,
+                                                     _ptr(d_ids), _ptr(d_vals), _ptr(d_counts)))
+
+
 def cmng_build(store: Store, degree, degree_cross, num_modalities, d_neighbors) -> float:
     """build_cmng over the store's rows into d_neighbors (N x degree, device)."""
     ms = C.c_float()
@@ -624,6 +644,10 @@ class CmngContext:
         _check(lib().mars_cmng_ctx_create(device, max_queries, K, degree, bfs_hops, max_nodes,
                                           C.byref(h)))
         self.handle = h
+
+    def set_bfs_smem_nodes(self, max_nodes: int) -> None:
+        """Visited nodes per query the shared-memory BFS holds (<= 2048; 0: global tables only)."""
+        _check(lib().mars_cmng_ctx_set_bfs_smem_nodes(self.handle, int(max_nodes)))
 
     def search_bfs(self, store: Store, d_neighbors, degree, d_queries, nq, t_q, cfg: CmngConfig,
                    bfs_hops, bfs_score_decay, d_ids, d_scores, d_counts, d_mods=None, d_hops=None,

@@ -404,11 +404,16 @@ int mars_shard_last_times(mars_shard_comm* comm, float* local_ms, float* gather_
  * the same queries, B, K, t_q, lambda, filter and use_importance (a
  * collective).  s: this rank's shard; row_offset: its first global row.
  * Outputs on every rank: the global top-K [B][K] (global ids), d_counts [B].
- * Each shard runs the batched tensor-core pipeline; between its two rescore
- * passes one NCCL all-reduce (max) of the B certified K-th lower bounds gives
+ * Each shard runs the batched tensor-core pipeline with three NCCL
+ * all-gathers: after the sample pass, every shard's best sampled lower
+ * bounds per query (B x 16 floats per rank), from which all shards take one
+ * short-list threshold (the level a sample of the whole corpus gives);
+ * between the two rescore passes, per query the count of candidates whose
+ * lower bound reaches it and two lower-bound order statistics (3 B + 1
+ * floats per rank), which certify the short lists over all shards and give
  * every shard a bound of the global K-th score, so a shard rescores only
- * rows that can still place; then one NCCL all-gather of B x K packed 64-bit
- * keys (score, then id) and a per-query selection on every rank.  The
+ * rows that can still place; and B x K packed 64-bit keys (score, then id),
+ * followed by a per-query selection on every rank.  The
  * results equal mars_query_batch_topk over the whole corpus on one GPU, bit
  * for bit.  Asynchronous on `stream` (NULL: the batch context's stream).  If
  * any rank's call fails (an argument, or a bounded device wait that gave
@@ -420,6 +425,22 @@ int mars_shard_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx, mars_s
                                 float query_timestamp, float lambda, int32_t modality_filter,
                                 int32_t use_importance, int32_t K, int32_t row_offset,
                                 int32_t* d_ids, float* d_vals, int32_t* d_counts, void* stream);
+
+/* Test hook, no reference counterpart: mars_shard_query_batch_topk over
+ * `world` row shards that all live on ONE GPU (stores[r] holds global rows
+ * [row_offsets[r], row_offsets[r] + n_r), ctxs[r] is its batch context),
+ * each shard's pipeline on its own host thread and its context's stream,
+ * with the three all-gathers replaced by device copies between the shards'
+ * buffers (host barriers order them; no kernel waits on another).  The same
+ * code runs for every shard as under NCCL, so the merged answer in d_ids /
+ * d_vals / d_counts ([B][K], [B]) shows what `world` GPUs would return.
+ * Blocks until the answer is written.  world <= 16. */
+int mars_shard_emulate_query_batch_topk(int32_t world, const mars_store* const* stores,
+                                        mars_batch_ctx* const* ctxs, const int32_t* row_offsets,
+                                        const float* d_queries, int32_t query_pitch, int32_t B,
+                                        float query_timestamp, float lambda, int32_t modality_filter,
+                                        int32_t use_importance, int32_t K, int32_t* d_ids, float* d_vals,
+                                        int32_t* d_counts);
 
 /* query_memory_fast (include/memory_cuda.cuh:188-194, src/memory_cuda.cu:
  * 1069-1158) over a row-sharded corpus, one process per GPU (a collective:
@@ -503,6 +524,11 @@ typedef struct mars_cmng_ctx mars_cmng_ctx;
 int mars_cmng_ctx_create(int32_t device, int32_t max_queries, int32_t K, int32_t degree,
                          int32_t bfs_hops, int32_t max_nodes, mars_cmng_ctx** out);
 int mars_cmng_ctx_destroy(mars_cmng_ctx* ctx);
+/* The BFS keeps each query's visited set in shared memory while it holds at
+ * most max_nodes nodes (default and limit 2048); a query that visits more is
+ * answered again with the context's global-memory tables, with the same
+ * result.  0: global tables only.  Tests use it to compare the two. */
+int mars_cmng_ctx_set_bfs_smem_nodes(mars_cmng_ctx* ctx, int32_t max_nodes);
 
 int mars_cmng_search_bfs_batch(const mars_store* s, mars_cmng_ctx* ctx,
                                const int32_t* d_neighbors, int32_t degree,

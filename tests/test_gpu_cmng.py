@@ -222,3 +222,50 @@ def test_cmng_search_bfs_matches_oracle(torch_mod, clustered, hops):
         assert_ranked_equivalent(ids[q, :n].cpu().numpy(), sc[q, :n].cpu().numpy(), ref["node_id"],
                                  ref["score"], hp[q, :n].cpu().numpy(), ref["hops"], rtol=2e-6,
                                  what=f"q{q}")
+
+
+@pytest.mark.parametrize("hops,K", [(1, 10), (2, 10), (2, 64), (3, 16)])
+def test_bfs_shared_tables_equal_global_tables(torch_mod, clustered, hops, K):
+    """The BFS with its visited set in shared memory (the default), the
+    global-table kernel alone, and a shared-table limit so small that every
+    query is handed to the global kernel, give the same answers bit for bit
+    (ids, scores, hops, counts, visited)."""
+    import mars_b200 as mb
+    from mars_b200 import datagen
+    torch = torch_mod
+    E, mod, ts = clustered
+    N, D = E.shape
+    deg = 36
+    st = _store(mb, E, mod, ts)
+    nb = torch.empty((N, deg), dtype=torch.int32, device="cuda")
+    mb.cmng_build(st, deg, 4, 4, nb)
+    nq = 300
+    Q = datagen.queries(nq, D, seed=70 + hops)
+    Q[:100] = E[np.arange(100) * 53] + 0.05 * Q[:100]
+    Qd = torch.from_numpy(np.ascontiguousarray(Q)).cuda()
+    cfg = mb.CmngConfig(K=K, beam_width=64, max_iterations=64, time_decay_lambda=0.05)
+    ctx = mb.CmngContext(nq, K, deg, hops, N)
+
+    def run(limit):
+        ctx.set_bfs_smem_nodes(limit)
+        out = [torch.full((nq, K), -9, dtype=torch.int32, device="cuda"),
+               torch.zeros((nq, K), dtype=torch.float32, device="cuda"),
+               torch.full((nq, K), -9, dtype=torch.int32, device="cuda"),
+               torch.full((nq,), -9, dtype=torch.int32, device="cuda"),
+               torch.full((nq,), -9, dtype=torch.int32, device="cuda")]
+        ctx.search_bfs(st, nb, deg, Qd, nq, 10.0, cfg, hops, 0.5, out[0], out[1], out[3], d_hops=out[2],
+                       d_visited=out[4], use_importance=True)
+        torch.cuda.synchronize()
+        return [o.cpu().numpy() for o in out]
+
+    shared = run(2048)
+    glob = run(0)
+    redo = run(16)            # more than 16 visited nodes: every query goes to the global kernel
+    again = run(2048)
+    for other in (glob, redo, again):
+        assert np.array_equal(shared[3], other[3])
+        assert np.array_equal(shared[4], other[4])
+        assert np.array_equal(shared[0], other[0])
+        assert np.array_equal(shared[1].view(np.int32), other[1].view(np.int32))
+        assert np.array_equal(shared[2], other[2])
+    assert shared[4].max() > 16

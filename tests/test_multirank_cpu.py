@@ -166,15 +166,27 @@ def test_query_split_covers_every_query_once():
 
 
 # ---------------------------------------------------------------------------
-# Row shards with a shared pruning bound (mars_shard_query_batch_topk):
-# every rank certifies a lower bound of its shard's K-th score (here the
-# approximate scores' K-th lower bound, approximate = exact + noise within a
-# stated margin), one all-reduce (max) gives a bound of the global K-th score,
-# every rank keeps only rows whose upper bound reaches it, packs its local
-# top-K as 64-bit rank keys (score, then id), and one all-gather + a per-query
-# selection gives the global answer.  A rank that flags a failure makes every
-# rank's answer invalid (count -1).
-NS, DS, KS, QS, MARGIN = 4001, 32, 9, 6, 2e-3
+# Row shards with a shared short-list threshold and a shared pruning bound
+# (mars_shard_query_batch_topk), restated on the CPU with approximate scores
+# = exact + noise within a stated margin (lower / upper bounds = approx -+
+# margin):
+#  1. every rank sends its 16 best sampled lower bounds per query and its
+#     (sampled rows, rows); one all-gather; every rank takes the same
+#     threshold theta = the j-th largest of the union, j = ceil(mu + 5 sqrt(mu)
+#     + 3), mu = K x sampled rows / rows over all ranks;
+#  2. candidates: rows whose upper bound reaches theta;
+#  3. per query a record (count of candidates with lower bound >= theta, K-th
+#     and ceil(K / world)-th largest candidate lower bound, -inf where fewer)
+#     and a failure flag; one all-gather;
+#  4. the counts over all ranks certify every rank's short list (>= K);
+#     the bound max(theta, largest K-th, smallest ceil(K / world)-th) is a
+#     lower bound of the global K-th score, so only candidates whose upper
+#     bound reaches it are rescored exactly; an uncertified query is scanned
+#     exactly on every rank;
+#  5. local top-K as 64-bit rank keys (score, then id), one all-gather, a
+#     per-query selection.  A rank that flags a failure makes every rank's
+#     answer invalid (count -1).
+NS, DS, KS, QS, MARGIN, SAMPLE_STRIDE, JMAX = 4001, 32, 9, 6, 2e-3, 7, 16
 
 
 def _f2key(v):
@@ -194,10 +206,16 @@ def _key_decode(k):
     return ids, u.view(np.float32)
 
 
-def _bound_worker(rank, world, port, out_path, fail_rank):
+def _kth(v, k):
+    v = np.sort(np.asarray(v, np.float32))[::-1]
+    return np.float32(v[k - 1]) if v.size >= k else np.float32(-np.inf)
+
+
+def _bound_worker(rank, world, port, out_path, fail_rank, theta_shift):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
+    import math
     import sys
     root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
     sys.path.insert(0, os.path.join(root, "cuda-multimodal-memory_b200"))
@@ -211,50 +229,82 @@ def _bound_worker(rank, world, port, out_path, fail_rank):
     rng = np.random.default_rng(100 + rank)
     exact = np.stack([O.fused_scores(c, Qm[q], 600.0, 0.01, use_importance=True) for q in range(QS)])
     approx = exact + rng.uniform(-MARGIN, MARGIN, exact.shape).astype(np.float32)
-    # pass 1: the K-th largest lower bound of the shard, and the failure flag
-    bound = np.sort(approx - MARGIN, axis=1)[:, -KS].astype(np.float32)
-    flag = np.float32(1.0 if rank == fail_rank else 0.0)
-    t = torch.from_numpy(np.concatenate([bound, [flag]]).astype(np.float32))
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    gbound, failed = t[:QS].numpy(), float(t[QS])
-    # pass 2: exact scores of the rows whose upper bound reaches the global bound
+    lob, hib = approx - MARGIN, approx + MARGIN
+    n = hi - lo
+    # 1. the threshold record: 16 best sampled lower bounds, sampled rows, rows
+    samp = np.arange(0, n, SAMPLE_STRIDE)
+    top = np.full((QS, JMAX), -np.inf, np.float32)
+    for q in range(QS):
+        v = np.sort(lob[q, samp])[::-1][:JMAX]
+        top[q, :v.size] = v
+    rec = torch.from_numpy(np.concatenate([top.ravel(), [samp.size, n]]).astype(np.float64))
+    got = [torch.empty_like(rec) for _ in range(world)]
+    dist.all_gather(got, rec)
+    recs = torch.stack(got).numpy()
+    srows, rows = recs[:, -2].sum(), recs[:, -1].sum()
+    mu = KS * srows / rows
+    j = max(1, min(JMAX, int(math.ceil(mu + 5.0 * math.sqrt(mu) + 3.0))))
+    union = recs[:, :-2].reshape(world, QS, JMAX)
+    theta = np.array([_kth(union[:, q, :].ravel(), j) for q in range(QS)], np.float32) + np.float32(theta_shift)
+    # 2-3. candidates and the bound record
+    m = (KS + world - 1) // world
+    cand = [np.nonzero(hib[q] >= theta[q])[0] for q in range(QS)]
+    cnt = np.array([(lob[q, cand[q]] >= theta[q]).sum() for q in range(QS)], np.float64)
+    kth = np.array([_kth(lob[q, cand[q]], KS) for q in range(QS)], np.float64)
+    mth = np.array([_kth(lob[q, cand[q]], m) for q in range(QS)], np.float64)
+    flag = 1.0 if rank == fail_rank else 0.0
+    rec2 = torch.from_numpy(np.concatenate([cnt, kth, mth, [flag]]))
+    got2 = [torch.empty_like(rec2) for _ in range(world)]
+    dist.all_gather(got2, rec2)
+    r2 = torch.stack(got2).numpy()
+    failed = r2[:, -1].max()
+    total = r2[:, :QS].sum(axis=0)
+    bound = np.maximum(np.maximum(r2[:, QS:2 * QS].max(axis=0), r2[:, 2 * QS:3 * QS].min(axis=0)), theta)
+    # 4. exact scores of the rows that can still place (all rows when uncertified)
     ids = np.full((QS, KS), -1, np.int32)
     vals = np.full((QS, KS), -np.inf, np.float32)
-    kept = 0
+    kept, uncertified = 0, 0
     for q in range(QS):
-        rows = np.nonzero(approx[q] + MARGIN >= max(gbound[q], bound[q]))[0]
-        kept += rows.size
-        order = sorted(rows.tolist(), key=lambda r: (-float(exact[q, r]), r))[:KS]
+        if total[q] >= KS:
+            rowsq = cand[q][hib[q, cand[q]] >= np.float32(bound[q])]
+        else:
+            rowsq = np.arange(n)
+            uncertified += 1
+        kept += rowsq.size
+        order = sorted(rowsq.tolist(), key=lambda r: (-float(exact[q, r]), r))[:KS]
         ids[q, :len(order)] = np.asarray(order, np.int32) + lo
         vals[q, :len(order)] = exact[q, order]
+    # 5. keys, all-gather, merge
     keys = torch.from_numpy(_rank_keys(ids, vals).view(np.int64))
-    got = [torch.empty_like(keys) for _ in range(world)]
-    dist.all_gather(got, keys)
-    allk = torch.stack(got).numpy().view(np.uint64)           # [world][Q][K]
+    got3 = [torch.empty_like(keys) for _ in range(world)]
+    dist.all_gather(got3, keys)
+    allk = torch.stack(got3).numpy().view(np.uint64)           # [world][Q][K]
     out_i = np.full((QS, KS), -1, np.int32)
     out_v = np.full((QS, KS), -np.inf, np.float32)
-    cnt = np.zeros(QS, np.int32)
+    outc = np.zeros(QS, np.int32)
     for q in range(QS):
         if failed > 0:
-            cnt[q] = -1
+            outc[q] = -1
             continue
         k = np.sort(allk[:, q, :].ravel())[::-1]
         k = k[k != 0][:KS]
         out_i[q, :k.size], out_v[q, :k.size] = _key_decode(k)
-        cnt[q] = k.size
-    kept_all = torch.tensor([kept], dtype=torch.int64)
-    dist.all_reduce(kept_all)
+        outc[q] = k.size
+    stats = torch.tensor([kept, uncertified, sum(x.size for x in cand)], dtype=torch.int64)
+    dist.all_reduce(stats)
     if rank == 0:
-        np.savez(out_path, ids=out_i, vals=out_v, cnt=cnt, kept=int(kept_all))
+        np.savez(out_path, ids=out_i, vals=out_v, cnt=outc, kept=int(stats[0]), uncertified=int(stats[1]),
+                 cand=int(stats[2]))
     dist.barrier()
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world,fail_rank", [(2, -1), (3, -1), (2, 1)])
-def test_shared_bound_shards_equal_whole_corpus(tmp_path, world, fail_rank):
+@pytest.mark.parametrize("world,fail_rank,theta_shift", [(2, -1, 0.0), (3, -1, 0.0), (4, -1, 0.0), (2, 1, 0.0),
+                                                         (3, -1, 10.0)])
+def test_shared_threshold_shards_equal_whole_corpus(tmp_path, world, fail_rank, theta_shift):
     out = str(tmp_path / "bound.npz")
-    mp.start_processes(_bound_worker, args=(world, _free_port(), out, fail_rank), nprocs=world, join=True,
-                       start_method="spawn")
+    mp.start_processes(_bound_worker, args=(world, _free_port(), out, fail_rank, theta_shift), nprocs=world,
+                       join=True, start_method="spawn")
     z = np.load(out)
     if fail_rank >= 0:
         assert np.all(z["cnt"] == -1) and np.all(z["ids"] == -1)
@@ -270,8 +320,17 @@ def test_shared_bound_shards_equal_whole_corpus(tmp_path, world, fail_rank):
         assert np.array_equal(z["ids"][q], i)
         assert np.array_equal(z["vals"][q], v)
         assert z["cnt"][q] == KS
-    # the shared bound prunes: far fewer rows than world x K per query survive
+    if theta_shift > 0:
+        # a threshold above every score certifies nothing: every query is
+        # answered by the exact scans, still exactly
+        assert z["uncertified"] == world * QS
+        return
+    assert z["uncertified"] == 0
+    # the shared threshold and bound prune: far fewer rows than world x K per
+    # query are rescored, and the shards together short-list about what one
+    # corpus-wide sample would
     assert z["kept"] < world * KS * QS
+    assert z["cand"] < 40 * KS * QS
 
 
 # ---------------------------------------------------------------------------
