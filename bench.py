@@ -894,8 +894,9 @@ def cfg_c2(a, env):
     return {"workload": "c2", "metric": f"queries/s (batched exact top-K, N={N}, D={D}, B={B}, K={K})",
             "value": B / (ms * 1e-3), "unit": "queries/s", "n_gpus": world, "steps": steps,
             "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-            "parallelism": (f"rows sharded x{world}: mars_shard_query_batch_topk (NCCL bound all-reduce + "
-                            f"one all-gather of packed keys + merge, inside the library)" if world > 1
+            "parallelism": (f"rows sharded x{world}: mars_shard_query_batch_topk (inside the library: NCCL "
+                            f"all-gathers of the sampled bounds, of the per-query count / bound records and of "
+                            f"the packed keys, then the merge)" if world > 1
                             else "one GPU (mars_shard_query_batch_topk, world 1)"),
             "phases_ms_max_over_ranks": phases,
             "exact_vs_single_gpu": exact_single, "exact_vs_oracle": exact_oracle,

@@ -585,7 +585,7 @@ __global__ void neutral_rec_kernel(float* __restrict__ rec, int32_t B, float fai
 //    K-th score, so only rows that can still enter the global top-K are
 //    rescored (about K / world + a few per shard).
 // Both selections are block-wide bitonic sorts in shared memory ranked by
-// (score desc, id asc).
+// rank key (score desc, id asc; -0 below +0, as the fp32 scan ranks).
 constexpr int kSortCap = 4096;
 constexpr int kRescoreThreads = 256;
 
@@ -597,7 +597,9 @@ __device__ __forceinline__ void block_bitonic_desc(float* key, int32_t* id, int 
                 if (p > i) {
                     const float a = key[i], b = key[p];
                     const int32_t ia = id[i], ib = id[p];
-                    const bool a_first = better(a, ia, b, ib);
+                    // rank-key order (the fp32 scan's): with -0 below +0, so
+                    // the lists are sorted as their packed keys
+                    const bool a_first = rank_key(a, ia) > rank_key(b, ib);
                     const bool desc = (i & k) == 0;
                     if (desc != a_first) {
                         key[i] = b; key[p] = a;
@@ -618,7 +620,10 @@ __device__ __forceinline__ int pow2_at_least(int n) {
 
 // Rank by counting over at most this many lower bounds (shard pass 1):
 // every order statistic from one sweep, cheaper than radix passes.
-constexpr int kCountCap = 512;
+constexpr int kCountCap = 256;
+// ... and over at most this many rescored rows (their final order; the rank
+// keys fit the histogram's 8 KB).
+constexpr int kCountSortCap = 512;
 
 __global__ void __launch_bounds__(kRescoreThreads, 3)
 rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t B, float t_q,
@@ -881,13 +886,30 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
             s_id[p] = key_id(keys[p]);
         }
         __syncthreads();
+    } else if (n2 <= kCountSortCap) {
+        // a few hundred rows: each row's place is the number of rank keys
+        // above its own (keys are unique), so the first K go straight to the
+        // output -- one pass and one barrier instead of a bitonic network
+        unsigned long long* keys = reinterpret_cast<unsigned long long*>(s_hist);   // the row list is done
+        for (int p = threadIdx.x; p < n2; p += kRescoreThreads) keys[p] = rank_key(s_key[p], s_id[p]);
+        __syncthreads();
+        for (int i = threadIdx.x; i < n2; i += kRescoreThreads) {
+            const unsigned long long k = keys[i];
+            int r = 0;
+            for (int t = 0; t < n2; ++t) r += keys[t] > k ? 1 : 0;
+            if (r < K) {
+                out_vals[(int64_t)qi * K + r] = key_score(k);
+                out_ids[(int64_t)qi * K + r] = key_id(k);
+            }
+        }
     } else {
         const int p2 = pow2_at_least(n2);
         for (int i = n2 + threadIdx.x; i < p2; i += kRescoreThreads) { s_key[i] = -INFINITY; s_id[i] = INT32_MAX; }
         __syncthreads();
         block_bitonic_desc(s_key, s_id, p2);
     }
-    for (int p = threadIdx.x; p < K; p += kRescoreThreads) {
+    const bool ranked_out = n2 > 32 && n2 <= kCountSortCap;   // written above
+    for (int p = ranked_out ? n2 + threadIdx.x : threadIdx.x; p < K; p += kRescoreThreads) {
         const bool valid = p < n2;
         out_vals[(int64_t)qi * K + p] = valid ? s_key[p] : -INFINITY;
         out_ids[(int64_t)qi * K + p] = valid ? s_id[p] : -1;

@@ -168,7 +168,7 @@ __device__ __forceinline__ bool set_insert(int32_t* table, uint32_t mask, int32_
         if (old == v) return false;
         s = (s + 1) & mask;
     }
-    return false;   // unreachable: the table is sized to at most half full
+    return false;   // unreachable: the table is sized to at most 2/3 full
 }
 
 __device__ __forceinline__ bool set_contains(const int32_t* table, uint32_t mask, int32_t v) {
@@ -182,7 +182,14 @@ __device__ __forceinline__ bool set_contains(const int32_t* table, uint32_t mask
     return false;
 }
 
-__global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
+// Four warps per query and up to eight queries per SM: a query's latency
+// per iteration is mostly dependent loads (its neighbour list, then its rows,
+// about degree / 4 per warp), so more queries in flight per SM raise the
+// throughput more than more warps per query would.
+constexpr int kSearchThreads = 128;
+constexpr int kSearchWarps = kSearchThreads / 32;
+
+__global__ void __launch_bounds__(kSearchThreads, 8) search_kernel(const SearchArgs a) {
     extern __shared__ __align__(16) uint8_t smem[];
     float* s_q = reinterpret_cast<float*>(smem);                        // D (padded to 4)
     float* s_bs = s_q + ((a.D + 3) & ~3);                               // beam scores
@@ -193,8 +200,8 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
     float* s_dist = reinterpret_cast<float*>(s_nb + kMaxDegree);       // neighbour scores
     int32_t* s_hash = reinterpret_cast<int32_t*>(s_dist + kMaxDegree);
     __shared__ int s_scored;
-    __shared__ float s_red_v[kWarps];
-    __shared__ int s_red_i[kWarps];
+    __shared__ float s_red_v[kSearchWarps];
+    __shared__ int s_red_i[kSearchWarps];
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int bw = a.beam;
@@ -208,21 +215,21 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
         float* nbs = s_nbs;
         int32_t* nbi = s_nbi;
         const float* q = a.Q + (int64_t)qi * a.qpitch;
-        for (int d = tid; d < a.D; d += kThreads) s_q[d] = q[d];
-        for (int i = tid; i < a.hash_size; i += kThreads) s_hash[i] = -1;
-        for (int i = tid; i < bw; i += kThreads) { s_bs[i] = -FLT_MAX; s_bi[i] = -1; }
+        for (int d = tid; d < a.D; d += kSearchThreads) s_q[d] = q[d];
+        for (int i = tid; i < a.hash_size; i += kSearchThreads) s_hash[i] = -1;
+        for (int i = tid; i < bw; i += kSearchThreads) { s_bs[i] = -FLT_MAX; s_bi[i] = -1; }
         if (tid == 0) s_scored = 0;
         __syncthreads();
 
         // ---- seeds (src/cmng_search.cu:158-180) ----
         const int num_seeds = min(8 * a.num_parents, bw);
-        if (warp < num_seeds && warp < 8) {
+        for (int w = warp; w < min(num_seeds, 8); w += kSearchWarps) {
             const uint32_t h = __float_as_uint(s_q[0]) ^ __float_as_uint(s_q[1]);
-            const int32_t seed = (int32_t)((h + (uint32_t)warp * 7919u) % (uint32_t)a.N);
+            const int32_t seed = (int32_t)((h + (uint32_t)w * 7919u) % (uint32_t)a.N);
             const float sim = warp_dot_ref_fast(a.E + (int64_t)seed * a.pitch, s_q, a.D, lane);
             if (lane == 0) {
-                bs[warp] = sim;
-                bi[warp] = seed;
+                bs[w] = sim;
+                bi[w] = seed;
                 if (set_insert(s_hash, mask, seed)) atomicAdd(&s_scored, 1);
             }
         }
@@ -248,40 +255,37 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
             ++iters;
             const int32_t* nb = a.nbrs + (int64_t)parent * a.degree;
             // candidate slots: valid id, not visited, first occurrence in the
-            // list.  Each neighbour's row is requested into L2 as its id
-            // arrives, so the rows travel during the visited checks and the
-            // warps' dot products below (about degree / 8 rows per warp, one
-            // after another) wait on L2 instead of one DRAM trip per row.
-            for (int j = tid; j < a.degree; j += kThreads) {
-                const int32_t v = __ldg(nb + j);
-                s_nb[j] = v;
-                if (v >= 0 && v < a.N) prefetch_l2_bulk(a.E + (int64_t)v * a.pitch, row_bytes);
-            }
+            // list.  A candidate's row is requested into L2 as soon as it is
+            // known to be one, so the warps' dot products below (about
+            // degree / 4 rows per warp, one after another) mostly wait on L2
+            // instead of one DRAM trip per row; visited rows are not fetched.
+            for (int j = tid; j < a.degree; j += kSearchThreads) s_nb[j] = __ldg(nb + j);
             __syncthreads();
-            for (int j = tid; j < a.degree; j += kThreads) {
+            for (int j = tid; j < a.degree; j += kSearchThreads) {
                 const int32_t v = s_nb[j];
                 bool ok = v >= 0 && v < a.N && !set_contains(s_hash, mask, v);
                 for (int k = 0; ok && k < j; ++k) ok = s_nb[k] != v;
                 s_dist[j] = ok ? 0.0f : -FLT_MAX;
+                if (ok) prefetch_l2_bulk(a.E + (int64_t)v * a.pitch, row_bytes);
             }
             __syncthreads();
-            for (int j = warp; j < a.degree; j += kWarps) {
+            for (int j = warp; j < a.degree; j += kSearchWarps) {
                 if (s_dist[j] == -FLT_MAX) continue;                    // warp-uniform
                 const int32_t v = s_nb[j];
                 const float sim = warp_dot_ref_fast(a.E + (int64_t)v * a.pitch, s_q, a.D, lane);
                 if (lane == 0) s_dist[j] = sim;
             }
             __syncthreads();
-            for (int j = tid; j < a.degree; j += kThreads)
+            for (int j = tid; j < a.degree; j += kSearchThreads)
                 if (s_dist[j] > -FLT_MAX * 0.5f) { set_insert(s_hash, mask, s_nb[j]); atomicAdd(&s_scored, 1); }
             // rank merge: beam entries keep their order and precede equal candidates
-            for (int o = tid; o < bw; o += kThreads) {
+            for (int o = tid; o < bw; o += kSearchThreads) {
                 const float so = bs[o];
                 int pos = o;
                 for (int j = 0; j < a.degree; ++j) pos += (s_dist[j] > -FLT_MAX * 0.5f && s_dist[j] > so) ? 1 : 0;
                 if (pos < bw) { nbs[pos] = so; nbi[pos] = bi[o]; }
             }
-            for (int j = tid; j < a.degree; j += kThreads) {
+            for (int j = tid; j < a.degree; j += kSearchThreads) {
                 const float d = s_dist[j];
                 if (!(d > -FLT_MAX * 0.5f)) continue;
                 int pos = 0;
@@ -307,10 +311,10 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
 
         // ---- decay (src/cmng_search.cu:275-280) ----
         if (bs != s_bs) {   // the current beam sits in the second buffer: bring it home
-            for (int o = tid; o < bw; o += kThreads) { s_bs[o] = bs[o]; s_bi[o] = bi[o]; }
+            for (int o = tid; o < bw; o += kSearchThreads) { s_bs[o] = bs[o]; s_bi[o] = bi[o]; }
             __syncthreads();
         }
-        for (int o = tid; o < bw; o += kThreads) {
+        for (int o = tid; o < bw; o += kSearchThreads) {
             const int32_t id = s_bi[o];
             if (id >= 0) {
                 const float age = fmaxf(0.0f, a.t_q - __ldg(a.ts + id));
@@ -323,7 +327,7 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
         for (int i = 0; i < kk - 1; ++i) {
             float bv = -INFINITY;
             int bi = INT32_MAX;
-            for (int o = i + tid; o < bw; o += kThreads) {
+            for (int o = i + tid; o < bw; o += kSearchThreads) {
                 const float v = s_bs[o];
                 if (v > bv || (v == bv && o < bi)) { bv = v; bi = o; }
             }
@@ -338,7 +342,7 @@ __global__ void __launch_bounds__(kThreads) search_kernel(const SearchArgs a) {
             if (tid == 0) {
                 float v = s_red_v[0];
                 int best = s_red_i[0];
-                for (int w = 1; w < kWarps; ++w)
+                for (int w = 1; w < kSearchWarps; ++w)
                     if (s_red_v[w] > v || (s_red_v[w] == v && s_red_i[w] < best)) { v = s_red_v[w]; best = s_red_i[w]; }
                 // (max score, lowest position) = the reference's strict '>' scan
                 if (best != i && best != INT32_MAX) {
@@ -643,6 +647,7 @@ __global__ void __launch_bounds__(kThreads, 3) bfs_smem_kernel(const BfsArgs2 a)
     int32_t* list = a.lists + (int64_t)blockIdx.x * a.vcap;
     float* lscore = reinterpret_cast<float*>(list + a.vcap / 2);
     const int limit = min(a.smem_nodes, a.vcap / 2);
+    const uint32_t row_bytes = (uint32_t)a.nc * 16u;
 
     for (int qi = blockIdx.x; qi < a.nq; qi += gridDim.x) {
         for (int i = tid; i < kBfsSlots; i += kThreads) { s_tag[i] = kEmptyTag; s_state[i] = 0ull; }
@@ -676,7 +681,16 @@ __global__ void __launch_bounds__(kThreads, 3) bfs_smem_kernel(const BfsArgs2 a)
                 for (int idx = beg + tid; idx < end; idx += kThreads)
                     lscore[idx] = key2f((uint32_t)(s_state[s_lslot[idx]] & 0xffffffffull));
             } else {
+                // each warp requests its next two rows into L2 while it
+                // scores the current one (three rows travel per warp)
+                auto prefetch_node = [&](int idx) {
+                    if (lane == 0 && idx < end)
+                        prefetch_l2_bulk(reinterpret_cast<const float4*>(a.E) + (int64_t)list[idx] * a.pitch4,
+                                         row_bytes);
+                };
+                prefetch_node(beg + warp + kWarps);
                 for (int idx = beg + warp; idx < end; idx += kWarps) {
+                    prefetch_node(idx + 2 * kWarps);
                     const float own = bfs_own_score(a, q4, list[idx], lane);
                     const float best = key2f((uint32_t)(s_state[s_lslot[idx]] & 0xffffffffull));
                     if (lane == 0) lscore[idx] = fmaxf(best, own * 0.8f);
@@ -686,17 +700,33 @@ __global__ void __launch_bounds__(kThreads, 3) bfs_smem_kernel(const BfsArgs2 a)
             __syncthreads();
             const unsigned long long nst = (unsigned long long)((1u << 4) | (uint32_t)(15 - (h + 1))) << 32;
             const int total = (end - beg) * a.degree;
-            for (int p = tid; p < total; p += kThreads) {
-                const int k = p / a.degree;
-                const int idx = beg + k;
-                const int32_t v = __ldg(a.nbrs + (int64_t)list[idx] * a.degree + (p - k * a.degree));
-                if (v < 0 || v >= a.N) continue;
-                const int slot = smem_claim(s_tag, v);
-                if (slot < 0) { s_ovf = 1; continue; }
-                const unsigned long long old = atomicMax(s_state + slot, nst | f2key(lscore[idx] * a.hop_decay));
-                if ((old >> 32) == 0ull) {
-                    const int pos = atomicAdd(&s_tail, 1);
-                    if (pos < limit) { list[pos] = v; s_lslot[pos] = (uint16_t)slot; } else { s_ovf = 1; }
+            // two edges per thread at a time: both neighbour ids are loaded
+            // before either is claimed
+            for (int p0 = tid; p0 < total; p0 += 2 * kThreads) {
+                int32_t v[2];
+                int ix[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int p = p0 + u * kThreads;
+                    v[u] = -1;
+                    ix[u] = beg;
+                    if (p < total) {
+                        const int k = p / a.degree;
+                        ix[u] = beg + k;
+                        v[u] = __ldg(a.nbrs + (int64_t)list[ix[u]] * a.degree + (p - k * a.degree));
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    if (v[u] < 0 || v[u] >= a.N) continue;
+                    const int slot = smem_claim(s_tag, v[u]);
+                    if (slot < 0) { s_ovf = 1; continue; }
+                    const unsigned long long old =
+                        atomicMax(s_state + slot, nst | f2key(lscore[ix[u]] * a.hop_decay));
+                    if ((old >> 32) == 0ull) {
+                        const int pos = atomicAdd(&s_tail, 1);
+                        if (pos < limit) { list[pos] = v[u]; s_lslot[pos] = (uint16_t)slot; } else { s_ovf = 1; }
+                    }
                 }
             }
             __syncthreads();
@@ -729,7 +759,8 @@ using namespace mars::cmng;
 namespace {
 
 int hash_size_for(int32_t max_iter, int32_t degree) {
-    int64_t need = 2 * (8 + (int64_t)max_iter * degree);
+    // at most 8 seeds + max_iter x degree entries, the table at most 2/3 full
+    int64_t need = (3 * (8 + (int64_t)max_iter * degree) + 1) / 2;
     int64_t h = 256;
     while (h < need) h <<= 1;
     return (int)h;
@@ -895,10 +926,10 @@ int mars_cmng_search_batch(const mars_store* s, const int32_t* d_neighbors, int3
     if (smem > 48 * 1024)
         MARS_CUDA_TRY(cudaFuncSetAttribute(search_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
     int nb = 0, dev = s->device, sms = 0;
-    MARS_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, search_kernel, kThreads, smem));
+    MARS_CUDA_TRY(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, search_kernel, kSearchThreads, smem));
     MARS_CUDA_TRY(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
     const int grid = std::max(1, std::min(nq, std::max(nb, 1) * sms));
-    search_kernel<<<grid, kThreads, smem, st>>>(a);
+    search_kernel<<<grid, kSearchThreads, smem, st>>>(a);
     MARS_CUDA_TRY(cudaGetLastError());
     return MARS_OK;
 }

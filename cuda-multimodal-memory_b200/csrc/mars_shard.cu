@@ -107,56 +107,69 @@ __global__ void pack_keys_kernel(const int32_t* __restrict__ ids, const float* _
     }
 }
 
-// Query qi's top-K of the world x K gathered keys ([rank][B][K] layout): the
-// non-empty keys go to shared memory and the block's radix selection takes
-// the K largest.  world x K <= kMergeKeys.  recs: every shard's bound record
+// Query qi's top-K of the world x K gathered keys ([rank][B][K] layout).
+// Every rank's K keys of a query are sorted (largest first, 0 = no entry,
+// after the real keys), as every path of the batched pipeline writes them,
+// so a key's place in the answer is its place in its own list plus, for
+// every other list, the number of keys above it (a binary search; keys are
+// unique: global ids differ).  One pass over the world x K keys in shared
+// memory, no selection passes.  recs: every shard's bound record
 // (rank-major, 3 B + 1 floats each, the last the shard's failure flag); when
 // some shard's call failed no result is served and counts are -1.
-__global__ void __launch_bounds__(kThreads) merge_keys_kernel(const unsigned long long* __restrict__ keys, int world,
-                                                              int K, int B, const float* __restrict__ recs,
-                                                              int32_t* __restrict__ ids_out,
-                                                              float* __restrict__ vals_out,
-                                                              int32_t* __restrict__ cnt_out) {
-    __shared__ unsigned long long s_keys[kMergeKeys];
-    __shared__ __align__(16) int s_hist[2048];   // also read as 64-bit keys
-    __shared__ int s_misc[16];
+constexpr int kSortedMergeThreads = 128;
+__global__ void __launch_bounds__(kSortedMergeThreads) merge_sorted_keys_kernel(
+    const unsigned long long* __restrict__ keys, int world, int K, int B, const float* __restrict__ recs,
+    int32_t* __restrict__ ids_out, float* __restrict__ vals_out, int32_t* __restrict__ cnt_out) {
+    extern __shared__ unsigned long long s_lists[];   // world x K
+    __shared__ int s_n;
     const int qi = blockIdx.x;
     bool failed = false;
     for (int r = 0; r < world; ++r) failed = failed || __ldcg(recs + (int64_t)r * (3 * (int64_t)B + 1) + 3 * B) > 0.0f;
-    if (failed) {
-        for (int p = threadIdx.x; p < K; p += kThreads) {
-            vals_out[(int64_t)qi * K + p] = -INFINITY;
-            ids_out[(int64_t)qi * K + p] = -1;
-        }
-        if (threadIdx.x == 0 && cnt_out != nullptr) cnt_out[qi] = -1;
-        return;
-    }
+    if (threadIdx.x == 0) s_n = 0;
     const int total = world * K;
-    if (threadIdx.x == 0) s_misc[15] = 0;
+    for (int j = threadIdx.x; j < total; j += kSortedMergeThreads) {
+        const int r = j / K, e = j - r * K;
+        s_lists[j] = __ldg(keys + ((int64_t)r * B + qi) * K + e);
+    }
     __syncthreads();
-    for (int j0 = 0; j0 < total; j0 += kThreads) {
-        const int j = j0 + threadIdx.x;
-        unsigned long long k = 0ull;
-        if (j < total) {
-            const int r = j / K, e = j - r * K;
-            k = __ldg(keys + ((int64_t)r * B + qi) * K + e);
+    if (!failed) {
+        int n = 0;
+        for (int j = threadIdx.x; j < total; j += kSortedMergeThreads) {
+            const unsigned long long x = s_lists[j];
+            if (x == 0ull) continue;
+            ++n;
+            const int r0 = j / K;
+            int rank = j - r0 * K;                     // keys above x in its own list
+            for (int r = 0; r < world && rank < K; ++r) {
+                if (r == r0) continue;
+                const unsigned long long* l = s_lists + r * K;
+                int lo = 0, hi = K;                    // first position whose key is below x
+                while (lo < hi) {
+                    const int mid = (lo + hi) >> 1;
+                    if (l[mid] > x) lo = mid + 1; else hi = mid;
+                }
+                rank += lo;
+            }
+            if (rank < K) {
+                vals_out[(int64_t)qi * K + rank] = key_score(x);
+                ids_out[(int64_t)qi * K + rank] = key_id(x);
+            }
         }
-        warp_append(k != 0ull, k, s_keys, &s_misc[15], kMergeKeys);
+        n = warp_reduce_sum_int(n);
+        if ((threadIdx.x & 31) == 0) atomicAdd(&s_n, n);
     }
     __syncthreads();
-    const int M = s_misc[15];
-    __syncthreads();
-    const int cnt = block_select_topk<kThreads>(s_keys, M, K, s_hist, s_misc);
-    for (int p = threadIdx.x; p < K; p += kThreads) {
-        const bool valid = p < cnt;
-        vals_out[(int64_t)qi * K + p] = valid ? key_score(s_keys[p]) : -INFINITY;
-        ids_out[(int64_t)qi * K + p] = valid ? key_id(s_keys[p]) : -1;
+    const int cnt = failed ? 0 : min(s_n, K);
+    for (int p = cnt + threadIdx.x; p < K; p += kSortedMergeThreads) {
+        vals_out[(int64_t)qi * K + p] = -INFINITY;
+        ids_out[(int64_t)qi * K + p] = -1;
     }
-    if (threadIdx.x == 0 && cnt_out != nullptr) cnt_out[qi] = cnt;
+    if (threadIdx.x == 0 && cnt_out != nullptr) cnt_out[qi] = failed ? -1 : cnt;
 }
 
-// Merge for the sharded query's seeds: as merge_keys_kernel, but a rank
-// that failed sends all-ones keys (kFailedKey, never a rank key of a
+// Merge for the sharded query's seeds (lists in any order): the non-empty
+// keys go to shared memory and the block's radix selection takes the K
+// largest; a rank that failed sends all-ones keys (kFailedKey, never a rank key of a
 // finite score); any such key marks the merge failed (count -1).
 constexpr unsigned long long kFailedKey = ~0ull;
 __global__ void __launch_bounds__(kThreads) merge_keys_flagged_kernel(const unsigned long long* __restrict__ keys,
@@ -462,8 +475,8 @@ int mars_shard_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx, mars_s
     if (c->timed) MARS_CUDA_TRY(cudaEventRecord(c->ev[2], st));
 
     // 5: every rank merges
-    shard::merge_keys_kernel<<<B, shard::kThreads, 0, st>>>(c->d_recv, c->world, K, B, c->d_xrecv[1], d_ids,
-                                                            d_vals, d_counts);
+    shard::merge_sorted_keys_kernel<<<B, shard::kSortedMergeThreads, (size_t)c->world * K * 8, st>>>(
+        c->d_recv, c->world, K, B, c->d_xrecv[1], d_ids, d_vals, d_counts);
     MARS_CUDA_TRY(cudaGetLastError());
     if (c->timed) MARS_CUDA_TRY(cudaEventRecord(c->ev[3], st));
     if (local_rc != MARS_OK) return fail(local_rc, local_msg);
@@ -627,8 +640,8 @@ extern "C" int mars_shard_emulate_query_batch_topk(int32_t world, const mars_sto
             T(cudaMemcpyAsync(all_keys + (size_t)r * n, keys[r], n * 8, cudaMemcpyDeviceToDevice, st0), "key copy");
         }
         if (rc == MARS_OK) {
-            shard::merge_keys_kernel<<<B, shard::kThreads, 0, st0>>>(all_keys, world, K, B, sh.recv[1][0], d_ids,
-                                                                     d_vals, d_counts);
+            shard::merge_sorted_keys_kernel<<<B, shard::kSortedMergeThreads, (size_t)world * K * 8, st0>>>(
+                all_keys, world, K, B, sh.recv[1][0], d_ids, d_vals, d_counts);
             T(cudaGetLastError(), "merge");
         }
         T(cudaStreamSynchronize(st0), "emulation");
