@@ -427,45 +427,66 @@ def run_mars(a):
 
     # ---- end to end through the public API with host buffers --------------
     # A serving loop: every step copies its queries host -> device, answers
-    # them and copies the ids and scores device -> host into one of two pinned
-    # buffers; the host then waits for the previous step's results and reads
-    # them, so the GPU is not idle while the host issues the next step.  The
-    # device buffers are reused in stream order.
+    # them and copies the ids, scores and counts device -> host into one of
+    # two pinned buffers; the host waits for the previous step's results and
+    # reads them, so the GPU is not idle while the host issues the next step.
+    # The copies run on their own stream: step s + 1's queries travel while
+    # step s is answered, and step s's results while step s + 1 is; the
+    # device buffers (two of each) are reused in event order.
     Qpin = torch.from_numpy(Qh).pin_memory()
-    qbuf = torch.empty((Q, a.dim), dtype=torch.float32, device="cuda")
+    cstream = torch.cuda.Stream(device=torch.device("cuda", local))
+    qbufs = [torch.empty((Q, a.dim), dtype=torch.float32, device="cuda") for _ in range(2)]
     # one packed result buffer per step (ids | scores | counts): one D2H copy
-    res = torch.empty(2 * Q * K + Q, dtype=torch.int32, device="cuda")
-    r_ids = res[:Q * K].view(Q, K)
-    r_vals = res[Q * K:2 * Q * K].view(torch.float32).view(Q, K)
-    r_cnt = res[2 * Q * K:]
+    ress = [torch.empty(2 * Q * K + Q, dtype=torch.int32, device="cuda") for _ in range(2)]
     outs = [torch.empty(2 * Q * K + Q, dtype=torch.int32).pin_memory() for _ in range(2)]
     outs_np = [o.numpy() for o in outs]
-    done = [torch.cuda.Event() for _ in range(2)]
+    q_in = [torch.cuda.Event() for _ in range(2)]       # a step's queries are on the device
+    answered = [torch.cuda.Event() for _ in range(2)]   # a step's results are in its device buffer
+    done = [torch.cuda.Event() for _ in range(2)]       # ... and in its pinned host buffer
     checksum = 0
     e2e_valid = True
+
+    def h2d(step):
+        base = (step * Q) % (n_pool - Q + 1)
+        with torch.cuda.stream(cstream):
+            qbufs[step % 2].copy_(Qpin[base:base + Q], non_blocking=True)
+            q_in[step % 2].record(cstream)
+
     barrier()
     t0 = time.perf_counter()
+    h2d(0)
     for s in range(a.steps + 1):
         if s < a.steps:
             b = s % 2
-            base = (s * Q) % (n_pool - Q + 1)
-            qbuf.copy_(Qpin[base:base + Q], non_blocking=True)
+            res = ress[b]
+            r_ids = res[:Q * K].view(Q, K)
+            r_vals = res[Q * K:2 * Q * K].view(torch.float32).view(Q, K)
+            r_cnt = res[2 * Q * K:]
+            stream.wait_event(q_in[b])
             if sharded:
-                bc.query_batch_topk(store, qbuf, Q, a.ts_max, a.lam, K, ids, vals, use_importance=True,
+                bc.query_batch_topk(store, qbufs[b], Q, a.ts_max, a.lam, K, ids, vals, use_importance=True,
                                     row_offset=lo, stream=ctx.stream)
                 dist.all_gather_into_tensor(gids, ids)
                 dist.all_gather_into_tensor(gvals, vals)
                 ctx.topk_merge_batch(gids, gvals, world, K, Q, r_ids, r_vals, r_cnt, stream=ctx.stream)
             else:
-                bc.query_batch_topk(store, qbuf, Q, a.ts_max, a.lam, K, r_ids, r_vals, r_cnt,
+                bc.query_batch_topk(store, qbufs[b], Q, a.ts_max, a.lam, K, r_ids, r_vals, r_cnt,
                                     use_importance=True, row_offset=lo, stream=ctx.stream)
-            outs[b].copy_(res, non_blocking=True)
-            done[b].record(stream)
+            answered[b].record(stream)
+            if s + 1 < a.steps:
+                # the next step's queries, into the buffer step s - 1 read
+                # (answered: the copy stream waited for it before its D2H)
+                h2d(s + 1)
+            cstream.wait_event(answered[b])
+            with torch.cuda.stream(cstream):
+                outs[b].copy_(res, non_blocking=True)
+                done[b].record(cstream)
         if s > 0:   # the previous step's results, read and checked on the host
             p = (s - 1) % 2
             done[p].synchronize()
             e2e_valid = e2e_valid and bool(outs_np[p][2 * Q * K:].min() == K)
             checksum += int(outs_np[p][0])
+    torch.cuda.synchronize()
     dt = time.perf_counter() - t0
     bc.last_stats()      # raises if the last step's pipeline reported an error
     if world > 1:
@@ -479,9 +500,10 @@ def run_mars(a):
            "path": "pinned H2D of the step's queries, mars_query_batch_topk"
                    + (" per shard, NCCL all-gather, mars_topk_merge_batch" if sharded else
                       (" on every replica" if world > 1 else ""))
-                   + ", one packed D2H of the top-K ids, scores and counts into one of two pinned buffers; "
-                     "the host waits for and reads each step's results (checking every count) while the "
-                     "next step runs"}
+                   + ", one packed D2H of the top-K ids, scores and counts into one of two pinned buffers "
+                     "(both copies on a copy stream, overlapped with the neighbouring steps' compute); the "
+                     "host waits for and reads each step's results (checking every count) while the next "
+                     "step runs"}
     latency = None
     if world == 1:
         # single-query latency through mars_query (host query in, host results out)
