@@ -624,6 +624,8 @@ constexpr int kCountCap = 256;
 // ... and over at most this many rescored rows (their final order; the rank
 // keys fit the histogram's 8 KB).
 constexpr int kCountSortCap = 512;
+// Rows each rescoring warp keeps requested ahead of the one it scores.
+constexpr int kRescoreAhead = 4;
 
 __global__ void __launch_bounds__(kRescoreThreads, 3)
 rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t B, float t_q,
@@ -823,8 +825,8 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     }
     __syncthreads();
     const int nk = min(s_nk, kRowsCap);
-    // each warp requests its next two rows into L2 (one bulk prefetch each)
-    // while it scores the current one: three of its rows travel at a time
+    // each warp requests its next four rows into L2 (one bulk prefetch each)
+    // while it scores the current one: five of its rows travel at a time
     // instead of one, and L2 holds only rows about to be read
     const uint32_t row_bytes = (uint32_t)s.nc * 16u;
     auto prefetch_row = [&](int t) {
@@ -842,9 +844,9 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
             s_id[pos] = rr + row_offset;
         }
     };
-    prefetch_row(warp + kWarps);
+    for (int d = 1; d < kRescoreAhead; ++d) prefetch_row(warp + d * kWarps);
     for (int t = warp; t < nk; t += kWarps) {
-        prefetch_row(t + 2 * kWarps);
+        prefetch_row(t + kRescoreAhead * kWarps);
         score_row(s_rows[t]);
     }
     if (s_nk > kRowsCap) {
