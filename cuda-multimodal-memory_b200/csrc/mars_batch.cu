@@ -107,6 +107,13 @@ __device__ __forceinline__ float row_weight(const RowMeta& m, int32_t row) {
     return w;
 }
 
+// One short-listed candidate as a single 16-byte record: row, approximate
+// fused score and its error slack (margin x |weight|) as float bits (the
+// exact score lies in score -+ slack).  One store per candidate.
+__device__ __forceinline__ int4 cand_entry(int32_t row, float f, float slack) {
+    return make_int4(row, __float_as_int(f), __float_as_int(slack), 0);
+}
+
 struct GemmArgs {
     int32_t B, n, nkb;               // queries, rows, K blocks
     int32_t qtiles, rtiles;          // tiles along queries / rows
@@ -116,9 +123,7 @@ struct GemmArgs {
     const float* theta;              // B thresholds (candidate mode)
     const float* margin;             // B margins
     float* sample_buf;               // [n_tiles][B][kJ]
-    int32_t* cand;                   // [B][cap] row ids
-    float* cand_f;                   // [B][cap] approximate fused scores
-    float* cand_s;                   // [B][cap] their error slack (margin x |weight|)
+    int4* cand;                      // [B][cap] candidates (cand_entry)
     int32_t* cand_cnt;               // [B]
     int32_t cap;
     int32_t self_base;               // query b leaves out row self_base + b (-1: none)
@@ -294,10 +299,13 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                         for (int j = 0; j < 32; ++j) {
                             if (pass & (1u << j)) {
                                 if (pos < a.cap) {
+                                    // three 4-byte stores into the one 16-byte record (a 16-byte
+                                    // store here costs the epilogue registers it does not have)
                                     const float w = s_w[c * 32 + j];
-                                    a.cand[(int64_t)q * a.cap + pos] = rbase + j;
-                                    a.cand_f[(int64_t)q * a.cap + pos] = __uint_as_float(r[j]) * w;
-                                    a.cand_s[(int64_t)q * a.cap + pos] = mg * fabsf(w);
+                                    int* e = reinterpret_cast<int*>(a.cand + (int64_t)q * a.cap + pos);
+                                    e[0] = rbase + j;
+                                    e[1] = __float_as_int(__uint_as_float(r[j]) * w);
+                                    e[2] = __float_as_int(mg * fabsf(w));
                                 }
                                 ++pos;
                             }
@@ -631,9 +639,7 @@ __global__ void __launch_bounds__(kRescoreThreads, 3)
 rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t B, float t_q,
                float lambda, int32_t use_imp, int32_t K, int32_t row_offset,
                const float* __restrict__ theta, const float* __restrict__ margin,
-               const int32_t* __restrict__ cand,
-               const float* __restrict__ cand_f, const float* __restrict__ cand_s,
-               const int32_t* __restrict__ cand_cnt, int32_t cap,
+               const int4* __restrict__ cand, const int32_t* __restrict__ cand_cnt, int32_t cap,
                int32_t* __restrict__ out_ids, float* __restrict__ out_vals,
                int32_t* __restrict__ out_cnt, int32_t* __restrict__ fallback,
                int32_t* __restrict__ rescored, const int32_t* __restrict__ bad,
@@ -701,9 +707,9 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         return;
     }
     const float th = theta[qi];
-    const int32_t* ci = cand + (int64_t)qi * cap;
-    const float* cf = cand_f + (int64_t)qi * cap;
-    const float* cs = cand_s + (int64_t)qi * cap;   // slack: the exact score lies in cf -+ cs
+    // candidate i: row .x, approximate score .y and slack .z (float bits);
+    // the exact score lies in score -+ slack
+    const int4* cq = cand + (int64_t)qi * cap;
 
     // ---- pass 1: lower bounds, completeness, K-th largest lower bound -------
     // Unsharded, K <= 32: every warp keeps its K best lower bounds (ranked by
@@ -719,7 +725,11 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     for (int i0 = warp * 32; i0 < nc_; i0 += kRescoreThreads) {
         const int i = i0 + lane;
         const bool in = i < nc_;
-        const float lo = in ? cf[i] - cs[i] : -INFINITY;
+        float lo = -INFINITY;
+        if (in) {
+            const int4 e = __ldcg(cq + i);
+            lo = __int_as_float(e.y) - __int_as_float(e.z);
+        }
         ge += (in && lo >= th) ? 1 : 0;
         if (warp_lists) top.offer_lanes(lo, i, in, lane);
         else if ((need_th2 || shard_pass1) && in) s_key[i] = lo;
@@ -813,8 +823,9 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         int32_t r = 0;
         bool keep = false;
         if (i < nc_) {
-            r = ci[i];
-            keep = cf[i] + cs[i] >= th2;
+            const int4 e = __ldcg(cq + i);
+            r = e.x;
+            keep = __int_as_float(e.y) + __int_as_float(e.z) >= th2;
         }
         const unsigned mk = __ballot_sync(0xffffffffu, keep);
         int base = 0;
@@ -857,8 +868,9 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
             int32_t r = 0;
             bool keep = false;
             if (i < nc_) {
-                r = ci[i];
-                keep = cf[i] + cs[i] >= th2;
+                const int4 e = __ldcg(cq + i);
+                r = e.x;
+                keep = __int_as_float(e.y) + __int_as_float(e.z) >= th2;
             }
             // the first kRowsCap kept rows (in list order) are done; ranks are
             // not known here, so every kept row not in the list is scored by
@@ -966,9 +978,7 @@ struct SmallArgs {
     const float* theta;
     const float* margin;
     float* sample_buf;               // sample mode: [n_tiles][B][sample_per_tile] maxima
-    int32_t* cand;
-    float* cand_f;
-    float* cand_s;
+    int4* cand;                      // [B][cap] candidates (cand_entry)
     int32_t* cand_cnt;
     int32_t cap;
     int32_t self_base;
@@ -1180,11 +1190,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
             for (int i = et; i < m; i += kSmallEpi) {
                 const int q = s_cq[i];
                 const int pos = s_qbase[q] + atomicAdd(&s_qn[q], 1);
-                if (pos < a.cap) {
-                    a.cand[(int64_t)q * a.cap + pos] = s_crow[i];
-                    a.cand_f[(int64_t)q * a.cap + pos] = s_cf[i];
-                    a.cand_s[(int64_t)q * a.cap + pos] = s_cs[i];
-                }
+                if (pos < a.cap) a.cand[(int64_t)q * a.cap + pos] = cand_entry(s_crow[i], s_cf[i], s_cs[i]);
             }
             asm volatile("bar.sync 1, 256;" ::: "memory");
             for (int q = et; q < a.B; q += kSmallEpi) s_qn[q] = 0;
@@ -1272,11 +1278,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                             s_cs[p] = slack;
                         } else {   // the stage is full: straight to the query's list
                             const int pos = atomicAdd(a.cand_cnt + q, 1);
-                            if (pos < a.cap) {
-                                a.cand[(int64_t)q * a.cap + pos] = row;
-                                a.cand_f[(int64_t)q * a.cap + pos] = f;
-                                a.cand_s[(int64_t)q * a.cap + pos] = slack;
-                            }
+                            if (pos < a.cap) a.cand[(int64_t)q * a.cap + pos] = cand_entry(row, f, slack);
                         }
                     }
                     }
@@ -1360,8 +1362,7 @@ struct mars_batch_ctx {
     cudaStream_t stream = nullptr;
     float* d_margin = nullptr;       // max_batch
     float* d_theta = nullptr;
-    int32_t* d_cand = nullptr;       // max_batch * cap
-    float* d_cand_f = nullptr;       // max_batch * cap
+    int4* d_cand = nullptr;          // max_batch * cap candidate records
     // the call's status words, one block read back with one copy:
     // [err, sync_err, fallback[max_batch], cand_cnt[max_batch], rescored[max_batch], bad[max_batch]]
     // (err: a pipeline wait gave up; sync_err: the grid-wide arrival wait gave up)
@@ -1489,7 +1490,7 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     c->dim = dim;
     c->max_k = max_k;
     c->max_nodes = max_nodes;
-    c->cap = 16384;
+    c->cap = kSortCap;   // a query with more candidates is rescanned exactly anyway
     c->num_sms = prop.multiProcessorCount;
     c->max_smem = (int32_t)prop.sharedMemPerBlockOptin;
     c->coop = prop.cooperativeLaunch != 0;
@@ -1502,8 +1503,7 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     T(cudaEventCreate(&c->ev_gemm[1]), "event");
     T(cudaMalloc(&c->d_margin, (size_t)max_batch * 4), "margins");
     T(cudaMalloc(&c->d_theta, (size_t)max_batch * 4), "thresholds");
-    T(cudaMalloc(&c->d_cand, (size_t)max_batch * c->cap * 4), "candidates");
-    T(cudaMalloc(&c->d_cand_f, (size_t)max_batch * c->cap * 8), "candidate scores and slacks");
+    T(cudaMalloc(&c->d_cand, (size_t)max_batch * c->cap * sizeof(int4)), "candidates");
     const size_t status_words = 2 + 4 * (size_t)max_batch;
     T(cudaMalloc(&c->d_status, status_words * 4), "status words");
     T(cudaHostAlloc(&c->h_status, status_words * 4, cudaHostAllocMapped), "pinned status words");
@@ -1575,7 +1575,7 @@ int mars_batch_ctx_destroy(mars_batch_ctx* c) {
     MarsDeviceGuard g(c->device);
     if (c->stream) cudaStreamSynchronize(c->stream);
     cudaFree(c->d_margin); cudaFree(c->d_theta); cudaFree(c->d_cand);
-    cudaFree(c->d_cand_f); cudaFree(c->d_sample); cudaFree(c->d_sample_rt);
+    cudaFree(c->d_sample); cudaFree(c->d_sample_rt);
     cudaFree(c->d_status); cudaFreeHost(c->h_status);
     cudaFree(c->d_q16);
     cudaFree(c->d_fb_val); cudaFree(c->d_fb_idx); cudaFree(c->d_fb_slots);
@@ -1851,8 +1851,6 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         sa.margin = c->d_margin;
         sa.sample_buf = c->d_sample;
         sa.cand = c->d_cand;
-        sa.cand_f = c->d_cand_f;
-        sa.cand_s = c->d_cand_f + (size_t)c->max_batch * c->cap;
         sa.cand_cnt = c->d_cand_cnt;
         sa.cap = c->cap;
         sa.self_base = self_base;
@@ -1907,8 +1905,6 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         ga.margin = c->d_margin;
         ga.sample_buf = c->d_sample;
         ga.cand = c->d_cand;
-        ga.cand_f = c->d_cand_f;
-        ga.cand_s = c->d_cand_f + (size_t)c->max_batch * c->cap;
         ga.cand_cnt = c->d_cand_cnt;
         ga.cap = c->cap;
         ga.self_base = self_base;
@@ -1960,7 +1956,6 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     auto rescore = [&](float* bound_out, const float* bound_in) {
         rescore_kernel<<<B, kRescoreThreads, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, use_importance, K,
                                                       row_offset, c->d_theta, c->d_margin, c->d_cand,
-                                                      c->d_cand_f, c->d_cand_f + (size_t)c->max_batch * c->cap,
                                                       c->d_cand_cnt, c->cap, d_ids, d_vals, d_counts,
                                                       c->d_fallback, c->d_rescored, f16 ? c->d_bad : nullptr,
                                                       c->d_status, bound_out, bound_in,
