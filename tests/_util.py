@@ -98,3 +98,27 @@ def assert_bfs_set_valued(oracle_mod, corpus, q, t_q, lam, K, hops, decay, ref_i
             f"{what}: node {nid} score {s} not reachable from any parent {possible}"
     if ours_scores is not None and len(ours_scores) and len(ref_scores):
         assert float(ours_scores[-1]) >= float(ref_scores[-1]) - atol - rtol * abs(ref_scores[-1])
+
+
+def load_golden(path: str):
+    """np.load of a golden fixture after checking its SHA-256 against the
+    MANIFEST.sha256 beside it: a fixture that was truncated, corrupted or
+    replaced is refused (ValueError) instead of silently pinning the oracle
+    to wrong vectors."""
+    import hashlib
+    import os
+    folder, name = os.path.split(path)
+    want = None
+    with open(os.path.join(folder, "MANIFEST.sha256")) as f:
+        for line in f:
+            parts = line.split()
+            if len(parts) == 2 and parts[1] == name:
+                want = parts[0]
+    if want is None:
+        raise ValueError(f"{name}: not listed in MANIFEST.sha256")
+    with open(path, "rb") as f:
+        got = hashlib.sha256(f.read()).hexdigest()
+    if got != want:
+        raise ValueError(f"{name}: SHA-256 {got} does not match the manifest ({want})")
+    return np.load(path)
+

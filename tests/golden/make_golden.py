@@ -82,6 +82,15 @@ def main() -> None:
         path = os.path.join(HERE, f"{name}.npz")
         np.savez_compressed(path, **out)
         print(f"wrote {path}  N={N} dim={dim} edges={len(col_idx)}")
+    # the checksums the tests verify before they read a fixture
+    import hashlib
+    lines = []
+    for f in sorted(os.listdir(HERE)):
+        if f.endswith(".npz"):
+            with open(os.path.join(HERE, f), "rb") as fh:
+                lines.append(f"{hashlib.sha256(fh.read()).hexdigest()}  {f}")
+    with open(os.path.join(HERE, "MANIFEST.sha256"), "w") as fh:
+        fh.write("\n".join(lines) + "\n")
 
 
 if __name__ == "__main__":

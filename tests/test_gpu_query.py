@@ -16,7 +16,7 @@ import numpy as np
 import pytest
 
 import oracle as O
-from _util import assert_ranked_equivalent, assert_topk_matches_scores, close
+from _util import assert_ranked_equivalent, assert_topk_matches_scores, close, load_golden
 
 pytestmark = pytest.mark.gpu
 
@@ -218,7 +218,7 @@ def test_graph_replay_equals_direct_launch(torch_mod, mb):
 
 @pytest.mark.parametrize("name", ["pipeline_d64", "pipeline_d768"])
 def test_gpu_matches_reference_golden(torch_mod, mb, name):
-    z = np.load(os.path.join(HERE, "golden", f"{name}.npz"))
+    z = load_golden(os.path.join(HERE, "golden", f"{name}.npz"))
     meta = json.loads(bytes(z["meta"]).decode())
     E, mods, ts = z["emb"], z["mods"], z["ts"]
     st, ctx = build(mb, E, mods, ts, None, z["row_off"], z["col_idx"])

@@ -14,18 +14,36 @@ import numpy as np
 import pytest
 
 import oracle as O
-from _util import assert_ranked_equivalent, close
+from _util import assert_ranked_equivalent, close, load_golden
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CASES = ["pipeline_d64", "pipeline_d768"]
 
 
 def _load(name):
-    z = np.load(os.path.join(HERE, "golden", f"{name}.npz"))
+    z = load_golden(os.path.join(HERE, "golden", f"{name}.npz"))
     meta = json.loads(bytes(z["meta"]).decode())
     corpus = O.Corpus(E=z["emb"], ts=z["ts"], mod=z["mods"], row_offsets=z["row_off"],
                       col_indices=z["col_idx"])
     return z, meta, corpus
+
+
+def test_corrupt_or_unlisted_fixture_is_refused(tmp_path):
+    """A fixture whose bytes changed (one flipped byte) or that the manifest
+    does not list is refused before any test reads it."""
+    import shutil
+    src = os.path.join(HERE, "golden")
+    shutil.copy(os.path.join(src, "MANIFEST.sha256"), tmp_path / "MANIFEST.sha256")
+    shutil.copy(os.path.join(src, "pipeline_d64.npz"), tmp_path / "pipeline_d64.npz")
+    load_golden(str(tmp_path / "pipeline_d64.npz"))           # intact: loads
+    raw = bytearray((tmp_path / "pipeline_d64.npz").read_bytes())
+    raw[len(raw) // 2] ^= 0x01
+    (tmp_path / "pipeline_d64.npz").write_bytes(bytes(raw))
+    with pytest.raises(ValueError, match="does not match"):
+        load_golden(str(tmp_path / "pipeline_d64.npz"))
+    shutil.copy(os.path.join(src, "pipeline_d64.npz"), tmp_path / "other.npz")
+    with pytest.raises(ValueError, match="not listed"):
+        load_golden(str(tmp_path / "other.npz"))
 
 
 @pytest.mark.parametrize("name", CASES)
