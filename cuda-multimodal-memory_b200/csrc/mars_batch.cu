@@ -253,6 +253,7 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
         int buf = 0;
         uint32_t bphase = 0;
         const int et = threadIdx.x - 64;           // 0..255 among the epilogue threads
+        float* stg = s_w + kBN + (warp - 2) * (32 * 32);   // this warp's 32 x 32 score stage
         for (int t = blockIdx.x; t < a.n_tiles; t += gridDim.x) {
             int qt, row0;
             tile_coords(a, t, MODE, qt, row0);
@@ -280,38 +281,43 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                 sm100::tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(sub * 32) << 16) +
                                               (uint32_t)(buf * kBN + c * 32), r);
                 sm100::tmem_ld_wait();
-                if (!qv) continue;
                 const int rbase = row0 + c * 32;
                 if constexpr (MODE == kCandidates) {
-                    // which of the 32 rows pass; one atomic per chunk for all
-                    // of them (clustered data can make a query's candidates
-                    // dense in a few tiles), then the writes
+                    // which of the 32 rows pass (none for an absent query)
                     uint32_t pass = 0u;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
                         const float w = (rbase + j == self_row) ? NAN : s_w[c * 32 + j];
                         const float f = __uint_as_float(r[j]) * w;
-                        if (f + mg * fabsf(w) >= th) pass |= 1u << j;   // NaN weights never pass
+                        if (qv && f + mg * fabsf(w) >= th) pass |= 1u << j;   // NaN weights never pass
                     }
-                    if (pass != 0u) {
-                        int pos = atomicAdd(a.cand_cnt + q, __popc(pass));
+                    if (__any_sync(0xffffffffu, pass != 0u)) {
+                        // the warp's 32 x 32 scores go to its shared-memory
+                        // stage, column j of lane l at [j][l] (no bank
+                        // conflicts writing or reading), so each lane then
+                        // walks only its own hits: one atomic for all of them
+                        // (clustered data can make a query's candidates dense
+                        // in a few tiles) and one 16-byte record per hit
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) {
-                            if (pass & (1u << j)) {
+                        for (int j = 0; j < 32; ++j) stg[j * 32 + lane] = __uint_as_float(r[j]);
+                        __syncwarp();
+                        if (pass != 0u) {
+                            int pos = atomicAdd(a.cand_cnt + q, __popc(pass));
+                            int4* dst = a.cand + (int64_t)q * a.cap;
+                            while (pass != 0u) {
+                                const int j = __ffs(pass) - 1;
+                                pass &= pass - 1u;
                                 if (pos < a.cap) {
-                                    // three 4-byte stores into the one 16-byte record (a 16-byte
-                                    // store here costs the epilogue registers it does not have)
                                     const float w = s_w[c * 32 + j];
-                                    int* e = reinterpret_cast<int*>(a.cand + (int64_t)q * a.cap + pos);
-                                    e[0] = rbase + j;
-                                    e[1] = __float_as_int(__uint_as_float(r[j]) * w);
-                                    e[2] = __float_as_int(mg * fabsf(w));
+                                    dst[pos] = cand_entry(rbase + j, stg[j * 32 + lane] * w, mg * fabsf(w));
                                 }
                                 ++pos;
                             }
                         }
+                        __syncwarp();   // the next chunk rewrites the stage
                     }
                 } else {
+                    if (!qv) continue;
 #pragma unroll
                     for (int j4 = 0; j4 < 8; ++j4) {
                         const float4 w4 = reinterpret_cast<const float4*>(s_w + c * 32)[j4];
@@ -1467,7 +1473,9 @@ int cached_map(MapCache& mc, const void* base, int64_t rows, int64_t cols, int64
 }
 
 constexpr size_t kGemmSmem = (size_t)kStages * kStageBytes + 1024 /*align*/ + 256 /*barriers*/ +
-                             kBN * sizeof(float) /*row weights*/;
+                             kBN * sizeof(float) /*row weights*/ +
+                             (kGemmEpi / 32) * 32 * 32 * sizeof(float) /*epilogue warps' score stages*/;
+static_assert(kGemmSmem <= 232448, "the 128 x 256 tile's shared memory exceeds the opt-in limit");
 
 }  // namespace
 
@@ -1497,7 +1505,11 @@ int mars_batch_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     c->single_launch = c->coop;
     c->sample_tiles_cap = 0;
     int rc = MARS_OK;
-    auto T = [&](cudaError_t e, const char* w) { if (rc == MARS_OK && e != cudaSuccess) rc = cuda_fail(e, w, __FILE__, __LINE__); };
+    auto T = [&](cudaError_t e, const char* w) {
+        if (e == cudaSuccess) return;
+        if (rc == MARS_OK) rc = cuda_fail(e, w, __FILE__, __LINE__);   // records the first failure
+        else (void)cudaGetLastError();                                 // later ones only clear the state
+    };
     T(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
     T(cudaEventCreate(&c->ev_gemm[0]), "event");
     T(cudaEventCreate(&c->ev_gemm[1]), "event");

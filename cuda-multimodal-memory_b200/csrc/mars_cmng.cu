@@ -820,8 +820,10 @@ int mars_cmng_build_rows(const mars_store* s, int32_t first, int32_t count, int3
         bcache.rows = 0;
         if (cudaMalloc(&bcache.d_knn, entries * 4) != cudaSuccess ||
             cudaMalloc(&bcache.d_vals, entries * 4) != cudaSuccess ||
-            cudaMalloc(&bcache.d_cnt, (size_t)count * 4) != cudaSuccess)
+            cudaMalloc(&bcache.d_cnt, (size_t)count * 4) != cudaSuccess) {
+            (void)cudaGetLastError();   // the failed allocation's error is reported here, not by the next launch
             return fail(MARS_ERR_OOM, "mars_cmng_build: kNN buffers");
+        }
         bcache.entries = entries;
         bcache.rows = count;
     }
@@ -983,7 +985,11 @@ int mars_cmng_ctx_create(int32_t device, int32_t max_queries, int32_t K, int32_t
     cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, bfs_kernel<1>, kThreads, 0);
     c->grid = std::max(1, std::min(max_queries, sms * std::max(1, std::min(nb, 4))));
     int rc = MARS_OK;
-    auto T = [&](cudaError_t e, const char* w) { if (rc == MARS_OK && e != cudaSuccess) rc = cuda_fail(e, w, __FILE__, __LINE__); };
+    auto T = [&](cudaError_t e, const char* w) {
+        if (e == cudaSuccess) return;
+        if (rc == MARS_OK) rc = cuda_fail(e, w, __FILE__, __LINE__);   // records the first failure
+        else (void)cudaGetLastError();                                 // later ones only clear the state
+    };
     T(cudaMalloc(&c->d_seed_ids, (size_t)max_queries * K * 4), "seeds");
     T(cudaMalloc(&c->d_seed_scores, (size_t)max_queries * K * 4), "seeds");
     T(cudaMalloc(&c->d_seed_cnt, (size_t)max_queries * 4), "seeds");

@@ -13,7 +13,8 @@ namespace mars {
 
 struct NcclApi {
     ncclResult_t (*GetUniqueId)(ncclUniqueId*);
-    ncclResult_t (*CommInitRank)(ncclComm_t*, int, ncclUniqueId, int);
+    ncclResult_t (*CommInitRankConfig)(ncclComm_t*, int, ncclUniqueId, int, ncclConfig_t*);
+    ncclResult_t (*CommFinalize)(ncclComm_t);
     ncclResult_t (*CommDestroy)(ncclComm_t);
     ncclResult_t (*CommAbort)(ncclComm_t);
     ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*);

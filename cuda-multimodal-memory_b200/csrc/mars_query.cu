@@ -268,7 +268,9 @@ int mars_query_ctx_create(int32_t device, int32_t max_nodes, int32_t dim, int32_
     const size_t nmax = (size_t)std::max(max_nodes, 1);
     int rc = MARS_OK;
     auto T = [&](cudaError_t e, const char* what) {
-        if (rc == MARS_OK && e != cudaSuccess) rc = cuda_fail(e, what, __FILE__, __LINE__);
+        if (e == cudaSuccess) return;
+        if (rc == MARS_OK) rc = cuda_fail(e, what, __FILE__, __LINE__);   // records the first failure
+        else (void)cudaGetLastError();                                 // later ones only clear the state
     };
     T(cudaStreamCreateWithFlags(&c->stream, cudaStreamNonBlocking), "stream");
     for (int i = 0; i < 5; ++i) T(cudaEventCreate(&c->ev[i]), "event");

@@ -43,6 +43,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstddef>
+#include <chrono>
 #include <condition_variable>
 #include <cstring>
 #include <mutex>
@@ -79,7 +80,8 @@ const NcclApi* nccl_api(const char** why) {
             all = all && fn != nullptr;
         };
         get(api.GetUniqueId, "ncclGetUniqueId");
-        get(api.CommInitRank, "ncclCommInitRank");
+        get(api.CommInitRankConfig, "ncclCommInitRankConfig");
+        get(api.CommFinalize, "ncclCommFinalize");
         get(api.CommDestroy, "ncclCommDestroy");
         get(api.CommAbort, "ncclCommAbort");
         get(api.CommGetAsyncError, "ncclCommGetAsyncError");
@@ -227,6 +229,7 @@ struct mars_shard_comm {
     float* d_xrecv[2] = {nullptr, nullptr};  // every rank's, rank-major
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};   // local / exchange / merge boundaries
     bool timed = false;
+    int32_t timeout_ms = 0;                 // deadline of NCCL's set-up work (creation, first use, teardown)
     void* bfs_state = nullptr;              // mars_shard_query's scratch (made on first use)
 };
 
@@ -237,16 +240,39 @@ int nccl_fail(const NcclApi* api, ncclResult_t r, const char* what) {
                                    (api ? api->GetErrorString(r) : "?") + ")");
 }
 
+// The communicator is non-blocking: a call returns once its work is
+// enqueued, or ncclInProgress while NCCL still sets something up in the
+// background (the communicator itself, a connection on first use, the
+// teardown).  The next NCCL call may only follow once the communicator has
+// left that state, polled here up to the communicator's deadline: a peer
+// that never arrives ends the wait with MARS_ERR_TIMEOUT instead of a hang.
+int nccl_settle(const NcclApi* api, ncclComm_t comm, ncclResult_t r, int32_t timeout_ms, const char* what) {
+    if (r != ncclSuccess && r != ncclInProgress) return nccl_fail(api, r, what);
+    if (r == ncclSuccess) return MARS_OK;
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        ncclResult_t state = ncclSuccess;
+        const ncclResult_t q = api->CommGetAsyncError(comm, &state);
+        if (q != ncclSuccess) return nccl_fail(api, q, what);
+        if (state == ncclSuccess) return MARS_OK;
+        if (state != ncclInProgress) return nccl_fail(api, state, what);
+        const auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(std::chrono::steady_clock::now() - t0);
+        if (timeout_ms > 0 && ms.count() >= timeout_ms)
+            return fail(MARS_ERR_TIMEOUT, std::string(what) + ": NCCL still in progress after " +
+                                              std::to_string(timeout_ms) + " ms (a peer that did not join?)");
+        std::this_thread::sleep_for(std::chrono::microseconds(20));
+    }
+}
+
 // all-gather of one record (`which`: 0 threshold, 1 bound) of `count`
 // floats per rank, on st
 int exchange_records(void* arg, int which, int32_t count, cudaStream_t st) {
     auto* c = static_cast<mars_shard_comm*>(arg);
     const ncclResult_t r = c->nccl->AllGather(c->d_xsend[which], c->d_xrecv[which], (size_t)count, ncclFloat32,
                                               c->comm, st);
-    if (r != ncclSuccess)
-        return nccl_fail(c->nccl, r, which == 0 ? "mars_shard_query_batch_topk: threshold all-gather"
-                                                : "mars_shard_query_batch_topk: bound all-gather");
-    return MARS_OK;
+    return nccl_settle(c->nccl, c->comm, r, c->timeout_ms,
+                       which == 0 ? "mars_shard_query_batch_topk: threshold all-gather"
+                                  : "mars_shard_query_batch_topk: bound all-gather");
 }
 
 }  // namespace
@@ -280,7 +306,7 @@ int mars::shard_gather_merge(const ShardCommView& v, const int32_t* d_ids, const
         MARS_CUDA_TRY(cudaMemsetAsync(c->d_send, 0xff, (size_t)n * 8, st));   // kFailedKey
     }
     const ncclResult_t r = c->nccl->AllGather(c->d_send, c->d_recv, (size_t)n, ncclUint64, c->comm, st);
-    if (r != ncclSuccess) return nccl_fail(c->nccl, r, "shard merge: all-gather");
+    MARS_TRY(nccl_settle(c->nccl, c->comm, r, c->timeout_ms, "shard merge: all-gather"));
     shard::merge_keys_flagged_kernel<<<B, shard::kThreads, 0, st>>>(c->d_recv, c->world, K, B, d_ids_out, d_vals_out,
                                                                     d_counts);
     MARS_CUDA_TRY(cudaGetLastError());
@@ -290,15 +316,13 @@ int mars::shard_gather_merge(const ShardCommView& v, const int32_t* d_ids, const
 int mars::shard_allreduce_max_f32(const ShardCommView& v, float* d, int32_t n, cudaStream_t st) {
     mars_shard_comm* c = comm_of(v);
     const ncclResult_t r = c->nccl->AllReduce(d, d, (size_t)n, ncclFloat32, ncclMax, c->comm, st);
-    if (r != ncclSuccess) return nccl_fail(c->nccl, r, "shard all-reduce");
-    return MARS_OK;
+    return nccl_settle(c->nccl, c->comm, r, c->timeout_ms, "shard all-reduce");
 }
 
 int mars::shard_allreduce_max_i32(const ShardCommView& v, int32_t* d, int32_t n, cudaStream_t st) {
     mars_shard_comm* c = comm_of(v);
     const ncclResult_t r = c->nccl->AllReduce(d, d, (size_t)n, ncclInt32, ncclMax, c->comm, st);
-    if (r != ncclSuccess) return nccl_fail(c->nccl, r, "shard all-reduce");
-    return MARS_OK;
+    return nccl_settle(c->nccl, c->comm, r, c->timeout_ms, "shard all-reduce");
 }
 
 extern "C" {
@@ -317,10 +341,16 @@ int mars_shard_unique_id(void* id_out) {
 
 int mars_shard_comm_create(int32_t device, int32_t rank, int32_t world, const void* unique_id, int32_t max_batch,
                            int32_t max_k, mars_shard_comm** out) {
+    return mars_shard_comm_create_timeout(device, rank, world, unique_id, max_batch, max_k,
+                                          MARS_SHARD_DEFAULT_TIMEOUT_MS, out);
+}
+
+int mars_shard_comm_create_timeout(int32_t device, int32_t rank, int32_t world, const void* unique_id,
+                                   int32_t max_batch, int32_t max_k, int32_t timeout_ms, mars_shard_comm** out) {
     if (out == nullptr || unique_id == nullptr) return fail(MARS_ERR_INVALID, "mars_shard_comm_create: NULL argument");
     *out = nullptr;
     if (world <= 0 || rank < 0 || rank >= world || max_batch <= 0 || max_k <= 0 || max_k > MARS_MAX_TOP_K ||
-        (int64_t)world * max_k > kMergeKeys)
+        (int64_t)world * max_k > kMergeKeys || timeout_ms < 0)
         return fail(MARS_ERR_INVALID, "mars_shard_comm_create: need 0 <= rank < world, max_k <= " +
                                           std::to_string(MARS_MAX_TOP_K) + " and world x max_k <= " +
                                           std::to_string(kMergeKeys));
@@ -336,9 +366,12 @@ int mars_shard_comm_create(int32_t device, int32_t rank, int32_t world, const vo
     c->max_batch = max_batch;
     c->max_k = max_k;
     c->nccl = api;
+    c->timeout_ms = timeout_ms;
     int rc = MARS_OK;
     auto T = [&](cudaError_t e, const char* w) {
-        if (rc == MARS_OK && e != cudaSuccess) rc = cuda_fail(e, w, __FILE__, __LINE__);
+        if (e == cudaSuccess) return;
+        if (rc == MARS_OK) rc = cuda_fail(e, w, __FILE__, __LINE__);   // records the first failure
+        else (void)cudaGetLastError();                                 // later ones only clear the state
     };
     const size_t keys = (size_t)max_batch * max_k;
     T(cudaMalloc(&c->d_send, keys * 8), "shard send keys");
@@ -352,8 +385,22 @@ int mars_shard_comm_create(int32_t device, int32_t rank, int32_t world, const vo
     if (rc == MARS_OK) {
         ncclUniqueId id;
         std::memcpy(&id, unique_id, sizeof(id));
-        const ncclResult_t r = api->CommInitRank(&c->comm, world, id, rank);
-        if (r != ncclSuccess) { c->comm = nullptr; rc = nccl_fail(api, r, "mars_shard_comm_create: ncclCommInitRank"); }
+        // non-blocking: creation runs in the background and is polled
+        // against the deadline (a rank that never joins ends it with
+        // MARS_ERR_TIMEOUT, and the half-made communicator is aborted)
+        ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+        cfg.blocking = 0;
+        const ncclResult_t r = api->CommInitRankConfig(&c->comm, world, id, rank, &cfg);
+        if (r != ncclSuccess && r != ncclInProgress) {
+            c->comm = nullptr;
+            rc = nccl_fail(api, r, "mars_shard_comm_create: ncclCommInitRankConfig");
+        } else {
+            rc = nccl_settle(api, c->comm, r, timeout_ms, "mars_shard_comm_create");
+            if (rc != MARS_OK) {
+                api->CommAbort(c->comm);
+                c->comm = nullptr;
+            }
+        }
     }
     if (rc != MARS_OK) { mars_shard_comm_destroy(c); return rc; }
     *out = c;
@@ -365,7 +412,15 @@ int mars_shard_comm_destroy(mars_shard_comm* c) {
     MarsDeviceGuard g(c->device);
     cudaDeviceSynchronize();
     if (c->bfs_state != nullptr) shard_bfs_state_free(c->bfs_state);
-    if (c->comm != nullptr) c->nccl->CommDestroy(c->comm);
+    if (c->comm != nullptr) {
+        // flush and quiesce (polled against the deadline), then free; a
+        // teardown that does not settle is aborted instead
+        if (nccl_settle(c->nccl, c->comm, c->nccl->CommFinalize(c->comm), c->timeout_ms,
+                        "mars_shard_comm_destroy") == MARS_OK)
+            c->nccl->CommDestroy(c->comm);
+        else
+            c->nccl->CommAbort(c->comm);
+    }
     cudaFree(c->d_send);
     cudaFree(c->d_recv);
     for (int w = 0; w < 2; ++w) {
@@ -383,7 +438,9 @@ int mars_shard_comm_status(mars_shard_comm* c) {
     ncclResult_t async = ncclSuccess;
     const ncclResult_t r = c->nccl->CommGetAsyncError(c->comm, &async);
     if (r != ncclSuccess) return nccl_fail(c->nccl, r, "mars_shard_comm_status");
-    if (async != ncclSuccess) return nccl_fail(c->nccl, async, "mars_shard_comm_status: asynchronous error");
+    // ncclInProgress: NCCL is still setting up an operation (not an error)
+    if (async != ncclSuccess && async != ncclInProgress)
+        return nccl_fail(c->nccl, async, "mars_shard_comm_status: asynchronous error");
     return MARS_OK;
 }
 
@@ -471,7 +528,7 @@ int mars_shard_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx, mars_s
         MARS_CUDA_TRY(cudaMemsetAsync(c->d_send, 0, (size_t)n * 8, st));
     }
     const ncclResult_t r = c->nccl->AllGather(c->d_send, c->d_recv, (size_t)n, ncclUint64, c->comm, st);
-    if (r != ncclSuccess) return nccl_fail(c->nccl, r, "mars_shard_query_batch_topk: all-gather");
+    MARS_TRY(nccl_settle(c->nccl, c->comm, r, c->timeout_ms, "mars_shard_query_batch_topk: all-gather"));
     if (c->timed) MARS_CUDA_TRY(cudaEventRecord(c->ev[2], st));
 
     // 5: every rank merges
@@ -580,7 +637,9 @@ extern "C" int mars_shard_emulate_query_batch_topk(int32_t world, const mars_sto
     }
     int rc = MARS_OK;
     auto T = [&](cudaError_t e, const char* what) {
-        if (rc == MARS_OK && e != cudaSuccess) rc = cuda_fail(e, what, __FILE__, __LINE__);
+        if (e == cudaSuccess) return;
+        if (rc == MARS_OK) rc = cuda_fail(e, what, __FILE__, __LINE__);   // records the first failure
+        else (void)cudaGetLastError();                                 // later ones only clear the state
     };
     for (int r = 0; r < world; ++r) {
         T(cudaMalloc(&l_ids[r], n * 4), "emulation buffers");

@@ -280,7 +280,9 @@ int prepare(ShardCommView& v, int32_t n_global, int32_t pitch, int32_t K, ShardB
         b->max_k = std::max(K, 64);
         int rc = MARS_OK;
         auto T = [&](cudaError_t e, const char* w) {
-            if (rc == MARS_OK && e != cudaSuccess) rc = cuda_fail(e, w, __FILE__, __LINE__);
+            if (e == cudaSuccess) return;
+            if (rc == MARS_OK) rc = cuda_fail(e, w, __FILE__, __LINE__);   // records the first failure
+            else (void)cudaGetLastError();                                 // later ones only clear the state
         };
         T(cudaMalloc(&b->d_stamp, (size_t)n_global * 8), "shard BFS marks");
         if (rc == MARS_OK) T(cudaMemset(b->d_stamp, 0, (size_t)n_global * 8), "memset");

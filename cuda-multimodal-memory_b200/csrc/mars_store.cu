@@ -40,6 +40,11 @@ int cuda_fail(cudaError_t e, const char* what, const char* file, int line) {
     std::snprintf(buf, sizeof(buf), "CUDA error %s (%s) in %s at %s:%d", cudaGetErrorName(e),
                   cudaGetErrorString(e), what, file, line);
     g_last_error = buf;
+    // a failed call (an allocation that ran out of memory, say) also left
+    // the runtime's last-error state set; clear it, or the next launch check
+    // anywhere in the process would report this failure as its own (errors
+    // that corrupted the context stay: they are sticky)
+    (void)cudaGetLastError();
     return e == cudaErrorMemoryAllocation ? MARS_ERR_OOM : MARS_ERR_CUDA;
 }
 
@@ -616,6 +621,7 @@ int mars_store_append_edges(mars_store* s, int32_t n, const int32_t* src, const 
     }
     int32_t* d_tmp = nullptr;
     if (cudaMallocAsync(&d_tmp, (size_t)n * 4 * 4, st) != cudaSuccess) {
+        (void)cudaGetLastError();   // reported here, not by the next launch check
         rollback(n);
         return fail(MARS_ERR_OOM, "mars_store_append_edges: scratch allocation failed");
     }

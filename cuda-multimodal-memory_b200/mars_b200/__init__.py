@@ -140,6 +140,7 @@ _SIGS = {
     "mars_batch_ctx_debug_wait": [_VP, C.c_uint32, _I32],
     "mars_shard_unique_id": [_VP],
     "mars_shard_comm_create": [_I32, _I32, _I32, _VP, _I32, _I32, C.POINTER(_VP)],
+    "mars_shard_comm_create_timeout": [_I32, _I32, _I32, _VP, _I32, _I32, _I32, C.POINTER(_VP)],
     "mars_shard_comm_destroy": [_VP],
     "mars_shard_comm_status": [_VP],
     "mars_shard_comm_abort": [_VP],
@@ -531,11 +532,18 @@ def shard_unique_id() -> bytes:
 class ShardComm:
     """Row-shard communicator (one per rank and GPU; NCCL owned by the library)."""
 
-    def __init__(self, device: int, rank: int, world: int, unique_id: bytes, max_batch: int, max_k: int):
+    def __init__(self, device: int, rank: int, world: int, unique_id: bytes, max_batch: int, max_k: int,
+                 timeout_ms: int = None):
+        """timeout_ms: deadline of NCCL's set-up work (creation, first use,
+        teardown); None: the library's default, 0: none."""
         assert len(unique_id) == SHARD_ID_BYTES
         h = C.c_void_p()
         buf = C.create_string_buffer(unique_id, SHARD_ID_BYTES)
-        _check(lib().mars_shard_comm_create(device, rank, world, buf, max_batch, max_k, C.byref(h)))
+        if timeout_ms is None:
+            _check(lib().mars_shard_comm_create(device, rank, world, buf, max_batch, max_k, C.byref(h)))
+        else:
+            _check(lib().mars_shard_comm_create_timeout(device, rank, world, buf, max_batch, max_k,
+                                                        int(timeout_ms), C.byref(h)))
         self.handle = h
         self.rank, self.world = rank, world
 

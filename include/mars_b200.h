@@ -384,9 +384,19 @@ typedef struct mars_shard_comm mars_shard_comm;
 
 int mars_shard_unique_id(void* id_out);
 /* Collective over the `world` ranks (blocks until all have joined).  Calls
- * on it take B <= max_batch queries and K <= max_k; world x max_k <= 4096. */
+ * on it take B <= max_batch queries and K <= max_k; world x max_k <= 4096.
+ * The NCCL communicator is non-blocking: its creation, the set-up NCCL does
+ * on a first use and its teardown are polled (ncclCommGetAsyncError)
+ * against a deadline -- MARS_SHARD_DEFAULT_TIMEOUT_MS here, timeout_ms with
+ * the _timeout form (0: none) -- and a rank that never joins ends the call
+ * with MARS_ERR_TIMEOUT (the half-made communicator is aborted) instead of
+ * waiting for ever. */
+#define MARS_SHARD_DEFAULT_TIMEOUT_MS 600000
 int mars_shard_comm_create(int32_t device, int32_t rank, int32_t world, const void* unique_id,
                            int32_t max_batch, int32_t max_k, mars_shard_comm** out);
+int mars_shard_comm_create_timeout(int32_t device, int32_t rank, int32_t world, const void* unique_id,
+                                   int32_t max_batch, int32_t max_k, int32_t timeout_ms,
+                                   mars_shard_comm** out);
 /* Waits for the device, then frees the communicator.  NULL is accepted. */
 int mars_shard_comm_destroy(mars_shard_comm* comm);
 /* MARS_OK, or the communicator's asynchronous NCCL error (a peer that failed

@@ -145,3 +145,38 @@ def test_world1_sharded_bfs_query_equals_mars_query(hops, K, filt):
         assert np.array_equal(got["hops"], ref["hops"])
         assert np.array_equal(got["modality"], ref["modality"])
     comm.close()
+
+
+def test_rank_that_never_joins_ends_creation_with_timeout():
+    """A communicator of two ranks of which only rank 0 ever calls create:
+    the non-blocking creation is polled against its deadline (3 s) and ends
+    with MARS_ERR_TIMEOUT (the half-made communicator aborted) instead of
+    waiting for ever; the same process then makes a working communicator.
+    It runs in a child process with a hard time limit of its own; nothing of
+    it runs on the GPU beyond NCCL's start-up."""
+    import mars_b200 as mb
+    code = "\n".join([
+        "import sys, time",
+        f"sys.path.insert(0, {os.path.join(ROOT, 'cuda-multimodal-memory_b200')!r})",
+        "import mars_b200 as mb",
+        "uid = mb.shard_unique_id()",
+        "t0 = time.time()",
+        "try:",
+        "    mb.ShardComm(0, 0, 2, uid, max_batch=4, max_k=8, timeout_ms=3000)",
+        "    print('created')",
+        "except mb.MarsError as e:",
+        "    print('status', e.status, 'elapsed', round(time.time() - t0, 1))",
+        "c = mb.ShardComm(0, 0, 1, mb.shard_unique_id(), max_batch=4, max_k=8, timeout_ms=60000)",
+        "c.status()",
+        "c.close()",
+        "print('ok')",
+    ])
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    r = subprocess.run(["timeout", "-k", "10", "120", sys.executable, "-c", code], capture_output=True, text=True,
+                       env=env)
+    assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+    words = r.stdout.split()
+    assert "status" in words, r.stdout
+    assert int(words[words.index("status") + 1]) == mb.MARS_ERR_TIMEOUT, r.stdout
+    assert float(words[words.index("elapsed") + 1]) < 60.0, r.stdout
+    assert words[-1] == "ok", r.stdout
