@@ -151,7 +151,21 @@ struct SearchArgs {
     int32_t* out_cnt;         // nq
     int32_t* stat_iters;      // nq (may be null)
     int32_t* stat_scored;     // nq (may be null)
+    int* ticket;              // zeroed counter handing out queries (NULL: block b takes b, b + grid, ...)
 };
+
+// The next query of a block.  With a ticket counter (zeroed before the
+// launch) the blocks draw queries one at a time, so a block that drew quick
+// queries takes more and the launch ends about one query after the last
+// start, whatever the spread of the queries' costs; without one, block b
+// takes b, b + grid, ...  Block-collective.
+__device__ __forceinline__ int next_query(int* ticket, int* s_slot, int prev) {
+    if (ticket == nullptr) return prev < 0 ? (int)blockIdx.x : prev + (int)gridDim.x;
+    __syncthreads();                       // the previous query's slot has been read
+    if (threadIdx.x == 0) *s_slot = atomicAdd(ticket, 1);
+    __syncthreads();
+    return *s_slot;
+}
 
 __device__ __forceinline__ uint32_t hash32(int32_t v) {
     uint32_t x = (uint32_t)v;
@@ -208,7 +222,8 @@ __global__ void __launch_bounds__(kSearchThreads, 8) search_kernel(const SearchA
     const uint32_t mask = (uint32_t)a.hash_size - 1u;
     const uint32_t row_bytes = (uint32_t)((a.D + 3) & ~3) * 4u;   // rows are float4 aligned
 
-    for (int qi = blockIdx.x; qi < a.nq; qi += gridDim.x) {
+    __shared__ int s_qslot;
+    for (int qi = next_query(a.ticket, &s_qslot, -1); qi < a.nq; qi = next_query(a.ticket, &s_qslot, qi)) {
         // the beam and its merged successor swap roles every iteration
         float* bs = s_bs;
         int32_t* bi = s_bi;
@@ -421,6 +436,7 @@ struct BfsArgs2 {
     int32_t* redo;
     int32_t* redo_cnt;
     int32_t smem_nodes;           // visited nodes the shared table takes per query
+    int* ticket;                  // shared-memory kernel: zeroed counter handing out queries (NULL: static order)
 };
 
 __device__ __forceinline__ int table_find_or_claim(unsigned long long* tags, uint32_t mask, uint32_t epoch,
@@ -649,7 +665,8 @@ __global__ void __launch_bounds__(kThreads, 3) bfs_smem_kernel(const BfsArgs2 a)
     const int limit = min(a.smem_nodes, a.vcap / 2);
     const uint32_t row_bytes = (uint32_t)a.nc * 16u;
 
-    for (int qi = blockIdx.x; qi < a.nq; qi += gridDim.x) {
+    __shared__ int s_qslot;
+    for (int qi = next_query(a.ticket, &s_qslot, -1); qi < a.nq; qi = next_query(a.ticket, &s_qslot, qi)) {
         for (int i = tid; i < kBfsSlots; i += kThreads) { s_tag[i] = kEmptyTag; s_state[i] = 0ull; }
         if (tid == 0) { s_tail = 0; s_ovf = 0; s_lvl[0] = 0; }
         __syncthreads();
@@ -881,10 +898,25 @@ int mars_cmng_knn(const mars_store* s, int32_t k, int32_t* d_ids, float* d_vals,
     return rc;
 }
 
+static int cmng_search_launch(const mars_store* s, const int32_t* d_neighbors, int32_t degree,
+                              const float* d_queries, int32_t query_pitch, int32_t nq, float t_q,
+                              const mars_cmng_config* cfg, int32_t* d_ids, float* d_scores, int32_t* d_mods,
+                              int32_t* d_counts, int32_t* d_iters, int32_t* d_scored, void* stream, int* ticket);
+
 int mars_cmng_search_batch(const mars_store* s, const int32_t* d_neighbors, int32_t degree,
                            const float* d_queries, int32_t query_pitch, int32_t nq, float t_q,
                            const mars_cmng_config* cfg, int32_t* d_ids, float* d_scores, int32_t* d_mods,
                            int32_t* d_counts, int32_t* d_iters, int32_t* d_scored, void* stream) {
+    return cmng_search_launch(s, d_neighbors, degree, d_queries, query_pitch, nq, t_q, cfg, d_ids, d_scores, d_mods,
+                              d_counts, d_iters, d_scored, stream, nullptr);
+}
+
+// The beam-search launch; ticket (device int, may be NULL) hands the queries
+// out dynamically and is zeroed here on the stream first.
+static int cmng_search_launch(const mars_store* s, const int32_t* d_neighbors, int32_t degree,
+                              const float* d_queries, int32_t query_pitch, int32_t nq, float t_q,
+                              const mars_cmng_config* cfg, int32_t* d_ids, float* d_scores, int32_t* d_mods,
+                              int32_t* d_counts, int32_t* d_iters, int32_t* d_scored, void* stream, int* ticket) {
     if (s == nullptr || d_neighbors == nullptr || d_queries == nullptr || cfg == nullptr || d_ids == nullptr ||
         d_scores == nullptr || d_counts == nullptr)
         return fail(MARS_ERR_INVALID, "mars_cmng_search_batch: NULL argument");
@@ -924,6 +956,8 @@ int mars_cmng_search_batch(const mars_store* s, const int32_t* d_neighbors, int3
     a.out_cnt = d_counts;
     a.stat_iters = d_iters;
     a.stat_scored = d_scored;
+    a.ticket = ticket;
+    if (ticket != nullptr) MARS_CUDA_TRY(cudaMemsetAsync(ticket, 0, sizeof(int), st));
     const size_t smem = search_smem(s->dim, hs);
     if (smem > 48 * 1024)
         MARS_CUDA_TRY(cudaFuncSetAttribute(search_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
@@ -951,7 +985,8 @@ struct mars_cmng_ctx {
     int32_t* d_lists = nullptr;
     uint32_t* d_epochs = nullptr;
     int* d_err = nullptr;
-    int32_t* d_redo = nullptr;           // max_queries + 1: queries for the global-table BFS, their count
+    int32_t* d_redo = nullptr;           // max_queries + 3: queries for the global-table BFS, their count,
+                                         // the search's and the shared-memory BFS's query tickets
     int32_t smem_nodes = kBfsSlots / 2;  // visited nodes per query in the shared-memory BFS (0: never)
 };
 
@@ -998,7 +1033,7 @@ int mars_cmng_ctx_create(int32_t device, int32_t max_queries, int32_t K, int32_t
     T(cudaMalloc(&c->d_lists, (size_t)c->grid * c->vcap * 4), "level lists");
     T(cudaMalloc(&c->d_epochs, (size_t)c->grid * 4), "epochs");
     T(cudaMalloc(&c->d_err, sizeof(int)), "error word");
-    T(cudaMalloc(&c->d_redo, ((size_t)max_queries + 1) * 4), "BFS redo list");
+    T(cudaMalloc(&c->d_redo, ((size_t)max_queries + 3) * 4), "BFS redo list and query tickets");
     if (rc == MARS_OK) {
         T(cudaFuncSetAttribute(bfs_smem_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBfsSmemBytes), "attribute");
         T(cudaFuncSetAttribute(bfs_smem_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kBfsSmemBytes), "attribute");
@@ -1048,8 +1083,9 @@ int mars_cmng_search_bfs_batch(const mars_store* s, mars_cmng_ctx* c, const int3
     MarsDeviceGuard g(s->device);
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream) : s->stream;
     // 1. beam search into the context's seed buffers
-    MARS_TRY(mars_cmng_search_batch(s, d_neighbors, degree, d_queries, query_pitch, nq, t_q, cfg, c->d_seed_ids,
-                                    c->d_seed_scores, nullptr, c->d_seed_cnt, nullptr, nullptr, st));
+    int* tickets = reinterpret_cast<int*>(c->d_redo + c->max_queries + 1);
+    MARS_TRY(cmng_search_launch(s, d_neighbors, degree, d_queries, query_pitch, nq, t_q, cfg, c->d_seed_ids,
+                                c->d_seed_scores, nullptr, c->d_seed_cnt, nullptr, nullptr, st, tickets));
     // 2. BFS + final top-K
     BfsArgs2 a{};
     a.nbrs = d_neighbors;
@@ -1095,7 +1131,9 @@ int mars_cmng_search_bfs_batch(const mars_store* s, mars_cmng_ctx* c, const int3
         a.redo = c->d_redo;
         a.redo_cnt = c->d_redo + c->max_queries;
         a.smem_nodes = c->smem_nodes;
+        a.ticket = tickets + 1;
         MARS_CUDA_TRY(cudaMemsetAsync(a.redo_cnt, 0, sizeof(int32_t), st));
+        MARS_CUDA_TRY(cudaMemsetAsync(a.ticket, 0, sizeof(int), st));
         if (cfg->K <= 32) launch(bfs_smem_kernel<1>, kBfsSmemBytes);
         else if (cfg->K <= 64) launch(bfs_smem_kernel<2>, kBfsSmemBytes);
         else if (cfg->K <= 128) launch(bfs_smem_kernel<4>, kBfsSmemBytes);
