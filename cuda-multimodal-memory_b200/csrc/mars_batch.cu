@@ -640,18 +640,21 @@ constexpr int kCountCap = 256;
 constexpr int kCountSortCap = 512;
 // Rows each rescoring warp keeps requested ahead of the one it scores.
 constexpr int kRescoreAhead = 4;
+// Unsharded batches of at least this many queries rescore in three kernels
+// (rows listed / scored / ranked), smaller ones in one.
+constexpr int kSplitRescoreMinB = 256;
 
 __global__ void __launch_bounds__(kRescoreThreads, 3)
 rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t B, float t_q,
                float lambda, int32_t use_imp, int32_t K, int32_t row_offset,
                const float* __restrict__ theta, const float* __restrict__ margin,
-               const int4* __restrict__ cand, const int32_t* __restrict__ cand_cnt, int32_t cap,
+               int4* __restrict__ cand, const int32_t* __restrict__ cand_cnt, int32_t cap,
                int32_t* __restrict__ out_ids, float* __restrict__ out_vals,
                int32_t* __restrict__ out_cnt, int32_t* __restrict__ fallback,
                int32_t* __restrict__ rescored, const int32_t* __restrict__ bad,
                const int32_t* __restrict__ status, float* __restrict__ bound_out,
                const float* __restrict__ bound_in, int32_t shard_world, int32_t shard_global,
-               int32_t* __restrict__ status_mirror, int32_t max_batch) {
+               int32_t* __restrict__ status_mirror, int32_t max_batch, int32_t split) {
     // The call's status words, [err, sync_err, fallback[], cand_cnt[],
     // rescored[], bad[]] (max_batch each), also go straight to the caller's
     // host-mapped mirror by the final pass (status_mirror != NULL), so no
@@ -715,7 +718,7 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     const float th = theta[qi];
     // candidate i: row .x, approximate score .y and slack .z (float bits);
     // the exact score lies in score -+ slack
-    const int4* cq = cand + (int64_t)qi * cap;
+    int4* cq = cand + (int64_t)qi * cap;
 
     // ---- pass 1: lower bounds, completeness, K-th largest lower bound -------
     // Unsharded, K <= 32: every warp keeps its K best lower bounds (ranked by
@@ -842,6 +845,19 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
     }
     __syncthreads();
     const int nk = min(s_nk, kRowsCap);
+    if (split != 0) {
+        // split rescore (large batches): the rows go back to the front of
+        // this query's candidate list (every read of it is done) for
+        // rescore_rows_kernel; a longer row list than this block's is
+        // answered by the exact scan instead
+        if (s_nk > kRowsCap) {
+            if (threadIdx.x == 0) { fallback[qi] = 1; rescored[qi] = 0; if (out_cnt) out_cnt[qi] = 0; }
+            return;
+        }
+        for (int t = threadIdx.x; t < nk; t += kRescoreThreads) cq[t].x = s_rows[t];
+        if (threadIdx.x == 0) { fallback[qi] = 0; rescored[qi] = nk; }
+        return;
+    }
     // each warp requests its next four rows into L2 (one bulk prefetch each)
     // while it scores the current one: five of its rows travel at a time
     // instead of one, and L2 holds only rows about to be read
@@ -939,6 +955,113 @@ rescore_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, int32_t
         fallback[qi] = 0;
         rescored[qi] = n2;
     }
+    publish(0, n2);
+}
+
+// Split rescore of large batches, after rescore_kernel listed each query's
+// rows (split = 1): the rows' exact scores with nothing else in the kernel --
+// the query in 3 KB of shared memory, the row alone in registers -- so six
+// 256-thread blocks fit an SM and about twice as many rows travel at once as
+// in the one-kernel form, whose selection arrays allow three blocks per SM.  Warp w of block q takes
+// rows w, w + 8, ... of query q, each warp keeping its next rows requested
+// into L2; the score (the canonical dot, the same arithmetic as the fp32
+// scan) replaces the approximate one in the row's record.
+template <int C>   // float4 chunks per lane and row: D <= 128 C
+__global__ void __launch_bounds__(kRescoreThreads, 6)
+rescore_rows_kernel(StoreView s, const float* __restrict__ Q, int64_t qpitch, float t_q, float lambda,
+                    int32_t use_imp, int4* __restrict__ cand, int32_t cap, const int32_t* __restrict__ rescored,
+                    const int32_t* __restrict__ fallback, const int32_t* __restrict__ status) {
+    __shared__ float4 s_q[32 * C];
+    const int qi = blockIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int kWarps = kRescoreThreads / 32;
+    if (status[0] != 0 || status[1] != 0 || fallback[qi] != 0) return;
+    const int nk = rescored[qi];
+    const float4* q4 = reinterpret_cast<const float4*>(Q + (int64_t)qi * qpitch);
+    for (int i = threadIdx.x; i < s.nc; i += kRescoreThreads) s_q[i] = q4[i];
+    __syncthreads();
+    int4* cq = cand + (int64_t)qi * cap;
+    const bool use_w = use_imp != 0 && s.imp != nullptr;
+    const float4* E4 = reinterpret_cast<const float4*>(s.E);
+    const uint32_t row_bytes = (uint32_t)s.nc * 16u;
+    auto prefetch_row = [&](int t) {
+        if (lane == 0 && t < nk) prefetch_l2_bulk(E4 + (int64_t)__ldcg(&cq[t].x) * s.pitch4, row_bytes);
+    };
+    for (int d = 1; d < kRescoreAhead; ++d) prefetch_row(warp + d * kWarps);
+    for (int t = warp; t < nk; t += kWarps) {
+        prefetch_row(t + kRescoreAhead * kWarps);
+        const int32_t rr = __ldcg(&cq[t].x);
+        const float dot = warp_dot_canonical_smemq<C>(E4 + (int64_t)rr * s.pitch4, s_q, s.nc, lane);
+        float f = fused_weight_apply(dot, __ldg(s.ts + rr), t_q, lambda);
+        if (use_w) f = f * __ldg(s.imp + rr);
+        if (lane == 0) cq[t].y = __float_as_int(f);
+    }
+}
+
+// Split rescore, last step: each query's rescored rows ranked by rank key
+// (score desc, id asc) into the outputs, and the call's status words
+// published (as rescore_kernel's final pass does).
+__global__ void __launch_bounds__(kRescoreThreads)
+rescore_rank_kernel(int32_t K, int32_t row_offset, const int4* __restrict__ cand, int32_t cap,
+                    int32_t* __restrict__ out_ids, float* __restrict__ out_vals, int32_t* __restrict__ out_cnt,
+                    const int32_t* __restrict__ fallback, const int32_t* __restrict__ rescored,
+                    const int32_t* __restrict__ cand_cnt, const int32_t* __restrict__ bad,
+                    const int32_t* __restrict__ status, int32_t* __restrict__ status_mirror, int32_t max_batch) {
+    __shared__ __align__(16) unsigned long long s_keys[kSortCap / 2];
+    __shared__ float s_key[kSortCap / 2];
+    __shared__ int32_t s_id[kSortCap / 2];
+    const int qi = blockIdx.x;
+    auto publish = [&](int32_t fb, int32_t resc) {
+        if (status_mirror == nullptr || threadIdx.x != 0) return;
+        if (blockIdx.x == 0) { status_mirror[0] = status[0]; status_mirror[1] = status[1]; }
+        status_mirror[2 + blockIdx.x] = fb;
+        status_mirror[2 + max_batch + blockIdx.x] = cand_cnt[blockIdx.x];
+        status_mirror[2 + 2 * max_batch + blockIdx.x] = resc;
+        status_mirror[2 + 3 * max_batch + blockIdx.x] = bad != nullptr ? bad[blockIdx.x] : 0;
+    };
+    if (status[0] != 0 || status[1] != 0) { publish(0, 0); return; }   // outputs already marked invalid
+    if (fallback[qi] != 0) { publish(1, 0); return; }                   // answered by the exact scan
+    const int n2 = rescored[qi];
+    const int4* cq = cand + (int64_t)qi * cap;
+    if (n2 <= kCountSortCap) {
+        for (int p = threadIdx.x; p < n2; p += kRescoreThreads) {
+            const int4 e = __ldcg(cq + p);
+            s_keys[p] = rank_key(__int_as_float(e.y), e.x + row_offset);
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < n2; i += kRescoreThreads) {
+            const unsigned long long k = s_keys[i];
+            int r = 0;
+            for (int t = 0; t < n2; ++t) r += s_keys[t] > k ? 1 : 0;
+            if (r < K) {
+                out_vals[(int64_t)qi * K + r] = key_score(k);
+                out_ids[(int64_t)qi * K + r] = key_id(k);
+            }
+        }
+    } else {
+        const int p2 = pow2_at_least(n2);
+        for (int p = threadIdx.x; p < p2; p += kRescoreThreads) {
+            if (p < n2) {
+                const int4 e = __ldcg(cq + p);
+                s_key[p] = __int_as_float(e.y);
+                s_id[p] = e.x + row_offset;
+            } else {
+                s_key[p] = -INFINITY;
+                s_id[p] = INT32_MAX;
+            }
+        }
+        __syncthreads();
+        block_bitonic_desc(s_key, s_id, p2);
+        for (int p = threadIdx.x; p < min(n2, K); p += kRescoreThreads) {
+            out_vals[(int64_t)qi * K + p] = s_key[p];
+            out_ids[(int64_t)qi * K + p] = s_id[p];
+        }
+    }
+    for (int p = n2 + threadIdx.x; p < K; p += kRescoreThreads) {
+        out_vals[(int64_t)qi * K + p] = -INFINITY;
+        out_ids[(int64_t)qi * K + p] = -1;
+    }
+    if (threadIdx.x == 0 && out_cnt) out_cnt[qi] = min(n2, K);
     publish(0, n2);
 }
 
@@ -1965,14 +2088,15 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
     StoreView v{};
     v.E = s->d_E; v.ts = s->d_ts; v.imp = s->d_imp; v.mod = s->d_mod; v.d_n = s->d_n;
     v.pitch4 = s->pitch / 4; v.nc = (s->dim + 3) / 4;
-    auto rescore = [&](float* bound_out, const float* bound_in) {
+    auto rescore = [&](float* bound_out, const float* bound_in, bool split) {
         rescore_kernel<<<B, kRescoreThreads, 0, st>>>(v, d_queries, query_pitch, B, t_q, lambda, use_importance, K,
                                                       row_offset, c->d_theta, c->d_margin, c->d_cand,
                                                       c->d_cand_cnt, c->cap, d_ids, d_vals, d_counts,
                                                       c->d_fallback, c->d_rescored, f16 ? c->d_bad : nullptr,
                                                       c->d_status, bound_out, bound_in,
                                                       xchg != nullptr ? xchg->world : 1, shard_global ? 1 : 0,
-                                                      bound_out == nullptr ? c->dm_status : nullptr, c->max_batch);
+                                                      (bound_out == nullptr && !split) ? c->dm_status : nullptr,
+                                                      c->max_batch, split ? 1 : 0);
         return cudaGetLastError();
     };
     if (xchg != nullptr) {
@@ -1985,12 +2109,32 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
             xchg->theta_done = true;
             MARS_TRY(xchg->gather(xchg->arg, 0, shard_thr_floats(B), st));
         }
-        MARS_CUDA_TRY(rescore(xchg->send[1], nullptr));
+        MARS_CUDA_TRY(rescore(xchg->send[1], nullptr, false));
         xchg->done = true;
         MARS_TRY(xchg->gather(xchg->arg, 1, shard_rec_floats(B), st));
-        MARS_CUDA_TRY(rescore(nullptr, xchg->recv[1]));
+        MARS_CUDA_TRY(rescore(nullptr, xchg->recv[1], false));
+    } else if (B >= kSplitRescoreMinB) {
+        // large batches: selection and row lists, then the rows' exact
+        // scores in a light kernel (more rows in flight per SM), then the
+        // ranking and the status words
+        MARS_CUDA_TRY(rescore(nullptr, nullptr, true));
+        const int cpl = (v.nc + 31) / 32;   // float4 chunks per lane and row
+        auto rows = [&](auto kfn) {
+            kfn<<<B, kRescoreThreads, 0, st>>>(v, d_queries, query_pitch, t_q, lambda, use_importance, c->d_cand,
+                                               c->cap, c->d_rescored, c->d_fallback, c->d_status);
+        };
+        if (cpl <= 2) rows(rescore_rows_kernel<2>);
+        else if (cpl <= 4) rows(rescore_rows_kernel<4>);
+        else if (cpl <= 6) rows(rescore_rows_kernel<6>);
+        else rows(rescore_rows_kernel<8>);
+        MARS_CUDA_TRY(cudaGetLastError());
+        rescore_rank_kernel<<<B, kRescoreThreads, 0, st>>>(K, row_offset, c->d_cand, c->cap, d_ids, d_vals, d_counts,
+                                                           c->d_fallback, c->d_rescored, c->d_cand_cnt,
+                                                           f16 ? c->d_bad : nullptr, c->d_status, c->dm_status,
+                                                           c->max_batch);
+        MARS_CUDA_TRY(cudaGetLastError());
     } else {
-        MARS_CUDA_TRY(rescore(nullptr, nullptr));
+        MARS_CUDA_TRY(rescore(nullptr, nullptr, false));
     }
     // 6. exact rescans of the flagged queries (every CTA of an unflagged
     // query leaves at once)

@@ -64,6 +64,29 @@ __device__ __forceinline__ float warp_butterfly_sum(float v) {
     return v;
 }
 
+// The canonical dot with the query in shared memory and at most C float4
+// chunks per lane (nc <= 32 C): the row's loads are all issued before the
+// first fused multiply-add, and the query is read from shared memory as the
+// chain runs, so only the row occupies registers.  The same chain and
+// butterfly as warp_dot_canonical, bit for bit.
+template <int C>
+__device__ __forceinline__ float warp_dot_canonical_smemq(const float4* __restrict__ row,
+                                                          const float4* __restrict__ q_smem, int nc, int lane) {
+    float4 e[C];
+#pragma unroll
+    for (int k = 0; k < C; ++k) {
+        const int c = lane + k * kWarp;
+        if (c < nc) e[k] = ldg_stream(row + c);
+    }
+    float acc = 0.0f;
+#pragma unroll
+    for (int k = 0; k < C; ++k) {
+        const int c = lane + k * kWarp;
+        if (c < nc) acc = fma4(e[k], q_smem[c], acc);
+    }
+    return warp_butterfly_sum(acc);
+}
+
 // Row dot with the query held in shared or global memory (generic D).
 __device__ __forceinline__ float warp_dot_canonical(const float4* __restrict__ row,
                                                     const float4* __restrict__ q,

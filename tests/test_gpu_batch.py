@@ -73,7 +73,9 @@ def test_batch_small_smoke(torch_mod):
 
 @pytest.mark.parametrize("tf32_only", [False, True])
 @pytest.mark.parametrize("N,D,B,K", [(100_003, 768, 200, 100), (60_000, 768, 256, 10),
-                                     (50_000, 64, 130, 32), (40_000, 100, 64, 50)])
+                                     (50_000, 64, 130, 32), (40_000, 100, 64, 50),
+                                     # B >= 256: the three-kernel rescore, at D = 1024 and D = 100
+                                     (30_011, 1024, 300, 64), (20_000, 100, 512, 32)])
 def test_batch_matches_single_query_scans(torch_mod, N, D, B, K, tf32_only):
     """fp16 operands (default) and TF32 operands give the same results."""
     stats = _run(torch_mod, N, D, B, K, seed=N % 97, tf32_only=tf32_only)
