@@ -640,8 +640,8 @@ constexpr int kCountCap = 256;
 constexpr int kCountSortCap = 512;
 // Rows each rescoring warp keeps requested ahead of the one it scores.
 constexpr int kRescoreAhead = 4;
-// Unsharded batches of at least this many queries rescore in three kernels
-// (rows listed / scored / ranked), smaller ones in one.
+// Batches of at least this many queries take their final rescore pass in
+// three kernels (rows listed / scored / ranked), smaller ones in one.
 constexpr int kSplitRescoreMinB = 256;
 
 __global__ void __launch_bounds__(kRescoreThreads, 3)
@@ -2099,25 +2099,13 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
                                                       c->max_batch, split ? 1 : 0);
         return cudaGetLastError();
     };
-    if (xchg != nullptr) {
-        // row shards: a small batch took its thresholds inside the fused
-        // launch (its own shard's), so it joins the threshold exchange with a
-        // neutral record; then every shard's bound record, one all-gather,
-        // and the rescore against all of them
-        if (!xchg->theta_done) {
-            MARS_TRY(shard_neutral_thr(xchg->send[0], B, st));
-            xchg->theta_done = true;
-            MARS_TRY(xchg->gather(xchg->arg, 0, shard_thr_floats(B), st));
-        }
-        MARS_CUDA_TRY(rescore(xchg->send[1], nullptr, false));
-        xchg->done = true;
-        MARS_TRY(xchg->gather(xchg->arg, 1, shard_rec_floats(B), st));
-        MARS_CUDA_TRY(rescore(nullptr, xchg->recv[1], false));
-    } else if (B >= kSplitRescoreMinB) {
-        // large batches: selection and row lists, then the rows' exact
-        // scores in a light kernel (more rows in flight per SM), then the
-        // ranking and the status words
-        MARS_CUDA_TRY(rescore(nullptr, nullptr, true));
+    // large batches: the final pass lists each query's rows, a light kernel
+    // scores them (more rows in flight per SM), a third ranks them and
+    // publishes the status words
+    const bool split = B >= kSplitRescoreMinB;
+    auto final_pass = [&](const float* bound_in) -> int {
+        MARS_CUDA_TRY(rescore(nullptr, bound_in, split));
+        if (!split) return MARS_OK;
         const int cpl = (v.nc + 31) / 32;   // float4 chunks per lane and row
         auto rows = [&](auto kfn) {
             kfn<<<B, kRescoreThreads, 0, st>>>(v, d_queries, query_pitch, t_q, lambda, use_importance, c->d_cand,
@@ -2133,8 +2121,24 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
                                                            f16 ? c->d_bad : nullptr, c->d_status, c->dm_status,
                                                            c->max_batch);
         MARS_CUDA_TRY(cudaGetLastError());
+        return MARS_OK;
+    };
+    if (xchg != nullptr) {
+        // row shards: a small batch took its thresholds inside the fused
+        // launch (its own shard's), so it joins the threshold exchange with a
+        // neutral record; then every shard's bound record, one all-gather,
+        // and the rescore against all of them
+        if (!xchg->theta_done) {
+            MARS_TRY(shard_neutral_thr(xchg->send[0], B, st));
+            xchg->theta_done = true;
+            MARS_TRY(xchg->gather(xchg->arg, 0, shard_thr_floats(B), st));
+        }
+        MARS_CUDA_TRY(rescore(xchg->send[1], nullptr, false));
+        xchg->done = true;
+        MARS_TRY(xchg->gather(xchg->arg, 1, shard_rec_floats(B), st));
+        MARS_TRY(final_pass(xchg->recv[1]));
     } else {
-        MARS_CUDA_TRY(rescore(nullptr, nullptr, false));
+        MARS_TRY(final_pass(nullptr));
     }
     // 6. exact rescans of the flagged queries (every CTA of an unflagged
     // query leaves at once)
