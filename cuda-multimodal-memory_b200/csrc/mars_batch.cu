@@ -428,12 +428,13 @@ constexpr int kThrThreads = 256;
 constexpr int kThrKeep = 32;
 
 // Streams `total` values (load(i); -inf marks an empty slot) through one
-// warp: each lane keeps its kThrKeep largest sorted in registers.  Returns
-// the warp's count of non-empty values.
-template <class Load>
-__device__ __forceinline__ int warp_keep_largest(Load load, int total, float (&keep)[kThrKeep], int lane) {
+// warp: each lane keeps its KEEP largest sorted in registers (enough for
+// the warp's j <= KEEP largest: no lane holds more than j of them).
+// Returns the warp's count of non-empty values.
+template <int KEEP, class Load>
+__device__ __forceinline__ int warp_keep_largest(Load load, int total, float (&keep)[KEEP], int lane) {
 #pragma unroll
-    for (int s = 0; s < kThrKeep; ++s) keep[s] = -INFINITY;
+    for (int s = 0; s < KEEP; ++s) keep[s] = -INFINITY;
     int valid = 0;
     for (int i0 = lane; i0 < total; i0 += 8 * 32) {
         float v[8];   // eight loads in flight per lane
@@ -447,9 +448,9 @@ __device__ __forceinline__ int warp_keep_largest(Load load, int total, float (&k
             float x = v[k];
             if (!(x > -INFINITY)) continue;   // empty slot
             ++valid;
-            if (x > keep[kThrKeep - 1]) {
+            if (x > keep[KEEP - 1]) {
 #pragma unroll
-                for (int s = 0; s < kThrKeep; ++s)
+                for (int s = 0; s < KEEP; ++s)
                     if (x > keep[s]) { const float t = keep[s]; keep[s] = x; x = t; }
             }
         }
@@ -460,8 +461,8 @@ __device__ __forceinline__ int warp_keep_largest(Load load, int total, float (&k
 // Takes the warp's largest kept value n times (a max butterfly; the lowest
 // lane holding it drops it); emit(r, m) receives the (r+1)-th largest, -inf
 // once the kept values are used up.
-template <class Emit>
-__device__ __forceinline__ void warp_take_largest(float (&keep)[kThrKeep], int n, int lane, Emit emit) {
+template <int KEEP, class Emit>
+__device__ __forceinline__ void warp_take_largest(float (&keep)[KEEP], int n, int lane, Emit emit) {
     for (int r = 0; r < n; ++r) {
         float m = keep[0];
 #pragma unroll
@@ -469,17 +470,19 @@ __device__ __forceinline__ void warp_take_largest(float (&keep)[kThrKeep], int n
         const unsigned who = __ballot_sync(0xffffffffu, keep[0] == m);
         if (lane == __ffs(who) - 1) {
 #pragma unroll
-            for (int s = 0; s < kThrKeep - 1; ++s) keep[s] = keep[s + 1];
-            keep[kThrKeep - 1] = -INFINITY;
+            for (int s = 0; s < KEEP - 1; ++s) keep[s] = keep[s + 1];
+            keep[KEEP - 1] = -INFINITY;
         }
         emit(r, m);
     }
 }
 
-// The j-th largest of query q's values for one warp (see threshold_kernel).
+// The j-th largest of query q's values for one warp (see threshold_kernel);
+// j <= KEEP.
+template <int KEEP>
 __device__ float warp_threshold(const float* __restrict__ sample_buf, int32_t n_sample_tiles, int32_t B, int q,
                                 int32_t j, int32_t per_tile, int lane) {
-    float keep[kThrKeep];
+    float keep[KEEP];
     // L2 loads: other CTAs may have written the values
     const int valid = warp_keep_largest(
         [&](int i) { return __ldcg(sample_buf + ((int64_t)(i / per_tile) * B + q) * per_tile + (i % per_tile)); },
@@ -489,13 +492,14 @@ __device__ float warp_threshold(const float* __restrict__ sample_buf, int32_t n_
     return th;
 }
 
+template <int KEEP>   // j <= KEEP
 __global__ void __launch_bounds__(kThrThreads)
 threshold_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tiles, int32_t B, int32_t j,
                  int32_t per_tile, float* __restrict__ theta) {
     const int q = (int)((blockIdx.x * (unsigned)blockDim.x + threadIdx.x) >> 5);
     const int lane = threadIdx.x & 31;
     if (q >= B) return;
-    const float th = warp_threshold(sample_buf, n_sample_tiles, B, q, j, per_tile, lane);
+    const float th = warp_threshold<KEEP>(sample_buf, n_sample_tiles, B, q, j, per_tile, lane);
     if (lane == 0) theta[q] = th;
 }
 
@@ -518,7 +522,7 @@ sample_record_kernel(const float* __restrict__ sample_buf, int32_t n_sample_tile
         h[2] = 1;
     }
     if (q >= B) return;
-    float keep[kThrKeep];
+    float keep[kJ];
     warp_keep_largest(
         [&](int i) { return __ldcg(sample_buf + ((int64_t)(i / per_tile) * B + q) * per_tile + (i % per_tile)); },
         n_sample_tiles * per_tile, keep, lane);
@@ -544,7 +548,7 @@ union_threshold_kernel(const float* __restrict__ recs, int32_t world, int32_t st
     }
     const double mu = rows > 0 ? (double)K * (double)srows / (double)rows : 0.0;
     const int j = max(1, min(kJ, (int)ceil(mu + 5.0 * sqrt(mu) + 3.0)));
-    float keep[kThrKeep];
+    float keep[kJ];
     const int valid = warp_keep_largest(
         [&](int i) {
             const int r = i / kJ;
@@ -1095,13 +1099,18 @@ constexpr int kSmallThreads = 320;
 constexpr int kSmallEpi = kSmallThreads - 64;
 constexpr int kSmallStaticSmem = 6144;               // bound on the kernel's static shared memory
 constexpr int kStageCand = 256;                      // candidates staged in shared memory per CTA
+// Accumulator buffers in TMEM (as many as 512 columns hold, up to this many):
+// the MMAs run this many tiles ahead of the epilogue, which covers the
+// fused launch's wait for every CTA's sample tile and its thresholds.
+constexpr int kSmallAccBufs = 8;
 
 struct SmallArgs {
     int32_t B, NQ;                   // queries, MMA N (B rounded up to 16)
     int32_t n, nkb;                  // rows, 64-half k-blocks
     int32_t n_tiles;                 // 128-row tiles of this launch
     int32_t stages;                  // row stages in the ring
-    uint32_t tmem_cols;              // columns allocated (power of two >= 2 NQ, >= 32)
+    uint32_t tmem_cols;              // columns allocated (power of two >= nbuf NQ, >= 32)
+    int32_t nbuf;                    // accumulator buffers in TMEM (2 .. kSmallAccBufs)
     const int32_t* sample_rt;        // sample mode: 128-row tile of sample tile i
     RowMeta meta;
     const float* theta;
@@ -1181,8 +1190,8 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     uint64_t* empty = full + kSmallMaxStages;
     uint64_t* qfull = empty + kSmallMaxStages;
     uint64_t* tfull = qfull + 1;
-    uint64_t* tempty = tfull + 2;
-    uint64_t* mdrain = tempty + 2;      // the MMA issuer's last commit
+    uint64_t* tempty = tfull + kSmallAccBufs;
+    uint64_t* mdrain = tempty + kSmallAccBufs;      // the MMA issuer's last commit
     uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mdrain + 1);
 
     // this launch's thresholds (kFused: after the grid wait) and the queries'
@@ -1202,7 +1211,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
     if (threadIdx.x == 0) {
         for (int s = 0; s < a.stages; ++s) { sm100::mbar_init(full + s, 1); sm100::mbar_init(empty + s, 1); }
         sm100::mbar_init(qfull, 1);
-        for (int b = 0; b < 2; ++b) { sm100::mbar_init(tfull + b, 1); sm100::mbar_init(tempty + b, kSmallEpi); }
+        for (int b = 0; b < a.nbuf; ++b) { sm100::mbar_init(tfull + b, 1); sm100::mbar_init(tempty + b, kSmallEpi); }
         sm100::mbar_init(mdrain, 1);
         sm100::fence_mbar_init();
         sm100::prefetch_tmap(&tmap_q);
@@ -1278,7 +1287,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                 }
                 if (!ok) break;
                 sm100::mma_commit(tfull + buf);         // accumulator ready
-                if (++buf == 2) { buf = 0; bphase ^= 1u; }
+                if (++buf == a.nbuf) { buf = 0; bphase ^= 1u; }
             }
             // every MMA this thread issued has finished before TMEM is freed
             // (also when a wait gave up and the loop ended early)
@@ -1350,7 +1359,9 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
                 }
                 asm volatile("bar.sync 1, 256;" ::: "memory");
                 for (int q = ew; q < a.B; q += 2 * kSmallWarps) {
-                    const float th = warp_threshold(a.sample_buf, a.n_sample, a.B, q, a.j, a.sample_per_tile, lane);
+                    const float th = a.j <= kJ
+                        ? warp_threshold<kJ>(a.sample_buf, a.n_sample, a.B, q, a.j, a.sample_per_tile, lane)
+                        : warp_threshold<kThrKeep>(a.sample_buf, a.n_sample, a.B, q, a.j, a.sample_per_tile, lane);
                     if (lane == 0) {
                         s_theta[q] = th;
                         if (blockIdx.x == 0) a.theta_out[q] = th;
@@ -1437,7 +1448,7 @@ gemm_small_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_const
             sm100::tc_fence_before();
             sm100::mbar_arrive(tempty + buf);
             }   // pipe_ok
-            if (++buf == 2) { buf = 0; bphase ^= 1u; }
+            if (++buf == a.nbuf) { buf = 0; bphase ^= 1u; }
             if (tl.sample && a.sample_per_tile == 1) {
                 // the tile's largest lower bound per query: sample_buf[tile][query]
                 asm volatile("bar.sync 1, 256;" ::: "memory");
@@ -1977,8 +1988,9 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
         sa.n = n;
         sa.nkb = nkb;
         sa.stages = stages;
+        sa.nbuf = std::max(2, std::min(kSmallAccBufs, 512 / NQ));
         uint32_t cols = 32;
-        while (cols < 2u * (uint32_t)NQ) cols <<= 1;
+        while (cols < (uint32_t)(sa.nbuf * NQ)) cols <<= 1;
         sa.tmem_cols = cols;
         sa.sample_rt = c->d_sample_rt;
         sa.meta = meta;
@@ -2018,8 +2030,12 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
             sa.n_tiles = n_sample;
             gemm_small_kernel<kSample><<<n_sample, kSmallThreads, smem, st>>>(mq, me, sa);
             MARS_CUDA_TRY(cudaGetLastError());
-            threshold_kernel<<<(B * 32 + kThrThreads - 1) / kThrThreads, kThrThreads, 0, st>>>(
-                c->d_sample, n_sample, B, j, sa.sample_per_tile, c->d_theta);
+            if (j <= kJ)
+                threshold_kernel<kJ><<<(B * 32 + kThrThreads - 1) / kThrThreads, kThrThreads, 0, st>>>(
+                    c->d_sample, n_sample, B, j, sa.sample_per_tile, c->d_theta);
+            else
+                threshold_kernel<kThrKeep><<<(B * 32 + kThrThreads - 1) / kThrThreads, kThrThreads, 0, st>>>(
+                    c->d_sample, n_sample, B, j, sa.sample_per_tile, c->d_theta);
             MARS_CUDA_TRY(cudaGetLastError());
             sa.n_tiles = all_tiles;
             MARS_CUDA_TRY(cudaEventRecord(c->ev_gemm[0], st));
@@ -2069,7 +2085,7 @@ int batch_topk_pass(const mars_store* s, mars_batch_ctx* c, const float* d_queri
                                                                      shard_thr_floats(B), B, K, c->d_theta);
             shard_global = true;
         } else {
-            threshold_kernel<<<thr_grid, kThrThreads, 0, st>>>(c->d_sample, n_sample, B, j, per_tile, c->d_theta);
+            threshold_kernel<kJ><<<thr_grid, kThrThreads, 0, st>>>(c->d_sample, n_sample, B, j, per_tile, c->d_theta);
         }
         MARS_CUDA_TRY(cudaGetLastError());
         // 4. candidates
