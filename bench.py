@@ -13,7 +13,8 @@ vs peak):
     results are those of the fp32 fused scan bit for bit, which the run
     checks, and the oracle's, which the run checks on 32 queries); 64 is the
     most the small-batch tiles hold, so a step stays one pass over the rows
-    (the line's `batch_sweep_per_gpu` has the step at 16 / 32 / 48);
+    (the line's `batch_sweep_per_gpu` has the step at 16 / 32 / 48 / 128 /
+    256);
   * N GPUs (`--shard replicas`, the default): the 1M-row corpus (4.6 GB with
     its fp16 copy) fits every GPU, so every GPU holds it and answers its own
     64 queries per step, with no data-path collective (weak scaling: 64 N
@@ -285,7 +286,7 @@ def run_mars(a):
     lo, hi = (a.n * rank // world, a.n * (rank + 1) // world) if sharded else (0, a.n)
     n_local = hi - lo
     E, mod, ts, imp = datagen.gaussian_rows(lo, hi, a.dim, seed=a.seed, ts_max=a.ts_max)
-    n_pool = max(64, 2 * a.queries_per_step)     # query pool the steps cycle through
+    n_pool = max(256, 2 * a.queries_per_step)    # query pool the steps cycle through (and the sweep's batches)
     Qh = datagen.queries(n_pool, a.dim, seed=a.seed + 1 + (0 if sharded else 1000 * rank))
     store = mb.Store(n_local, a.dim, device=local)
     store.upload(E, mod, ts, imp)
@@ -405,13 +406,14 @@ def run_mars(a):
     f16_ms = timed(lambda: ctx.scan_topk_f16(store, Qd[:Q], Q, a.ts_max, a.lam, K, ids, vals,
                                              use_importance=True, row_offset=lo, stream=ctx.stream), 8)
 
-    # the same step with fewer concurrent queries (device time per step, 20
-    # steps each, outside the timed region): how the step's cost grows with
-    # the batch
+    # the same step with fewer or more concurrent queries (device time per
+    # step, 20 steps each, outside the timed region): how the step's cost
+    # grows with the batch (above 64 queries the 128 x 256 tiles: one pass
+    # over the rows per 128 queries)
     sweep = {}
     if not sharded:
-        for Bs in (16, 32, 48):
-            if Bs >= Q:
+        for Bs in (16, 32, 48, 128, 256):
+            if Bs == Q:
                 continue
             bcs = mb.BatchContext(n_local, a.dim, max_batch=Bs, max_k=K, device=local)
             i2 = torch.empty((Bs, K), dtype=torch.int32, device="cuda")
