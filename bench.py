@@ -1089,9 +1089,12 @@ def cfg_c4(a, env):
                 dist.all_gather_into_tensor(all_sc, sc)
 
     step()
-    steps = 3
+    steps = 10
     e0, e1, e2 = (torch.cuda.Event(enable_timing=True) for _ in range(3))
     _barrier(dist)
+    sampler = ClockSampler(local) if rank == 0 else None
+    if sampler:
+        sampler.start()
     e0.record(stream)
     for _ in range(steps):
         step()
@@ -1101,6 +1104,7 @@ def cfg_c4(a, env):
                              stream=stream.cuda_stream)
     e2.record(stream)
     _barrier(dist)
+    clocks = sampler.stop() if sampler else None
     ms_local = e0.elapsed_time(e1) / steps
     ms = _max_over_ranks(dist, ms_local)
     ms_fastest = -_max_over_ranks(dist, -ms_local)     # the fastest rank (load balance across ranks)
@@ -1138,6 +1142,7 @@ def cfg_c4(a, env):
         rec = {"workload": "c4", "metric": f"queries/s (cmng_search + BFS depth 2, N={N}, K={K})",
                "value": nq / (ms * 1e-3), "unit": "queries/s", "n_gpus": world, "steps": steps, "scaling": "strong",
                "ms_per_batch": ms, "ms_per_batch_fastest_rank": ms_fastest, "queries_per_batch": nq,
+               "clocks": clocks,
                "parallelism": f"replicas x{world}, queries split" + (" + NCCL all-gather of results" if world > 1 else ""),
                "beam_only_queries_per_s": nq / (ms_beam * 1e-3), "graph_build_ms": build_ms,
                "mean_rows_scored_beam": rows_beam, "mean_nodes_visited_bfs": rows_bfs,
