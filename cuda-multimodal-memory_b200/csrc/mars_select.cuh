@@ -234,6 +234,8 @@ __device__ int block_select_topk(unsigned long long* cand, int M, int K, int* hi
 // with __syncthreads().
 template <int NT, class Load>
 __device__ uint32_t block_kth_largest_key(Load load, int n, int k, int* hist, uint32_t* s_sel) {
+    static_assert(NT % 32 == 0 && 1024 % NT == 0, "whole warps, bucket groups of equal size");
+    __shared__ int s_wsum[NT / 32];   // each warp's share of the bucket counts
     const int lane = threadIdx.x & 31;
     uint32_t prefix = 0, pmask = 0;
     int rem = k;
@@ -255,11 +257,13 @@ __device__ uint32_t block_kth_largest_key(Load load, int n, int k, int* hist, ui
             if (in && (threadIdx.x & 31) == __ffs(peers) - 1) atomicAdd(&hist[bucket], __popc(peers));
         }
         __syncthreads();
-        // the bucket holding the rem-th largest key: warp 0, lane l sums the
-        // l-th group of nb / 32 buckets counted from the top
-        if (threadIdx.x < 32) {
-            const int per = nb / 32;
-            const int top = nb - lane * per;
+        // the bucket holding the rem-th largest key: thread t sums the t-th
+        // group of nb / NT buckets counted from the top, a block-wide
+        // prefix sum over the groups (warp scans, then the warps' totals)
+        // finds the one group that holds it, and its thread walks it
+        {
+            const int per = nb / NT;
+            const int top = nb - (int)threadIdx.x * per;
             int sum = 0;
             for (int b = top - 1; b >= top - per; --b) sum += hist[b];
             int incl = sum;
@@ -268,9 +272,13 @@ __device__ uint32_t block_kth_largest_key(Load load, int n, int k, int* hist, ui
                 const int t = __shfl_up_sync(0xffffffffu, incl, o);
                 if (lane >= o) incl += t;
             }
+            if (lane == 31) s_wsum[threadIdx.x >> 5] = incl;
+            __syncthreads();
+            int before = 0;
+            for (int w = 0; w < (int)(threadIdx.x >> 5); ++w) before += s_wsum[w];
+            incl += before;
             const int excl = incl - sum;
-            const unsigned mine = __ballot_sync(0xffffffffu, excl < rem && rem <= incl);
-            if (lane == __ffs(mine) - 1) {
+            if (excl < rem && rem <= incl) {
                 int acc = excl;
                 for (int b = top - 1; b >= top - per; --b) {
                     if (acc + hist[b] >= rem) {
