@@ -14,7 +14,9 @@ mars_query_batch_topk over the whole corpus on one store, bit for bit:
   certifies itself);
 * K = 256 (exact per-query scans on every shard, neutral records);
 * a shard too small for the tensor-core path next to large ones;
-* a modality filter without importance.
+* a modality filter without importance;
+* a shard whose bounded device wait gives up: every merged answer of that
+  call is invalid, and the calls after it recover.
 
 With the shared threshold the shards together short-list about as many
 candidates as one store does, not `world` times as many.
@@ -117,6 +119,36 @@ def test_emulated_shards_equal_one_store(corpus, sizes, B, K, filt, use_imp):
                                                                        K, i, v, c, modality_filter=filt,
                                                                        use_importance=use_imp), B, K)
         assert np.array_equal(again[0], ref[0]) and np.array_equal(again[2], ref[2])
+    finally:
+        for s in stores:
+            s.close()
+
+
+def test_failed_shard_invalidates_every_answer(corpus):
+    """A shard whose bounded device wait gives up (the batch context's test
+    hook) flags its bound record: the merged answers of that call are all
+    invalid (counts -1); the failing shard reports the timeout on its next
+    call, whose answers are invalid too (it joins the exchanges with neutral
+    records), and the call after that is exact again."""
+    import mars_b200 as mb
+    E, mod, ts, imp, st, Qd = corpus
+    B, K = 16, 10
+    bc = mb.BatchContext(N, D, max_batch=256, max_k=256)
+    ref = _run(lambda i, v, c: bc.query_batch_topk(st, Qd[:B], B, 600.0, 0.01, K, i, v, c, use_importance=True),
+               B, K)
+    stores, ctxs, offs = _shards(corpus, _even(3))
+    try:
+        call = lambda i, v, c: mb.shard_emulate_query_batch_topk(stores, ctxs, offs, Qd[:B], B, 600.0, 0.01, K, i,
+                                                                  v, c, use_importance=True)
+        ctxs[1].debug_wait(4096, 1)        # shard 1's grid-wide wait cannot end
+        ids, vals, cnt = _run(call, B, K)
+        assert np.all(cnt == -1) and np.all(ids == -1) and np.all(np.isneginf(vals))
+        with pytest.raises(mb.MarsError) as e:
+            _run(call, B, K)
+        assert e.value.status == mb.MARS_ERR_TIMEOUT
+        got = _run(call, B, K)
+        assert np.array_equal(got[0], ref[0]) and np.array_equal(got[2], ref[2])
+        assert np.array_equal(got[1].view(np.int32), ref[1].view(np.int32))
     finally:
         for s in stores:
             s.close()
