@@ -229,6 +229,7 @@ struct mars_shard_comm {
     float* d_xrecv[2] = {nullptr, nullptr};  // every rank's, rank-major
     cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};   // local / exchange / merge boundaries
     bool timed = false;
+    bool exchange_single = false;           // test hook: world 1 runs the whole exchange protocol
     int32_t timeout_ms = 0;                 // deadline of NCCL's set-up work (creation, first use, teardown)
     void* bfs_state = nullptr;              // mars_shard_query's scratch (made on first use)
 };
@@ -459,6 +460,12 @@ int mars_shard_comm_set_timing(mars_shard_comm* c, int32_t enable) {
     return MARS_OK;
 }
 
+int mars_shard_comm_set_exchange_at_world1(mars_shard_comm* c, int32_t enable) {
+    if (c == nullptr) return fail(MARS_ERR_INVALID, "mars_shard_comm_set_exchange_at_world1: NULL communicator");
+    c->exchange_single = enable != 0;
+    return MARS_OK;
+}
+
 int mars_shard_last_times(mars_shard_comm* c, float* local_ms, float* gather_ms, float* merge_ms) {
     if (c == nullptr) return fail(MARS_ERR_INVALID, "mars_shard_last_times: NULL communicator");
     if (!c->timed) return fail(MARS_ERR_INVALID, "mars_shard_last_times: timing is off (mars_shard_comm_set_timing)");
@@ -494,6 +501,20 @@ int mars_shard_query_batch_topk(const mars_store* s, mars_batch_ctx* ctx, mars_s
     cudaStream_t st = stream ? static_cast<cudaStream_t>(stream)
                              : (ctx != nullptr ? batch_ctx_stream(ctx) : static_cast<cudaStream_t>(nullptr));
     if (c->timed) MARS_CUDA_TRY(cudaEventRecord(c->ev[0], st));
+    if (c->world == 1 && !c->exchange_single) {
+        // one shard holds every row: its local answer is the merged one, so
+        // the call is the single-store pipeline (no records, no exchange,
+        // no merge)
+        const int rc = (s == nullptr || ctx == nullptr || s->device != c->device)
+                           ? fail(MARS_ERR_INVALID, "mars_shard_query_batch_topk: store and context must be on "
+                                                    "the communicator's device")
+                           : batch_topk_sharded(s, ctx, d_queries, query_pitch, B, query_timestamp, lambda,
+                                                modality_filter, use_importance, K, row_offset, d_ids, d_vals,
+                                                d_counts, st, nullptr);
+        if (c->timed)
+            for (int e = 1; e < 4; ++e) MARS_CUDA_TRY(cudaEventRecord(c->ev[e], st));
+        return rc;
+    }
 
     // 1-4: the local pipeline with the two record exchanges
     BoundExchange xchg{&exchange_records, c, c->world, {c->d_xsend[0], c->d_xsend[1]},

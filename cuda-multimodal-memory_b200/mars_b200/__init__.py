@@ -145,6 +145,7 @@ _SIGS = {
     "mars_shard_comm_status": [_VP],
     "mars_shard_comm_abort": [_VP],
     "mars_shard_comm_set_timing": [_VP, _I32],
+    "mars_shard_comm_set_exchange_at_world1": [_VP, _I32],
     "mars_shard_last_times": [_VP, C.POINTER(C.c_float), C.POINTER(C.c_float), C.POINTER(C.c_float)],
     "mars_shard_query": [_VP, _VP, _VP, _VP, _VP, _I32, _VP, _F32, C.POINTER(RetrievalConfig), _I32, _VP,
                          C.POINTER(_I32)],
@@ -571,6 +572,11 @@ class ShardComm:
 
     def set_timing(self, enable: bool) -> None:
         _check(lib().mars_shard_comm_set_timing(self.handle, int(bool(enable))))
+
+    def set_exchange_at_world1(self, enable: bool) -> None:
+        """Test hook: one rank runs the whole exchange protocol (records, NCCL
+        all-gathers, merge) instead of the single-store pipeline."""
+        _check(lib().mars_shard_comm_set_exchange_at_world1(self.handle, int(bool(enable))))
 
     def last_times(self) -> dict:
         a, b, m = C.c_float(), C.c_float(), C.c_float()

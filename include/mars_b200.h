@@ -409,6 +409,12 @@ int mars_shard_comm_abort(mars_shard_comm* comm);
  * for the last call and returns their device times in ms. */
 int mars_shard_comm_set_timing(mars_shard_comm* comm, int32_t enable);
 int mars_shard_last_times(mars_shard_comm* comm, float* local_ms, float* gather_ms, float* merge_ms);
+/* A communicator of one rank answers mars_shard_query_batch_topk with the
+ * single-store pipeline (its local answer is the merged one).  Test hook:
+ * enable = 1 makes it run the whole exchange protocol instead (records,
+ * NCCL all-gathers, merge), so one GPU can check that path against the
+ * single-store call. */
+int mars_shard_comm_set_exchange_at_world1(mars_shard_comm* comm, int32_t enable);
 
 /* mars_query_batch_topk over a row-sharded corpus, called by every rank with
  * the same queries, B, K, t_q, lambda, filter and use_importance (a

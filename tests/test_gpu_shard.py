@@ -3,7 +3,9 @@ communicator owned by the library.
 
 * One rank on one GPU (world 1, real NCCL): the call equals
   mars_query_batch_topk on the same store bit for bit, for the small-batch
-  tiles (B <= 64), the 128 x 256 tiles and K = 256, with a row offset.
+  tiles (B <= 64), the 128 x 256 tiles and K = 256, with a row offset --
+  both as one rank answers by default (the single-store pipeline) and with
+  the whole exchange protocol forced (records, NCCL all-gathers, merge).
 * A bounded device wait that gives up on a rank (the batch context's test
   hook) marks that call's merged results invalid (counts -1) and the call
   after it is exact again.
@@ -54,10 +56,12 @@ def _answers(fn, B, K):
     return ids.cpu().numpy(), vals.cpu().numpy(), cnt.cpu().numpy()
 
 
+@pytest.mark.parametrize("full", [False, True])
 @pytest.mark.parametrize("B,K", [(16, 10), (200, 100), (64, 256)])
-def test_world1_equals_unsharded_call(env, B, K):
+def test_world1_equals_unsharded_call(env, B, K, full):
     import mars_b200 as mb
     st, comm, Qd, N, D = env
+    comm.set_exchange_at_world1(full)
     bc = mb.BatchContext(N, D, max_batch=256, max_k=256)
     off = 1_000_000
     ref = _answers(lambda i, v, c: bc.query_batch_topk(st, Qd[:B], B, 600.0, 0.01, K, i, v, c, use_importance=True,
@@ -72,13 +76,18 @@ def test_world1_equals_unsharded_call(env, B, K):
                                                    use_importance=True, row_offset=off), B, K)
     t = comm.last_times()
     comm.set_timing(False)
-    assert t["local_ms"] > 0 and t["gather_ms"] >= 0 and t["merge_ms"] > 0
+    assert t["local_ms"] > 0 and t["gather_ms"] >= 0 and t["merge_ms"] >= 0
+    if full:
+        assert t["merge_ms"] > 0
     comm.status()
+    comm.set_exchange_at_world1(False)
 
 
-def test_failed_rank_invalidates_merged_results(env):
+@pytest.mark.parametrize("full", [False, True])
+def test_failed_rank_invalidates_merged_results(env, full):
     import mars_b200 as mb
     st, comm, Qd, N, D = env
+    comm.set_exchange_at_world1(full)
     B, K = 16, 10
     bc = mb.BatchContext(N, D, max_batch=256, max_k=256)
     ref = _answers(lambda i, v, c: bc.query_batch_topk(st, Qd[:B], B, 600.0, 0.01, K, i, v, c,
@@ -97,6 +106,7 @@ def test_failed_rank_invalidates_merged_results(env):
     got = _answers(lambda i, v, c: comm.query_batch_topk(st, bc, Qd[:B], B, 600.0, 0.01, K, i, v, c,
                                                          use_importance=True), B, K)
     assert np.array_equal(got[0], ref[0]) and np.array_equal(got[2], ref[2])
+    comm.set_exchange_at_world1(False)
 
 
 def test_two_ranks_on_two_gpus(tmp_path):
