@@ -8,8 +8,8 @@
 //
 //  1. prep:      per-row weight w = __expf(-lambda*age) [x importance] (NaN for
 //                rows the modality filter rejects), per-query error margin.
-//  2. sample:    the GEMM over a strided sample of row tiles; each (query, tile)
-//                keeps its 16 best lower bounds.
+//  2. sample:    the GEMM over a strided sample of row tiles; each (query,
+//                32-row chunk) keeps its 4 best lower bounds.
 //  3. threshold: per query the j-th best sampled lower bound, theta.  j is
 //                chosen so that theta lies, with overwhelming probability,
 //                below the query's true K-th best score.
@@ -20,14 +20,15 @@
 //                can place), pruning by the K-th best lower bound, then the
 //                exact fp32 score of the survivors with the canonical dot (the
 //                same arithmetic as the single-query scan) and the top-K.
-//                Queries that fail the check are re-run by the host with the
-//                exact single-query scan.
+//                Queries that fail the check are rescanned exactly on the
+//                device (the fused scan, only those queries).
 //
 // GEMM: kind::tf32 (fp32 operands read by TMA straight from the store, 128-byte
 // swizzled K-major tiles), M = 128 queries x N = 256 rows per tile, K steps of
 // 32, 4-stage TMA ring, accumulators double-buffered in TMEM (2 x 256 columns).
-// Warp roles: warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2-5
-// epilogue (one query row per thread, tcgen05.ld 32x32b).
+// Warp roles: warp 0 TMA producer, warp 1 MMA issuer + TMEM owner, warps 2-9
+// epilogue (one query row per thread and half of the tile's columns,
+// tcgen05.ld 32x32b).
 //
 // Error bound of the approximate score: operands keep 10 mantissa bits, so
 // |A - dot| <= (2^-9 + 2^-20) |q||e| + accumulation (<= D 2^-23 |q||e|); the
@@ -67,7 +68,9 @@ constexpr int kStageBytes = kStageA + kStageB;
 constexpr int kGemmThreads = 320;
 constexpr int kGemmEpi = kGemmThreads - 64;  // epilogue threads
 constexpr int kTmemCols = 512;
-constexpr int kJ = 16;                // sampled lower bounds kept per (query, tile)
+constexpr int kJ = 16;                // sampled lower bounds kept per (query, tile half)
+constexpr int kSampleKeep = 4;        // ... as the 4 best of each of the half's 4 32-row chunks
+static_assert(kJ == kSampleKeep * (kBN / 64), "a tile half's chunks fill its kJ values");
 // Relative error margin of a short-listed score, times ||q|| max||e||.
 // TF32 operands: the tensor cores may truncate each fp32 operand to 10
 // mantissa bits (2^-10 relative each, 1.95e-3 for the product's two
@@ -122,7 +125,7 @@ struct GemmArgs {
     RowMeta meta;                    // row weights
     const float* theta;              // B thresholds (candidate mode)
     const float* margin;             // B margins
-    float* sample_buf;               // [n_tiles][B][kJ]
+    float* sample_buf;               // [sample tiles][B][2 halves][kJ]
     int4* cand;                      // [B][cap] candidates (cand_entry)
     int32_t* cand_cnt;               // [B]
     int32_t cap;
@@ -269,9 +272,6 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
             asm volatile("bar.sync 1, 256;" ::: "memory");
             if (!sm100::mbar_wait(tfull + buf, bphase, a.err, 5)) break;
             sm100::tc_fence_after();
-            float best[kJ];
-#pragma unroll
-            for (int j = 0; j < kJ; ++j) best[j] = -INFINITY;
             // one 32-row chunk of the accumulator at a time (the chunk loop is
             // left rolled: the epilogue's code shares the instruction cache
             // with the producer and MMA warps)
@@ -318,6 +318,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                     }
                 } else {
                     if (!qv) continue;
+                    // sample mode: this chunk's kSampleKeep best lower bounds
+                    // of query q, out to sample_buf[tile][query][half][chunk]
+                    // (-inf where fewer).  A subset of the sampled values: the
+                    // j-th largest of them is at most the j-th largest of all
+                    // (a threshold never above the full sample's), and with j
+                    // small against the sample the two almost always agree.
+                    float best[kSampleKeep];
+#pragma unroll
+                    for (int s = 0; s < kSampleKeep; ++s) best[s] = -INFINITY;
 #pragma unroll
                     for (int j4 = 0; j4 < 8; ++j4) {
                         const float4 w4 = reinterpret_cast<const float4*>(s_w + c * 32)[j4];
@@ -328,26 +337,23 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_q, const __grid_constant__ 
                             const float w = (rbase + j == self_row) ? NAN : wv[u];
                             const float f = __uint_as_float(r[j]) * w;
                             const float slack = mg * fabsf(w);
-                            // sample mode: the tile's kJ best lower bounds of query q
                             float lo = f - slack;
-                            if (lo > best[kJ - 1]) {    // NaN never passes
+                            if (lo > best[kSampleKeep - 1]) {    // NaN never passes
 #pragma unroll
-                                for (int s = 0; s < kJ; ++s) {
+                                for (int s = 0; s < kSampleKeep; ++s) {
                                     if (lo > best[s]) { const float tmp = best[s]; best[s] = lo; lo = tmp; }
                                 }
                             }
                         }
                     }
+                    float* dst = a.sample_buf + (((int64_t)(t / a.qtiles) * a.B + q) * 2 + half) * kJ +
+                                 (c - half * (kBN / 64)) * kSampleKeep;
+#pragma unroll
+                    for (int s = 0; s < kSampleKeep; ++s) dst[s] = best[s];
                 }
             }
             sm100::tc_fence_before();
             sm100::mbar_arrive(tempty + buf);
-            if (MODE == kSample && qv) {
-                // each half's kJ best of its 128 columns: [tile][query][2 kJ]
-                float* dst = a.sample_buf + (((int64_t)(t / a.qtiles) * a.B + q) * 2 + half) * kJ;
-#pragma unroll
-                for (int j = 0; j < kJ; ++j) dst[j] = best[j];
-            }
             if (++buf == 2) { buf = 0; bphase ^= 1u; }
         }
     }
